@@ -1,0 +1,286 @@
+"""Benchmark of the B200 DiT denoiser hot path (one JSON line on rank 0).
+
+Workload (the metric's 1024x1024 case): 36-block ERNIE DiT, 4096 image tokens
+(64x64 packed latent) + 64 text tokens, BF16 mode, turbo 8-step schedule, one seed per GPU
+(data-parallel, no collective in the data path; weak scaling). A bench "step" is one full denoise
+step (input head, 36 blocks, output head, Euler update) on every rank's seed; images/s counts 8 steps
+per image. Weights are seeded random-init (no checkpoint is available), inputs seeded N(0,1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ernie-image-ncnn-vulkan_b200"))
+
+METRIC = "DiT denoise ms/step and images/s (8-step 1024²) at 1/2/4/8 B200; % BF16 peak"
+WIDTH, HEIGHT, TEXT, VALID = 64, 64, 64, 64
+STEPS_PER_IMAGE = 8
+NUM_BLOCKS = 36
+PARAMS_PER_BLOCK = 218_103_808  # 7 GEMMs: 4*4096^2 + 3*4096*12288
+
+
+def step_flops(tokens, valid_keys, blocks=NUM_BLOCKS):
+    """Algorithmic FLOPs of one denoise step: 2*N*params (GEMMs) + 4*N*N_valid*4096 (QK^T and PV)."""
+    return blocks * (2.0 * tokens * PARAMS_PER_BLOCK + 4.0 * tokens * valid_keys * 4096)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return p["bf16_tflops"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), p["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [l.split(",") for l in open(self.file.name).read().strip().splitlines() if l.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        if not sm:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(sm),
+                "reasons": reasons}
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus and world > 1:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE {world}")
+    pg = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, local, world, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+
+
+def max_over_ranks(pg, value):
+    if pg is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline_block(threads=None):
+    """One oracle (CPU restatement) DiT block at the workload's token count, timed on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    if threads:
+        o.lib().orc_set_num_threads(threads)
+    seed = 0
+    w = o.BlockWeights(seed, 0)
+    cos, sin, mask = o.dit_constants(WIDTH, HEIGHT, VALID, TEXT)
+    n = WIDTH * HEIGHT + TEXT
+    x = o.synth_normal(seed, o.HIDDEN_STREAM, n * 4096).reshape(n, 4096)
+    mod = o.block_modulation(seed)
+    t0 = time.perf_counter()
+    o.block(x, w, mod, cos, sin, mask)
+    dt = time.perf_counter() - t0
+    return dt, o.lib().orc_num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the reference's CPU path on this host's cores (the
+    reference itself cannot be built: empty ncnn submodule, no Rust toolchain, no Vulkan)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times = []
+    cores = 1
+    for i in range(args.warmup + args.steps):
+        dt, cores = cpu_baseline_block()
+        if i >= args.warmup:
+            times.append(dt)
+    block_s = statistics.median(times)
+    step_s = block_s * NUM_BLOCKS
+    image_s = step_s * STEPS_PER_IMAGE
+    value = 1.0 / image_s
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "images/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C2 1024x1024: 4096 image + 64 text tokens, 36 blocks, 8 steps, 1 seed",
+                       "sample": "1 DiT block per step sample, extrapolated x36 blocks x8 steps"},
+            "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port",
+                             "sample": "one DiT block (4160 tokens) of the oracle per step; x36 x8 extrapolated"},
+            "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--blocks", type=int, default=NUM_BLOCKS, help=argparse.SUPPRESS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    ctx = ec.Context(local)
+    model = ec.Model(ctx, args.blocks)
+    model.synthesize(1234)
+    precision = ec.BF16 if args.precision == "bf16" else ec.FP32
+    session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision)
+    seed = 1000 + rank  # data parallel: one independent seed per GPU
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    rng = np.random.default_rng(seed)
+    latent = rng.standard_normal((128, HEIGHT, WIDTH), dtype=np.float32)
+    text = rng.standard_normal((TEXT, 3072), dtype=np.float32)
+    cos, sin, mask = ec.dit_constants(WIDTH, HEIGHT, VALID, TEXT)
+    session.set_conditioning(text, cos, sin, mask)
+    tokens = WIDTH * HEIGHT + TEXT
+    flops = step_flops(tokens, WIDTH * HEIGHT + VALID, args.blocks)
+    launches_per_step = session.launches_per_step()
+
+    # warm-up: graph capture of every step index, then W steps
+    lat_ptr = session.latent_ptr()
+    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(latent), latent.nbytes))
+    for i in range(args.warmup):
+        session.denoise_device(STEPS_PER_IMAGE, i % STEPS_PER_IMAGE, i % STEPS_PER_IMAGE + 1)
+    for i in range(STEPS_PER_IMAGE):
+        session.denoise_device(STEPS_PER_IMAGE, i, i + 1)
+
+    # timed region: K steps, device-timed with CUDA events on the library's stream
+    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(latent), latent.nbytes))
+    clocks = ClockSampler(local)
+    barrier(pg)
+    ctx.synchronize()
+    clocks.start()
+    ctx.record(0)
+    for i in range(args.steps):
+        session.denoise_device(STEPS_PER_IMAGE, i % STEPS_PER_IMAGE, i % STEPS_PER_IMAGE + 1)
+    ctx.record(1)
+    ctx.synchronize()
+    clock_info = clocks.stop()
+    barrier(pg)
+    ms = ctx.elapsed(0, 1)
+    ms_max = max_over_ranks(pg, ms)
+    ms_per_step = ms_max / args.steps
+    images_per_s = world * 1000.0 / (ms_per_step * STEPS_PER_IMAGE)
+
+    # dominant kernel, timed live: the up/gate GEMM (largest of the 7 per block)
+    prof = {}
+    for kernel, name in ((1, "qkv_gemm"), (2, "attention"), (3, "out_gemm"), (5, "upgate_gemm"), (6, "down_gemm"),
+                         (0, "norm_modulate")):
+        prof[name] = session.profile(kernel, 10)
+    bf16_peak, bf16_sustained, hbm_peak, peak_kind = peaks()
+    n_valid = WIDTH * HEIGHT + VALID
+    kernel_flops = {"qkv_gemm": 2.0 * tokens * 4096 * 12288, "attention": 4.0 * tokens * n_valid * 4096,
+                    "out_gemm": 2.0 * tokens * 4096 * 4096, "upgate_gemm": 2.0 * tokens * 4096 * 24576,
+                    "down_gemm": 2.0 * tokens * 12288 * 4096}
+    dominant = "upgate_gemm"
+    achieved = kernel_flops[dominant] / (prof[dominant] * 1e-3) / 1e12
+    step_tflops = flops / (ms_per_step * 1e-3) / 1e12
+
+    # end to end through the public API: host latent in, 8-step denoise, host latent out
+    e2e = None
+    if not args.no_e2e:
+        out = session.denoise(latent, STEPS_PER_IMAGE)  # warm (graph for the full range)
+        barrier(pg)
+        t0 = time.perf_counter()
+        reps = max(1, args.steps // STEPS_PER_IMAGE)
+        for _ in range(reps):
+            out = session.denoise(latent, STEPS_PER_IMAGE)
+        dt = (time.perf_counter() - t0) / reps
+        dt = max_over_ranks(pg, dt)
+        assert np.isfinite(out).all()
+        e2e = {"value": world / dt, "unit": "images/s", "h2d_bytes_per_step": latent.nbytes // STEPS_PER_IMAGE,
+               "d2h_bytes_per_step": latent.nbytes // STEPS_PER_IMAGE,
+               "call": "ernie_cuda_session_denoise (8 steps, host buffers); bytes per step = latent bytes / 8"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        block_s, cores = cpu_baseline_block()
+        image_s = block_s * args.blocks * STEPS_PER_IMAGE
+        cpu = {"value": 1.0 / image_s, "unit": "images/s", "cores": cores, "kind": "port",
+               "sample": f"one DiT block at {tokens} tokens on the CPU restatement ({block_s:.2f} s), "
+                         f"extrapolated x{args.blocks} blocks x{STEPS_PER_IMAGE} steps"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+                "config": {"workload": "C2 1024x1024: 64x64 packed latent (4096 image tokens) + 64 text tokens, "
+                                       f"{args.blocks} blocks, turbo 8-step schedule, one seed per GPU",
+                           "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
+                           "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
+                           "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
+                           "kernel_ms": prof},
+                "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": bf16_peak,
+                             "unit": "TFLOP/s", "frac": achieved / bf16_peak, "peak_kind": peak_kind,
+                             "traffic": None},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+                "clocks": clock_info}
+        print(json.dumps(line), flush=True)
+    session.close()
+    model.close()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

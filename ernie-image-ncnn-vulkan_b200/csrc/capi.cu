@@ -1,0 +1,1171 @@
+// C ABI (include/ernie_cuda.h): context, resident weights, layer operators and the request session
+// that runs the DiT denoise loop on one B200. Host orchestration only; all arithmetic of the path is
+// in the sm_100a kernels of gemm.cu, attention.cu and elementwise.cu.
+#include "ernie_cuda.h"
+#include "ernie_synth.h"
+#include "kernels.h"
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+using namespace ernie_b200;
+
+namespace
+{
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &message)
+{
+    g_last_error = message;
+    return code;
+}
+
+int from_cuda(cudaError_t e, const char *action)
+{
+    if (e == cudaSuccess) return ERNIE_CUDA_OK;
+    const int code = e == cudaErrorMemoryAllocation ? ERNIE_CUDA_OUT_OF_MEMORY : ERNIE_CUDA_ERROR;
+    return fail(code, std::string(action) + ": " + cudaGetErrorString(e));
+}
+
+int from_launch(int e, const char *action) { return from_cuda(static_cast<cudaError_t>(e), action); }
+
+#define ERNIE_TRY(expr)                                                                                             \
+    do                                                                                                              \
+    {                                                                                                               \
+        const int _rc = (expr);                                                                                     \
+        if (_rc != ERNIE_CUDA_OK) return _rc;                                                                       \
+    } while (0)
+#define ERNIE_LAUNCH(expr, what) ERNIE_TRY(from_launch((expr), what))
+#define ERNIE_CUDA(expr, what) ERNIE_TRY(from_cuda((expr), what))
+
+size_t align256(size_t bytes) { return (bytes + 255) & ~size_t(255); }
+
+// Carves one device allocation into 256-byte aligned sub-buffers.
+struct Arena
+{
+    std::vector<std::pair<void **, size_t>> parts;
+    void *base = nullptr;
+    template <class T> void add(T **ptr, size_t count) { parts.push_back({reinterpret_cast<void **>(ptr), align256(count * sizeof(T))}); }
+    size_t bytes() const
+    {
+        size_t total = 0;
+        for (const auto &p : parts) total += p.second;
+        return total;
+    }
+    cudaError_t allocate()
+    {
+        const cudaError_t e = cudaMalloc(&base, bytes());
+        if (e != cudaSuccess) return e;
+        char *cursor = static_cast<char *>(base);
+        for (auto &p : parts)
+        {
+            *p.first = cursor;
+            cursor += p.second;
+        }
+        return cudaSuccess;
+    }
+};
+
+struct DeviceGuard
+{
+    int previous = -1;
+    explicit DeviceGuard(int device)
+    {
+        cudaGetDevice(&previous);
+        if (previous != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard()
+    {
+        int now = -1;
+        cudaGetDevice(&now);
+        if (previous >= 0 && now != previous) cudaSetDevice(previous);
+    }
+};
+
+struct DevBlock
+{
+    __nv_bfloat16 *wqkv = nullptr, *wo = nullptr, *wug = nullptr, *wfc2 = nullptr;
+    float *gamma_sa = nullptr, *gamma_mlp = nullptr, *gamma_q = nullptr, *gamma_k = nullptr;
+    void *alloc = nullptr;
+};
+
+struct DevHeads
+{
+    __nv_bfloat16 *x_embed_w = nullptr, *text_proj_w = nullptr, *time1_w = nullptr, *time2_w = nullptr,
+                  *adaln_w = nullptr, *final_norm_w = nullptr, *final_w = nullptr;
+    float *x_embed_b = nullptr, *time1_b = nullptr, *time2_b = nullptr, *adaln_b = nullptr, *final_norm_b = nullptr,
+          *final_b = nullptr;
+    void *alloc = nullptr;
+};
+
+// FlowSchedule::turbo (src/latent_ops.cpp:89-109) and the evenly spaced variant.
+int host_schedule(int steps, int kind, float *sigmas, float *timesteps)
+{
+    if (steps < 1 || steps > 1000) return fail(ERNIE_CUDA_ERROR, "Steps must be in [1,1000]");
+    if (kind != ERNIE_SCHEDULE_TURBO && kind != ERNIE_SCHEDULE_LINEAR) return fail(ERNIE_CUDA_ERROR, "Unknown schedule");
+    const float increment = -1.f / float(steps);
+    for (int i = 0; i < steps; ++i)
+    {
+        const float raw = i < (steps + 1) / 2 ? std::fma(increment, float(i), 1.f) : -increment * float(steps - i);
+        if (kind == ERNIE_SCHEDULE_TURBO)
+        {
+            const float scaled = 4.f * raw;
+            const float denominator = 1.f + 3.f * raw;
+            sigmas[i] = scaled / denominator;
+        }
+        else
+            sigmas[i] = raw;
+        timesteps[i] = 1000.f * sigmas[i];
+    }
+    sigmas[steps] = 0.f;
+    return ERNIE_CUDA_OK;
+}
+
+// timestep_features (src/denoiser.cpp:152-169), evaluated on the host as the reference does.
+int host_features(float timestep, float *out)
+{
+    if (!std::isfinite(timestep) || timestep < 0.f || timestep > 1000.f)
+        return fail(ERNIE_CUDA_ERROR, "Timestep must be finite and in [0,1000]");
+    const float factor = -float(std::log(10000.0));
+    for (int i = 0; i < 2048; ++i)
+    {
+        // host code is built with -ffp-contract=off, as the reference library is
+        const float product = factor * float(i);
+        const float exponent = product / 2048.f;
+        const float phase = timestep * std::exp(exponent);
+        out[i] = std::sin(phase);
+        out[2048 + i] = std::cos(phase);
+    }
+    return ERNIE_CUDA_OK;
+}
+
+void official_frequencies(float *out)
+{
+    const int dims[3] = {32, 48, 48};
+    int j = 0;
+    for (int a = 0; a < 3; ++a)
+        for (int i = 0; i < dims[a]; i += 2) out[j++] = 1.f / std::pow(256.f, float(i) / float(dims[a]));
+}
+} // namespace
+
+struct ernie_cuda_context
+{
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    int *error_flag = nullptr; // device-side protocol status of the bounded waits
+    int query_rows = 128;
+    cudaEvent_t events[16] = {};
+};
+
+struct ernie_cuda_model
+{
+    ernie_cuda_context *ctx = nullptr;
+    int num_blocks = 0;
+    std::vector<DevBlock> blocks;
+    DevHeads heads;
+    uint64_t bytes = 0;
+};
+
+struct ernie_cuda_session
+{
+    ernie_cuda_model *model = nullptr;
+    ernie_cuda_context *ctx = nullptr;
+    int width = 0, height = 0, text = 0, valid = 0, precision = 0, splits = 1;
+    int image = 0, tokens = 0, rows_pad = 0;
+    int kv_len = 0;
+    bool use_mask = false, conditioned = false, has_text = false;
+    float *x = nullptr, *text_cache = nullptr, *cos_t = nullptr, *sin_t = nullptr, *mask = nullptr,
+          *latent = nullptr, *scratch_latent = nullptr, *pred = nullptr, *g1 = nullptr, *c = nullptr,
+          *mod = nullptr, *ss = nullptr;
+    __nv_bfloat16 *a = nullptr, *h = nullptr;
+    void *q = nullptr, *k = nullptr, *v = nullptr;
+    void *alloc = nullptr;
+    // per-schedule buffers
+    float *features = nullptr, *preds = nullptr;
+    int *flags = nullptr;
+    int feature_capacity = 0, pred_capacity = 0;
+    std::tuple<int, int> feature_key{-1, -1};
+    std::vector<float> deltas;
+    float *pinned = nullptr;
+    std::map<std::tuple<int, int, int, int, int>, cudaGraphExec_t> graphs;
+};
+
+// ------------------------------------------------------------------------------------------------
+extern "C" const char *ernie_cuda_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int ernie_cuda_device_count(int *count)
+{
+    if (!count) return fail(ERNIE_CUDA_ERROR, "null count");
+    return from_cuda(cudaGetDeviceCount(count), "cudaGetDeviceCount");
+}
+
+extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
+{
+    if (!out) return fail(ERNIE_CUDA_ERROR, "null output");
+    *out = nullptr;
+    int count = 0;
+    ERNIE_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device < 0 || device >= count) return fail(ERNIE_CUDA_ERROR, "No CUDA device " + std::to_string(device));
+    DeviceGuard guard(device);
+    cudaDeviceProp prop;
+    ERNIE_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10) return fail(ERNIE_CUDA_ERROR, std::string("Requires an sm_100 (B200) device, found ") + prop.name);
+    auto *ctx = new ernie_cuda_context();
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->error_flag, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->error_flag, 0, sizeof(int));
+    for (int i = 0; i < 16 && e == cudaSuccess; ++i) e = cudaEventCreate(&ctx->events[i]);
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_gemm_kernels());
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_attention_kernels());
+    if (e != cudaSuccess)
+    {
+        ernie_cuda_context_destroy(ctx);
+        return from_cuda(e, "Create CUDA context");
+    }
+    *out = ctx;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_context_destroy(ernie_cuda_context *ctx)
+{
+    if (!ctx) return ERNIE_CUDA_OK;
+    DeviceGuard guard(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (auto &ev : ctx->events)
+        if (ev) cudaEventDestroy(ev);
+    if (ctx->error_flag) cudaFree(ctx->error_flag);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_context_synchronize(ernie_cuda_context *ctx)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    DeviceGuard guard(ctx->device);
+    ERNIE_CUDA(cudaStreamSynchronize(ctx->stream), "Synchronize stream");
+    int flag = 0;
+    ERNIE_CUDA(cudaMemcpy(&flag, ctx->error_flag, sizeof(int), cudaMemcpyDeviceToHost), "Read device status");
+    if (flag)
+    {
+        cudaMemset(ctx->error_flag, 0, sizeof(int));
+        return fail(ERNIE_CUDA_ERROR, "Device-side wait timed out (status " + std::to_string(flag) + ")");
+    }
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_context_memory(ernie_cuda_context *ctx, uint64_t *free_bytes, uint64_t *total_bytes)
+{
+    if (!ctx || !free_bytes || !total_bytes) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(ctx->device);
+    size_t f = 0, t = 0;
+    ERNIE_CUDA(cudaMemGetInfo(&f, &t), "cudaMemGetInfo");
+    *free_bytes = f;
+    *total_bytes = t;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_context_sm_count(ernie_cuda_context *ctx, int *sms)
+{
+    if (!ctx || !sms) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *sms = ctx->num_sms;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_malloc(ernie_cuda_context *ctx, size_t bytes, void **dev)
+{
+    if (!ctx || !dev) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(ctx->device);
+    *dev = nullptr;
+    return from_cuda(cudaMalloc(dev, bytes ? bytes : 1), "cudaMalloc");
+}
+
+extern "C" int ernie_cuda_free(ernie_cuda_context *ctx, void *dev)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    DeviceGuard guard(ctx->device);
+    return from_cuda(cudaFree(dev), "cudaFree");
+}
+
+extern "C" int ernie_cuda_upload(ernie_cuda_context *ctx, void *dev, const void *host, size_t bytes)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    DeviceGuard guard(ctx->device);
+    ERNIE_CUDA(cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "upload");
+    return from_cuda(cudaStreamSynchronize(ctx->stream), "upload");
+}
+
+extern "C" int ernie_cuda_download(ernie_cuda_context *ctx, void *host, const void *dev, size_t bytes)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    DeviceGuard guard(ctx->device);
+    ERNIE_CUDA(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, ctx->stream), "download");
+    return from_cuda(cudaStreamSynchronize(ctx->stream), "download");
+}
+
+extern "C" int ernie_cuda_memset(ernie_cuda_context *ctx, void *dev, int value, size_t bytes)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    DeviceGuard guard(ctx->device);
+    return from_cuda(cudaMemsetAsync(dev, value, bytes, ctx->stream), "memset");
+}
+
+extern "C" int ernie_cuda_event_record(ernie_cuda_context *ctx, int slot)
+{
+    if (!ctx || slot < 0 || slot >= 16) return fail(ERNIE_CUDA_ERROR, "bad event slot");
+    DeviceGuard guard(ctx->device);
+    return from_cuda(cudaEventRecord(ctx->events[slot], ctx->stream), "cudaEventRecord");
+}
+
+extern "C" int ernie_cuda_event_elapsed(ernie_cuda_context *ctx, int start_slot, int end_slot, float *ms)
+{
+    if (!ctx || !ms || start_slot < 0 || start_slot >= 16 || end_slot < 0 || end_slot >= 16)
+        return fail(ERNIE_CUDA_ERROR, "bad event slot");
+    DeviceGuard guard(ctx->device);
+    ERNIE_CUDA(cudaEventSynchronize(ctx->events[end_slot]), "cudaEventSynchronize");
+    return from_cuda(cudaEventElapsedTime(ms, ctx->events[start_slot], ctx->events[end_slot]), "cudaEventElapsedTime");
+}
+
+// ---------------------------------------------------------------- model
+extern "C" int ernie_cuda_model_create(ernie_cuda_context *ctx, int num_blocks, ernie_cuda_model **out)
+{
+    if (!ctx || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (num_blocks < 1 || num_blocks > 36) return fail(ERNIE_CUDA_ERROR, "Require 1..36 blocks");
+    DeviceGuard guard(ctx->device);
+    auto *model = new ernie_cuda_model();
+    model->ctx = ctx;
+    model->num_blocks = num_blocks;
+    model->blocks.resize(num_blocks);
+    for (int b = 0; b < num_blocks; ++b)
+    {
+        DevBlock &blk = model->blocks[b];
+        Arena arena;
+        arena.add(&blk.wqkv, size_t(3) * kHidden * kHidden);
+        arena.add(&blk.wo, size_t(kHidden) * kHidden);
+        arena.add(&blk.wug, size_t(2) * kFfn * kHidden);
+        arena.add(&blk.wfc2, size_t(kHidden) * kFfn);
+        arena.add(&blk.gamma_sa, kHidden);
+        arena.add(&blk.gamma_mlp, kHidden);
+        arena.add(&blk.gamma_q, kHeadDim);
+        arena.add(&blk.gamma_k, kHeadDim);
+        const cudaError_t e = arena.allocate();
+        if (e != cudaSuccess)
+        {
+            ernie_cuda_model_destroy(model);
+            return from_cuda(e, ("Allocate weights of block " + std::to_string(b)).c_str());
+        }
+        blk.alloc = arena.base;
+        model->bytes += arena.bytes();
+    }
+    DevHeads &hd = model->heads;
+    Arena arena;
+    arena.add(&hd.x_embed_w, size_t(kHidden) * kLatent);
+    arena.add(&hd.text_proj_w, size_t(kHidden) * kTextDim);
+    arena.add(&hd.time1_w, size_t(kHidden) * kHidden);
+    arena.add(&hd.time2_w, size_t(kHidden) * kHidden);
+    arena.add(&hd.adaln_w, size_t(6) * kHidden * kHidden);
+    arena.add(&hd.final_norm_w, size_t(2) * kHidden * kHidden);
+    arena.add(&hd.final_w, size_t(kLatent) * kHidden);
+    arena.add(&hd.x_embed_b, kHidden);
+    arena.add(&hd.time1_b, kHidden);
+    arena.add(&hd.time2_b, kHidden);
+    arena.add(&hd.adaln_b, 6 * kHidden);
+    arena.add(&hd.final_norm_b, 2 * kHidden);
+    arena.add(&hd.final_b, kLatent);
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess)
+    {
+        ernie_cuda_model_destroy(model);
+        return from_cuda(e, "Allocate head weights");
+    }
+    hd.alloc = arena.base;
+    model->bytes += arena.bytes();
+    *out = model;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_model_destroy(ernie_cuda_model *model)
+{
+    if (!model) return ERNIE_CUDA_OK;
+    DeviceGuard guard(model->ctx->device);
+    cudaStreamSynchronize(model->ctx->stream);
+    for (auto &b : model->blocks)
+        if (b.alloc) cudaFree(b.alloc);
+    if (model->heads.alloc) cudaFree(model->heads.alloc);
+    delete model;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_model_bytes(ernie_cuda_model *model, uint64_t *bytes)
+{
+    if (!model || !bytes) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *bytes = model->bytes;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_model_upload_block(ernie_cuda_model *model, int block, const ernie_cuda_block_weights *w)
+{
+    if (!model || !w || block < 0 || block >= model->num_blocks) return fail(ERNIE_CUDA_ERROR, "Invalid block upload");
+    if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wup || !w->wgate || !w->wfc2 || !w->gamma_sa || !w->gamma_mlp ||
+        !w->gamma_q || !w->gamma_k)
+        return fail(ERNIE_CUDA_ERROR, "Block weights must provide all 11 tensors");
+    DeviceGuard guard(model->ctx->device);
+    const DevBlock &b = model->blocks[block];
+    const size_t sq = size_t(kHidden) * kHidden * 2;
+    auto copy = [](void *dst, const void *src, size_t bytes) { return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice); };
+    ERNIE_CUDA(copy(b.wqkv, w->wq, sq), "upload wq");
+    ERNIE_CUDA(copy(b.wqkv + size_t(kHidden) * kHidden, w->wk, sq), "upload wk");
+    ERNIE_CUDA(copy(b.wqkv + size_t(2) * kHidden * kHidden, w->wv, sq), "upload wv");
+    ERNIE_CUDA(copy(b.wo, w->wo, sq), "upload wo");
+    const size_t group = size_t(128) * kHidden;
+    for (int g = 0; g < kFfn / 128; ++g)
+    {
+        ERNIE_CUDA(copy(b.wug + size_t(2 * g) * group, w->wup + size_t(g) * group, group * 2), "upload up");
+        ERNIE_CUDA(copy(b.wug + size_t(2 * g + 1) * group, w->wgate + size_t(g) * group, group * 2), "upload gate");
+    }
+    ERNIE_CUDA(copy(b.wfc2, w->wfc2, size_t(kHidden) * kFfn * 2), "upload fc2");
+    ERNIE_CUDA(copy(b.gamma_sa, w->gamma_sa, kHidden * 4), "upload gamma");
+    ERNIE_CUDA(copy(b.gamma_mlp, w->gamma_mlp, kHidden * 4), "upload gamma");
+    ERNIE_CUDA(copy(b.gamma_q, w->gamma_q, kHeadDim * 4), "upload gamma");
+    ERNIE_CUDA(copy(b.gamma_k, w->gamma_k, kHeadDim * 4), "upload gamma");
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_model_upload_heads(ernie_cuda_model *model, const ernie_cuda_head_weights *w)
+{
+    if (!model || !w) return fail(ERNIE_CUDA_ERROR, "Invalid head upload");
+    DeviceGuard guard(model->ctx->device);
+    const DevHeads &h = model->heads;
+    struct Item { void *dst; const void *src; size_t bytes; };
+    const Item items[] = {
+        {h.x_embed_w, w->x_embed_w, size_t(kHidden) * kLatent * 2},
+        {h.text_proj_w, w->text_proj_w, size_t(kHidden) * kTextDim * 2},
+        {h.time1_w, w->time1_w, size_t(kHidden) * kHidden * 2},
+        {h.time2_w, w->time2_w, size_t(kHidden) * kHidden * 2},
+        {h.adaln_w, w->adaln_w, size_t(6) * kHidden * kHidden * 2},
+        {h.final_norm_w, w->final_norm_w, size_t(2) * kHidden * kHidden * 2},
+        {h.final_w, w->final_w, size_t(kLatent) * kHidden * 2},
+        {h.x_embed_b, w->x_embed_b, kHidden * 4},
+        {h.time1_b, w->time1_b, kHidden * 4},
+        {h.time2_b, w->time2_b, kHidden * 4},
+        {h.adaln_b, w->adaln_b, 6 * kHidden * 4},
+        {h.final_norm_b, w->final_norm_b, 2 * kHidden * 4},
+        {h.final_b, w->final_b, kLatent * 4},
+    };
+    for (const auto &it : items)
+    {
+        if (!it.src) return fail(ERNIE_CUDA_ERROR, "Head weights must provide all 13 tensors");
+        ERNIE_CUDA(cudaMemcpy(it.dst, it.src, it.bytes, cudaMemcpyHostToDevice), "upload head tensor");
+    }
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_model_synthesize(ernie_cuda_model *model, uint64_t seed)
+{
+    if (!model) return fail(ERNIE_CUDA_ERROR, "null model");
+    DeviceGuard guard(model->ctx->device);
+    cudaStream_t s = model->ctx->stream;
+    const float std = ERNIE_SYNTH_WEIGHT_STD;
+    const long long H = kHidden;
+    for (int b = 0; b < model->num_blocks; ++b)
+    {
+        const DevBlock &d = model->blocks[b];
+        auto sid = [b](int t) { return static_cast<uint64_t>(ERNIE_SYNTH_BLOCK_STREAM(b, t)); };
+        // [Wq; Wk; Wv]: each tensor is one group placed at its row offset.
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WQ), std, 0.f, H, kHidden, kHidden, 0, 0, d.wqkv, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WK), std, 0.f, H, kHidden, kHidden, 0, H, d.wqkv, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WV), std, 0.f, H, kHidden, kHidden, 0, 2 * H, d.wqkv, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WO), std, 0.f, H, kHidden, kHidden, 0, 0, d.wo, s), "synth");
+        // up/gate interleaved in 128-row groups
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WUP), std, 0.f, kFfn, kHidden, 128, 256, 0, d.wug, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WGATE), std, 0.f, kFfn, kHidden, 128, 256, 128, d.wug, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WFC2), std, 0.f, H, kFfn, kHidden, 0, 0, d.wfc2, s), "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_SA), std, 1.f, kHidden, d.gamma_sa, s), "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_MLP), std, 1.f, kHidden, d.gamma_mlp, s), "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_Q), std, 1.f, kHeadDim, d.gamma_q, s), "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_K), std, 1.f, kHeadDim, d.gamma_k, s), "synth");
+    }
+    const DevHeads &h = model->heads;
+    auto mat = [&](int id, __nv_bfloat16 *dst, long long rows, int cols) {
+        return launch_synth_bf16(seed, id, std, 0.f, rows, cols, static_cast<int>(rows), 0, 0, dst, s);
+    };
+    auto vec = [&](int id, float *dst, long long n) { return launch_synth_f32_bf16(seed, id, std, 0.f, n, dst, s); };
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_X_EMBED_W, h.x_embed_w, H, kLatent), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_TEXT_PROJ_W, h.text_proj_w, H, kTextDim), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_TIME1_W, h.time1_w, H, kHidden), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_TIME2_W, h.time2_w, H, kHidden), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_ADALN_W, h.adaln_w, 6 * H, kHidden), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_FINAL_NORM_W, h.final_norm_w, 2 * H, kHidden), "synth");
+    ERNIE_LAUNCH(mat(ERNIE_SYNTH_FINAL_W, h.final_w, kLatent, kHidden), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_X_EMBED_B, h.x_embed_b, H), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_TIME1_B, h.time1_b, H), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_TIME2_B, h.time2_b, H), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_ADALN_B, h.adaln_b, 6 * H), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_FINAL_NORM_B, h.final_norm_b, 2 * H), "synth");
+    ERNIE_LAUNCH(vec(ERNIE_SYNTH_FINAL_B, h.final_b, kLatent), "synth");
+    return from_cuda(cudaStreamSynchronize(s), "synthesize weights");
+}
+
+extern "C" int ernie_cuda_model_read_tensor(ernie_cuda_model *model, int block, int tensor, void *host, size_t bytes)
+{
+    if (!model || !host || block < 0 || block >= model->num_blocks) return fail(ERNIE_CUDA_ERROR, "Invalid tensor read");
+    const DevBlock &b = model->blocks[block];
+    const void *src = nullptr;
+    size_t size = 0;
+    switch (tensor)
+    {
+    case ERNIE_TENSOR_WQKV: src = b.wqkv; size = size_t(3) * kHidden * kHidden * 2; break;
+    case ERNIE_TENSOR_WO: src = b.wo; size = size_t(kHidden) * kHidden * 2; break;
+    case ERNIE_TENSOR_WUPGATE: src = b.wug; size = size_t(2) * kFfn * kHidden * 2; break;
+    case ERNIE_TENSOR_WFC2: src = b.wfc2; size = size_t(kHidden) * kFfn * 2; break;
+    default: return fail(ERNIE_CUDA_ERROR, "Unknown tensor id");
+    }
+    if (bytes > size) return fail(ERNIE_CUDA_ERROR, "Read exceeds tensor size");
+    DeviceGuard guard(model->ctx->device);
+    ERNIE_CUDA(cudaStreamSynchronize(model->ctx->stream), "sync");
+    return from_cuda(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost), "read tensor");
+}
+
+// ---------------------------------------------------------------- layer operators
+extern "C" int ernie_cuda_sdpa(ernie_cuda_context *ctx, const float *q, const float *k, const float *v,
+                               const float *mask, int heads, int kv_heads, int mask_heads, int mask_rows, int nq,
+                               int nk, int width, float *out)
+{
+    if (!ctx || !q || !k || !v || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (heads < 1 || nq < 1 || nk < 1 || width < 1 || width > 128 || (kv_heads != 1 && kv_heads != heads) ||
+        (mask && ((mask_heads != 1 && mask_heads != heads) || (mask_rows != 1 && mask_rows != nq))))
+        return fail(ERNIE_CUDA_ERROR, "Invalid SDPA shapes");
+    DeviceGuard guard(ctx->device);
+    AttentionF32Args a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.mask = mask;
+    a.heads = heads;
+    a.kv_heads = kv_heads;
+    a.mask_heads = mask_heads;
+    a.mask_rows = mask_rows;
+    a.nq = nq;
+    a.nk = nk;
+    a.kv_len = nk;
+    a.width = width;
+    a.q_head_stride = static_cast<long long>(nq) * width;
+    a.kv_head_stride = static_cast<long long>(nk) * width;
+    a.out_mode = 0;
+    a.out_f32 = out;
+    return from_launch(launch_attention_f32(a, ctx->stream), "SDPA");
+}
+
+extern "C" int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                                    const float *mask, int heads, int nq, int rows_pad, int kv_len, uint16_t *out)
+{
+    if (!ctx || !q || !k || !v || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_attention_bf16(reinterpret_cast<const __nv_bfloat16 *>(q),
+                                             reinterpret_cast<const __nv_bfloat16 *>(k),
+                                             reinterpret_cast<const __nv_bfloat16 *>(v), mask, nq, rows_pad, kv_len,
+                                             heads, reinterpret_cast<__nv_bfloat16 *>(out), ctx->stream),
+                       "SDPA bf16");
+}
+
+extern "C" int ernie_cuda_set_attention_query_rows(ernie_cuda_context *ctx, int rows)
+{
+    if (!ctx) return fail(ERNIE_CUDA_ERROR, "null context");
+    if (rows != 128 && rows != 64 && rows != 32 && rows != 16)
+        return fail(ERNIE_CUDA_ERROR, "Attention query rows must be 128, 64, 32 or 16");
+    ctx->query_rows = rows;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_attention_query_rows(ernie_cuda_context *ctx, int *rows)
+{
+    if (!ctx || !rows) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *rows = ctx->query_rows;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_rmsnorm(ernie_cuda_context *ctx, const float *x, const float *gamma, int64_t rows, int width,
+                                  float eps, float *out)
+{
+    if (!ctx || !x || !gamma || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (width != 128 && width != 3072 && width != 4096) return fail(ERNIE_CUDA_ERROR, "RMSNorm width must be 128, 3072 or 4096");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_rmsnorm(x, gamma, rows, width, eps, 0, out, ctx->stream), "RMSNorm");
+}
+
+extern "C" int ernie_cuda_layernorm(ernie_cuda_context *ctx, const float *x, int64_t rows, int width, float eps,
+                                    float *out)
+{
+    if (!ctx || !x || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (width != 4096) return fail(ERNIE_CUDA_ERROR, "LayerNorm width must be 4096");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_rmsnorm(x, nullptr, rows, width, eps, 1, out, ctx->stream), "LayerNorm");
+}
+
+extern "C" int ernie_cuda_gelu(ernie_cuda_context *ctx, float *data, int64_t count)
+{
+    if (!ctx || !data) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (count % 4) return fail(ERNIE_CUDA_ERROR, "ErnieGELU element count must be divisible by four");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_gelu(data, count, ctx->stream), "GELU");
+}
+
+extern "C" int ernie_cuda_residual_add(ernie_cuda_context *ctx, const float *a, const float *b, float *out, int64_t count)
+{
+    if (!ctx || !a || !b || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_residual_add(a, b, out, count, ctx->stream), "ResidualAdd");
+}
+
+extern "C" int ernie_cuda_linear_bf16(ernie_cuda_context *ctx, const uint16_t *a, const uint16_t *w, const float *bias,
+                                      float *c, int m, int n, int k)
+{
+    if (!ctx || !a || !w || !c) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (m < 1 || n % 128 || k % 64 || k < 64) return fail(ERNIE_CUDA_ERROR, "Linear needs N % 128 == 0 and K % 64 == 0");
+    DeviceGuard guard(ctx->device);
+    GemmEpilogueArgs args;
+    args.out = c;
+    args.ldo = n;
+    args.bias = bias;
+    args.error_flag = ctx->error_flag;
+    return from_launch(launch_gemm(reinterpret_cast<const __nv_bfloat16 *>(a), reinterpret_cast<const __nv_bfloat16 *>(w),
+                                   m, n, k, 1, n % 256 == 0 ? 256 : 128, Epilogue::F32Bias, args, ctx->num_sms,
+                                   ctx->stream),
+                       "Linear");
+}
+
+// ---------------------------------------------------------------- latent ops
+static bool latent_shape_ok(int w, int h) { return w >= 1 && h >= 1 && w <= 256 && h <= 256; }
+
+extern "C" int ernie_cuda_euler_step(ernie_cuda_context *ctx, const float *sample, const float *prediction, float delta,
+                                     int width, int height, float *out)
+{
+    if (!ctx || !sample || !prediction || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!latent_shape_ok(width, height) || !std::isfinite(delta) || delta >= 0.f || delta < -1.f)
+        return fail(ERNIE_CUDA_ERROR, "Incompatible Euler shapes or delta outside [-1,0)");
+    DeviceGuard guard(ctx->device);
+    return from_launch(launch_euler(sample, prediction, delta, 128LL * width * height, out, ctx->stream), "Euler");
+}
+
+extern "C" int ernie_cuda_finite_latent(ernie_cuda_context *ctx, const float *latent, int width, int height, int *finite)
+{
+    if (!ctx || !latent || !finite) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!latent_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Expected [128,H,W] latent with 1 <= H,W <= 256");
+    DeviceGuard guard(ctx->device);
+    int *d_flag = nullptr;
+    ERNIE_CUDA(cudaMallocAsync(&d_flag, sizeof(int), ctx->stream), "alloc flag");
+    ERNIE_CUDA(cudaMemsetAsync(d_flag, 0, sizeof(int), ctx->stream), "memset flag");
+    ERNIE_LAUNCH(launch_finite(latent, 128LL * width * height, d_flag, ctx->stream), "finite");
+    int host = 0;
+    ERNIE_CUDA(cudaMemcpyAsync(&host, d_flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "read flag");
+    ERNIE_CUDA(cudaFreeAsync(d_flag, ctx->stream), "free flag");
+    ERNIE_CUDA(cudaStreamSynchronize(ctx->stream), "finite");
+    *finite = host ? 0 : 1;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_unpack_for_vae(ernie_cuda_context *ctx, const float *packed, const float *mean,
+                                         const float *variance, int width, int height, float *out)
+{
+    if (!ctx || !packed || !mean || !variance || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!latent_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Expected [128,H,W] latent with 1 <= H,W <= 256");
+    DeviceGuard guard(ctx->device);
+    // BN statistics are validated on the host as the reference requires (src/latent_ops.h:35-36);
+    // the device copy is checked here with one small download.
+    float m[128], var[128];
+    ERNIE_CUDA(cudaMemcpyAsync(m, mean, sizeof(m), cudaMemcpyDeviceToHost, ctx->stream), "read BN mean");
+    ERNIE_CUDA(cudaMemcpyAsync(var, variance, sizeof(var), cudaMemcpyDeviceToHost, ctx->stream), "read BN variance");
+    ERNIE_CUDA(cudaStreamSynchronize(ctx->stream), "read BN statistics");
+    for (int c = 0; c < 128; ++c)
+        if (!std::isfinite(m[c]) || !std::isfinite(var[c]) || var[c] < 0.f)
+            return fail(ERNIE_CUDA_ERROR, "Invalid BN statistics");
+    return from_launch(launch_unpack_for_vae(packed, mean, variance, width, height, out, ctx->stream), "unpack");
+}
+
+extern "C" int ernie_cuda_schedule(int steps, int schedule, float *sigmas, float *timesteps)
+{
+    if (!sigmas || !timesteps) return fail(ERNIE_CUDA_ERROR, "null argument");
+    return host_schedule(steps, schedule, sigmas, timesteps);
+}
+
+extern "C" int ernie_cuda_timestep_features(float timestep, float *out)
+{
+    if (!out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    return host_features(timestep, out);
+}
+
+extern "C" int ernie_cuda_dit_constants(const float *freq64, int w, int h, int valid, int text, int token_limit,
+                                        float *cos_out, float *sin_out, float *mask_out)
+{
+    if (!cos_out || !sin_out || !mask_out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (w < 1 || w > 256 || h < 1 || h > 256 || valid < 1 || text < valid || text > 2048 || w * h + text > token_limit)
+        return fail(ERNIE_CUDA_ERROR, "Invalid DiT position dimensions or frequency file");
+    float freq[64];
+    if (freq64) std::memcpy(freq, freq64, sizeof(freq));
+    else official_frequencies(freq);
+    for (float f : freq)
+        if (!std::isfinite(f) || f <= 0.f) return fail(ERNIE_CUDA_ERROR, "Invalid DiT frequency");
+    const int image = w * h, length = image + text;
+    for (int i = 0; i < length; ++i)
+    {
+        const int positions[3] = {i < image ? valid : i - image, i < image ? i / w : 0, i < image ? i % w : 0};
+        float *c = cos_out + size_t(i) * 128;
+        float *s = sin_out + size_t(i) * 128;
+        for (int j = 0; j < 64; ++j)
+        {
+            const int axis = j < 16 ? 0 : j < 40 ? 1 : 2;
+            const float phase = float(positions[axis]) * freq[j];
+            c[2 * j] = c[2 * j + 1] = std::cos(phase);
+            s[2 * j] = s[2 * j + 1] = std::sin(phase);
+        }
+    }
+    for (int k = 0; k < length; ++k) mask_out[k] = k >= image + valid ? -1e30f : 0.f;
+    return ERNIE_CUDA_OK;
+}
+
+// ---------------------------------------------------------------- session
+extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
+                                         ernie_cuda_session **out)
+{
+    if (!model || !shape || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *out = nullptr;
+    if (!latent_shape_ok(shape->width, shape->height) || shape->text_tokens < 1 || shape->text_tokens > 2048 ||
+        shape->valid_text < 1 || shape->valid_text > shape->text_tokens ||
+        shape->width * shape->height + shape->text_tokens > 10240)
+        return fail(ERNIE_CUDA_ERROR, "Invalid DiT shape (w,h in 1..256, text 1..2048, tokens <= 10240)");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    ernie_cuda_context *ctx = model->ctx;
+    DeviceGuard guard(ctx->device);
+    auto *s = new ernie_cuda_session();
+    s->model = model;
+    s->ctx = ctx;
+    s->width = shape->width;
+    s->height = shape->height;
+    s->text = shape->text_tokens;
+    s->valid = shape->valid_text;
+    s->precision = precision;
+    s->splits = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    s->image = s->width * s->height;
+    s->tokens = s->image + s->text;
+    s->rows_pad = (s->tokens + 127) / 128 * 128;
+    s->kv_len = s->image + s->valid;
+    const size_t T = s->tokens, P = s->rows_pad, qkv_elem = precision == ERNIE_PRECISION_FP32 ? 4 : 2;
+    Arena arena;
+    arena.add(&s->x, T * kHidden);
+    arena.add(&s->text_cache, size_t(s->text) * kHidden);
+    arena.add(&s->cos_t, T * kHeadDim);
+    arena.add(&s->sin_t, T * kHeadDim);
+    arena.add(&s->mask, T);
+    arena.add(&s->latent, size_t(kLatent) * s->image);
+    arena.add(&s->scratch_latent, size_t(kLatent) * s->image);
+    arena.add(&s->pred, size_t(kLatent) * s->image);
+    arena.add(&s->g1, kHidden);
+    arena.add(&s->c, kHidden);
+    arena.add(&s->mod, 6 * kHidden);
+    arena.add(&s->ss, 2 * kHidden);
+    arena.add(&s->a, T * kHidden * s->splits);
+    arena.add(&s->h, T * kFfn * s->splits);
+    arena.add(reinterpret_cast<char **>(&s->q), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    arena.add(reinterpret_cast<char **>(&s->k), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    arena.add(reinterpret_cast<char **>(&s->v), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    cudaError_t e = arena.allocate();
+    if (e == cudaSuccess) e = cudaMemset(arena.base, 0, arena.bytes());
+    if (e == cudaSuccess) e = cudaMallocHost(&s->pinned, sizeof(float) * kLatent * s->image);
+    if (e != cudaSuccess)
+    {
+        s->alloc = arena.base;
+        ernie_cuda_session_destroy(s);
+        return from_cuda(e, "Allocate session activations");
+    }
+    s->alloc = arena.base;
+    *out = s;
+    return ERNIE_CUDA_OK;
+}
+
+static void release_graphs(ernie_cuda_session *s)
+{
+    for (auto &g : s->graphs) cudaGraphExecDestroy(g.second);
+    s->graphs.clear();
+}
+
+extern "C" int ernie_cuda_session_destroy(ernie_cuda_session *s)
+{
+    if (!s) return ERNIE_CUDA_OK;
+    DeviceGuard guard(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+    release_graphs(s);
+    if (s->alloc) cudaFree(s->alloc);
+    if (s->features) cudaFree(s->features);
+    if (s->flags) cudaFree(s->flags);
+    if (s->preds) cudaFree(s->preds);
+    if (s->pinned) cudaFreeHost(s->pinned);
+    delete s;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_tokens(ernie_cuda_session *s, int *tokens)
+{
+    if (!s || !tokens) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *tokens = s->tokens;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_latent(ernie_cuda_session *s, float **latent_dev)
+{
+    if (!s || !latent_dev) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *latent_dev = s->latent;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const float *text, const float *cos_table,
+                                                   const float *sin_table, const float *mask)
+{
+    if (!s || !cos_table || !sin_table || !mask) return fail(ERNIE_CUDA_ERROR, "Require cosine, sine and mask");
+    DeviceGuard guard(s->ctx->device);
+    cudaStream_t st = s->ctx->stream;
+    const size_t T = s->tokens;
+    // Valid key count from the additive row mask: keys past the last visible one contribute zero.
+    int last = -1;
+    bool general = false;
+    for (size_t k = 0; k < T; ++k)
+    {
+        if (!(mask[k] <= 0.f) || std::isnan(mask[k])) return fail(ERNIE_CUDA_ERROR, "Mask values must be <= 0");
+        if (mask[k] > -1e29f) last = static_cast<int>(k);
+    }
+    if (last < 0) return fail(ERNIE_CUDA_ERROR, "Mask hides every key");
+    for (int k = 0; k <= last; ++k)
+        if (mask[k] != 0.f) general = true;
+    s->kv_len = last + 1;
+    s->use_mask = general;
+    ERNIE_CUDA(cudaMemcpyAsync(s->cos_t, cos_table, T * kHeadDim * 4, cudaMemcpyHostToDevice, st), "upload cos");
+    ERNIE_CUDA(cudaMemcpyAsync(s->sin_t, sin_table, T * kHeadDim * 4, cudaMemcpyHostToDevice, st), "upload sin");
+    ERNIE_CUDA(cudaMemcpyAsync(s->mask, mask, T * 4, cudaMemcpyHostToDevice, st), "upload mask");
+    s->has_text = text != nullptr;
+    if (text)
+    {
+        // text_proj once per request (text is constant across steps): FP32 -> operand -> GEMM.
+        float *staging = s->x; // [text][3072] fits in the [tokens][4096] residual buffer
+        ERNIE_CUDA(cudaMemcpyAsync(staging, text, size_t(s->text) * kTextDim * 4, cudaMemcpyHostToDevice, st), "upload text");
+        ERNIE_LAUNCH(launch_to_operand(staging, s->text, kTextDim, s->a, s->splits == 3, st), "text operand");
+        GemmEpilogueArgs args;
+        args.out = s->text_cache;
+        args.ldo = kHidden;
+        args.error_flag = s->ctx->error_flag;
+        ERNIE_LAUNCH(launch_gemm(s->a, s->model->heads.text_proj_w, s->text, kHidden, kTextDim, s->splits, 256,
+                                 Epilogue::F32Bias, args, s->ctx->num_sms, st),
+                     "text_proj");
+    }
+    ERNIE_CUDA(cudaStreamSynchronize(st), "set conditioning");
+    release_graphs(s);
+    s->conditioned = true;
+    return ERNIE_CUDA_OK;
+}
+
+// One DiT block on x [tokens][4096] (block.ncnn.param:14-76), 7 launches.
+// `only` >= 0 enqueues just that part (0 norm sa, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 norm mlp,
+// 5 up/gate GEMM, 6 down GEMM); used by the benchmark's per-kernel timing.
+static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mod, int only = -1)
+{
+    auto on = [only](int part) { return only < 0 || only == part; };
+    const DevBlock &w = s->model->blocks[b];
+    cudaStream_t st = s->ctx->stream;
+    const int T = s->tokens, sp = s->splits, nsm = s->ctx->num_sms;
+    const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
+    const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
+    const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
+    if (on(0))
+        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_sa, scale_sa, shift_sa, 1e-6f, 0, s->a, fp32, st), "norm sa");
+    GemmEpilogueArgs qkv;
+    qkv.q = s->q;
+    qkv.k = s->k;
+    qkv.v = s->v;
+    qkv.rows_pad = s->rows_pad;
+    qkv.qkv_fp32 = fp32;
+    qkv.gamma_q = w.gamma_q;
+    qkv.gamma_k = w.gamma_k;
+    qkv.cos_t = s->cos_t;
+    qkv.sin_t = s->sin_t;
+    qkv.error_flag = s->ctx->error_flag;
+    if (on(1)) ERNIE_LAUNCH(launch_gemm(s->a, w.wqkv, T, 3 * kHidden, kHidden, sp, 256, Epilogue::Qkv, qkv, nsm, st), "qkv");
+    if (!on(2)) {}
+    else if (fp32)
+    {
+        AttentionF32Args a{};
+        a.q = static_cast<const float *>(s->q);
+        a.k = static_cast<const float *>(s->k);
+        a.v = static_cast<const float *>(s->v);
+        a.mask = s->use_mask ? s->mask : nullptr;
+        a.heads = kHeads;
+        a.kv_heads = kHeads;
+        a.mask_heads = 1;
+        a.mask_rows = 1;
+        a.nq = T;
+        a.nk = T;
+        a.kv_len = s->kv_len;
+        a.width = kHeadDim;
+        a.q_head_stride = static_cast<long long>(s->rows_pad) * kHeadDim;
+        a.kv_head_stride = a.q_head_stride;
+        a.out_mode = 1;
+        a.out_split3 = s->a;
+        ERNIE_LAUNCH(launch_attention_f32(a, st), "attention");
+    }
+    else
+        ERNIE_LAUNCH(launch_attention_bf16(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
+                                           static_cast<const __nv_bfloat16 *>(s->v), s->use_mask ? s->mask : nullptr, T,
+                                           s->rows_pad, s->kv_len, kHeads, s->a, st),
+                     "attention");
+    GemmEpilogueArgs res;
+    res.resid = x;
+    res.ldo = kHidden;
+    res.gate = gate_sa;
+    res.error_flag = s->ctx->error_flag;
+    if (on(3)) ERNIE_LAUNCH(launch_gemm(s->a, w.wo, T, kHidden, kHidden, sp, 128, Epilogue::ResidGate, res, nsm, st), "out proj");
+    if (on(4))
+        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
+    GemmEpilogueArgs gg;
+    gg.h = s->h;
+    gg.h_split3 = fp32;
+    gg.ffn = kFfn;
+    gg.error_flag = s->ctx->error_flag;
+    if (on(5)) ERNIE_LAUNCH(launch_gemm(s->a, w.wug, T, 2 * kFfn, kHidden, sp, 256, Epilogue::Geglu, gg, nsm, st), "up/gate");
+    res.gate = gate_mlp;
+    if (on(6)) ERNIE_LAUNCH(launch_gemm(s->h, w.wfc2, T, kHidden, kFfn, sp, 128, Epilogue::ResidGate, res, nsm, st), "down");
+    return ERNIE_CUDA_OK;
+}
+
+// Input head + 36 blocks + output head + Euler for one step (run_dit + euler_step).
+static int enqueue_step(ernie_cuda_session *s, float *latent, const float *features, float delta, float *prediction,
+                        int *finite_flag)
+{
+    const DevHeads &hd = s->model->heads;
+    cudaStream_t st = s->ctx->stream;
+    const int nsm = s->ctx->num_sms, sp = s->splits;
+    const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
+    // input head: image rows (x_embedder) and text rows (cached text_proj)
+    if (s->has_text)
+        ERNIE_CUDA(cudaMemcpyAsync(s->x + size_t(s->image) * kHidden, s->text_cache, size_t(s->text) * kHidden * 4,
+                                   cudaMemcpyDeviceToDevice, st),
+                   "text rows");
+    else
+        ERNIE_CUDA(cudaMemsetAsync(s->x + size_t(s->image) * kHidden, 0, size_t(s->text) * kHidden * 4, st), "text rows");
+    ERNIE_LAUNCH(launch_latent_to_tokens(latent, s->image, s->a, fp32, st), "latent operand");
+    GemmEpilogueArgs emb;
+    emb.out = s->x;
+    emb.ldo = kHidden;
+    emb.bias = hd.x_embed_b;
+    emb.error_flag = s->ctx->error_flag;
+    ERNIE_LAUNCH(launch_gemm(s->a, hd.x_embed_w, s->image, kHidden, kLatent, sp, 256, Epilogue::F32Bias, emb, nsm, st),
+                 "x_embedder");
+    ERNIE_LAUNCH(launch_gemv(hd.time1_w, features, hd.time1_b, s->g1, kHidden, kHidden, 0, st), "time linear_1");
+    ERNIE_LAUNCH(launch_gemv(hd.time2_w, s->g1, hd.time2_b, s->c, kHidden, kHidden, 1, st), "time linear_2");
+    ERNIE_LAUNCH(launch_gemv(hd.adaln_w, s->c, hd.adaln_b, s->mod, 6 * kHidden, kHidden, 1, st), "adaLN");
+    ERNIE_LAUNCH(launch_gemv(hd.final_norm_w, s->c, hd.final_norm_b, s->ss, 2 * kHidden, kHidden, 0, st), "final norm linear");
+    for (int b = 0; b < s->model->num_blocks; ++b) ERNIE_TRY(enqueue_block(s, b, s->x, s->mod));
+    // output head: LayerNorm + modulate on image rows, linear + bias, fused Euler update
+    ERNIE_LAUNCH(launch_norm_modulate(s->x, s->image, kHidden, nullptr, s->ss, s->ss + kHidden, 1e-6f, 1, s->a, fp32, st),
+                 "final norm");
+    GemmEpilogueArgs fin;
+    fin.bias = hd.final_b;
+    fin.latent = latent;
+    fin.prediction = prediction;
+    fin.delta = delta;
+    fin.finite_flag = finite_flag;
+    fin.error_flag = s->ctx->error_flag;
+    ERNIE_LAUNCH(launch_gemm(s->a, hd.final_w, s->image, kLatent, kHidden, sp, 128, Epilogue::FinalEuler, fin, nsm, st),
+                 "final linear + Euler");
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_blocks(ernie_cuda_session *s, int first, int count, float *x, const float *modulation)
+{
+    if (!s || !x || !modulation) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs its nine constants (set_conditioning)");
+    if (first < 0 || count < 1 || first + count > s->model->num_blocks) return fail(ERNIE_CUDA_ERROR, "Require 1..36 blocks");
+    DeviceGuard guard(s->ctx->device);
+    for (int b = first; b < first + count; ++b) ERNIE_TRY(enqueue_block(s, b, x, modulation));
+    return ERNIE_CUDA_OK;
+}
+
+static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, bool predictions)
+{
+    if (s->feature_capacity < steps)
+    {
+        if (s->features) cudaFree(s->features);
+        if (s->flags) cudaFree(s->flags);
+        s->features = nullptr;
+        s->flags = nullptr;
+        s->feature_capacity = 0;
+        ERNIE_CUDA(cudaMalloc(&s->features, size_t(steps) * kHidden * 4), "Allocate time features");
+        ERNIE_CUDA(cudaMalloc(&s->flags, size_t(steps) * sizeof(int)), "Allocate finite flags");
+        s->feature_capacity = steps;
+        s->feature_key = {-1, -1};
+        release_graphs(s);
+    }
+    if (predictions && s->pred_capacity < steps)
+    {
+        if (s->preds) cudaFree(s->preds);
+        s->preds = nullptr;
+        s->pred_capacity = 0;
+        ERNIE_CUDA(cudaMalloc(&s->preds, size_t(steps) * kLatent * s->image * 4), "Allocate predictions");
+        s->pred_capacity = steps;
+        release_graphs(s);
+    }
+    if (s->feature_key != std::make_tuple(steps, schedule))
+    {
+        std::vector<float> sigmas(steps + 1), timesteps(steps), features(size_t(steps) * kHidden);
+        ERNIE_TRY(host_schedule(steps, schedule, sigmas.data(), timesteps.data()));
+        s->deltas.resize(steps);
+        for (int i = 0; i < steps; ++i)
+        {
+            s->deltas[i] = sigmas[i + 1] - sigmas[i];
+            ERNIE_TRY(host_features(timesteps[i], features.data() + size_t(i) * kHidden));
+        }
+        ERNIE_CUDA(cudaMemcpy(s->features, features.data(), features.size() * 4, cudaMemcpyHostToDevice), "upload features");
+        s->feature_key = {steps, schedule};
+    }
+    return ERNIE_CUDA_OK;
+}
+
+static int enqueue_range(ernie_cuda_session *s, int start, int end, bool predictions)
+{
+    cudaStream_t st = s->ctx->stream;
+    ERNIE_CUDA(cudaMemsetAsync(s->flags + start, 0, size_t(end - start) * sizeof(int), st), "clear finite flags");
+    for (int i = start; i < end; ++i)
+    {
+        float *pred = predictions ? s->preds + size_t(i) * kLatent * s->image : nullptr;
+        ERNIE_TRY(enqueue_step(s, s->latent, s->features + size_t(i) * kHidden, s->deltas[i], pred, s->flags + i));
+    }
+    return ERNIE_CUDA_OK;
+}
+
+static int run_range(ernie_cuda_session *s, int steps, int start, int end, int schedule, bool use_graph,
+                     bool predictions, int *failed_step)
+{
+    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Require four constants (set_conditioning)");
+    if (start < 0 || start > steps || end < start || end > steps)
+        return fail(ERNIE_CUDA_ERROR, "Denoising start step must be in [0,steps]");
+    ERNIE_TRY(ensure_step_buffers(s, steps, schedule, predictions));
+    if (failed_step) *failed_step = 0;
+    if (end == start) return ERNIE_CUDA_OK;
+    cudaStream_t st = s->ctx->stream;
+    if (use_graph)
+    {
+        const auto key = std::make_tuple(steps, start, end, schedule, predictions ? 1 : 0);
+        auto it = s->graphs.find(key);
+        if (it == s->graphs.end())
+        {
+            ERNIE_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "Begin graph capture");
+            const int rc = enqueue_range(s, start, end, predictions);
+            cudaGraph_t graph = nullptr;
+            const cudaError_t end_e = cudaStreamEndCapture(st, &graph);
+            if (rc != ERNIE_CUDA_OK)
+            {
+                if (graph) cudaGraphDestroy(graph);
+                return rc;
+            }
+            ERNIE_CUDA(end_e, "End graph capture");
+            cudaGraphExec_t exec = nullptr;
+            const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            ERNIE_CUDA(inst, "Instantiate graph");
+            it = s->graphs.emplace(key, exec).first;
+        }
+        ERNIE_CUDA(cudaGraphLaunch(it->second, st), "Launch graph");
+    }
+    else
+        ERNIE_TRY(enqueue_range(s, start, end, predictions));
+    std::vector<int> flags(end - start);
+    ERNIE_CUDA(cudaMemcpyAsync(flags.data(), s->flags + start, flags.size() * sizeof(int), cudaMemcpyDeviceToHost, st),
+               "read finite flags");
+    ERNIE_TRY(ernie_cuda_context_synchronize(s->ctx));
+    for (int i = start; i < end; ++i)
+        if (flags[i - start])
+        {
+            if (failed_step) *failed_step = i + 1;
+            return fail(ERNIE_CUDA_ERROR, "Non-finite latent after denoise step " + std::to_string(i + 1));
+        }
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_denoise_device(ernie_cuda_session *s, int steps, int start_step, int end_step,
+                                                 int schedule, int use_graph, int *failed_step)
+{
+    if (!s) return fail(ERNIE_CUDA_ERROR, "null session");
+    DeviceGuard guard(s->ctx->device);
+    return run_range(s, steps, start_step, end_step, schedule, use_graph != 0, false, failed_step);
+}
+
+extern "C" int ernie_cuda_session_denoise(ernie_cuda_session *s, const float *initial, float *final_latent, int steps,
+                                          int start_step, int end_step, int schedule, float *predictions,
+                                          int *failed_step)
+{
+    if (!s || !initial || !final_latent) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(s->ctx->device);
+    const size_t count = size_t(kLatent) * s->image;
+    for (size_t i = 0; i < count; ++i)
+        if (!std::isfinite(initial[i])) return fail(ERNIE_CUDA_ERROR, "Initial latent is not finite");
+    cudaStream_t st = s->ctx->stream;
+    std::memcpy(s->pinned, initial, count * 4);
+    ERNIE_CUDA(cudaMemcpyAsync(s->latent, s->pinned, count * 4, cudaMemcpyHostToDevice, st), "upload latent");
+    const int rc = run_range(s, steps, start_step, end_step, schedule, true, predictions != nullptr, failed_step);
+    if (rc != ERNIE_CUDA_OK) return rc;
+    ERNIE_CUDA(cudaMemcpyAsync(s->pinned, s->latent, count * 4, cudaMemcpyDeviceToHost, st), "download latent");
+    if (predictions && end_step > start_step)
+        ERNIE_CUDA(cudaMemcpyAsync(predictions, s->preds + size_t(start_step) * count,
+                                   size_t(end_step - start_step) * count * 4, cudaMemcpyDeviceToHost, st),
+                   "download predictions");
+    ERNIE_CUDA(cudaStreamSynchronize(st), "denoise");
+    std::memcpy(final_latent, s->pinned, count * 4);
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent, float timestep, float *prediction)
+{
+    if (!s || !latent || !prediction) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Require six DiT inputs (set_conditioning)");
+    DeviceGuard guard(s->ctx->device);
+    std::vector<float> features(kHidden);
+    ERNIE_TRY(host_features(timestep, features.data()));
+    ERNIE_TRY(ensure_step_buffers(s, 1, ERNIE_SCHEDULE_TURBO, false));
+    cudaStream_t st = s->ctx->stream;
+    s->feature_key = {-1, -1}; // features[0] is overwritten below
+    ERNIE_CUDA(cudaMemcpyAsync(s->features, features.data(), kHidden * 4, cudaMemcpyHostToDevice, st), "features");
+    const size_t count = size_t(kLatent) * s->image;
+    ERNIE_CUDA(cudaMemcpyAsync(s->scratch_latent, latent, count * 4, cudaMemcpyDeviceToDevice, st), "copy latent");
+    ERNIE_CUDA(cudaMemsetAsync(s->flags, 0, sizeof(int), st), "flag");
+    // delta = 0 leaves the scratch latent unchanged; only the prediction output is used.
+    ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, prediction, s->flags));
+    return ernie_cuda_context_synchronize(s->ctx);
+}
+
+extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int iters, float *ms)
+{
+    if (!s || !ms || kernel < 0 || kernel > 6 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
+    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs set_conditioning");
+    DeviceGuard guard(s->ctx->device);
+    ernie_cuda_context *ctx = s->ctx;
+    ERNIE_TRY(enqueue_block(s, 0, s->x, s->mod, kernel)); // warm-up launch
+    ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
+    for (int i = 0; i < iters; ++i) ERNIE_TRY(enqueue_block(s, 0, s->x, s->mod, kernel));
+    ERNIE_CUDA(cudaEventRecord(ctx->events[15], ctx->stream), "event");
+    ERNIE_CUDA(cudaEventSynchronize(ctx->events[15]), "event");
+    float total = 0.f;
+    ERNIE_CUDA(cudaEventElapsedTime(&total, ctx->events[14], ctx->events[15]), "event");
+    *ms = total / iters;
+    return ernie_cuda_context_synchronize(ctx);
+}
+
+extern "C" int ernie_cuda_session_launches_per_step(ernie_cuda_session *s, int *launches)
+{
+    if (!s || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
+    // input head: latent transpose + x_embedder GEMM + 4 GEMVs; 7 per block; output head: norm + GEMM
+    *launches = 6 + 7 * s->model->num_blocks + 2;
+    return ERNIE_CUDA_OK;
+}

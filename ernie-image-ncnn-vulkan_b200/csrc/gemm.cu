@@ -1,0 +1,498 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with the DiT block's fused epilogues.
+//
+// Replaces the ncnn `Gemm` layers of the reference block graph (block.ncnn.param:19,22,25,61,70,71,74)
+// together with the elementwise layers that follow each of them:
+//   Qkv        gemm_0/1/2 + reshape/permute + rmsn_9/rmsn_10 (qk-RMSNorm) + the rotary slice/mul/sub/add/concat
+//              chain (:29-57), writing head-major Q/K/V for attention;
+//   ResidGate  gemm_3 / gemm_6 + mul_15 / mul_21 (gate) + add_16 / add_22 (FP32 residual, ErnieResidualAdd);
+//   Geglu      gemm_4 + gemm_5 + ErnieGELU + mul_20 over interleaved [up; gate] weights;
+//   F32Bias    head projections (x_embedder conv1x1 + bias, text_proj);
+//   FinalEuler output-head linear + bias + transpose to [128,h,w] + euler_step (src/latent_ops.cpp:130-150)
+//              + the finite scan (src/latent_ops.cpp:118-128).
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A [128 x 64] and B [BN x 64] BF16 tiles, 128-byte swizzle, S-stage ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instruction)
+//   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (one TMEM lane = one output row per
+//               thread), fused math, global stores. Two TMEM accumulators let the epilogue of tile
+//               i overlap the main loop of tile i+1.
+#include "kernels.h"
+#include "ptx.cuh"
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace ernie_b200
+{
+namespace
+{
+constexpr int BM = 128, BK = 64, kThreads = 192;
+
+template <int BN> struct Cfg
+{
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kABytes = BM * BK * 2;
+    static constexpr int kBBytes = BN * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kBarrierBytes = 8 * (2 * kStages + 4) + 16;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+};
+
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * erfcf(-0.7071067811865475f * x); }
+
+__device__ __forceinline__ void split3(float x, __nv_bfloat16 &hi, __nv_bfloat16 &mid, __nv_bfloat16 &lo)
+{
+    hi = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(hi);
+    mid = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(mid);
+    lo = __float2bfloat16_rn(r2);
+}
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16 *dst, const float *v)
+{
+    __align__(16) __nv_bfloat162 packed[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) packed[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(packed);
+}
+
+__device__ __forceinline__ void store_f32x4(float *dst, const float *v)
+{
+    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+// ---- epilogues: one thread owns one output row of the 128-row tile ---------------------------
+template <int BN>
+__device__ __forceinline__ void epi_f32_bias(uint32_t taddr, int row, bool valid, int col0,
+                                             const GemmEpilogueArgs &a)
+{
+    float *out = a.out + static_cast<size_t>(row) * a.ldo + col0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32)
+    {
+        float v[32];
+        tmem_load_32(taddr + c, v);
+        if (!valid) continue;
+        if (a.bias)
+        {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __ldg(a.bias + col0 + c + j);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) store_f32x4(out + c + j, v + j);
+    }
+}
+
+template <int BN>
+__device__ __forceinline__ void epi_resid_gate(uint32_t taddr, int row, bool valid, int col0,
+                                               const GemmEpilogueArgs &a)
+{
+    float *resid = a.resid + static_cast<size_t>(row) * a.ldo + col0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32)
+    {
+        float v[32];
+        tmem_load_32(taddr + c, v);
+        if (!valid) continue;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+        {
+            float4 r = *reinterpret_cast<const float4 *>(resid + c + j);
+            const float4 g = __ldg(reinterpret_cast<const float4 *>(a.gate + col0 + c + j));
+            r.x += g.x * v[j];
+            r.y += g.y * v[j + 1];
+            r.z += g.z * v[j + 2];
+            r.w += g.w * v[j + 3];
+            *reinterpret_cast<float4 *>(resid + c + j) = r;
+        }
+    }
+}
+
+// BN = 256: the tile spans two 128-wide heads of one of Q, K or V (weights are [Wq; Wk; Wv]).
+__device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int col0, const GemmEpilogueArgs &a)
+{
+    const int part = col0 / kHidden;             // 0 = Q, 1 = K, 2 = V
+    const int head0 = (col0 % kHidden) / kHeadDim;
+    const float *cs = a.cos_t + static_cast<size_t>(valid ? row : 0) * kHeadDim;
+    const float *sn = a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim;
+    const float *gamma = part == 0 ? a.gamma_q : a.gamma_k;
+    void *dst_base = part == 0 ? a.q : part == 1 ? a.k : a.v;
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh)
+    {
+        float v[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+        {
+            float chunk[32];
+            tmem_load_32(taddr + hh * 128 + c * 32, chunk);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[c * 32 + j] = chunk[j];
+        }
+        if (!valid) continue;
+        if (part < 2)
+        {
+            // rmsn_9 / rmsn_10: x * (mean(x^2) + 1e-6)^(-1/2) * gamma over the 128-wide head
+            float squared = 0.f;
+#pragma unroll
+            for (int d = 0; d < 128; ++d) squared += v[d] * v[d];
+            const float inverse = 1.f / sqrtf(squared * (1.f / 128.f) + 1e-6f);
+#pragma unroll
+            for (int d = 0; d < 128; ++d) v[d] = v[d] * inverse * __ldg(gamma + d);
+            // ERNIE rotary: halves rotated with the full-width, pair-duplicated angle table
+#pragma unroll
+            for (int d = 0; d < 64; ++d)
+            {
+                const float first = v[d], second = v[d + 64];
+                v[d] = first * __ldg(cs + d) - second * __ldg(sn + d);
+                v[d + 64] = second * __ldg(cs + d + 64) + first * __ldg(sn + d + 64);
+            }
+        }
+        const size_t offset = (static_cast<size_t>(head0 + hh) * a.rows_pad + row) * kHeadDim;
+        if (a.qkv_fp32)
+        {
+            float *dst = static_cast<float *>(dst_base) + offset;
+#pragma unroll
+            for (int d = 0; d < 128; d += 4) store_f32x4(dst + d, v + d);
+        }
+        else
+        {
+            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) + offset;
+#pragma unroll
+            for (int d = 0; d < 128; d += 8) store_bf16x8(dst + d, v + d);
+        }
+    }
+}
+
+// BN = 256: columns [0,128) are up-projection outputs, [128,256) the matching gate outputs.
+__device__ __forceinline__ void epi_geglu(uint32_t taddr, int row, bool valid, int n_blk, const GemmEpilogueArgs &a)
+{
+    const int f0 = n_blk * 128;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32)
+    {
+        float up[32], gate[32];
+        tmem_load_32(taddr + c, up);
+        tmem_load_32(taddr + 128 + c, gate);
+        if (!valid) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
+        if (!a.h_split3)
+        {
+            __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * a.ffn + f0 + c;
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, up + j);
+        }
+        else
+        {
+            __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * (3 * a.ffn) + f0 + c;
+#pragma unroll
+            for (int j = 0; j < 32; j += 8)
+            {
+                __align__(16) __nv_bfloat16 hi[8], mid[8], lo[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) split3(up[j + t], hi[t], mid[t], lo[t]);
+                *reinterpret_cast<uint4 *>(dst + j) = *reinterpret_cast<const uint4 *>(hi);
+                *reinterpret_cast<uint4 *>(dst + a.ffn + j) = *reinterpret_cast<const uint4 *>(mid);
+                *reinterpret_cast<uint4 *>(dst + 2 * a.ffn + j) = *reinterpret_cast<const uint4 *>(lo);
+            }
+        }
+    }
+}
+
+// BN = 128 = latent channels. Rows are image tokens; latent and prediction are [128][m].
+__device__ __forceinline__ void epi_final_euler(uint32_t taddr, int row, bool valid, int m,
+                                                const GemmEpilogueArgs &a)
+{
+    bool finite = true;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32)
+    {
+        float v[32];
+        tmem_load_32(taddr + c, v);
+        if (!valid) continue;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+        {
+            const int ch = c + j;
+            const float prediction = v[j] + __ldg(a.bias + ch);
+            const size_t idx = static_cast<size_t>(ch) * m + row;
+            // euler_step: change = delta * v; out = x + change, two roundings (no contraction)
+            const float next = __fadd_rn(a.latent[idx], __fmul_rn(a.delta, prediction));
+            a.latent[idx] = next;
+            if (a.prediction) a.prediction[idx] = prediction;
+            finite = finite && isfinite(next);
+        }
+    }
+    if (!finite) atomicOr(a.finite_flag, 1);
+}
+
+template <int BN, Epilogue EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m, int n,
+                int k_b, int splits, GemmEpilogueArgs args)
+{
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - raw);
+    const uint32_t bars = base + C::kStages * C::kStageBytes;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (C::kStages + s); };
+    auto tfull_bar = [&](int i) { return bars + 8u * (2 * C::kStages + i); };
+    auto tempty_bar = [&](int i) { return bars + 8u * (2 * C::kStages + 2 + i); };
+    const uint32_t slot = bars + 8u * (2 * C::kStages + 4);
+    auto tile_a = [&](int s) { return base + s * C::kStageBytes; };
+    auto tile_b = [&](int s) { return base + s * C::kStageBytes + C::kABytes; };
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int num_m = (m + BM - 1) / BM, num_n = n / BN, tiles = num_m * num_n;
+    const int k_blocks = (k_b * splits) / BK;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < C::kStages; ++s)
+        {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(tfull_bar(i), 1);
+            mbar_init(tempty_bar(i), 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0)
+    {
+        prefetch_tensormap(&map_a);
+        prefetch_tensormap(&map_b);
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
+            {
+                const int m_blk = tile % num_m, n_blk = tile / num_m;
+                for (int kb = 0; kb < k_blocks; ++kb)
+                {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u))
+                    {
+                        if (args.error_flag) atomicExch(args.error_flag, kErrGemmProducerTimeout);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
+                    tma_load_2d(tile_a(stage), &map_a, full_bar(stage), kb * BK, m_blk * BM);
+                    tma_load_2d(tile_b(stage), &map_b, full_bar(stage), (kb * BK) % k_b, n_blk * BN);
+                    if (++stage == C::kStages)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // On a timeout no drain is needed: the last load was issued before the failed wait
+            // began, kWaitLimitCycles earlier, and TMA loads complete without any consumer.
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            constexpr uint32_t idesc = idesc_bf16(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it)
+            {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (it >> 1) & 1;
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u))
+                {
+                    if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < k_blocks; ++kb)
+                {
+                    if (!mbar_wait(full_bar(stage), phase))
+                    {
+                        if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_desc = smem_desc_sw128(tile_a(stage));
+                    const uint64_t b_desc = smem_desc_sw128(tile_b(stage));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_bf16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(empty_bar(stage));
+                    if (++stage == C::kStages)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                umma_commit(tfull_bar(acc));
+            }
+        }
+    }
+    else
+    {
+        const int quarter = warp & 3;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it)
+        {
+            const int m_blk = tile % num_m, n_blk = tile / num_m;
+            const int acc = it & 1;
+            const uint32_t acc_phase = (it >> 1) & 1;
+            if (!mbar_wait(tfull_bar(acc), acc_phase))
+            {
+                if (args.error_flag && lane == 0) atomicExch(args.error_flag, kErrGemmEpilogueTimeout);
+                break;
+            }
+            tc_fence_after();
+            const int row = m_blk * BM + quarter * 32 + lane;
+            const bool valid = row < m;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+            const int col0 = n_blk * BN;
+            if constexpr (EPI == Epilogue::F32Bias) epi_f32_bias<BN>(taddr, row, valid, col0, args);
+            else if constexpr (EPI == Epilogue::ResidGate) epi_resid_gate<BN>(taddr, row, valid, col0, args);
+            else if constexpr (EPI == Epilogue::Qkv) epi_qkv(taddr, row, valid, col0, args);
+            else if constexpr (EPI == Epilogue::Geglu) epi_geglu(taddr, row, valid, n_blk, args);
+            else epi_final_euler(taddr, row, valid, m, args);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+        }
+    }
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major BF16 [rows, cols] operand, 64-column (128-byte) x box_rows boxes, 128-byte swizzle.
+bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows)
+{
+    auto fn = encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15u) || (cols * 2) % 16) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t element_strides[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+              element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, Epilogue EPI> cudaError_t ensure_attributes()
+{
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg<BN>::kSmemBytes);
+    });
+    return attr;
+}
+
+template <int BN, Epilogue EPI>
+int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits,
+                const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream)
+{
+    using C = Cfg<BN>;
+    const cudaError_t attr = ensure_attributes<BN, EPI>();
+    if (attr != cudaSuccess) return attr;
+    CUtensorMap map_a, map_b;
+    if (!make_map(&map_a, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k_b) * splits, BM) ||
+        !make_map(&map_b, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k_b), BN))
+        return cudaErrorInvalidValue;
+    const int tiles = ((m + BM - 1) / BM) * (n / BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    gemm_kernel<BN, EPI><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, args);
+    return cudaGetLastError();
+}
+} // namespace
+
+int prepare_gemm_kernels()
+{
+    cudaError_t e = ensure_attributes<256, Epilogue::F32Bias>();
+    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::ResidGate>();
+    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::Qkv>();
+    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::Geglu>();
+    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::F32Bias>();
+    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::ResidGate>();
+    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::FinalEuler>();
+    return e;
+}
+
+int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits, int block_n,
+                Epilogue epilogue, const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream)
+{
+    if (m < 1 || n < 1 || k_b < BK || k_b % BK || splits < 1 || splits > 3 || num_sms < 1) return cudaErrorInvalidValue;
+    if (block_n != 128 && block_n != 256) return cudaErrorInvalidValue;
+    if (n % block_n) return cudaErrorInvalidValue;
+    if ((epilogue == Epilogue::Qkv || epilogue == Epilogue::Geglu) && block_n != 256) return cudaErrorInvalidValue;
+    if (epilogue == Epilogue::FinalEuler && (block_n != 128 || n != 128)) return cudaErrorInvalidValue;
+    if (epilogue == Epilogue::Qkv && (n != 3 * kHidden || args.rows_pad < m)) return cudaErrorInvalidValue;
+    if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
+    if (block_n == 256)
+    {
+        switch (epilogue)
+        {
+        case Epilogue::F32Bias: return launch_impl<256, Epilogue::F32Bias>(a, b, m, n, k_b, splits, args, num_sms, stream);
+        case Epilogue::ResidGate: return launch_impl<256, Epilogue::ResidGate>(a, b, m, n, k_b, splits, args, num_sms, stream);
+        case Epilogue::Qkv: return launch_impl<256, Epilogue::Qkv>(a, b, m, n, k_b, splits, args, num_sms, stream);
+        case Epilogue::Geglu: return launch_impl<256, Epilogue::Geglu>(a, b, m, n, k_b, splits, args, num_sms, stream);
+        default: return cudaErrorInvalidValue;
+        }
+    }
+    switch (epilogue)
+    {
+    case Epilogue::F32Bias: return launch_impl<128, Epilogue::F32Bias>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::ResidGate: return launch_impl<128, Epilogue::ResidGate>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::FinalEuler: return launch_impl<128, Epilogue::FinalEuler>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+} // namespace ernie_b200

@@ -1,0 +1,109 @@
+// Internal launch interface of the sm_100a kernels (host side). Plain pointers and sizes; all
+// buffers are device memory owned by the caller and must outlive the enqueued work.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace ernie_b200
+{
+constexpr int kHidden = 4096, kHeads = 32, kHeadDim = 128, kFfn = 12288, kTextDim = 3072, kLatent = 128;
+
+enum class Epilogue : int
+{
+    F32Bias = 0,    // out[r, c] = acc + bias[c] (bias may be null), FP32, row stride ldo
+    Qkv = 1,        // per-head qk-RMSNorm + 3-axis RoPE on Q,K; write Q,K,V head-major
+    ResidGate = 2,  // resid[r, c] += gate[c] * acc (FP32, in place)
+    Geglu = 3,      // h[r, f] = up * gelu_erf(gate) from interleaved [up; gate] 128-column groups
+    FinalEuler = 4, // pred = acc + bias; latent[c][r] = latent + delta * pred (no FMA); finite flag
+};
+
+struct GemmEpilogueArgs
+{
+    // F32Bias
+    float *out = nullptr;
+    int ldo = 0;
+    const float *bias = nullptr;
+    // ResidGate
+    float *resid = nullptr;
+    const float *gate = nullptr;
+    // Qkv
+    void *q = nullptr, *k = nullptr, *v = nullptr; // [heads][rows_pad][128], BF16 or FP32
+    int rows_pad = 0;
+    int qkv_fp32 = 0;
+    const float *gamma_q = nullptr, *gamma_k = nullptr; // [128]
+    const float *cos_t = nullptr, *sin_t = nullptr;     // [rows][128]
+    // Geglu: BF16 [rows][ffn] or, when split3, hi/mid/lo BF16 planes at column offsets 0, ffn, 2*ffn
+    __nv_bfloat16 *h = nullptr;
+    int h_split3 = 0;
+    int ffn = 0;
+    // FinalEuler
+    float *latent = nullptr;     // [128][rows]
+    float *prediction = nullptr; // optional [128][rows]
+    float delta = 0.f;
+    int *finite_flag = nullptr; // set to 1 if any updated latent value is not finite
+    // all
+    int *error_flag = nullptr;
+};
+
+// C[M, N] = A[M, K_a] * B[N, K_b]^T with BF16 operands and FP32 accumulation on tcgen05.
+// K_a = splits * K_b: in FP32-exact mode A holds `splits` BF16 planes (hi, mid, lo) side by side
+// and every plane multiplies the same exact-BF16 weights. Returns a cudaError_t.
+int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits, int block_n,
+                Epilogue epilogue, const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream);
+
+// Row statistics + modulation: y = norm(x) * (1 + scale) + shift, written as BF16 or as 3 BF16 planes.
+// centered = 0: RMSNorm with gamma; centered = 1: non-affine LayerNorm. scale/shift may be null.
+int launch_norm_modulate(const float *x, int rows, int width, const float *gamma, const float *scale,
+                         const float *shift, float eps, int centered, __nv_bfloat16 *out, int split3,
+                         cudaStream_t stream);
+// Channel-major latent [128][tokens] -> token-major BF16 A operand [tokens][128] (or 3 planes).
+int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out, int split3, cudaStream_t stream);
+// FP32 [rows][cols] -> BF16 [rows][cols] (or 3 BF16 planes [rows][3*cols]).
+int launch_to_operand(const float *src, long long rows, int cols, __nv_bfloat16 *out, int split3, cudaStream_t stream);
+// y[n] = W[n, :] . act(x) + bias[n]; act = SiLU when silu_input.
+int launch_gemv(const __nv_bfloat16 *w, const float *x, const float *bias, float *y, int n, int k, int silu_input,
+                cudaStream_t stream);
+
+// BF16 flash attention (head dim 128) over head-major Q/K/V [heads][rows_pad][128]; keys >= kv_len
+// are excluded, `mask` (nullable) adds a per-key row. Output token-major BF16 [rows][heads*128].
+int launch_attention_bf16(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *v,
+                          const float *mask, int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out,
+                          cudaStream_t stream);
+
+// FP32 attention with FP64 softmax accumulation. q [heads][q_stride rows][width] (head stride
+// q_head_stride elements), k/v [kv_heads][...]; mask [mask_heads][mask_rows][nk] additive (nullable).
+// out_mode 0: FP32 [heads][nq][width]; out_mode 1: split-3 BF16 token-major [nq][3*heads*width].
+struct AttentionF32Args
+{
+    const float *q, *k, *v, *mask;
+    int heads, kv_heads, mask_heads, mask_rows, nq, nk, kv_len, width;
+    long long q_head_stride, kv_head_stride;
+    int out_mode;
+    float *out_f32;
+    __nv_bfloat16 *out_split3;
+};
+int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream);
+
+int launch_euler(const float *sample, const float *prediction, float delta, long long count, float *out,
+                 cudaStream_t stream);
+int launch_finite(const float *x, long long count, int *flag, cudaStream_t stream);
+int launch_unpack_for_vae(const float *packed, const float *mean, const float *variance, int w, int h, float *out,
+                          cudaStream_t stream);
+int launch_gelu(float *data, long long count, cudaStream_t stream);
+int launch_residual_add(const float *a, const float *b, float *out, long long count, cudaStream_t stream);
+int launch_rmsnorm(const float *x, const float *gamma, long long rows, int width, float eps, int centered,
+                   float *out, cudaStream_t stream);
+
+// Synthetic weights on device (ernie_synth.h protocol). rows x cols BF16 written at `out` with a
+// destination row index map: dst_row = (row / group) * group_stride + group_offset + row % group.
+int launch_synth_bf16(uint64_t seed, uint64_t stream_id, float scale, float offset, long long rows, int cols,
+                      int group, long long group_stride, long long group_offset, __nv_bfloat16 *out,
+                      cudaStream_t stream);
+// Sets the shared-memory attributes of every kernel once (call before any stream capture).
+int prepare_gemm_kernels();
+int prepare_attention_kernels();
+int launch_synth_f32_bf16(uint64_t seed, uint64_t stream_id, float scale, float offset, long long count, float *out,
+                          cudaStream_t stream);
+} // namespace ernie_b200

@@ -1,0 +1,203 @@
+/* C ABI of the B200-native ERNIE-Image-Turbo DiT denoiser hot path (libernie_b200.so).
+ *
+ * Drop-in boundary for mingshi2333/ernie-image-ncnn-vulkan's ncnn/Vulkan denoiser path. Plain
+ * pointers and sizes only. Return codes follow ncnn's convention as the reference maps it in
+ * check_ncnn_memory (src/vulkan_memory.cpp:21-30): 0 = success, -100 = (device) allocation failure
+ * (the C++ wrapper throws GpuAllocationError), -1 = any other failure (std::runtime_error or
+ * std::invalid_argument). ernie_cuda_last_error() returns the calling thread's last message.
+ *
+ * Memory: "dev" pointers are CUDA device memory owned by the caller (allocate with
+ * ernie_cuda_malloc or any CUDA allocator on the context's device); they must outlive the work
+ * enqueued on the context's stream, as the reference requires of its VkMat arguments
+ * (src/dit.h:26-29, src/latent_ops.h:32-35). "host" pointers are ordinary host memory and are
+ * consumed or filled before the call returns. Tensors are dense row-major FP32 unless noted;
+ * weights are BF16 bit patterns (uint16_t).
+ *
+ * Threading: a context owns one CUDA stream on one device. Calls on one context are serialised by
+ * the caller, as ernie::generate calls are (include/ernie/pipeline.h:145). Use one context (and one
+ * host thread) per GPU for data-parallel work.
+ */
+#ifndef ERNIE_CUDA_H
+#define ERNIE_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ERNIE_CUDA_OK 0
+#define ERNIE_CUDA_ERROR (-1)
+#define ERNIE_CUDA_OUT_OF_MEMORY (-100)
+
+/* Arithmetic modes. BF16: BF16 GEMM/attention operands, FP32 accumulation, FP32 residual stream,
+   norms, softmax and latent (the reference's use_bf16_storage path). FP32: FP32-exact mode
+   (activations split into three BF16 planes against exact-BF16 weights; FP32 attention with FP64
+   softmax sums), gated like the reference's FP32 path. */
+#define ERNIE_PRECISION_BF16 0
+#define ERNIE_PRECISION_FP32 1
+#define ERNIE_SCHEDULE_TURBO 0  /* FlowSchedule::turbo, src/latent_ops.cpp:89-109 */
+#define ERNIE_SCHEDULE_LINEAR 1 /* evenly spaced sigmas 1 -> 0 (benchmark configuration) */
+
+/* Block tensor ids for ernie_cuda_model_read_tensor (test hook). */
+#define ERNIE_TENSOR_WQKV 0  /* [12288,4096] = [Wq; Wk; Wv] */
+#define ERNIE_TENSOR_WO 1    /* [4096,4096] */
+#define ERNIE_TENSOR_WUPGATE 2 /* [24576,4096], 128-row groups interleaved: up g, gate g, ... */
+#define ERNIE_TENSOR_WFC2 3  /* [4096,12288] */
+
+typedef struct ernie_cuda_context ernie_cuda_context;
+typedef struct ernie_cuda_model ernie_cuda_model;
+typedef struct ernie_cuda_session ernie_cuda_session;
+
+/* Host weights of one block, as tools/build_dit_weights.py:19-31 binds them to the block graph. */
+typedef struct
+{
+    const uint16_t *wq, *wk, *wv, *wo; /* [4096,4096] BF16, [out,in] */
+    const uint16_t *wup, *wgate;       /* [12288,4096] */
+    const uint16_t *wfc2;              /* [4096,12288] */
+    const float *gamma_sa, *gamma_mlp; /* [4096] adaLN_sa_ln / adaLN_mlp_ln */
+    const float *gamma_q, *gamma_k;    /* [128] norm_q / norm_k */
+} ernie_cuda_block_weights;
+
+/* Host weights of the input and output heads (tools/export_dit_heads.py:19 HEADS). */
+typedef struct
+{
+    const uint16_t *x_embed_w;    /* [4096,128] x_embedder.proj (1x1 conv) */
+    const float *x_embed_b;       /* [4096] */
+    const uint16_t *text_proj_w;  /* [4096,3072] */
+    const uint16_t *time1_w;      /* [4096,4096] time_embedding.linear_1 */
+    const float *time1_b;
+    const uint16_t *time2_w;      /* [4096,4096] time_embedding.linear_2 */
+    const float *time2_b;
+    const uint16_t *adaln_w;      /* [24576,4096] adaLN_modulation.1 */
+    const float *adaln_b;
+    const uint16_t *final_norm_w; /* [8192,4096] final_norm.linear */
+    const float *final_norm_b;
+    const uint16_t *final_w;      /* [128,4096] final_linear */
+    const float *final_b;
+} ernie_cuda_head_weights;
+
+/* Packed latent geometry and text slots of one request (src/shape_plan.h:10-29, model.cfg keys). */
+typedef struct
+{
+    int width, height; /* packed latent grid, 1..256 */
+    int text_tokens;   /* DiT text slots (bucket), 1..2048 */
+    int valid_text;    /* valid text tokens T, 1..text_tokens */
+} ernie_cuda_shape;
+
+const char *ernie_cuda_last_error(void);
+int ernie_cuda_device_count(int *count);
+
+/* ---- GPU context: replaces GpuContext (src/gpu_context.h:12-27) -------------------------- */
+int ernie_cuda_context_create(int device, ernie_cuda_context **out);
+int ernie_cuda_context_destroy(ernie_cuda_context *ctx);
+/* Wait for the stream; reports a device-side protocol timeout (bounded waits) as -1. */
+int ernie_cuda_context_synchronize(ernie_cuda_context *ctx);
+/* Device budget reader (replaces the Vulkan budget reader, src/weight_placement.cpp:75-97). */
+int ernie_cuda_context_memory(ernie_cuda_context *ctx, uint64_t *free_bytes, uint64_t *total_bytes);
+int ernie_cuda_context_sm_count(ernie_cuda_context *ctx, int *sms);
+int ernie_cuda_malloc(ernie_cuda_context *ctx, size_t bytes, void **dev);
+int ernie_cuda_free(ernie_cuda_context *ctx, void *dev);
+int ernie_cuda_upload(ernie_cuda_context *ctx, void *dev, const void *host, size_t bytes);
+int ernie_cuda_download(ernie_cuda_context *ctx, void *host, const void *dev, size_t bytes);
+int ernie_cuda_memset(ernie_cuda_context *ctx, void *dev, int value, size_t bytes);
+/* Device time between two points on the context stream, for benchmarks (milliseconds). */
+int ernie_cuda_event_record(ernie_cuda_context *ctx, int slot);
+int ernie_cuda_event_elapsed(ernie_cuda_context *ctx, int start_slot, int end_slot, float *ms);
+
+/* ---- Resident weights: replace the per-block Net load/stream of run_block_sequence
+        (src/block_sequence.cpp:119-278), WeightPlacement (src/weight_placement.h:34-51) and
+        WeightSession (src/weight_session.h:29-73). All 36 blocks fit in HBM (15.7 GB BF16). --- */
+int ernie_cuda_model_create(ernie_cuda_context *ctx, int num_blocks, ernie_cuda_model **out);
+int ernie_cuda_model_destroy(ernie_cuda_model *model);
+int ernie_cuda_model_upload_block(ernie_cuda_model *model, int block, const ernie_cuda_block_weights *host);
+int ernie_cuda_model_upload_heads(ernie_cuda_model *model, const ernie_cuda_head_weights *host);
+/* Seeded random-init weights generated on the device (include/ernie_synth.h protocol). */
+int ernie_cuda_model_synthesize(ernie_cuda_model *model, uint64_t seed);
+int ernie_cuda_model_read_tensor(ernie_cuda_model *model, int block, int tensor, void *host, size_t bytes);
+int ernie_cuda_model_bytes(ernie_cuda_model *model, uint64_t *bytes);
+
+/* ---- ERNIE layer contracts (src/ernie_gelu.cpp:108-116 register_layers), dev pointers ---- */
+/* ErnieSDPA (src/ernie_attention.cpp:158-233): out = softmax(q k^T / sqrt(width) + mask) v.
+   q [heads][nq][width], k/v [kv_heads][nk][width] with kv_heads 1 or heads, mask NULL or
+   [mask_heads][mask_rows][nk] additive with mask_heads 1 or heads and mask_rows 1 or nq,
+   width 1..128. FP32 in/out, FP64 softmax accumulation. */
+int ernie_cuda_sdpa(ernie_cuda_context *ctx, const float *q, const float *k, const float *v, const float *mask,
+                    int heads, int kv_heads, int mask_heads, int mask_rows, int nq, int nk, int width, float *out);
+/* BF16 flash path of the same operator on head-major BF16 q/k/v [heads][rows_pad][128]
+   (rows_pad a multiple of 128, rows beyond nq zero), keys >= kv_len excluded, optional row mask
+   [nq]. Output token-major BF16 [nq][heads*128]. */
+int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                         const float *mask, int heads, int nq, int rows_pad, int kv_len, uint16_t *out);
+/* set_attention_query_rows (src/ernie_attention.cpp:245-255): 128, 64, 32 or 16, else -1.
+   The flash kernels need no query chunking; the value is recorded for the recovery contract. */
+int ernie_cuda_set_attention_query_rows(ernie_cuda_context *ctx, int rows);
+int ernie_cuda_attention_query_rows(ernie_cuda_context *ctx, int *rows);
+/* ErnieNorm RMSNorm (src/ernie_rmsnorm.cpp:21-135): width 128, 3072 or 4096, affine. */
+int ernie_cuda_rmsnorm(ernie_cuda_context *ctx, const float *x, const float *gamma, int64_t rows, int width,
+                       float eps, float *out);
+/* ErnieNorm LayerNorm: width 4096, non-affine. */
+int ernie_cuda_layernorm(ernie_cuda_context *ctx, const float *x, int64_t rows, int width, float eps, float *out);
+/* ErnieGELU (src/ernie_gelu.cpp:35-103): in place, count % 4 == 0 else -1. */
+int ernie_cuda_gelu(ernie_cuda_context *ctx, float *data, int64_t count);
+/* ErnieResidualAdd (src/ernie_residual.cpp:19-92): FP32 out = a + b. */
+int ernie_cuda_residual_add(ernie_cuda_context *ctx, const float *a, const float *b, float *out, int64_t count);
+/* tcgen05 GEMM: c[M,N] = a[M,K] (BF16) * w[N,K]^T (BF16) + bias (nullable), FP32 out.
+   K and N multiples of 64 and 128. */
+int ernie_cuda_linear_bf16(ernie_cuda_context *ctx, const uint16_t *a, const uint16_t *w, const float *bias,
+                           float *c, int m, int n, int k);
+
+/* ---- Latent ops (src/latent_ops.h:15-57), dev pointers, latent [128][h][w] ------------------ */
+int ernie_cuda_euler_step(ernie_cuda_context *ctx, const float *sample, const float *prediction, float delta,
+                          int width, int height, float *out);
+int ernie_cuda_finite_latent(ernie_cuda_context *ctx, const float *latent, int width, int height, int *finite);
+int ernie_cuda_unpack_for_vae(ernie_cuda_context *ctx, const float *packed, const float *mean,
+                              const float *variance, int width, int height, float *out);
+/* Host helpers of the same path: FlowSchedule::turbo / linear (sigmas [steps+1], timesteps
+   [steps]), timestep_features (src/denoiser.cpp:152-169), dit_constants (src/conditioning.cpp:10-44)
+   from the 64-value frequency table (NULL = the official table of tools/prepare_pipeline.py:63). */
+int ernie_cuda_schedule(int steps, int schedule, float *sigmas, float *timesteps);
+int ernie_cuda_timestep_features(float timestep, float *out4096);
+int ernie_cuda_dit_constants(const float *freq64, int width, int height, int valid_text, int text_tokens,
+                             int token_limit, float *cos_out, float *sin_out, float *mask_out);
+
+/* ---- Request session: one shape, one precision; activations sized once ------------------- */
+int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
+                              ernie_cuda_session **out);
+int ernie_cuda_session_destroy(ernie_cuda_session *session);
+/* Conditioning constants of the request (the four `constants` of denoise, src/denoiser.h:110-117):
+   text [text_tokens][3072] (padded, pad_text src/conditioning.cpp:56-67; NULL skips text_proj),
+   cos/sin [N][128], mask [N] with N = width*height + text_tokens. Host pointers. text_proj runs
+   once here, not once per step. */
+int ernie_cuda_session_set_conditioning(ernie_cuda_session *session, const float *text, const float *cos_table,
+                                        const float *sin_table, const float *mask);
+int ernie_cuda_session_tokens(ernie_cuda_session *session, int *tokens);
+/* run_block_sequence (src/block_sequence.h:38-60): blocks [first, first+count) on x (dev,
+   [N][4096] FP32, updated in place) with shared modulation (dev [6][4096]: shift_sa, scale_sa,
+   gate_sa, shift_mlp, scale_mlp, gate_mlp). */
+int ernie_cuda_session_blocks(ernie_cuda_session *session, int first, int count, float *x, const float *modulation);
+/* run_dit (src/dit.h:17-40): one prediction [128][h][w] for latent [128][h][w] at `timestep`
+   (dev pointers). */
+int ernie_cuda_session_dit(ernie_cuda_session *session, const float *latent, float timestep, float *prediction);
+/* denoise (src/denoiser.h:110-128) on the session's device latent: steps [start_step, end_step)
+   of an S-step schedule, captured as a CUDA graph when use_graph != 0. The latent lives at
+   ernie_cuda_session_latent(). *failed_step receives the first step k (1-based) after which the
+   latent was non-finite, else 0 (and the call returns -1 in that case). */
+int ernie_cuda_session_latent(ernie_cuda_session *session, float **latent_dev);
+int ernie_cuda_session_denoise_device(ernie_cuda_session *session, int steps, int start_step, int end_step,
+                                      int schedule, int use_graph, int *failed_step);
+/* Same loop end to end with host buffers: initial -> final (host [128][h][w]); predictions
+   (nullable, host [end-start][128][h][w]) receives every step's DiT output. */
+int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial, float *final_latent, int steps,
+                               int start_step, int end_step, int schedule, float *predictions, int *failed_step);
+
+/* Benchmark hooks: average device time in ms of `iters` back-to-back launches of one kernel of
+   block 0 on the session's buffers (kernel 0 norm+modulate, 1 QKV GEMM, 2 attention, 3 out-proj
+   GEMM, 4 MLP norm+modulate, 5 up/gate GEMM, 6 down GEMM), and the number of kernels one denoise
+   step launches. */
+int ernie_cuda_session_profile(ernie_cuda_session *session, int kernel, int iters, float *ms);
+int ernie_cuda_session_launches_per_step(ernie_cuda_session *session, int *launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
