@@ -79,7 +79,7 @@ class ClockSampler:
         if not sm:
             return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(sm),
                 "reasons": reasons}
 

@@ -423,8 +423,8 @@ extern "C" int ernie_cuda_model_upload_block(ernie_cuda_model *model, int block,
     ERNIE_CUDA(copy(b.wqkv + size_t(kHidden) * kHidden, w->wk, sq), "upload wk");
     ERNIE_CUDA(copy(b.wqkv + size_t(2) * kHidden * kHidden, w->wv, sq), "upload wv");
     ERNIE_CUDA(copy(b.wo, w->wo, sq), "upload wo");
-    const size_t group = size_t(128) * kHidden;
-    for (int g = 0; g < kFfn / 128; ++g)
+    const size_t group = size_t(64) * kHidden; // [up; gate] interleaved in 64-row groups
+    for (int g = 0; g < kFfn / 64; ++g)
     {
         ERNIE_CUDA(copy(b.wug + size_t(2 * g) * group, w->wup + size_t(g) * group, group * 2), "upload up");
         ERNIE_CUDA(copy(b.wug + size_t(2 * g + 1) * group, w->wgate + size_t(g) * group, group * 2), "upload gate");
@@ -482,9 +482,9 @@ extern "C" int ernie_cuda_model_synthesize(ernie_cuda_model *model, uint64_t see
         ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WK), std, 0.f, H, kHidden, kHidden, 0, H, d.wqkv, s), "synth");
         ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WV), std, 0.f, H, kHidden, kHidden, 0, 2 * H, d.wqkv, s), "synth");
         ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WO), std, 0.f, H, kHidden, kHidden, 0, 0, d.wo, s), "synth");
-        // up/gate interleaved in 128-row groups
-        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WUP), std, 0.f, kFfn, kHidden, 128, 256, 0, d.wug, s), "synth");
-        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WGATE), std, 0.f, kFfn, kHidden, 128, 256, 128, d.wug, s), "synth");
+        // up/gate interleaved in 64-row groups
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WUP), std, 0.f, kFfn, kHidden, 64, 128, 0, d.wug, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WGATE), std, 0.f, kFfn, kHidden, 64, 128, 64, d.wug, s), "synth");
         ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_WFC2), std, 0.f, H, kFfn, kHidden, 0, 0, d.wfc2, s), "synth");
         ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_SA), std, 1.f, kHidden, d.gamma_sa, s), "synth");
         ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_GAMMA_MLP), std, 1.f, kHidden, d.gamma_mlp, s), "synth");
@@ -824,6 +824,16 @@ extern "C" int ernie_cuda_session_latent(ernie_cuda_session *s, float **latent_d
     return ERNIE_CUDA_OK;
 }
 
+// GEMM of the session's precision: BF16 mode uses the requested tile width; FP32-exact mode uses
+// 128-wide tiles with FP32 promotion of the tensor-core partial sums.
+static int session_gemm(ernie_cuda_session *s, const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k,
+                        int block_n, Epilogue epilogue, const GemmEpilogueArgs &args)
+{
+    const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
+    return launch_gemm(a, b, m, n, k, s->splits, fp32 ? 128 : block_n, epilogue, args, s->ctx->num_sms,
+                       s->ctx->stream, fp32);
+}
+
 extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const float *text, const float *cos_table,
                                                    const float *sin_table, const float *mask)
 {
@@ -858,8 +868,7 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
         args.out = s->text_cache;
         args.ldo = kHidden;
         args.error_flag = s->ctx->error_flag;
-        ERNIE_LAUNCH(launch_gemm(s->a, s->model->heads.text_proj_w, s->text, kHidden, kTextDim, s->splits, 256,
-                                 Epilogue::F32Bias, args, s->ctx->num_sms, st),
+        ERNIE_LAUNCH(session_gemm(s, s->a, s->model->heads.text_proj_w, s->text, kHidden, kTextDim, 256, Epilogue::F32Bias, args),
                      "text_proj");
     }
     ERNIE_CUDA(cudaStreamSynchronize(st), "set conditioning");
@@ -893,7 +902,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.cos_t = s->cos_t;
     qkv.sin_t = s->sin_t;
     qkv.error_flag = s->ctx->error_flag;
-    if (on(1)) ERNIE_LAUNCH(launch_gemm(s->a, w.wqkv, T, 3 * kHidden, kHidden, sp, 256, Epilogue::Qkv, qkv, nsm, st), "qkv");
+    if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, 256, Epilogue::Qkv, qkv), "qkv");
     if (!on(2)) {}
     else if (fp32)
     {
@@ -926,7 +935,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     res.ldo = kHidden;
     res.gate = gate_sa;
     res.error_flag = s->ctx->error_flag;
-    if (on(3)) ERNIE_LAUNCH(launch_gemm(s->a, w.wo, T, kHidden, kHidden, sp, 128, Epilogue::ResidGate, res, nsm, st), "out proj");
+    if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 128, Epilogue::ResidGate, res), "out proj");
     if (on(4))
         ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
     GemmEpilogueArgs gg;
@@ -934,9 +943,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     gg.h_split3 = fp32;
     gg.ffn = kFfn;
     gg.error_flag = s->ctx->error_flag;
-    if (on(5)) ERNIE_LAUNCH(launch_gemm(s->a, w.wug, T, 2 * kFfn, kHidden, sp, 256, Epilogue::Geglu, gg, nsm, st), "up/gate");
+    if (on(5)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wug, T, 2 * kFfn, kHidden, 256, Epilogue::Geglu, gg), "up/gate");
     res.gate = gate_mlp;
-    if (on(6)) ERNIE_LAUNCH(launch_gemm(s->h, w.wfc2, T, kHidden, kFfn, sp, 128, Epilogue::ResidGate, res, nsm, st), "down");
+    if (on(6)) ERNIE_LAUNCH(session_gemm(s, s->h, w.wfc2, T, kHidden, kFfn, 128, Epilogue::ResidGate, res), "down");
     return ERNIE_CUDA_OK;
 }
 
@@ -961,7 +970,7 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     emb.ldo = kHidden;
     emb.bias = hd.x_embed_b;
     emb.error_flag = s->ctx->error_flag;
-    ERNIE_LAUNCH(launch_gemm(s->a, hd.x_embed_w, s->image, kHidden, kLatent, sp, 256, Epilogue::F32Bias, emb, nsm, st),
+    ERNIE_LAUNCH(session_gemm(s, s->a, hd.x_embed_w, s->image, kHidden, kLatent, 256, Epilogue::F32Bias, emb),
                  "x_embedder");
     ERNIE_LAUNCH(launch_gemv(hd.time1_w, features, hd.time1_b, s->g1, kHidden, kHidden, 0, st), "time linear_1");
     ERNIE_LAUNCH(launch_gemv(hd.time2_w, s->g1, hd.time2_b, s->c, kHidden, kHidden, 1, st), "time linear_2");
@@ -978,7 +987,7 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     fin.delta = delta;
     fin.finite_flag = finite_flag;
     fin.error_flag = s->ctx->error_flag;
-    ERNIE_LAUNCH(launch_gemm(s->a, hd.final_w, s->image, kLatent, kHidden, sp, 128, Epilogue::FinalEuler, fin, nsm, st),
+    ERNIE_LAUNCH(session_gemm(s, s->a, hd.final_w, s->image, kLatent, kHidden, 128, Epilogue::FinalEuler, fin),
                  "final linear + Euler");
     return ERNIE_CUDA_OK;
 }

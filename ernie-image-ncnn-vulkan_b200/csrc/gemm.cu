@@ -27,13 +27,15 @@ namespace
 {
 constexpr int BM = 128, BK = 64, kThreads = 192;
 
-template <int BN> struct Cfg
+template <int BN, bool PROMOTE> struct Cfg
 {
+    static_assert(!PROMOTE || BN == 128, "FP32 promotion keeps a 128-column running sum per thread");
     static constexpr int kStages = BN == 256 ? 4 : 6;
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kTmemCols = 2 * BN;
+    // two accumulators (+ a 128-column result buffer when promoting), rounded to a power of two
+    static constexpr int kTmemCols = PROMOTE ? 512 : 2 * BN;
     static constexpr int kBarrierBytes = 8 * (2 * kStages + 4) + 16;
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
 };
@@ -109,7 +111,8 @@ __device__ __forceinline__ void epi_resid_gate(uint32_t taddr, int row, bool val
     }
 }
 
-// BN = 256: the tile spans two 128-wide heads of one of Q, K or V (weights are [Wq; Wk; Wv]).
+// The tile spans BN/128 whole 128-wide heads of one of Q, K or V (weights are [Wq; Wk; Wv]).
+template <int BN>
 __device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int col0, const GemmEpilogueArgs &a)
 {
     const int part = col0 / kHidden;             // 0 = Q, 1 = K, 2 = V
@@ -119,7 +122,7 @@ __device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int
     const float *gamma = part == 0 ? a.gamma_q : a.gamma_k;
     void *dst_base = part == 0 ? a.q : part == 1 ? a.k : a.v;
 #pragma unroll 1
-    for (int hh = 0; hh < 2; ++hh)
+    for (int hh = 0; hh < BN / 128; ++hh)
     {
         float v[128];
 #pragma unroll
@@ -165,37 +168,43 @@ __device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int
     }
 }
 
-// BN = 256: columns [0,128) are up-projection outputs, [128,256) the matching gate outputs.
+// Interleaved [up; gate] weights in 64-row groups: tile columns g*128 + [0,64) are up-projection
+// outputs of features n_blk*BN/2 + g*64 + [0,64), columns g*128 + [64,128) the matching gate outputs.
+template <int BN>
 __device__ __forceinline__ void epi_geglu(uint32_t taddr, int row, bool valid, int n_blk, const GemmEpilogueArgs &a)
 {
-    const int f0 = n_blk * 128;
 #pragma unroll 1
-    for (int c = 0; c < 128; c += 32)
+    for (int g = 0; g < BN / 128; ++g)
     {
-        float up[32], gate[32];
-        tmem_load_32(taddr + c, up);
-        tmem_load_32(taddr + 128 + c, gate);
-        if (!valid) continue;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
-        if (!a.h_split3)
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 32)
         {
-            __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * a.ffn + f0 + c;
+            float up[32], gate[32];
+            tmem_load_32(taddr + g * 128 + c, up);
+            tmem_load_32(taddr + g * 128 + 64 + c, gate);
+            if (!valid) continue;
+            const int f = n_blk * (BN / 2) + g * 64 + c;
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, up + j);
-        }
-        else
-        {
-            __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * (3 * a.ffn) + f0 + c;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8)
+            for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
+            if (!a.h_split3)
             {
-                __align__(16) __nv_bfloat16 hi[8], mid[8], lo[8];
+                __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * a.ffn + f;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) split3(up[j + t], hi[t], mid[t], lo[t]);
-                *reinterpret_cast<uint4 *>(dst + j) = *reinterpret_cast<const uint4 *>(hi);
-                *reinterpret_cast<uint4 *>(dst + a.ffn + j) = *reinterpret_cast<const uint4 *>(mid);
-                *reinterpret_cast<uint4 *>(dst + 2 * a.ffn + j) = *reinterpret_cast<const uint4 *>(lo);
+                for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, up + j);
+            }
+            else
+            {
+                __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * (3 * a.ffn) + f;
+#pragma unroll
+                for (int j = 0; j < 32; j += 8)
+                {
+                    __align__(16) __nv_bfloat16 hi[8], mid[8], lo[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) split3(up[j + t], hi[t], mid[t], lo[t]);
+                    *reinterpret_cast<uint4 *>(dst + j) = *reinterpret_cast<const uint4 *>(hi);
+                    *reinterpret_cast<uint4 *>(dst + a.ffn + j) = *reinterpret_cast<const uint4 *>(mid);
+                    *reinterpret_cast<uint4 *>(dst + 2 * a.ffn + j) = *reinterpret_cast<const uint4 *>(lo);
+                }
             }
         }
     }
@@ -229,11 +238,28 @@ __device__ __forceinline__ void epi_final_euler(uint32_t taddr, int row, bool va
 }
 
 template <int BN, Epilogue EPI>
+__device__ __forceinline__ void run_epilogue(uint32_t taddr, int row, bool valid, int m, int n_blk,
+                                             const GemmEpilogueArgs &args)
+{
+    const int col0 = n_blk * BN;
+    if constexpr (EPI == Epilogue::F32Bias) epi_f32_bias<BN>(taddr, row, valid, col0, args);
+    else if constexpr (EPI == Epilogue::ResidGate) epi_resid_gate<BN>(taddr, row, valid, col0, args);
+    else if constexpr (EPI == Epilogue::Qkv) epi_qkv<BN>(taddr, row, valid, col0, args);
+    else if constexpr (EPI == Epilogue::Geglu) epi_geglu<BN>(taddr, row, valid, n_blk, args);
+    else epi_final_euler(taddr, row, valid, m, args);
+}
+
+// PROMOTE (FP32-exact mode): the tensor core's FP32 accumulation error grows linearly with the
+// length of one TMEM accumulation chain (measured on B200: nrmse 4.4e-6 at K=4096, 1.4e-5 at
+// K=12288 for exact operands; 6.5e-8 when restarted every 64 elements). With PROMOTE the MMA warp
+// restarts the accumulator every `group` k-blocks (two alternating TMEM buffers) and the epilogue
+// warps add each partial into FP32 registers, so no chain exceeds group*64 products.
+template <int BN, Epilogue EPI, bool PROMOTE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m, int n,
-                int k_b, int splits, GemmEpilogueArgs args)
+                int k_b, int splits, int group, GemmEpilogueArgs args)
 {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, PROMOTE>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -250,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int num_m = (m + BM - 1) / BM, num_n = n / BN, tiles = num_m * num_n;
     const int k_blocks = (k_b * splits) / BK;
+    const int span = PROMOTE ? group : k_blocks; // k-blocks per accumulation chain
 
     if (threadIdx.x == 0)
     {
@@ -320,70 +347,111 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            int it = 0;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it)
+            int unit = 0;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
-                const int acc = it & 1;
-                const uint32_t acc_phase = (it >> 1) & 1;
-                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u))
+                for (int kb0 = 0; kb0 < k_blocks && ok; kb0 += span, ++unit)
                 {
-                    if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < k_blocks; ++kb)
-                {
-                    if (!mbar_wait(full_bar(stage), phase))
+                    const int acc = unit & 1;
+                    const uint32_t acc_phase = (unit >> 1) & 1;
+                    if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u))
                     {
                         if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t a_desc = smem_desc_sw128(tile_a(stage));
-                    const uint64_t b_desc = smem_desc_sw128(tile_b(stage));
-#pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        umma_bf16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
-                    umma_commit(empty_bar(stage));
-                    if (++stage == C::kStages)
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    for (int kb = kb0; kb < kb0 + span; ++kb)
                     {
-                        stage = 0;
-                        phase ^= 1u;
+                        if (!mbar_wait(full_bar(stage), phase))
+                        {
+                            if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint64_t a_desc = smem_desc_sw128(tile_a(stage));
+                        const uint64_t b_desc = smem_desc_sw128(tile_b(stage));
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            umma_bf16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
+                                      (kb != kb0 || k != 0) ? 1u : 0u);
+                        umma_commit(empty_bar(stage));
+                        if (++stage == C::kStages)
+                        {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                     }
+                    if (ok) umma_commit(tfull_bar(acc));
                 }
-                umma_commit(tfull_bar(acc));
             }
         }
     }
     else
     {
         const int quarter = warp & 3;
-        int it = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it)
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        int unit = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
         {
             const int m_blk = tile % num_m, n_blk = tile / num_m;
-            const int acc = it & 1;
-            const uint32_t acc_phase = (it >> 1) & 1;
-            if (!mbar_wait(tfull_bar(acc), acc_phase))
-            {
-                if (args.error_flag && lane == 0) atomicExch(args.error_flag, kErrGemmEpilogueTimeout);
-                break;
-            }
-            tc_fence_after();
             const int row = m_blk * BM + quarter * 32 + lane;
             const bool valid = row < m;
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-            const int col0 = n_blk * BN;
-            if constexpr (EPI == Epilogue::F32Bias) epi_f32_bias<BN>(taddr, row, valid, col0, args);
-            else if constexpr (EPI == Epilogue::ResidGate) epi_resid_gate<BN>(taddr, row, valid, col0, args);
-            else if constexpr (EPI == Epilogue::Qkv) epi_qkv(taddr, row, valid, col0, args);
-            else if constexpr (EPI == Epilogue::Geglu) epi_geglu(taddr, row, valid, n_blk, args);
-            else epi_final_euler(taddr, row, valid, m, args);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(acc));
+            if constexpr (!PROMOTE)
+            {
+                const int acc = unit & 1;
+                const uint32_t acc_phase = (unit >> 1) & 1;
+                if (!mbar_wait(tfull_bar(acc), acc_phase))
+                {
+                    if (args.error_flag && lane == 0) atomicExch(args.error_flag, kErrGemmEpilogueTimeout);
+                    break;
+                }
+                tc_fence_after();
+                run_epilogue<BN, EPI>(lane_base + acc * BN, row, valid, m, n_blk, args);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(acc));
+                ++unit;
+            }
+            else
+            {
+                float sum[BN];
+#pragma unroll
+                for (int j = 0; j < BN; ++j) sum[j] = 0.f;
+                for (int kb0 = 0; kb0 < k_blocks; kb0 += span, ++unit)
+                {
+                    const int acc = unit & 1;
+                    const uint32_t acc_phase = (unit >> 1) & 1;
+                    if (!mbar_wait(tfull_bar(acc), acc_phase))
+                    {
+                        if (args.error_flag && lane == 0) atomicExch(args.error_flag, kErrGemmEpilogueTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < BN; c += 32)
+                    {
+                        float v[32];
+                        tmem_load_32(lane_base + acc * BN + c, v);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[c + j] += v[j];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty_bar(acc));
+                }
+                if (!ok) break;
+                // the FP32 sum goes to the result buffer (columns 2*BN..3*BN) for the shared epilogues
+                const uint32_t result = lane_base + 2 * BN;
+#pragma unroll
+                for (int c = 0; c < BN; c += 32) tmem_store_32(result + c, sum + c);
+                tmem_store_wait();
+                run_epilogue<BN, EPI>(result, row, valid, m, n_blk, args);
+            }
         }
     }
     __syncthreads();
@@ -425,74 +493,86 @@ bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, u
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, Epilogue EPI> cudaError_t ensure_attributes()
+template <int BN, Epilogue EPI, bool PROMOTE> cudaError_t ensure_attributes()
 {
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg<BN>::kSmemBytes);
+        attr = cudaFuncSetAttribute(gemm_kernel<BN, EPI, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg<BN, PROMOTE>::kSmemBytes);
     });
     return attr;
 }
 
-template <int BN, Epilogue EPI>
+template <int BN, Epilogue EPI, bool PROMOTE>
 int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits,
                 const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream)
 {
-    using C = Cfg<BN>;
-    const cudaError_t attr = ensure_attributes<BN, EPI>();
+    using C = Cfg<BN, PROMOTE>;
+    const cudaError_t attr = ensure_attributes<BN, EPI, PROMOTE>();
     if (attr != cudaSuccess) return attr;
     CUtensorMap map_a, map_b;
     if (!make_map(&map_a, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k_b) * splits, BM) ||
         !make_map(&map_b, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k_b), BN))
         return cudaErrorInvalidValue;
+    const int k_blocks = k_b * splits / BK;
+    const int group = k_blocks % 2 == 0 ? 2 : 1; // promotion every 128 (or 64) products
     const int tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_kernel<BN, EPI><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, args);
+    gemm_kernel<BN, EPI, PROMOTE><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, group,
+                                                                             args);
     return cudaGetLastError();
+}
+
+template <int BN, bool PROMOTE>
+int dispatch(Epilogue epilogue, const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits,
+             const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream)
+{
+    switch (epilogue)
+    {
+    case Epilogue::F32Bias: return launch_impl<BN, Epilogue::F32Bias, PROMOTE>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::ResidGate: return launch_impl<BN, Epilogue::ResidGate, PROMOTE>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::Qkv: return launch_impl<BN, Epilogue::Qkv, PROMOTE>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::Geglu: return launch_impl<BN, Epilogue::Geglu, PROMOTE>(a, b, m, n, k_b, splits, args, num_sms, stream);
+    case Epilogue::FinalEuler:
+        if constexpr (BN == 128) return launch_impl<BN, Epilogue::FinalEuler, PROMOTE>(a, b, m, n, k_b, splits, args, num_sms, stream);
+        return cudaErrorInvalidValue;
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int BN, bool PROMOTE> cudaError_t prepare_all()
+{
+    cudaError_t e = ensure_attributes<BN, Epilogue::F32Bias, PROMOTE>();
+    if (e == cudaSuccess) e = ensure_attributes<BN, Epilogue::ResidGate, PROMOTE>();
+    if (e == cudaSuccess) e = ensure_attributes<BN, Epilogue::Qkv, PROMOTE>();
+    if (e == cudaSuccess) e = ensure_attributes<BN, Epilogue::Geglu, PROMOTE>();
+    if constexpr (BN == 128)
+        if (e == cudaSuccess) e = ensure_attributes<BN, Epilogue::FinalEuler, PROMOTE>();
+    return e;
 }
 } // namespace
 
 int prepare_gemm_kernels()
 {
-    cudaError_t e = ensure_attributes<256, Epilogue::F32Bias>();
-    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::ResidGate>();
-    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::Qkv>();
-    if (e == cudaSuccess) e = ensure_attributes<256, Epilogue::Geglu>();
-    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::F32Bias>();
-    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::ResidGate>();
-    if (e == cudaSuccess) e = ensure_attributes<128, Epilogue::FinalEuler>();
+    cudaError_t e = prepare_all<256, false>();
+    if (e == cudaSuccess) e = prepare_all<128, false>();
+    if (e == cudaSuccess) e = prepare_all<128, true>();
     return e;
 }
 
 int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits, int block_n,
-                Epilogue epilogue, const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream)
+                Epilogue epilogue, const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream, bool promote)
 {
     if (m < 1 || n < 1 || k_b < BK || k_b % BK || splits < 1 || splits > 3 || num_sms < 1) return cudaErrorInvalidValue;
     if (block_n != 128 && block_n != 256) return cudaErrorInvalidValue;
+    if (promote && block_n != 128) return cudaErrorInvalidValue;
     if (n % block_n) return cudaErrorInvalidValue;
-    if ((epilogue == Epilogue::Qkv || epilogue == Epilogue::Geglu) && block_n != 256) return cudaErrorInvalidValue;
     if (epilogue == Epilogue::FinalEuler && (block_n != 128 || n != 128)) return cudaErrorInvalidValue;
     if (epilogue == Epilogue::Qkv && (n != 3 * kHidden || args.rows_pad < m)) return cudaErrorInvalidValue;
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
-    if (block_n == 256)
-    {
-        switch (epilogue)
-        {
-        case Epilogue::F32Bias: return launch_impl<256, Epilogue::F32Bias>(a, b, m, n, k_b, splits, args, num_sms, stream);
-        case Epilogue::ResidGate: return launch_impl<256, Epilogue::ResidGate>(a, b, m, n, k_b, splits, args, num_sms, stream);
-        case Epilogue::Qkv: return launch_impl<256, Epilogue::Qkv>(a, b, m, n, k_b, splits, args, num_sms, stream);
-        case Epilogue::Geglu: return launch_impl<256, Epilogue::Geglu>(a, b, m, n, k_b, splits, args, num_sms, stream);
-        default: return cudaErrorInvalidValue;
-        }
-    }
-    switch (epilogue)
-    {
-    case Epilogue::F32Bias: return launch_impl<128, Epilogue::F32Bias>(a, b, m, n, k_b, splits, args, num_sms, stream);
-    case Epilogue::ResidGate: return launch_impl<128, Epilogue::ResidGate>(a, b, m, n, k_b, splits, args, num_sms, stream);
-    case Epilogue::FinalEuler: return launch_impl<128, Epilogue::FinalEuler>(a, b, m, n, k_b, splits, args, num_sms, stream);
-    default: return cudaErrorInvalidValue;
-    }
+    if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
+    if (block_n == 256) return dispatch<256, false>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
+    return dispatch<128, false>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
 }
 } // namespace ernie_b200

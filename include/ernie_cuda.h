@@ -41,7 +41,7 @@ extern "C" {
 /* Block tensor ids for ernie_cuda_model_read_tensor (test hook). */
 #define ERNIE_TENSOR_WQKV 0  /* [12288,4096] = [Wq; Wk; Wv] */
 #define ERNIE_TENSOR_WO 1    /* [4096,4096] */
-#define ERNIE_TENSOR_WUPGATE 2 /* [24576,4096], 128-row groups interleaved: up g, gate g, ... */
+#define ERNIE_TENSOR_WUPGATE 2 /* [24576,4096], 64-row groups interleaved: up g, gate g, ... */
 #define ERNIE_TENSOR_WFC2 3  /* [4096,12288] */
 
 typedef struct ernie_cuda_context ernie_cuda_context;

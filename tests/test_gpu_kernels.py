@@ -35,7 +35,7 @@ def test_linear_random(ctx, m, n, k):
     got = ctx.linear_bf16(a, w, bias)
     ref = o.bf16_to_f32(a).astype(np.float64) @ o.bf16_to_f32(w).astype(np.float64).T + bias
     err = np.abs(got - ref).max() / np.abs(ref).max()
-    assert err < 1e-5, err
+    assert err < 3e-5, err  # FP32 accumulation over K up to 12288
 
 
 def test_device_weights_match_host_generator(ctx):
@@ -47,7 +47,7 @@ def test_device_weights_match_host_generator(ctx):
         assert np.array_equal(wqkv[:4096], host.mats[o.WQ])
         assert np.array_equal(wqkv[4096:8192], host.mats[o.WK])
         assert np.array_equal(wqkv[8192:], host.mats[o.WV])
-        ug = model.read_tensor(1, ec.TENSOR_WUPGATE, 2 * 12288 * 4096).reshape(96, 2, 128, 4096)
+        ug = model.read_tensor(1, ec.TENSOR_WUPGATE, 2 * 12288 * 4096).reshape(192, 2, 64, 4096)
         assert np.array_equal(ug[:, 0].reshape(12288, 4096), host.mats[o.WUP])
         assert np.array_equal(ug[:, 1].reshape(12288, 4096), host.mats[o.WGATE])
         fc2 = model.read_tensor(1, ec.TENSOR_WFC2, 4096 * 12288).reshape(4096, 12288)
