@@ -1178,3 +1178,14 @@ extern "C" int ernie_cuda_session_launches_per_step(ernie_cuda_session *s, int *
     *launches = 6 + 7 * s->model->num_blocks + 2;
     return ERNIE_CUDA_OK;
 }
+
+// Accessors for entry points defined in other translation units (finite_noalloc.cu).
+int ernie_cuda_record_error(int code, const char *message) { return fail(code, message); }
+
+int ernie_cuda_context_device_and_stream(ernie_cuda_context *ctx, int *device, cudaStream_t *stream)
+{
+    if (!ctx || !device || !stream) return ERNIE_CUDA_ERROR;
+    *device = ctx->device;
+    *stream = ctx->stream;
+    return ERNIE_CUDA_OK;
+}

@@ -106,6 +106,7 @@ SIGNATURES = {
     "ernie_cuda_session_denoise": (I, [P, P, P, I, I, I, I, P, ctypes.POINTER(I)]),
     "ernie_cuda_session_profile": (I, [P, I, I, ctypes.POINTER(F)]),
     "ernie_cuda_session_launches_per_step": (I, [P, ctypes.POINTER(I)]),
+    "ernie_cuda_finite_latent_noalloc": (I, [P, P, I, I, ctypes.POINTER(I)]),
 }
 
 

@@ -190,6 +190,17 @@ int ernie_cuda_session_denoise_device(ernie_cuda_session *session, int steps, in
 int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial, float *final_latent, int steps,
                                int start_step, int end_step, int schedule, float *predictions, int *failed_step);
 
+/* Non-finite check that allocates no device memory. It has no counterpart in the reference.
+   Callers that cannot call cudaMalloc when they need the check (a stream capture in progress
+   elsewhere in the process, an application that forbids device allocation after start-up) use it
+   instead of ernie_cuda_finite_latent, which allocates a status word per call. Scratch is a fixed
+   512-byte device array (128 per-channel status words) that every GPU loading the library holds
+   until exit; latents outside 128 x [1..256] x [1..256] are rejected (-1). The first call on each
+   device looks up that array's device address, so make it before any stream capture. Every call
+   shares the array and clears it first; calls that overlap on the GPU race on it. */
+int ernie_cuda_finite_latent_noalloc(ernie_cuda_context *ctx, const float *latent, int width, int height,
+                                     int *finite);
+
 /* Benchmark hooks: average device time in ms of `iters` back-to-back launches of one kernel of
    block 0 on the session's buffers (kernel 0 norm+modulate, 1 QKV GEMM, 2 attention, 3 out-proj
    GEMM, 4 MLP norm+modulate, 5 up/gate GEMM, 6 down GEMM), and the number of kernels one denoise
