@@ -161,6 +161,30 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+KERNELS = {"norm_modulate": 0, "qkv_gemm": 1, "attention": 2, "out_gemm": 3, "upgate_gemm": 5, "down_gemm": 6}
+
+
+def run_kernel_only(args):
+    """Set up the C2 session (with --blocks resident blocks) and launch one block kernel `iters` times.
+    Used under ncu on a small case: a 2-block model keeps the device footprint near 1.6 GB while every
+    operand of the C2 kernels is still larger than L2."""
+    import ernie_cuda as ec
+    ctx = ec.Context(0)
+    model = ec.Model(ctx, args.blocks)
+    model.synthesize(1234)
+    session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, ec.BF16 if args.precision == "bf16" else ec.FP32)
+    rng = np.random.default_rng(0)
+    cos, sin, mask = ec.dit_constants(WIDTH, HEIGHT, VALID, TEXT)
+    session.set_conditioning(rng.standard_normal((TEXT, 3072), dtype=np.float32), cos, sin, mask)
+    session.denoise(rng.standard_normal((128, HEIGHT, WIDTH), dtype=np.float32), STEPS_PER_IMAGE, 0, 1)
+    # the buffers now hold one real step's activations; each block kernel ran `blocks` times above
+    ms = session.profile(KERNELS[args.kernel_only], args.iters)
+    print(json.dumps({"kernel": args.kernel_only, "ms_per_launch": ms, "launches": args.iters + 1}), flush=True)
+    session.close()
+    model.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -171,7 +195,12 @@ def main():
     ap.add_argument("--blocks", type=int, default=NUM_BLOCKS, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
+                    help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
+    ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
+    if args.kernel_only:
+        return run_kernel_only(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -223,6 +223,7 @@ extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
     for (int i = 0; i < 16 && e == cudaSuccess; ++i) e = cudaEventCreate(&ctx->events[i]);
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_gemm_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_attention_kernels());
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_kernels());
     if (e != cudaSuccess)
     {
         ernie_cuda_context_destroy(ctx);
@@ -562,15 +563,15 @@ extern "C" int ernie_cuda_sdpa(ernie_cuda_context *ctx, const float *q, const fl
     return from_launch(launch_attention_f32(a, ctx->stream), "SDPA");
 }
 
-extern "C" int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+extern "C" int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *vt,
                                     const float *mask, int heads, int nq, int rows_pad, int kv_len, uint16_t *out)
 {
-    if (!ctx || !q || !k || !v || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!ctx || !q || !k || !vt || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
     DeviceGuard guard(ctx->device);
-    return from_launch(launch_attention_bf16(reinterpret_cast<const __nv_bfloat16 *>(q),
-                                             reinterpret_cast<const __nv_bfloat16 *>(k),
-                                             reinterpret_cast<const __nv_bfloat16 *>(v), mask, nq, rows_pad, kv_len,
-                                             heads, reinterpret_cast<__nv_bfloat16 *>(out), ctx->stream),
+    return from_launch(launch_flash_tc(reinterpret_cast<const __nv_bfloat16 *>(q),
+                                       reinterpret_cast<const __nv_bfloat16 *>(k),
+                                       reinterpret_cast<const __nv_bfloat16 *>(vt), mask, nq, rows_pad, kv_len, heads,
+                                       reinterpret_cast<__nv_bfloat16 *>(out), ctx->error_flag, ctx->stream),
                        "SDPA bf16");
 }
 
@@ -897,6 +898,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.v = s->v;
     qkv.rows_pad = s->rows_pad;
     qkv.qkv_fp32 = fp32;
+    qkv.v_transposed = !fp32;
     qkv.gamma_q = w.gamma_q;
     qkv.gamma_k = w.gamma_k;
     qkv.cos_t = s->cos_t;
@@ -926,9 +928,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
         ERNIE_LAUNCH(launch_attention_f32(a, st), "attention");
     }
     else
-        ERNIE_LAUNCH(launch_attention_bf16(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
-                                           static_cast<const __nv_bfloat16 *>(s->v), s->use_mask ? s->mask : nullptr, T,
-                                           s->rows_pad, s->kv_len, kHeads, s->a, st),
+        ERNIE_LAUNCH(launch_flash_tc(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
+                                     static_cast<const __nv_bfloat16 *>(s->v), s->use_mask ? s->mask : nullptr, T,
+                                     s->rows_pad, s->kv_len, kHeads, s->a, s->ctx->error_flag, st),
                      "attention");
     GemmEpilogueArgs res;
     res.resid = x;

@@ -152,6 +152,15 @@ __device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int
                 v[d + 64] = second * __ldg(cs + d + 64) + first * __ldg(sn + d + 64);
             }
         }
+        if (part == 2 && a.v_transposed)
+        {
+            // V^T [head][dim][token]: lanes hold consecutive tokens, so each dim is a 64-byte run
+            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) +
+                                 static_cast<size_t>(head0 + hh) * kHeadDim * a.rows_pad + row;
+#pragma unroll
+            for (int d = 0; d < 128; ++d) dst[static_cast<size_t>(d) * a.rows_pad] = __float2bfloat16_rn(v[d]);
+            continue;
+        }
         const size_t offset = (static_cast<size_t>(head0 + hh) * a.rows_pad + row) * kHeadDim;
         if (a.qkv_fp32)
         {

@@ -15,7 +15,7 @@ enum class Epilogue : int
     F32Bias = 0,    // out[r, c] = acc + bias[c] (bias may be null), FP32, row stride ldo
     Qkv = 1,        // per-head qk-RMSNorm + 3-axis RoPE on Q,K; write Q,K,V head-major
     ResidGate = 2,  // resid[r, c] += gate[c] * acc (FP32, in place)
-    Geglu = 3,      // h[r, f] = up * gelu_erf(gate) from interleaved [up; gate] 128-column groups
+    Geglu = 3,      // h[r, f] = up * gelu_erf(gate) from [up; gate] weights interleaved in 64-row groups
     FinalEuler = 4, // pred = acc + bias; latent[c][r] = latent + delta * pred (no FMA); finite flag
 };
 
@@ -32,6 +32,7 @@ struct GemmEpilogueArgs
     void *q = nullptr, *k = nullptr, *v = nullptr; // [heads][rows_pad][128], BF16 or FP32
     int rows_pad = 0;
     int qkv_fp32 = 0;
+    int v_transposed = 0; // BF16 mode: V written as [heads][128][rows_pad] for the tcgen05 attention
     const float *gamma_q = nullptr, *gamma_k = nullptr; // [128]
     const float *cos_t = nullptr, *sin_t = nullptr;     // [rows][128]
     // Geglu: BF16 [rows][ffn] or, when split3, hi/mid/lo BF16 planes at column offsets 0, ffn, 2*ffn
@@ -69,11 +70,13 @@ int launch_to_operand(const float *src, long long rows, int cols, __nv_bfloat16 
 int launch_gemv(const __nv_bfloat16 *w, const float *x, const float *bias, float *y, int n, int k, int silu_input,
                 cudaStream_t stream);
 
-// BF16 flash attention (head dim 128) over head-major Q/K/V [heads][rows_pad][128]; keys >= kv_len
-// are excluded, `mask` (nullable) adds a per-key row. Output token-major BF16 [rows][heads*128].
-int launch_attention_bf16(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *v,
-                          const float *mask, int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out,
-                          cudaStream_t stream);
+// tcgen05 flash attention (BF16 operands, FP32 softmax/accumulation in TMEM and registers):
+// q, k head-major [heads][rows_pad][128], vt transposed [heads][128][rows_pad]; keys >= kv_len
+// excluded, optional additive row mask [rows]. Output token-major BF16 [rows][heads*128].
+int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
+                    int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out, int *error_flag,
+                    cudaStream_t stream);
+int prepare_flash_kernels();
 
 // FP32 attention with FP64 softmax accumulation. q [heads][q_stride rows][width] (head stride
 // q_head_stride elements), k/v [kv_heads][...]; mask [mask_heads][mask_rows][nk] additive (nullable).

@@ -123,10 +123,11 @@ int ernie_cuda_model_bytes(ernie_cuda_model *model, uint64_t *bytes);
    width 1..128. FP32 in/out, FP64 softmax accumulation. */
 int ernie_cuda_sdpa(ernie_cuda_context *ctx, const float *q, const float *k, const float *v, const float *mask,
                     int heads, int kv_heads, int mask_heads, int mask_rows, int nq, int nk, int width, float *out);
-/* BF16 flash path of the same operator on head-major BF16 q/k/v [heads][rows_pad][128]
-   (rows_pad a multiple of 128, rows beyond nq zero), keys >= kv_len excluded, optional row mask
-   [nq]. Output token-major BF16 [nq][heads*128]. */
-int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+/* BF16 flash path of the same operator (tcgen05/TMEM kernel) on head-major BF16 q/k
+   [heads][rows_pad][128] and transposed v [heads][128][rows_pad] (rows_pad a multiple of 128, padded
+   rows zero), keys >= kv_len excluded, optional additive row mask [nq]. Output token-major BF16
+   [nq][heads*128]. */
+int ernie_cuda_sdpa_bf16(ernie_cuda_context *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *vt,
                          const float *mask, int heads, int nq, int rows_pad, int kv_len, uint16_t *out);
 /* set_attention_query_rows (src/ernie_attention.cpp:245-255): 128, 64, 32 or 16, else -1.
    The flash kernels need no query chunking; the value is recorded for the recovery contract. */

@@ -82,8 +82,9 @@ def test_sdpa_accuracy_probe(ctx):
     assert np.sqrt((err ** 2).sum() / (ref ** 2).sum()) <= 5e-7
 
 
-@pytest.mark.parametrize("n,valid", [(288, 280), (1056, 1048), (4160, 4160)])
-def test_sdpa_bf16_flash(ctx, n, valid):
+@pytest.mark.parametrize("n,valid,masked", [(288, 280, False), (1056, 1048, False), (4160, 4160, False),
+                                            (200, 130, True), (100, 100, False), (6176, 5208, False)])
+def test_sdpa_bf16_flash(ctx, n, valid, masked):
     rng = np.random.default_rng(n)
     heads, pad = 4, (n + 127) // 128 * 128
     q = np.zeros((heads, pad, 128), np.float32)
@@ -93,16 +94,25 @@ def test_sdpa_bf16_flash(ctx, n, valid):
     k[:, :n] = rng.standard_normal((heads, n, 128)) * 1.5
     v[:, :n] = rng.standard_normal((heads, n, 128))
     qb, kb, vb = bf16_bits(q), bf16_bits(k), bf16_bits(v)
-    bq, bk, bv = ctx.to_device(qb), ctx.to_device(kb), ctx.to_device(vb)
+    vt = np.ascontiguousarray(vb.transpose(0, 2, 1))  # the tcgen05 kernel takes V^T [heads][128][rows_pad]
+    bq, bk, bv = ctx.to_device(qb), ctx.to_device(kb), ctx.to_device(vt)
     out = ctx.buffer(n * heads * 128 * 2)
-    ec.check(ec.lib().ernie_cuda_sdpa_bf16(ctx.handle, bq.c, bk.c, bv.c, None, heads, n, pad, valid, out.c))
+    mask = None
+    if masked:  # additive row mask inside the valid range (a general ErnieSDPA row mask)
+        mask = np.where(np.arange(n) % 7 == 3, np.float32(-1e30), np.float32(0.0)).astype(np.float32)
+        mask[:valid] += rng.uniform(-2.0, 0.0, valid).astype(np.float32) * (np.arange(valid) % 7 != 3)
+    bm = ctx.to_device(mask) if masked else None
+    ec.check(ec.lib().ernie_cuda_sdpa_bf16(ctx.handle, bq.c, bk.c, bv.c, bm.c if bm else None, heads, n, pad, valid,
+                                           out.c))
     ctx.synchronize()
     got = o.bf16_to_f32(out.download((n, heads * 128), np.uint16)).reshape(n, heads, 128).transpose(1, 0, 2)
-    ref = o.sdpa(o.bf16_to_f32(qb)[:, :n], o.bf16_to_f32(kb)[:, :valid], o.bf16_to_f32(vb)[:, :valid])
+    ref = o.sdpa(o.bf16_to_f32(qb)[:, :n], o.bf16_to_f32(kb)[:, :valid], o.bf16_to_f32(vb)[:, :valid],
+                 None if mask is None else mask[:valid])
     err = got.astype(np.float64) - ref
     assert np.sqrt((err ** 2).sum() / (ref.astype(np.float64) ** 2).sum()) < 1e-2
-    for b in (bq, bk, bv, out):
-        b.free()
+    for b in (bq, bk, bv, out, bm):
+        if b:
+            b.free()
 
 
 @pytest.mark.parametrize("shape", [0, 1])
