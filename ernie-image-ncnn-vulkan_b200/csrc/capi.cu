@@ -937,7 +937,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     res.ldo = kHidden;
     res.gate = gate_sa;
     res.error_flag = s->ctx->error_flag;
-    if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 128, Epilogue::ResidGate, res), "out proj");
+    if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 256, Epilogue::ResidGate, res), "out proj");
     if (on(4))
         ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
     GemmEpilogueArgs gg;
@@ -947,7 +947,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     gg.error_flag = s->ctx->error_flag;
     if (on(5)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wug, T, 2 * kFfn, kHidden, 256, Epilogue::Geglu, gg), "up/gate");
     res.gate = gate_mlp;
-    if (on(6)) ERNIE_LAUNCH(session_gemm(s, s->h, w.wfc2, T, kHidden, kFfn, 128, Epilogue::ResidGate, res), "down");
+    if (on(6)) ERNIE_LAUNCH(session_gemm(s, s->h, w.wfc2, T, kHidden, kFfn, 256, Epilogue::ResidGate, res), "down");
     return ERNIE_CUDA_OK;
 }
 

@@ -36,8 +36,11 @@ template <int BN, bool PROMOTE> struct Cfg
     static constexpr int kStageBytes = kABytes + kBBytes;
     // two accumulators (+ a 128-column result buffer when promoting), rounded to a power of two
     static constexpr int kTmemCols = PROMOTE ? 512 : 2 * BN;
-    static constexpr int kBarrierBytes = 8 * (2 * kStages + 4) + 16;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+    static constexpr int kBarrierBytes = 256;
+    // per-epilogue-warp staging tile for coalesced global stores (FP32 [32][36] or BF16 [64][40])
+    static constexpr int kStagingBytes = 5120;
+    static constexpr int kStagingOffset = kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kSmemBytes = kStagingOffset + 4 * kStagingBytes + 1024;
 };
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * erfcf(-0.7071067811865475f * x); }
@@ -64,17 +67,42 @@ __device__ __forceinline__ void store_f32x4(float *dst, const float *v)
     *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
 }
 
-// ---- epilogues: one thread owns one output row of the 128-row tile ---------------------------
-template <int BN>
-__device__ __forceinline__ void epi_f32_bias(uint32_t taddr, int row, bool valid, int col0,
-                                             const GemmEpilogueArgs &a)
+// ---- epilogues ---------------------------------------------------------------------------------
+// Each epilogue warp owns 32 rows of the 128-row tile (its TMEM lane quarter); tcgen05.ld gives
+// thread `lane` row row0 + lane. Stores that would be strided by a full output row per thread are
+// staged through the warp's shared-memory tile and written as whole 64/128-byte row segments.
+struct EpiCtx
 {
+    uint32_t taddr; // TMEM address of the accumulator (this warp's lane quarter, column 0)
+    int row0;       // first output row of this warp
+    int lane;
+    int m;          // valid rows
+    int n_blk;
+    uint8_t *stage; // this warp's staging tile
+};
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float *v)
+{
+    uint4 r;
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]), p1 = __floats2bfloat162_rn(v[2], v[3]);
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(v[4], v[5]), p3 = __floats2bfloat162_rn(v[6], v[7]);
+    r.x = *reinterpret_cast<uint32_t *>(&p0);
+    r.y = *reinterpret_cast<uint32_t *>(&p1);
+    r.z = *reinterpret_cast<uint32_t *>(&p2);
+    r.w = *reinterpret_cast<uint32_t *>(&p3);
+    return r;
+}
+
+template <int BN> __device__ __forceinline__ void epi_f32_bias(const EpiCtx &e, const GemmEpilogueArgs &a)
+{
+    const int row = e.row0 + e.lane, col0 = e.n_blk * BN;
+    const bool valid = row < e.m;
     float *out = a.out + static_cast<size_t>(row) * a.ldo + col0;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32)
     {
         float v[32];
-        tmem_load_32(taddr + c, v);
+        tmem_load_32(e.taddr + c, v);
         if (!valid) continue;
         if (a.bias)
         {
@@ -86,102 +114,168 @@ __device__ __forceinline__ void epi_f32_bias(uint32_t taddr, int row, bool valid
     }
 }
 
-template <int BN>
-__device__ __forceinline__ void epi_resid_gate(uint32_t taddr, int row, bool valid, int col0,
-                                               const GemmEpilogueArgs &a)
+// gemm_3 / gemm_6 + mul_15 / mul_21 + add_16 / add_22: resid += gate * acc, FP32, coalesced rows.
+template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
-    float *resid = a.resid + static_cast<size_t>(row) * a.ldo + col0;
+    float *st = reinterpret_cast<float *>(e.stage); // [32][36]
+    const int col0 = e.n_blk * BN, cc = (e.lane & 7) * 4;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32)
     {
         float v[32];
-        tmem_load_32(taddr + c, v);
-        if (!valid) continue;
+        tmem_load_32(e.taddr + c, v);
+        float4 *mine = reinterpret_cast<float4 *>(st + e.lane * 36);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
+        for (int j = 0; j < 8; ++j) mine[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        __syncwarp();
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(a.gate + col0 + c + cc));
+        // all eight residual loads are issued before any store, so their latencies overlap
+        float4 r[8];
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
         {
-            float4 r = *reinterpret_cast<const float4 *>(resid + c + j);
-            const float4 g = __ldg(reinterpret_cast<const float4 *>(a.gate + col0 + c + j));
-            r.x += g.x * v[j];
-            r.y += g.y * v[j + 1];
-            r.z += g.z * v[j + 2];
-            r.w += g.w * v[j + 3];
-            *reinterpret_cast<float4 *>(resid + c + j) = r;
+            const int row = e.row0 + p * 4 + (e.lane >> 3);
+            r[p] = row < e.m ? *reinterpret_cast<const float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+        {
+            const int rr = p * 4 + (e.lane >> 3), row = e.row0 + rr;
+            const float4 acc = *reinterpret_cast<const float4 *>(st + rr * 36 + cc);
+            r[p].x += g.x * acc.x;
+            r[p].y += g.y * acc.y;
+            r[p].z += g.z * acc.z;
+            r[p].w += g.w * acc.w;
+            if (row < e.m)
+                *reinterpret_cast<float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc) = r[p];
+        }
+        __syncwarp();
     }
 }
 
 // The tile spans BN/128 whole 128-wide heads of one of Q, K or V (weights are [Wq; Wk; Wv]).
-template <int BN>
-__device__ __forceinline__ void epi_qkv(uint32_t taddr, int row, bool valid, int col0, const GemmEpilogueArgs &a)
+// Q, K: rmsn_9 / rmsn_10 + the rotary chain, head-major [head][token][128]; V: head-major, or
+// transposed [head][dim][token] for the tcgen05 attention (BF16 mode).
+template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
-    const int part = col0 / kHidden;             // 0 = Q, 1 = K, 2 = V
+    const int col0 = e.n_blk * BN;
+    const int part = col0 / kHidden; // 0 = Q, 1 = K, 2 = V
     const int head0 = (col0 % kHidden) / kHeadDim;
-    const float *cs = a.cos_t + static_cast<size_t>(valid ? row : 0) * kHeadDim;
-    const float *sn = a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim;
-    const float *gamma = part == 0 ? a.gamma_q : a.gamma_k;
+    const int row = e.row0 + e.lane;
+    const bool valid = row < e.m;
+    const float4 *cs = reinterpret_cast<const float4 *>(a.cos_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
+    const float4 *sn = reinterpret_cast<const float4 *>(a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
+    const float4 *gamma = reinterpret_cast<const float4 *>(part == 0 ? a.gamma_q : a.gamma_k);
     void *dst_base = part == 0 ? a.q : part == 1 ? a.k : a.v;
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh)
     {
+        const int head = head0 + hh;
         float v[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
         {
             float chunk[32];
-            tmem_load_32(taddr + hh * 128 + c * 32, chunk);
+            tmem_load_32(e.taddr + hh * 128 + c * 32, chunk);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[c * 32 + j] = chunk[j];
         }
-        if (!valid) continue;
         if (part < 2)
         {
-            // rmsn_9 / rmsn_10: x * (mean(x^2) + 1e-6)^(-1/2) * gamma over the 128-wide head
+            // x * (mean(x^2) + 1e-6)^(-1/2) * gamma over the 128-wide head
             float squared = 0.f;
 #pragma unroll
             for (int d = 0; d < 128; ++d) squared += v[d] * v[d];
             const float inverse = 1.f / sqrtf(squared * (1.f / 128.f) + 1e-6f);
 #pragma unroll
-            for (int d = 0; d < 128; ++d) v[d] = v[d] * inverse * __ldg(gamma + d);
+            for (int d = 0; d < 128; d += 4)
+            {
+                const float4 g = __ldg(gamma + d / 4);
+                v[d] = v[d] * inverse * g.x;
+                v[d + 1] = v[d + 1] * inverse * g.y;
+                v[d + 2] = v[d + 2] * inverse * g.z;
+                v[d + 3] = v[d + 3] * inverse * g.w;
+            }
             // ERNIE rotary: halves rotated with the full-width, pair-duplicated angle table
 #pragma unroll
-            for (int d = 0; d < 64; ++d)
+            for (int d = 0; d < 64; d += 4)
             {
-                const float first = v[d], second = v[d + 64];
-                v[d] = first * __ldg(cs + d) - second * __ldg(sn + d);
-                v[d + 64] = second * __ldg(cs + d + 64) + first * __ldg(sn + d + 64);
+                const float4 c1 = __ldg(cs + d / 4), s1 = __ldg(sn + d / 4);
+                const float4 c2 = __ldg(cs + 16 + d / 4), s2 = __ldg(sn + 16 + d / 4);
+                const float c1v[4] = {c1.x, c1.y, c1.z, c1.w}, s1v[4] = {s1.x, s1.y, s1.z, s1.w};
+                const float c2v[4] = {c2.x, c2.y, c2.z, c2.w}, s2v[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                {
+                    const float first = v[d + t], second = v[d + t + 64];
+                    v[d + t] = first * c1v[t] - second * s1v[t];
+                    v[d + t + 64] = second * c2v[t] + first * s2v[t];
+                }
             }
         }
-        if (part == 2 && a.v_transposed)
-        {
-            // V^T [head][dim][token]: lanes hold consecutive tokens, so each dim is a 64-byte run
-            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) +
-                                 static_cast<size_t>(head0 + hh) * kHeadDim * a.rows_pad + row;
-#pragma unroll
-            for (int d = 0; d < 128; ++d) dst[static_cast<size_t>(d) * a.rows_pad] = __float2bfloat16_rn(v[d]);
-            continue;
-        }
-        const size_t offset = (static_cast<size_t>(head0 + hh) * a.rows_pad + row) * kHeadDim;
         if (a.qkv_fp32)
         {
-            float *dst = static_cast<float *>(dst_base) + offset;
+            if (valid)
+            {
+                float *dst = static_cast<float *>(dst_base) + (static_cast<size_t>(head) * a.rows_pad + row) * kHeadDim;
 #pragma unroll
-            for (int d = 0; d < 128; d += 4) store_f32x4(dst + d, v + d);
+                for (int d = 0; d < 128; d += 4) store_f32x4(dst + d, v + d);
+            }
+            continue;
         }
-        else
+        __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage);
+        __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
+        if (part == 2 && a.v_transposed)
         {
-            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) + offset;
+            // stage [64 dims][40] then write 64-byte token runs of V^T [head][dim][token]
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half)
+            {
 #pragma unroll
-            for (int d = 0; d < 128; d += 8) store_bf16x8(dst + d, v + d);
+                for (int d = 0; d < 64; ++d) st[d * 40 + e.lane] = __float2bfloat16_rn(v[half * 64 + d]);
+                __syncwarp();
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+                {
+                    const int d = p * 8 + (e.lane >> 2), q4 = e.lane & 3;
+                    const uint4 val = *reinterpret_cast<const uint4 *>(st + d * 40 + q4 * 8);
+                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * kHeadDim + half * 64 + d) * a.rows_pad +
+                                               e.row0 + q4 * 8) = val;
+                }
+                __syncwarp();
+            }
+            continue;
+        }
+        // stage [32 rows][72] then write 128-byte row segments of [head][token][128]
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half)
+        {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<uint4 *>(st + e.lane * 72 + j * 8) = pack_bf16x8(v + half * 64 + j * 8);
+            __syncwarp();
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+            {
+                const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
+                if (row_g < e.m)
+                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * a.rows_pad + row_g) * kHeadDim +
+                                               half * 64 + j * 8) = *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
+            }
+            __syncwarp();
         }
     }
 }
 
 // Interleaved [up; gate] weights in 64-row groups: tile columns g*128 + [0,64) are up-projection
 // outputs of features n_blk*BN/2 + g*64 + [0,64), columns g*128 + [64,128) the matching gate outputs.
-template <int BN>
-__device__ __forceinline__ void epi_geglu(uint32_t taddr, int row, bool valid, int n_blk, const GemmEpilogueArgs &a)
+// gemm_4 + gemm_5 + ErnieGELU + mul_20.
+template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
+    const int row = e.row0 + e.lane;
+    const bool valid = row < e.m;
+    __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage); // [32][40]
 #pragma unroll 1
     for (int g = 0; g < BN / 128; ++g)
     {
@@ -189,20 +283,14 @@ __device__ __forceinline__ void epi_geglu(uint32_t taddr, int row, bool valid, i
         for (int c = 0; c < 64; c += 32)
         {
             float up[32], gate[32];
-            tmem_load_32(taddr + g * 128 + c, up);
-            tmem_load_32(taddr + g * 128 + 64 + c, gate);
-            if (!valid) continue;
-            const int f = n_blk * (BN / 2) + g * 64 + c;
+            tmem_load_32(e.taddr + g * 128 + c, up);
+            tmem_load_32(e.taddr + g * 128 + 64 + c, gate);
+            const int f = e.n_blk * (BN / 2) + g * 64 + c;
 #pragma unroll
             for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
-            if (!a.h_split3)
+            if (a.h_split3)
             {
-                __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * a.ffn + f;
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, up + j);
-            }
-            else
-            {
+                if (!valid) continue;
                 __nv_bfloat16 *dst = a.h + static_cast<size_t>(row) * (3 * a.ffn) + f;
 #pragma unroll
                 for (int j = 0; j < 32; j += 8)
@@ -214,28 +302,44 @@ __device__ __forceinline__ void epi_geglu(uint32_t taddr, int row, bool valid, i
                     *reinterpret_cast<uint4 *>(dst + a.ffn + j) = *reinterpret_cast<const uint4 *>(mid);
                     *reinterpret_cast<uint4 *>(dst + 2 * a.ffn + j) = *reinterpret_cast<const uint4 *>(lo);
                 }
+                continue;
             }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4 *>(st + e.lane * 40 + j * 8) = pack_bf16x8(up + j * 8);
+            __syncwarp();
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+            {
+                const int rr = p * 8 + (e.lane >> 2), q4 = e.lane & 3, row_g = e.row0 + rr;
+                if (row_g < e.m)
+                    *reinterpret_cast<uint4 *>(a.h + static_cast<size_t>(row_g) * a.ffn + f + q4 * 8) =
+                        *reinterpret_cast<const uint4 *>(st + rr * 40 + q4 * 8);
+            }
+            __syncwarp();
         }
     }
 }
 
-// BN = 128 = latent channels. Rows are image tokens; latent and prediction are [128][m].
-__device__ __forceinline__ void epi_final_euler(uint32_t taddr, int row, bool valid, int m,
-                                                const GemmEpilogueArgs &a)
+// BN = 128 = latent channels. Rows are image tokens; latent and prediction are [128][m]
+// (consecutive lanes hold consecutive tokens, so these accesses are already coalesced).
+__device__ __forceinline__ void epi_final_euler(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
+    const int row = e.row0 + e.lane;
+    const bool valid = row < e.m;
     bool finite = true;
 #pragma unroll 1
     for (int c = 0; c < 128; c += 32)
     {
         float v[32];
-        tmem_load_32(taddr + c, v);
+        tmem_load_32(e.taddr + c, v);
         if (!valid) continue;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
         {
             const int ch = c + j;
             const float prediction = v[j] + __ldg(a.bias + ch);
-            const size_t idx = static_cast<size_t>(ch) * m + row;
+            const size_t idx = static_cast<size_t>(ch) * e.m + row;
             // euler_step: change = delta * v; out = x + change, two roundings (no contraction)
             const float next = __fadd_rn(a.latent[idx], __fmul_rn(a.delta, prediction));
             a.latent[idx] = next;
@@ -247,15 +351,13 @@ __device__ __forceinline__ void epi_final_euler(uint32_t taddr, int row, bool va
 }
 
 template <int BN, Epilogue EPI>
-__device__ __forceinline__ void run_epilogue(uint32_t taddr, int row, bool valid, int m, int n_blk,
-                                             const GemmEpilogueArgs &args)
+__device__ __forceinline__ void run_epilogue(const EpiCtx &e, const GemmEpilogueArgs &args)
 {
-    const int col0 = n_blk * BN;
-    if constexpr (EPI == Epilogue::F32Bias) epi_f32_bias<BN>(taddr, row, valid, col0, args);
-    else if constexpr (EPI == Epilogue::ResidGate) epi_resid_gate<BN>(taddr, row, valid, col0, args);
-    else if constexpr (EPI == Epilogue::Qkv) epi_qkv<BN>(taddr, row, valid, col0, args);
-    else if constexpr (EPI == Epilogue::Geglu) epi_geglu<BN>(taddr, row, valid, n_blk, args);
-    else epi_final_euler(taddr, row, valid, m, args);
+    if constexpr (EPI == Epilogue::F32Bias) epi_f32_bias<BN>(e, args);
+    else if constexpr (EPI == Epilogue::ResidGate) epi_resid_gate<BN>(e, args);
+    else if constexpr (EPI == Epilogue::Qkv) epi_qkv<BN>(e, args);
+    else if constexpr (EPI == Epilogue::Geglu) epi_geglu<BN>(e, args);
+    else epi_final_euler(e, args);
 }
 
 // PROMOTE (FP32-exact mode): the tensor core's FP32 accumulation error grows linearly with the
@@ -407,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
         {
             const int m_blk = tile % num_m, n_blk = tile / num_m;
-            const int row = m_blk * BM + quarter * 32 + lane;
-            const bool valid = row < m;
+            const int row0 = m_blk * BM + quarter * 32;
+            uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
             if constexpr (!PROMOTE)
             {
                 const int acc = unit & 1;
@@ -419,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                run_epilogue<BN, EPI>(lane_base + acc * BN, row, valid, m, n_blk, args);
+                run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -459,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < BN; c += 32) tmem_store_32(result + c, sum + c);
                 tmem_store_wait();
-                run_epilogue<BN, EPI>(result, row, valid, m, n_blk, args);
+                run_epilogue<BN, EPI>(EpiCtx{result, row0, lane, m, n_blk, stage}, args);
             }
         }
     }
