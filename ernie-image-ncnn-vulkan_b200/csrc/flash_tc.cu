@@ -10,9 +10,12 @@
 //                 S_j = Q K_j^T   (M=128, N=128, K=128) into one of two TMEM S buffers
 //                 O  += P_j V_j   (M=128, N=128 dims, K=128 keys) into the TMEM O accumulator
 //   warps 2..5  softmax, one query row per thread: tcgen05.ld of S_j, online max/sum in FP32,
-//               rescale of O in TMEM when the row max grows, P_j written as BF16 into a
-//               128-byte-swizzled shared tile (the K-major A operand of the next MMA), final O / l.
-// Issue order S_0, S_1, PV_0, S_2, PV_1, S_3, ... lets S_{j+1} run while softmax works on S_j.
+//               P_j written as BF16 into one of two 128-byte-swizzled shared tiles (the K-major
+//               A operand of the next MMA), final O / l. The running max is only raised (and O in
+//               TMEM rescaled) when a tile's max exceeds it by more than 2^8; between raises the
+//               stale max is exact because O and l share it, and P stays <= 256.
+// Issue order S_0, S_1, PV_0, S_2, PV_1, S_3, ... lets S_{j+1} run while softmax works on S_j,
+// and the two P buffers let softmax j+1 write while PV_j is still executing.
 // V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so both MMAs use
 // K-major operands. All mbarrier waits are bounded. No TMA multicast.
 #include "kernels.h"
@@ -28,7 +31,7 @@ constexpr int kThreads = 192;
 constexpr int kTile = 128;                   // queries per CTA, keys per KV tile, head dim
 constexpr int kHalfBytes = kTile * 64 * 2;   // one 64-column half of a 128 x 128 BF16 tile
 constexpr int kTileBytes = 2 * kHalfBytes;   // 32 KB
-constexpr int kSmemBytes = 6 * kTileBytes + 1024 + 256;
+constexpr int kSmemBytes = 7 * kTileBytes + 1024 + 256; // Q, 2 K, 2 V^T, 2 P tiles
 constexpr int kTmemCols = 512;               // S buffers at columns 0 and 128, O at 256
 
 enum FlashError : int
@@ -78,17 +81,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_q = base;
     auto s_k = [&](int s) { return base + (1 + s) * kTileBytes; };
     auto s_v = [&](int s) { return base + (3 + s) * kTileBytes; };
-    const uint32_t s_p = base + 5 * kTileBytes;
-    const uint32_t bars = base + 6 * kTileBytes;
+    auto s_p = [&](int b) { return base + (5 + b) * kTileBytes; };
+    const uint32_t bars = base + 7 * kTileBytes;
     const uint32_t q_full = bars;
     auto k_full = [&](int s) { return bars + 8u * (1 + s); };
     auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
     auto v_full = [&](int s) { return bars + 8u * (5 + s); };
     auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
     auto s_full = [&](int s) { return bars + 8u * (9 + s); };
-    const uint32_t p_full = bars + 8u * 11;
-    const uint32_t o_done = bars + 8u * 12;
-    const uint32_t slot = bars + 8u * 13;
+    auto p_full = [&](int b) { return bars + 8u * (11 + b); };
+    auto p_empty = [&](int b) { return bars + 8u * (13 + b); };
+    const uint32_t slot = bars + 8u * 15;
 
     const int head = blockIdx.y, q0 = blockIdx.x * kTile;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -104,9 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(v_full(s), 1);
             mbar_init(v_empty(s), 1);
             mbar_init(s_full(s), 1);
+            mbar_init(p_full(s), 4);
+            mbar_init(p_empty(s), 1);
         }
-        mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0)
@@ -183,8 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok && tiles > 1) ok = issue_s(1);
             for (int j = 0; j < tiles && ok; ++j)
             {
-                const int s = j & 1;
-                if (!mbar_wait(p_full, j & 1) || !mbar_wait(v_full(s), (j >> 1) & 1))
+                const int b = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(p_full(b), ph) || !mbar_wait(v_full(b), ph))
                 {
                     ok = false;
                     break;
@@ -193,12 +197,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
                 {
-                    const uint64_t ad = smem_desc_sw128(s_p + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    const uint64_t bd = smem_desc_sw128(s_v(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                    const uint64_t ad = smem_desc_sw128(s_p(b) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                    const uint64_t bd = smem_desc_sw128(s_v(b) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
                     umma_bf16(tmem_base + o_col, ad, bd, idesc, (j > 0 || k > 0) ? 1u : 0u);
                 }
-                umma_commit(v_empty(s));
-                umma_commit(o_done);
+                umma_commit(v_empty(b));
+                umma_commit(p_empty(b));
                 if (j + 2 < tiles) ok = issue_s(j + 2);
             }
             if (!ok && a.error_flag) atomicExch(a.error_flag, kErrFlashMmaTimeout);
@@ -209,91 +213,105 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane; // row within the query tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        constexpr float kScaleLog2 = 0.08838834764831845f * 1.4426950408889634f;
-        constexpr float kLog2e = 1.4426950408889634f;
+        // scores stay in raw units; c folds 1/sqrt(128) and log2(e) into one FFMA per element
+        constexpr float c = 0.08838834764831845f * 1.4426950408889634f;
+        constexpr float kMaskToRaw = 11.313708498984761f; // log2(e)/c = sqrt(128)
+        constexpr float kRescaleLog2 = 8.f;              // rescale O only when the max grows by 2^8
         float m_run = -INFINITY, l_run = 0.f;
+        int waited0 = 0, waited1 = 0; // completions of p_empty[0] / p_empty[1] already observed
         bool ok = true;
-        for (int j = 0; j < tiles; ++j)
+        auto wait_pv = [&](int i) -> bool { // PV_i complete
+            const int b = i & 1, k = i >> 1;
+            int &waited = b ? waited1 : waited0;
+            if (waited > k) return true;
+            if (!mbar_wait(p_empty(b), k & 1)) return false;
+            waited = k + 1;
+            return true;
+        };
+        for (int j = 0; j < tiles && ok; ++j)
         {
-            const int s = j & 1;
-            if (!mbar_wait(s_full(s), (j >> 1) & 1))
+            const int b = j & 1;
+            if (!mbar_wait(s_full(b), (j >> 1) & 1))
             {
                 ok = false;
                 break;
             }
             tc_fence_after();
             float x[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-            {
-                float chunk[32];
-                tmem_load_32(lane_base + s * 128 + c * 32, chunk);
-#pragma unroll
-                for (int t = 0; t < 32; ++t) x[c * 32 + t] = chunk[t];
-            }
+            tmem_load_128(lane_base + b * 128, x);
             const int key0 = j * kTile;
-            float tile_max = -INFINITY;
+            if (a.mask)
+            {
 #pragma unroll
-            for (int k = 0; k < 128; ++k)
-            {
-                float v = x[k] * kScaleLog2;
-                if (key0 + k >= a.kv_len) v = -INFINITY;
-                else if (a.mask) v += __ldg(a.mask + key0 + k) * kLog2e;
-                x[k] = v;
-                tile_max = fmaxf(tile_max, v);
+                for (int k = 0; k < 128; ++k)
+                    if (key0 + k < a.kv_len) x[k] = fmaf(__ldg(a.mask + key0 + k), kMaskToRaw, x[k]);
             }
-            const float m_new = fmaxf(m_run, tile_max);
-            const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            float row_sum = 0.f;
+            if (key0 + kTile > a.kv_len)
+            {
 #pragma unroll
-            for (int k = 0; k < 128; ++k)
-            {
-                x[k] = fast_exp2(x[k] - m_use);
-                row_sum += x[k];
+                for (int k = 0; k < 128; ++k)
+                    if (key0 + k >= a.kv_len) x[k] = -INFINITY;
             }
-            const float alpha = fast_exp2(m_run - m_use);
-            if (j > 0)
+            float tmax = x[0];
+#pragma unroll
+            for (int k = 1; k < 128; ++k) tmax = fmaxf(tmax, x[k]);
+            if (j == 0) m_run = tmax;
+            else if (__any_sync(0xffffffffu, (tmax - m_run) * c > kRescaleLog2))
             {
-                // PV_{j-1} done: O is stable and the P tile is free again
-                if (!mbar_wait(o_done, (j - 1) & 1))
+                // the O rescale must land between PV_{j-1} and PV_j
+                const float m_new = fmaxf(m_run, tmax);
+                const float alpha = fast_exp2((m_run - m_new) * c);
+                if (!wait_pv(j - 1))
                 {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f))
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
                 {
+                    float o[32];
+                    tmem_load_32(lane_base + o_col + cc * 32, o);
 #pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                    {
-                        float o[32];
-                        tmem_load_32(lane_base + o_col + c * 32, o);
-#pragma unroll
-                        for (int t = 0; t < 32; ++t) o[t] *= alpha;
-                        tmem_store_32(lane_base + o_col + c * 32, o);
-                    }
-                    tmem_store_wait();
+                    for (int t = 0; t < 32; ++t) o[t] *= alpha;
+                    tmem_store_32(lane_base + o_col + cc * 32, o);
                 }
+                tmem_store_wait();
+                l_run *= alpha;
+                m_run = m_new;
             }
-            l_run = l_run * alpha + row_sum;
-            m_run = m_new;
+            const float neg = -m_run * c;
+            float row_sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 128; ++k)
+            {
+                x[k] = fast_exp2(fmaf(x[k], c, neg));
+                row_sum += x[k];
+            }
+            l_run += row_sum;
+            // P buffer b is free once PV_{j-2} has consumed it
+            if (j >= 2 && !wait_pv(j - 2))
+            {
+                ok = false;
+                break;
+            }
             // P row r as BF16 into the swizzled K-major tile: half h holds keys 64h..64h+63,
-            // 16-byte chunk c of row r sits at chunk c ^ (r & 7).
+            // 16-byte chunk cc of row r sits at chunk cc ^ (r & 7).
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
+                for (int cc = 0; cc < 8; ++cc)
                 {
-                    const float *v = x + h * 64 + c * 8;
-                    const uint32_t addr = s_p + h * kHalfBytes + r * 128 + ((c ^ (r & 7)) << 4);
+                    const float *v = x + h * 64 + cc * 8;
+                    const uint32_t addr = s_p(b) + h * kHalfBytes + r * 128 + ((cc ^ (r & 7)) << 4);
                     st_shared_v4(addr, pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
                 }
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full(b));
         }
-        if (ok && tiles > 0 && !mbar_wait(o_done, (tiles - 1) & 1)) ok = false;
+        if (ok && !wait_pv(tiles - 1)) ok = false;
         if (!ok)
         {
             if (a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashSoftmaxTimeout);
@@ -305,10 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float inv = 1.f / l_run;
             __nv_bfloat16 *dst = a.out + static_cast<size_t>(row) * a.ld_out + head * kTile;
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+            for (int cc = 0; cc < 4; ++cc)
             {
                 float o[32];
-                tmem_load_32(lane_base + o_col + c * 32, o);
+                tmem_load_32(lane_base + o_col + cc * 32, o);
                 if (row < a.rows)
                 {
 #pragma unroll
@@ -319,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         packed.y = pack2(o[t + 2] * inv, o[t + 3] * inv);
                         packed.z = pack2(o[t + 4] * inv, o[t + 5] * inv);
                         packed.w = pack2(o[t + 6] * inv, o[t + 7] * inv);
-                        *reinterpret_cast<uint4 *>(dst + c * 32 + t) = packed;
+                        *reinterpret_cast<uint4 *>(dst + cc * 32 + t) = packed;
                     }
                 }
             }
