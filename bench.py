@@ -22,6 +22,7 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "ernie-image-ncnn-vulkan_b200"))
+import dp  # noqa: E402  (data-parallel helpers of the package)
 
 METRIC = "DiT denoise ms/step and images/s (8-step 1024²) at 1/2/4/8 B200; % BF16 peak"
 WIDTH, HEIGHT, TEXT, VALID = 64, 64, 64, 64
@@ -85,9 +86,7 @@ class ClockSampler:
 
 
 def dist_setup(gpus):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, local, world = dp.world_from_env()
     if world != gpus and world > 1:
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE {world}")
     pg = None
@@ -103,17 +102,11 @@ def dist_setup(gpus):
 
 
 def barrier(pg):
-    if pg is not None:
-        pg.barrier()
+    dp.barrier(pg)
 
 
 def max_over_ranks(pg, value):
-    if pg is None:
-        return value
-    import torch
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    return float(t.item())
+    return dp.max_over_ranks(pg, value, device="cuda")
 
 
 def cpu_baseline_block(threads=None):
@@ -213,7 +206,8 @@ def main():
     model.synthesize(1234)
     precision = ec.BF16 if args.precision == "bf16" else ec.FP32
     session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision)
-    seed = 1000 + rank  # data parallel: one independent seed per GPU
+    # data parallel: one independent request (seed) per GPU, no collective in the data path
+    seed = dp.request_seed(1000, dp.shard_requests(world, rank, world)[0])
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     rng = np.random.default_rng(seed)
     latent = rng.standard_normal((128, HEIGHT, WIDTH), dtype=np.float32)

@@ -202,10 +202,10 @@ int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial
 int ernie_cuda_finite_latent_noalloc(ernie_cuda_context *ctx, const float *latent, int width, int height,
                                      int *finite);
 
-/* Benchmark hooks: average device time in ms of `iters` back-to-back launches of one kernel of
-   block 0 on the session's buffers (kernel 0 norm+modulate, 1 QKV GEMM, 2 attention, 3 out-proj
-   GEMM, 4 MLP norm+modulate, 5 up/gate GEMM, 6 down GEMM), and the number of kernels one denoise
-   step launches. */
+/* Benchmark hooks: average device time in ms of `iters` back-to-back launches of one kernel of the
+   block on the session's buffers, cycling through the model's blocks so that weights stream from HBM
+   as in a step (kernel 0 norm+modulate, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 MLP
+   norm+modulate, 5 up/gate GEMM, 6 down GEMM); and the number of kernels one denoise step launches. */
 int ernie_cuda_session_profile(ernie_cuda_session *session, int kernel, int iters, float *ms);
 int ernie_cuda_session_launches_per_step(ernie_cuda_session *session, int *launches);
 
