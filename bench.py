@@ -247,8 +247,10 @@ def main():
     # dominant kernel, timed live: the up/gate GEMM (largest of the 7 per block)
     prof = {}
     for kernel, name in ((1, "qkv_gemm"), (2, "attention"), (3, "out_gemm"), (5, "upgate_gemm"), (6, "down_gemm"),
-                         (0, "norm_modulate")):
-        prof[name] = session.profile(kernel, 10)
+                         (0, "norm_modulate"), (7, "block")):
+        prof[name] = session.profile(kernel, 10 if kernel < 7 else 36)
+    prof["step_eager"] = session.profile(8, 2)  # one step enqueued without a graph
+    prof["heads"] = session.profile(9, 10)  # input head, GEMVs, output head + Euler of one step
     bf16_peak, bf16_sustained, hbm_peak, peak_kind = peaks()
     n_valid = WIDTH * HEIGHT + VALID
     kernel_flops = {"qkv_gemm": 2.0 * tokens * 4096 * 12288, "attention": 4.0 * tokens * n_valid * 4096,

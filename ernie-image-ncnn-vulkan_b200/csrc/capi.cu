@@ -953,7 +953,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
 
 // Input head + 36 blocks + output head + Euler for one step (run_dit + euler_step).
 static int enqueue_step(ernie_cuda_session *s, float *latent, const float *features, float delta, float *prediction,
-                        int *finite_flag)
+                        int *finite_flag, bool with_blocks = true)
 {
     const DevHeads &hd = s->model->heads;
     cudaStream_t st = s->ctx->stream;
@@ -978,7 +978,8 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     ERNIE_LAUNCH(launch_gemv(hd.time2_w, s->g1, hd.time2_b, s->c, kHidden, kHidden, 1, st), "time linear_2");
     ERNIE_LAUNCH(launch_gemv(hd.adaln_w, s->c, hd.adaln_b, s->mod, 6 * kHidden, kHidden, 1, st), "adaLN");
     ERNIE_LAUNCH(launch_gemv(hd.final_norm_w, s->c, hd.final_norm_b, s->ss, 2 * kHidden, kHidden, 0, st), "final norm linear");
-    for (int b = 0; b < s->model->num_blocks; ++b) ERNIE_TRY(enqueue_block(s, b, s->x, s->mod));
+    if (with_blocks)
+        for (int b = 0; b < s->model->num_blocks; ++b) ERNIE_TRY(enqueue_block(s, b, s->x, s->mod));
     // output head: LayerNorm + modulate on image rows, linear + bias, fused Euler update
     ERNIE_LAUNCH(launch_norm_modulate(s->x, s->image, kHidden, nullptr, s->ss, s->ss + kHidden, 1e-6f, 1, s->a, fp32, st),
                  "final norm");
@@ -1158,15 +1159,29 @@ extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent
 
 extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int iters, float *ms)
 {
-    if (!s || !ms || kernel < 0 || kernel > 6 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
+    if (!s || !ms || kernel < 0 || kernel > 9 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
     if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs set_conditioning");
     DeviceGuard guard(s->ctx->device);
     ernie_cuda_context *ctx = s->ctx;
-    // launches cycle through the model's blocks so weights stream from HBM as in a real step
+    // launches cycle through the model's blocks so weights stream from HBM as in a real step;
+    // kernel 7 = one whole block (all seven launches), kernel 8 = one full denoise step
     const int nb = s->model->num_blocks;
-    ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, kernel)); // warm-up launch
-    ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
-    for (int i = 0; i < iters; ++i) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, kernel));
+    if (kernel >= 8)
+    {
+        if (s->feature_capacity < 1 || s->deltas.empty()) return fail(ERNIE_CUDA_ERROR, "Run a denoise step first");
+        const bool blocks = kernel == 8; // 9: the heads of a step without its blocks
+        ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks));
+        ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
+        for (int i = 0; i < iters; ++i)
+            ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks));
+    }
+    else
+    {
+        const int only = kernel == 7 ? -1 : kernel;
+        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, only)); // warm-up launch
+        ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
+        for (int i = 0; i < iters; ++i) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, only));
+    }
     ERNIE_CUDA(cudaEventRecord(ctx->events[15], ctx->stream), "event");
     ERNIE_CUDA(cudaEventSynchronize(ctx->events[15]), "event");
     float total = 0.f;
