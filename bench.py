@@ -25,7 +25,17 @@ sys.path.insert(0, os.path.join(ROOT, "ernie-image-ncnn-vulkan_b200"))
 import dp  # noqa: E402  (data-parallel helpers of the package)
 
 METRIC = "DiT denoise ms/step and images/s (8-step 1024²) at 1/2/4/8 B200; % BF16 peak"
-WIDTH, HEIGHT, TEXT, VALID = 64, 64, 64, 64
+# BASELINE.json configs as (packed width, packed height, DiT text slots, valid text tokens, precision).
+# c2 is the metric's workload and the default; the others run single-GPU for their own bench lines.
+CONFIGS = {
+    "c1": (32, 32, 32, 32, "bf16", "C1 512x512: 32x32 packed latent (1024 image tokens) + 32 text tokens"),
+    "c1-fp32": (32, 32, 32, 32, "fp32", "C1 512x512 in FP32-exact mode"),
+    "c2": (64, 64, 64, 64, "bf16", "C2 1024x1024: 64x64 packed latent (4096 image tokens) + 64 text tokens"),
+    "c3": (86, 48, 2048, 1080, "bf16",
+           "C3 1376x768: 86x48 packed latent (4128 image tokens) + 2048-slot text bucket, 968 padded keys"),
+    "c4": (128, 64, 64, 64, "bf16", "C4 2048x1024: 128x64 packed latent (8192 image tokens) + 64 text tokens"),
+}
+WIDTH, HEIGHT, TEXT, VALID = CONFIGS["c2"][:4]
 STEPS_PER_IMAGE = 8
 NUM_BLOCKS = 36
 PARAMS_PER_BLOCK = 218_103_808  # 7 GEMMs: 4*4096^2 + 3*4096*12288
@@ -146,10 +156,11 @@ def run_reference(args):
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "images/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C2 1024x1024: 4096 image + 64 text tokens, 36 blocks, 8 steps, 1 seed",
+            "config": {"workload": f"{args.workload}, 36 blocks, 8 steps, 1 seed",
                        "sample": "1 DiT block per step sample, extrapolated x36 blocks x8 steps"},
             "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port",
-                             "sample": "one DiT block (4160 tokens) of the oracle per step; x36 x8 extrapolated"},
+                             "sample": f"one DiT block ({WIDTH * HEIGHT + TEXT} tokens) of the oracle per step; "
+                                       "x36 x8 extrapolated"},
             "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -184,7 +195,8 @@ def main():
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--precision", choices=["bf16", "fp32"], default=None)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--blocks", type=int, default=NUM_BLOCKS, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -192,6 +204,9 @@ def main():
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
+    global WIDTH, HEIGHT, TEXT, VALID
+    WIDTH, HEIGHT, TEXT, VALID, config_precision, args.workload = CONFIGS[args.config]
+    args.precision = args.precision or config_precision
     if args.kernel_only:
         return run_kernel_only(args)
     if args.warmup < 3:
@@ -288,8 +303,8 @@ def main():
         line = {"metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-                "config": {"workload": "C2 1024x1024: 64x64 packed latent (4096 image tokens) + 64 text tokens, "
-                                       f"{args.blocks} blocks, turbo 8-step schedule, one seed per GPU",
+                "config": {"workload": f"{args.workload}, {args.blocks} blocks, turbo 8-step schedule, "
+                                       "one seed per GPU",
                            "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
