@@ -1,0 +1,786 @@
+// C++ host surface (include/ernie_b200/ernie.h) over the C ABI. Host orchestration only.
+#include "ernie_b200/ernie.h"
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <new>
+#include <utility>
+
+namespace ernie
+{
+namespace
+{
+using Clock = std::chrono::steady_clock;
+double seconds_since(Clock::time_point t) { return std::chrono::duration<double>(Clock::now() - t).count(); }
+
+void require(bool ok, const char *message)
+{
+    if (!ok) throw std::invalid_argument(message);
+}
+
+void check_latent(const Tensor &t)
+{
+    require(!t.empty() && t.dims == 3 && t.c == 128 && t.w >= 1 && t.h >= 1 && t.w <= 256 && t.h <= 256,
+            "Expected pack1 FP32 [128,H,W] latent with 1 <= H,W <= 256");
+}
+
+void check_latent(const DeviceTensor &t)
+{
+    require(!t.empty() && t.dims == 3 && t.c == 128 && t.w >= 1 && t.h >= 1 && t.w <= 256 && t.h <= 256 &&
+                t.bytes() >= size_t(128) * t.w * t.h * 4,
+            "Expected pack1 FP32 [128,H,W] latent with 1 <= H,W <= 256");
+}
+} // namespace
+
+void check_cuda(int result, const char *action)
+{
+    if (result == ERNIE_CUDA_OK) return;
+    const std::string message = std::string(action) + ": " + ernie_cuda_last_error();
+    if (result == ERNIE_CUDA_OUT_OF_MEMORY) throw GpuAllocationError(message);
+    throw std::runtime_error(message);
+}
+
+// ---- DeviceTensor -------------------------------------------------------------------------------
+DeviceTensor::DeviceTensor(GpuContext &ctx, size_t bytes, int w_, int h_, int c_, int dims_)
+    : w(w_), h(h_), c(c_), dims(dims_), ctx_(&ctx), bytes_(bytes)
+{
+    check_cuda(ernie_cuda_malloc(ctx.handle(), bytes, &ptr_), "allocate device tensor");
+}
+
+DeviceTensor::DeviceTensor(DeviceTensor &&o) noexcept
+    : w(o.w), h(o.h), c(o.c), dims(o.dims), ctx_(o.ctx_), ptr_(o.ptr_), bytes_(o.bytes_)
+{
+    o.ptr_ = nullptr;
+    o.bytes_ = 0;
+}
+
+DeviceTensor &DeviceTensor::operator=(DeviceTensor &&o) noexcept
+{
+    if (this != &o)
+    {
+        if (ptr_) ernie_cuda_free(ctx_->handle(), ptr_);
+        w = o.w, h = o.h, c = o.c, dims = o.dims, ctx_ = o.ctx_, ptr_ = o.ptr_, bytes_ = o.bytes_;
+        o.ptr_ = nullptr;
+        o.bytes_ = 0;
+    }
+    return *this;
+}
+
+DeviceTensor::~DeviceTensor()
+{
+    if (ptr_ && ctx_ && ctx_->available()) ernie_cuda_free(ctx_->handle(), ptr_);
+}
+
+DeviceTensor DeviceTensor::upload(GpuContext &ctx, const Tensor &host)
+{
+    DeviceTensor t(ctx, host.total() * 4, host.w, host.h, host.c, host.dims);
+    check_cuda(ernie_cuda_upload(ctx.handle(), t.ptr_, host.ptr(), host.total() * 4), "upload tensor");
+    return t;
+}
+
+Tensor DeviceTensor::download() const
+{
+    Tensor out;
+    out.w = w, out.h = h, out.c = c, out.dims = dims;
+    out.data.resize(size_t(w) * h * c);
+    if (out.data.size() * 4 > bytes_) throw std::logic_error("Device tensor smaller than its shape");
+    check_cuda(ernie_cuda_download(ctx_->handle(), out.ptr(), ptr_, out.data.size() * 4), "download tensor");
+    return out;
+}
+
+// ---- GpuContext ---------------------------------------------------------------------------------
+GpuContext::GpuContext(bool enabled, int requested_index, bool require_device)
+{
+    if (!enabled)
+    {
+        initialization_error_ = "GPU disabled";
+        if (require_device) throw std::runtime_error("A CUDA device is required");
+        return;
+    }
+    int count = 0;
+    if (ernie_cuda_device_count(&count) != ERNIE_CUDA_OK || count < 1)
+    {
+        initialization_error_ = std::string("No CUDA device: ") + ernie_cuda_last_error();
+        if (require_device) throw std::runtime_error(initialization_error_);
+        return;
+    }
+    const int index = requested_index < 0 ? 0 : requested_index;
+    if (index >= count)
+    {
+        initialization_error_ = "CUDA device index out of range";
+        if (require_device) throw std::invalid_argument(initialization_error_);
+        return;
+    }
+    const int rc = ernie_cuda_context_create(index, &handle_);
+    if (rc != ERNIE_CUDA_OK)
+    {
+        initialization_error_ = ernie_cuda_last_error();
+        handle_ = nullptr;
+        if (require_device) check_cuda(rc, "create CUDA context");
+        return;
+    }
+    device_ = index;
+}
+
+GpuContext::~GpuContext()
+{
+    if (handle_) ernie_cuda_context_destroy(handle_);
+}
+
+ernie_cuda_context *GpuContext::handle() const
+{
+    if (!handle_) throw std::logic_error("GPU context is not available");
+    return handle_;
+}
+
+void GpuContext::synchronize() const { check_cuda(ernie_cuda_context_synchronize(handle()), "synchronize"); }
+
+// ---- latent ops ---------------------------------------------------------------------------------
+static FlowSchedule make_schedule(int steps, int kind)
+{
+    require(steps >= 1 && steps <= 1000, "Steps must be in [1,1000]");
+    FlowSchedule s;
+    s.sigmas.resize(size_t(steps) + 1);
+    s.timesteps.resize(steps);
+    check_cuda(ernie_cuda_schedule(steps, kind, s.sigmas.data(), s.timesteps.data()), "schedule");
+    return s;
+}
+FlowSchedule FlowSchedule::turbo(int steps) { return make_schedule(steps, ERNIE_SCHEDULE_TURBO); }
+FlowSchedule FlowSchedule::linear(int steps) { return make_schedule(steps, ERNIE_SCHEDULE_LINEAR); }
+
+float FlowSchedule::delta(size_t step) const
+{
+    if (step >= timesteps.size() || sigmas.size() != timesteps.size() + 1)
+        throw std::out_of_range("Euler schedule exhausted or malformed");
+    return sigmas[step + 1] - sigmas[step];
+}
+
+void euler_step(GpuContext &ctx, const DeviceTensor &sample, const DeviceTensor &prediction, float delta,
+                DeviceTensor &next)
+{
+    check_latent(sample);
+    check_latent(prediction);
+    require(sample.w == prediction.w && sample.h == prediction.h && std::isfinite(delta) && delta < 0.f && delta >= -1.f,
+            "Incompatible Euler shapes or delta outside [-1,0)");
+    if (next.empty() || next.bytes() < sample.bytes())
+        next = DeviceTensor(ctx, sample.bytes(), sample.w, sample.h, sample.c, 3);
+    check_cuda(ernie_cuda_euler_step(ctx.handle(), sample.f32(), prediction.f32(), delta, sample.w, sample.h, next.f32()),
+               "Euler step");
+}
+
+bool finite_latent(GpuContext &ctx, const DeviceTensor &value)
+{
+    check_latent(value);
+    int finite = 0;
+    check_cuda(ernie_cuda_finite_latent(ctx.handle(), value.f32(), value.w, value.h, &finite), "finite check");
+    return finite != 0;
+}
+
+DeviceTensor unpack_for_vae(GpuContext &ctx, const DeviceTensor &packed, const Tensor &mean, const Tensor &variance)
+{
+    check_latent(packed);
+    require(mean.total() == 128 && variance.total() == 128, "Expected pack1 FP32 [128] BN statistics");
+    for (size_t c = 0; c < 128; ++c)
+        require(std::isfinite(mean[c]) && std::isfinite(variance[c]) && variance[c] >= 0.f, "Invalid BN statistics");
+    const DeviceTensor m = DeviceTensor::upload(ctx, mean), v = DeviceTensor::upload(ctx, variance);
+    DeviceTensor out(ctx, size_t(32) * 4 * packed.w * packed.h * 4, 2 * packed.w, 2 * packed.h, 32, 3);
+    check_cuda(ernie_cuda_unpack_for_vae(ctx.handle(), packed.f32(), m.f32(), v.f32(), packed.w, packed.h, out.f32()),
+               "unpack for VAE");
+    ctx.synchronize();
+    return out;
+}
+
+// ---- conditioning and features --------------------------------------------------------------------
+std::vector<Tensor> dit_constants(const std::vector<float> &frequencies, int width, int height, int valid_text,
+                                  int text_bucket, int token_limit)
+{
+    require(frequencies.empty() || frequencies.size() == 64, "Invalid DiT position dimensions or frequency file");
+    require(width >= 1 && height >= 1 && text_bucket >= 1 && width * height + text_bucket <= 10240,
+            "Invalid DiT position dimensions or frequency file");
+    const int n = width * height + text_bucket;
+    Tensor cos(128, n), sin(128, n), mask(n, 1);
+    const int rc = ernie_cuda_dit_constants(frequencies.empty() ? nullptr : frequencies.data(), width, height,
+                                            valid_text, text_bucket, token_limit, cos.ptr(), sin.ptr(), mask.ptr());
+    if (rc != ERNIE_CUDA_OK) throw std::invalid_argument(ernie_cuda_last_error());
+    return {cos, sin, mask};
+}
+
+Tensor pad_text(const Tensor &embeddings, int bucket)
+{
+    require(!embeddings.empty() && embeddings.dims == 2 && embeddings.w == 3072 && embeddings.h >= 1 &&
+                embeddings.h <= bucket && bucket <= 2048,
+            "Invalid text embeddings or padding bucket");
+    Tensor out(3072, bucket);
+    std::copy(embeddings.data.begin(), embeddings.data.end(), out.data.begin());
+    return out;
+}
+
+Tensor timestep_features(float timestep)
+{
+    Tensor out(4096);
+    const int rc = ernie_cuda_timestep_features(timestep, out.ptr());
+    if (rc != ERNIE_CUDA_OK) throw std::invalid_argument(ernie_cuda_last_error());
+    return out;
+}
+
+// ---- layers ----------------------------------------------------------------------------------------
+void set_attention_query_rows(GpuContext &ctx, int rows)
+{
+    require(rows == 128 || rows == 64 || rows == 32 || rows == 16, "Attention query rows must be 128, 64, 32 or 16");
+    check_cuda(ernie_cuda_set_attention_query_rows(ctx.handle(), rows), "set attention query rows");
+}
+
+int attention_query_rows(GpuContext &ctx)
+{
+    int rows = 0;
+    check_cuda(ernie_cuda_attention_query_rows(ctx.handle(), &rows), "attention query rows");
+    return rows;
+}
+
+DeviceTensor sdpa(GpuContext &ctx, const DeviceTensor &q, const DeviceTensor &k, const DeviceTensor &v,
+                  const DeviceTensor *mask)
+{
+    // ncnn layout: q (w=width, h=nq, c=heads), k/v (w=width, h=nk, c=kv_heads), mask (w=nk, h=rows, c=mask_heads)
+    require(q.w == k.w && k.w == v.w && k.h == v.h && k.c == v.c && q.w >= 1 && q.w <= 128, "SDPA shapes differ");
+    const int mask_heads = mask ? mask->c : 1, mask_rows = mask ? mask->h : 1;
+    if (mask) require(mask->w == k.h, "SDPA mask width must equal the key count");
+    DeviceTensor out(ctx, q.bytes(), q.w, q.h, q.c, 3);
+    check_cuda(ernie_cuda_sdpa(ctx.handle(), q.f32(), k.f32(), v.f32(), mask ? mask->f32() : nullptr, q.c, k.c, mask_heads,
+                               mask_rows, q.h, k.h, q.w, out.f32()),
+               "SDPA");
+    return out;
+}
+
+DeviceTensor rms_norm(GpuContext &ctx, const DeviceTensor &x, const Tensor &gamma, float eps)
+{
+    require(x.w == 128 || x.w == 3072 || x.w == 4096, "RMSNorm width must be 128, 3072 or 4096");
+    require(int(gamma.total()) == x.w, "RMSNorm affine weights must match the width");
+    const DeviceTensor g = DeviceTensor::upload(ctx, gamma);
+    DeviceTensor out(ctx, x.bytes(), x.w, x.h, x.c, x.dims);
+    check_cuda(ernie_cuda_rmsnorm(ctx.handle(), x.f32(), g.f32(), int64_t(x.h) * x.c, x.w, eps, out.f32()), "RMSNorm");
+    ctx.synchronize();
+    return out;
+}
+
+DeviceTensor layer_norm(GpuContext &ctx, const DeviceTensor &x, float eps)
+{
+    require(x.w == 4096, "LayerNorm width must be 4096");
+    DeviceTensor out(ctx, x.bytes(), x.w, x.h, x.c, x.dims);
+    check_cuda(ernie_cuda_layernorm(ctx.handle(), x.f32(), int64_t(x.h) * x.c, x.w, eps, out.f32()), "LayerNorm");
+    return out;
+}
+
+void gelu_inplace(GpuContext &ctx, DeviceTensor &x)
+{
+    const int64_t count = int64_t(x.w) * x.h * x.c;
+    check_cuda(ernie_cuda_gelu(ctx.handle(), x.f32(), count), "ErnieGELU");
+}
+
+DeviceTensor residual_add(GpuContext &ctx, const DeviceTensor &a, const DeviceTensor &b)
+{
+    require(a.w == b.w && a.h == b.h && a.c == b.c, "Residual shapes differ");
+    DeviceTensor out(ctx, a.bytes(), a.w, a.h, a.c, a.dims);
+    check_cuda(ernie_cuda_residual_add(ctx.handle(), a.f32(), b.f32(), out.f32(), int64_t(a.w) * a.h * a.c),
+               "ErnieResidualAdd");
+    return out;
+}
+
+// ---- weights ------------------------------------------------------------------------------------------
+DitModel::DitModel(GpuContext &ctx, int num_blocks) : ctx_(ctx), num_blocks_(num_blocks)
+{
+    require(num_blocks >= 1 && num_blocks <= 36, "Require 1..36 blocks");
+    check_cuda(ernie_cuda_model_create(ctx.handle(), num_blocks, &handle_), "allocate DiT weights");
+}
+
+DitModel::~DitModel()
+{
+    if (handle_) ernie_cuda_model_destroy(handle_);
+}
+
+void DitModel::upload_block(int block, const BlockWeights &w)
+{
+    const size_t sq = size_t(4096) * 4096, ffn = size_t(12288) * 4096;
+    require(w.wq.size() == sq && w.wk.size() == sq && w.wv.size() == sq && w.wo.size() == sq && w.wup.size() == ffn &&
+                w.wgate.size() == ffn && w.wfc2.size() == ffn && w.gamma_sa.size() == 4096 &&
+                w.gamma_mlp.size() == 4096 && w.gamma_q.size() == 128 && w.gamma_k.size() == 128,
+            "Block weights must provide all 11 tensors with the ERNIE shapes");
+    const ernie_cuda_block_weights c{w.wq.data(),       w.wk.data(),        w.wv.data(),      w.wo.data(),
+                                     w.wup.data(),      w.wgate.data(),     w.wfc2.data(),    w.gamma_sa.data(),
+                                     w.gamma_mlp.data(), w.gamma_q.data(), w.gamma_k.data()};
+    check_cuda(ernie_cuda_model_upload_block(handle_, block, &c), "upload block weights");
+}
+
+void DitModel::upload_heads(const HeadWeights &w)
+{
+    const ernie_cuda_head_weights c{w.x_embed_w.data(), w.x_embed_b.data(), w.text_proj_w.data(), w.time1_w.data(),
+                                    w.time1_b.data(),   w.time2_w.data(),   w.time2_b.data(),     w.adaln_w.data(),
+                                    w.adaln_b.data(),   w.final_norm_w.data(), w.final_norm_b.data(), w.final_w.data(),
+                                    w.final_b.data()};
+    check_cuda(ernie_cuda_model_upload_heads(handle_, &c), "upload head weights");
+}
+
+void DitModel::synthesize(uint64_t seed) { check_cuda(ernie_cuda_model_synthesize(handle_, seed), "synthesize weights"); }
+
+uint64_t DitModel::bytes() const
+{
+    uint64_t b = 0;
+    check_cuda(ernie_cuda_model_bytes(handle_, &b), "model bytes");
+    return b;
+}
+
+WeightMemory parse_weight_memory(const std::string &value)
+{
+    if (value == "auto") return WeightMemory::Auto;
+    if (value == "device") return WeightMemory::Device;
+    if (value == "host") return WeightMemory::Host;
+    throw std::invalid_argument("DiT weights must be auto, device, or host");
+}
+
+// Decision order of src/weight_placement.cpp:18-46: explicit mode, shape preference, then the
+// device budget after the reserve.
+WeightPlacementDecision choose_weight_placement(WeightMemory mode, bool shape_prefers_host, std::uint64_t weight_bytes,
+                                                std::uint64_t reserve_bytes, std::optional<DeviceMemoryBudget> memory)
+{
+    WeightPlacementDecision d;
+    d.weight_bytes = weight_bytes;
+    d.reserve_bytes = reserve_bytes;
+    if (memory) d.available_bytes = memory->usage_bytes < memory->budget_bytes ? memory->budget_bytes - memory->usage_bytes : 0;
+    if (mode != WeightMemory::Auto)
+    {
+        d.host = mode == WeightMemory::Host;
+        d.reason = "explicit";
+    }
+    else if (shape_prefers_host)
+    {
+        d.host = true;
+        d.reason = "shape";
+    }
+    else if (d.available_bytes)
+    {
+        d.host = *d.available_bytes < reserve_bytes || *d.available_bytes - reserve_bytes < weight_bytes;
+        d.reason = d.host ? "budget" : "available";
+    }
+    return d;
+}
+
+WeightPlacement::WeightPlacement(WeightMemory mode, std::uint64_t reserve_bytes, BudgetReader reader, Observer observer)
+    : mode_(mode), reserve_bytes_(reserve_bytes), reader_(std::move(reader)), observer_(std::move(observer))
+{
+}
+
+bool WeightPlacement::use_host(const std::string &component, std::uint64_t weight_bytes, bool shape_prefers_host,
+                               bool cache_prefers_host, const char *host_reason)
+{
+    const auto memory = mode_ == WeightMemory::Auto && reader_ ? reader_() : std::nullopt;
+    auto d = choose_weight_placement(mode_, shape_prefers_host, weight_bytes, reserve_bytes_, memory);
+    if (mode_ == WeightMemory::Auto && cache_prefers_host)
+    {
+        d.host = true;
+        d.reason = host_reason;
+    }
+    if (mode_ == WeightMemory::Auto && !memory) ++unavailable_queries_;
+    if (d.host) ++host_requests_;
+    else ++device_requests_;
+    if (observer_) observer_(component, d);
+    return d.host;
+}
+
+WeightPlacement::BudgetReader cuda_memory_budget_reader(GpuContext &ctx)
+{
+    ernie_cuda_context *handle = ctx.handle();
+    return [handle]() -> std::optional<DeviceMemoryBudget> {
+        uint64_t free_bytes = 0, total = 0;
+        if (ernie_cuda_context_memory(handle, &free_bytes, &total) != ERNIE_CUDA_OK) return std::nullopt;
+        return DeviceMemoryBudget{total, total - free_bytes};
+    };
+}
+
+// WeightSession: the admission policy of src/weight_session.cpp:60-118 over an opaque payload.
+struct WeightSession::State
+{
+    struct Entry
+    {
+        Payload payload;
+        std::uint64_t charge;
+    };
+    WeightBudget budget;
+    AvailableReader available;
+    Inspector inspect;
+    WeightSessionStats stats;
+    std::map<std::size_t, Entry> idle;
+    std::map<std::size_t, std::string> identities;
+    const void *request = nullptr;
+    bool active = false, cancelled = false;
+    bool headroom(std::uint64_t extra)
+    {
+        const auto bytes = available ? available() : std::nullopt;
+        if (!bytes)
+        {
+            ++stats.unavailable_queries;
+            return false;
+        }
+        return *bytes >= budget.reserve_bytes && *bytes - budget.reserve_bytes >= extra;
+    }
+    void evict_last()
+    {
+        auto last = std::prev(idle.end());
+        stats.live_bytes -= last->second.charge;
+        --stats.cached_nets;
+        idle.erase(last);
+        ++stats.evictions;
+    }
+};
+
+WeightSession::WeightSession(WeightBudget budget, AvailableReader available, Inspector inspect)
+    : state_(std::make_shared<State>())
+{
+    state_->budget = budget;
+    state_->available = std::move(available);
+    state_->inspect = std::move(inspect);
+}
+
+WeightSession::~WeightSession() { cancel(); }
+WeightSessionStats WeightSession::stats() const { return state_->stats; }
+bool WeightSession::contains(std::size_t block) const { return state_->idle.count(block) != 0; }
+
+void WeightSession::cancel()
+{
+    state_->cancelled = true;
+    while (!state_->idle.empty()) state_->evict_last();
+}
+
+WeightSession::Lease WeightSession::acquire(std::size_t block, const std::string &identity, const void *request,
+                                            std::uint64_t estimate, const Loader &loader)
+{
+    auto &s = *state_;
+    if (s.cancelled || s.active) throw std::logic_error("Weight session cancelled or lease still active");
+    if (block >= 36 || !request || !loader || identity.empty()) throw std::invalid_argument("Invalid weight session request");
+    if (s.request && s.request != request) throw std::logic_error("Weight session request identity changed");
+    s.request = request;
+    const auto known = s.identities.find(block);
+    if (known != s.identities.end() && known->second != identity)
+        throw std::logic_error("Weight session model identity changed");
+    s.identities.emplace(block, identity);
+    if (s.budget.host_bytes)
+        while (!s.idle.empty() && !s.headroom(s.idle.count(block) ? 0 : estimate)) s.evict_last();
+    auto found = s.idle.find(block);
+    if (found != s.idle.end())
+    {
+        auto entry = std::move(found->second);
+        s.idle.erase(found);
+        ++s.stats.hits;
+        s.active = true;
+        return Lease(state_, block, std::move(entry.payload), entry.charge);
+    }
+    const bool candidate = s.inspect && s.budget.host_bytes && estimate <= s.budget.host_bytes - s.stats.live_bytes &&
+                           s.headroom(estimate);
+    Payload payload = loader(candidate);
+    if (!payload) throw std::runtime_error("Weight loader returned nothing");
+    ++s.stats.loads;
+    std::uint64_t charge = 0;
+    if (candidate)
+    {
+        const auto measured = s.inspect(payload);
+        if (measured && *measured && *measured <= s.budget.host_bytes - s.stats.live_bytes && s.headroom(0))
+        {
+            charge = *measured;
+            s.stats.live_bytes += charge;
+            s.stats.peak_bytes = std::max(s.stats.peak_bytes, s.stats.live_bytes);
+            ++s.stats.cached_nets;
+            s.stats.peak_nets = std::max(s.stats.peak_nets, s.stats.cached_nets);
+            ++s.stats.admissions;
+        }
+    }
+    s.active = true;
+    return Lease(state_, block, std::move(payload), charge);
+}
+
+WeightSession::Lease::Lease(std::shared_ptr<State> state, std::size_t block, Payload payload, std::uint64_t charge)
+    : state_(std::move(state)), block_(block), payload_(std::move(payload)), charge_(charge)
+{
+}
+
+WeightSession::Lease::Lease(Lease &&o) noexcept
+    : state_(std::move(o.state_)), block_(o.block_), payload_(std::move(o.payload_)), charge_(o.charge_)
+{
+}
+
+WeightSession::Lease &WeightSession::Lease::operator=(Lease &&o) noexcept
+{
+    if (this != &o)
+    {
+        release(false);
+        state_ = std::move(o.state_);
+        block_ = o.block_;
+        payload_ = std::move(o.payload_);
+        charge_ = o.charge_;
+    }
+    return *this;
+}
+
+WeightSession::Lease::~Lease() { release(false); }
+
+const WeightSession::Payload &WeightSession::Lease::payload() const
+{
+    if (!payload_) throw std::logic_error("Weight lease already released");
+    return payload_;
+}
+
+void WeightSession::Lease::complete()
+{
+    if (!payload_) throw std::logic_error("Weight lease already released");
+    release(true);
+}
+
+void WeightSession::Lease::release(bool completed)
+{
+    if (!payload_ || !state_) return;
+    auto &s = *state_;
+    if (completed && charge_ && !s.cancelled) s.idle.emplace(block_, State::Entry{std::move(payload_), charge_});
+    else
+    {
+        payload_.reset();
+        s.stats.live_bytes -= charge_;
+        if (charge_) --s.stats.cached_nets;
+    }
+    s.active = false;
+    state_.reset();
+}
+
+// ---- sessions, block sequence, DiT, denoise --------------------------------------------------------------
+DenoiseSession::DenoiseSession(DitModel &model, int width, int height, int text_tokens, int valid_text,
+                               Precision precision)
+    : model_(model), width_(width), height_(height), tokens_(width * height + text_tokens)
+{
+    const ernie_cuda_shape shape{width, height, text_tokens, valid_text};
+    const int rc = ernie_cuda_session_create(model.handle(), &shape,
+                                             precision == Precision::FP32 ? ERNIE_PRECISION_FP32 : ERNIE_PRECISION_BF16,
+                                             &handle_);
+    if (rc == ERNIE_CUDA_ERROR) throw std::invalid_argument(ernie_cuda_last_error());
+    check_cuda(rc, "create denoise session");
+}
+
+DenoiseSession::~DenoiseSession()
+{
+    if (handle_) ernie_cuda_session_destroy(handle_);
+}
+
+void DenoiseSession::set_constants(const std::vector<Tensor> &k)
+{
+    require(k.size() == 4, "Require four constants: text, cosine, sine and mask");
+    const size_t n = size_t(tokens_);
+    require(k[1].total() == n * 128 && k[2].total() == n * 128 && k[3].total() == n, "Constants do not match the shape");
+    require(k[0].empty() || k[0].total() == size_t(tokens_ - width_ * height_) * 3072, "Text must be [slots][3072]");
+    check_cuda(ernie_cuda_session_set_conditioning(handle_, k[0].empty() ? nullptr : k[0].ptr(), k[1].ptr(), k[2].ptr(),
+                                                   k[3].ptr()),
+               "set constants");
+}
+
+void run_block_sequence(DenoiseSession &s, DeviceTensor &x, const DeviceTensor &modulation, int first, int count,
+                        BlockSequenceStats &stats)
+{
+    require(count >= 1 && first >= 0 && first + count <= s.model().num_blocks() && count <= 36,
+            "Require 1..36 blocks");
+    require(x.w == 4096 && x.h == s.tokens() && x.bytes() >= size_t(s.tokens()) * 4096 * 4, "x must be [N][4096] FP32");
+    require(modulation.bytes() >= size_t(6) * 4096 * 4, "Require six shared modulation vectors");
+    stats = {};
+    const auto start = Clock::now();
+    check_cuda(ernie_cuda_session_blocks(s.handle(), first, count, x.f32(), modulation.f32()), "run block sequence");
+    s.model().context().synchronize();
+    stats.compute_seconds.push_back(seconds_since(start));
+    stats.compute_submissions = 1;
+}
+
+DeviceTensor run_dit(DenoiseSession &s, const DeviceTensor &latent, float timestep, DitStats &stats)
+{
+    check_latent(latent);
+    require(latent.w == s.width() && latent.h == s.height(), "Latent does not match the session shape");
+    stats = {};
+    DeviceTensor prediction(s.model().context(), latent.bytes(), latent.w, latent.h, 128, 3);
+    const auto start = Clock::now();
+    check_cuda(ernie_cuda_session_dit(s.handle(), latent.f32(), timestep, prediction.f32()), "run DiT");
+    stats.blocks.compute_seconds.push_back(seconds_since(start));
+    return prediction;
+}
+
+Tensor denoise(DenoiseSession &s, const Tensor &initial, int steps, std::vector<DenoiseStepStats> &stats,
+               const StepObserver &observer, int start_step, int schedule_kind)
+{
+    check_latent(initial);
+    require(initial.w == s.width() && initial.h == s.height(), "Latent does not match the session shape");
+    require(start_step >= 0 && start_step <= steps, "Denoising start step must be in [0,steps]");
+    const FlowSchedule schedule = schedule_kind == ERNIE_SCHEDULE_LINEAR ? FlowSchedule::linear(steps)
+                                                                           : FlowSchedule::turbo(steps);
+    stats.clear();
+    Tensor sample = initial;
+    for (float v : sample.data) require(std::isfinite(v), "Initial latent is not finite");
+    if (!observer)
+    {
+        // the whole range in one CUDA graph; per-step stats carry the range's average time
+        const auto start = Clock::now();
+        int failed = 0;
+        const int rc = ernie_cuda_session_denoise(s.handle(), initial.ptr(), sample.ptr(), steps, start_step, steps,
+                                                  schedule_kind, nullptr, &failed);
+        const double each = (steps - start_step) ? seconds_since(start) / (steps - start_step) : 0.0;
+        const int done = rc == ERNIE_CUDA_OK ? steps : (failed ? failed : start_step);
+        for (int i = start_step; i < steps && i < std::max(done, start_step + 1); ++i)
+        {
+            DenoiseStepStats st;
+            st.timestep = schedule.timesteps[i];
+            st.delta = schedule.delta(i);
+            st.elapsed_seconds = each;
+            st.complete = rc == ERNIE_CUDA_OK || i + 1 < done;
+            stats.push_back(st);
+        }
+        if (failed) throw std::runtime_error("Non-finite latent after denoise step " + std::to_string(failed));
+        check_cuda(rc, "denoise");
+        return sample;
+    }
+    Tensor prediction(s.width(), s.height(), 128);
+    for (int i = start_step; i < steps; ++i)
+    {
+        DenoiseStepStats st;
+        st.timestep = schedule.timesteps[i];
+        st.delta = schedule.delta(i);
+        const auto start = Clock::now();
+        int failed = 0;
+        const int rc = ernie_cuda_session_denoise(s.handle(), sample.ptr(), sample.ptr(), steps, i, i + 1, schedule_kind,
+                                                  prediction.ptr(), &failed);
+        st.elapsed_seconds = seconds_since(start);
+        if (rc != ERNIE_CUDA_OK)
+        {
+            stats.push_back(st);
+            if (failed) throw std::runtime_error("Non-finite latent after denoise step " + std::to_string(failed));
+            check_cuda(rc, "denoise step");
+        }
+        st.complete = true;
+        stats.push_back(st);
+        observer(size_t(i), prediction, sample);
+    }
+    return sample;
+}
+
+// ---- recovery (src/vulkan_denoise.cpp:40-202 semantics) ------------------------------------------------
+Tensor denoise_with_recovery(DenoiseBackend &backend, const Tensor &initial, int steps, int start_step,
+                             const CudaDenoiseSettings &settings, CudaDenoiseStats &total,
+                             const CudaDenoiseObservers &observer)
+{
+    check_latent(initial);
+    require(settings.retries <= 3 && start_step >= 0 && start_step <= steps, "Invalid recovery session");
+    for (float v : initial.data) require(std::isfinite(v), "Invalid recovery session");
+    const FlowSchedule schedule = settings.schedule == ERNIE_SCHEDULE_LINEAR ? FlowSchedule::linear(steps)
+                                                                               : FlowSchedule::turbo(steps);
+    total = {};
+    Tensor checkpoint = initial;
+    int resume = start_step;
+    for (unsigned attempt = 0; resume < steps; ++attempt)
+    {
+        total.query_rows = 128 >> attempt;
+        std::string failure;
+        bool observer_failed = false;
+        try
+        {
+            backend.begin_attempt(attempt, checkpoint, total.query_rows);
+            try
+            {
+                for (int i = resume; i < steps; ++i)
+                {
+                    if (settings.before_step) settings.before_step(attempt, i);
+                    DenoiseStepStats st;
+                    st.timestep = schedule.timesteps[i];
+                    st.delta = schedule.delta(i);
+                    const auto start = Clock::now();
+                    Tensor prediction = backend.run_step(i, st.timestep, st.delta);
+                    Tensor saved = backend.latent();
+                    for (float v : saved.data)
+                        if (!std::isfinite(v)) throw std::runtime_error("Non-finite latent after denoise step " + std::to_string(i + 1));
+                    // commit only after the whole checkpoint transfer succeeded
+                    checkpoint = std::move(saved);
+                    resume = i + 1;
+                    st.elapsed_seconds = seconds_since(start);
+                    st.complete = true;
+                    if (observer.step)
+                    {
+                        try
+                        {
+                            observer.step(size_t(i), prediction, checkpoint, st);
+                        }
+                        catch (...)
+                        {
+                            observer_failed = true;
+                            throw;
+                        }
+                    }
+                }
+            }
+            catch (...)
+            {
+                backend.end_attempt();
+                throw;
+            }
+            backend.end_attempt();
+        }
+        catch (const GpuAllocationError &error)
+        {
+            if (observer_failed) throw;
+            failure = error.what();
+        }
+        catch (const std::bad_alloc &)
+        {
+            if (observer_failed) throw;
+            failure = "Memory allocation failed";
+        }
+        if (failure.empty()) break;
+        if (attempt >= settings.retries)
+            throw GpuAllocationError("Denoise allocation recovery exhausted after " + std::to_string(attempt) +
+                                     " retries at step " + std::to_string(resume + 1) + ": " + failure);
+        ++total.retries;
+        if (observer.retry) observer.retry(total.retries, resume, 128 >> (attempt + 1), failure);
+    }
+    return checkpoint;
+}
+
+CudaDenoiseBackend::CudaDenoiseBackend(DitModel &model, int width, int height, int text_tokens, int valid_text,
+                                       Precision precision, std::vector<Tensor> constants)
+    : model_(model), width_(width), height_(height), text_(text_tokens), valid_(valid_text), precision_(precision),
+      constants_(std::move(constants))
+{
+}
+
+void CudaDenoiseBackend::begin_attempt(unsigned, const Tensor &checkpoint, int query_rows)
+{
+    // each attempt owns its activations; a retry rebuilds them from the host checkpoint
+    session_ = std::make_unique<DenoiseSession>(model_, width_, height_, text_, valid_, precision_);
+    session_->set_constants(constants_);
+    set_attention_query_rows(model_.context(), query_rows);
+    float *latent = nullptr;
+    check_cuda(ernie_cuda_session_latent(session_->handle(), &latent), "session latent");
+    check_cuda(ernie_cuda_upload(model_.context().handle(), latent, checkpoint.ptr(), checkpoint.total() * 4),
+               "upload checkpoint");
+}
+
+Tensor CudaDenoiseBackend::run_step(int step, float, float)
+{
+    Tensor latent_now = latent();
+    Tensor prediction(width_, height_, 128);
+    int failed = 0;
+    const int rc = ernie_cuda_session_denoise(session_->handle(), latent_now.ptr(), latent_now.ptr(), steps, step,
+                                              step + 1, ERNIE_SCHEDULE_TURBO, prediction.ptr(), &failed);
+    if (failed) throw std::runtime_error("Non-finite latent after denoise step " + std::to_string(failed));
+    check_cuda(rc, "denoise step");
+    return prediction;
+}
+
+Tensor CudaDenoiseBackend::latent()
+{
+    Tensor out(width_, height_, 128);
+    float *latent = nullptr;
+    check_cuda(ernie_cuda_session_latent(session_->handle(), &latent), "session latent");
+    check_cuda(ernie_cuda_download(model_.context().handle(), out.ptr(), latent, out.total() * 4), "download latent");
+    return out;
+}
+
+void CudaDenoiseBackend::end_attempt() { session_.reset(); }
+} // namespace ernie

@@ -1,0 +1,371 @@
+// C++ host surface of the B200 DiT denoiser, mirroring mingshi2333/ernie-image-ncnn-vulkan's denoiser,
+// DiT, block-sequence, latent-op, conditioning, layer, weight-placement/-session, GPU-context and
+// recovery interfaces (each declaration names the reference header it mirrors). ncnn::Mat / VkMat
+// arguments become ernie::Tensor (host FP32) and ernie::DeviceTensor (CUDA memory). Everything here
+// calls the C ABI of include/ernie_cuda.h; failures throw the reference's exception types
+// (GpuAllocationError for allocation failures, std::invalid_argument for contract violations,
+// std::runtime_error otherwise).
+#pragma once
+#include "ernie_cuda.h"
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <optional>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace ernie
+{
+// ---- errors (src/vulkan_memory.h:11-17, check_ncnn_memory src/vulkan_memory.cpp:21-30) --------
+class GpuAllocationError : public std::runtime_error
+{
+  public:
+    using std::runtime_error::runtime_error;
+};
+// 0 -> return, -100 -> GpuAllocationError, anything else -> std::runtime_error("<action>: <message>").
+void check_cuda(int result, const char *action);
+
+// ---- tensors ------------------------------------------------------------------------------------
+// Host FP32 tensor with ncnn's (w, h, c) naming: dims 1 = [w], 2 = [h][w], 3 = [c][h][w].
+struct Tensor
+{
+    int w = 0, h = 1, c = 1, dims = 0;
+    std::vector<float> data;
+    Tensor() = default;
+    explicit Tensor(int w_) : w(w_), dims(1), data(size_t(w_)) {}
+    Tensor(int w_, int h_) : w(w_), h(h_), dims(2), data(size_t(w_) * h_) {}
+    Tensor(int w_, int h_, int c_) : w(w_), h(h_), c(c_), dims(3), data(size_t(w_) * h_ * c_) {}
+    bool empty() const { return data.empty(); }
+    size_t total() const { return data.size(); }
+    float *ptr() { return data.data(); }
+    const float *ptr() const { return data.data(); }
+    float &operator[](size_t i) { return data[i]; }
+    float operator[](size_t i) const { return data[i]; }
+};
+
+class GpuContext;
+
+// Device allocation owned by the caller (freed on destruction), shape in ncnn naming.
+class DeviceTensor
+{
+  public:
+    DeviceTensor() = default;
+    DeviceTensor(GpuContext &ctx, size_t bytes, int w, int h = 1, int c = 1, int dims = 1);
+    DeviceTensor(DeviceTensor &&) noexcept;
+    DeviceTensor &operator=(DeviceTensor &&) noexcept;
+    DeviceTensor(const DeviceTensor &) = delete;
+    DeviceTensor &operator=(const DeviceTensor &) = delete;
+    ~DeviceTensor();
+    static DeviceTensor upload(GpuContext &ctx, const Tensor &host);
+    Tensor download() const; // FP32 tensors only
+    void *data() const { return ptr_; }
+    float *f32() const { return static_cast<float *>(ptr_); }
+    size_t bytes() const { return bytes_; }
+    bool empty() const { return ptr_ == nullptr; }
+    int w = 0, h = 1, c = 1, dims = 0;
+
+  private:
+    GpuContext *ctx_ = nullptr;
+    void *ptr_ = nullptr;
+    size_t bytes_ = 0;
+};
+
+// ---- GPU context (src/gpu_context.h:12-27) -------------------------------------------------------
+// One CUDA device + stream. With enabled=false or no device (and require_device=false), available()
+// is false and initialization_error() says why; nothing falls back to the CPU.
+class GpuContext
+{
+  public:
+    explicit GpuContext(bool enabled, int requested_index = -1, bool require_device = true);
+    ~GpuContext();
+    GpuContext(const GpuContext &) = delete;
+    GpuContext &operator=(const GpuContext &) = delete;
+    bool available() const noexcept { return handle_ != nullptr; }
+    const std::string &initialization_error() const noexcept { return initialization_error_; }
+    ernie_cuda_context *handle() const;
+    int device() const noexcept { return device_; }
+    void synchronize() const;
+
+  private:
+    ernie_cuda_context *handle_ = nullptr;
+    int device_ = -1;
+    std::string initialization_error_;
+};
+
+// ---- latent ops (src/latent_ops.h:15-57) ---------------------------------------------------------
+struct FlowSchedule
+{
+    std::vector<float> sigmas;    // steps + 1, last 0
+    std::vector<float> timesteps; // 1000 * sigma
+    static FlowSchedule turbo(int steps = 8);
+    static FlowSchedule linear(int steps = 8);
+    float delta(size_t step) const; // sigma[step+1] - sigma[step]; std::out_of_range past the end
+};
+// Device latents [128][h][w]. Shapes and delta are validated as in src/latent_ops.cpp:69-86.
+void euler_step(GpuContext &, const DeviceTensor &sample, const DeviceTensor &prediction, float delta,
+                DeviceTensor &next);
+bool finite_latent(GpuContext &, const DeviceTensor &value);
+DeviceTensor unpack_for_vae(GpuContext &, const DeviceTensor &packed, const Tensor &mean, const Tensor &variance);
+
+// ---- conditioning (src/conditioning.h:12-15) and features (src/denoiser.h:96) --------------------
+// Returns {cosine [N][128], sine [N][128], mask [N]}; frequency table (64 values) or empty for the
+// official table. token_limit 6144 (static graphs) or 10240 (runtime).
+std::vector<Tensor> dit_constants(const std::vector<float> &frequencies, int width, int height, int valid_text,
+                                  int text_bucket, int token_limit = 10240);
+Tensor pad_text(const Tensor &embeddings /*[T][3072]*/, int bucket);
+Tensor timestep_features(float timestep);
+
+// ---- ERNIE layer contracts (register_layers, src/ernie_gelu.cpp:108-116) --------------------------
+void set_attention_query_rows(GpuContext &, int rows); // 128, 64, 32 or 16, else std::invalid_argument
+int attention_query_rows(GpuContext &);
+// ErnieSDPA: q [heads][nq][w], k/v [kv_heads][nk][w], optional mask [mask_heads][rows][nk] (rows 1 or nq).
+DeviceTensor sdpa(GpuContext &, const DeviceTensor &q, const DeviceTensor &k, const DeviceTensor &v,
+                  const DeviceTensor *mask);
+DeviceTensor rms_norm(GpuContext &, const DeviceTensor &x, const Tensor &gamma, float eps = 1e-6f); // w 128/3072/4096
+DeviceTensor layer_norm(GpuContext &, const DeviceTensor &x, float eps = 1e-6f);                     // w 4096
+void gelu_inplace(GpuContext &, DeviceTensor &x);                                                   // total % 4
+DeviceTensor residual_add(GpuContext &, const DeviceTensor &a, const DeviceTensor &b);
+
+// ---- weights --------------------------------------------------------------------------------------
+// Host copy of one block's BF16 weights (tools/build_dit_weights.py:19-31 bindings).
+struct BlockWeights
+{
+    std::vector<uint16_t> wq, wk, wv, wo, wup, wgate, wfc2;
+    std::vector<float> gamma_sa, gamma_mlp, gamma_q, gamma_k;
+};
+struct HeadWeights
+{
+    std::vector<uint16_t> x_embed_w, text_proj_w, time1_w, time2_w, adaln_w, final_norm_w, final_w;
+    std::vector<float> x_embed_b, time1_b, time2_b, adaln_b, final_norm_b, final_b;
+};
+// Device-resident DiT weights (all blocks stay in HBM: 15.7 GB for 36 blocks in BF16).
+class DitModel
+{
+  public:
+    DitModel(GpuContext &ctx, int num_blocks);
+    ~DitModel();
+    DitModel(const DitModel &) = delete;
+    DitModel &operator=(const DitModel &) = delete;
+    void upload_block(int block, const BlockWeights &);
+    void upload_heads(const HeadWeights &);
+    void synthesize(uint64_t seed); // seeded random init (include/ernie_synth.h)
+    int num_blocks() const noexcept { return num_blocks_; }
+    uint64_t bytes() const;
+    ernie_cuda_model *handle() const noexcept { return handle_; }
+    GpuContext &context() const noexcept { return ctx_; }
+
+  private:
+    GpuContext &ctx_;
+    ernie_cuda_model *handle_ = nullptr;
+    int num_blocks_ = 0;
+};
+
+// WeightPlacement (src/weight_placement.h:19-54): the decision logic of the reference, with the
+// CUDA device budget (cudaMemGetInfo) as the reader.
+enum class WeightMemory { Auto, Device, Host };
+WeightMemory parse_weight_memory(const std::string &value);
+struct DeviceMemoryBudget
+{
+    std::uint64_t budget_bytes = 0, usage_bytes = 0;
+};
+struct WeightPlacementDecision
+{
+    bool host = false;
+    const char *reason = "unavailable";
+    std::optional<std::uint64_t> available_bytes;
+    std::uint64_t weight_bytes = 0, reserve_bytes = 0;
+};
+WeightPlacementDecision choose_weight_placement(WeightMemory mode, bool shape_prefers_host, std::uint64_t weight_bytes,
+                                                std::uint64_t reserve_bytes, std::optional<DeviceMemoryBudget> memory);
+class WeightPlacement
+{
+  public:
+    using BudgetReader = std::function<std::optional<DeviceMemoryBudget>()>;
+    using Observer = std::function<void(const std::string &component, const WeightPlacementDecision &)>;
+    WeightPlacement(WeightMemory mode, std::uint64_t reserve_bytes, BudgetReader reader = {}, Observer observer = {});
+    // weight_bytes = the component's payload estimate (the reference uses 2x the file size)
+    bool use_host(const std::string &component, std::uint64_t weight_bytes, bool shape_prefers_host,
+                  bool cache_prefers_host = false, const char *host_reason = "cache");
+    std::uint64_t host_requests() const { return host_requests_; }
+    std::uint64_t device_requests() const { return device_requests_; }
+    std::uint64_t unavailable_queries() const { return unavailable_queries_; }
+
+  private:
+    WeightMemory mode_;
+    std::uint64_t reserve_bytes_, host_requests_ = 0, device_requests_ = 0, unavailable_queries_ = 0;
+    BudgetReader reader_;
+    Observer observer_;
+};
+WeightPlacement::BudgetReader cuda_memory_budget_reader(GpuContext &);
+
+// WeightSession (src/weight_session.h:29-73): request-local cache of prepared per-block payloads with
+// one lease at a time. Admitted entries stay while the rest stream (LRU would miss every block of a
+// repeated 36-block scan). The payload type is opaque here.
+struct WeightBudget
+{
+    std::uint64_t host_bytes = 0;
+    std::uint64_t reserve_bytes = 3ull * 1024 * 1024 * 1024;
+};
+struct WeightSessionStats
+{
+    std::uint64_t hits = 0, loads = 0, admissions = 0, evictions = 0;
+    std::uint64_t live_bytes = 0, peak_bytes = 0, cached_nets = 0, peak_nets = 0;
+    std::uint64_t unavailable_queries = 0;
+};
+class WeightSession
+{
+    struct State;
+
+  public:
+    using Payload = std::shared_ptr<void>;
+    using AvailableReader = std::function<std::optional<std::uint64_t>()>;
+    using Inspector = std::function<std::optional<std::uint64_t>(const Payload &)>;
+    using Loader = std::function<Payload(bool prefer_cache)>;
+    class Lease
+    {
+      public:
+        Lease() = default;
+        Lease(const Lease &) = delete;
+        Lease &operator=(const Lease &) = delete;
+        Lease(Lease &&) noexcept;
+        Lease &operator=(Lease &&) noexcept;
+        ~Lease();
+        const Payload &payload() const;
+        bool cached() const { return charge_ != 0; }
+        void complete(); // only after all work using the payload has completed
+      private:
+        friend class WeightSession;
+        Lease(std::shared_ptr<State>, std::size_t, Payload, std::uint64_t);
+        void release(bool completed);
+        std::shared_ptr<State> state_;
+        std::size_t block_ = 0;
+        Payload payload_;
+        std::uint64_t charge_ = 0;
+    };
+    WeightSession(WeightBudget, AvailableReader, Inspector);
+    ~WeightSession();
+    WeightSession(const WeightSession &) = delete;
+    WeightSession &operator=(const WeightSession &) = delete;
+    Lease acquire(std::size_t block, const std::string &identity, const void *request_identity,
+                  std::uint64_t estimated_bytes, const Loader &);
+    void cancel();
+    WeightSessionStats stats() const;
+    bool contains(std::size_t block) const;
+
+  private:
+    std::shared_ptr<State> state_;
+};
+
+// ---- block sequence / DiT / denoise ---------------------------------------------------------------
+enum class Precision { BF16, FP32 };
+struct BlockSequenceStats // src/block_sequence.h:20-32
+{
+    std::vector<double> load_seconds, compute_seconds;
+    int peak_loaded_nets = 0, compute_submissions = 0;
+};
+struct DitStats // src/dit.h:6-14
+{
+    BlockSequenceStats blocks;
+    double input_head_seconds = 0, output_head_seconds = 0;
+};
+using CudaStageObserver = std::function<void(const std::string &, const DeviceTensor &)>;
+
+// A request: shape, precision and the four constants (text, cos, sin, mask) on the device.
+class DenoiseSession
+{
+  public:
+    DenoiseSession(DitModel &model, int width, int height, int text_tokens, int valid_text, Precision precision);
+    ~DenoiseSession();
+    DenoiseSession(const DenoiseSession &) = delete;
+    DenoiseSession &operator=(const DenoiseSession &) = delete;
+    // constants: text [T][3072] (may be empty), cos [N][128], sin [N][128], mask [N]
+    void set_constants(const std::vector<Tensor> &constants);
+    int tokens() const noexcept { return tokens_; }
+    int width() const noexcept { return width_; }
+    int height() const noexcept { return height_; }
+    ernie_cuda_session *handle() const noexcept { return handle_; }
+    DitModel &model() const noexcept { return model_; }
+
+  private:
+    DitModel &model_;
+    ernie_cuda_session *handle_ = nullptr;
+    int width_, height_, tokens_;
+};
+
+// run_block_sequence (src/block_sequence.h:38-60): blocks [first, first+count) on x [N][4096] (device,
+// in place) with the shared modulation [6][4096] (device). 1..36 blocks.
+void run_block_sequence(DenoiseSession &, DeviceTensor &x, const DeviceTensor &modulation, int first, int count,
+                        BlockSequenceStats &stats);
+// run_dit (src/dit.h:17-40): one prediction [128][h][w] for latent [128][h][w] at `timestep`.
+DeviceTensor run_dit(DenoiseSession &, const DeviceTensor &latent, float timestep, DitStats &stats);
+
+struct DenoiseStepStats // src/denoiser.h:102-108
+{
+    float timestep = 0, delta = 0;
+    DitStats dit;
+    double elapsed_seconds = 0;
+    bool complete = false;
+};
+using StepObserver = std::function<void(size_t, const Tensor &prediction, const Tensor &latent)>;
+// denoise (src/denoiser.h:110-128): steps [start_step, steps) of the turbo schedule; the observer
+// (optional) sees each step's prediction and latent (forcing one step per launch). Throws
+// std::invalid_argument on contract errors and std::runtime_error("Non-finite latent after denoise
+// step k"); stats holds the executed steps, a failed one with complete = false.
+Tensor denoise(DenoiseSession &, const Tensor &initial, int steps, std::vector<DenoiseStepStats> &stats,
+               const StepObserver &observer = {}, int start_step = 0, int schedule = ERNIE_SCHEDULE_TURBO);
+
+// ---- recovery (src/vulkan_denoise.h:8-47) ---------------------------------------------------------
+// One attempt runs steps on some backend; on GpuAllocationError (or std::bad_alloc) the wrapper
+// retries from the last host checkpoint with the same absolute schedule, at most `retries` times,
+// halving the recorded attention query rows (128 >> attempt). Any other failure propagates.
+class DenoiseBackend
+{
+  public:
+    virtual ~DenoiseBackend() = default;
+    // Prepare an attempt from the checkpoint (may throw GpuAllocationError).
+    virtual void begin_attempt(unsigned attempt, const Tensor &checkpoint, int query_rows) = 0;
+    // Run absolute step i of the schedule; returns the prediction, updates the backend's latent.
+    virtual Tensor run_step(int step, float timestep, float delta) = 0;
+    virtual Tensor latent() = 0;     // download the current latent (the checkpoint source)
+    virtual void end_attempt() = 0;  // release the attempt's resources (also after a failure)
+};
+struct CudaDenoiseSettings
+{
+    unsigned retries = 3;
+    int schedule = ERNIE_SCHEDULE_TURBO;
+    std::function<void(unsigned attempt, int step)> before_step; // test seam, invoked before each step
+};
+struct CudaDenoiseStats
+{
+    unsigned retries = 0;
+    int query_rows = 128;
+};
+struct CudaDenoiseObservers
+{
+    std::function<void(size_t, const Tensor &prediction, const Tensor &latent, const DenoiseStepStats &)> step;
+    std::function<void(unsigned attempt, int step, int rows, const std::string &)> retry;
+};
+Tensor denoise_with_recovery(DenoiseBackend &, const Tensor &initial, int steps, int start_step,
+                             const CudaDenoiseSettings &, CudaDenoiseStats &, const CudaDenoiseObservers & = {});
+// The B200 backend: a DenoiseSession per attempt on one model.
+class CudaDenoiseBackend : public DenoiseBackend
+{
+  public:
+    CudaDenoiseBackend(DitModel &model, int width, int height, int text_tokens, int valid_text, Precision,
+                       std::vector<Tensor> constants);
+    void begin_attempt(unsigned attempt, const Tensor &checkpoint, int query_rows) override;
+    Tensor run_step(int step, float timestep, float delta) override;
+    Tensor latent() override;
+    void end_attempt() override;
+    int steps = 8; // schedule length the steps belong to
+
+  private:
+    DitModel &model_;
+    int width_, height_, text_, valid_;
+    Precision precision_;
+    std::vector<Tensor> constants_;
+    std::unique_ptr<DenoiseSession> session_;
+};
+} // namespace ernie
