@@ -197,6 +197,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["bf16", "fp32"], default=None)
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--parallel", choices=["dp", "sp"], default=None,
+                    help="dp: one seed per GPU (default); sp: one request split over the GPUs by Ulysses "
+                         "sequence parallelism (default for --config c4)")
     ap.add_argument("--blocks", type=int, default=NUM_BLOCKS, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -216,33 +219,49 @@ def main():
 
     import ernie_cuda as ec
     rank, local, world, pg = dist_setup(args.gpus)
+    parallel = args.parallel or ("sp" if args.config == "c4" else "dp")
+    sp = parallel == "sp" and world > 1
     ctx = ec.Context(local)
     model = ec.Model(ctx, args.blocks)
     model.synthesize(1234)
     precision = ec.BF16 if args.precision == "bf16" else ec.FP32
-    session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision)
-    # data parallel: one independent request (seed) per GPU, no collective in the data path
-    seed = dp.request_seed(1000, dp.shard_requests(world, rank, world)[0])
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    tokens = WIDTH * HEIGHT + TEXT
+    n_valid = WIDTH * HEIGHT + VALID
+    if sp:
+        # one request over all ranks: rank 0's NCCL id reaches the others through the process group
+        ids = [ec.nccl_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(ids, src=0)
+        session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision, sp=(ids[0], rank, world))
+        shard, _, img_rows, local_rows, _ = ec.sp_layout(tokens, WIDTH * HEIGHT, world, rank)
+        seed = dp.request_seed(1000, 0)
+    else:
+        session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision)
+        # data parallel: one independent request (seed) per GPU, no collective in the data path
+        seed = dp.request_seed(1000, dp.shard_requests(world, rank, world)[0])
+        local_rows = tokens
     rng = np.random.default_rng(seed)
     latent = rng.standard_normal((128, HEIGHT, WIDTH), dtype=np.float32)
     text = rng.standard_normal((TEXT, 3072), dtype=np.float32)
     cos, sin, mask = ec.dit_constants(WIDTH, HEIGHT, VALID, TEXT)
     session.set_conditioning(text, cos, sin, mask)
-    tokens = WIDTH * HEIGHT + TEXT
-    flops = step_flops(tokens, WIDTH * HEIGHT + VALID, args.blocks)
+    flops = step_flops(tokens, n_valid, args.blocks) / (world if sp else 1)  # per GPU
     launches_per_step = session.launches_per_step()
 
     # warm-up: graph capture of every step index, then W steps
     lat_ptr = session.latent_ptr()
-    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(latent), latent.nbytes))
+    if sp:  # this rank's token slice [128][S] of the latent
+        device_latent = np.zeros((128, shard), np.float32)
+        device_latent[:, :img_rows] = latent.reshape(128, -1)[:, rank * shard: rank * shard + img_rows]
+    else:
+        device_latent = latent
+    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(device_latent), device_latent.nbytes))
     for i in range(args.warmup):
         session.denoise_device(STEPS_PER_IMAGE, i % STEPS_PER_IMAGE, i % STEPS_PER_IMAGE + 1)
     for i in range(STEPS_PER_IMAGE):
         session.denoise_device(STEPS_PER_IMAGE, i, i + 1)
 
     # timed region: K steps, device-timed with CUDA events on the library's stream
-    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(latent), latent.nbytes))
+    ec.check(ec.lib().ernie_cuda_upload(ctx.handle, lat_ptr, ec.ptr(device_latent), device_latent.nbytes))
     clocks = ClockSampler(local)
     barrier(pg)
     ctx.synchronize()
@@ -257,7 +276,7 @@ def main():
     ms = ctx.elapsed(0, 1)
     ms_max = max_over_ranks(pg, ms)
     ms_per_step = ms_max / args.steps
-    images_per_s = world * 1000.0 / (ms_per_step * STEPS_PER_IMAGE)
+    images_per_s = (1 if sp else world) * 1000.0 / (ms_per_step * STEPS_PER_IMAGE)
 
     # dominant kernel, timed live: the up/gate GEMM (largest of the 7 per block)
     prof = {}
@@ -267,10 +286,13 @@ def main():
     prof["step_eager"] = session.profile(8, 2)  # one step enqueued without a graph
     prof["heads"] = session.profile(9, 10)  # input head, GEMVs, output head + Euler of one step
     bf16_peak, bf16_sustained, hbm_peak, peak_kind = peaks()
-    n_valid = WIDTH * HEIGHT + VALID
-    kernel_flops = {"qkv_gemm": 2.0 * tokens * 4096 * 12288, "attention": 4.0 * tokens * n_valid * 4096,
-                    "out_gemm": 2.0 * tokens * 4096 * 4096, "upgate_gemm": 2.0 * tokens * 4096 * 24576,
-                    "down_gemm": 2.0 * tokens * 12288 * 4096}
+    # per-launch algorithmic FLOPs on this GPU: GEMMs over its token rows; attention over every query
+    # row for its share of the heads (SP: 32/P heads, the all-to-alls inside the timed launch)
+    T = local_rows
+    kernel_flops = {"qkv_gemm": 2.0 * T * 4096 * 12288,
+                    "attention": 4.0 * tokens * n_valid * 4096 / (world if sp else 1),
+                    "out_gemm": 2.0 * T * 4096 * 4096, "upgate_gemm": 2.0 * T * 4096 * 24576,
+                    "down_gemm": 2.0 * T * 12288 * 4096}
     dominant = "upgate_gemm"
     achieved = kernel_flops[dominant] / (prof[dominant] * 1e-3) / 1e12
     step_tflops = flops / (ms_per_step * 1e-3) / 1e12
@@ -287,7 +309,7 @@ def main():
         dt = (time.perf_counter() - t0) / reps
         dt = max_over_ranks(pg, dt)
         assert np.isfinite(out).all()
-        e2e = {"value": world / dt, "unit": "images/s", "h2d_bytes_per_step": latent.nbytes // STEPS_PER_IMAGE,
+        e2e = {"value": (1 if sp else world) / dt, "unit": "images/s", "h2d_bytes_per_step": latent.nbytes // STEPS_PER_IMAGE,
                "d2h_bytes_per_step": latent.nbytes // STEPS_PER_IMAGE,
                "call": "ernie_cuda_session_denoise (8 steps, host buffers); bytes per step = latent bytes / 8"}
 
@@ -301,11 +323,13 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-                "config": {"workload": f"{args.workload}, {args.blocks} blocks, turbo 8-step schedule, "
-                                       "one seed per GPU",
-                           "global_batch": world, "seq_len": tokens, "parallelism": f"dp{world}",
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if sp else "weak", "vs_baseline": None, "dtype": args.precision,
+                "data": "synthetic",
+                "config": {"workload": f"{args.workload}, {args.blocks} blocks, turbo 8-step schedule, " +
+                                       ("one request split over the GPUs" if sp else "one seed per GPU"),
+                           "global_batch": 1 if sp else world, "seq_len": tokens,
+                           "parallelism": f"sp{world}" if sp else f"dp{world}", "rows_per_gpu": T,
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
                            "kernel_ms": prof},

@@ -4,6 +4,7 @@
 #include "ernie_cuda.h"
 #include "ernie_synth.h"
 #include "kernels.h"
+#include "nccl_dyn.h"
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -192,6 +193,15 @@ struct ernie_cuda_session
     std::vector<float> deltas;
     float *pinned = nullptr;
     std::map<std::tuple<int, int, int, int, int>, cudaGraphExec_t> graphs;
+    // Rows of this session's token range (the whole sequence unless sequence-parallel): image rows,
+    // real (unpadded) rows, first text slot, and the latent's channel stride.
+    int img_local = 0, real_local = 0, text_begin = 0, latent_ld = 0;
+    // Ulysses sequence parallelism (world 1 = one GPU): this rank owns tokens [rank*S, rank*S + S).
+    int sp_world = 1, sp_rank = 0, full_tokens = 0, shard = 0, full_rows = 0, heads_local = kHeads;
+    ncclComm_t comm = nullptr;
+    __nv_bfloat16 *q_full = nullptr, *k_full = nullptr, *v_full = nullptr, *vt_full = nullptr, *o_full = nullptr,
+                  *o_recv = nullptr, *text_op = nullptr;
+    float *text_stage = nullptr, *gathered = nullptr;
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -731,8 +741,22 @@ extern "C" int ernie_cuda_dit_constants(const float *freq64, int w, int h, int v
 }
 
 // ---------------------------------------------------------------- session
-extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
-                                         ernie_cuda_session **out)
+// Token range of one sequence-parallel rank: shard S = ceil(N / world) rounded up to 16 rows.
+static void sp_geometry(int tokens, int image, int world, int rank, int *shard, int *full_rows, int *img_local,
+                        int *real_local, int *text_begin)
+{
+    const int S = ((tokens + world - 1) / world + 15) / 16 * 16;
+    const int begin = rank * S;
+    auto clamp = [](int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; };
+    *shard = S;
+    *full_rows = (world * S + 127) / 128 * 128;
+    *img_local = clamp(image - begin, 0, S);
+    *real_local = clamp(tokens - begin, 0, S);
+    *text_begin = begin + *img_local >= image ? begin + *img_local - image : 0;
+}
+
+static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision, int world, int rank,
+                          const void *nccl_id, ernie_cuda_session **out)
 {
     if (!model || !shape || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
     *out = nullptr;
@@ -742,6 +766,9 @@ extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cu
         return fail(ERNIE_CUDA_ERROR, "Invalid DiT shape (w,h in 1..256, text 1..2048, tokens <= 10240)");
     if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
         return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    if (world > 1 && (precision != ERNIE_PRECISION_BF16 || (world != 2 && world != 4 && world != 8) || rank < 0 ||
+                      rank >= world || !nccl_id))
+        return fail(ERNIE_CUDA_ERROR, "Sequence parallelism needs BF16, 2, 4 or 8 ranks and an NCCL id");
     ernie_cuda_context *ctx = model->ctx;
     DeviceGuard guard(ctx->device);
     auto *s = new ernie_cuda_session();
@@ -754,19 +781,38 @@ extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cu
     s->precision = precision;
     s->splits = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
     s->image = s->width * s->height;
-    s->tokens = s->image + s->text;
-    s->rows_pad = (s->tokens + 127) / 128 * 128;
+    s->full_tokens = s->image + s->text;
     s->kv_len = s->image + s->valid;
+    s->sp_world = world;
+    s->sp_rank = rank;
+    if (world > 1)
+    {
+        sp_geometry(s->full_tokens, s->image, world, rank, &s->shard, &s->full_rows, &s->img_local, &s->real_local,
+                    &s->text_begin);
+        s->tokens = s->shard;
+        s->heads_local = kHeads / world;
+        s->latent_ld = s->shard;
+    }
+    else
+    {
+        s->tokens = s->full_tokens;
+        s->img_local = s->image;
+        s->real_local = s->tokens;
+        s->text_begin = 0;
+        s->latent_ld = s->image;
+    }
+    s->rows_pad = (s->tokens + 127) / 128 * 128;
     const size_t T = s->tokens, P = s->rows_pad, qkv_elem = precision == ERNIE_PRECISION_FP32 ? 4 : 2;
+    const size_t L = size_t(kLatent) * (world > 1 ? s->shard : s->image);
     Arena arena;
     arena.add(&s->x, T * kHidden);
     arena.add(&s->text_cache, size_t(s->text) * kHidden);
     arena.add(&s->cos_t, T * kHeadDim);
     arena.add(&s->sin_t, T * kHeadDim);
-    arena.add(&s->mask, T);
-    arena.add(&s->latent, size_t(kLatent) * s->image);
-    arena.add(&s->scratch_latent, size_t(kLatent) * s->image);
-    arena.add(&s->pred, size_t(kLatent) * s->image);
+    arena.add(&s->mask, size_t(s->full_tokens));
+    arena.add(&s->latent, L);
+    arena.add(&s->scratch_latent, L);
+    arena.add(&s->pred, L);
     arena.add(&s->g1, kHidden);
     arena.add(&s->c, kHidden);
     arena.add(&s->mod, 6 * kHidden);
@@ -776,17 +822,81 @@ extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cu
     arena.add(reinterpret_cast<char **>(&s->q), size_t(kHeads) * P * kHeadDim * qkv_elem);
     arena.add(reinterpret_cast<char **>(&s->k), size_t(kHeads) * P * kHeadDim * qkv_elem);
     arena.add(reinterpret_cast<char **>(&s->v), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    if (world > 1)
+    {
+        const size_t F = s->full_rows, hl = s->heads_local;
+        arena.add(&s->q_full, hl * F * kHeadDim);
+        arena.add(&s->k_full, hl * F * kHeadDim);
+        arena.add(&s->v_full, hl * F * kHeadDim);
+        arena.add(&s->vt_full, hl * F * kHeadDim);
+        arena.add(&s->o_full, F * hl * kHeadDim);
+        arena.add(&s->o_recv, size_t(world) * T * hl * kHeadDim);
+        arena.add(&s->text_op, size_t(s->text) * kTextDim);
+        arena.add(&s->text_stage, size_t(s->text) * kTextDim);
+        arena.add(&s->gathered, size_t(world) * L);
+    }
     cudaError_t e = arena.allocate();
+    s->alloc = arena.base;
     if (e == cudaSuccess) e = cudaMemset(arena.base, 0, arena.bytes());
     if (e == cudaSuccess) e = cudaMallocHost(&s->pinned, sizeof(float) * kLatent * s->image);
     if (e != cudaSuccess)
     {
-        s->alloc = arena.base;
         ernie_cuda_session_destroy(s);
         return from_cuda(e, "Allocate session activations");
     }
-    s->alloc = arena.base;
+    if (world > 1)
+    {
+        const NcclApi &api = nccl();
+        if (!api.ok)
+        {
+            ernie_cuda_session_destroy(s);
+            return fail(ERNIE_CUDA_ERROR, "libnccl.so.2 not found: sequence parallelism needs NCCL");
+        }
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        const ncclResult_t r = api.comm_init_rank(&s->comm, world, id, rank);
+        if (r != ncclSuccess)
+        {
+            s->comm = nullptr;
+            ernie_cuda_session_destroy(s);
+            return fail(ERNIE_CUDA_ERROR, std::string("ncclCommInitRank: ") + api.error_string(r));
+        }
+    }
     *out = s;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
+                                         ernie_cuda_session **out)
+{
+    return create_session(model, shape, precision, 1, 0, nullptr, out);
+}
+
+extern "C" int ernie_cuda_nccl_unique_id(void *id)
+{
+    if (!id) return fail(ERNIE_CUDA_ERROR, "null argument");
+    const NcclApi &api = nccl();
+    if (!api.ok) return fail(ERNIE_CUDA_ERROR, "libnccl.so.2 not found");
+    ncclUniqueId uid;
+    const ncclResult_t r = api.get_unique_id(&uid);
+    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("ncclGetUniqueId: ") + api.error_string(r));
+    std::memcpy(id, &uid, sizeof(uid));
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_session_create_sp(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
+                                            const void *nccl_id, int rank, int world, ernie_cuda_session **out)
+{
+    return create_session(model, shape, precision, world, rank, nccl_id, out);
+}
+
+extern "C" int ernie_cuda_sp_layout(int tokens, int image, int world, int rank, int *shard, int *full_rows,
+                                    int *image_rows, int *real_rows, int *text_begin)
+{
+    if (!shard || !full_rows || !image_rows || !real_rows || !text_begin) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (tokens < 1 || image < 0 || image > tokens || world < 1 || rank < 0 || rank >= world)
+        return fail(ERNIE_CUDA_ERROR, "Invalid sequence-parallel layout");
+    sp_geometry(tokens, image, world, rank, shard, full_rows, image_rows, real_rows, text_begin);
     return ERNIE_CUDA_OK;
 }
 
@@ -801,7 +911,8 @@ extern "C" int ernie_cuda_session_destroy(ernie_cuda_session *s)
     if (!s) return ERNIE_CUDA_OK;
     DeviceGuard guard(s->ctx->device);
     cudaStreamSynchronize(s->ctx->stream);
-    release_graphs(s);
+    release_graphs(s); // graphs that hold NCCL calls go before the communicator
+    if (s->comm) nccl().comm_destroy(s->comm);
     if (s->alloc) cudaFree(s->alloc);
     if (s->features) cudaFree(s->features);
     if (s->flags) cudaFree(s->flags);
@@ -841,11 +952,11 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
     if (!s || !cos_table || !sin_table || !mask) return fail(ERNIE_CUDA_ERROR, "Require cosine, sine and mask");
     DeviceGuard guard(s->ctx->device);
     cudaStream_t st = s->ctx->stream;
-    const size_t T = s->tokens;
+    const size_t N = s->full_tokens;
     // Valid key count from the additive row mask: keys past the last visible one contribute zero.
     int last = -1;
     bool general = false;
-    for (size_t k = 0; k < T; ++k)
+    for (size_t k = 0; k < N; ++k)
     {
         if (!(mask[k] <= 0.f) || std::isnan(mask[k])) return fail(ERNIE_CUDA_ERROR, "Mask values must be <= 0");
         if (mask[k] > -1e29f) last = static_cast<int>(k);
@@ -855,21 +966,35 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
         if (mask[k] != 0.f) general = true;
     s->kv_len = last + 1;
     s->use_mask = general;
-    ERNIE_CUDA(cudaMemcpyAsync(s->cos_t, cos_table, T * kHeadDim * 4, cudaMemcpyHostToDevice, st), "upload cos");
-    ERNIE_CUDA(cudaMemcpyAsync(s->sin_t, sin_table, T * kHeadDim * 4, cudaMemcpyHostToDevice, st), "upload sin");
-    ERNIE_CUDA(cudaMemcpyAsync(s->mask, mask, T * 4, cudaMemcpyHostToDevice, st), "upload mask");
+    // cos/sin rows of this session's token range (rows past the sequence stay zero)
+    const size_t first = size_t(s->sp_rank) * s->tokens, rows = s->real_local;
+    ERNIE_CUDA(cudaMemsetAsync(s->cos_t, 0, size_t(s->tokens) * kHeadDim * 4, st), "clear cos");
+    ERNIE_CUDA(cudaMemsetAsync(s->sin_t, 0, size_t(s->tokens) * kHeadDim * 4, st), "clear sin");
+    if (rows)
+    {
+        ERNIE_CUDA(cudaMemcpyAsync(s->cos_t, cos_table + (s->sp_world > 1 ? first : 0) * kHeadDim, rows * kHeadDim * 4,
+                                   cudaMemcpyHostToDevice, st),
+                   "upload cos");
+        ERNIE_CUDA(cudaMemcpyAsync(s->sin_t, sin_table + (s->sp_world > 1 ? first : 0) * kHeadDim, rows * kHeadDim * 4,
+                                   cudaMemcpyHostToDevice, st),
+                   "upload sin");
+    }
+    ERNIE_CUDA(cudaMemcpyAsync(s->mask, mask, N * 4, cudaMemcpyHostToDevice, st), "upload mask");
     s->has_text = text != nullptr;
     if (text)
     {
         // text_proj once per request (text is constant across steps): FP32 -> operand -> GEMM.
-        float *staging = s->x; // [text][3072] fits in the [tokens][4096] residual buffer
+        // Single GPU: [text][3072] fits in the [tokens][4096] residual and operand buffers.
+        float *staging = s->sp_world > 1 ? s->text_stage : s->x;
+        __nv_bfloat16 *operand = s->sp_world > 1 ? s->text_op : s->a;
         ERNIE_CUDA(cudaMemcpyAsync(staging, text, size_t(s->text) * kTextDim * 4, cudaMemcpyHostToDevice, st), "upload text");
-        ERNIE_LAUNCH(launch_to_operand(staging, s->text, kTextDim, s->a, s->splits == 3, st), "text operand");
+        ERNIE_LAUNCH(launch_to_operand(staging, s->text, kTextDim, operand, s->splits == 3, st), "text operand");
         GemmEpilogueArgs args;
         args.out = s->text_cache;
         args.ldo = kHidden;
         args.error_flag = s->ctx->error_flag;
-        ERNIE_LAUNCH(session_gemm(s, s->a, s->model->heads.text_proj_w, s->text, kHidden, kTextDim, 256, Epilogue::F32Bias, args),
+        ERNIE_LAUNCH(session_gemm(s, operand, s->model->heads.text_proj_w, s->text, kHidden, kTextDim, 256,
+                                  Epilogue::F32Bias, args),
                      "text_proj");
     }
     ERNIE_CUDA(cudaStreamSynchronize(st), "set conditioning");
@@ -878,15 +1003,62 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
     return ERNIE_CUDA_OK;
 }
 
+// Ulysses all-to-all #1: this rank's Q, K, V rows of all 32 heads ([32][S][128] each) go out as
+// per-head blocks; the rank receives every rank's rows of its own 32/P heads into [heads_local][F][128].
+static int exchange_qkv(ernie_cuda_session *s)
+{
+    const NcclApi &api = nccl();
+    cudaStream_t st = s->ctx->stream;
+    const int P = s->sp_world, hl = s->heads_local, S = s->tokens;
+    const size_t block = size_t(S) * kHeadDim;
+    const __nv_bfloat16 *send[3] = {static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
+                                    static_cast<const __nv_bfloat16 *>(s->v)};
+    __nv_bfloat16 *recv[3] = {s->q_full, s->k_full, s->v_full};
+    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
+    for (int t = 0; t < 3; ++t)
+        for (int peer = 0; peer < P; ++peer)
+            for (int h = 0; h < hl; ++h)
+            {
+                api.send(send[t] + (size_t(peer) * hl + h) * block, block, ncclBfloat16, peer, s->comm, st);
+                api.recv(recv[t] + (size_t(h) * s->full_rows + size_t(peer) * S) * kHeadDim, block, ncclBfloat16, peer,
+                         s->comm, st);
+            }
+    const ncclResult_t r = api.group_end();
+    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("Q/K/V all-to-all: ") + api.error_string(r));
+    return ERNIE_CUDA_OK;
+}
+
+// Ulysses all-to-all #2: attention rows of rank p's tokens (all of this rank's heads) go back to p.
+static int exchange_o(ernie_cuda_session *s)
+{
+    const NcclApi &api = nccl();
+    cudaStream_t st = s->ctx->stream;
+    const int P = s->sp_world, S = s->tokens;
+    const size_t block = size_t(S) * s->heads_local * kHeadDim;
+    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
+    for (int peer = 0; peer < P; ++peer)
+    {
+        api.send(s->o_full + size_t(peer) * block, block, ncclBfloat16, peer, s->comm, st);
+        api.recv(s->o_recv + size_t(peer) * block, block, ncclBfloat16, peer, s->comm, st);
+    }
+    const ncclResult_t r = api.group_end();
+    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("attention all-to-all: ") + api.error_string(r));
+    return ERNIE_CUDA_OK;
+}
+
 // One DiT block on x [tokens][4096] (block.ncnn.param:14-76), 7 launches.
 // `only` >= 0 enqueues just that part (0 norm sa, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 norm mlp,
 // 5 up/gate GEMM, 6 down GEMM); used by the benchmark's per-kernel timing.
 static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mod, int only = -1)
 {
-    auto on = [only](int part) { return only < 0 || only == part; };
+    // T = real rows of this session's token range; a sequence-parallel rank with none still joins
+    // both all-to-alls and computes its heads' attention for every token.
+    const int T = s->real_local;
+    const bool seq_parallel = s->sp_world > 1;
+    auto on = [only, T](int part) { return (only < 0 || only == part) && (T > 0 || part == 2); };
     const DevBlock &w = s->model->blocks[b];
     cudaStream_t st = s->ctx->stream;
-    const int T = s->tokens, sp = s->splits, nsm = s->ctx->num_sms;
+    const int sp = s->splits, nsm = s->ctx->num_sms;
     const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
     const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
     const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
@@ -896,9 +1068,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.q = s->q;
     qkv.k = s->k;
     qkv.v = s->v;
-    qkv.rows_pad = s->rows_pad;
+    qkv.rows_pad = seq_parallel ? s->tokens : s->rows_pad; // SP: [32][S][128] all-to-all send blocks
     qkv.qkv_fp32 = fp32;
-    qkv.v_transposed = !fp32;
+    qkv.v_transposed = !fp32 && !seq_parallel;
     qkv.gamma_q = w.gamma_q;
     qkv.gamma_k = w.gamma_k;
     qkv.cos_t = s->cos_t;
@@ -906,6 +1078,19 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.error_flag = s->ctx->error_flag;
     if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, 256, Epilogue::Qkv, qkv), "qkv");
     if (!on(2)) {}
+    else if (seq_parallel)
+    {
+        const int rows = s->sp_world * s->tokens; // the gathered sequence, padding rows at the end
+        ERNIE_TRY(exchange_qkv(s));
+        ERNIE_LAUNCH(launch_transpose_heads(s->v_full, s->heads_local, s->full_rows, s->full_rows, s->vt_full, st),
+                     "transpose V");
+        ERNIE_LAUNCH(launch_flash_tc(s->q_full, s->k_full, s->vt_full, s->use_mask ? s->mask : nullptr, rows,
+                                     s->full_rows, s->kv_len, s->heads_local, s->o_full, s->ctx->error_flag, st),
+                     "attention");
+        ERNIE_TRY(exchange_o(s));
+        ERNIE_LAUNCH(launch_gather_heads(s->o_recv, s->sp_world, s->tokens, s->heads_local * kHeadDim, s->a, st),
+                     "gather heads");
+    }
     else if (fp32)
     {
         AttentionF32Args a{};
@@ -959,21 +1144,28 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     cudaStream_t st = s->ctx->stream;
     const int nsm = s->ctx->num_sms, sp = s->splits;
     const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
-    // input head: image rows (x_embedder) and text rows (cached text_proj)
-    if (s->has_text)
-        ERNIE_CUDA(cudaMemcpyAsync(s->x + size_t(s->image) * kHidden, s->text_cache, size_t(s->text) * kHidden * 4,
-                                   cudaMemcpyDeviceToDevice, st),
-                   "text rows");
-    else
-        ERNIE_CUDA(cudaMemsetAsync(s->x + size_t(s->image) * kHidden, 0, size_t(s->text) * kHidden * 4, st), "text rows");
-    ERNIE_LAUNCH(launch_latent_to_tokens(latent, s->image, s->a, fp32, st), "latent operand");
-    GemmEpilogueArgs emb;
-    emb.out = s->x;
-    emb.ldo = kHidden;
-    emb.bias = hd.x_embed_b;
-    emb.error_flag = s->ctx->error_flag;
-    ERNIE_LAUNCH(session_gemm(s, s->a, hd.x_embed_w, s->image, kHidden, kLatent, 256, Epilogue::F32Bias, emb),
-                 "x_embedder");
+    // input head over this session's token range: image rows (x_embedder) then text rows (cached text_proj)
+    const int img = s->img_local, text_rows = s->real_local - s->img_local;
+    if (text_rows > 0)
+    {
+        if (s->has_text)
+            ERNIE_CUDA(cudaMemcpyAsync(s->x + size_t(img) * kHidden, s->text_cache + size_t(s->text_begin) * kHidden,
+                                       size_t(text_rows) * kHidden * 4, cudaMemcpyDeviceToDevice, st),
+                       "text rows");
+        else
+            ERNIE_CUDA(cudaMemsetAsync(s->x + size_t(img) * kHidden, 0, size_t(text_rows) * kHidden * 4, st), "text rows");
+    }
+    if (img > 0)
+    {
+        ERNIE_LAUNCH(launch_latent_to_tokens(latent, img, s->a, fp32, st, s->latent_ld), "latent operand");
+        GemmEpilogueArgs emb;
+        emb.out = s->x;
+        emb.ldo = kHidden;
+        emb.bias = hd.x_embed_b;
+        emb.error_flag = s->ctx->error_flag;
+        ERNIE_LAUNCH(session_gemm(s, s->a, hd.x_embed_w, img, kHidden, kLatent, 256, Epilogue::F32Bias, emb),
+                     "x_embedder");
+    }
     ERNIE_LAUNCH(launch_gemv(hd.time1_w, features, hd.time1_b, s->g1, kHidden, kHidden, 0, st), "time linear_1");
     ERNIE_LAUNCH(launch_gemv(hd.time2_w, s->g1, hd.time2_b, s->c, kHidden, kHidden, 1, st), "time linear_2");
     ERNIE_LAUNCH(launch_gemv(hd.adaln_w, s->c, hd.adaln_b, s->mod, 6 * kHidden, kHidden, 1, st), "adaLN");
@@ -981,17 +1173,21 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     if (with_blocks)
         for (int b = 0; b < s->model->num_blocks; ++b) ERNIE_TRY(enqueue_block(s, b, s->x, s->mod));
     // output head: LayerNorm + modulate on image rows, linear + bias, fused Euler update
-    ERNIE_LAUNCH(launch_norm_modulate(s->x, s->image, kHidden, nullptr, s->ss, s->ss + kHidden, 1e-6f, 1, s->a, fp32, st),
-                 "final norm");
-    GemmEpilogueArgs fin;
-    fin.bias = hd.final_b;
-    fin.latent = latent;
-    fin.prediction = prediction;
-    fin.delta = delta;
-    fin.finite_flag = finite_flag;
-    fin.error_flag = s->ctx->error_flag;
-    ERNIE_LAUNCH(session_gemm(s, s->a, hd.final_w, s->image, kLatent, kHidden, 128, Epilogue::FinalEuler, fin),
-                 "final linear + Euler");
+    if (img > 0)
+    {
+        ERNIE_LAUNCH(launch_norm_modulate(s->x, img, kHidden, nullptr, s->ss, s->ss + kHidden, 1e-6f, 1, s->a, fp32, st),
+                     "final norm");
+        GemmEpilogueArgs fin;
+        fin.bias = hd.final_b;
+        fin.latent = latent;
+        fin.ld_latent = s->latent_ld;
+        fin.prediction = prediction;
+        fin.delta = delta;
+        fin.finite_flag = finite_flag;
+        fin.error_flag = s->ctx->error_flag;
+        ERNIE_LAUNCH(session_gemm(s, s->a, hd.final_w, img, kLatent, kHidden, 128, Epilogue::FinalEuler, fin),
+                     "final linear + Euler");
+    }
     return ERNIE_CUDA_OK;
 }
 
@@ -1015,7 +1211,8 @@ static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, b
         s->flags = nullptr;
         s->feature_capacity = 0;
         ERNIE_CUDA(cudaMalloc(&s->features, size_t(steps) * kHidden * 4), "Allocate time features");
-        ERNIE_CUDA(cudaMalloc(&s->flags, size_t(steps) * sizeof(int)), "Allocate finite flags");
+        // sequence parallel: every rank's flags are gathered behind this session's own
+        ERNIE_CUDA(cudaMalloc(&s->flags, size_t(steps) * (1 + s->sp_world) * sizeof(int)), "Allocate finite flags");
         s->feature_capacity = steps;
         s->feature_key = {-1, -1};
         release_graphs(s);
@@ -1025,7 +1222,7 @@ static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, b
         if (s->preds) cudaFree(s->preds);
         s->preds = nullptr;
         s->pred_capacity = 0;
-        ERNIE_CUDA(cudaMalloc(&s->preds, size_t(steps) * kLatent * s->image * 4), "Allocate predictions");
+        ERNIE_CUDA(cudaMalloc(&s->preds, size_t(steps) * kLatent * s->latent_ld * 4), "Allocate predictions");
         s->pred_capacity = steps;
         release_graphs(s);
     }
@@ -1051,59 +1248,93 @@ static int enqueue_range(ernie_cuda_session *s, int start, int end, bool predict
     ERNIE_CUDA(cudaMemsetAsync(s->flags + start, 0, size_t(end - start) * sizeof(int), st), "clear finite flags");
     for (int i = start; i < end; ++i)
     {
-        float *pred = predictions ? s->preds + size_t(i) * kLatent * s->image : nullptr;
+        float *pred = predictions ? s->preds + size_t(i) * kLatent * s->latent_ld : nullptr;
         ERNIE_TRY(enqueue_step(s, s->latent, s->features + size_t(i) * kHidden, s->deltas[i], pred, s->flags + i));
     }
+    return ERNIE_CUDA_OK;
+}
+
+// Enqueues steps [start, end) (through a cached CUDA graph when use_graph) without waiting for them.
+static int launch_range(ernie_cuda_session *s, int steps, int start, int end, int schedule, bool use_graph,
+                        bool predictions)
+{
+    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Require four constants (set_conditioning)");
+    if (start < 0 || start > steps || end < start || end > steps)
+        return fail(ERNIE_CUDA_ERROR, "Denoising start step must be in [0,steps]");
+    ERNIE_TRY(ensure_step_buffers(s, steps, schedule, predictions));
+    if (end == start) return ERNIE_CUDA_OK;
+    cudaStream_t st = s->ctx->stream;
+    if (!use_graph) return enqueue_range(s, start, end, predictions);
+    const auto key = std::make_tuple(steps, start, end, schedule, predictions ? 1 : 0);
+    auto it = s->graphs.find(key);
+    if (it == s->graphs.end())
+    {
+        ERNIE_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "Begin graph capture");
+        const int rc = enqueue_range(s, start, end, predictions);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t end_e = cudaStreamEndCapture(st, &graph);
+        if (rc != ERNIE_CUDA_OK)
+        {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        ERNIE_CUDA(end_e, "End graph capture");
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        ERNIE_CUDA(inst, "Instantiate graph");
+        it = s->graphs.emplace(key, exec).first;
+    }
+    ERNIE_CUDA(cudaGraphLaunch(it->second, st), "Launch graph");
+    return ERNIE_CUDA_OK;
+}
+
+// Waits for the enqueued steps and reports the first one whose latent went non-finite. `flags` holds
+// `sources` rows of (end - start) device flags (one row per sequence-parallel rank).
+static int finish_range(ernie_cuda_session *s, int start, int end, const int *flags_dev, int sources, int *failed_step)
+{
+    const int n = end - start;
+    std::vector<int> flags(size_t(n) * sources);
+    if (n > 0)
+        ERNIE_CUDA(cudaMemcpyAsync(flags.data(), flags_dev, flags.size() * sizeof(int), cudaMemcpyDeviceToHost,
+                                   s->ctx->stream),
+                   "read finite flags");
+    ERNIE_TRY(ernie_cuda_context_synchronize(s->ctx));
+    for (int i = 0; i < n; ++i)
+        for (int r = 0; r < sources; ++r)
+            if (flags[size_t(r) * n + i])
+            {
+                if (failed_step) *failed_step = start + i + 1;
+                return fail(ERNIE_CUDA_ERROR, "Non-finite latent after denoise step " + std::to_string(start + i + 1));
+            }
     return ERNIE_CUDA_OK;
 }
 
 static int run_range(ernie_cuda_session *s, int steps, int start, int end, int schedule, bool use_graph,
                      bool predictions, int *failed_step)
 {
-    if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Require four constants (set_conditioning)");
-    if (start < 0 || start > steps || end < start || end > steps)
-        return fail(ERNIE_CUDA_ERROR, "Denoising start step must be in [0,steps]");
-    ERNIE_TRY(ensure_step_buffers(s, steps, schedule, predictions));
     if (failed_step) *failed_step = 0;
-    if (end == start) return ERNIE_CUDA_OK;
+    ERNIE_TRY(launch_range(s, steps, start, end, schedule, use_graph, predictions));
+    return finish_range(s, start, end, s->flags + start, 1, failed_step);
+}
+
+// Sequence parallel: after the steps, every rank gathers all ranks' latent slices ([P][128][S]) and finite
+// flags, whatever happened locally, so that the ranks' collectives stay in step.
+static int run_range_sp(ernie_cuda_session *s, int steps, int start, int end, int schedule, bool gather_latent,
+                        int *failed_step)
+{
+    if (failed_step) *failed_step = 0;
+    ERNIE_TRY(launch_range(s, steps, start, end, schedule, true, false));
     cudaStream_t st = s->ctx->stream;
-    if (use_graph)
-    {
-        const auto key = std::make_tuple(steps, start, end, schedule, predictions ? 1 : 0);
-        auto it = s->graphs.find(key);
-        if (it == s->graphs.end())
-        {
-            ERNIE_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "Begin graph capture");
-            const int rc = enqueue_range(s, start, end, predictions);
-            cudaGraph_t graph = nullptr;
-            const cudaError_t end_e = cudaStreamEndCapture(st, &graph);
-            if (rc != ERNIE_CUDA_OK)
-            {
-                if (graph) cudaGraphDestroy(graph);
-                return rc;
-            }
-            ERNIE_CUDA(end_e, "End graph capture");
-            cudaGraphExec_t exec = nullptr;
-            const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
-            cudaGraphDestroy(graph);
-            ERNIE_CUDA(inst, "Instantiate graph");
-            it = s->graphs.emplace(key, exec).first;
-        }
-        ERNIE_CUDA(cudaGraphLaunch(it->second, st), "Launch graph");
-    }
-    else
-        ERNIE_TRY(enqueue_range(s, start, end, predictions));
-    std::vector<int> flags(end - start);
-    ERNIE_CUDA(cudaMemcpyAsync(flags.data(), s->flags + start, flags.size() * sizeof(int), cudaMemcpyDeviceToHost, st),
-               "read finite flags");
-    ERNIE_TRY(ernie_cuda_context_synchronize(s->ctx));
-    for (int i = start; i < end; ++i)
-        if (flags[i - start])
-        {
-            if (failed_step) *failed_step = i + 1;
-            return fail(ERNIE_CUDA_ERROR, "Non-finite latent after denoise step " + std::to_string(i + 1));
-        }
-    return ERNIE_CUDA_OK;
+    const NcclApi &api = nccl();
+    const size_t slice = size_t(kLatent) * s->tokens;
+    int *all_flags = s->flags + s->feature_capacity;
+    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
+    if (gather_latent) api.all_gather(s->latent, s->gathered, slice, ncclFloat32, s->comm, st);
+    if (end > start) api.all_gather(s->flags + start, all_flags, size_t(end - start), ncclInt32, s->comm, st);
+    const ncclResult_t r = api.group_end();
+    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("latent all-gather: ") + api.error_string(r));
+    return finish_range(s, start, end, all_flags, s->sp_world, failed_step);
 }
 
 extern "C" int ernie_cuda_session_denoise_device(ernie_cuda_session *s, int steps, int start_step, int end_step,
@@ -1111,6 +1342,7 @@ extern "C" int ernie_cuda_session_denoise_device(ernie_cuda_session *s, int step
 {
     if (!s) return fail(ERNIE_CUDA_ERROR, "null session");
     DeviceGuard guard(s->ctx->device);
+    if (s->sp_world > 1) return run_range_sp(s, steps, start_step, end_step, schedule, false, failed_step);
     return run_range(s, steps, start_step, end_step, schedule, use_graph != 0, false, failed_step);
 }
 
@@ -1124,6 +1356,29 @@ extern "C" int ernie_cuda_session_denoise(ernie_cuda_session *s, const float *in
     for (size_t i = 0; i < count; ++i)
         if (!std::isfinite(initial[i])) return fail(ERNIE_CUDA_ERROR, "Initial latent is not finite");
     cudaStream_t st = s->ctx->stream;
+    if (s->sp_world > 1)
+    {
+        // every rank passes the whole latent, keeps its own token slice [128][S] on the device, and
+        // receives the whole result gathered over NCCL (a collective: all ranks call together)
+        if (predictions) return fail(ERNIE_CUDA_ERROR, "Predictions are not gathered in sequence-parallel mode");
+        const int S = s->tokens, P = s->sp_world, begin = s->sp_rank * S;
+        std::vector<float> slice(size_t(kLatent) * S, 0.f), gathered(size_t(P) * kLatent * S);
+        if (s->img_local > 0)
+            for (int c = 0; c < kLatent; ++c)
+                std::memcpy(slice.data() + size_t(c) * S, initial + size_t(c) * s->image + begin,
+                            size_t(s->img_local) * 4);
+        ERNIE_CUDA(cudaMemcpyAsync(s->latent, slice.data(), slice.size() * 4, cudaMemcpyHostToDevice, st), "upload slice");
+        ERNIE_TRY(run_range_sp(s, steps, start_step, end_step, schedule, true, failed_step));
+        ERNIE_CUDA(cudaMemcpy(gathered.data(), s->gathered, gathered.size() * 4, cudaMemcpyDeviceToHost), "download latent");
+        for (int p = 0; p < P; ++p)
+        {
+            const int img_p = std::max(0, std::min(S, s->image - p * S));
+            for (int c = 0; c < kLatent && img_p > 0; ++c)
+                std::memcpy(final_latent + size_t(c) * s->image + size_t(p) * S,
+                            gathered.data() + (size_t(p) * kLatent + c) * S, size_t(img_p) * 4);
+        }
+        return ERNIE_CUDA_OK;
+    }
     std::memcpy(s->pinned, initial, count * 4);
     ERNIE_CUDA(cudaMemcpyAsync(s->latent, s->pinned, count * 4, cudaMemcpyHostToDevice, st), "upload latent");
     const int rc = run_range(s, steps, start_step, end_step, schedule, true, predictions != nullptr, failed_step);
@@ -1142,6 +1397,7 @@ extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent
 {
     if (!s || !latent || !prediction) return fail(ERNIE_CUDA_ERROR, "null argument");
     if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Require six DiT inputs (set_conditioning)");
+    if (s->sp_world > 1) return fail(ERNIE_CUDA_ERROR, "run_dit takes a whole latent: use a single-GPU session");
     DeviceGuard guard(s->ctx->device);
     std::vector<float> features(kHidden);
     ERNIE_TRY(host_features(timestep, features.data()));
@@ -1193,8 +1449,16 @@ extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int
 extern "C" int ernie_cuda_session_launches_per_step(ernie_cuda_session *s, int *launches)
 {
     if (!s || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
-    // input head: latent transpose + x_embedder GEMM + 4 GEMVs; 7 per block; output head: norm + GEMM
-    *launches = 6 + 7 * s->model->num_blocks + 2;
+    // input head: latent transpose + x_embedder GEMM + 4 GEMVs; 7 per block; output head: norm + GEMM.
+    // Sequence parallel: + V transpose and head gather per block (NCCL's own kernels not counted); a
+    // rank without image rows skips the x_embedder and output head, one without real rows all but attention.
+    if (s->sp_world > 1)
+    {
+        const int per_block = s->real_local > 0 ? 9 : 3;
+        *launches = 4 + per_block * s->model->num_blocks + (s->img_local > 0 ? 4 : 0);
+    }
+    else
+        *launches = 6 + 7 * s->model->num_blocks + 2;
     return ERNIE_CUDA_OK;
 }
 

@@ -17,7 +17,7 @@
 // Issue order S_0, S_1, PV_0, S_2, PV_1, S_3, ... lets S_{j+1} run while softmax works on S_j,
 // and the two P buffers let softmax j+1 write while PV_j is still executing.
 // V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so both MMAs use
-// K-major operands. All mbarrier waits are bounded. No TMA multicast.
+// K-major operands. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
 #include "kernels.h"
 #include "ptx.cuh"
 #include <cudaTypedefs.h>

@@ -339,7 +339,7 @@ __device__ __forceinline__ void epi_final_euler(const EpiCtx &e, const GemmEpilo
         {
             const int ch = c + j;
             const float prediction = v[j] + __ldg(a.bias + ch);
-            const size_t idx = static_cast<size_t>(ch) * e.m + row;
+            const size_t idx = static_cast<size_t>(ch) * (a.ld_latent > 0 ? a.ld_latent : e.m) + row;
             // euler_step: change = delta * v; out = x + change, two roundings (no contraction)
             const float next = __fadd_rn(a.latent[idx], __fmul_rn(a.delta, prediction));
             a.latent[idx] = next;

@@ -40,7 +40,8 @@ struct GemmEpilogueArgs
     int h_split3 = 0;
     int ffn = 0;
     // FinalEuler
-    float *latent = nullptr;     // [128][rows]
+    float *latent = nullptr;     // [128][ld_latent] (ld_latent 0: rows)
+    int ld_latent = 0;
     float *prediction = nullptr; // optional [128][rows]
     float delta = 0.f;
     int *finite_flag = nullptr; // set to 1 if any updated latent value is not finite
@@ -63,7 +64,14 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
                          const float *shift, float eps, int centered, __nv_bfloat16 *out, int split3,
                          cudaStream_t stream);
 // Channel-major latent [128][tokens] -> token-major BF16 A operand [tokens][128] (or 3 planes).
-int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out, int split3, cudaStream_t stream);
+int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out, int split3, cudaStream_t stream,
+                            int ld = 0);
+// Sequence parallelism: V [heads][rows][128] -> V^T [heads][128][rows_pad] (rows_pad % 64 == 0, padding
+// columns zero); [sources][rows][width] -> [rows][sources*width].
+int launch_transpose_heads(const __nv_bfloat16 *v, int heads, int rows, int rows_pad, __nv_bfloat16 *vt,
+                           cudaStream_t stream);
+int launch_gather_heads(const __nv_bfloat16 *in, int sources, int rows, int width, __nv_bfloat16 *out,
+                        cudaStream_t stream);
 // FP32 [rows][cols] -> BF16 [rows][cols] (or 3 BF16 planes [rows][3*cols]).
 int launch_to_operand(const float *src, long long rows, int cols, __nv_bfloat16 *out, int split3, cudaStream_t stream);
 // y[n] = W[n, :] . act(x) + bias[n]; act = SiLU when silu_input.

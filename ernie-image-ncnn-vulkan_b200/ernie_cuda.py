@@ -107,7 +107,23 @@ SIGNATURES = {
     "ernie_cuda_session_profile": (I, [P, I, I, ctypes.POINTER(F)]),
     "ernie_cuda_session_launches_per_step": (I, [P, ctypes.POINTER(I)]),
     "ernie_cuda_finite_latent_noalloc": (I, [P, P, I, I, ctypes.POINTER(I)]),
+    "ernie_cuda_nccl_unique_id": (I, [P]),
+    "ernie_cuda_session_create_sp": (I, [P, ctypes.POINTER(Shape), I, P, I, I, ctypes.POINTER(P)]),
+    "ernie_cuda_sp_layout": (I, [I, I, I, I] + [ctypes.POINTER(I)] * 5),
 }
+
+
+def sp_layout(tokens, image, world, rank):
+    """(shard rows, gathered rows, image rows, real rows, first text slot) of a sequence-parallel rank."""
+    out = [I(0) for _ in range(5)]
+    check(lib().ernie_cuda_sp_layout(tokens, image, world, rank, *[ctypes.byref(o) for o in out]))
+    return tuple(o.value for o in out)
+
+
+def nccl_unique_id():
+    buf = ctypes.create_string_buffer(128)
+    check(lib().ernie_cuda_nccl_unique_id(buf))
+    return buf.raw
 
 
 def declared_functions():
@@ -403,12 +419,19 @@ class Model:
 
 
 class Session:
-    """One request shape and precision (activations sized once, CUDA graphs cached)."""
+    """One request shape and precision (activations sized once, CUDA graphs cached). With `sp=(id, rank,
+    world)` the session is one rank of a Ulysses sequence-parallel group."""
 
-    def __init__(self, model, width, height, text_tokens, valid_text, precision=BF16):
+    def __init__(self, model, width, height, text_tokens, valid_text, precision=BF16, sp=None):
         shape = Shape(width, height, text_tokens, valid_text)
         h = P()
-        check(lib().ernie_cuda_session_create(model.handle, ctypes.byref(shape), precision, ctypes.byref(h)))
+        if sp is None:
+            check(lib().ernie_cuda_session_create(model.handle, ctypes.byref(shape), precision, ctypes.byref(h)))
+        else:
+            nccl_id, rank, world = sp
+            buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            check(lib().ernie_cuda_session_create_sp(model.handle, ctypes.byref(shape), precision, buf, rank, world,
+                                                     ctypes.byref(h)))
         self.handle, self.model, self.ctx = h, model, model.ctx
         self.width, self.height, self.text_tokens, self.valid_text = width, height, text_tokens, valid_text
         self.tokens = width * height + text_tokens

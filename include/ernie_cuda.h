@@ -191,6 +191,21 @@ int ernie_cuda_session_denoise_device(ernie_cuda_session *session, int steps, in
 int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial, float *final_latent, int steps,
                                int start_step, int end_step, int schedule, float *predictions, int *failed_step);
 
+/* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 ranks, BF16) ---------------
+   Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every rank
+   holds the full weights. Per block, an NCCL all-to-all swaps heads and tokens around attention
+   (each rank attends with 32/world heads over the whole sequence) and a second one returns the
+   attention output. Each rank keeps its own token slice of the latent across steps; the denoise call
+   takes and returns whole latents (gathered at the end). All ranks must make the same calls in the
+   same order. NCCL is loaded at run time (libnccl.so.2). */
+int ernie_cuda_nccl_unique_id(void *id128);
+int ernie_cuda_session_create_sp(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
+                                 const void *nccl_id128, int rank, int world, ernie_cuda_session **out);
+/* Layout of rank `rank`: shard rows S, gathered rows (world*S rounded up to 128), this rank's image rows,
+   real rows, and the first text slot it owns. Host-only. */
+int ernie_cuda_sp_layout(int tokens, int image_tokens, int world, int rank, int *shard, int *full_rows,
+                         int *image_rows, int *real_rows, int *text_begin);
+
 /* Non-finite check that allocates no device memory. It has no counterpart in the reference.
    Callers that cannot call cudaMalloc when they need the check (a stream capture in progress
    elsewhere in the process, an application that forbids device allocation after start-up) use it
