@@ -228,10 +228,12 @@ def main():
     tokens = WIDTH * HEIGHT + TEXT
     n_valid = WIDTH * HEIGHT + VALID
     if sp:
-        # one request over all ranks: rank 0's NCCL id reaches the others through the process group
-        ids = [ec.nccl_unique_id() if rank == 0 else None]
-        pg.broadcast_object_list(ids, src=0)
-        session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision, sp=(ids[0], rank, world))
+        # one request over all ranks; the members' memory handles travel through the process group
+        def exchange(handle):
+            handles = [None] * world
+            pg.all_gather_object(handles, handle)
+            return handles
+        session = ec.Session(model, WIDTH, HEIGHT, TEXT, VALID, precision, sp=(rank, world, exchange))
         shard, _, img_rows, local_rows, _ = ec.sp_layout(tokens, WIDTH * HEIGHT, world, rank)
         seed = dp.request_seed(1000, 0)
     else:

@@ -4,7 +4,6 @@
 #include "ernie_cuda.h"
 #include "ernie_synth.h"
 #include "kernels.h"
-#include "nccl_dyn.h"
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -198,11 +197,52 @@ struct ernie_cuda_session
     int img_local = 0, real_local = 0, text_begin = 0, latent_ld = 0;
     // Ulysses sequence parallelism (world 1 = one GPU): this rank owns tokens [rank*S, rank*S + S).
     int sp_world = 1, sp_rank = 0, full_tokens = 0, shard = 0, full_rows = 0, heads_local = kHeads;
-    ncclComm_t comm = nullptr;
-    __nv_bfloat16 *q_full = nullptr, *k_full = nullptr, *v_full = nullptr, *vt_full = nullptr, *o_full = nullptr,
-                  *o_recv = nullptr, *text_op = nullptr;
+    bool connected = false;
+    // Peer-visible arena (CUDA IPC; the same layout on every member): Q, K and V^T of this GPU's heads
+    // for the whole sequence, the out-projection operand `a` (attention rows of this GPU's tokens),
+    // every member's latent slice and step flags, barrier slots. peer[p] = member p's arena as mapped
+    // into this process (peer[rank] = this GPU's own).
+    void *shared = nullptr;
+    char *peer[kMaxDest] = {};
+    __nv_bfloat16 *q_full = nullptr, *k_full = nullptr, *vt_full = nullptr, *text_op = nullptr;
     float *text_stage = nullptr, *gathered = nullptr;
+    int *flags_all = nullptr;
+    unsigned *slots = nullptr, *epoch = nullptr;
 };
+
+namespace
+{
+constexpr int kMaxSteps = 1000;
+constexpr long long kPeerTimeoutNs = 20000000000LL; // a member more than 20 s behind counts as lost
+
+// The address of `local` (inside this GPU's peer-visible arena) in member p's arena.
+template <class T> T *peer_ptr(const ernie_cuda_session *s, int p, T *local)
+{
+    return reinterpret_cast<T *>(s->peer[p] + (reinterpret_cast<char *>(local) - static_cast<char *>(s->shared)));
+}
+
+int sp_barrier(ernie_cuda_session *s)
+{
+    PeerBarrier b;
+    b.slots = s->slots;
+    for (int p = 0; p < s->sp_world; ++p) b.peer_slots[p] = peer_ptr(s, p, s->slots);
+    b.epoch = s->epoch;
+    b.rank = s->sp_rank;
+    b.world = s->sp_world;
+    b.timeout_ns = kPeerTimeoutNs;
+    b.error_flag = s->ctx->error_flag;
+    return from_launch(launch_peer_barrier(b, s->ctx->stream), "peer barrier");
+}
+
+// Stores `bytes` of this GPU's `src` at `dst_local`'s place in every member's arena.
+template <class T> int sp_put(ernie_cuda_session *s, const T *src, T *dst_local, size_t bytes)
+{
+    PeerPut put;
+    put.members = s->sp_world;
+    for (int p = 0; p < s->sp_world; ++p) put.dst[p] = peer_ptr(s, p, dst_local);
+    return from_launch(launch_peer_put(src, bytes, put, s->ctx->stream), "peer put");
+}
+} // namespace
 
 // ------------------------------------------------------------------------------------------------
 extern "C" const char *ernie_cuda_last_error(void) { return g_last_error.c_str(); }
@@ -756,7 +796,7 @@ static void sp_geometry(int tokens, int image, int world, int rank, int *shard, 
 }
 
 static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision, int world, int rank,
-                          const void *nccl_id, ernie_cuda_session **out)
+                          ernie_cuda_session **out)
 {
     if (!model || !shape || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
     *out = nullptr;
@@ -767,8 +807,8 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
     if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
         return fail(ERNIE_CUDA_ERROR, "Unknown precision");
     if (world > 1 && (precision != ERNIE_PRECISION_BF16 || (world != 2 && world != 4 && world != 8) || rank < 0 ||
-                      rank >= world || !nccl_id))
-        return fail(ERNIE_CUDA_ERROR, "Sequence parallelism needs BF16, 2, 4 or 8 ranks and an NCCL id");
+                      rank >= world))
+        return fail(ERNIE_CUDA_ERROR, "Sequence parallelism needs BF16 and 2, 4 or 8 ranks");
     ernie_cuda_context *ctx = model->ctx;
     DeviceGuard guard(ctx->device);
     auto *s = new ernie_cuda_session();
@@ -817,50 +857,44 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
     arena.add(&s->c, kHidden);
     arena.add(&s->mod, 6 * kHidden);
     arena.add(&s->ss, 2 * kHidden);
-    arena.add(&s->a, T * kHidden * s->splits);
+    if (world == 1) arena.add(&s->a, T * kHidden * s->splits);
     arena.add(&s->h, T * kFfn * s->splits);
-    arena.add(reinterpret_cast<char **>(&s->q), size_t(kHeads) * P * kHeadDim * qkv_elem);
-    arena.add(reinterpret_cast<char **>(&s->k), size_t(kHeads) * P * kHeadDim * qkv_elem);
-    arena.add(reinterpret_cast<char **>(&s->v), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    if (world == 1) // sequence parallel: Q, K, V^T land in the peer-visible arena below
+    {
+        arena.add(reinterpret_cast<char **>(&s->q), size_t(kHeads) * P * kHeadDim * qkv_elem);
+        arena.add(reinterpret_cast<char **>(&s->k), size_t(kHeads) * P * kHeadDim * qkv_elem);
+        arena.add(reinterpret_cast<char **>(&s->v), size_t(kHeads) * P * kHeadDim * qkv_elem);
+    }
+    Arena shared;
     if (world > 1)
     {
         const size_t F = s->full_rows, hl = s->heads_local;
-        arena.add(&s->q_full, hl * F * kHeadDim);
-        arena.add(&s->k_full, hl * F * kHeadDim);
-        arena.add(&s->v_full, hl * F * kHeadDim);
-        arena.add(&s->vt_full, hl * F * kHeadDim);
-        arena.add(&s->o_full, F * hl * kHeadDim);
-        arena.add(&s->o_recv, size_t(world) * T * hl * kHeadDim);
         arena.add(&s->text_op, size_t(s->text) * kTextDim);
         arena.add(&s->text_stage, size_t(s->text) * kTextDim);
-        arena.add(&s->gathered, size_t(world) * L);
+        arena.add(&s->epoch, 1);
+        shared.add(&s->q_full, hl * F * kHeadDim);
+        shared.add(&s->k_full, hl * F * kHeadDim);
+        shared.add(&s->vt_full, hl * kHeadDim * F);
+        shared.add(&s->a, T * kHidden);
+        shared.add(&s->gathered, size_t(world) * L);
+        shared.add(&s->flags_all, size_t(world) * kMaxSteps);
+        shared.add(&s->slots, kMaxDest);
     }
     cudaError_t e = arena.allocate();
     s->alloc = arena.base;
     if (e == cudaSuccess) e = cudaMemset(arena.base, 0, arena.bytes());
+    if (e == cudaSuccess && world > 1)
+    {
+        e = shared.allocate();
+        s->shared = shared.base;
+        s->peer[rank] = static_cast<char *>(shared.base);
+        if (e == cudaSuccess) e = cudaMemset(shared.base, 0, shared.bytes());
+    }
     if (e == cudaSuccess) e = cudaMallocHost(&s->pinned, sizeof(float) * kLatent * s->image);
     if (e != cudaSuccess)
     {
         ernie_cuda_session_destroy(s);
         return from_cuda(e, "Allocate session activations");
-    }
-    if (world > 1)
-    {
-        const NcclApi &api = nccl();
-        if (!api.ok)
-        {
-            ernie_cuda_session_destroy(s);
-            return fail(ERNIE_CUDA_ERROR, "libnccl.so.2 not found: sequence parallelism needs NCCL");
-        }
-        ncclUniqueId id;
-        std::memcpy(&id, nccl_id, sizeof(id));
-        const ncclResult_t r = api.comm_init_rank(&s->comm, world, id, rank);
-        if (r != ncclSuccess)
-        {
-            s->comm = nullptr;
-            ernie_cuda_session_destroy(s);
-            return fail(ERNIE_CUDA_ERROR, std::string("ncclCommInitRank: ") + api.error_string(r));
-        }
     }
     *out = s;
     return ERNIE_CUDA_OK;
@@ -869,25 +903,56 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
 extern "C" int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
                                          ernie_cuda_session **out)
 {
-    return create_session(model, shape, precision, 1, 0, nullptr, out);
-}
-
-extern "C" int ernie_cuda_nccl_unique_id(void *id)
-{
-    if (!id) return fail(ERNIE_CUDA_ERROR, "null argument");
-    const NcclApi &api = nccl();
-    if (!api.ok) return fail(ERNIE_CUDA_ERROR, "libnccl.so.2 not found");
-    ncclUniqueId uid;
-    const ncclResult_t r = api.get_unique_id(&uid);
-    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("ncclGetUniqueId: ") + api.error_string(r));
-    std::memcpy(id, &uid, sizeof(uid));
-    return ERNIE_CUDA_OK;
+    return create_session(model, shape, precision, 1, 0, out);
 }
 
 extern "C" int ernie_cuda_session_create_sp(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
-                                            const void *nccl_id, int rank, int world, ernie_cuda_session **out)
+                                            int rank, int world, ernie_cuda_session **out)
 {
-    return create_session(model, shape, precision, world, rank, nccl_id, out);
+    return create_session(model, shape, precision, world, rank, out);
+}
+
+extern "C" int ernie_cuda_sp_handle(ernie_cuda_session *s, void *handle)
+{
+    if (!s || !handle) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (s->sp_world < 2) return fail(ERNIE_CUDA_ERROR, "Not a sequence-parallel session");
+    DeviceGuard guard(s->ctx->device);
+    cudaIpcMemHandle_t h;
+    ERNIE_CUDA(cudaIpcGetMemHandle(&h, s->shared), "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == ERNIE_CUDA_SP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_sp_connect(ernie_cuda_session *s, const void *handles)
+{
+    if (!s || !handles) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (s->sp_world < 2) return fail(ERNIE_CUDA_ERROR, "Not a sequence-parallel session");
+    if (s->connected) return fail(ERNIE_CUDA_ERROR, "Session already connected");
+    DeviceGuard guard(s->ctx->device);
+    for (int p = 0; p < s->sp_world; ++p)
+    {
+        if (p == s->sp_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char *>(handles) + size_t(p) * sizeof(h), sizeof(h));
+        void *mapped = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&mapped, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+        {
+            for (int q = 0; q < p; ++q)
+                if (q != s->sp_rank && s->peer[q])
+                {
+                    cudaIpcCloseMemHandle(s->peer[q]);
+                    s->peer[q] = nullptr;
+                }
+            return from_cuda(e, "Map a member's memory (cudaIpcOpenMemHandle)");
+        }
+        s->peer[p] = static_cast<char *>(mapped);
+    }
+    s->connected = true;
+    // every member mapped every other: the first barrier proves the group is complete
+    ERNIE_TRY(sp_barrier(s));
+    return ernie_cuda_context_synchronize(s->ctx);
 }
 
 extern "C" int ernie_cuda_sp_layout(int tokens, int image, int world, int rank, int *shard, int *full_rows,
@@ -911,8 +976,15 @@ extern "C" int ernie_cuda_session_destroy(ernie_cuda_session *s)
     if (!s) return ERNIE_CUDA_OK;
     DeviceGuard guard(s->ctx->device);
     cudaStreamSynchronize(s->ctx->stream);
-    release_graphs(s); // graphs that hold NCCL calls go before the communicator
-    if (s->comm) nccl().comm_destroy(s->comm);
+    release_graphs(s);
+    if (s->connected)
+    {
+        // members leave together (bounded barrier), so no member still stores into this GPU's arena
+        if (sp_barrier(s) == ERNIE_CUDA_OK) ernie_cuda_context_synchronize(s->ctx);
+        for (int p = 0; p < s->sp_world; ++p)
+            if (p != s->sp_rank && s->peer[p]) cudaIpcCloseMemHandle(s->peer[p]);
+    }
+    if (s->shared) cudaFree(s->shared);
     if (s->alloc) cudaFree(s->alloc);
     if (s->features) cudaFree(s->features);
     if (s->flags) cudaFree(s->flags);
@@ -1003,49 +1075,6 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
     return ERNIE_CUDA_OK;
 }
 
-// Ulysses all-to-all #1: this rank's Q, K, V rows of all 32 heads ([32][S][128] each) go out as
-// per-head blocks; the rank receives every rank's rows of its own 32/P heads into [heads_local][F][128].
-static int exchange_qkv(ernie_cuda_session *s)
-{
-    const NcclApi &api = nccl();
-    cudaStream_t st = s->ctx->stream;
-    const int P = s->sp_world, hl = s->heads_local, S = s->tokens;
-    const size_t block = size_t(S) * kHeadDim;
-    const __nv_bfloat16 *send[3] = {static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
-                                    static_cast<const __nv_bfloat16 *>(s->v)};
-    __nv_bfloat16 *recv[3] = {s->q_full, s->k_full, s->v_full};
-    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
-    for (int t = 0; t < 3; ++t)
-        for (int peer = 0; peer < P; ++peer)
-            for (int h = 0; h < hl; ++h)
-            {
-                api.send(send[t] + (size_t(peer) * hl + h) * block, block, ncclBfloat16, peer, s->comm, st);
-                api.recv(recv[t] + (size_t(h) * s->full_rows + size_t(peer) * S) * kHeadDim, block, ncclBfloat16, peer,
-                         s->comm, st);
-            }
-    const ncclResult_t r = api.group_end();
-    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("Q/K/V all-to-all: ") + api.error_string(r));
-    return ERNIE_CUDA_OK;
-}
-
-// Ulysses all-to-all #2: attention rows of rank p's tokens (all of this rank's heads) go back to p.
-static int exchange_o(ernie_cuda_session *s)
-{
-    const NcclApi &api = nccl();
-    cudaStream_t st = s->ctx->stream;
-    const int P = s->sp_world, S = s->tokens;
-    const size_t block = size_t(S) * s->heads_local * kHeadDim;
-    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
-    for (int peer = 0; peer < P; ++peer)
-    {
-        api.send(s->o_full + size_t(peer) * block, block, ncclBfloat16, peer, s->comm, st);
-        api.recv(s->o_recv + size_t(peer) * block, block, ncclBfloat16, peer, s->comm, st);
-    }
-    const ncclResult_t r = api.group_end();
-    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("attention all-to-all: ") + api.error_string(r));
-    return ERNIE_CUDA_OK;
-}
-
 // One DiT block on x [tokens][4096] (block.ncnn.param:14-76), 7 launches.
 // `only` >= 0 enqueues just that part (0 norm sa, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 norm mlp,
 // 5 up/gate GEMM, 6 down GEMM); used by the benchmark's per-kernel timing.
@@ -1065,12 +1094,30 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     if (on(0))
         ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_sa, scale_sa, shift_sa, 1e-6f, 0, s->a, fp32, st), "norm sa");
     GemmEpilogueArgs qkv;
-    qkv.q = s->q;
-    qkv.k = s->k;
-    qkv.v = s->v;
-    qkv.rows_pad = seq_parallel ? s->tokens : s->rows_pad; // SP: [32][S][128] all-to-all send blocks
+    if (seq_parallel)
+    {
+        // Ulysses, fused into the GEMM epilogue: head h of this GPU's rows goes straight into member
+        // h / (32/P)'s gathered Q, K, V^T at rows rank*S + r (peer stores over NVLink)
+        for (int p = 0; p < s->sp_world; ++p)
+        {
+            qkv.q[p] = peer_ptr(s, p, s->q_full);
+            qkv.k[p] = peer_ptr(s, p, s->k_full);
+            qkv.v[p] = peer_ptr(s, p, s->vt_full);
+        }
+        qkv.heads_per_dest = s->heads_local;
+        qkv.row_offset = s->sp_rank * s->tokens;
+        qkv.row_limit = s->tokens;
+        qkv.rows_pad = s->full_rows;
+    }
+    else
+    {
+        qkv.q[0] = s->q;
+        qkv.k[0] = s->k;
+        qkv.v[0] = s->v;
+        qkv.rows_pad = s->rows_pad;
+    }
     qkv.qkv_fp32 = fp32;
-    qkv.v_transposed = !fp32 && !seq_parallel;
+    qkv.v_transposed = !fp32;
     qkv.gamma_q = w.gamma_q;
     qkv.gamma_k = w.gamma_k;
     qkv.cos_t = s->cos_t;
@@ -1080,16 +1127,19 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     if (!on(2)) {}
     else if (seq_parallel)
     {
+        // every member's heads have arrived -> attention of this GPU's heads over the whole sequence,
+        // each output row stored into its owner's out-projection operand -> every row has arrived
         const int rows = s->sp_world * s->tokens; // the gathered sequence, padding rows at the end
-        ERNIE_TRY(exchange_qkv(s));
-        ERNIE_LAUNCH(launch_transpose_heads(s->v_full, s->heads_local, s->full_rows, s->full_rows, s->vt_full, st),
-                     "transpose V");
+        FlashOutput o;
+        for (int p = 0; p < s->sp_world; ++p) o.dst[p] = peer_ptr(s, p, s->a);
+        o.rows_per_dest = s->tokens;
+        o.ld = kHidden;
+        o.col_offset = s->sp_rank * s->heads_local * kHeadDim;
+        ERNIE_TRY(sp_barrier(s));
         ERNIE_LAUNCH(launch_flash_tc(s->q_full, s->k_full, s->vt_full, s->use_mask ? s->mask : nullptr, rows,
-                                     s->full_rows, s->kv_len, s->heads_local, s->o_full, s->ctx->error_flag, st),
+                                     s->full_rows, s->kv_len, s->heads_local, o, s->ctx->error_flag, st),
                      "attention");
-        ERNIE_TRY(exchange_o(s));
-        ERNIE_LAUNCH(launch_gather_heads(s->o_recv, s->sp_world, s->tokens, s->heads_local * kHeadDim, s->a, st),
-                     "gather heads");
+        ERNIE_TRY(sp_barrier(s));
     }
     else if (fp32)
     {
@@ -1211,8 +1261,7 @@ static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, b
         s->flags = nullptr;
         s->feature_capacity = 0;
         ERNIE_CUDA(cudaMalloc(&s->features, size_t(steps) * kHidden * 4), "Allocate time features");
-        // sequence parallel: every rank's flags are gathered behind this session's own
-        ERNIE_CUDA(cudaMalloc(&s->flags, size_t(steps) * (1 + s->sp_world) * sizeof(int)), "Allocate finite flags");
+        ERNIE_CUDA(cudaMalloc(&s->flags, size_t(steps) * sizeof(int)), "Allocate finite flags");
         s->feature_capacity = steps;
         s->feature_key = {-1, -1};
         release_graphs(s);
@@ -1318,23 +1367,37 @@ static int run_range(ernie_cuda_session *s, int steps, int start, int end, int s
     return finish_range(s, start, end, s->flags + start, 1, failed_step);
 }
 
-// Sequence parallel: after the steps, every rank gathers all ranks' latent slices ([P][128][S]) and finite
-// flags, whatever happened locally, so that the ranks' collectives stay in step.
+// Sequence parallel: after the steps, every member stores its step flags (and latent slice) into every
+// member's arena and meets the others at a barrier, whatever happened locally, so the members stay in
+// step; then each reports the first non-finite step of any member.
 static int run_range_sp(ernie_cuda_session *s, int steps, int start, int end, int schedule, bool gather_latent,
                         int *failed_step)
 {
     if (failed_step) *failed_step = 0;
+    if (!s->connected) return fail(ERNIE_CUDA_ERROR, "Sequence-parallel session is not connected (sp_connect)");
     ERNIE_TRY(launch_range(s, steps, start, end, schedule, true, false));
-    cudaStream_t st = s->ctx->stream;
-    const NcclApi &api = nccl();
-    const size_t slice = size_t(kLatent) * s->tokens;
-    int *all_flags = s->flags + s->feature_capacity;
-    if (api.group_start() != ncclSuccess) return fail(ERNIE_CUDA_ERROR, "ncclGroupStart");
-    if (gather_latent) api.all_gather(s->latent, s->gathered, slice, ncclFloat32, s->comm, st);
-    if (end > start) api.all_gather(s->flags + start, all_flags, size_t(end - start), ncclInt32, s->comm, st);
-    const ncclResult_t r = api.group_end();
-    if (r != ncclSuccess) return fail(ERNIE_CUDA_ERROR, std::string("latent all-gather: ") + api.error_string(r));
-    return finish_range(s, start, end, all_flags, s->sp_world, failed_step);
+    const int n = end - start;
+    int *mine = s->flags_all + size_t(s->sp_rank) * kMaxSteps;
+    if (gather_latent)
+        ERNIE_TRY(sp_put(s, s->latent, s->gathered + size_t(s->sp_rank) * kLatent * s->tokens,
+                         size_t(kLatent) * s->tokens * sizeof(float)));
+    if (n > 0) ERNIE_TRY(sp_put(s, s->flags + start, mine, size_t(n) * sizeof(int)));
+    ERNIE_TRY(sp_barrier(s));
+    // rows of flags_all are kMaxSteps apart: read the first n of each member's row
+    std::vector<int> flags(size_t(s->sp_world) * n);
+    for (int p = 0; p < s->sp_world && n > 0; ++p)
+        ERNIE_CUDA(cudaMemcpyAsync(flags.data() + size_t(p) * n, s->flags_all + size_t(p) * kMaxSteps, n * sizeof(int),
+                                   cudaMemcpyDeviceToHost, s->ctx->stream),
+                   "read finite flags");
+    ERNIE_TRY(ernie_cuda_context_synchronize(s->ctx));
+    for (int i = 0; i < n; ++i)
+        for (int p = 0; p < s->sp_world; ++p)
+            if (flags[size_t(p) * n + i])
+            {
+                if (failed_step) *failed_step = start + i + 1;
+                return fail(ERNIE_CUDA_ERROR, "Non-finite latent after denoise step " + std::to_string(start + i + 1));
+            }
+    return ERNIE_CUDA_OK;
 }
 
 extern "C" int ernie_cuda_session_denoise_device(ernie_cuda_session *s, int steps, int start_step, int end_step,
@@ -1358,8 +1421,8 @@ extern "C" int ernie_cuda_session_denoise(ernie_cuda_session *s, const float *in
     cudaStream_t st = s->ctx->stream;
     if (s->sp_world > 1)
     {
-        // every rank passes the whole latent, keeps its own token slice [128][S] on the device, and
-        // receives the whole result gathered over NCCL (a collective: all ranks call together)
+        // every member passes the whole latent, keeps its own token slice [128][S] on the device, and
+        // receives the whole result gathered through peer memory (all members call together)
         if (predictions) return fail(ERNIE_CUDA_ERROR, "Predictions are not gathered in sequence-parallel mode");
         const int S = s->tokens, P = s->sp_world, begin = s->sp_rank * S;
         std::vector<float> slice(size_t(kLatent) * S, 0.f), gathered(size_t(P) * kLatent * S);

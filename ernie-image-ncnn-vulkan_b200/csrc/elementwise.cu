@@ -336,69 +336,6 @@ int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out,
     return cudaGetLastError();
 }
 
-// Sequence-parallel layout helpers (BF16, 16-byte vectors).
-// [heads][rows][128] -> [heads][128][rows_pad]: V of the gathered full sequence, transposed for the
-// tcgen05 attention. One CTA moves a 64-row x 128-dim tile of one head through shared memory.
-__global__ void transpose_heads_kernel(const __nv_bfloat16 *__restrict__ v, int rows, int rows_pad,
-                                       __nv_bfloat16 *__restrict__ vt)
-{
-    __shared__ __align__(16) __nv_bfloat16 tile[128][72];
-    const int head = blockIdx.y, r0 = blockIdx.x * 64;
-    const __nv_bfloat16 *src = v + static_cast<size_t>(head) * rows * kHeadDim;
-    for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x)
-    {
-        const int r = i / 16, ch = i % 16;
-        uint4 val = make_uint4(0, 0, 0, 0);
-        if (r0 + r < rows) val = *reinterpret_cast<const uint4 *>(src + static_cast<size_t>(r0 + r) * kHeadDim + ch * 8);
-        const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&val);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) tile[ch * 8 + t][r] = e[t];
-    }
-    __syncthreads();
-    __nv_bfloat16 *dst = vt + static_cast<size_t>(head) * kHeadDim * rows_pad;
-    for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x)
-    {
-        const int d = i / 8, part = i % 8;
-        if (r0 + part * 8 < rows_pad)
-            *reinterpret_cast<uint4 *>(dst + static_cast<size_t>(d) * rows_pad + r0 + part * 8) =
-                *reinterpret_cast<const uint4 *>(&tile[d][part * 8]);
-    }
-}
-
-// [sources][rows][width] -> [rows][sources * width]: attention outputs of every rank's heads back
-// into token-major order for the out-projection.
-__global__ void gather_heads_kernel(const __nv_bfloat16 *__restrict__ in, int sources, int rows, int width,
-                                    __nv_bfloat16 *__restrict__ out)
-{
-    const long long vecs = static_cast<long long>(sources) * rows * (width / 8);
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < vecs;
-         i += static_cast<long long>(gridDim.x) * blockDim.x)
-    {
-        const int c8 = static_cast<int>(i % (width / 8));
-        const long long rest = i / (width / 8);
-        const int row = static_cast<int>(rest % rows), src = static_cast<int>(rest / rows);
-        *reinterpret_cast<uint4 *>(out + static_cast<size_t>(row) * sources * width + static_cast<size_t>(src) * width +
-                                   c8 * 8) = reinterpret_cast<const uint4 *>(in)[i];
-    }
-}
-
-int launch_transpose_heads(const __nv_bfloat16 *v, int heads, int rows, int rows_pad, __nv_bfloat16 *vt,
-                           cudaStream_t stream)
-{
-    if (rows < 1 || rows_pad < rows || rows_pad % 64) return cudaErrorInvalidValue;
-    transpose_heads_kernel<<<dim3(rows_pad / 64, heads), 256, 0, stream>>>(v, rows, rows_pad, vt);
-    return cudaGetLastError();
-}
-
-int launch_gather_heads(const __nv_bfloat16 *in, int sources, int rows, int width, __nv_bfloat16 *out,
-                        cudaStream_t stream)
-{
-    if (width % 8) return cudaErrorInvalidValue;
-    gather_heads_kernel<<<grid_for(static_cast<long long>(sources) * rows * (width / 8)), 256, 0, stream>>>(
-        in, sources, rows, width, out);
-    return cudaGetLastError();
-}
-
 int launch_gemv(const __nv_bfloat16 *w, const float *x, const float *bias, float *y, int n, int k, int silu_input,
                 cudaStream_t stream)
 {

@@ -45,8 +45,7 @@ struct FlashArgs
 {
     int rows, rows_pad, kv_len;
     const float *mask;
-    __nv_bfloat16 *out;
-    int ld_out;
+    FlashOutput out;
     int *error_flag;
 };
 
@@ -321,7 +320,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int row = q0 + r;
             const float inv = 1.f / l_run;
-            __nv_bfloat16 *dst = a.out + static_cast<size_t>(row) * a.ld_out + head * kTile;
+            // output row `row` belongs to destination row / rows_per_dest (its owner GPU in a
+            // sequence-parallel group; destination 0 on one GPU)
+            const int dest = row / a.out.rows_per_dest, dest_row = row - dest * a.out.rows_per_dest;
+            __nv_bfloat16 *dst_base = nullptr;
+#pragma unroll
+            for (int d = 0; d < kMaxDest; ++d)
+                if (d == dest) dst_base = a.out.dst[d];
+            __nv_bfloat16 *dst = dst_base + static_cast<size_t>(dest_row) * a.out.ld + a.out.col_offset + head * kTile;
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc)
             {
@@ -386,19 +392,34 @@ int prepare_flash_kernels()
 }
 
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
-                    int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out, int *error_flag,
+                    int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
                     cudaStream_t stream)
 {
-    if (rows < 1 || kv_len < 1 || kv_len > rows_pad || rows_pad % kTile || rows > rows_pad || heads < 1)
+    if (rows < 1 || kv_len < 1 || kv_len > rows_pad || rows_pad % kTile || rows > rows_pad || heads < 1 ||
+        out.rows_per_dest < 1 || out.ld % 8 || out.col_offset % 8 || out.col_offset + heads * kTile > out.ld)
         return cudaErrorInvalidValue;
+    for (int d = 0; d < (rows + out.rows_per_dest - 1) / out.rows_per_dest; ++d)
+        if (d >= kMaxDest || !out.dst[d]) return cudaErrorInvalidValue;
     CUtensorMap mq, mk, mv;
     if (!map_2d(&mq, q, static_cast<uint64_t>(heads) * rows_pad, kTile) ||
         !map_2d(&mk, k, static_cast<uint64_t>(heads) * rows_pad, kTile) ||
         !map_2d(&mv, vt, static_cast<uint64_t>(heads) * kTile, static_cast<uint64_t>(rows_pad)))
         return cudaErrorInvalidValue;
-    FlashArgs a{rows, rows_pad, kv_len, mask, out, heads * kTile, error_flag};
+    FlashArgs a{rows, rows_pad, kv_len, mask, out, error_flag};
     const dim3 grid((rows + kTile - 1) / kTile, heads);
     flash_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
     return cudaGetLastError();
+}
+
+int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
+                    int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out, int *error_flag,
+                    cudaStream_t stream)
+{
+    FlashOutput o;
+    o.dst[0] = out;
+    o.rows_per_dest = rows;
+    o.ld = heads * kTile;
+    o.col_offset = 0;
+    return launch_flash_tc(q, k, vt, mask, rows, rows_pad, kv_len, heads, o, error_flag, stream);
 }
 } // namespace ernie_b200

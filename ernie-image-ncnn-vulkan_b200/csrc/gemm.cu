@@ -167,11 +167,16 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
     const float4 *cs = reinterpret_cast<const float4 *>(a.cos_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
     const float4 *sn = reinterpret_cast<const float4 *>(a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
     const float4 *gamma = reinterpret_cast<const float4 *>(part == 0 ? a.gamma_q : a.gamma_k);
-    void *dst_base = part == 0 ? a.q : part == 1 ? a.k : a.v;
+    const int row_limit = a.row_limit > 0 ? a.row_limit : a.rows_pad;
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh)
     {
-        const int head = head0 + hh;
+        // destination GPU and its head index (selected with constant indices: no local copy of args)
+        const int dest = (head0 + hh) / a.heads_per_dest, head = head0 + hh - dest * a.heads_per_dest;
+        void *dst_base = nullptr;
+#pragma unroll
+        for (int d = 0; d < kMaxDest; ++d)
+            if (d == dest) dst_base = part == 0 ? a.q[d] : part == 1 ? a.k[d] : a.v[d];
         float v[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -216,9 +221,10 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
         }
         if (a.qkv_fp32)
         {
-            if (valid)
+            if (valid && row < row_limit)
             {
-                float *dst = static_cast<float *>(dst_base) + (static_cast<size_t>(head) * a.rows_pad + row) * kHeadDim;
+                float *dst = static_cast<float *>(dst_base) +
+                             (static_cast<size_t>(head) * a.rows_pad + a.row_offset + row) * kHeadDim;
 #pragma unroll
                 for (int d = 0; d < 128; d += 4) store_f32x4(dst + d, v + d);
             }
@@ -238,10 +244,13 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
 #pragma unroll
                 for (int p = 0; p < 8; ++p)
                 {
+                    // 8-row runs: row_limit and row_offset are multiples of 16, so a run is all in or all out
                     const int d = p * 8 + (e.lane >> 2), q4 = e.lane & 3;
                     const uint4 val = *reinterpret_cast<const uint4 *>(st + d * 40 + q4 * 8);
-                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * kHeadDim + half * 64 + d) * a.rows_pad +
-                                               e.row0 + q4 * 8) = val;
+                    if (e.row0 + q4 * 8 < row_limit)
+                        *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * kHeadDim + half * 64 + d) *
+                                                             a.rows_pad +
+                                                   a.row_offset + e.row0 + q4 * 8) = val;
                 }
                 __syncwarp();
             }
@@ -259,8 +268,9 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
             for (int p = 0; p < 8; ++p)
             {
                 const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
-                if (row_g < e.m)
-                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * a.rows_pad + row_g) * kHeadDim +
+                if (row_g < e.m && row_g < row_limit)
+                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * a.rows_pad + a.row_offset + row_g) *
+                                                         kHeadDim +
                                                half * 64 + j * 8) = *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
             }
             __syncwarp();
@@ -680,7 +690,16 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     if (promote && block_n != 128) return cudaErrorInvalidValue;
     if (n % block_n) return cudaErrorInvalidValue;
     if (epilogue == Epilogue::FinalEuler && (block_n != 128 || n != 128)) return cudaErrorInvalidValue;
-    if (epilogue == Epilogue::Qkv && (n != 3 * kHidden || args.rows_pad < m)) return cudaErrorInvalidValue;
+    if (epilogue == Epilogue::Qkv)
+    {
+        const int limit = args.row_limit > 0 ? args.row_limit : args.rows_pad;
+        if (n != 3 * kHidden || args.heads_per_dest < 1 || kHeads % args.heads_per_dest ||
+            kHeads / args.heads_per_dest > kMaxDest || args.row_offset < 0 || args.row_offset % 16 || limit % 16 ||
+            args.row_offset + limit > args.rows_pad || (args.row_limit == 0 && args.rows_pad < m))
+            return cudaErrorInvalidValue;
+        for (int d = 0; d < kHeads / args.heads_per_dest; ++d)
+            if (!args.q[d] || !args.k[d] || !args.v[d]) return cudaErrorInvalidValue;
+    }
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
     if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
     if (block_n == 256) return dispatch<256, false>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);

@@ -19,6 +19,9 @@ enum class Epilogue : int
     FinalEuler = 4, // pred = acc + bias; latent[c][r] = latent + delta * pred (no FMA); finite flag
 };
 
+// Destinations of the fused sequence-parallel stores (one per GPU of the group).
+constexpr int kMaxDest = 8;
+
 struct GemmEpilogueArgs
 {
     // F32Bias
@@ -28,8 +31,13 @@ struct GemmEpilogueArgs
     // ResidGate
     float *resid = nullptr;
     const float *gate = nullptr;
-    // Qkv
-    void *q = nullptr, *k = nullptr, *v = nullptr; // [heads][rows_pad][128], BF16 or FP32
+    // Qkv: head h of output row r goes to destination d = h / heads_per_dest (a GPU of a sequence-parallel
+    // group, through peer memory; destination 0 alone on one GPU) as head h % heads_per_dest, row
+    // row_offset + r, of [heads][rows_pad][128] arrays (BF16 or FP32); BF16 V^T is [heads][128][rows_pad].
+    // Rows at or past row_limit (0: rows_pad) are not written.
+    void *q[kMaxDest] = {}, *k[kMaxDest] = {}, *v[kMaxDest] = {};
+    int heads_per_dest = 32;
+    int row_offset = 0, row_limit = 0;
     int rows_pad = 0;
     int qkv_fp32 = 0;
     int v_transposed = 0; // BF16 mode: V written as [heads][128][rows_pad] for the tcgen05 attention
@@ -66,12 +74,6 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
 // Channel-major latent [128][tokens] -> token-major BF16 A operand [tokens][128] (or 3 planes).
 int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out, int split3, cudaStream_t stream,
                             int ld = 0);
-// Sequence parallelism: V [heads][rows][128] -> V^T [heads][128][rows_pad] (rows_pad % 64 == 0, padding
-// columns zero); [sources][rows][width] -> [rows][sources*width].
-int launch_transpose_heads(const __nv_bfloat16 *v, int heads, int rows, int rows_pad, __nv_bfloat16 *vt,
-                           cudaStream_t stream);
-int launch_gather_heads(const __nv_bfloat16 *in, int sources, int rows, int width, __nv_bfloat16 *out,
-                        cudaStream_t stream);
 // FP32 [rows][cols] -> BF16 [rows][cols] (or 3 BF16 planes [rows][3*cols]).
 int launch_to_operand(const float *src, long long rows, int cols, __nv_bfloat16 *out, int split3, cudaStream_t stream);
 // y[n] = W[n, :] . act(x) + bias[n]; act = SiLU when silu_input.
@@ -84,6 +86,38 @@ int launch_gemv(const __nv_bfloat16 *w, const float *x, const float *bias, float
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
                     int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out, int *error_flag,
                     cudaStream_t stream);
+// Output rows scattered over destinations: row r goes to dst[r / rows_per_dest], row r % rows_per_dest,
+// columns col_offset + head*128 of a [rows][ld] BF16 array (sequence parallel: each token row to the
+// GPU that owns it, through peer memory).
+struct FlashOutput
+{
+    __nv_bfloat16 *dst[kMaxDest] = {};
+    int rows_per_dest = 0, ld = 0, col_offset = 0;
+};
+int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
+                    int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
+                    cudaStream_t stream);
+// Barrier of a sequence-parallel group over peer memory: this GPU's arrival is stored (release, system
+// scope) into slot `rank` of every member's slots; then it waits (acquire, bounded by `timeout_ns`) until
+// every member's arrival in its own slots reaches the same epoch. Epochs count up on the device, so the
+// barrier can sit inside a CUDA graph. On timeout it sets error_flag and returns.
+struct PeerBarrier
+{
+    unsigned *slots = nullptr;              // this GPU's [world] arrival slots
+    unsigned *peer_slots[kMaxDest] = {};    // every member's slots (this GPU's own included)
+    unsigned *epoch = nullptr;              // this GPU's barrier counter
+    int rank = 0, world = 1;
+    long long timeout_ns = 0;
+    int *error_flag = nullptr;
+};
+int launch_peer_barrier(const PeerBarrier &barrier, cudaStream_t stream);
+// Stores `bytes` (a multiple of 4) of src into every destination (peer memory included).
+struct PeerPut
+{
+    void *dst[kMaxDest] = {};
+    int members = 0;
+};
+int launch_peer_put(const void *src, size_t bytes, const PeerPut &put, cudaStream_t stream);
 int prepare_flash_kernels();
 
 // FP32 attention with FP64 softmax accumulation. q [heads][q_stride rows][width] (head stride

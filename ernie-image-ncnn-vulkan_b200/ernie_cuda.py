@@ -107,8 +107,9 @@ SIGNATURES = {
     "ernie_cuda_session_profile": (I, [P, I, I, ctypes.POINTER(F)]),
     "ernie_cuda_session_launches_per_step": (I, [P, ctypes.POINTER(I)]),
     "ernie_cuda_finite_latent_noalloc": (I, [P, P, I, I, ctypes.POINTER(I)]),
-    "ernie_cuda_nccl_unique_id": (I, [P]),
-    "ernie_cuda_session_create_sp": (I, [P, ctypes.POINTER(Shape), I, P, I, I, ctypes.POINTER(P)]),
+    "ernie_cuda_session_create_sp": (I, [P, ctypes.POINTER(Shape), I, I, I, ctypes.POINTER(P)]),
+    "ernie_cuda_sp_handle": (I, [P, P]),
+    "ernie_cuda_sp_connect": (I, [P, P]),
     "ernie_cuda_sp_layout": (I, [I, I, I, I] + [ctypes.POINTER(I)] * 5),
 }
 
@@ -119,11 +120,6 @@ def sp_layout(tokens, image, world, rank):
     check(lib().ernie_cuda_sp_layout(tokens, image, world, rank, *[ctypes.byref(o) for o in out]))
     return tuple(o.value for o in out)
 
-
-def nccl_unique_id():
-    buf = ctypes.create_string_buffer(128)
-    check(lib().ernie_cuda_nccl_unique_id(buf))
-    return buf.raw
 
 
 def declared_functions():
@@ -418,9 +414,15 @@ class Model:
         return b.value
 
 
+SP_HANDLE_BYTES = 64
+
+
 class Session:
-    """One request shape and precision (activations sized once, CUDA graphs cached). With `sp=(id, rank,
-    world)` the session is one rank of a Ulysses sequence-parallel group."""
+    """One request shape and precision (activations sized once, CUDA graphs cached).
+
+    With `sp=(rank, world, exchange)` the session is one member of a Ulysses sequence-parallel group:
+    `exchange(handle_bytes)` must return every member's handle in rank order (any host channel: a
+    torch.distributed all_gather_object, files, MPI)."""
 
     def __init__(self, model, width, height, text_tokens, valid_text, precision=BF16, sp=None):
         shape = Shape(width, height, text_tokens, valid_text)
@@ -428,10 +430,20 @@ class Session:
         if sp is None:
             check(lib().ernie_cuda_session_create(model.handle, ctypes.byref(shape), precision, ctypes.byref(h)))
         else:
-            nccl_id, rank, world = sp
-            buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
-            check(lib().ernie_cuda_session_create_sp(model.handle, ctypes.byref(shape), precision, buf, rank, world,
+            rank, world, exchange = sp
+            check(lib().ernie_cuda_session_create_sp(model.handle, ctypes.byref(shape), precision, rank, world,
                                                      ctypes.byref(h)))
+            mine = ctypes.create_string_buffer(SP_HANDLE_BYTES)
+            try:
+                check(lib().ernie_cuda_sp_handle(h, mine))
+                handles = list(exchange(mine.raw))
+                if len(handles) != world or any(len(x) != SP_HANDLE_BYTES for x in handles):
+                    raise CudaError(f"exchange returned {len(handles)} handles for {world} members")
+                check(lib().ernie_cuda_sp_connect(h, ctypes.create_string_buffer(b"".join(handles),
+                                                                                 SP_HANDLE_BYTES * world)))
+            except BaseException:
+                lib().ernie_cuda_session_destroy(h)
+                raise
         self.handle, self.model, self.ctx = h, model, model.ctx
         self.width, self.height, self.text_tokens, self.valid_text = width, height, text_tokens, valid_text
         self.tokens = width * height + text_tokens

@@ -191,16 +191,21 @@ int ernie_cuda_session_denoise_device(ernie_cuda_session *session, int steps, in
 int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial, float *final_latent, int steps,
                                int start_step, int end_step, int schedule, float *predictions, int *failed_step);
 
-/* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 ranks, BF16) ---------------
-   Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every rank
-   holds the full weights. Per block, an NCCL all-to-all swaps heads and tokens around attention
-   (each rank attends with 32/world heads over the whole sequence) and a second one returns the
-   attention output. Each rank keeps its own token slice of the latent across steps; the denoise call
-   takes and returns whole latents (gathered at the end). All ranks must make the same calls in the
-   same order. NCCL is loaded at run time (libnccl.so.2). */
-int ernie_cuda_nccl_unique_id(void *id128);
-int ernie_cuda_session_create_sp(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
-                                 const void *nccl_id128, int rank, int world, ernie_cuda_session **out);
+/* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 members, BF16) ---------------
+   Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every member
+   holds the full weights. Per block, the QKV GEMM's epilogue stores each head of this GPU's rows straight
+   into the memory of the member that attends with it (32/world heads each, over the whole sequence),
+   and the attention kernel stores each output row back into the memory of the member owning that token
+   (NVLink peer stores into buffers shared through CUDA IPC), with a bounded device-side barrier after
+   each. Each member keeps its own token slice of the latent across steps; denoise takes and returns
+   whole latents. Setup: create on every member, exchange the 64-byte handles through any host channel,
+   connect with all handles in rank order. All members must then make the same calls in the same order;
+   destroying a connected session is such a call too (the members leave together). */
+#define ERNIE_CUDA_SP_HANDLE_BYTES 64
+int ernie_cuda_session_create_sp(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision, int rank,
+                                 int world, ernie_cuda_session **out);
+int ernie_cuda_sp_handle(ernie_cuda_session *session, void *handle);
+int ernie_cuda_sp_connect(ernie_cuda_session *session, const void *handles);
 /* Layout of rank `rank`: shard rows S, gathered rows (world*S rounded up to 128), this rank's image rows,
    real rows, and the first text slot it owns. Host-only. */
 int ernie_cuda_sp_layout(int tokens, int image_tokens, int world, int rank, int *shard, int *full_rows,

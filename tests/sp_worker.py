@@ -1,9 +1,9 @@
 """One rank of the sequence-parallel parity run (started by test_gpu_sp.py, one process per GPU).
 
-Rank 0 makes the NCCL id and publishes it in the file ERNIE_SP_ID_FILE (written, then renamed); every
-rank builds the same synthetic model, joins a Ulysses session with that id, and denoises the same seeded
-latent. Rank 0 then denoises the same request with a single-GPU session on its own device and writes
-both results to ERNIE_SP_OUT (.npz). All ranks load the same libnccl.so.2 (none imports torch).
+Every rank builds the same synthetic model and a Ulysses session member; the members swap their
+64-byte memory handles through files in ERNIE_SP_DIR (each written, then renamed) and denoise the same
+seeded latent. Rank 0 then denoises the same request with a single-GPU session on its own device and
+writes both results to ERNIE_SP_DIR/sp.npz.
 """
 import os
 import sys
@@ -20,18 +20,25 @@ import ernie_cuda as ec  # noqa: E402
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     w, h, text, valid, blocks, steps, end = (int(v) for v in os.environ["ERNIE_SP_CASE"].split(","))
-    id_file = os.environ["ERNIE_SP_ID_FILE"]
-    if rank == 0:
-        with open(id_file + ".tmp", "wb") as f:
-            f.write(ec.nccl_unique_id())
-        os.replace(id_file + ".tmp", id_file)
-    deadline = time.time() + 120
-    while not os.path.exists(id_file):
-        if time.time() > deadline:
-            raise SystemExit("rank 0 never published the NCCL id")
-        time.sleep(0.05)
-    with open(id_file, "rb") as f:
-        nccl_id = f.read()
+    folder = os.environ["ERNIE_SP_DIR"]
+
+    def exchange(handle):
+        mine = os.path.join(folder, f"handle{rank}")
+        with open(mine + ".tmp", "wb") as f:
+            f.write(handle)
+        os.replace(mine + ".tmp", mine)
+        handles = []
+        deadline = time.time() + 120
+        for r in range(world):
+            path = os.path.join(folder, f"handle{r}")
+            while not os.path.exists(path):
+                if time.time() > deadline:
+                    raise SystemExit(f"rank {r} never published its handle")
+                time.sleep(0.05)
+            with open(path, "rb") as f:
+                handles.append(f.read())
+        return handles
+
     ctx = ec.Context(rank)
     model = ec.Model(ctx, blocks)
     model.synthesize(11)
@@ -39,7 +46,7 @@ def main():
     latent = rng.standard_normal((128, h, w), dtype=np.float32)
     text_in = rng.standard_normal((text, 3072), dtype=np.float32)
     cos, sin, mask = ec.dit_constants(w, h, valid, text)
-    s = ec.Session(model, w, h, text, valid, ec.BF16, sp=(nccl_id, rank, world))
+    s = ec.Session(model, w, h, text, valid, ec.BF16, sp=(rank, world, exchange))
     s.set_conditioning(text_in, cos, sin, mask)
     got = s.denoise(latent, steps, 0, end)
     again = s.denoise(latent, steps, 0, end)
@@ -49,7 +56,7 @@ def main():
         single.set_conditioning(text_in, cos, sin, mask)
         ref = single.denoise(latent, steps, 0, end)
         single.close()
-        np.savez(os.environ["ERNIE_SP_OUT"], sp=got, sp_again=again, single=ref)
+        np.savez(os.path.join(folder, "sp.npz"), sp=got, sp_again=again, single=ref)
     model.close()
     ctx.close()
 

@@ -1,7 +1,8 @@
-"""Ulysses sequence parallelism on 2+ B200s: the denoised latent of a P-rank session equals the
+"""Ulysses sequence parallelism on 2+ B200s: the denoised latent of a P-member session equals the
 single-GPU session's bit for bit (shards are contiguous token ranges, so every GEMM row, attention
-tile and key order is the same as on one GPU). Shapes cover a shard holding image and text rows, a
-text-only shard and a shard with no real rows at all. Skipped with fewer than two GPUs.
+tile and key order is the same as on one GPU; the head and token exchanges are peer stores from the
+QKV GEMM and attention epilogues). Shapes cover a shard holding image and text rows, a text-only
+shard and a shard with no real rows at all. Skipped with fewer than two GPUs.
 """
 import os
 import subprocess
@@ -38,8 +39,8 @@ def test_sp_matches_single_gpu(tmp_path, case):
     out = tmp_path / "sp.npz"
     procs = []
     for rank in range(world):
-        env = dict(os.environ, RANK=str(rank), WORLD_SIZE=str(world), ERNIE_SP_ID_FILE=str(tmp_path / "nccl.id"),
-                   ERNIE_SP_CASE=",".join(map(str, case)), ERNIE_SP_OUT=str(out), NCCL_NVLS_ENABLE="0")
+        env = dict(os.environ, RANK=str(rank), WORLD_SIZE=str(world), ERNIE_SP_DIR=str(tmp_path),
+                   ERNIE_SP_CASE=",".join(map(str, case)))
         procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "sp_worker.py")], env=env,
                                       stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
     logs = []
