@@ -39,6 +39,9 @@ WIDTH, HEIGHT, TEXT, VALID = CONFIGS["c2"][:4]
 STEPS_PER_IMAGE = 8
 NUM_BLOCKS = 36
 PARAMS_PER_BLOCK = 218_103_808  # 7 GEMMs: 4*4096^2 + 3*4096*12288
+# DRAM bytes of one C2 up/gate GEMM launch from an ncu capture of the same launch shape (239.6 MB read +
+# 93.1 MB written); the algorithmic bytes are A 34 MB + W 201 MB + h 102 MB = 337 MB.
+UPGATE_TRAFFIC_C2 = 332.7e6
 
 
 def step_flops(tokens, valid_keys, blocks=NUM_BLOCKS):
@@ -337,7 +340,9 @@ def main():
                            "kernel_ms": prof},
                 "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": bf16_peak,
                              "unit": "TFLOP/s", "frac": achieved / bf16_peak, "peak_kind": peak_kind,
-                             "traffic": None},
+                             "traffic": UPGATE_TRAFFIC_C2 if args.config == "c2" else None,
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one C2 up/gate "
+                                               "launch (profiles/gemm_kernels_c2.md); algorithmic 337 MB"},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
                 "clocks": clock_info}
         print(json.dumps(line), flush=True)

@@ -156,7 +156,9 @@ template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e
 
 // The tile spans BN/128 whole 128-wide heads of one of Q, K or V (weights are [Wq; Wk; Wv]).
 // Q, K: rmsn_9 / rmsn_10 + the rotary chain, head-major [head][token][128]; V: head-major, or
-// transposed [head][dim][token] for the tcgen05 attention (BF16 mode).
+// transposed [head][dim][token] for the tcgen05 attention (BF16 mode). A head row is read from TMEM
+// twice (sum of squares, then the rotation pairs d and d+64 in two 32-pair halves), so at most 64
+// values are live per thread and nothing spills to local memory.
 template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
     const int col0 = e.n_blk * BN;
@@ -168,6 +170,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
     const float4 *sn = reinterpret_cast<const float4 *>(a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
     const float4 *gamma = reinterpret_cast<const float4 *>(part == 0 ? a.gamma_q : a.gamma_k);
     const int row_limit = a.row_limit > 0 ? a.row_limit : a.rows_pad;
+    __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage);
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh)
     {
@@ -177,69 +180,22 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
 #pragma unroll
         for (int d = 0; d < kMaxDest; ++d)
             if (d == dest) dst_base = part == 0 ? a.q[d] : part == 1 ? a.k[d] : a.v[d];
-        float v[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-        {
-            float chunk[32];
-            tmem_load_32(e.taddr + hh * 128 + c * 32, chunk);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[c * 32 + j] = chunk[j];
-        }
-        if (part < 2)
-        {
-            // x * (mean(x^2) + 1e-6)^(-1/2) * gamma over the 128-wide head
-            float squared = 0.f;
-#pragma unroll
-            for (int d = 0; d < 128; ++d) squared += v[d] * v[d];
-            const float inverse = 1.f / sqrtf(squared * (1.f / 128.f) + 1e-6f);
-#pragma unroll
-            for (int d = 0; d < 128; d += 4)
-            {
-                const float4 g = __ldg(gamma + d / 4);
-                v[d] = v[d] * inverse * g.x;
-                v[d + 1] = v[d + 1] * inverse * g.y;
-                v[d + 2] = v[d + 2] * inverse * g.z;
-                v[d + 3] = v[d + 3] * inverse * g.w;
-            }
-            // ERNIE rotary: halves rotated with the full-width, pair-duplicated angle table
-#pragma unroll
-            for (int d = 0; d < 64; d += 4)
-            {
-                const float4 c1 = __ldg(cs + d / 4), s1 = __ldg(sn + d / 4);
-                const float4 c2 = __ldg(cs + 16 + d / 4), s2 = __ldg(sn + 16 + d / 4);
-                const float c1v[4] = {c1.x, c1.y, c1.z, c1.w}, s1v[4] = {s1.x, s1.y, s1.z, s1.w};
-                const float c2v[4] = {c2.x, c2.y, c2.z, c2.w}, s2v[4] = {s2.x, s2.y, s2.z, s2.w};
-#pragma unroll
-                for (int t = 0; t < 4; ++t)
-                {
-                    const float first = v[d + t], second = v[d + t + 64];
-                    v[d + t] = first * c1v[t] - second * s1v[t];
-                    v[d + t + 64] = second * c2v[t] + first * s2v[t];
-                }
-            }
-        }
-        if (a.qkv_fp32)
-        {
-            if (valid && row < row_limit)
-            {
-                float *dst = static_cast<float *>(dst_base) +
-                             (static_cast<size_t>(head) * a.rows_pad + a.row_offset + row) * kHeadDim;
-#pragma unroll
-                for (int d = 0; d < 128; d += 4) store_f32x4(dst + d, v + d);
-            }
-            continue;
-        }
-        __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage);
-        __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
-        if (part == 2 && a.v_transposed)
+        const uint32_t tcol = e.taddr + hh * 128;
+        if (part == 2 && !a.qkv_fp32 && a.v_transposed)
         {
             // stage [64 dims][40] then write 64-byte token runs of V^T [head][dim][token]
+            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
 #pragma unroll 1
             for (int half = 0; half < 2; ++half)
             {
 #pragma unroll
-                for (int d = 0; d < 64; ++d) st[d * 40 + e.lane] = __float2bfloat16_rn(v[half * 64 + d]);
+                for (int c = 0; c < 2; ++c)
+                {
+                    float chunk[32];
+                    tmem_load_32(tcol + half * 64 + c * 32, chunk);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) st[(c * 32 + j) * 40 + e.lane] = __float2bfloat16_rn(chunk[j]);
+                }
                 __syncwarp();
 #pragma unroll
                 for (int p = 0; p < 8; ++p)
@@ -256,22 +212,82 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
             }
             continue;
         }
-        // stage [32 rows][72] then write 128-byte row segments of [head][token][128]
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half)
+        // x * (mean(x^2) + 1e-6)^(-1/2), summed in dimension order
+        float inverse = 1.f;
+        if (part < 2)
         {
+            float squared = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c)
+            {
+                float chunk[32];
+                tmem_load_32(tcol + c * 32, chunk);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<uint4 *>(st + e.lane * 72 + j * 8) = pack_bf16x8(v + half * 64 + j * 8);
+                for (int j = 0; j < 32; ++j) squared += chunk[j] * chunk[j];
+            }
+            inverse = 1.f / sqrtf(squared * (1.f / 128.f) + 1e-6f);
+        }
+        const size_t dst_row = static_cast<size_t>(head) * a.rows_pad + a.row_offset;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c)
+        {
+            // lo = dims c*32 + [0,32), hi = dims 64 + c*32 + [0,32): the rotation pairs (d, d+64)
+            float lo[32], hi[32];
+            tmem_load_32(tcol + c * 32, lo);
+            tmem_load_32(tcol + 64 + c * 32, hi);
+            if (part < 2)
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                {
+                    const int d = c * 32 + j;
+                    const float4 g1 = __ldg(gamma + d / 4), g2 = __ldg(gamma + 16 + d / 4);
+                    const float4 c1 = __ldg(cs + d / 4), s1 = __ldg(sn + d / 4);
+                    const float4 c2 = __ldg(cs + 16 + d / 4), s2 = __ldg(sn + 16 + d / 4);
+                    const float g1v[4] = {g1.x, g1.y, g1.z, g1.w}, g2v[4] = {g2.x, g2.y, g2.z, g2.w};
+                    const float c1v[4] = {c1.x, c1.y, c1.z, c1.w}, s1v[4] = {s1.x, s1.y, s1.z, s1.w};
+                    const float c2v[4] = {c2.x, c2.y, c2.z, c2.w}, s2v[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                    {
+                        // ERNIE rotary: halves rotated with the full-width, pair-duplicated angle table
+                        const float first = lo[j + t] * inverse * g1v[t], second = hi[j + t] * inverse * g2v[t];
+                        lo[j + t] = first * c1v[t] - second * s1v[t];
+                        hi[j + t] = second * c2v[t] + first * s2v[t];
+                    }
+                }
+            }
+            if (a.qkv_fp32)
+            {
+                if (valid && row < row_limit)
+                {
+                    float *dst = static_cast<float *>(dst_base) + (dst_row + row) * kHeadDim;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                    {
+                        store_f32x4(dst + c * 32 + j, lo + j);
+                        store_f32x4(dst + 64 + c * 32 + j, hi + j);
+                    }
+                }
+                continue;
+            }
+            // stage [32 rows][72]: columns 0..31 = lo, 32..63 = hi; then 64-byte row segments
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+            {
+                *reinterpret_cast<uint4 *>(st + e.lane * 72 + j * 8) = pack_bf16x8(lo + j * 8);
+                *reinterpret_cast<uint4 *>(st + e.lane * 72 + 32 + j * 8) = pack_bf16x8(hi + j * 8);
+            }
             __syncwarp();
+            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
 #pragma unroll
             for (int p = 0; p < 8; ++p)
             {
                 const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
+                const int dim = (j < 4 ? 0 : 64) + c * 32 + (j & 3) * 8;
                 if (row_g < e.m && row_g < row_limit)
-                    *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * a.rows_pad + a.row_offset + row_g) *
-                                                         kHeadDim +
-                                               half * 64 + j * 8) = *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
+                    *reinterpret_cast<uint4 *>(dst + (dst_row + row_g) * kHeadDim + dim) =
+                        *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
             }
             __syncwarp();
         }
