@@ -599,6 +599,220 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---- CTA-pair GEMM (cta_group::2) ------------------------------------------------------------
+// Same warp roles and epilogues as gemm_kernel, on 256 x BN output tiles computed by a cluster of two
+// CTAs on neighbouring SMs. CTA r of the pair loads A rows [256*i + 128*r, +128) and B rows
+// [BN*j + (BN/2)*r, +BN/2) into its own shared memory; the even CTA's single MMA thread issues
+// M=256 tcgen05.mma.cta_group::2 instructions that read both CTAs' tiles and write each CTA's 128
+// accumulator rows into that CTA's TMEM. Per 256 x BN x 64 step each SM's shared memory supplies
+// 16 KB of A and BN/2 x 128 B of B, half the B traffic of the single-CTA 128 x BN tile, which is
+// what bounds the single-CTA kernel. Barrier traffic between the two CTAs:
+//   full[s]   (even CTA)  both producers' TMA bytes (expect_tx by the even CTA only)
+//   empty[s]  (each CTA)  MMA commit, issued once to each CTA's barrier
+//   tfull[i]  (each CTA)  MMA commit after a tile's last k-block, once to each CTA
+//   tempty[i] (even CTA)  all 8 epilogue warps of the pair (the odd CTA's arrive remotely)
+template <int BN> struct PairCfg
+{
+    static constexpr int kStages = 6;
+    static constexpr int kABytes = BM * BK * 2;
+    static constexpr int kBBytes = (BN / 2) * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kBarrierBytes = 256;
+    static constexpr int kStagingBytes = 5120;
+    static constexpr int kStagingOffset = kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kSmemBytes = kStagingOffset + 4 * kStagingBytes + 1024;
+};
+
+template <int BN, Epilogue EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m,
+                     int n, int k_b, GemmEpilogueArgs args)
+{
+    using C = PairCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - raw);
+    const uint32_t bars = base + C::kStages * C::kStageBytes;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (C::kStages + s); };
+    auto tfull_bar = [&](int i) { return bars + 8u * (2 * C::kStages + i); };
+    auto tempty_bar = [&](int i) { return bars + 8u * (2 * C::kStages + 2 + i); };
+    const uint32_t slot = bars + 8u * (2 * C::kStages + 4);
+    auto tile_a = [&](int s) { return base + s * C::kStageBytes; };
+    auto tile_b = [&](int s) { return base + s * C::kStageBytes + C::kABytes; };
+
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int num_m = (m + 2 * BM - 1) / (2 * BM), num_n = n / BN, tiles = num_m * num_n;
+    const int k_blocks = k_b / BK;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < C::kStages; ++s)
+        {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int i = 0; i < 2; ++i)
+        {
+            mbar_init(tfull_bar(i), 1);
+            mbar_init(tempty_bar(i), 8);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0)
+    {
+        prefetch_tensormap(&map_a);
+        prefetch_tensormap(&map_b);
+    }
+    if (warp == 1)
+    {
+        tmem_alloc_pair(slot, C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync(); // both CTAs' barriers are initialised before any remote arrive or TMA completion
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += pairs)
+            {
+                const int m_blk = tile % num_m, n_blk = tile / num_m;
+                for (int kb = 0; kb < k_blocks; ++kb)
+                {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u))
+                    {
+                        if (args.error_flag) atomicExch(args.error_flag, kErrGemmProducerTimeout);
+                        ok = false;
+                        break;
+                    }
+                    // the even CTA expects both CTAs' bytes on its full barrier
+                    if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
+                    const uint32_t bar = mapa_shared(full_bar(stage), 0);
+                    tma_load_2d_pair(tile_a(stage), &map_a, bar, kb * BK, m_blk * 2 * BM + static_cast<int>(rank) * BM);
+                    tma_load_2d_pair(tile_b(stage), &map_b, bar, kb * BK,
+                                     n_blk * BN + static_cast<int>(rank) * (BN / 2));
+                    if (++stage == C::kStages)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // tail: wait until the MMA has released every filled stage, so that no commit from the
+            // even CTA is still on its way to this CTA's barriers when the CTA exits
+            for (int i = 0; i < C::kStages && ok; ++i)
+            {
+                if (!mbar_wait(empty_bar(stage), phase ^ 1u))
+                {
+                    if (args.error_flag) atomicExch(args.error_flag, kErrGemmProducerTimeout);
+                    ok = false;
+                }
+                if (++stage == C::kStages)
+                {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0 && leader)
+        {
+            constexpr uint32_t idesc = idesc_bf16(2 * BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int unit = 0;
+            for (int tile = pair; tile < tiles && ok; tile += pairs, ++unit)
+            {
+                const int acc = unit & 1;
+                const uint32_t acc_phase = (unit >> 1) & 1;
+                if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u))
+                {
+                    if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < k_blocks; ++kb)
+                {
+                    if (!mbar_wait(full_bar(stage), phase))
+                    {
+                        if (args.error_flag) atomicExch(args.error_flag, kErrGemmMmaTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t a_desc = smem_desc_sw128(tile_a(stage));
+                    const uint64_t b_desc = smem_desc_sw128(tile_b(stage));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_bf16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb != 0 || k != 0) ? 1u : 0u);
+                    umma_commit_pair(empty_bar(stage));
+                    umma_commit_pair(mapa_shared(empty_bar(stage), peer));
+                    if (++stage == C::kStages)
+                    {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok)
+                {
+                    umma_commit_pair(tfull_bar(acc));
+                    umma_commit_pair(mapa_shared(tfull_bar(acc), peer));
+                }
+            }
+        }
+    }
+    else
+    {
+        const int quarter = warp & 3;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t leader_tempty0 = mapa_shared(tempty_bar(0), 0), leader_tempty1 = mapa_shared(tempty_bar(1), 0);
+        int unit = 0;
+        for (int tile = pair; tile < tiles; tile += pairs, ++unit)
+        {
+            const int m_blk = tile % num_m, n_blk = tile / num_m;
+            const int row0 = m_blk * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;
+            uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
+            const int acc = unit & 1;
+            const uint32_t acc_phase = (unit >> 1) & 1;
+            if (!mbar_wait(tfull_bar(acc), acc_phase))
+            {
+                if (args.error_flag && lane == 0) atomicExch(args.error_flag, kErrGemmEpilogueTimeout);
+                break;
+            }
+            tc_fence_after();
+            run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+        }
+    }
+    // no CTA leaves (or frees TMEM) while its partner may still signal its barriers or use its TMEM
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    }
+}
+
 // ---- host side ------------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 {
@@ -639,6 +853,71 @@ template <int BN, Epilogue EPI, bool PROMOTE> cudaError_t ensure_attributes()
                                     Cfg<BN, PROMOTE>::kSmemBytes);
     });
     return attr;
+}
+
+template <int BN, Epilogue EPI> cudaError_t ensure_pair_attributes()
+{
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(gemm_pair_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    PairCfg<BN>::kSmemBytes);
+    });
+    return attr;
+}
+
+// Pairs that can be resident at once (one CTA per SM, both SMs of a pair in one GPC).
+template <int BN, Epilogue EPI> int resident_pairs(int num_sms)
+{
+    static std::once_flag once;
+    static int pairs = 0;
+    std::call_once(once, [num_sms] {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (num_sms / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = PairCfg<BN>::kSmemBytes;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<BN, EPI>, &cfg) == cudaSuccess && clusters > 0)
+            pairs = clusters;
+        else
+            cudaGetLastError();
+    });
+    return pairs > 0 ? pairs : num_sms / 2;
+}
+
+template <int BN, Epilogue EPI>
+int launch_pair(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, const GemmEpilogueArgs &args,
+                int num_sms, cudaStream_t stream)
+{
+    const cudaError_t attr = ensure_pair_attributes<BN, EPI>();
+    if (attr != cudaSuccess) return attr;
+    CUtensorMap map_a, map_b;
+    if (!make_map(&map_a, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k_b), BM) ||
+        !make_map(&map_b, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k_b), BN / 2))
+        return cudaErrorInvalidValue;
+    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
+    const int max_pairs = resident_pairs<BN, EPI>(num_sms);
+    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = PairCfg<BN>::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 2;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, args);
 }
 
 template <int BN, Epilogue EPI, bool PROMOTE>
@@ -688,11 +967,40 @@ template <int BN, bool PROMOTE> cudaError_t prepare_all()
         if (e == cudaSuccess) e = ensure_attributes<BN, Epilogue::FinalEuler, PROMOTE>();
     return e;
 }
+
+cudaError_t prepare_pairs()
+{
+    cudaError_t e = ensure_pair_attributes<256, Epilogue::F32Bias>();
+    if (e == cudaSuccess) e = ensure_pair_attributes<256, Epilogue::ResidGate>();
+    if (e == cudaSuccess) e = ensure_pair_attributes<256, Epilogue::Qkv>();
+    if (e == cudaSuccess) e = ensure_pair_attributes<256, Epilogue::Geglu>();
+    // resident pair counts are queried here, outside any stream capture
+    int device = 0, sms = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess)
+    {
+        resident_pairs<256, Epilogue::F32Bias>(sms);
+        resident_pairs<256, Epilogue::ResidGate>(sms);
+        resident_pairs<256, Epilogue::Qkv>(sms);
+        resident_pairs<256, Epilogue::Geglu>(sms);
+    }
+    return e;
+}
+
+// CTA pairs pay off unless 256-row tiles pad M much more than 128-row tiles do.
+bool use_pairs(int m, int splits, int block_n, bool promote)
+{
+    if (promote || splits != 1 || block_n != 256) return false;
+    const long long rows1 = (m + BM - 1) / BM * BM, rows2 = (m + 2 * BM - 1) / (2 * BM) * (2 * BM);
+    return rows2 * 100 <= rows1 * 112;
+}
 } // namespace
 
 int prepare_gemm_kernels()
 {
-    cudaError_t e = prepare_all<256, false>();
+    cudaError_t e = prepare_pairs();
+    if (e == cudaSuccess) e = prepare_all<256, false>();
     if (e == cudaSuccess) e = prepare_all<128, false>();
     if (e == cudaSuccess) e = prepare_all<128, true>();
     return e;
@@ -718,6 +1026,17 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     }
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
     if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
+    if (use_pairs(m, splits, block_n, promote) && epilogue != Epilogue::FinalEuler)
+    {
+        switch (epilogue)
+        {
+        case Epilogue::F32Bias: return launch_pair<256, Epilogue::F32Bias>(a, b, m, n, k_b, args, num_sms, stream);
+        case Epilogue::ResidGate: return launch_pair<256, Epilogue::ResidGate>(a, b, m, n, k_b, args, num_sms, stream);
+        case Epilogue::Qkv: return launch_pair<256, Epilogue::Qkv>(a, b, m, n, k_b, args, num_sms, stream);
+        case Epilogue::Geglu: return launch_pair<256, Epilogue::Geglu>(a, b, m, n, k_b, args, num_sms, stream);
+        default: return cudaErrorInvalidValue;
+        }
+    }
     if (block_n == 256) return dispatch<256, false>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
     return dispatch<128, false>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
 }
