@@ -988,12 +988,17 @@ cudaError_t prepare_pairs()
     return e;
 }
 
-// CTA pairs pay off unless 256-row tiles pad M much more than 128-row tiles do.
-bool use_pairs(int m, int splits, int block_n, bool promote)
+// Measured on B200 (C2 shapes, power-capped clocks): a pair tile takes as long per 128 rows as a
+// single-CTA tile, and pairs gain only on the long-K, narrow-N projections (out, down: 3-5%). They
+// are used when they need no more rounds of tiles over the SMs than single CTAs do; otherwise the
+// coarser 256-row quantisation loses (up/gate: 23 rounds instead of 22 at 4160 rows).
+bool use_pairs(int m, int n, int splits, int block_n, bool promote, int num_sms)
 {
-    if (promote || splits != 1 || block_n != 256) return false;
-    const long long rows1 = (m + BM - 1) / BM * BM, rows2 = (m + 2 * BM - 1) / (2 * BM) * (2 * BM);
-    return rows2 * 100 <= rows1 * 112;
+    if (promote || splits != 1 || block_n != 256 || num_sms < 2) return false;
+    const long long tiles1 = static_cast<long long>((m + BM - 1) / BM) * (n / block_n);
+    const long long tiles2 = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * (n / block_n);
+    const long long rounds1 = (tiles1 + num_sms - 1) / num_sms, rounds2 = (tiles2 + num_sms / 2 - 1) / (num_sms / 2);
+    return rounds2 <= rounds1;
 }
 } // namespace
 
@@ -1026,7 +1031,7 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     }
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
     if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
-    if (use_pairs(m, splits, block_n, promote) && epilogue != Epilogue::FinalEuler)
+    if (use_pairs(m, n, splits, block_n, promote, num_sms) && epilogue != Epilogue::FinalEuler)
     {
         switch (epilogue)
         {

@@ -26,7 +26,9 @@ def test_linear_exact_kat(ctx, m, n, k, bias):
     assert np.array_equal(flat, ref)
 
 
-# (1056|4160|256|1000|3000|4096, N % 256 == 0) run on CTA pairs (256-row tiles); the others on single CTAs
+# on 148 SMs these run on CTA pairs (256-row tiles, chosen when they need no more tile rounds than
+# single CTAs): (100, 256), (4160, 1024), (256, 512), (1000, 256), (3000, 768), (4096, 4096); the
+# others on single CTAs
 @pytest.mark.parametrize("m,n,k", [(1, 128, 64), (100, 256, 4096), (1056, 4096, 4096), (4160, 1024, 12288),
                                    (256, 512, 128), (1000, 256, 128), (3000, 768, 640), (4096, 4096, 64)])
 def test_linear_random(ctx, m, n, k):
