@@ -4,20 +4,26 @@
 // softmax(Q K^T / sqrt(128) + mask_row) V per head over the joint image+text sequence, non-causal,
 // keys past the valid count (the -1e30 text padding of src/conditioning.cpp:41-42) skipped.
 //
-// One CTA = one head x 128 queries; KV tiles of 128 keys.
-//   warp 0      TMA producer: Q once, then K and V^T tiles through a 2-stage ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
-//                 S_j = Q K_j^T   (M=128, N=128, K=128) into one of two TMEM S buffers
-//                 O  += P_j V_j   (M=128, N=128 dims, K=128 keys) into the TMEM O accumulator
-//   warps 2..5  softmax, one query row per thread: tcgen05.ld of S_j, online max/sum in FP32,
-//               P_j written as BF16 into one of two 128-byte-swizzled shared tiles (the K-major
-//               A operand of the next MMA), final O / l. The running max is only raised (and O in
-//               TMEM rescaled) when a tile's max exceeds it by more than 2^8; between raises the
-//               stale max is exact because O and l share it, and P stays <= 256.
-// Issue order S_0, S_1, PV_0, S_2, PV_1, S_3, ... lets S_{j+1} run while softmax works on S_j,
-// and the two P buffers let softmax j+1 write while PV_j is still executing.
-// V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so both MMAs use
-// K-major operands. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
+// One CTA = one head x 256 queries as two 128-row query tiles A and B that share every K / V^T tile;
+// KV tiles of 128 keys. TMEM (512 columns): S_A, S_B, O_A, O_B, 128 columns each; P_g (BF16 pairs,
+// 64 columns) overwrites the first half of S_g once softmax has read S_g, and is the TMEM A operand
+// of the PV MMA, so P never touches shared memory.
+//   warp 0      TMA producer: Q_A, Q_B once, then K and V^T tiles through a 2-stage ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, in the order
+//                 S_A(j), PV_B(j-1), S_B(j), PV_A(j), S_A(j+1), ...
+//               so the tensor core computes one group's MMAs while the other group's softmax runs
+//               (MMAs of one thread execute in issue order, so S_g(j+1) overwrites P_g(j) only after
+//               PV_g(j) has read it)
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B; one query row per thread:
+//               tcgen05.ld of S_g(j), online max/sum in FP32, P_g(j) stored to TMEM, final O / l.
+//               exp2 runs on the MUFU for three of every four keys and as a degree-3 polynomial on the
+//               FMA pipe for the fourth (relative error 7.5e-5, far below P's BF16 rounding), so the
+//               two softmax groups together stay under the tensor core's time per tile.
+//               The running max is only raised (and O_g rescaled in TMEM) when a tile's max exceeds
+//               it by more than 2^8; between raises the stale max is exact because O and l share it.
+//               The commit of S_g(j) also covers PV_g(j-1), so a rescale never races the PV MMA.
+// V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so the PV MMA's B
+// operand is K-major. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
 #include "kernels.h"
 #include "ptx.cuh"
 #include <cudaTypedefs.h>
@@ -27,12 +33,13 @@ namespace ernie_b200
 {
 namespace
 {
-constexpr int kThreads = 192;
-constexpr int kTile = 128;                   // queries per CTA, keys per KV tile, head dim
+constexpr int kThreads = 320;
+constexpr int kTile = 128;                   // queries per tile, keys per KV tile, head dim
+constexpr int kRowsPerCta = 2 * kTile;       // two query tiles
 constexpr int kHalfBytes = kTile * 64 * 2;   // one 64-column half of a 128 x 128 BF16 tile
 constexpr int kTileBytes = 2 * kHalfBytes;   // 32 KB
-constexpr int kSmemBytes = 7 * kTileBytes + 1024 + 256; // Q, 2 K, 2 V^T, 2 P tiles
-constexpr int kTmemCols = 512;               // S buffers at columns 0 and 128, O at 256
+constexpr int kSmemBytes = 6 * kTileBytes + 1024 + 256; // Q_A, Q_B, 2 K, 2 V^T tiles
+constexpr int kTmemCols = 512;               // S_A 0, S_B 128, O_A 256, O_B 384
 
 enum FlashError : int
 {
@@ -56,17 +63,50 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+// 2^x on the FMA/ALU pipes: x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f by a degree-3
+// polynomial (coefficients fitted here for minimal relative error on [-0.5, 0.5], 7.5e-5), 2^n added
+// to the exponent field. Arguments at or below -125 give 0 (masked keys stay exactly zero).
+__device__ __forceinline__ float poly_exp2(float x)
 {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+    const float xc = fmaxf(x, -125.f);
+    const float shifter = 12582912.f; // 1.5 * 2^23: x + shifter rounds x to an integer in the low bits
+    const float t = __fadd_rn(xc, shifter);
+    const int n = __float_as_int(t) - 0x4B400000;
+    const float f = __fsub_rn(xc, __fsub_rn(t, shifter));
+    float p = fmaf(0.055171649903059006f, f, 0.2426111251115799f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999280571937561f);
+    const float r = __int_as_float(__float_as_int(p) + (n << 23));
+    return x <= -125.f ? 0.f : r;
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi)
 {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// O (+)= P V: A = P from TMEM (128 lanes x 16 keys per instruction = 8 columns of BF16 pairs).
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_store_32u(uint32_t taddr, const uint32_t *v)
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+                 "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+                 "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+                 "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+                 : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -77,22 +117,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *base_ptr = smem_raw + (base - raw);
-    const uint32_t s_q = base;
-    auto s_k = [&](int s) { return base + (1 + s) * kTileBytes; };
-    auto s_v = [&](int s) { return base + (3 + s) * kTileBytes; };
-    auto s_p = [&](int b) { return base + (5 + b) * kTileBytes; };
-    const uint32_t bars = base + 7 * kTileBytes;
+    auto s_q = [&](int g) { return base + g * kTileBytes; };
+    auto s_k = [&](int s) { return base + (2 + s) * kTileBytes; };
+    auto s_v = [&](int s) { return base + (4 + s) * kTileBytes; };
+    const uint32_t bars = base + 6 * kTileBytes;
     const uint32_t q_full = bars;
     auto k_full = [&](int s) { return bars + 8u * (1 + s); };
     auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
     auto v_full = [&](int s) { return bars + 8u * (5 + s); };
     auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
-    auto s_full = [&](int s) { return bars + 8u * (9 + s); };
-    auto p_full = [&](int b) { return bars + 8u * (11 + b); };
-    auto p_empty = [&](int b) { return bars + 8u * (13 + b); };
+    auto s_full = [&](int g) { return bars + 8u * (9 + g); };
+    auto p_full = [&](int g) { return bars + 8u * (11 + g); };
+    auto o_full = [&](int g) { return bars + 8u * (13 + g); };
     const uint32_t slot = bars + 8u * 15;
 
-    const int head = blockIdx.y, q0 = blockIdx.x * kTile;
+    const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int tiles = (a.kv_len + kTile - 1) / kTile;
 
@@ -107,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(v_empty(s), 1);
             mbar_init(s_full(s), 1);
             mbar_init(p_full(s), 4);
-            mbar_init(p_empty(s), 1);
+            mbar_init(o_full(s), 1);
         }
         fence_barrier_init();
     }
@@ -126,16 +165,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
-    const uint32_t o_col = 256;
+    auto s_col = [](int g) { return static_cast<uint32_t>(g * 128); };
+    auto o_col = [](int g) { return static_cast<uint32_t>(256 + g * 128); };
 
     if (warp == 0)
     {
         if (lane == 0)
         {
             const int row_q = head * a.rows_pad + q0;
-            mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_2d(s_q, &map_q, q_full, 0, row_q);
-            tma_load_2d(s_q + kHalfBytes, &map_q, q_full, 64, row_q);
+            mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+            for (int g = 0; g < 2; ++g)
+            {
+                tma_load_2d(s_q(g), &map_q, q_full, 0, row_q + g * kTile);
+                tma_load_2d(s_q(g) + kHalfBytes, &map_q, q_full, 64, row_q + g * kTile);
+            }
             for (int j = 0; j < tiles; ++j)
             {
                 const int s = j & 1;
@@ -166,50 +209,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             constexpr uint32_t idesc = idesc_bf16(128, 128);
             bool ok = mbar_wait(q_full, 0);
-            auto issue_s = [&](int j) -> bool {
+            auto issue_s = [&](int g, int s) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                {
+                    const uint64_t ad = smem_desc_sw128(s_q(g) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                    const uint64_t bd = smem_desc_sw128(s_k(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                    umma_bf16(tmem_base + s_col(g), ad, bd, idesc, k > 0 ? 1u : 0u);
+                }
+                umma_commit(s_full(g));
+            };
+            // PV_g(j): waits for P_g(j) and V_j
+            auto issue_pv = [&](int g, int j) -> bool {
                 const int s = j & 1;
-                if (!mbar_wait(k_full(s), (j >> 1) & 1)) return false;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(p_full(g), j & 1) || !mbar_wait(v_full(s), ph)) return false;
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
                 {
-                    const uint64_t ad = smem_desc_sw128(s_q + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    const uint64_t bd = smem_desc_sw128(s_k(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    umma_bf16(tmem_base + s * 128, ad, bd, idesc, k > 0 ? 1u : 0u);
+                    const uint64_t bd = smem_desc_sw128(s_v(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                    umma_bf16_tmem_a(tmem_base + o_col(g), tmem_base + s_col(g) + 8u * k, bd, idesc,
+                                     (j > 0 || k > 0) ? 1u : 0u);
                 }
-                umma_commit(k_empty(s));
-                umma_commit(s_full(s));
                 return true;
             };
-            if (ok) ok = issue_s(0);
-            if (ok && tiles > 1) ok = issue_s(1);
             for (int j = 0; j < tiles && ok; ++j)
             {
-                const int b = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(p_full(b), ph) || !mbar_wait(v_full(b), ph))
+                const int s = j & 1;
+                if (!mbar_wait(k_full(s), (j >> 1) & 1))
                 {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
+                issue_s(0, s);
+                if (j > 0)
                 {
-                    const uint64_t ad = smem_desc_sw128(s_p(b) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    const uint64_t bd = smem_desc_sw128(s_v(b) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    umma_bf16(tmem_base + o_col, ad, bd, idesc, (j > 0 || k > 0) ? 1u : 0u);
+                    if (!issue_pv(1, j - 1))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    umma_commit(v_empty((j - 1) & 1));
                 }
-                umma_commit(v_empty(b));
-                umma_commit(p_empty(b));
-                if (j + 2 < tiles) ok = issue_s(j + 2);
+                issue_s(1, s);
+                umma_commit(k_empty(s));
+                if (!issue_pv(0, j))
+                {
+                    ok = false;
+                    break;
+                }
+                if (j == tiles - 1) umma_commit(o_full(0));
+            }
+            if (ok)
+            {
+                ok = issue_pv(1, tiles - 1);
+                if (ok)
+                {
+                    umma_commit(v_empty((tiles - 1) & 1));
+                    umma_commit(o_full(1));
+                }
             }
             if (!ok && a.error_flag) atomicExch(a.error_flag, kErrFlashMmaTimeout);
         }
     }
     else
     {
-        const int quarter = warp & 3;
+        const int g = (warp - 2) >> 2;    // 0: tile A (warps 2..5), 1: tile B (warps 6..9)
+        const int quarter = warp & 3;     // TMEM lane quarter this warp may access
         const int r = quarter * 32 + lane; // row within the query tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         // scores stay in raw units; c folds 1/sqrt(128) and log2(e) into one FFMA per element
@@ -217,27 +285,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr float kMaskToRaw = 11.313708498984761f; // log2(e)/c = sqrt(128)
         constexpr float kRescaleLog2 = 8.f;              // rescale O only when the max grows by 2^8
         float m_run = -INFINITY, l_run = 0.f;
-        int waited0 = 0, waited1 = 0; // completions of p_empty[0] / p_empty[1] already observed
         bool ok = true;
-        auto wait_pv = [&](int i) -> bool { // PV_i complete
-            const int b = i & 1, k = i >> 1;
-            int &waited = b ? waited1 : waited0;
-            if (waited > k) return true;
-            if (!mbar_wait(p_empty(b), k & 1)) return false;
-            waited = k + 1;
-            return true;
-        };
         for (int j = 0; j < tiles && ok; ++j)
         {
-            const int b = j & 1;
-            if (!mbar_wait(s_full(b), (j >> 1) & 1))
+            if (!mbar_wait(s_full(g), j & 1))
             {
                 ok = false;
                 break;
             }
             tc_fence_after();
             float x[128];
-            tmem_load_128(lane_base + b * 128, x);
+            tmem_load_128(lane_base + s_col(g), x);
             const int key0 = j * kTile;
             if (a.mask)
             {
@@ -257,60 +315,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (j == 0) m_run = tmax;
             else if (__any_sync(0xffffffffu, (tmax - m_run) * c > kRescaleLog2))
             {
-                // the O rescale must land between PV_{j-1} and PV_j
+                // PV_g(j-1) is complete: its commit preceded S_g(j)'s
                 const float m_new = fmaxf(m_run, tmax);
                 const float alpha = fast_exp2((m_run - m_new) * c);
-                if (!wait_pv(j - 1))
-                {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
                 {
                     float o[32];
-                    tmem_load_32(lane_base + o_col + cc * 32, o);
+                    tmem_load_32(lane_base + o_col(g) + cc * 32, o);
 #pragma unroll
                     for (int t = 0; t < 32; ++t) o[t] *= alpha;
-                    tmem_store_32(lane_base + o_col + cc * 32, o);
+                    tmem_store_32(lane_base + o_col(g) + cc * 32, o);
                 }
-                tmem_store_wait();
                 l_run *= alpha;
                 m_run = m_new;
             }
             const float neg = -m_run * c;
             float row_sum = 0.f;
+            uint32_t pk[64];
 #pragma unroll
-            for (int k = 0; k < 128; ++k)
+            for (int k = 0; k < 128; k += 2)
             {
-                x[k] = fast_exp2(fmaf(x[k], c, neg));
-                row_sum += x[k];
+                const float e0 = fast_exp2(fmaf(x[k], c, neg));
+                const float arg1 = fmaf(x[k + 1], c, neg);
+                const float e1 = (k & 2) ? poly_exp2(arg1) : fast_exp2(arg1);
+                row_sum += e0 + e1;
+                pk[k / 2] = pack2(e0, e1);
             }
             l_run += row_sum;
-            // P buffer b is free once PV_{j-2} has consumed it
-            if (j >= 2 && !wait_pv(j - 2))
-            {
-                ok = false;
-                break;
-            }
-            // P row r as BF16 into the swizzled K-major tile: half h holds keys 64h..64h+63,
-            // 16-byte chunk cc of row r sits at chunk cc ^ (r & 7).
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc)
-                {
-                    const float *v = x + h * 64 + cc * 8;
-                    const uint32_t addr = s_p(b) + h * kHalfBytes + r * 128 + ((cc ^ (r & 7)) << 4);
-                    st_shared_v4(addr, pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
-                }
-            fence_async_smem();
+            // P_g(j) over the first 64 columns of S_g (the MMA reads it as BF16 pairs, key 2i low)
+            tmem_store_32u(lane_base + s_col(g), pk);
+            tmem_store_32u(lane_base + s_col(g) + 32, pk + 32);
+            tmem_store_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full(b));
+            if (lane == 0) mbar_arrive(p_full(g));
         }
-        if (ok && !wait_pv(tiles - 1)) ok = false;
+        if (ok && !mbar_wait(o_full(g), 0)) ok = false;
         if (!ok)
         {
             if (a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashSoftmaxTimeout);
@@ -318,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
         {
             tc_fence_after();
-            const int row = q0 + r;
+            const int row = q0 + g * kTile + r;
             const float inv = 1.f / l_run;
             // output row `row` belongs to destination row / rows_per_dest (its owner GPU in a
             // sequence-parallel group; destination 0 on one GPU)
@@ -332,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int cc = 0; cc < 4; ++cc)
             {
                 float o[32];
-                tmem_load_32(lane_base + o_col + cc * 32, o);
+                tmem_load_32(lane_base + o_col(g) + cc * 32, o);
                 if (row < a.rows)
                 {
 #pragma unroll
@@ -406,7 +447,7 @@ int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_b
         !map_2d(&mv, vt, static_cast<uint64_t>(heads) * kTile, static_cast<uint64_t>(rows_pad)))
         return cudaErrorInvalidValue;
     FlashArgs a{rows, rows_pad, kv_len, mask, out, error_flag};
-    const dim3 grid((rows + kTile - 1) / kTile, heads);
+    const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, heads);
     flash_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
     return cudaGetLastError();
 }
