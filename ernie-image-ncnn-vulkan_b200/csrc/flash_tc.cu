@@ -16,9 +16,10 @@
 //               PV_g(j) has read it)
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B; one query row per thread:
 //               tcgen05.ld of S_g(j), online max/sum in FP32, P_g(j) stored to TMEM, final O / l.
-//               exp2 runs on the MUFU for three of every four keys and as a degree-3 polynomial on the
-//               FMA pipe for the fourth (relative error 7.5e-5, far below P's BF16 rounding), so the
-//               two softmax groups together stay under the tensor core's time per tile.
+//               exp2 on the MUFU (a degree-3 polynomial on the FMA pipe for part of the keys was
+//               measured slower: at ~9 instructions per element it costs more issue slots than the
+//               MUFU's 8 cycles per warp instruction save). Row max over 8 independent chains, the
+//               exponent arguments and row sums as packed FP32x2 operations.
 //               The running max is only raised (and O_g rescaled in TMEM) when a tile's max exceeds
 //               it by more than 2^8; between raises the stale max is exact because O and l share it.
 //               The commit of S_g(j) also covers PV_g(j-1), so a rescale never races the PV MMA.
@@ -61,23 +62,6 @@ __device__ __forceinline__ float fast_exp2(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// 2^x on the FMA/ALU pipes: x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f by a degree-3
-// polynomial (coefficients fitted here for minimal relative error on [-0.5, 0.5], 7.5e-5), 2^n added
-// to the exponent field. Arguments at or below -125 give 0 (masked keys stay exactly zero).
-__device__ __forceinline__ float poly_exp2(float x)
-{
-    const float xc = fmaxf(x, -125.f);
-    const float shifter = 12582912.f; // 1.5 * 2^23: x + shifter rounds x to an integer in the low bits
-    const float t = __fadd_rn(xc, shifter);
-    const int n = __float_as_int(t) - 0x4B400000;
-    const float f = __fsub_rn(xc, __fsub_rn(t, shifter));
-    float p = fmaf(0.055171649903059006f, f, 0.2426111251115799f);
-    p = fmaf(p, f, 0.6932609677314758f);
-    p = fmaf(p, f, 0.9999280571937561f);
-    const float r = __int_as_float(__float_as_int(p) + (n << 23));
-    return x <= -125.f ? 0.f : r;
 }
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi)
@@ -309,9 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < 128; ++k)
                     if (key0 + k >= a.kv_len) x[k] = -INFINITY;
             }
-            float tmax = x[0];
+            // row max over 8 independent chains (a single 127-long chain is latency bound)
+            float mx[8];
 #pragma unroll
-            for (int k = 1; k < 128; ++k) tmax = fmaxf(tmax, x[k]);
+            for (int k = 0; k < 8; ++k) mx[k] = x[k];
+#pragma unroll
+            for (int k = 8; k < 128; ++k) mx[k & 7] = fmaxf(mx[k & 7], x[k]);
+            const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             if (j == 0) m_run = tmax;
             else if (__any_sync(0xffffffffu, (tmax - m_run) * c > kRescaleLog2))
             {
@@ -330,19 +319,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l_run *= alpha;
                 m_run = m_new;
             }
-            const float neg = -m_run * c;
-            float row_sum = 0.f;
+            // exponent arguments two at a time (packed FP32x2 FFMA), four independent pair sums
+            const float2 scale2 = make_float2(c, c), neg2 = make_float2(-m_run * c, -m_run * c);
+            float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
             uint32_t pk[64];
 #pragma unroll
             for (int k = 0; k < 128; k += 2)
             {
-                const float e0 = fast_exp2(fmaf(x[k], c, neg));
-                const float arg1 = fmaf(x[k + 1], c, neg);
-                const float e1 = (k & 2) ? poly_exp2(arg1) : fast_exp2(arg1);
-                row_sum += e0 + e1;
+                const float2 arg = __ffma2_rn(make_float2(x[k], x[k + 1]), scale2, neg2);
+                const float e0 = fast_exp2(arg.x), e1 = fast_exp2(arg.y);
+                sum2[(k >> 1) & 3] = __fadd2_rn(sum2[(k >> 1) & 3], make_float2(e0, e1));
                 pk[k / 2] = pack2(e0, e1);
             }
-            l_run += row_sum;
+            const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+            const float2 s4 = __fadd2_rn(s01, s23);
+            l_run += s4.x + s4.y;
             // P_g(j) over the first 64 columns of S_g (the MMA reads it as BF16 pairs, key 2i low)
             tmem_store_32u(lane_base + s_col(g), pk);
             tmem_store_32u(lane_base + s_col(g) + 32, pk + 32);
