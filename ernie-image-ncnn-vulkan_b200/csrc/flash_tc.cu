@@ -14,7 +14,8 @@
 //               so the tensor core computes one group's MMAs while the other group's softmax runs
 //               (MMAs of one thread execute in issue order, so S_g(j+1) overwrites P_g(j) only after
 //               PV_g(j) has read it)
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B; one query row per thread:
+//   warps 2, 3  idle (warpgroup 0 hands its registers to the softmax warpgroups)
+//   warps 4..7  softmax of tile A, warps 8..11 softmax of tile B; one query row per thread:
 //               tcgen05.ld of S_g(j), online max/sum in FP32, P_g(j) stored to TMEM, final O / l.
 //               exp2 on the MUFU (a degree-3 polynomial on the FMA pipe for part of the keys was
 //               measured slower: at ~9 instructions per element it costs more issue slots than the
@@ -34,7 +35,13 @@ namespace ernie_b200
 {
 namespace
 {
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;               // three warpgroups (register reallocation is per warpgroup)
+// Registers per thread after setmaxnreg: warpgroup 0 (TMA, MMA, two idle warps) gives registers to
+// the two softmax warpgroups (216 each: no spills; at 168 the softmax spilled). 128 x 72 + 256 x 216 =
+// 64512 = 384 x 168, so the launch must have 168 registers per thread, which ptxas assigns at 384
+// threads; the host refuses to launch otherwise (an increase the block cannot satisfy would wait).
+constexpr int kRegsControl = 72, kRegsSoftmax = 216, kMinLaunchRegs = 168;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kMinLaunchRegs, "register split");
 constexpr int kTile = 128;                   // queries per tile, keys per KV tile, head dim
 constexpr int kRowsPerCta = 2 * kTile;       // two query tiles
 constexpr int kHalfBytes = kTile * 64 * 2;   // one 64-column half of a 128 x 128 BF16 tile
@@ -113,7 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto s_full = [&](int g) { return bars + 8u * (9 + g); };
     auto p_full = [&](int g) { return bars + 8u * (11 + g); };
     auto o_full = [&](int g) { return bars + 8u * (13 + g); };
-    const uint32_t slot = bars + 8u * 15;
+    const uint32_t tmem_done = bars + 8u * 15;
+    const uint32_t slot = bars + 8u * 16;
 
     const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -132,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(p_full(s), 4);
             mbar_init(o_full(s), 1);
         }
+        mbar_init(tmem_done, 8);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0)
@@ -151,7 +160,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
     auto s_col = [](int g) { return static_cast<uint32_t>(g * 128); };
     auto o_col = [](int g) { return static_cast<uint32_t>(256 + g * 128); };
-
+    // Each role ends the kernel on its own: the register split differs per warpgroup, so no code
+    // after the split is shared. TMEM is freed by warp 1 once all 8 softmax warps are done with it.
+    if (warp < 4)
+    {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     if (warp == 0)
     {
         if (lane == 0)
@@ -257,10 +270,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok && a.error_flag) atomicExch(a.error_flag, kErrFlashMmaTimeout);
         }
+        __syncwarp();
+        if (!mbar_wait(tmem_done, 0) && a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashMmaTimeout);
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
     }
     else
     {
-        const int g = (warp - 2) >> 2;    // 0: tile A (warps 2..5), 1: tile B (warps 6..9)
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+        const int g = (warp - 4) >> 2;    // 0: tile A (warps 4..7), 1: tile B (warps 8..11)
         const int quarter = warp & 3;     // TMEM lane quarter this warp may access
         const int r = quarter * 32 + lane; // row within the query tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -381,12 +400,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    }
-    __syncthreads();
-    if (warp == 1)
-    {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_done);
     }
 }
 
@@ -421,6 +437,11 @@ bool map_2d(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols)
 
 int prepare_flash_kernels()
 {
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, flash_tc_kernel);
+    if (e != cudaSuccess) return e;
+    // the register split above needs this many registers per thread at launch
+    if (attr.numRegs < kMinLaunchRegs) return cudaErrorInvalidConfiguration;
     return cudaFuncSetAttribute(flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
 }
 
