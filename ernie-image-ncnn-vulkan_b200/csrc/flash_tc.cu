@@ -5,27 +5,25 @@
 // keys past the valid count (the -1e30 text padding of src/conditioning.cpp:41-42) skipped.
 //
 // One CTA = one head x 256 queries as two 128-row query tiles A and B that share every K / V^T tile;
-// KV tiles of 128 keys. TMEM (512 columns): S_A, S_B, O_A, O_B, 128 columns each; P_g (BF16 pairs,
-// 64 columns) overwrites the first half of S_g once softmax has read S_g, and is the TMEM A operand
-// of the PV MMA, so P never touches shared memory.
-//   warp 0      TMA producer: Q_A, Q_B once, then K and V^T tiles through a 2-stage ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, in the order
-//                 S_A(j), PV_B(j-1), S_B(j), PV_A(j), S_A(j+1), ...
-//               so the tensor core computes one group's MMAs while the other group's softmax runs
-//               (MMAs of one thread execute in issue order, so S_g(j+1) overwrites P_g(j) only after
-//               PV_g(j) has read it)
-//   warps 2, 3  idle (warpgroup 0 hands its registers to the softmax warpgroups)
+// KV tiles of 128 keys. TMEM (512 columns): S_A, S_B, O_A, O_B, 128 columns each. Softmax copies S_g
+// into registers and frees it at once, so S_g(j+1) is computed while softmax works on S_g(j); P_g goes
+// to a 128-byte-swizzled shared tile (the K-major A operand of the PV MMA). Each softmax warpgroup
+// therefore runs tile after tile without waiting for its own PV and next S, and the two groups keep
+// the MUFU (16 ex2 per clock per SM, as many per tile as the tensor core's cycles) and the tensor core
+// busy together.
+//   warp 0      TMA producer of Q_A, Q_B (once) and the K tiles (2-stage ring)
+//   warp 2      TMA producer of the V^T tiles (one buffer, refilled once both PVs have read it)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, per KV tile j:
+//                 S_A(j+1), S_B(j+1) (each once softmax has freed S_g(j)), PV_A(j), PV_B(j)
+//   warp 3      idle (warpgroup 0 hands its registers to the softmax warpgroups)
 //   warps 4..7  softmax of tile A, warps 8..11 softmax of tile B; one query row per thread:
-//               tcgen05.ld of S_g(j), online max/sum in FP32, P_g(j) stored to TMEM, final O / l.
-//               exp2 on the MUFU (a degree-3 polynomial on the FMA pipe for part of the keys was
-//               measured slower: at ~9 instructions per element it costs more issue slots than the
-//               MUFU's 8 cycles per warp instruction save). Row max over 8 independent chains, the
-//               exponent arguments and row sums as packed FP32x2 operations.
-//               The running max is only raised (and O_g rescaled in TMEM) when a tile's max exceeds
-//               it by more than 2^8; between raises the stale max is exact because O and l share it.
-//               The commit of S_g(j) also covers PV_g(j-1), so a rescale never races the PV MMA.
-// V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so the PV MMA's B
-// operand is K-major. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
+//               tcgen05.ld of S_g(j), online max/sum in FP32 (8 max chains, packed FP32x2 FFMA/FADD),
+//               ex2 on the MUFU, P_g(j) as BF16 into its shared tile once PV_g(j-1) has read the
+//               previous one, final O / l. The running max is only raised (and O_g rescaled in TMEM,
+//               after PV_g(j-1)) when a tile's max exceeds it by more than 2^8; between raises the
+//               stale max is exact because O and l share it.
+// V is stored transposed ([head][dim][token], written by the QKV GEMM epilogue) so both MMAs use
+// K-major operands. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
 #include "kernels.h"
 #include "ptx.cuh"
 #include <cudaTypedefs.h>
@@ -36,17 +34,17 @@ namespace ernie_b200
 namespace
 {
 constexpr int kThreads = 384;               // three warpgroups (register reallocation is per warpgroup)
-// Registers per thread after setmaxnreg: warpgroup 0 (TMA, MMA, two idle warps) gives registers to
-// the two softmax warpgroups (216 each: no spills; at 168 the softmax spilled). 128 x 72 + 256 x 216 =
-// 64512 = 384 x 168, so the launch must have 168 registers per thread, which ptxas assigns at 384
-// threads; the host refuses to launch otherwise (an increase the block cannot satisfy would wait).
-constexpr int kRegsControl = 72, kRegsSoftmax = 216, kMinLaunchRegs = 168;
+// Registers per thread after setmaxnreg: warpgroup 0 (producers, MMA, one idle warp) gives registers
+// to the two softmax warpgroups. 128 x 88 + 256 x 208 = 64512 = 384 x 168, so the launch must have
+// 168 registers per thread, which ptxas assigns at 384 threads; the host refuses to launch otherwise
+// (an increase the block cannot satisfy would wait).
+constexpr int kRegsControl = 88, kRegsSoftmax = 208, kMinLaunchRegs = 168;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kMinLaunchRegs, "register split");
 constexpr int kTile = 128;                   // queries per tile, keys per KV tile, head dim
 constexpr int kRowsPerCta = 2 * kTile;       // two query tiles
 constexpr int kHalfBytes = kTile * 64 * 2;   // one 64-column half of a 128 x 128 BF16 tile
 constexpr int kTileBytes = 2 * kHalfBytes;   // 32 KB
-constexpr int kSmemBytes = 6 * kTileBytes + 1024 + 256; // Q_A, Q_B, 2 K, 2 V^T tiles
+constexpr int kSmemBytes = 7 * kTileBytes + 1024 + 256; // Q_A, Q_B, P_A, P_B, 2 K, 1 V^T
 constexpr int kTmemCols = 512;               // S_A 0, S_B 128, O_A 256, O_B 384
 
 enum FlashError : int
@@ -71,33 +69,17 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi)
 {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
-}
-
-// O (+)= P V: A = P from TMEM (128 lanes x 16 keys per instruction = 8 columns of BF16 pairs).
-__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate)
-{
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "setp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_store_32u(uint32_t taddr, const uint32_t *v)
-{
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-                 "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-                 "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
-                 "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
-                 "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-                 : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -109,17 +91,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *base_ptr = smem_raw + (base - raw);
     auto s_q = [&](int g) { return base + g * kTileBytes; };
-    auto s_k = [&](int s) { return base + (2 + s) * kTileBytes; };
-    auto s_v = [&](int s) { return base + (4 + s) * kTileBytes; };
-    const uint32_t bars = base + 6 * kTileBytes;
+    auto s_p = [&](int g) { return base + (2 + g) * kTileBytes; };
+    auto s_k = [&](int s) { return base + (4 + s) * kTileBytes; };
+    const uint32_t s_v = base + 6 * kTileBytes;
+    const uint32_t bars = base + 7 * kTileBytes;
     const uint32_t q_full = bars;
     auto k_full = [&](int s) { return bars + 8u * (1 + s); };
     auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
-    auto v_full = [&](int s) { return bars + 8u * (5 + s); };
-    auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
-    auto s_full = [&](int g) { return bars + 8u * (9 + g); };
+    const uint32_t v_full = bars + 8u * 5, v_empty = bars + 8u * 6;
+    auto s_full = [&](int g) { return bars + 8u * (7 + g); };
+    auto s_free = [&](int g) { return bars + 8u * (9 + g); };
     auto p_full = [&](int g) { return bars + 8u * (11 + g); };
-    auto o_full = [&](int g) { return bars + 8u * (13 + g); };
+    auto pv_done = [&](int g) { return bars + 8u * (13 + g); };
     const uint32_t tmem_done = bars + 8u * 15;
     const uint32_t slot = bars + 8u * 16;
 
@@ -134,12 +117,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             mbar_init(k_full(s), 1);
             mbar_init(k_empty(s), 1);
-            mbar_init(v_full(s), 1);
-            mbar_init(v_empty(s), 1);
             mbar_init(s_full(s), 1);
+            mbar_init(s_free(s), 4);
             mbar_init(p_full(s), 4);
-            mbar_init(o_full(s), 1);
+            mbar_init(pv_done(s), 1);
         }
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
         mbar_init(tmem_done, 8);
         fence_barrier_init();
     }
@@ -165,9 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp < 4)
     {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    if (warp == 0)
-    {
-        if (lane == 0)
+        if (warp == 0 && lane == 0)
         {
             const int row_q = head * a.rows_pad + q0;
             mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
@@ -179,9 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < tiles; ++j)
             {
                 const int s = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
                 const int row_k = head * a.rows_pad + j * kTile;
-                if (!mbar_wait(k_empty(s), ph ^ 1u))
+                if (!mbar_wait(k_empty(s), ((j >> 1) & 1) ^ 1u))
                 {
                     if (a.error_flag) atomicExch(a.error_flag, kErrFlashProducerTimeout);
                     break;
@@ -189,92 +170,105 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(k_full(s), kTileBytes);
                 tma_load_2d(s_k(s), &map_k, k_full(s), 0, row_k);
                 tma_load_2d(s_k(s) + kHalfBytes, &map_k, k_full(s), 64, row_k);
-                if (!mbar_wait(v_empty(s), ph ^ 1u))
+            }
+        }
+        else if (warp == 2 && lane == 0)
+        {
+            for (int j = 0; j < tiles; ++j)
+            {
+                if (!mbar_wait(v_empty, (j & 1) ^ 1u))
                 {
                     if (a.error_flag) atomicExch(a.error_flag, kErrFlashProducerTimeout);
                     break;
                 }
-                mbar_arrive_expect_tx(v_full(s), kTileBytes);
-                tma_load_2d(s_v(s), &map_vt, v_full(s), j * kTile, head * kTile);
-                tma_load_2d(s_v(s) + kHalfBytes, &map_vt, v_full(s), j * kTile + 64, head * kTile);
+                mbar_arrive_expect_tx(v_full, kTileBytes);
+                tma_load_2d(s_v, &map_vt, v_full, j * kTile, head * kTile);
+                tma_load_2d(s_v + kHalfBytes, &map_vt, v_full, j * kTile + 64, head * kTile);
             }
         }
-    }
-    else if (warp == 1)
-    {
-        if (lane == 0)
+        else if (warp == 1)
         {
-            constexpr uint32_t idesc = idesc_bf16(128, 128);
-            bool ok = mbar_wait(q_full, 0);
-            auto issue_s = [&](int g, int s) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                {
-                    const uint64_t ad = smem_desc_sw128(s_q(g) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    const uint64_t bd = smem_desc_sw128(s_k(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    umma_bf16(tmem_base + s_col(g), ad, bd, idesc, k > 0 ? 1u : 0u);
-                }
-                umma_commit(s_full(g));
-            };
-            // PV_g(j): waits for P_g(j) and V_j
-            auto issue_pv = [&](int g, int j) -> bool {
-                const int s = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(p_full(g), j & 1) || !mbar_wait(v_full(s), ph)) return false;
-                tc_fence_after();
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                {
-                    const uint64_t bd = smem_desc_sw128(s_v(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
-                    umma_bf16_tmem_a(tmem_base + o_col(g), tmem_base + s_col(g) + 8u * k, bd, idesc,
-                                     (j > 0 || k > 0) ? 1u : 0u);
-                }
-                return true;
-            };
-            for (int j = 0; j < tiles && ok; ++j)
+            if (lane == 0)
             {
-                const int s = j & 1;
-                if (!mbar_wait(k_full(s), (j >> 1) & 1))
+                constexpr uint32_t idesc = idesc_bf16(128, 128);
+                bool ok = mbar_wait(q_full, 0);
+                auto issue_s = [&](int g, int j) {
+                    const int s = j & 1;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                    {
+                        const uint64_t ad = smem_desc_sw128(s_q(g) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                        const uint64_t bd = smem_desc_sw128(s_k(s) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                        umma_bf16(tmem_base + s_col(g), ad, bd, idesc, k > 0 ? 1u : 0u);
+                    }
+                    umma_commit(s_full(g));
+                };
+                auto issue_pv = [&](int g, int j) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                    {
+                        const uint64_t ad = smem_desc_sw128(s_p(g) + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                        const uint64_t bd = smem_desc_sw128(s_v + (k >> 2) * kHalfBytes) + 2u * (k & 3);
+                        umma_bf16(tmem_base + o_col(g), ad, bd, idesc, (j > 0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(pv_done(g));
+                };
+                if (ok && (ok = mbar_wait(k_full(0), 0)))
                 {
-                    ok = false;
-                    break;
+                    tc_fence_after();
+                    issue_s(0, 0);
+                    issue_s(1, 0);
+                    umma_commit(k_empty(0));
                 }
-                tc_fence_after();
-                issue_s(0, s);
-                if (j > 0)
+                for (int j = 0; j < tiles && ok; ++j)
                 {
-                    if (!issue_pv(1, j - 1))
+                    if (j + 1 < tiles)
+                    {
+                        // S_g(j+1) as soon as softmax g has copied S_g(j) out of TMEM
+                        const int n = j + 1;
+                        if (!mbar_wait(k_full(n & 1), (n >> 1) & 1))
+                        {
+                            ok = false;
+                            break;
+                        }
+                        for (int g = 0; g < 2 && ok; ++g)
+                        {
+                            if (!mbar_wait(s_free(g), j & 1))
+                            {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_s(g, n);
+                        }
+                        if (!ok) break;
+                        umma_commit(k_empty(n & 1));
+                    }
+                    if (!mbar_wait(v_full, j & 1))
                     {
                         ok = false;
                         break;
                     }
-                    umma_commit(v_empty((j - 1) & 1));
+                    for (int g = 0; g < 2 && ok; ++g)
+                    {
+                        if (!mbar_wait(p_full(g), j & 1))
+                        {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_pv(g, j);
+                    }
+                    if (!ok) break;
+                    umma_commit(v_empty);
                 }
-                issue_s(1, s);
-                umma_commit(k_empty(s));
-                if (!issue_pv(0, j))
-                {
-                    ok = false;
-                    break;
-                }
-                if (j == tiles - 1) umma_commit(o_full(0));
+                if (!ok && a.error_flag) atomicExch(a.error_flag, kErrFlashMmaTimeout);
             }
-            if (ok)
-            {
-                ok = issue_pv(1, tiles - 1);
-                if (ok)
-                {
-                    umma_commit(v_empty((tiles - 1) & 1));
-                    umma_commit(o_full(1));
-                }
-            }
-            if (!ok && a.error_flag) atomicExch(a.error_flag, kErrFlashMmaTimeout);
+            __syncwarp();
+            if (!mbar_wait(tmem_done, 0) && a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashMmaTimeout);
+            tc_fence_after();
+            tmem_dealloc(tmem_base, kTmemCols);
         }
-        __syncwarp();
-        if (!mbar_wait(tmem_done, 0) && a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashMmaTimeout);
-        tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
-    }
     }
     else
     {
@@ -299,6 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             float x[128];
             tmem_load_128(lane_base + s_col(g), x);
+            // S_g is in registers: the MMA warp may compute S_g(j+1) now
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free(g));
             const int key0 = j * kTile;
             if (a.mask)
             {
@@ -312,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < 128; ++k)
                     if (key0 + k >= a.kv_len) x[k] = -INFINITY;
             }
-            // row max over 8 independent chains (a single 127-long chain is latency bound)
+            // row max over 8 independent chains
             float mx[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) mx[k] = x[k];
@@ -320,10 +318,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 8; k < 128; ++k) mx[k & 7] = fmaxf(mx[k & 7], x[k]);
             const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            // PV_g(j-1) has read P_g(j-1) (and added into O_g) before P_g(j) or a rescale may touch them
+            if (j > 0)
+            {
+                if (!mbar_wait(pv_done(g), (j - 1) & 1))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
             if (j == 0) m_run = tmax;
             else if (__any_sync(0xffffffffu, (tmax - m_run) * c > kRescaleLog2))
             {
-                // PV_g(j-1) is complete: its commit preceded S_g(j)'s
                 const float m_new = fmaxf(m_run, tmax);
                 const float alpha = fast_exp2((m_run - m_new) * c);
 #pragma unroll
@@ -335,34 +342,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int t = 0; t < 32; ++t) o[t] *= alpha;
                     tmem_store_32(lane_base + o_col(g) + cc * 32, o);
                 }
+                tmem_store_wait();
                 l_run *= alpha;
                 m_run = m_new;
             }
-            // exponent arguments two at a time (packed FP32x2 FFMA), four independent pair sums
+            // exponent arguments two at a time (packed FP32x2 FFMA), four independent pair sums; P row r
+            // as BF16 into the swizzled K-major tile: half h holds keys 64h..64h+63, 16-byte chunk cc of
+            // row r sits at chunk cc ^ (r & 7)
             const float2 scale2 = make_float2(c, c), neg2 = make_float2(-m_run * c, -m_run * c);
             float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
-            uint32_t pk[64];
 #pragma unroll
-            for (int k = 0; k < 128; k += 2)
+            for (int k8 = 0; k8 < 128; k8 += 8)
             {
-                const float2 arg = __ffma2_rn(make_float2(x[k], x[k + 1]), scale2, neg2);
-                const float e0 = fast_exp2(arg.x), e1 = fast_exp2(arg.y);
-                sum2[(k >> 1) & 3] = __fadd2_rn(sum2[(k >> 1) & 3], make_float2(e0, e1));
-                pk[k / 2] = pack2(e0, e1);
+                uint32_t w[4];
+#pragma unroll
+                for (int t = 0; t < 8; t += 2)
+                {
+                    const float2 arg = __ffma2_rn(make_float2(x[k8 + t], x[k8 + t + 1]), scale2, neg2);
+                    const float e0 = fast_exp2(arg.x), e1 = fast_exp2(arg.y);
+                    sum2[t >> 1] = __fadd2_rn(sum2[t >> 1], make_float2(e0, e1));
+                    w[t >> 1] = pack2(e0, e1);
+                }
+                const int h = k8 >> 6, cc = (k8 & 63) >> 3;
+                st_shared_v4(s_p(g) + h * kHalfBytes + r * 128 + ((cc ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
             }
             const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
             const float2 s4 = __fadd2_rn(s01, s23);
             l_run += s4.x + s4.y;
-            // P_g(j) over the first 64 columns of S_g (the MMA reads it as BF16 pairs, key 2i low)
-            tmem_store_32u(lane_base + s_col(g), pk);
-            tmem_store_32u(lane_base + s_col(g) + 32, pk + 32);
-            tmem_store_wait();
+            fence_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full(g));
         }
-        if (ok && !mbar_wait(o_full(g), 0)) ok = false;
+        if (ok && !mbar_wait(pv_done(g), (tiles - 1) & 1)) ok = false;
         if (!ok)
         {
             if (a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashSoftmaxTimeout);
