@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <random>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -777,6 +778,17 @@ extern "C" int ernie_cuda_dit_constants(const float *freq64, int w, int h, int v
         }
     }
     for (int k = 0; k < length; ++k) mask_out[k] = k >= image + valid ? -1e30f : 0.f;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out)
+{
+    if (!out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!latent_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Invalid latent shape");
+    std::mt19937 engine(seed);
+    std::normal_distribution<float> normal(0.f, 1.f);
+    const size_t count = size_t(kLatent) * width * height;
+    for (size_t i = 0; i < count; ++i) out[i] = normal(engine);
     return ERNIE_CUDA_OK;
 }
 

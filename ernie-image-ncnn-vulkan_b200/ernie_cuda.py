@@ -107,6 +107,7 @@ SIGNATURES = {
     "ernie_cuda_session_profile": (I, [P, I, I, ctypes.POINTER(F)]),
     "ernie_cuda_session_launches_per_step": (I, [P, ctypes.POINTER(I)]),
     "ernie_cuda_finite_latent_noalloc": (I, [P, P, I, I, ctypes.POINTER(I)]),
+    "ernie_cuda_initial_noise": (I, [ctypes.c_uint, I, I, P]),
     "ernie_cuda_session_create_sp": (I, [P, ctypes.POINTER(Shape), I, I, I, ctypes.POINTER(P)]),
     "ernie_cuda_sp_handle": (I, [P, P]),
     "ernie_cuda_sp_connect": (I, [P, P]),
@@ -412,6 +413,13 @@ class Model:
         b = U64(0)
         check(lib().ernie_cuda_model_bytes(self.handle, ctypes.byref(b)))
         return b.value
+
+
+def initial_noise(seed, width, height):
+    """The reference pipeline's initial latent noise [128, height, width] (mt19937 + normal_distribution)."""
+    out = np.empty((128, height, width), np.float32)
+    check(lib().ernie_cuda_initial_noise(seed, width, height, ptr(out)))
+    return out
 
 
 SP_HANDLE_BYTES = 64

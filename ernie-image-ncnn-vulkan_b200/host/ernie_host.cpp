@@ -4,8 +4,11 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <filesystem>
+#include <fstream>
 #include <limits>
 #include <new>
+#include <random>
 #include <utility>
 
 namespace ernie
@@ -783,4 +786,103 @@ Tensor CudaDenoiseBackend::latent()
 }
 
 void CudaDenoiseBackend::end_attempt() { session_.reset(); }
+
+// ---- pipeline DiT stage -----------------------------------------------------------------------
+Tensor read_tensor(const std::string &path, int w, int h, int c)
+{
+    require(w >= 1 && h >= 1 && c >= 1, "Invalid tensor shape");
+    std::error_code ec;
+    const auto bytes = std::filesystem::file_size(path, ec);
+    if (ec || bytes != size_t(w) * h * c * 4) throw std::runtime_error("Wrong tensor size: " + path);
+    Tensor out = c > 1 ? Tensor(w, h, c) : h > 1 ? Tensor(w, h) : Tensor(w);
+    std::ifstream file(path, std::ios::binary);
+    if (!file.read(reinterpret_cast<char *>(out.ptr()), std::streamsize(out.total() * 4)))
+        throw std::runtime_error("Tensor read failed");
+    for (float v : out.data)
+        if (!std::isfinite(v)) throw std::runtime_error("Tensor contains non-finite values: " + path);
+    return out;
+}
+
+void write_tensor(const std::string &path, const Tensor &value)
+{
+    if (std::filesystem::exists(path)) throw std::runtime_error("Trace file exists");
+    if (value.empty()) throw std::runtime_error("Trace tensor must be FP32");
+    std::ofstream out(path, std::ios::binary);
+    out.write(reinterpret_cast<const char *>(value.ptr()), std::streamsize(value.total() * 4));
+    if (!out) throw std::runtime_error("Trace write failed");
+}
+
+std::string numbered(const std::string &stem, int index)
+{
+    return stem + (index < 10 ? "0" : "") + std::to_string(index);
+}
+
+Tensor initial_noise(int width, int height, uint32_t seed)
+{
+    require(width >= 1 && height >= 1 && width <= 256 && height <= 256, "Invalid latent shape");
+    Tensor noise(width, height, 128);
+    std::mt19937 engine(seed);
+    std::normal_distribution<float> normal(0.f, 1.f);
+    for (float &v : noise.data) v = normal(engine); // channel-major: channel c holds values [c*w*h, (c+1)*w*h)
+    return noise;
+}
+
+DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucket, const std::vector<float> &frequencies,
+                             const DitStageRequest &r, const std::function<void(const DitStageProgress &)> &notify)
+{
+    require(r.width % 16 == 0 && r.height % 16 == 0 && r.width >= 16 && r.height >= 16 && r.width <= 4096 &&
+                r.height <= 4096,
+            "Width and height must be multiples of 16 in [16,4096]");
+    require(r.steps >= 1 && r.steps <= 1000, "Steps must be in [1,1000]");
+    require(text.dims == 2 && text.w == 3072 && text.h >= 1 && text.h <= text_bucket, "Text must be [T][3072], T <= bucket");
+    require(r.oom_retries <= 3, "oom_retries must be in [0,3]");
+    const int w = r.width / 16, h = r.height / 16, valid = text.h;
+    const auto rotary = dit_constants(frequencies, w, h, valid, text_bucket);
+    std::vector<Tensor> constants{pad_text(text, text_bucket), rotary[0], rotary[1], rotary[2]};
+    const Tensor initial = r.latent.empty() ? initial_noise(w, h, r.seed) : read_tensor(r.latent, w, h, 128);
+    DitStageResult result;
+    auto step_done = [&](int i, double seconds) {
+        if (notify) notify({"denoise", i + 1, r.steps, seconds});
+    };
+    auto recover = [&](const Tensor &from, int start) {
+        CudaDenoiseBackend backend(model, w, h, text_bucket, valid, r.precision, constants);
+        backend.steps = r.steps;
+        CudaDenoiseSettings settings;
+        settings.retries = r.oom_retries;
+        CudaDenoiseObservers observers;
+        observers.step = [&](size_t i, const Tensor &prediction, const Tensor &latent, const DenoiseStepStats &st) {
+            if (!r.trace.empty())
+            {
+                write_tensor((std::filesystem::path(r.trace) / ("prediction-" + std::to_string(i) + ".f32")).string(),
+                             prediction);
+                write_tensor((std::filesystem::path(r.trace) / ("step-" + std::to_string(i) + ".f32")).string(), latent);
+            }
+            result.steps.push_back(st);
+            step_done(int(i), st.elapsed_seconds);
+        };
+        observers.retry = [&](unsigned retry, int, int, const std::string &) {
+            if (notify) notify({"memory-recovery", int(retry), int(r.oom_retries), 0});
+        };
+        return denoise_with_recovery(backend, from, r.steps, start, settings, result.recovery, observers);
+    };
+    if (!r.trace.empty())
+    {
+        require(std::filesystem::is_directory(r.trace), "Trace folder does not exist");
+        result.latent = recover(initial, 0);
+        return result;
+    }
+    try
+    {
+        DenoiseSession session(model, w, h, text_bucket, valid, r.precision);
+        session.set_constants(constants);
+        result.latent = denoise(session, initial, r.steps, result.steps);
+        for (size_t i = 0; i < result.steps.size(); ++i) step_done(int(i), result.steps[i].elapsed_seconds);
+    }
+    catch (const GpuAllocationError &)
+    {
+        result.steps.clear();
+        result.latent = recover(initial, 0);
+    }
+    return result;
+}
 } // namespace ernie

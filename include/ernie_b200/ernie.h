@@ -368,4 +368,43 @@ class CudaDenoiseBackend : public DenoiseBackend
     std::vector<Tensor> constants_;
     std::unique_ptr<DenoiseSession> session_;
 };
+
+// ---- the pipeline's DiT stage (src/pipeline.cpp:164-300 and :513-531, src/tensor_io.h:8-10) -------
+// Raw little-endian FP32 files, channel after channel. read_tensor checks the byte size and that every
+// value is finite; write_tensor refuses to overwrite ("Trace file exists").
+Tensor read_tensor(const std::string &path, int w, int h = 1, int c = 1);
+void write_tensor(const std::string &path, const Tensor &value);
+std::string numbered(const std::string &stem, int index); // "block-07"
+// Initial noise of a request without a latent file: std::mt19937(seed) feeding
+// std::normal_distribution<float>(0, 1), channel after channel, as src/pipeline.cpp:520-531 draws it.
+Tensor initial_noise(int width, int height, uint32_t seed);
+struct DitStageRequest // the GenerationRequest fields the DiT stage reads (include/ernie/pipeline.h)
+{
+    int width = 1024, height = 1024; // pixels, multiples of 16 (the packed latent is width/16 x height/16)
+    int steps = 8;
+    uint32_t seed = 0;
+    std::string latent;              // optional initial latent file [128][height/16][width/16]
+    std::string trace;               // optional existing folder: prediction-i.f32 and step-i.f32 per step
+    Precision precision = Precision::BF16;
+    unsigned oom_retries = 3;
+};
+struct DitStageProgress // the "denoise" / "memory-recovery" notifications of src/pipeline.cpp:180-186, 259
+{
+    std::string stage;
+    int step = 0, total = 0;
+    double seconds = 0;
+};
+struct DitStageResult
+{
+    Tensor latent;                        // [128][h][w] after the last step
+    std::vector<DenoiseStepStats> steps;  // executed steps
+    CudaDenoiseStats recovery;
+};
+// text: the encoder's [T][3072] rows for the T prompt tokens, padded to `text_bucket` slots; frequencies:
+// the 64 RoPE inverse frequencies (empty = the built-in table). Without a trace the whole schedule runs
+// as one CUDA graph, and an allocation failure falls back to denoise_with_recovery from the initial
+// latent; with a trace every step goes through denoise_with_recovery and its tensors are written.
+DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucket, const std::vector<float> &frequencies,
+                             const DitStageRequest &request,
+                             const std::function<void(const DitStageProgress &)> &notify = {});
 } // namespace ernie

@@ -191,6 +191,10 @@ int ernie_cuda_session_denoise_device(ernie_cuda_session *session, int steps, in
 int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial, float *final_latent, int steps,
                                int start_step, int end_step, int schedule, float *predictions, int *failed_step);
 
+/* Initial noise of a request without a latent file (src/pipeline.cpp:520-531): std::mt19937(seed) feeding
+   std::normal_distribution<float>(0, 1), channel after channel, into out [128][height][width]. Host-only. */
+int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out);
+
 /* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 members, BF16) ---------------
    Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every member
    holds the full weights. Per block, the QKV GEMM's epilogue stores each head of this GPU's rows straight

@@ -1,10 +1,13 @@
 // The C++ surface on a B200: denoise through one CUDA graph equals the step-by-step observer path and
 // the recovery wrapper (allocation failure injected before step 2) bit-exactly; run_dit and layer
-// wrappers keep the reference contracts.
+// wrappers keep the reference contracts; the pipeline's DiT stage (seeded noise, constants, graph or
+// traced path) equals the same denoise built by hand and writes the reference's trace files.
 #include "ernie_b200/ernie.h"
 #include "ernie_synth.h"
 #include <cmath>
+#include <filesystem>
 #include <iostream>
+#include <unistd.h>
 
 using namespace ernie;
 
@@ -70,6 +73,50 @@ int main()
         for (float v : prediction.data) finite = finite && std::isfinite(v);
         REQUIRE(finite && prediction.total() == initial.total(), "run_dit prediction");
         REQUIRE(finite_latent(ctx, dlat), "finite_latent");
+
+        // DiT stage: 128x96 pixels -> 8x6 latent, 10 prompt tokens in a 16-slot bucket, seed 3
+        {
+            DitStageRequest req;
+            req.width = 128;
+            req.height = 96;
+            req.seed = 3;
+            const Tensor prompt = normal(3072, 10, 1, ERNIE_SYNTH_TEXT);
+            int notified = 0;
+            const DitStageResult fast =
+                run_dit_stage(model, prompt, 16, {}, req, [&](const DitStageProgress &p) { notified += p.stage == "denoise"; });
+            auto kk = dit_constants({}, 8, 6, 10, 16);
+            DenoiseSession manual(model, 8, 6, 16, 10, Precision::BF16);
+            manual.set_constants({pad_text(prompt, 16), kk[0], kk[1], kk[2]});
+            std::vector<DenoiseStepStats> mstats;
+            const Tensor by_hand = denoise(manual, initial_noise(8, 6, 3), 8, mstats);
+            REQUIRE(fast.latent.data == by_hand.data && fast.steps.size() == 8 && notified == 8,
+                    "DiT stage differs from the hand-built denoise");
+            const auto dir = std::filesystem::temp_directory_path() / ("ernie_trace_" + std::to_string(::getpid()));
+            std::filesystem::remove_all(dir);
+            std::filesystem::create_directories(dir);
+            req.trace = dir.string();
+            const DitStageResult traced = run_dit_stage(model, prompt, 16, {}, req);
+            REQUIRE(traced.latent.data == fast.latent.data, "traced DiT stage differs from the graph path");
+            bool files = true;
+            for (int i = 0; i < 8; ++i)
+                files = files && std::filesystem::file_size(dir / ("prediction-" + std::to_string(i) + ".f32")) ==
+                                     size_t(128 * 8 * 6 * 4) &&
+                        std::filesystem::file_size(dir / ("step-" + std::to_string(i) + ".f32")) == size_t(128 * 8 * 6 * 4);
+            REQUIRE(files, "trace files");
+            const Tensor last = read_tensor((dir / "step-7.f32").string(), 8, 6, 128);
+            REQUIRE(last.data == traced.latent.data, "last traced step is the result");
+            bool refused = false;
+            try
+            {
+                run_dit_stage(model, prompt, 16, {}, req);
+            }
+            catch (const std::runtime_error &e)
+            {
+                refused = std::string(e.what()).find("Trace file exists") != std::string::npos;
+            }
+            REQUIRE(refused, "existing trace files overwritten");
+            std::filesystem::remove_all(dir);
+        }
 
         Tensor x(64, 4);
         DeviceTensor dx = DeviceTensor::upload(ctx, x);

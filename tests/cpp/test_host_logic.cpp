@@ -2,15 +2,18 @@
 // mapping, weight placement decisions, weight-session admission/leases and the recovery loop with a
 // host-side fake backend. Cases follow the reference's tests/test_latent_contract.cpp,
 // tests/test_weight_placement.cpp:42-56, tests/test_weight_session.cpp:36-131 and
-// tests/test_memory_execution.cpp:298-419 (recovery_contract).
+// tests/test_memory_execution.cpp:298-419 (recovery_contract); tensor files as src/tensor_io.cpp:10-43.
 #include "ernie_b200/ernie.h"
 #include <cmath>
+#include <filesystem>
+#include <fstream>
 #include <cstdio>
 #include <cstdlib>
 #include <iostream>
 #include <memory>
 #include <new>
 #include <tuple>
+#include <unistd.h>
 
 using namespace ernie;
 
@@ -340,6 +343,33 @@ static void recovery_contract()
             "more than three retries accepted");
 }
 
+static void tensor_io_contract()
+{
+    const auto dir = std::filesystem::temp_directory_path() / ("ernie_b200_io_" + std::to_string(::getpid()));
+    std::filesystem::remove_all(dir);
+    std::filesystem::create_directories(dir);
+    const std::string path = (dir / "t.f32").string();
+    Tensor t(3, 2, 2);
+    for (size_t i = 0; i < t.total(); ++i) t[i] = float(i) - 2.5f;
+    write_tensor(path, t);
+    REQUIRE(std::filesystem::file_size(path) == 48, "raw FP32 size");
+    const Tensor back = read_tensor(path, 3, 2, 2);
+    REQUIRE(back.data == t.data && back.w == 3 && back.h == 2 && back.c == 2, "round trip");
+    REQUIRE(throws<std::runtime_error>([&] { write_tensor(path, t); }), "existing trace file overwritten");
+    REQUIRE(throws<std::runtime_error>([&] { read_tensor(path, 4, 2, 2); }), "wrong size accepted");
+    {
+        std::ofstream f((dir / "nan.f32").string(), std::ios::binary);
+        const float v[2] = {1.f, NAN};
+        f.write(reinterpret_cast<const char *>(v), sizeof(v));
+    }
+    REQUIRE(throws<std::runtime_error>([&] { read_tensor((dir / "nan.f32").string(), 2); }), "non-finite accepted");
+    REQUIRE(numbered("block-", 7) == "block-07" && numbered("block-", 35) == "block-35", "numbered");
+    std::filesystem::remove_all(dir);
+    const Tensor n1 = initial_noise(5, 4, 42), n2 = initial_noise(5, 4, 42), n3 = initial_noise(5, 4, 43);
+    REQUIRE(n1.c == 128 && n1.h == 4 && n1.w == 5 && n1.data == n2.data && n1.data != n3.data, "initial noise");
+    REQUIRE(throws<std::invalid_argument>([] { initial_noise(0, 4, 1); }), "empty latent accepted");
+}
+
 int main()
 {
     latent_contract();
@@ -348,6 +378,7 @@ int main()
     placement_contract();
     session_contract();
     recovery_contract();
+    tensor_io_contract();
     if (failures)
     {
         std::cerr << failures << " host contract failure(s)\n";
