@@ -1,0 +1,89 @@
+"""Full-depth denoise on a B200: all 36 blocks and all 8 turbo steps.
+
+* Against the CPU oracle, with the reference's per-tensor pipeline gates (tools/validate_pipeline.py:218-222),
+  on a small token count so the oracle finishes in seconds. The 36 device blocks alternate two weight sets
+  (blocks 0 and 1 of the seeded model) so the oracle needs only two sets in host memory.
+* At the C1 geometry (32x32 latent + 32 text slots, 24 valid; 1056 tokens), where the oracle would take
+  tens of minutes: BF16 mode against the FP32-exact mode within the BF16 pipeline gate, and each mode
+  repeated bit-exactly.
+"""
+import numpy as np
+import pytest
+
+import ernie_cuda as ec
+import oracle as o
+from conftest import GATES, gate
+
+pytestmark = pytest.mark.gpu
+SEED = 11
+MAT_NAMES = {"wq": o.WQ, "wk": o.WK, "wv": o.WV, "wo": o.WO, "wup": o.WUP, "wgate": o.WGATE, "wfc2": o.WFC2}
+GAMMA_NAMES = {"gamma_sa": o.GAMMA_SA, "gamma_mlp": o.GAMMA_MLP, "gamma_q": o.GAMMA_Q, "gamma_k": o.GAMMA_K}
+
+
+@pytest.fixture(scope="module")
+def deep():
+    ctx = ec.Context(0)
+    model = ec.Model(ctx, 36)
+    model.synthesize(SEED)  # heads and blocks 0, 1 as the host generator makes them
+    host = [o.BlockWeights(SEED, 0), o.BlockWeights(SEED, 1)]
+    for b in range(2, 36):
+        w = host[b % 2]
+        model.upload_block(b, {n: w.mats[t] for n, t in MAT_NAMES.items()},
+                           {n: w.gammas[t] for n, t in GAMMA_NAMES.items()})
+    yield ctx, model, [host[b % 2] for b in range(36)], o.HeadWeights(SEED)
+    model.close()
+    ctx.close()
+
+
+def case(w, h, text, valid):
+    latent = o.synth_normal(SEED, o.LATENT_STREAM, 128 * h * w).reshape(128, h, w)
+    txt = o.synth_normal(SEED, o.TEXT_STREAM, text * 3072).reshape(text, 3072)
+    txt[valid:] = 0.0
+    cos, sin, mask = o.dit_constants(w, h, valid, text)
+    return latent, txt, cos, sin, mask
+
+
+SMALL = (4, 4, 8, 6)  # w, h, text slots, valid text: 24 tokens
+
+
+@pytest.fixture(scope="module")
+def oracle_final(deep):
+    """The oracle's 8-step, 36-block result at the small shape (computed once, ~15-30 s on the host)."""
+    _, _, host_blocks, host_heads = deep
+    latent, txt, cos, sin, mask = case(*SMALL)
+    return o.denoise(host_heads, host_blocks, latent, txt, cos, sin, mask, 8)
+
+
+@pytest.mark.parametrize("precision", [ec.FP32, ec.BF16])
+def test_36_blocks_8_steps_against_oracle(deep, oracle_final, precision):
+    ctx, model, _, _ = deep
+    w, h, text, valid = SMALL
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    ref = oracle_final
+    s = ec.Session(model, w, h, text, valid, precision)
+    try:
+        s.set_conditioning(txt, cos, sin, mask)
+        got = s.denoise(latent, 8)
+    finally:
+        s.close()
+    ok, metrics = gate(ref, got, *GATES["pipeline_fp32" if precision == ec.FP32 else "pipeline_bf16"])
+    assert ok, metrics
+
+
+def test_c1_geometry_bf16_against_fp32_mode(deep):
+    ctx, model, _, _ = deep
+    w, h, text, valid = 32, 32, 32, 24
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    out = {}
+    for precision in (ec.FP32, ec.BF16):
+        s = ec.Session(model, w, h, text, valid, precision)
+        try:
+            s.set_conditioning(txt, cos, sin, mask)
+            first = s.denoise(latent, 8)
+            again = s.denoise(latent, 8)
+        finally:
+            s.close()
+        assert np.isfinite(first).all() and np.array_equal(first, again), "repeat execution must be bit-exact"
+        out[precision] = first
+    ok, metrics = gate(out[ec.FP32], out[ec.BF16], *GATES["pipeline_bf16"])
+    assert ok, metrics
