@@ -67,6 +67,7 @@ def test_36_blocks_8_steps_against_oracle(deep, oracle_final, precision):
     finally:
         s.close()
     ok, metrics = gate(ref, got, *GATES["pipeline_fp32" if precision == ec.FP32 else "pipeline_bf16"])
+    print("36 blocks x 8 steps vs oracle", "fp32" if precision == ec.FP32 else "bf16", metrics)
     assert ok, metrics
 
 
@@ -86,4 +87,5 @@ def test_c1_geometry_bf16_against_fp32_mode(deep):
         assert np.isfinite(first).all() and np.array_equal(first, again), "repeat execution must be bit-exact"
         out[precision] = first
     ok, metrics = gate(out[ec.FP32], out[ec.BF16], *GATES["pipeline_bf16"])
+    print("C1 geometry, 36 blocks x 8 steps, BF16 vs FP32-exact", metrics)
     assert ok, metrics
