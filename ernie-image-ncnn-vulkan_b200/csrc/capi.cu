@@ -275,6 +275,7 @@ extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_gemm_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_attention_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_kernels());
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_f32_kernels());
     if (e != cudaSuccess)
     {
         ernie_cuda_context_destroy(ctx);
@@ -854,7 +855,8 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
         s->latent_ld = s->image;
     }
     s->rows_pad = (s->tokens + 127) / 128 * 128;
-    const size_t T = s->tokens, P = s->rows_pad, qkv_elem = precision == ERNIE_PRECISION_FP32 ? 4 : 2;
+    // BF16 Q, K, V^T; FP32-exact mode: three BF16 planes of each
+    const size_t T = s->tokens, P = s->rows_pad, qkv_elem = precision == ERNIE_PRECISION_FP32 ? 6 : 2;
     const size_t L = size_t(kLatent) * (world > 1 ? s->shard : s->image);
     Arena arena;
     arena.add(&s->x, T * kHidden);
@@ -1128,8 +1130,8 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
         qkv.v[0] = s->v;
         qkv.rows_pad = s->rows_pad;
     }
-    qkv.qkv_fp32 = fp32;
-    qkv.v_transposed = !fp32;
+    qkv.qkv_split3 = fp32;
+    qkv.v_transposed = 1;
     qkv.gamma_q = w.gamma_q;
     qkv.gamma_k = w.gamma_k;
     qkv.cos_t = s->cos_t;
@@ -1154,26 +1156,10 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
         ERNIE_TRY(sp_barrier(s));
     }
     else if (fp32)
-    {
-        AttentionF32Args a{};
-        a.q = static_cast<const float *>(s->q);
-        a.k = static_cast<const float *>(s->k);
-        a.v = static_cast<const float *>(s->v);
-        a.mask = s->use_mask ? s->mask : nullptr;
-        a.heads = kHeads;
-        a.kv_heads = kHeads;
-        a.mask_heads = 1;
-        a.mask_rows = 1;
-        a.nq = T;
-        a.nk = T;
-        a.kv_len = s->kv_len;
-        a.width = kHeadDim;
-        a.q_head_stride = static_cast<long long>(s->rows_pad) * kHeadDim;
-        a.kv_head_stride = a.q_head_stride;
-        a.out_mode = 1;
-        a.out_split3 = s->a;
-        ERNIE_LAUNCH(launch_attention_f32(a, st), "attention");
-    }
+        ERNIE_LAUNCH(launch_flash_f32(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
+                                      static_cast<const __nv_bfloat16 *>(s->v), s->use_mask ? s->mask : nullptr, T,
+                                      s->rows_pad, s->kv_len, kHeads, s->a, s->ctx->error_flag, st),
+                     "attention");
     else
         ERNIE_LAUNCH(launch_flash_tc(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
                                      static_cast<const __nv_bfloat16 *>(s->v), s->use_mask ? s->mask : nullptr, T,

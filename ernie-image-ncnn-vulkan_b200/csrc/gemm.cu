@@ -54,6 +54,17 @@ __device__ __forceinline__ void split3(float x, __nv_bfloat16 &hi, __nv_bfloat16
     lo = __float2bfloat16_rn(r2);
 }
 
+// Plane p (0 hi, 1 mid, 2 lo) of x's three-BF16 split (x = hi + mid + lo to 24 significant bits); with
+// one plane, plain BF16 rounding.
+__device__ __forceinline__ float split_plane(float x, int p)
+{
+    const float hi = __bfloat162float(__float2bfloat16_rn(x));
+    if (p == 0) return hi;
+    const float r1 = x - hi, mid = __bfloat162float(__float2bfloat16_rn(r1));
+    if (p == 1) return mid;
+    return __bfloat162float(__float2bfloat16_rn(r1 - mid));
+}
+
 __device__ __forceinline__ void store_bf16x8(__nv_bfloat16 *dst, const float *v)
 {
     __align__(16) __nv_bfloat162 packed[4];
@@ -181,20 +192,24 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
         for (int d = 0; d < kMaxDest; ++d)
             if (d == dest) dst_base = part == 0 ? a.q[d] : part == 1 ? a.k[d] : a.v[d];
         const uint32_t tcol = e.taddr + hh * 128;
-        if (part == 2 && !a.qkv_fp32 && a.v_transposed)
+        const int planes = a.qkv_split3 ? 3 : 1;
+        const size_t plane_stride = static_cast<size_t>(a.heads_per_dest) * a.rows_pad * kHeadDim;
+        if (part == 2 && a.v_transposed)
         {
-            // stage [64 dims][40] then write 64-byte token runs of V^T [head][dim][token]
-            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
+            // stage [64 dims][40] then write 64-byte token runs of V^T [head][dim][token], per plane
 #pragma unroll 1
-            for (int half = 0; half < 2; ++half)
+            for (int pl = 0; pl < planes * 2; ++pl)
             {
+                const int plane = pl >> 1, half = pl & 1;
+                __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) + plane * plane_stride;
 #pragma unroll
                 for (int c = 0; c < 2; ++c)
                 {
                     float chunk[32];
                     tmem_load_32(tcol + half * 64 + c * 32, chunk);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) st[(c * 32 + j) * 40 + e.lane] = __float2bfloat16_rn(chunk[j]);
+                    for (int j = 0; j < 32; ++j)
+                        st[(c * 32 + j) * 40 + e.lane] = __float2bfloat16_rn(planes == 3 ? split_plane(chunk[j], plane) : chunk[j]);
                 }
                 __syncwarp();
 #pragma unroll
@@ -257,39 +272,37 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
                     }
                 }
             }
-            if (a.qkv_fp32)
+#pragma unroll 1
+            for (int plane = 0; plane < planes; ++plane)
             {
-                if (valid && row < row_limit)
+                // stage [32 rows][72]: columns 0..31 = lo, 32..63 = hi; then 64-byte row segments
+                float pv[32];
+#pragma unroll
+                for (int half = 0; half < 2; ++half)
                 {
-                    float *dst = static_cast<float *>(dst_base) + (dst_row + row) * kHeadDim;
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
+                    for (int j = 0; j < 32; ++j)
                     {
-                        store_f32x4(dst + c * 32 + j, lo + j);
-                        store_f32x4(dst + 64 + c * 32 + j, hi + j);
+                        const float x = half ? hi[j] : lo[j];
+                        pv[j] = planes == 3 ? split_plane(x, plane) : x;
                     }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        *reinterpret_cast<uint4 *>(st + e.lane * 72 + half * 32 + j * 8) = pack_bf16x8(pv + j * 8);
                 }
-                continue;
-            }
-            // stage [32 rows][72]: columns 0..31 = lo, 32..63 = hi; then 64-byte row segments
+                __syncwarp();
+                __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) + plane * plane_stride;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-            {
-                *reinterpret_cast<uint4 *>(st + e.lane * 72 + j * 8) = pack_bf16x8(lo + j * 8);
-                *reinterpret_cast<uint4 *>(st + e.lane * 72 + 32 + j * 8) = pack_bf16x8(hi + j * 8);
+                for (int p = 0; p < 8; ++p)
+                {
+                    const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
+                    const int dim = (j < 4 ? 0 : 64) + c * 32 + (j & 3) * 8;
+                    if (row_g < e.m && row_g < row_limit)
+                        *reinterpret_cast<uint4 *>(dst + (dst_row + row_g) * kHeadDim + dim) =
+                            *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
+                }
+                __syncwarp();
             }
-            __syncwarp();
-            __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base);
-#pragma unroll
-            for (int p = 0; p < 8; ++p)
-            {
-                const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
-                const int dim = (j < 4 ? 0 : 64) + c * 32 + (j & 3) * 8;
-                if (row_g < e.m && row_g < row_limit)
-                    *reinterpret_cast<uint4 *>(dst + (dst_row + row_g) * kHeadDim + dim) =
-                        *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
-            }
-            __syncwarp();
         }
     }
 }

@@ -39,8 +39,9 @@ struct GemmEpilogueArgs
     int heads_per_dest = 32;
     int row_offset = 0, row_limit = 0;
     int rows_pad = 0;
-    int qkv_fp32 = 0;
-    int v_transposed = 0; // BF16 mode: V written as [heads][128][rows_pad] for the tcgen05 attention
+    int qkv_split3 = 0;   // FP32-exact mode: each of Q, K, V^T as three BF16 planes (hi, mid, lo), plane
+                          // p at element offset p * heads_per_dest * rows_pad * 128
+    int v_transposed = 0; // V written as [heads][128][rows_pad] (per plane) for the tcgen05 attention
     const float *gamma_q = nullptr, *gamma_k = nullptr; // [128]
     const float *cos_t = nullptr, *sin_t = nullptr;     // [rows][128]
     // Geglu: BF16 [rows][ffn] or, when split3, hi/mid/lo BF16 planes at column offsets 0, ffn, 2*ffn
@@ -119,6 +120,12 @@ struct PeerPut
 };
 int launch_peer_put(const void *src, size_t bytes, const PeerPut &put, cudaStream_t stream);
 int prepare_flash_kernels();
+// FP32-exact attention on the tensor cores: q3, k3 = three BF16 planes [3][heads][rows_pad][128], vt3 =
+// [3][heads][128][rows_pad]; out_split3 = token-major [rows][3 * heads * 128] planes (hi, mid, lo).
+int launch_flash_f32(const __nv_bfloat16 *q3, const __nv_bfloat16 *k3, const __nv_bfloat16 *vt3, const float *mask,
+                     int rows, int rows_pad, int kv_len, int heads, __nv_bfloat16 *out_split3, int *error_flag,
+                     cudaStream_t stream);
+int prepare_flash_f32_kernels();
 
 // FP32 attention with FP64 softmax accumulation. q [heads][q_stride rows][width] (head stride
 // q_head_stride elements), k/v [kv_heads][...]; mask [mask_heads][mask_rows][nk] additive (nullable).
