@@ -945,7 +945,8 @@ int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
         !make_map(&map_b, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k_b), BN))
         return cudaErrorInvalidValue;
     const int k_blocks = k_b * splits / BK;
-    const int group = k_blocks % 2 == 0 ? 2 : 1; // promotion every 128 (or 64) products
+    // promotion every 256 products (fewer if K allows no multiple of 4 k-blocks)
+    const int group = k_blocks % 4 == 0 ? 4 : k_blocks % 2 == 0 ? 2 : 1;
     const int tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     gemm_kernel<BN, EPI, PROMOTE><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, group,

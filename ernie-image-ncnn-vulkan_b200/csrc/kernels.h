@@ -61,7 +61,7 @@ struct GemmEpilogueArgs
 // C[M, N] = A[M, K_a] * B[N, K_b]^T with BF16 operands and FP32 accumulation on tcgen05.
 // K_a = splits * K_b: in FP32-exact mode A holds `splits` BF16 planes (hi, mid, lo) side by side
 // and every plane multiplies the same exact-BF16 weights. `promote` (block_n 128 only) restarts
-// the tensor-core accumulator every 128 products and sums the partials in FP32 registers.
+// the tensor-core accumulator every 256 products and sums the partials in FP32 registers.
 // Geglu weights are [up; gate] interleaved in 64-row groups. Returns a cudaError_t.
 int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, int k_b, int splits, int block_n,
                 Epilogue epilogue, const GemmEpilogueArgs &args, int num_sms, cudaStream_t stream,
