@@ -827,6 +827,58 @@ Tensor initial_noise(int width, int height, uint32_t seed)
     return noise;
 }
 
+Img2ImgStart make_img2img_start(const Tensor &encoded, const Tensor &saved_noise, const FlowSchedule &schedule,
+                                float strength, int threads)
+{
+    require(std::isfinite(strength) && strength >= 0.f && strength <= 1.f && threads >= 1 && threads <= 256,
+            "Img2img requires strength in [0,1] and threads in [1,256]");
+    const size_t count = schedule.timesteps.size();
+    require(count >= 1 && count <= 1000 && schedule.sigmas.size() == count + 1 && schedule.sigmas.front() == 1.f &&
+                schedule.sigmas.back() == 0.f,
+            "Invalid img2img flow schedule");
+    for (size_t i = 0; i < count; ++i)
+        require(std::isfinite(schedule.sigmas[i]) && std::isfinite(schedule.timesteps[i]) &&
+                    schedule.sigmas[i] > schedule.sigmas[i + 1] && schedule.sigmas[i] >= 0.f && schedule.sigmas[i] <= 1.f,
+                "Img2img flow schedule must descend from one to zero");
+    auto finite = [](const Tensor &t) {
+        if (t.empty() || t.dims != 3 || t.c != 128) return false;
+        for (float v : t.data)
+            if (!std::isfinite(v)) return false;
+        return true;
+    };
+    require(finite(encoded), "Encoded img2img latent must be finite");
+    Img2ImgStart result;
+    result.start_step = int(count);
+    if (strength == 0.f)
+    {
+        result.latent = encoded;
+        return result;
+    }
+    require(finite(saved_noise) && saved_noise.w == encoded.w && saved_noise.h == encoded.h,
+            "Img2img noise must be finite and match the encoded shape");
+    const float scaled = float(count) * strength;
+    result.denoise_steps = std::min(int(count), std::max(1, int(std::floor(scaled + .5f))));
+    result.start_step = int(count) - result.denoise_steps;
+    result.sigma = schedule.sigmas[size_t(result.start_step)];
+    if (result.sigma == 1.f)
+    {
+        result.latent = saved_noise;
+        return result;
+    }
+    result.latent = Tensor(encoded.w, encoded.h, 128);
+    const float retained = 1.f - result.sigma;
+    for (size_t i = 0; i < encoded.total(); ++i)
+    {
+        // two roundings and a third for the sum, no contraction (this file builds with -ffp-contract=off)
+        const float weighted_noise = result.sigma * saved_noise[i];
+        const float weighted_image = retained * encoded[i];
+        result.latent[i] = weighted_noise + weighted_image;
+    }
+    for (float v : result.latent.data)
+        if (!std::isfinite(v)) throw std::runtime_error("Non-finite img2img initial latent");
+    return result;
+}
+
 DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucket, const std::vector<float> &frequencies,
                              const DitStageRequest &r, const std::function<void(const DitStageProgress &)> &notify)
 {
@@ -839,10 +891,20 @@ DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucke
     const int w = r.width / 16, h = r.height / 16, valid = text.h;
     const auto rotary = dit_constants(frequencies, w, h, valid, text_bucket);
     std::vector<Tensor> constants{pad_text(text, text_bucket), rotary[0], rotary[1], rotary[2]};
-    const Tensor initial = r.latent.empty() ? initial_noise(w, h, r.seed) : read_tensor(r.latent, w, h, 128);
+    const Tensor noise = r.latent.empty() ? initial_noise(w, h, r.seed) : read_tensor(r.latent, w, h, 128);
     DitStageResult result;
+    Tensor initial = noise;
+    if (!r.encoded.empty())
+    {
+        // img2img (src/pipeline.cpp:533-538): the start latent and step from the encoded image
+        require(r.encoded.w == w && r.encoded.h == h, "Encoded image latent does not match the request size");
+        Img2ImgStart start = make_img2img_start(r.encoded, noise, FlowSchedule::turbo(r.steps), r.strength);
+        initial = std::move(start.latent);
+        result.start_step = start.start_step;
+    }
+    // progress counts the executed steps (src/pipeline.cpp:180-186): step i is number i - start + 1
     auto step_done = [&](int i, double seconds) {
-        if (notify) notify({"denoise", i + 1, r.steps, seconds});
+        if (notify) notify({"denoise", i - result.start_step + 1, r.steps - result.start_step, seconds});
     };
     auto recover = [&](const Tensor &from, int start) {
         CudaDenoiseBackend backend(model, w, h, text_bucket, valid, r.precision, constants);
@@ -865,23 +927,29 @@ DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucke
         };
         return denoise_with_recovery(backend, from, r.steps, start, settings, result.recovery, observers);
     };
+    if (result.start_step >= r.steps)
+    {
+        result.latent = initial; // strength 0: the reconstruction latent, no step runs
+        return result;
+    }
     if (!r.trace.empty())
     {
         require(std::filesystem::is_directory(r.trace), "Trace folder does not exist");
-        result.latent = recover(initial, 0);
+        result.latent = recover(initial, result.start_step);
         return result;
     }
     try
     {
         DenoiseSession session(model, w, h, text_bucket, valid, r.precision);
         session.set_constants(constants);
-        result.latent = denoise(session, initial, r.steps, result.steps);
-        for (size_t i = 0; i < result.steps.size(); ++i) step_done(int(i), result.steps[i].elapsed_seconds);
+        result.latent = denoise(session, initial, r.steps, result.steps, {}, result.start_step);
+        for (size_t i = 0; i < result.steps.size(); ++i)
+            step_done(result.start_step + int(i), result.steps[i].elapsed_seconds);
     }
     catch (const GpuAllocationError &)
     {
         result.steps.clear();
-        result.latent = recover(initial, 0);
+        result.latent = recover(initial, result.start_step);
     }
     return result;
 }

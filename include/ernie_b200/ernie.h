@@ -378,6 +378,23 @@ std::string numbered(const std::string &stem, int index); // "block-07"
 // Initial noise of a request without a latent file: std::mt19937(seed) feeding
 // std::normal_distribution<float>(0, 1), channel after channel, as src/pipeline.cpp:520-531 draws it.
 Tensor initial_noise(int width, int height, uint32_t seed);
+// img2img start (src/img2img.h:8-21): the latent and step to begin denoising an encoded image from.
+// `encoded` is the patchified, BN-normalised mean posterior [128][h][w]; strength 0 returns it unchanged
+// (start_step = schedule length) without using the noise; otherwise denoise_steps = clamp(round-half-up
+// (steps * strength), 1, steps), start_step = steps - denoise_steps and the latent is
+// sigma * noise + (1 - sigma) * encoded at sigma = sigmas[start_step] (the noise itself when sigma is 1).
+// std::invalid_argument for strength outside [0,1], threads outside [1,256], a malformed schedule, or a
+// non-finite / mismatched encoded latent or noise.
+struct Img2ImgStart
+{
+    Tensor latent; // independent storage, never aliases the inputs
+    int start_step = 0;
+    int denoise_steps = 0;
+    float sigma = 0.f;
+};
+Img2ImgStart make_img2img_start(const Tensor &encoded, const Tensor &saved_noise, const FlowSchedule &schedule,
+                                float strength, int threads = 4);
+
 struct DitStageRequest // the GenerationRequest fields the DiT stage reads (include/ernie/pipeline.h)
 {
     int width = 1024, height = 1024; // pixels, multiples of 16 (the packed latent is width/16 x height/16)
@@ -387,6 +404,8 @@ struct DitStageRequest // the GenerationRequest fields the DiT stage reads (incl
     std::string trace;               // optional existing folder: prediction-i.f32 and step-i.f32 per step
     Precision precision = Precision::BF16;
     unsigned oom_retries = 3;
+    Tensor encoded;                  // img2img: the encoded image latent [128][h][w] (empty: text to image)
+    float strength = 1.f;            // img2img strength
 };
 struct DitStageProgress // the "denoise" / "memory-recovery" notifications of src/pipeline.cpp:180-186, 259
 {
@@ -399,6 +418,7 @@ struct DitStageResult
     Tensor latent;                        // [128][h][w] after the last step
     std::vector<DenoiseStepStats> steps;  // executed steps
     CudaDenoiseStats recovery;
+    int start_step = 0;                   // first executed step (img2img)
 };
 // text: the encoder's [T][3072] rows for the T prompt tokens, padded to `text_bucket` slots; frequencies:
 // the 64 RoPE inverse frequencies (empty = the built-in table). Without a trace the whole schedule runs

@@ -116,6 +116,21 @@ int main()
             }
             REQUIRE(refused, "existing trace files overwritten");
             std::filesystem::remove_all(dir);
+
+            // img2img: strength 0.5 starts at step 4 from sigma*noise + (1-sigma)*encoded
+            req.trace.clear();
+            req.encoded = normal(8, 6, 128, ERNIE_SYNTH_HIDDEN);
+            req.strength = 0.5f;
+            const DitStageResult i2i = run_dit_stage(model, prompt, 16, {}, req);
+            const Img2ImgStart start = make_img2img_start(req.encoded, initial_noise(8, 6, 3), FlowSchedule::turbo(8), 0.5f);
+            std::vector<DenoiseStepStats> istats;
+            const Tensor i2i_hand = denoise(manual, start.latent, 8, istats, {}, start.start_step);
+            REQUIRE(i2i.start_step == 4 && start.start_step == 4 && i2i.steps.size() == 4 && i2i.latent.data == i2i_hand.data,
+                    "img2img DiT stage");
+            req.strength = 0.f;
+            const DitStageResult recon = run_dit_stage(model, prompt, 16, {}, req);
+            REQUIRE(recon.start_step == 8 && recon.steps.empty() && recon.latent.data == req.encoded.data,
+                    "strength 0 ran a step");
         }
 
         Tensor x(64, 4);

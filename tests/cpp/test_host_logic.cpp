@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <iostream>
+#include <limits>
 #include <memory>
 #include <new>
 #include <tuple>
@@ -370,6 +371,51 @@ static void tensor_io_contract()
     REQUIRE(throws<std::invalid_argument>([] { initial_noise(0, 4, 1); }), "empty latent accepted");
 }
 
+// tests/test_img2img_contract.cpp: endpoints, interpolation, round-half-up step selection, rejections
+static void img2img_contract()
+{
+    const FlowSchedule schedule = FlowSchedule::turbo(8);
+    Tensor encoded(2, 3, 128), noise(2, 3, 128);
+    for (auto &v : encoded.data) v = 2.f;
+    for (auto &v : noise.data) v = -1.f;
+    const Img2ImgStart zero = make_img2img_start(encoded, Tensor(), schedule, 0.f, 1);
+    REQUIRE(zero.start_step == 8 && zero.denoise_steps == 0 && zero.sigma == 0.f && zero.latent.data == encoded.data,
+            "strength zero");
+    const Img2ImgStart one = make_img2img_start(encoded, noise, schedule, 1.f, 1);
+    REQUIRE(one.start_step == 0 && one.denoise_steps == 8 && one.sigma == 1.f && one.latent.data == noise.data,
+            "strength one");
+    for (const float fraction : {.25f, .5f, .75f})
+    {
+        const int count = int(fraction * 8);
+        const Img2ImgStart start = make_img2img_start(encoded, noise, schedule, fraction, 1);
+        const float expected = -start.sigma + (1.f - start.sigma) * 2.f;
+        bool same = start.denoise_steps == count && start.start_step == 8 - count;
+        for (float v : start.latent.data) same = same && v == expected;
+        REQUIRE(same, "strength step selection / interpolation");
+    }
+    REQUIRE(make_img2img_start(encoded, noise, schedule, .3125f, 1).denoise_steps == 3, "half step rounds up");
+    REQUIRE(make_img2img_start(encoded, noise, schedule, std::numeric_limits<float>::min(), 1).denoise_steps == 1,
+            "positive strength skipped all steps");
+    for (const float bad : {-1.f, 1.01f, INFINITY, NAN})
+        REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, noise, schedule, bad); }),
+                "bad strength accepted");
+    REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, noise, schedule, .5f, 0); }),
+            "zero threads accepted");
+    REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, Tensor(1, 1, 128), schedule, .5f); }),
+            "mismatched noise accepted");
+    FlowSchedule malformed = schedule;
+    malformed.sigmas[4] = NAN;
+    REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, noise, malformed, .5f); }),
+            "NaN sigma accepted");
+    malformed = schedule;
+    malformed.timesteps.pop_back();
+    REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, noise, malformed, .5f); }),
+            "short schedule accepted");
+    noise[6] = NAN; // channel 1, element 0
+    REQUIRE(throws<std::invalid_argument>([&] { make_img2img_start(encoded, noise, schedule, .5f); }),
+            "NaN noise accepted");
+}
+
 int main()
 {
     latent_contract();
@@ -379,6 +425,7 @@ int main()
     session_contract();
     recovery_contract();
     tensor_io_contract();
+    img2img_contract();
     if (failures)
     {
         std::cerr << failures << " host contract failure(s)\n";
