@@ -1511,8 +1511,9 @@ extern "C" int ernie_cuda_session_launches_per_step(ernie_cuda_session *s, int *
 {
     if (!s || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
     // input head: latent transpose + x_embedder GEMM + 4 GEMVs; 7 per block; output head: norm + GEMM.
-    // Sequence parallel: + V transpose and head gather per block (NCCL's own kernels not counted); a
-    // rank without image rows skips the x_embedder and output head, one without real rows all but attention.
+    // Sequence parallel: + two peer barriers per block; a member without image rows skips the latent
+    // transpose, x_embedder and output head, one without real rows everything but the attention and its
+    // barriers.
     if (s->sp_world > 1)
     {
         const int per_block = s->real_local > 0 ? 9 : 3;
