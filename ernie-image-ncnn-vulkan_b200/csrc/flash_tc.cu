@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int tiles = (a.kv_len + kTile - 1) / kTile;
+    // the second query tile of the last CTA of a head may hold no row at all: then only tile A runs
+    const int groups = q0 + kTile < a.rows ? 2 : 1;
 
     if (threadIdx.x == 0)
     {
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 {
                     tc_fence_after();
                     issue_s(0, 0);
-                    issue_s(1, 0);
+                    if (groups > 1) issue_s(1, 0);
                     umma_commit(k_empty(0));
                 }
                 for (int j = 0; j < tiles && ok; ++j)
@@ -231,8 +233,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = false;
                             break;
                         }
-                        for (int g = 0; g < 2 && ok; ++g)
+#pragma unroll
+                        for (int g = 0; g < 2; ++g)
                         {
+                            if (g >= groups || !ok) continue;
                             if (!mbar_wait(s_free(g), j & 1))
                             {
                                 ok = false;
@@ -249,8 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    for (int g = 0; g < 2 && ok; ++g)
+#pragma unroll
+                    for (int g = 0; g < 2; ++g)
                     {
+                        if (g >= groups || !ok) continue;
                         if (!mbar_wait(p_full(g), j & 1))
                         {
                             ok = false;
@@ -274,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
         const int g = (warp - 4) >> 2;    // 0: tile A (warps 4..7), 1: tile B (warps 8..11)
+        const bool active = g < groups;
         const int quarter = warp & 3;     // TMEM lane quarter this warp may access
         const int r = quarter * 32 + lane; // row within the query tile == TMEM lane
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -283,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr float kRescaleLog2 = 8.f;              // rescale O only when the max grows by 2^8
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
-        for (int j = 0; j < tiles && ok; ++j)
+        for (int j = 0; j < tiles && ok && active; ++j)
         {
             if (!mbar_wait(s_full(g), j & 1))
             {
@@ -375,12 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full(g));
         }
-        if (ok && !mbar_wait(pv_done(g), (tiles - 1) & 1)) ok = false;
+        if (ok && active && !mbar_wait(pv_done(g), (tiles - 1) & 1)) ok = false;
         if (!ok)
         {
             if (a.error_flag && lane == 0) atomicExch(a.error_flag, kErrFlashSoftmaxTimeout);
         }
-        else
+        else if (active)
         {
             tc_fence_after();
             const int row = q0 + g * kTile + r;
