@@ -1476,13 +1476,36 @@ extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent
 
 extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int iters, float *ms)
 {
-    if (!s || !ms || kernel < 0 || kernel > 9 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
+    if (!s || !ms || kernel < 0 || kernel > 16 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
     if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs set_conditioning");
     DeviceGuard guard(s->ctx->device);
     ernie_cuda_context *ctx = s->ctx;
     // launches cycle through the model's blocks so weights stream from HBM as in a real step;
     // kernel 7 = one whole block (all seven launches), kernel 8 = one full denoise step
     const int nb = s->model->num_blocks;
+    if (kernel >= 10)
+    {
+        // one part inside whole blocks: events around it in each of up to 7 consecutive blocks
+        const int part = kernel - 10, n = iters < 7 ? iters : 7;
+        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod)); // warm-up block
+        for (int i = 0; i < n; ++i)
+            for (int p = 0; p < 7; ++p)
+            {
+                if (p == part) ERNIE_CUDA(cudaEventRecord(ctx->events[2 * i], ctx->stream), "event");
+                ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p));
+                if (p == part) ERNIE_CUDA(cudaEventRecord(ctx->events[2 * i + 1], ctx->stream), "event");
+            }
+        ERNIE_CUDA(cudaEventSynchronize(ctx->events[2 * n - 1]), "event");
+        float total = 0.f;
+        for (int i = 0; i < n; ++i)
+        {
+            float each = 0.f;
+            ERNIE_CUDA(cudaEventElapsedTime(&each, ctx->events[2 * i], ctx->events[2 * i + 1]), "event");
+            total += each;
+        }
+        *ms = total / n;
+        return ernie_cuda_context_synchronize(ctx);
+    }
     if (kernel >= 8)
     {
         if (s->feature_capacity < 1 || s->deltas.empty()) return fail(ERNIE_CUDA_ERROR, "Run a denoise step first");
