@@ -1050,6 +1050,10 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
     if (last < 0) return fail(ERNIE_CUDA_ERROR, "Mask hides every key");
     for (int k = 0; k <= last; ++k)
         if (mask[k] != 0.f) general = true;
+    // the cached step graphs bake in the valid key count, whether a mask row is read and whether text
+    // rows exist; everything else they read from the buffers refilled below
+    const bool same_graphs = s->conditioned && s->kv_len == last + 1 && s->use_mask == general &&
+                             s->has_text == (text != nullptr);
     s->kv_len = last + 1;
     s->use_mask = general;
     // cos/sin rows of this session's token range (rows past the sequence stay zero)
@@ -1084,7 +1088,7 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
                      "text_proj");
     }
     ERNIE_CUDA(cudaStreamSynchronize(st), "set conditioning");
-    release_graphs(s);
+    if (!same_graphs) release_graphs(s);
     s->conditioned = true;
     return ERNIE_CUDA_OK;
 }
