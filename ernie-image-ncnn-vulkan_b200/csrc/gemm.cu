@@ -45,6 +45,21 @@ template <int BN, bool PROMOTE> struct Cfg
 
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * erfcf(-0.7071067811865475f * x); }
 
+// The BF16 path's GELU: erfc(|x|/sqrt 2) by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), the form the
+// reference's own GPU GELU evaluates (src/ernie_gelu.cpp:13-30); far below the BF16 rounding of h, and
+// about half the instructions of erfcf.
+__device__ __forceinline__ float gelu_as(float x)
+{
+    const float z = fabsf(x) * 0.7071067811865475f;
+    const float t = __frcp_rn(fmaf(0.3275911f, z, 1.f));
+    float poly = fmaf(1.061405429f, t, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    const float tail = poly * t * __expf(-z * z);
+    return x * (x >= 0.f ? 1.f - 0.5f * tail : 0.5f * tail);
+}
+
 __device__ __forceinline__ void split3(float x, __nv_bfloat16 &hi, __nv_bfloat16 &mid, __nv_bfloat16 &lo)
 {
     hi = __float2bfloat16_rn(x);
@@ -325,8 +340,16 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
             tmem_load_32(e.taddr + g * 128 + c, up);
             tmem_load_32(e.taddr + g * 128 + 64 + c, gate);
             const int f = e.n_blk * (BN / 2) + g * 64 + c;
+            if (a.h_split3) // FP32-exact mode: erfc as the reference's CPU path computes it
+            {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
+                for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_as(gate[j]);
+            }
             if (a.h_split3)
             {
                 if (!valid) continue;
