@@ -4,6 +4,7 @@
 #include "ernie_cuda.h"
 #include "ernie_synth.h"
 #include "kernels.h"
+#include "capi_internal.h"
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -13,79 +14,10 @@
 #include <vector>
 
 using namespace ernie_b200;
+using namespace ernie_b200::capi;
 
 namespace
 {
-thread_local std::string g_last_error;
-
-int fail(int code, const std::string &message)
-{
-    g_last_error = message;
-    return code;
-}
-
-int from_cuda(cudaError_t e, const char *action)
-{
-    if (e == cudaSuccess) return ERNIE_CUDA_OK;
-    const int code = e == cudaErrorMemoryAllocation ? ERNIE_CUDA_OUT_OF_MEMORY : ERNIE_CUDA_ERROR;
-    return fail(code, std::string(action) + ": " + cudaGetErrorString(e));
-}
-
-int from_launch(int e, const char *action) { return from_cuda(static_cast<cudaError_t>(e), action); }
-
-#define ERNIE_TRY(expr)                                                                                             \
-    do                                                                                                              \
-    {                                                                                                               \
-        const int _rc = (expr);                                                                                     \
-        if (_rc != ERNIE_CUDA_OK) return _rc;                                                                       \
-    } while (0)
-#define ERNIE_LAUNCH(expr, what) ERNIE_TRY(from_launch((expr), what))
-#define ERNIE_CUDA(expr, what) ERNIE_TRY(from_cuda((expr), what))
-
-size_t align256(size_t bytes) { return (bytes + 255) & ~size_t(255); }
-
-// Carves one device allocation into 256-byte aligned sub-buffers.
-struct Arena
-{
-    std::vector<std::pair<void **, size_t>> parts;
-    void *base = nullptr;
-    template <class T> void add(T **ptr, size_t count) { parts.push_back({reinterpret_cast<void **>(ptr), align256(count * sizeof(T))}); }
-    size_t bytes() const
-    {
-        size_t total = 0;
-        for (const auto &p : parts) total += p.second;
-        return total;
-    }
-    cudaError_t allocate()
-    {
-        const cudaError_t e = cudaMalloc(&base, bytes());
-        if (e != cudaSuccess) return e;
-        char *cursor = static_cast<char *>(base);
-        for (auto &p : parts)
-        {
-            *p.first = cursor;
-            cursor += p.second;
-        }
-        return cudaSuccess;
-    }
-};
-
-struct DeviceGuard
-{
-    int previous = -1;
-    explicit DeviceGuard(int device)
-    {
-        cudaGetDevice(&previous);
-        if (previous != device) cudaSetDevice(device);
-    }
-    ~DeviceGuard()
-    {
-        int now = -1;
-        cudaGetDevice(&now);
-        if (previous >= 0 && now != previous) cudaSetDevice(previous);
-    }
-};
-
 struct DevBlock
 {
     __nv_bfloat16 *wqkv = nullptr, *wo = nullptr, *wug = nullptr, *wfc2 = nullptr;
@@ -151,16 +83,6 @@ void official_frequencies(float *out)
         for (int i = 0; i < dims[a]; i += 2) out[j++] = 1.f / std::pow(256.f, float(i) / float(dims[a]));
 }
 } // namespace
-
-struct ernie_cuda_context
-{
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    int num_sms = 148;
-    int *error_flag = nullptr; // device-side protocol status of the bounded waits
-    int query_rows = 128;
-    cudaEvent_t events[16] = {};
-};
 
 struct ernie_cuda_model
 {
@@ -276,6 +198,7 @@ extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_attention_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_f32_kernels());
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_conv_kernels());
     if (e != cudaSuccess)
     {
         ernie_cuda_context_destroy(ctx);

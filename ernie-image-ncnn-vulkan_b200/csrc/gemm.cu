@@ -1039,6 +1039,8 @@ bool use_pairs(int m, int n, int splits, int block_n, bool promote, int num_sms)
 }
 } // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
 int prepare_gemm_kernels()
 {
     cudaError_t e = prepare_pairs();

@@ -151,6 +151,66 @@ int launch_residual_add(const float *a, const float *b, float *out, long long co
 int launch_rmsnorm(const float *x, const float *gamma, long long rows, int width, float eps, int centered,
                    float *out, cudaStream_t stream);
 
+// ---- VAE decoder (vae.cu) --------------------------------------------------------------------------
+// Implicit-GEMM convolution on tcgen05 (stride 1, same padding): out[pixel][c] over an NHWC BF16 operand.
+struct ConvArgs
+{
+    // geometry and schedule (set by launch_conv)
+    int height = 0, width = 0, cin = 0, taps = 0, cout = 0, products = 1, group = 1;
+    // out[pixel][c] = acc + bias[c] + resid[pixel][c], FP32 NHWC with row stride ldo (resid may equal out)
+    float *out = nullptr;
+    int ldo = 0;
+    const float *bias = nullptr;
+    const float *resid = nullptr;
+    // GroupNorm partials of the written values: stats[group][row_block] = (sum, sum of squares) in FP64
+    // over groups of cpg channels (4, 8 or 16) and row blocks of 32 pixels (conv_row_blocks of them)
+    double2 *stats = nullptr;
+    int cpg = 0;
+    // conv_out (16 output columns, valid_out used): planar FP32 [valid_out][pixels], interleaved bytes
+    // [pixels][valid_out] of clamp(x / 2 + 0.5, 0, 1) * 255 rounded to nearest even, non-finite flag
+    float *planar = nullptr;
+    uint8_t *rgb = nullptr;
+    int valid_out = 0;
+    int *nonfinite = nullptr;
+    int *error_flag = nullptr;
+};
+struct ConvLaunch
+{
+    const __nv_bfloat16 *a = nullptr; // operand [height][width][a_planes * cin] (planes side by side per pixel)
+    int a_planes = 1;                 // 3: FP32-exact mode (hi, mid, lo)
+    const __nv_bfloat16 *b = nullptr; // weights [cout_rows][b_row]: plane p, tap t, channel c at p*taps*cin + t*cin + c
+    int b_planes = 1;                 // weight planes multiplied in FP32-exact mode (1: exact-BF16 weights)
+    long long b_row = 0;
+    int cout_rows = 0;
+    int height = 0, width = 0, cin = 0, taps = 1, cout = 0; // cin a multiple of 64; cout 16 or a multiple of 128
+};
+inline int conv_row_blocks(int height, int width) { return height * ((width + 127) / 128) * 4; }
+constexpr int kSoftmaxMaxRow = 57344; // keys per attention row (the row is staged in shared memory)
+int launch_conv(const ConvLaunch &launch, const ConvArgs &epilogue, int num_sms, cudaStream_t stream);
+// scale[c] = gamma[c] / sqrt(var_g + eps), shift[c] = beta[c] - mean_g * scale[c] from the partials of 32 groups.
+int launch_gn_finalize(const double2 *stats, int row_blocks, long long count, int cpg, const float *gamma,
+                       const float *beta, float eps, float *scale, float *shift, cudaStream_t stream);
+// x * scale + shift (+ Swish), FP32 NHWC [pixels][channels] -> BF16 operand [pixels][planes * channels].
+int launch_gn_apply(const float *x, long long pixels, int channels, const float *scale, const float *shift, int silu,
+                    __nv_bfloat16 *out, int planes, cudaStream_t stream);
+// Nearest x2 of FP32 NHWC [h][w][channels] -> BF16 operand [2h][2w][planes * channels].
+int launch_upsample(const float *x, int h, int w, int channels, __nv_bfloat16 *out, int planes, cudaStream_t stream);
+// post_quant_conv (w [32][32], bias [32], FP32) of the unpacked latent [32][pixels] -> operand [pixels][planes * 64].
+int launch_vae_input(const float *unpacked, long long pixels, const float *w, const float *bias, __nv_bfloat16 *out,
+                     int planes, cudaStream_t stream);
+// softmax(S[r, :n] * scale) -> BF16 planes [rows][planes * ldp] (columns n.. zero).
+int launch_softmax_rows(const float *s, int rows, int lds, int n, float scale, __nv_bfloat16 *p, int ldp, int planes,
+                        cudaStream_t stream);
+// [n][1536] FP32 q|k|v -> Q, K [n][planes * 512] and V^T [512][planes * ldv] BF16 planes.
+int launch_attention_split(const float *qkv, int n, __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt, int ldv,
+                           int planes, cudaStream_t stream);
+// OIHW FP32 [cout][cin][taps] -> conv weights [cout_rows][3 * taps * cin_pad] (three BF16 planes).
+int launch_conv_weight_prep(const float *w, int cout, int cin, int taps, int cout_rows, int cin_pad,
+                            __nv_bfloat16 *out, int *inexact, cudaStream_t stream);
+int launch_synth_f32(uint64_t seed, uint64_t stream_id, float scale, float offset, long long count, int round_bf16,
+                     float *out, cudaStream_t stream);
+int prepare_conv_kernels();
+
 // Synthetic weights on device (ernie_synth.h protocol). rows x cols BF16 written at `out` with a
 // destination row index map: dst_row = (row / group) * group_stride + group_offset + row % group.
 int launch_synth_bf16(uint64_t seed, uint64_t stream_id, float scale, float offset, long long rows, int cols,

@@ -1,0 +1,745 @@
+// C ABI of the VAE decoder (include/ernie_cuda.h, "VAE decoder"): resident weights addressed by their
+// diffusers parameter names, a per-shape workspace, and the decoder's layer program replayed as one CUDA
+// graph. Host orchestration only; the arithmetic is in vae.cu's kernels.
+//
+// The program follows the reference's exported decoder graph (AutoencoderKLFlux2 post_quant_conv +
+// decoder as vae/head.ncnn.param lists it, run by decode_vae, src/vae.cpp:18-66): post_quant_conv 1x1
+// 32->32, conv_in 3x3 32->512, mid block (resnet, single-head self-attention over all pixels, resnet),
+// four up blocks of three resnets (512, 512, 256, 128 channels; 1x1 shortcut where the width changes)
+// with nearest x2 upsampling + conv after the first three, GroupNorm(32, eps 1e-6) + Swish, conv_out
+// 3x3 128->3. The RGB bytes follow rgb_image (src/pipeline.cpp:145-163).
+#include "capi_internal.h"
+#include "ernie_synth.h"
+#include "kernels.h"
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+using namespace ernie_b200;
+using namespace ernie_b200::capi;
+
+namespace
+{
+constexpr float kGroupNormEps = 1e-6f;
+constexpr int kGroups = 32, kMaxLatentSide = 256;
+
+struct ConvW
+{
+    int cin = 0, cout = 0, taps = 1, cin_pad = 0, cout_rows = 0;
+    __nv_bfloat16 *w = nullptr; // [cout_rows][3 * taps * cin_pad]: hi, mid, lo planes
+    float *bias = nullptr;      // [cout_rows]
+    int inexact = 0;            // some weight is not a BF16 value (FP32-exact mode multiplies 3 planes)
+};
+struct NormW
+{
+    int c = 0;
+    float *gamma = nullptr, *beta = nullptr;
+};
+struct ResnetW
+{
+    int cin = 0, cout = 0;
+    NormW norm1, norm2;
+    ConvW conv1, conv2, shortcut;
+    bool has_shortcut = false;
+};
+struct AttnW
+{
+    NormW norm;
+    ConvW qkv, out; // qkv rows: to_q, to_k, to_v
+};
+
+enum class Role
+{
+    ConvWeight,
+    ConvBias,
+    Vector, // GroupNorm gamma/beta, post_quant_conv weight and bias: FP32 copied as is
+};
+
+struct Param
+{
+    std::string name;
+    std::vector<int> shape;
+    Role role = Role::Vector;
+    ConvW *conv = nullptr;
+    int row_offset = 0;
+    float *dst = nullptr;
+    float scale = 0.f, offset = 0.f; // synthetic initialisation (include/ernie_synth.h)
+    bool loaded = false;
+    size_t count() const
+    {
+        size_t n = 1;
+        for (int d : shape) n *= static_cast<size_t>(d);
+        return n;
+    }
+};
+
+// Diffusers parameter names and shapes of the decoder, in the order the reference graph runs them.
+struct Layout
+{
+    float *pq_w = nullptr, *pq_b = nullptr;
+    ConvW conv_in;
+    ResnetW mid[2];
+    AttnW attn;
+    ResnetW up[4][3];
+    ConvW upsample[3];
+    NormW norm_out;
+    ConvW conv_out;
+    std::vector<Param> params;
+    std::vector<ConvW *> convs;
+    std::vector<NormW *> norms;
+
+    static constexpr int kUpOut[4] = {512, 512, 256, 128};
+
+    void conv(const std::string &name, ConvW &c, int cin, int cout, int taps)
+    {
+        c.cin = cin;
+        c.cout = cout;
+        c.taps = taps;
+        c.cin_pad = (cin + 63) / 64 * 64;
+        c.cout_rows = cout < 16 ? 16 : cout;
+        convs.push_back(&c);
+        const int k = taps == 9 ? 3 : 1;
+        add(name + ".weight", {cout, cin, k, k}, Role::ConvWeight, &c, 0, 1.f / std::sqrt(float(cin * taps)), 0.f);
+        add(name + ".bias", {cout}, Role::ConvBias, &c, 0, 0.02f, 0.f);
+    }
+    void norm(const std::string &name, NormW &n, int c)
+    {
+        n.c = c;
+        norms.push_back(&n);
+        add(name + ".weight", {c}, Role::Vector, nullptr, 0, 0.1f, 1.f);
+        add(name + ".bias", {c}, Role::Vector, nullptr, 0, 0.1f, 0.f);
+    }
+    void resnet(const std::string &name, ResnetW &r, int cin, int cout)
+    {
+        r.cin = cin;
+        r.cout = cout;
+        norm(name + ".norm1", r.norm1, cin);
+        conv(name + ".conv1", r.conv1, cin, cout, 9);
+        norm(name + ".norm2", r.norm2, cout);
+        conv(name + ".conv2", r.conv2, cout, cout, 9);
+        if (cin != cout)
+        {
+            r.has_shortcut = true;
+            conv(name + ".conv_shortcut", r.shortcut, cin, cout, 1);
+        }
+    }
+    void add(const std::string &name, std::vector<int> shape, Role role, ConvW *c, int row_offset, float scale,
+             float offset)
+    {
+        Param p;
+        p.name = name;
+        p.shape = std::move(shape);
+        p.role = role;
+        p.conv = c;
+        p.row_offset = row_offset;
+        p.scale = scale;
+        p.offset = offset;
+        params.push_back(std::move(p));
+    }
+
+    Layout()
+    {
+        add("post_quant_conv.weight", {32, 32, 1, 1}, Role::Vector, nullptr, 0, 1.f / std::sqrt(32.f), 0.f);
+        add("post_quant_conv.bias", {32}, Role::Vector, nullptr, 0, 0.02f, 0.f);
+        conv("decoder.conv_in", conv_in, 32, 512, 9);
+        resnet("decoder.mid_block.resnets.0", mid[0], 512, 512);
+        norm("decoder.mid_block.attentions.0.group_norm", attn.norm, 512);
+        attn.qkv.cin = 512;
+        attn.qkv.cout = 1536;
+        attn.qkv.taps = 1;
+        attn.qkv.cin_pad = 512;
+        attn.qkv.cout_rows = 1536;
+        convs.push_back(&attn.qkv);
+        const float lin = 1.f / std::sqrt(512.f);
+        const char *proj[3] = {"to_q", "to_k", "to_v"};
+        for (int i = 0; i < 3; ++i)
+        {
+            const std::string base = std::string("decoder.mid_block.attentions.0.") + proj[i];
+            add(base + ".weight", {512, 512}, Role::ConvWeight, &attn.qkv, 512 * i, lin, 0.f);
+            add(base + ".bias", {512}, Role::ConvBias, &attn.qkv, 512 * i, 0.02f, 0.f);
+        }
+        attn.out.cin = 512;
+        attn.out.cout = 512;
+        attn.out.taps = 1;
+        attn.out.cin_pad = 512;
+        attn.out.cout_rows = 512;
+        convs.push_back(&attn.out);
+        add("decoder.mid_block.attentions.0.to_out.0.weight", {512, 512}, Role::ConvWeight, &attn.out, 0, lin, 0.f);
+        add("decoder.mid_block.attentions.0.to_out.0.bias", {512}, Role::ConvBias, &attn.out, 0, 0.02f, 0.f);
+        resnet("decoder.mid_block.resnets.1", mid[1], 512, 512);
+        int c = 512;
+        for (int i = 0; i < 4; ++i)
+        {
+            for (int j = 0; j < 3; ++j)
+            {
+                resnet("decoder.up_blocks." + std::to_string(i) + ".resnets." + std::to_string(j), up[i][j], c,
+                       kUpOut[i]);
+                c = kUpOut[i];
+            }
+            if (i < 3) conv("decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv", upsample[i], c, c, 9);
+        }
+        norm("decoder.conv_norm_out", norm_out, 128);
+        conv("decoder.conv_out", conv_out, 128, 3, 9);
+    }
+};
+
+// Buffers of one decode shape and precision (levels L0..L3 at 1x, 2x, 4x, 8x the input side).
+struct Plan
+{
+    int h0 = 0, w0 = 0, precision = 0, planes = 1;
+    int n = 0, npad = 0; // attention tokens (h0 * w0) and their padding to 256
+    float *input = nullptr, *x = nullptr, *h1 = nullptr, *sc = nullptr, *qkv = nullptr, *s = nullptr, *o = nullptr;
+    float *scale = nullptr, *shift = nullptr, *decoded = nullptr;
+    __nv_bfloat16 *a = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *p = nullptr;
+    double2 *stats_x = nullptr, *stats_h = nullptr;
+    uint8_t *rgb = nullptr;
+    int *nonfinite = nullptr;
+    void *alloc = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    int launches = 0;
+    size_t bytes = 0;
+};
+
+size_t pixels_of(int h, int w) { return static_cast<size_t>(h) * static_cast<size_t>(w); }
+} // namespace
+
+struct ernie_cuda_vae
+{
+    ernie_cuda_context *ctx = nullptr;
+    Layout layout;
+    void *alloc = nullptr;
+    float *staging = nullptr;
+    int *d_inexact = nullptr;
+    uint64_t bytes = 0;
+    std::unique_ptr<Plan> plan;
+};
+
+namespace
+{
+void free_plan(Plan *p)
+{
+    if (!p) return;
+    if (p->graph) cudaGraphExecDestroy(p->graph);
+    if (p->alloc) cudaFree(p->alloc);
+}
+
+int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_ptr<Plan> &out)
+{
+    auto plan = std::make_unique<Plan>();
+    Plan &p = *plan;
+    p.h0 = h0;
+    p.w0 = w0;
+    p.precision = precision;
+    p.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    p.n = h0 * w0;
+    p.npad = (p.n + 255) / 256 * 256;
+    const size_t px0 = pixels_of(h0, w0), top = 64 * px0;
+    const int rb_max = conv_row_blocks(8 * h0, 8 * w0);
+    Arena arena;
+    arena.add(&p.input, 32 * px0);
+    arena.add(&p.x, 16384 * px0);
+    arena.add(&p.h1, 8192 * px0);
+    arena.add(&p.sc, 8192 * px0);
+    arena.add(&p.a, static_cast<size_t>(p.planes) * 16384 * px0);
+    arena.add(&p.qkv, static_cast<size_t>(p.n) * 1536);
+    arena.add(&p.q, static_cast<size_t>(p.planes) * 512 * p.npad);
+    arena.add(&p.k, static_cast<size_t>(p.planes) * 512 * p.npad);
+    arena.add(&p.vt, static_cast<size_t>(p.planes) * 512 * p.npad);
+    arena.add(&p.s, static_cast<size_t>(p.n) * p.npad);
+    arena.add(&p.p, static_cast<size_t>(p.planes) * p.n * p.npad);
+    arena.add(&p.o, static_cast<size_t>(p.n) * 512);
+    arena.add(&p.stats_x, static_cast<size_t>(kGroups) * rb_max);
+    arena.add(&p.stats_h, static_cast<size_t>(kGroups) * rb_max);
+    arena.add(&p.scale, 512);
+    arena.add(&p.shift, 512);
+    arena.add(&p.decoded, 3 * top);
+    arena.add(&p.rgb, 3 * top);
+    arena.add(&p.nonfinite, 1);
+    p.bytes = arena.bytes();
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess) return from_cuda(e, "Allocate VAE workspace");
+    p.alloc = arena.base;
+    // K's rows and V^T's columns past the last token stay zero: their scores and products vanish
+    cudaError_t z = cudaMemsetAsync(p.k, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, v->ctx->stream);
+    if (z == cudaSuccess)
+        z = cudaMemsetAsync(p.vt, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, v->ctx->stream);
+    if (z == cudaSuccess) z = cudaStreamSynchronize(v->ctx->stream);
+    if (z != cudaSuccess)
+    {
+        free_plan(plan.get());
+        return from_cuda(z, "Clear VAE workspace");
+    }
+    out = std::move(plan);
+    return ERNIE_CUDA_OK;
+}
+
+// ---- the decoder program -----------------------------------------------------------------------------
+struct Program
+{
+    ernie_cuda_vae *v;
+    Plan &p;
+    cudaStream_t stream;
+    int sms;
+    bool fp32() const { return p.planes == 3; }
+
+    int conv(const ConvW &c, const __nv_bfloat16 *a, int h, int w, const ConvArgs &epi)
+    {
+        ConvLaunch l;
+        l.a = a;
+        l.a_planes = p.planes;
+        l.b = c.w;
+        l.b_planes = fp32() && c.inexact ? 3 : 1;
+        l.b_row = 3LL * c.taps * c.cin_pad;
+        l.cout_rows = c.cout_rows;
+        l.height = h;
+        l.width = w;
+        l.cin = c.cin_pad;
+        l.taps = c.taps;
+        l.cout = c.cout_rows;
+        ConvArgs args = epi;
+        args.bias = c.bias;
+        args.error_flag = v->ctx->error_flag;
+        ++p.launches;
+        return from_launch(launch_conv(l, args, sms, stream), "VAE convolution");
+    }
+    // GroupNorm(32) of x (statistics from its producer) + optional Swish -> operand `a`
+    int group_norm(const NormW &n, const float *x, const double2 *stats, int h, int w, bool silu)
+    {
+        const int cpg = n.c / kGroups;
+        ERNIE_LAUNCH(launch_gn_finalize(stats, conv_row_blocks(h, w), static_cast<long long>(pixels_of(h, w)) * cpg,
+                                        cpg, n.gamma, n.beta, kGroupNormEps, p.scale, p.shift, stream),
+                     "GroupNorm statistics");
+        ERNIE_LAUNCH(launch_gn_apply(x, static_cast<long long>(pixels_of(h, w)), n.c, p.scale, p.shift, silu ? 1 : 0,
+                                     p.a, p.planes, stream),
+                     "GroupNorm");
+        p.launches += 2;
+        return ERNIE_CUDA_OK;
+    }
+    ConvArgs writes_x(int cout, const float *resid)
+    {
+        ConvArgs e;
+        e.out = p.x;
+        e.ldo = cout;
+        e.resid = resid;
+        e.stats = p.stats_x;
+        e.cpg = cout / kGroups;
+        return e;
+    }
+    // ResnetBlock2D: x <- shortcut(x) + conv2(swish(norm2(conv1(swish(norm1(x))))))
+    int resnet(const ResnetW &r, int h, int w)
+    {
+        const float *resid = p.x;
+        if (r.has_shortcut)
+        {
+            ERNIE_LAUNCH(launch_to_operand(p.x, static_cast<long long>(pixels_of(h, w)), r.cin, p.a, fp32() ? 1 : 0,
+                                           stream),
+                         "shortcut operand");
+            ++p.launches;
+            ConvArgs e;
+            e.out = p.sc;
+            e.ldo = r.cout;
+            ERNIE_TRY(conv(r.shortcut, p.a, h, w, e));
+            resid = p.sc;
+        }
+        ERNIE_TRY(group_norm(r.norm1, p.x, p.stats_x, h, w, true));
+        ConvArgs e1;
+        e1.out = p.h1;
+        e1.ldo = r.cout;
+        e1.stats = p.stats_h;
+        e1.cpg = r.cout / kGroups;
+        ERNIE_TRY(conv(r.conv1, p.a, h, w, e1));
+        ERNIE_TRY(group_norm(r.norm2, p.h1, p.stats_h, h, w, true));
+        return conv(r.conv2, p.a, h, w, writes_x(r.cout, resid));
+    }
+    // Attention block over all h*w pixels (one head of 512): x <- x + out(softmax(q k^T / sqrt 512) v)
+    int attention(const AttnW &at, int h, int w)
+    {
+        const int n = p.n, npad = p.npad;
+        ERNIE_TRY(group_norm(at.norm, p.x, p.stats_x, h, w, false));
+        ConvArgs eq;
+        eq.out = p.qkv;
+        eq.ldo = 1536;
+        ERNIE_TRY(conv(at.qkv, p.a, h, w, eq));
+        ERNIE_LAUNCH(launch_attention_split(p.qkv, n, p.q, p.k, p.vt, npad, p.planes, stream), "attention split");
+        p.launches += 2;
+        ConvLaunch ls;
+        ls.a = p.q;
+        ls.a_planes = p.planes;
+        ls.b = p.k;
+        ls.b_planes = p.planes;
+        ls.b_row = static_cast<long long>(p.planes) * 512;
+        ls.cout_rows = npad;
+        ls.height = 1;
+        ls.width = n;
+        ls.cin = 512;
+        ls.taps = 1;
+        ls.cout = npad;
+        ConvArgs es;
+        es.out = p.s;
+        es.ldo = npad;
+        es.error_flag = v->ctx->error_flag;
+        ERNIE_LAUNCH(launch_conv(ls, es, sms, stream), "attention scores");
+        ERNIE_LAUNCH(launch_softmax_rows(p.s, n, npad, n, 1.f / std::sqrt(512.f), p.p, npad, p.planes, stream),
+                     "attention softmax");
+        ConvLaunch lo;
+        lo.a = p.p;
+        lo.a_planes = p.planes;
+        lo.b = p.vt;
+        lo.b_planes = p.planes;
+        lo.b_row = static_cast<long long>(p.planes) * npad;
+        lo.cout_rows = 512;
+        lo.height = 1;
+        lo.width = n;
+        lo.cin = npad;
+        lo.taps = 1;
+        lo.cout = 512;
+        ConvArgs eo;
+        eo.out = p.o;
+        eo.ldo = 512;
+        eo.error_flag = v->ctx->error_flag;
+        ERNIE_LAUNCH(launch_conv(lo, eo, sms, stream), "attention values");
+        ERNIE_LAUNCH(launch_to_operand(p.o, n, 512, p.a, fp32() ? 1 : 0, stream), "attention output operand");
+        p.launches += 4;
+        return conv(at.out, p.a, h, w, writes_x(512, p.x));
+    }
+    int run()
+    {
+        const Layout &L = v->layout;
+        int h = p.h0, w = p.w0;
+        ERNIE_LAUNCH(launch_vae_input(p.input, static_cast<long long>(pixels_of(h, w)), L.pq_w, L.pq_b, p.a,
+                                      p.planes, stream),
+                     "post_quant_conv");
+        ++p.launches;
+        ERNIE_TRY(conv(L.conv_in, p.a, h, w, writes_x(512, nullptr)));
+        ERNIE_TRY(resnet(L.mid[0], h, w));
+        ERNIE_TRY(attention(L.attn, h, w));
+        ERNIE_TRY(resnet(L.mid[1], h, w));
+        for (int i = 0; i < 4; ++i)
+        {
+            for (int j = 0; j < 3; ++j) ERNIE_TRY(resnet(L.up[i][j], h, w));
+            if (i == 3) break;
+            const int c = L.up[i][2].cout;
+            ERNIE_LAUNCH(launch_upsample(p.x, h, w, c, p.a, p.planes, stream), "upsample");
+            ++p.launches;
+            h *= 2;
+            w *= 2;
+            ERNIE_TRY(conv(L.upsample[i], p.a, h, w, writes_x(c, nullptr)));
+        }
+        ERNIE_TRY(group_norm(L.norm_out, p.x, p.stats_x, h, w, true));
+        ConvArgs e;
+        e.planar = p.decoded;
+        e.rgb = p.rgb;
+        e.valid_out = 3;
+        e.nonfinite = p.nonfinite;
+        return conv(L.conv_out, p.a, h, w, e);
+    }
+};
+
+bool vae_shape_ok(int width, int height)
+{
+    return width >= 1 && height >= 1 && width <= kMaxLatentSide && height <= kMaxLatentSide &&
+           width * height <= kSoftmaxMaxRow;
+}
+
+int find_param(ernie_cuda_vae *v, const char *name)
+{
+    for (size_t i = 0; i < v->layout.params.size(); ++i)
+        if (v->layout.params[i].name == name) return static_cast<int>(i);
+    return -1;
+}
+
+// Moves staged FP32 values (device) of parameter i to their resident form.
+int place(ernie_cuda_vae *v, Param &prm)
+{
+    cudaStream_t stream = v->ctx->stream;
+    if (prm.role == Role::Vector)
+    {
+        ERNIE_CUDA(cudaMemcpyAsync(prm.dst, v->staging, prm.count() * 4, cudaMemcpyDeviceToDevice, stream), "place");
+    }
+    else if (prm.role == Role::ConvBias)
+    {
+        ERNIE_CUDA(cudaMemcpyAsync(prm.conv->bias + prm.row_offset, v->staging, prm.count() * 4,
+                                   cudaMemcpyDeviceToDevice, stream),
+                   "place bias");
+    }
+    else
+    {
+        ConvW &c = *prm.conv;
+        const int cout = prm.shape[0];
+        const int rows = prm.row_offset == 0 && cout == c.cout ? c.cout_rows : cout;
+        ERNIE_CUDA(cudaMemsetAsync(v->d_inexact, 0, sizeof(int), stream), "clear flag");
+        ERNIE_LAUNCH(launch_conv_weight_prep(v->staging, cout, c.cin, c.taps, rows, c.cin_pad,
+                                             c.w + static_cast<size_t>(prm.row_offset) * 3 * c.taps * c.cin_pad,
+                                             v->d_inexact, stream),
+                     "prepare weights");
+        int inexact = 0;
+        ERNIE_CUDA(cudaMemcpyAsync(&inexact, v->d_inexact, sizeof(int), cudaMemcpyDeviceToHost, stream), "read flag");
+        ERNIE_CUDA(cudaStreamSynchronize(stream), "prepare weights");
+        c.inexact |= inexact;
+    }
+    prm.loaded = true;
+    return ERNIE_CUDA_OK;
+}
+
+void drop_plan(ernie_cuda_vae *v)
+{
+    if (v->plan)
+    {
+        free_plan(v->plan.get());
+        v->plan.reset();
+    }
+}
+
+int ensure_plan(ernie_cuda_vae *v, int width, int height, int precision)
+{
+    if (v->plan && v->plan->w0 == width && v->plan->h0 == height && v->plan->precision == precision)
+        return ERNIE_CUDA_OK;
+    drop_plan(v);
+    std::unique_ptr<Plan> plan;
+    ERNIE_TRY(plan_create(v, height, width, precision, plan));
+    // capture the whole decoder once; every later decode of this shape replays it
+    Program prog{v, *plan, v->ctx->stream, v->ctx->num_sms};
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(v->ctx->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess)
+    {
+        free_plan(plan.get());
+        return from_cuda(e, "Begin VAE capture");
+    }
+    const int rc = prog.run();
+    e = cudaStreamEndCapture(v->ctx->stream, &graph);
+    if (rc != ERNIE_CUDA_OK || e != cudaSuccess)
+    {
+        if (graph) cudaGraphDestroy(graph);
+        free_plan(plan.get());
+        return rc != ERNIE_CUDA_OK ? rc : from_cuda(e, "End VAE capture");
+    }
+    e = cudaGraphInstantiate(&plan->graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess)
+    {
+        free_plan(plan.get());
+        return from_cuda(e, "Instantiate VAE graph");
+    }
+    v->plan = std::move(plan);
+    return ERNIE_CUDA_OK;
+}
+
+int check_loaded(ernie_cuda_vae *v)
+{
+    for (const auto &prm : v->layout.params)
+        if (!prm.loaded) return fail(ERNIE_CUDA_ERROR, "VAE tensor not uploaded: " + prm.name);
+    return ERNIE_CUDA_OK;
+}
+
+int run_decode(ernie_cuda_vae *v, int width, int height, int precision)
+{
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    ERNIE_CUDA(cudaMemsetAsync(p.nonfinite, 0, sizeof(int), v->ctx->stream), "clear flag");
+    ERNIE_CUDA(cudaGraphLaunch(p.graph, v->ctx->stream), "VAE decode");
+    return ERNIE_CUDA_OK;
+}
+
+int read_status(ernie_cuda_vae *v, int *nonfinite)
+{
+    int flags[2] = {0, 0};
+    ERNIE_CUDA(cudaMemcpyAsync(&flags[0], v->plan->nonfinite, sizeof(int), cudaMemcpyDeviceToHost, v->ctx->stream),
+               "read flag");
+    ERNIE_CUDA(cudaMemcpyAsync(&flags[1], v->ctx->error_flag, sizeof(int), cudaMemcpyDeviceToHost, v->ctx->stream),
+               "read status");
+    ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE decode");
+    if (flags[1]) return fail(ERNIE_CUDA_ERROR, "VAE kernel protocol timeout (status " + std::to_string(flags[1]) + ")");
+    if (nonfinite) *nonfinite = flags[0];
+    return ERNIE_CUDA_OK;
+}
+} // namespace
+
+extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **out)
+{
+    if (!ctx || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *out = nullptr;
+    DeviceGuard guard(ctx->device);
+    auto v = std::make_unique<ernie_cuda_vae>();
+    v->ctx = ctx;
+    Layout &L = v->layout;
+    Arena arena;
+    size_t staging = 0;
+    for (auto &prm : L.params) staging = std::max(staging, prm.count());
+    arena.add(&v->staging, staging);
+    arena.add(&v->d_inexact, 1);
+    arena.add(&L.pq_w, 32 * 32);
+    arena.add(&L.pq_b, 32);
+    for (ConvW *c : L.convs)
+    {
+        arena.add(&c->w, static_cast<size_t>(c->cout_rows) * 3 * c->taps * c->cin_pad);
+        arena.add(&c->bias, static_cast<size_t>(c->cout_rows));
+    }
+    for (NormW *n : L.norms)
+    {
+        arena.add(&n->gamma, static_cast<size_t>(n->c));
+        arena.add(&n->beta, static_cast<size_t>(n->c));
+    }
+    v->bytes = arena.bytes();
+    ERNIE_CUDA(arena.allocate(), "Allocate VAE weights");
+    v->alloc = arena.base;
+    // zero padding rows/channels and the padded conv_out bias
+    cudaError_t e = cudaMemsetAsync(v->alloc, 0, arena.bytes(), ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess)
+    {
+        cudaFree(v->alloc);
+        return from_cuda(e, "Clear VAE weights");
+    }
+    // destinations of the FP32 vectors, in table order
+    size_t norm_index = 0;
+    for (auto &prm : L.params)
+    {
+        if (prm.role != Role::Vector) continue;
+        if (prm.name == "post_quant_conv.weight") prm.dst = L.pq_w;
+        else if (prm.name == "post_quant_conv.bias") prm.dst = L.pq_b;
+        else
+        {
+            NormW *n = L.norms[norm_index / 2];
+            prm.dst = norm_index % 2 == 0 ? n->gamma : n->beta;
+            ++norm_index;
+        }
+    }
+    *out = v.release();
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_destroy(ernie_cuda_vae *v)
+{
+    if (!v) return ERNIE_CUDA_OK;
+    DeviceGuard guard(v->ctx->device);
+    cudaStreamSynchronize(v->ctx->stream);
+    drop_plan(v);
+    if (v->alloc) cudaFree(v->alloc);
+    delete v;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_tensor_count(int *count)
+{
+    if (!count) return fail(ERNIE_CUDA_ERROR, "null argument");
+    static const Layout table;
+    *count = static_cast<int>(table.params.size());
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim)
+{
+    static const Layout table;
+    if (index < 0 || index >= static_cast<int>(table.params.size()) || !name || !dims || !ndim)
+        return fail(ERNIE_CUDA_ERROR, "Invalid VAE tensor index or null argument");
+    const Param &prm = table.params[static_cast<size_t>(index)];
+    if (prm.name.size() + 1 > name_bytes) return fail(ERNIE_CUDA_ERROR, "Name buffer too small");
+    std::copy(prm.name.begin(), prm.name.end(), name);
+    name[prm.name.size()] = '\0';
+    *ndim = static_cast<int>(prm.shape.size());
+    for (size_t d = 0; d < prm.shape.size(); ++d) dims[d] = prm.shape[d];
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_upload(ernie_cuda_vae *v, const char *name, const float *host, size_t count)
+{
+    if (!v || !name || !host) return fail(ERNIE_CUDA_ERROR, "null argument");
+    const int i = find_param(v, name);
+    if (i < 0) return fail(ERNIE_CUDA_ERROR, std::string("Unknown VAE tensor: ") + name);
+    Param &prm = v->layout.params[static_cast<size_t>(i)];
+    if (count != prm.count()) return fail(ERNIE_CUDA_ERROR, "VAE tensor size differs: " + prm.name);
+    for (size_t j = 0; j < count; ++j)
+        if (!std::isfinite(host[j])) return fail(ERNIE_CUDA_ERROR, "VAE tensor is not finite: " + prm.name);
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_CUDA(cudaMemcpyAsync(v->staging, host, count * 4, cudaMemcpyHostToDevice, v->ctx->stream), "upload");
+    ERNIE_TRY(place(v, prm));
+    ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "upload");
+    drop_plan(v); // FP32-exact plane counts may change
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_synthesize(ernie_cuda_vae *v, uint64_t seed, int bf16_weights)
+{
+    if (!v) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(v->ctx->device);
+    for (auto &prm : v->layout.params)
+    {
+        const bool round = bf16_weights && prm.role == Role::ConvWeight;
+        ERNIE_LAUNCH(launch_synth_f32(seed, ernie_synth_name_stream(prm.name.c_str()), prm.scale, prm.offset,
+                                      static_cast<long long>(prm.count()), round ? 1 : 0, v->staging, v->ctx->stream),
+                     "synthesize");
+        ERNIE_TRY(place(v, prm));
+    }
+    ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "synthesize");
+    drop_plan(v);
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_bytes(ernie_cuda_vae *v, uint64_t *weights, uint64_t *workspace)
+{
+    if (!v) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (weights) *weights = v->bytes;
+    if (workspace) *workspace = v->plan ? v->plan->bytes : 0;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_launches(ernie_cuda_vae *v, int width, int height, int precision, int *launches)
+{
+    if (!v || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    *launches = v->plan->launches;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_decode_device(ernie_cuda_vae *v, const float *unpacked, int width, int height,
+                                            int precision, float *decoded, uint8_t *rgb, int *nonfinite)
+{
+    if (!v || !unpacked || !decoded) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    const size_t in = 32 * pixels_of(height, width), out = 3 * 64 * pixels_of(height, width);
+    ERNIE_CUDA(cudaMemcpyAsync(p.input, unpacked, in * 4, cudaMemcpyDeviceToDevice, v->ctx->stream), "VAE input");
+    ERNIE_TRY(run_decode(v, width, height, precision));
+    ERNIE_CUDA(cudaMemcpyAsync(decoded, p.decoded, out * 4, cudaMemcpyDeviceToDevice, v->ctx->stream), "VAE output");
+    if (rgb) ERNIE_CUDA(cudaMemcpyAsync(rgb, p.rgb, out, cudaMemcpyDeviceToDevice, v->ctx->stream), "RGB output");
+    if (!nonfinite) return ERNIE_CUDA_OK; // stays asynchronous
+    return read_status(v, nonfinite);
+}
+
+extern "C" int ernie_cuda_vae_decode(ernie_cuda_vae *v, const float *unpacked, int width, int height, int precision,
+                                     float *decoded, uint8_t *rgb, int *nonfinite)
+{
+    if (!v || !unpacked || !decoded) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    const size_t in = 32 * pixels_of(height, width), out = 3 * 64 * pixels_of(height, width);
+    ERNIE_CUDA(cudaMemcpyAsync(p.input, unpacked, in * 4, cudaMemcpyHostToDevice, v->ctx->stream), "VAE input");
+    ERNIE_TRY(run_decode(v, width, height, precision));
+    ERNIE_CUDA(cudaMemcpyAsync(decoded, p.decoded, out * 4, cudaMemcpyDeviceToHost, v->ctx->stream), "VAE output");
+    if (rgb) ERNIE_CUDA(cudaMemcpyAsync(rgb, p.rgb, out, cudaMemcpyDeviceToHost, v->ctx->stream), "RGB output");
+    int flag = 0;
+    ERNIE_TRY(read_status(v, &flag));
+    if (nonfinite) *nonfinite = flag;
+    return ERNIE_CUDA_OK;
+}

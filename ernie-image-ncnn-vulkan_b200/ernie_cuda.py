@@ -112,6 +112,16 @@ SIGNATURES = {
     "ernie_cuda_sp_handle": (I, [P, P]),
     "ernie_cuda_sp_connect": (I, [P, P]),
     "ernie_cuda_sp_layout": (I, [I, I, I, I] + [ctypes.POINTER(I)] * 5),
+    "ernie_cuda_vae_create": (I, [P, ctypes.POINTER(P)]),
+    "ernie_cuda_vae_destroy": (I, [P]),
+    "ernie_cuda_vae_tensor_count": (I, [ctypes.POINTER(I)]),
+    "ernie_cuda_vae_tensor_info": (I, [I, ctypes.c_char_p, SZ, ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "ernie_cuda_vae_upload": (I, [P, ctypes.c_char_p, P, SZ]),
+    "ernie_cuda_vae_synthesize": (I, [P, U64, I]),
+    "ernie_cuda_vae_bytes": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "ernie_cuda_vae_launches": (I, [P, I, I, I, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_decode": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_decode_device": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
 }
 
 
@@ -413,6 +423,67 @@ class Model:
         b = U64(0)
         check(lib().ernie_cuda_model_bytes(self.handle, ctypes.byref(b)))
         return b.value
+
+
+def vae_tensors():
+    """[(diffusers name, shape)] of every VAE decoder tensor the library holds, in execution order."""
+    n = I(0)
+    check(lib().ernie_cuda_vae_tensor_count(ctypes.byref(n)))
+    out = []
+    for i in range(n.value):
+        name = ctypes.create_string_buffer(128)
+        dims = (I * 4)()
+        nd = I(0)
+        check(lib().ernie_cuda_vae_tensor_info(i, name, 128, dims, ctypes.byref(nd)))
+        out.append((name.value.decode(), tuple(dims[j] for j in range(nd.value))))
+    return out
+
+
+class Vae:
+    """Device-resident VAE decoder (decode_vae of src/vae.h on the B200)."""
+
+    def __init__(self, ctx):
+        h = P()
+        check(lib().ernie_cuda_vae_create(ctx.handle, ctypes.byref(h)))
+        self.handle, self.ctx = h, ctx
+
+    def close(self):
+        if self.handle:
+            lib().ernie_cuda_vae_destroy(self.handle)
+            self.handle = None
+
+    def synthesize(self, seed, bf16_weights=False):
+        check(lib().ernie_cuda_vae_synthesize(self.handle, seed, 1 if bf16_weights else 0))
+
+    def upload(self, name, array):
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        check(lib().ernie_cuda_vae_upload(self.handle, name.encode(), ptr(a), a.size))
+
+    def nbytes(self):
+        w, ws = U64(0), U64(0)
+        check(lib().ernie_cuda_vae_bytes(self.handle, ctypes.byref(w), ctypes.byref(ws)))
+        return w.value, ws.value
+
+    def launches(self, width, height, precision=BF16):
+        n = I(0)
+        check(lib().ernie_cuda_vae_launches(self.handle, width, height, precision, ctypes.byref(n)))
+        return n.value
+
+    def decode(self, unpacked, precision=BF16, rgb=False):
+        """unpacked [32, h, w] -> (decoded [3, 8h, 8w] FP32, rgb bytes [8h, 8w, 3] or None, nonfinite flag)."""
+        u = np.ascontiguousarray(unpacked, dtype=np.float32)
+        _, h, w = u.shape
+        out = np.empty((3, 8 * h, 8 * w), np.float32)
+        pixels = np.empty((8 * h, 8 * w, 3), np.uint8) if rgb else None
+        flag = I(0)
+        check(lib().ernie_cuda_vae_decode(self.handle, ptr(u), w, h, precision, ptr(out), ptr(pixels),
+                                          ctypes.byref(flag)))
+        return out, pixels, flag.value
+
+    def decode_device(self, unpacked_dev, width, height, decoded_dev, precision=BF16, rgb_dev=None):
+        """Asynchronous decode between device buffers (Buffer objects) on the context's stream."""
+        check(lib().ernie_cuda_vae_decode_device(self.handle, unpacked_dev.c, width, height, precision,
+                                                 decoded_dev.c, rgb_dev.c if rgb_dev is not None else None, None))
 
 
 def initial_noise(seed, width, height):

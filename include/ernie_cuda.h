@@ -195,6 +195,38 @@ int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial
    std::normal_distribution<float>(0, 1), channel after channel, into out [128][height][width]. Host-only. */
 int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out);
 
+/* ---- VAE decoder (the stage after the denoise loop) -----------------------------------------------
+   decode_vae (src/vae.h:16-22, src/vae.cpp:18-66) of the pinned AutoencoderKLFlux2 post_quant_conv +
+   decoder, and rgb_image (src/pipeline.cpp:145-163), on one B200. Weights are addressed by their
+   diffusers parameter names and shapes (ernie_cuda_vae_tensor_info lists all of them, e.g.
+   "decoder.up_blocks.2.resnets.0.conv_shortcut.weight" [256,512,1,1]), uploaded as FP32. The input is
+   the unpacked latent [32][height][width] (ernie_cuda_unpack_for_vae's output); the output is the
+   decoded image [3][8*height][8*width] FP32 and, optionally, its RGB bytes [8*height][8*width][3]
+   (clamp(x/2 + 0.5, 0, 1) * 255 rounded to nearest even). *nonfinite (nullable) is set to 1 when a
+   decoded value is not finite: the reference's rgb_image throws there; those pixels' bytes are
+   unspecified. 1 <= width, height <= 256 with width * height <= 57344 (the mid-block attention row).
+   precision: ERNIE_PRECISION_BF16 (BF16 convolution operands, FP32 accumulation and residuals) or
+   ERNIE_PRECISION_FP32 (three-plane FP32-exact operands; the reference's FP32 CPU path is the gate). */
+typedef struct ernie_cuda_vae ernie_cuda_vae;
+int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **out);
+int ernie_cuda_vae_destroy(ernie_cuda_vae *vae);
+int ernie_cuda_vae_tensor_count(int *count);
+/* name (NUL-terminated, name_bytes >= 64 suffices) and shape (up to 4 dims) of tensor `index`. */
+int ernie_cuda_vae_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim);
+int ernie_cuda_vae_upload(ernie_cuda_vae *vae, const char *name, const float *host, size_t count);
+/* Seeded random-init weights (include/ernie_synth.h, VAE section); bf16_weights rounds the convolution
+   and projection weights to BF16 values. */
+int ernie_cuda_vae_synthesize(ernie_cuda_vae *vae, uint64_t seed, int bf16_weights);
+int ernie_cuda_vae_bytes(ernie_cuda_vae *vae, uint64_t *weights, uint64_t *workspace);
+/* Kernel launches of one decode of this shape (builds the shape's workspace and graph). */
+int ernie_cuda_vae_launches(ernie_cuda_vae *vae, int width, int height, int precision, int *launches);
+/* Host buffers, synchronous. */
+int ernie_cuda_vae_decode(ernie_cuda_vae *vae, const float *unpacked, int width, int height, int precision,
+                          float *decoded, uint8_t *rgb, int *nonfinite);
+/* Device buffers on the context's stream; synchronous only when nonfinite is non-null. */
+int ernie_cuda_vae_decode_device(ernie_cuda_vae *vae, const float *unpacked, int width, int height, int precision,
+                                 float *decoded, uint8_t *rgb, int *nonfinite);
+
 /* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 members, BF16) ---------------
    Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every member
    holds the full weights. Per block, the QKV GEMM's epilogue stores each head of this GPU's rows straight

@@ -109,4 +109,22 @@ enum ernie_synth_tensor
 #define ERNIE_SYNTH_BLOCK_STREAM(block, tensor) ((uint64_t)((block) + 1) * 64u + (uint64_t)(tensor))
 #define ERNIE_SYNTH_WEIGHT_STD 0.02f
 
+/* VAE decoder tensors are addressed by their diffusers parameter name (e.g. "decoder.conv_in.weight"):
+ * stream = FNV-1a 64 of the name. Values are FP32, float(N(0,1) * scale) + offset, with
+ *   convolution / linear weights   scale 1/sqrt(fan_in), offset 0
+ *   GroupNorm weights (gamma)      scale 0.1, offset 1
+ *   GroupNorm biases (beta)        scale 0.1, offset 0
+ *   other biases                   scale 0.02, offset 0
+ * optionally rounded to BF16 (weights stored as BF16). */
+ERNIE_SYNTH_FN uint64_t ernie_synth_name_stream(const char *name)
+{
+    uint64_t h = 0xCBF29CE484222325ULL;
+    for (; *name; ++name)
+    {
+        h ^= (uint64_t)(unsigned char)*name;
+        h *= 0x100000001B3ULL;
+    }
+    return h;
+}
+
 #endif
