@@ -170,6 +170,138 @@ def run_reference(args):
 
 KERNELS = {"norm_modulate": 0, "qkv_gemm": 1, "attention": 2, "out_gemm": 3, "upgate_gemm": 5, "down_gemm": 6}
 
+# ---- the stage after the denoise loop: VAE decode (--stage vae) -----------------------------------------
+VAE_METRIC = "VAE decode images/s (1024² output from the 128x128x32 unpacked latent); % BF16 peak"
+VAE_LATENT = (128, 128)  # unpacked latent [32][h][w] of a 1024x1024 image (the C2 request's decode)
+VAE_SAMPLE = (16, 16)    # CPU sample: a 128x128 output, 1/64 of the pixels
+
+
+def vae_cpu_sample():
+    """The oracle's decode (float64 numpy, all host cores) of one VAE_SAMPLE latent: (seconds, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import vae as ov
+    threads = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=threads)
+    except ImportError:
+        pass
+    w = ov.synth_weights(4321)
+    u = np.random.default_rng(0).standard_normal((32,) + VAE_SAMPLE).astype(np.float32)
+    ov.decode(w, u)  # warm
+    t0 = time.perf_counter()
+    ov.decode(w, u)
+    return time.perf_counter() - t0, threads
+
+
+def vae_cpu_line_fields(seconds, threads):
+    scale = (VAE_LATENT[0] * VAE_LATENT[1]) / (VAE_SAMPLE[0] * VAE_SAMPLE[1])
+    image_s = seconds * scale
+    return 1.0 / image_s, {"value": 1.0 / image_s, "unit": "images/s", "cores": threads, "kind": "port",
+                           "sample": f"oracle decode of a {VAE_SAMPLE[0]}x{VAE_SAMPLE[1]} latent "
+                                     f"({8 * VAE_SAMPLE[0]}x{8 * VAE_SAMPLE[1]} output, {seconds:.2f} s), "
+                                     f"scaled x{scale:.0f} by pixel count (the attention's quadratic term, "
+                                     "5% of the 1024² FLOPs, is not scaled up)"}
+
+
+def run_vae_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times = []
+    threads = 1
+    for i in range(args.warmup + args.steps):
+        dt, threads = vae_cpu_sample()
+        if i >= args.warmup:
+            times.append(dt)
+    value, cpu = vae_cpu_line_fields(statistics.median(times), threads)
+    line = {"metric": VAE_METRIC, "impl": "reference", "value": value, "unit": "images/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "VAE decode of one 1024x1024 image", "sample": cpu["sample"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_vae(args):
+    """One VAE decode per GPU per step (independent images, no collective)."""
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    ctx = ec.Context(local)
+    vae = ec.Vae(ctx)
+    vae.synthesize(4321)
+    precision = ec.BF16 if args.precision == "bf16" else ec.FP32
+    h, w = tuple(int(v) for v in args.vae_latent.split(",")) if args.vae_latent else VAE_LATENT
+    u = np.random.default_rng(dp.request_seed(2000, rank)).standard_normal((32, h, w)).astype(np.float32)
+    out_elems = 3 * 64 * h * w
+    src, dst, rgb = ctx.to_device(u), ctx.buffer(out_elems * 4), ctx.buffer(out_elems)
+    launches = vae.launches(w, h, precision)
+    for _ in range(args.warmup):
+        vae.decode_device(src, w, h, dst, precision, rgb)
+    clocks = ClockSampler(local)
+    barrier(pg)
+    ctx.synchronize()
+    clocks.start()
+    ctx.record(0)
+    for _ in range(args.steps):
+        vae.decode_device(src, w, h, dst, precision, rgb)
+    ctx.record(1)
+    ctx.synchronize()
+    clock_info = clocks.stop()
+    barrier(pg)
+    ms = max_over_ranks(pg, ctx.elapsed(0, 1)) / args.steps
+    images_per_s = world * 1000.0 / ms
+
+    prof = vae.profile(w, h, precision, iters=3)
+    bf16_peak, _, hbm_peak, peak_kind = peaks()
+    classes = {}
+    for name, (t, work) in prof.items():
+        tensor = name in ("conv", "attention_gemm")
+        rate = work / (t * 1e-3) / (1e12 if tensor else 1e9) if t > 0 else 0.0
+        classes[name] = {"ms": t, "work": work, "work_unit": "FLOP" if tensor else "byte",
+                         "achieved": rate, "unit": "TFLOP/s" if tensor else "GB/s",
+                         "frac": rate / (bf16_peak if tensor else hbm_peak)}
+    total_flops = prof["conv"][1] + prof["attention_gemm"][1]
+    conv = classes["conv"]
+
+    e2e = None
+    if not args.no_e2e:
+        vae.decode(u, precision, rgb=True)
+        barrier(pg)
+        reps = max(1, args.steps)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            decoded, pixels, bad = vae.decode(u, precision, rgb=True)
+        dt = max_over_ranks(pg, (time.perf_counter() - t0) / reps)
+        assert bad == 0 and np.isfinite(decoded).all()
+        e2e = {"value": world / dt, "unit": "images/s", "h2d_bytes_per_step": u.nbytes,
+               "d2h_bytes_per_step": decoded.nbytes + pixels.nbytes,
+               "call": "ernie_cuda_vae_decode (host unpacked latent in, host decoded FP32 + RGB bytes out)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        _, cpu = vae_cpu_line_fields(*vae_cpu_sample())
+
+    if rank == 0:
+        line = {"metric": VAE_METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+                "config": {"workload": "VAE decode (post_quant_conv + AutoencoderKLFlux2 decoder + RGB bytes) of "
+                                       f"one {8 * w}x{8 * h} image per GPU per step, seeded synthetic weights",
+                           "global_batch": world, "parallelism": f"dp{world}",
+                           "l2": "inputs larger than L2 (activations of 0.5-1 GB per layer at the top levels)",
+                           "decode_tflops": total_flops / (ms * 1e-3) / 1e12, "kernel_classes": classes},
+                "roofline": {"bound": "tensor", "kernel": "conv_kernel (all decoder convolutions)",
+                             "achieved": conv["achieved"], "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": conv["achieved"] / bf16_peak, "peak_kind": peak_kind, "traffic": None},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clock_info}
+        print(json.dumps(line), flush=True)
+    vae.close()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+
 
 def run_kernel_only(args):
     """Set up the C2 session (with --blocks resident blocks) and launch one block kernel `iters` times.
@@ -209,6 +341,10 @@ def main():
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--stage", choices=["dit", "vae"], default="dit",
+                    help="dit: the denoise loop (the metric); vae: the VAE decode after it")
+    ap.add_argument("--vae-latent", default=None,
+                    help="profiling aid: H,W of the unpacked latent of --stage vae (default 128,128: 1024x1024)")
     args = ap.parse_args()
     global WIDTH, HEIGHT, TEXT, VALID
     WIDTH, HEIGHT, TEXT, VALID, config_precision, args.workload = CONFIGS[args.config]
@@ -217,6 +353,8 @@ def main():
         return run_kernel_only(args)
     if args.warmup < 3:
         args.warmup = 3
+    if args.stage == "vae":
+        return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
     if args.impl == "reference":
         return run_reference(args)
 

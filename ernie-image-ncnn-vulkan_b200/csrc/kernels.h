@@ -162,8 +162,8 @@ struct ConvArgs
     int ldo = 0;
     const float *bias = nullptr;
     const float *resid = nullptr;
-    // GroupNorm partials of the written values: stats[group][row_block] = (sum, sum of squares) in FP64
-    // over groups of cpg channels (4, 8 or 16) and row blocks of 32 pixels (conv_row_blocks of them)
+    // GroupNorm partials of the written values: stats[group][slot] = (sum, sum of squares) in FP64 over
+    // groups of cpg channels (4, 8 or 16); one slot per epilogue warp (conv_stat_slots of them)
     double2 *stats = nullptr;
     int cpg = 0;
     // conv_out (16 output columns, valid_out used): planar FP32 [valid_out][pixels], interleaved bytes
@@ -184,11 +184,13 @@ struct ConvLaunch
     int cout_rows = 0;
     int height = 0, width = 0, cin = 0, taps = 1, cout = 0; // cin a multiple of 64; cout 16 or a multiple of 128
 };
-inline int conv_row_blocks(int height, int width) { return height * ((width + 127) / 128) * 4; }
+// GroupNorm partial slots per group that launch_conv writes for this launch (8 per CTA of its grid).
+int conv_stat_slots(const ConvLaunch &launch, int num_sms);
 constexpr int kSoftmaxMaxRow = 57344; // keys per attention row (the row is staged in shared memory)
 int launch_conv(const ConvLaunch &launch, const ConvArgs &epilogue, int num_sms, cudaStream_t stream);
-// scale[c] = gamma[c] / sqrt(var_g + eps), shift[c] = beta[c] - mean_g * scale[c] from the partials of 32 groups.
-int launch_gn_finalize(const double2 *stats, int row_blocks, long long count, int cpg, const float *gamma,
+// scale[c] = gamma[c] / sqrt(var_g + eps), shift[c] = beta[c] - mean_g * scale[c] from `slots` partials of
+// each of 32 groups.
+int launch_gn_finalize(const double2 *stats, int slots, long long count, int cpg, const float *gamma,
                        const float *beta, float eps, float *scale, float *shift, cudaStream_t stream);
 // x * scale + shift (+ Swish), FP32 NHWC [pixels][channels] -> BF16 operand [pixels][planes * channels].
 int launch_gn_apply(const float *x, long long pixels, int channels, const float *scale, const float *shift, int silu,

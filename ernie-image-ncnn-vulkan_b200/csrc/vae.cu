@@ -36,7 +36,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 namespace
 {
-constexpr int CM = 128, CK = 64, kConvThreads = 192;
+constexpr int CM = 128, CK = 64, kConvThreads = 320, kEpiWarps = 8;
 enum : int
 {
     kErrConvProducerTimeout = 31,
@@ -44,23 +44,28 @@ enum : int
     kErrConvEpilogueTimeout = 33,
 };
 
-template <int BN, bool PROMOTE> struct ConvCfg
+// Output tile: MSUB sub-tiles of 128 pixels (128-pixel row segments, consecutive in the flattened
+// row-segment order) x BN channels. MSUB = 2 lets two M=128 MMAs share each B tile.
+template <int BN, bool PROMOTE, int MSUB> struct ConvCfg
 {
     static_assert(BN == 16 || BN == 128 || BN == 256, "tile widths");
-    static_assert(!PROMOTE || BN <= 128, "FP32 promotion keeps a BN-column running sum per thread");
-    static constexpr int kStages = BN == 256 ? 4 : BN == 128 ? 6 : 8;
-    static constexpr int kABytes = CM * CK * 2;
+    static_assert(MSUB == 1 || (MSUB == 2 && BN == 128), "two pixel sub-tiles with 128-channel tiles only");
+    static_assert(!PROMOTE || (BN <= 128 && MSUB == 1), "FP32 promotion keeps BN/2 running sums per thread");
+    static constexpr int kStages = (BN == 256 || MSUB == 2) ? 4 : BN == 128 ? 6 : 8;
+    static constexpr int kABytes = MSUB * CM * CK * 2;
     static constexpr int kBBytes = BN * CK * 2;
-    static constexpr int kStageBytes = kABytes + kBBytes; // a multiple of 1024 for every BN
-    static constexpr int kUsedCols = PROMOTE ? 3 * BN : 2 * BN;
-    static constexpr int kTmemCols = kUsedCols <= 32    ? 32
-                                     : kUsedCols <= 64  ? 64
-                                     : kUsedCols <= 128 ? 128
-                                     : kUsedCols <= 256 ? 256
-                                                        : 512;
-    static constexpr int kChunk = BN >= 32 ? 32 : 16;
+    static constexpr int kStageBytes = kABytes + kBBytes; // a multiple of 1024 for every configuration
+    static constexpr int kAccCols = MSUB * BN;           // one accumulator buffer
+    static constexpr int kTmemCols = 2 * kAccCols <= 32 ? 32 : 2 * kAccCols;
+    // columns per epilogue warp: warps 2..5 and 6..9 take the two sub-tiles, or the two column halves
+    static constexpr int kWarpCols = MSUB == 2 ? BN : (BN >= 32 ? BN / 2 : BN);
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+    // per epilogue warp: a [32][20] FP32 staging tile and 32 FP64 (sum, sum of squares) GroupNorm slots
+    static constexpr int kStageFloats = 32 * 20;
+    static constexpr int kEpilogueOffset = kStages * kStageBytes + kBarrierBytes;
+    static constexpr int kEpilogueBytes = kEpiWarps * (kStageFloats * 4 + 32 * 16);
+    static constexpr int kSmemBytes = kEpilogueOffset + kEpilogueBytes + 1024;
+    static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 };
 
 // Plane pair (operand plane, weight plane) of product p: one product in BF16 mode; (0,0) (1,0) (2,0)
@@ -86,101 +91,115 @@ __device__ __forceinline__ double warp_sum(double v)
     return v;
 }
 
-// GroupNorm partials of one chunk: per group of CPG channels, the warp's (sum, sum of squares) over its
-// 32 pixels in FP64, stored at stats[group][row_block] (every slot written once: deterministic).
-template <int CH, int CPG>
-__device__ __forceinline__ void chunk_stats(const float (&v)[CH], bool valid, int col, int row_block,
-                                            int row_blocks, int lane, double2 *stats)
+// conv_out's chunk: planar FP32 [valid_out][pixels] and the RGB bytes of src/pipeline.cpp:145-163, one
+// pixel per thread (the lanes' stores are consecutive pixels).
+__device__ __forceinline__ void planar_chunk(const float (&v)[16], int col, bool valid, long long pixel,
+                                             long long pixels, const ConvArgs &a)
 {
+    if (!valid) return;
 #pragma unroll
-    for (int g = 0; g < CH / CPG; ++g)
-    {
-        double s = 0.0, q = 0.0;
-        if (valid)
+    for (int j = 0; j < 16; ++j)
+        if (col + j < a.valid_out)
         {
-#pragma unroll
-            for (int j = 0; j < CPG; ++j)
+            const float x = v[j] + (a.bias ? __ldg(a.bias + col + j) : 0.f);
+            a.planar[static_cast<size_t>(col + j) * pixels + pixel] = x;
+            if (!isfinite(x))
             {
-                const double d = v[g * CPG + j];
-                s += d;
-                q = fma(d, d, q);
+                if (a.nonfinite) atomicOr(a.nonfinite, 1);
+            }
+            else if (a.rgb)
+            {
+                const float n = fminf(fmaxf(__fadd_rn(__fmul_rn(x, 0.5f), 0.5f), 0.f), 1.f);
+                a.rgb[static_cast<size_t>(pixel) * a.valid_out + col + j] =
+                    static_cast<uint8_t>(rintf(__fmul_rn(n, 255.f)));
             }
         }
-        s = warp_sum(s);
-        q = warp_sum(q);
-        if (lane == 0) stats[static_cast<size_t>(col / CPG + g) * row_blocks + row_block] = make_double2(s, q);
-    }
 }
 
-template <int CH>
-__device__ __forceinline__ void conv_chunk(float (&v)[CH], int col, bool valid, long long pixel, long long pixels,
-                                           int row_block, int row_blocks, int lane, const ConvArgs &a)
+// One 16-column chunk of the warp's 32 pixels (thread `lane` holds pixel row `lane` in v), staged through
+// shared memory and written row-major: lane covers columns col + 4*(lane % 4) .. +3 of rows 8*i + lane / 4,
+// so 4 lanes store one 64-byte row segment. out = (acc + bias) + resid for the first `limit` rows; the
+// GroupNorm partial sums of the written values are added, per group, into the warp's FP64 slots `acc`.
+__device__ __forceinline__ void rows_chunk(const float (&v)[16], float *stage, double2 *acc, int col, int limit,
+                                           long long pixel_first, int lane, const ConvArgs &a)
 {
-    if (a.bias)
-    {
+    float4 *mine = reinterpret_cast<float4 *>(stage + lane * 20);
 #pragma unroll
-        for (int j = 0; j < CH; ++j) v[j] += __ldg(a.bias + col + j);
+    for (int k = 0; k < 4; ++k) mine[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    __syncwarp();
+    const int c4 = (lane & 3) * 4, oct = lane >> 2;
+    const float4 b = a.bias ? __ldg(reinterpret_cast<const float4 *>(a.bias + col + c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // all residual loads first: `out` may alias `resid` (in place), so a load placed after an earlier
+    // row's store could not be hoisted above it
+    float4 u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        const int r = 8 * i + oct;
+        u[i] = a.resid && r < limit ? *reinterpret_cast<const float4 *>(a.resid + (pixel_first + r) * a.ldo + col + c4)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (a.planar)
-    {
-        // conv_out: planar FP32 [valid_out][pixels] and the RGB bytes of src/pipeline.cpp:145-163
-        if (valid)
-        {
+    const bool stats = a.stats != nullptr;
+    double s = 0.0, q = 0.0;
 #pragma unroll
-            for (int j = 0; j < CH; ++j)
-                if (col + j < a.valid_out)
-                {
-                    const float x = v[j];
-                    a.planar[static_cast<size_t>(col + j) * pixels + pixel] = x;
-                    if (!isfinite(x))
-                    {
-                        if (a.nonfinite) atomicOr(a.nonfinite, 1);
-                    }
-                    else if (a.rgb)
-                    {
-                        const float n = fminf(fmaxf(__fadd_rn(__fmul_rn(x, 0.5f), 0.5f), 0.f), 1.f);
-                        a.rgb[static_cast<size_t>(pixel) * a.valid_out + col + j] =
-                            static_cast<uint8_t>(rintf(__fmul_rn(n, 255.f)));
-                    }
-                }
-        }
-        return;
-    }
-    if (valid && a.resid)
+    for (int i = 0; i < 4; ++i)
     {
-        const float4 *r = reinterpret_cast<const float4 *>(a.resid + pixel * a.ldo + col);
-#pragma unroll
-        for (int j = 0; j < CH / 4; ++j)
+        const int r = 8 * i + oct;
+        float4 t = *reinterpret_cast<const float4 *>(stage + r * 20 + c4);
+        // (conv + bias) + residual, the reference graph's Convolution then BinaryOp add
+        t.x = (t.x + b.x) + u[i].x;
+        t.y = (t.y + b.y) + u[i].y;
+        t.z = (t.z + b.z) + u[i].z;
+        t.w = (t.w + b.w) + u[i].w;
+        if (r < limit)
         {
-            const float4 t = r[j];
-            v[4 * j] += t.x;
-            v[4 * j + 1] += t.y;
-            v[4 * j + 2] += t.z;
-            v[4 * j + 3] += t.w;
+            if (a.out) *reinterpret_cast<float4 *>(a.out + (pixel_first + r) * a.ldo + col + c4) = t;
+            if (stats)
+            {
+                const double d0 = t.x, d1 = t.y, d2 = t.z, d3 = t.w;
+                s += (d0 + d1) + (d2 + d3);
+                q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+            }
         }
     }
-    if (valid && a.out)
-    {
-        float4 *o = reinterpret_cast<float4 *>(a.out + pixel * a.ldo + col);
+    __syncwarp();
+    if (!stats) return;
+    // lanes of one group: the eight row octets, and cpg / 4 neighbouring column quads
 #pragma unroll
-        for (int j = 0; j < CH / 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    }
-    if (a.stats)
+    for (int o = 4; o <= 16; o <<= 1)
     {
-        switch (a.cpg)
-        {
-        case 4: chunk_stats<CH, 4>(v, valid, col, row_block, row_blocks, lane, a.stats); break;
-        case 8: chunk_stats<CH, 8>(v, valid, col, row_block, row_blocks, lane, a.stats); break;
-        default: chunk_stats<CH, 16>(v, valid, col, row_block, row_blocks, lane, a.stats); break;
-        }
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        q += __shfl_xor_sync(0xffffffffu, q, o);
+    }
+    if (a.cpg >= 8)
+    {
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        q += __shfl_xor_sync(0xffffffffu, q, 1);
+    }
+    if (a.cpg >= 16)
+    {
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        q += __shfl_xor_sync(0xffffffffu, q, 2);
+    }
+    if (lane < 4 && (lane & (a.cpg / 4 - 1)) == 0)
+    {
+        const int g = (col + c4) / a.cpg;
+        acc[g].x += s;
+        acc[g].y += q;
     }
 }
 
-template <int BN, bool PROMOTE>
+template <int N> __device__ __forceinline__ void tmem_load_n(uint32_t taddr, float (&v)[N])
+{
+    static_assert(N == 16, "16-column loads");
+    tmem_load_16(taddr, v);
+}
+
+template <int BN, bool PROMOTE, int MSUB>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, ConvArgs args)
 {
-    using C = ConvCfg<BN, PROMOTE>;
+    using C = ConvCfg<BN, PROMOTE, MSUB>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -191,11 +210,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     auto tfull_bar = [&](int i) { return bars + 8u * (2 * C::kStages + i); };
     auto tempty_bar = [&](int i) { return bars + 8u * (2 * C::kStages + 2 + i); };
     const uint32_t slot = bars + 8u * (2 * C::kStages + 4);
-    auto tile_a = [&](int s) { return base + s * C::kStageBytes; };
+    auto tile_a = [&](int s, int sub) { return base + s * C::kStageBytes + sub * (CM * CK * 2); };
     auto tile_b = [&](int s) { return base + s * C::kStageBytes + C::kABytes; };
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int tiles_x = (args.width + CM - 1) / CM, m_tiles = args.height * tiles_x;
+    const int tiles_x = (args.width + CM - 1) / CM, segments = args.height * tiles_x;
+    const int m_tiles = (segments + MSUB - 1) / MSUB;
     const int n_tiles = args.cout / BN, tiles = m_tiles * n_tiles;
     const int cblk = args.cin / CK, k_blocks = args.taps * cblk;
     const int span = PROMOTE ? args.group : k_blocks; // k-blocks per accumulation chain
@@ -211,7 +231,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         for (int i = 0; i < 2; ++i)
         {
             mbar_init(tfull_bar(i), 1);
-            mbar_init(tempty_bar(i), 4);
+            mbar_init(tempty_bar(i), kEpiWarps);
         }
         fence_barrier_init();
     }
@@ -241,7 +261,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             {
                 // output channels fastest: CTAs working at the same time share operand rows in L2
                 const int m_blk = tile / n_tiles, n_blk = tile - m_blk * n_tiles;
-                const int y = m_blk / tiles_x, x0 = (m_blk - y * tiles_x) * CM;
+                int ys[MSUB], xs[MSUB];
+#pragma unroll
+                for (int sub = 0; sub < MSUB; ++sub)
+                {
+                    const int seg = m_blk * MSUB + sub; // past the last segment: rows past the image, zero-filled
+                    ys[sub] = seg / tiles_x;
+                    xs[sub] = (seg - ys[sub] * tiles_x) * CM;
+                }
                 for (int kb = 0; kb < k_blocks && ok; ++kb)
                 {
                     const int tap = kb / cblk, c0 = (kb - tap * cblk) * CK;
@@ -257,7 +284,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                             break;
                         }
                         mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
-                        tma_load_3d(tile_a(stage), &map_a, full_bar(stage), pa * args.cin + c0, x0 + dx, y + dy);
+#pragma unroll
+                        for (int sub = 0; sub < MSUB; ++sub)
+                            tma_load_3d(tile_a(stage, sub), &map_a, full_bar(stage), pa * args.cin + c0, xs[sub] + dx,
+                                        ys[sub] + dy);
                         tma_load_2d(tile_b(stage), &map_b, full_bar(stage), pb * args.taps * args.cin + kb * CK,
                                     n_blk * BN);
                         if (++stage == C::kStages)
@@ -294,7 +324,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccCols);
                     for (int kb = kb0; kb < kb0 + span && ok; ++kb)
                     {
                         for (int p = 0; p < products; ++p)
@@ -306,12 +336,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                                 break;
                             }
                             tc_fence_after();
-                            const uint64_t a_desc = smem_desc_sw128(tile_a(stage));
                             const uint64_t b_desc = smem_desc_sw128(tile_b(stage));
 #pragma unroll
-                            for (int k = 0; k < CK / 16; ++k)
-                                umma_bf16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
-                                          (kb != kb0 || p != 0 || k != 0) ? 1u : 0u);
+                            for (int sub = 0; sub < MSUB; ++sub)
+                            {
+                                const uint64_t a_desc = smem_desc_sw128(tile_a(stage, sub));
+#pragma unroll
+                                for (int k = 0; k < CK / 16; ++k)
+                                    umma_bf16(d_tmem + sub * BN, a_desc + 2u * k, b_desc + 2u * k, idesc,
+                                              (kb != kb0 || p != 0 || k != 0) ? 1u : 0u);
+                            }
                             umma_commit(empty_bar(stage));
                             if (++stage == C::kStages)
                             {
@@ -327,20 +361,36 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     else
     {
-        constexpr int CH = C::kChunk;
-        const int quarter = warp & 3;
+        constexpr int CH = 16, CW = C::kWarpCols;
+        const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+        // this warp's pixel sub-tile and column range of each tile
+        const int sub = MSUB == 2 ? half : 0;
+        const int col0 = MSUB == 2 ? 0 : half * CW;
+        const bool active = MSUB == 2 || BN >= 32 || half == 0; // conv_out's 16 columns: one warp group
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const long long pixels = static_cast<long long>(args.height) * args.width;
-        const int row_blocks = m_tiles * 4;
+        float *stage = reinterpret_cast<float *>(base_ptr + C::kEpilogueOffset) + e * C::kStageFloats;
+        double2 *group_acc =
+            reinterpret_cast<double2 *>(base_ptr + C::kEpilogueOffset + kEpiWarps * C::kStageFloats * 4) + e * 32;
+        group_acc[lane] = make_double2(0.0, 0.0);
+        __syncwarp();
         int unit = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
         {
             const int m_blk = tile / n_tiles, n_blk = tile - m_blk * n_tiles;
-            const int y = m_blk / tiles_x, x = (m_blk - y * tiles_x) * CM + quarter * 32 + lane;
-            const bool valid = x < args.width;
-            const long long pixel = static_cast<long long>(y) * args.width + x;
-            const int row_block = m_blk * 4 + quarter;
+            const int seg = m_blk * MSUB + sub;
+            const int y = seg / tiles_x, x_first = (seg - y * tiles_x) * CM + quarter * 32;
+            // rows of this warp inside the image (0 for a sub-tile past the last row)
+            const int limit = y < args.height ? min(32, args.width - x_first) : 0;
+            const long long pixel_first = static_cast<long long>(y) * args.width + x_first;
+            const uint32_t acc_cols = static_cast<uint32_t>(sub * BN + col0);
+            auto emit = [&](const float(&v)[CH], int c) {
+                if constexpr (BN >= 32)
+                    rows_chunk(v, stage, group_acc, n_blk * BN + col0 + c, limit, pixel_first, lane, args);
+                else
+                    planar_chunk(v, n_blk * BN + col0 + c, lane < limit, pixel_first + lane, pixels, args);
+            };
             if constexpr (!PROMOTE)
             {
                 const int acc = unit & 1;
@@ -351,13 +401,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     break;
                 }
                 tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < BN; c += CH)
+                if (active)
                 {
-                    float v[CH];
-                    if constexpr (CH == 32) tmem_load_32(lane_base + acc * BN + c, v);
-                    else tmem_load_16(lane_base + acc * BN + c, v);
-                    conv_chunk<CH>(v, n_blk * BN + c, valid, pixel, pixels, row_block, row_blocks, lane, args);
+#pragma unroll 1
+                    for (int c = 0; c < CW; c += CH)
+                    {
+                        float v[CH];
+                        tmem_load_n(lane_base + acc * C::kAccCols + acc_cols + c, v);
+                        emit(v, c);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -366,9 +418,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
             else
             {
-                float sum[BN];
+                float sum[CW];
 #pragma unroll
-                for (int j = 0; j < BN; ++j) sum[j] = 0.f;
+                for (int j = 0; j < CW; ++j) sum[j] = 0.f;
                 for (int kb0 = 0; kb0 < k_blocks; kb0 += span, ++unit)
                 {
                     const int acc = unit & 1;
@@ -380,30 +432,40 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         break;
                     }
                     tc_fence_after();
-#pragma unroll
-                    for (int c = 0; c < BN; c += CH)
+                    if (active)
                     {
-                        float v[CH];
-                        if constexpr (CH == 32) tmem_load_32(lane_base + acc * BN + c, v);
-                        else tmem_load_16(lane_base + acc * BN + c, v);
 #pragma unroll
-                        for (int j = 0; j < CH; ++j) sum[c + j] += v[j];
+                        for (int c = 0; c < CW; c += CH)
+                        {
+                            float v[CH];
+                            tmem_load_n(lane_base + acc * C::kAccCols + acc_cols + c, v);
+#pragma unroll
+                            for (int j = 0; j < CH; ++j) sum[c + j] += v[j];
+                        }
                     }
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty_bar(acc));
                 }
                 if (!ok) break;
-#pragma unroll
-                for (int c = 0; c < BN; c += CH)
+                if (active)
                 {
-                    float v[CH];
 #pragma unroll
-                    for (int j = 0; j < CH; ++j) v[j] = sum[c + j];
-                    conv_chunk<CH>(v, n_blk * BN + c, valid, pixel, pixels, row_block, row_blocks, lane, args);
+                    for (int c = 0; c < CW; c += CH)
+                    {
+                        float v[CH];
+#pragma unroll
+                        for (int j = 0; j < CH; ++j) v[j] = sum[c + j];
+                        emit(v, c);
+                    }
                 }
             }
         }
+        // this warp's GroupNorm partials: every slot written (zero for groups it saw no tile of), in the
+        // fixed tile order of this CTA, so the sums are deterministic for a given grid
+        __syncwarp();
+        if (args.stats)
+            args.stats[static_cast<size_t>(lane) * gridDim.x * kEpiWarps + blockIdx.x * kEpiWarps + e] = group_acc[lane];
     }
     __syncthreads();
     if (warp == 1)
@@ -413,13 +475,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
 }
 
-template <int BN, bool PROMOTE> cudaError_t ensure_conv_attributes()
+template <int BN, bool PROMOTE, int MSUB> cudaError_t ensure_conv_attributes()
 {
     static std::once_flag once;
     static cudaError_t attr = cudaSuccess;
     std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(conv_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    ConvCfg<BN, PROMOTE>::kSmemBytes);
+        attr = cudaFuncSetAttribute(conv_kernel<BN, PROMOTE, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    ConvCfg<BN, PROMOTE, MSUB>::kSmemBytes);
     });
     return attr;
 }
@@ -453,18 +515,41 @@ bool make_weight_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool PROMOTE> int launch_conv_impl(const ConvLaunch &l, ConvArgs args, int num_sms, cudaStream_t stream)
+// Tile shape of a launch: (BN, MSUB). conv_out: 16 columns; FP32-exact mode: 128; BF16 mode: 256 columns,
+// or 2 x 128 pixels x 128 columns where the width is not a multiple of 256.
+void conv_shape(const ConvLaunch &l, int &bn, int &msub)
 {
-    const cudaError_t attr = ensure_conv_attributes<BN, PROMOTE>();
+    msub = 1;
+    if (l.cout == 16) bn = 16;
+    else if (l.a_planes == 3) bn = 128;
+    else if (l.cout % 256 == 0) bn = 256;
+    else
+    {
+        bn = 128;
+        msub = 2;
+    }
+}
+
+int conv_grid(const ConvLaunch &l, int num_sms)
+{
+    int bn = 0, msub = 1;
+    conv_shape(l, bn, msub);
+    const long long segments = static_cast<long long>(l.height) * ((l.width + CM - 1) / CM);
+    const long long tiles = (segments + msub - 1) / msub * (l.cout / bn);
+    return static_cast<int>(tiles < num_sms ? tiles : num_sms);
+}
+
+template <int BN, bool PROMOTE, int MSUB>
+int launch_conv_impl(const ConvLaunch &l, ConvArgs args, int num_sms, cudaStream_t stream)
+{
+    using C = ConvCfg<BN, PROMOTE, MSUB>;
+    const cudaError_t attr = ensure_conv_attributes<BN, PROMOTE, MSUB>();
     if (attr != cudaSuccess) return attr;
     CUtensorMap map_a, map_b;
     if (!make_operand_map(&map_a, l.a, static_cast<uint64_t>(l.a_planes) * l.cin, l.width, l.height) ||
         !make_weight_map(&map_b, l.b, static_cast<uint64_t>(l.cout_rows), static_cast<uint64_t>(l.b_row), BN))
         return cudaErrorInvalidValue;
-    const long long tiles =
-        static_cast<long long>(l.height) * ((l.width + CM - 1) / CM) * (l.cout / BN);
-    const int grid = tiles < num_sms ? static_cast<int>(tiles) : num_sms;
-    conv_kernel<BN, PROMOTE><<<grid, kConvThreads, ConvCfg<BN, PROMOTE>::kSmemBytes, stream>>>(map_a, map_b, args);
+    conv_kernel<BN, PROMOTE, MSUB><<<conv_grid(l, num_sms), kConvThreads, C::kSmemBytes, stream>>>(map_a, map_b, args);
     return cudaGetLastError();
 }
 
@@ -508,15 +593,15 @@ __device__ __forceinline__ void store_planes8(__nv_bfloat16 *dst, long long plan
     for (int q = 0; q < 3; ++q) *reinterpret_cast<uint4 *>(dst + q * plane_stride) = *reinterpret_cast<const uint4 *>(p[q]);
 }
 
-__global__ void gn_finalize_kernel(const double2 *stats, int row_blocks, long long count, int cpg,
+__global__ void gn_finalize_kernel(const double2 *stats, int slots, long long count, int cpg,
                                    const float *gamma, const float *beta, float eps, float *scale, float *shift)
 {
     __shared__ double part[2][32];
     const int g = blockIdx.x;
     double s = 0.0, q = 0.0;
-    for (int i = threadIdx.x; i < row_blocks; i += blockDim.x)
+    for (int i = threadIdx.x; i < slots; i += blockDim.x)
     {
-        const double2 v = stats[static_cast<size_t>(g) * row_blocks + i];
+        const double2 v = stats[static_cast<size_t>(g) * slots + i];
         s += v.x;
         q += v.y;
     }
@@ -550,27 +635,39 @@ __global__ void gn_finalize_kernel(const double2 *stats, int row_blocks, long lo
 }
 
 // y = x * scale[c] + shift[c] (then Swish x / (1 + exp(-x)) when silu), FP32 NHWC -> BF16 operand planes.
-__global__ void gn_apply_kernel(const float *x, long long pixels, int channels, const float *scale,
-                                const float *shift, int silu, __nv_bfloat16 *out, int planes)
+// channels = 2^log2c (the decoder's widths 128, 256, 512); 8 channels per thread. BF16 mode evaluates the
+// Swish with the fast exponential and reciprocal (far below the BF16 rounding that follows); FP32-exact
+// mode with expf and an IEEE division.
+__global__ void gn_apply_kernel(const float *x, long long pixels, int log2c, const float *scale, const float *shift,
+                                int silu, __nv_bfloat16 *out, int planes)
 {
-    const int per_pixel = channels / 8;
-    const long long total = pixels * per_pixel;
+    const int channels = 1 << log2c;
+    const long long total = pixels << (log2c - 3);
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x)
     {
-        const long long p = i / per_pixel;
-        const int c0 = static_cast<int>(i - p * per_pixel) * 8;
-        const float4 *src = reinterpret_cast<const float4 *>(x + p * channels + c0);
+        const long long e = i * 8; // element index p * channels + c0
+        const int c0 = static_cast<int>(e & (channels - 1));
+        const float4 *src = reinterpret_cast<const float4 *>(x + e);
         const float4 a = src[0], b = src[1];
+        const float4 sa = __ldg(reinterpret_cast<const float4 *>(scale + c0)),
+                     sb = __ldg(reinterpret_cast<const float4 *>(scale + c0 + 4));
+        const float4 ha = __ldg(reinterpret_cast<const float4 *>(shift + c0)),
+                     hb = __ldg(reinterpret_cast<const float4 *>(shift + c0 + 4));
         float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const float sc[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+        const float sh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j)
         {
-            float y = __fadd_rn(__fmul_rn(v[j], __ldg(scale + c0 + j)), __ldg(shift + c0 + j));
-            if (silu) y = __fdiv_rn(y, __fadd_rn(1.f, expf(-y)));
+            float y = __fadd_rn(__fmul_rn(v[j], sc[j]), sh[j]);
+            if (silu)
+                y = planes == 1 ? __fmul_rn(y, __frcp_rn(__fadd_rn(1.f, __expf(-y))))
+                                : __fdiv_rn(y, __fadd_rn(1.f, expf(-y)));
             v[j] = y;
         }
-        store_planes8(out + p * planes * channels + c0, channels, planes, v);
+        // planes side by side per pixel: pixel p's plane q starts at p * planes * channels + q * channels
+        store_planes8(out + (planes == 1 ? e : 3 * e - 2 * c0), channels, planes, v);
     }
 }
 
@@ -630,6 +727,90 @@ __global__ void vae_input_kernel(const float *unpacked, long long pixels, const 
         const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int o0 = 32; o0 < 64; o0 += 8) store_planes8(dst + o0, 64, planes, zero);
+    }
+}
+
+// Row softmax with the row in registers (n <= 2048 * EPT4 keys, 512 threads): FP32 max and exp, per-thread
+// FP32 partial sums reduced in FP64; P = e * (1 / sum) as BF16 planes [rows][planes * ldp], zero from n.
+template <int EPT4>
+__global__ void __launch_bounds__(512) softmax_rows_reg_kernel(const float *s, int lds, int n, float scale,
+                                                               __nv_bfloat16 *p, int ldp, int planes)
+{
+    __shared__ float red_max[16];
+    __shared__ double red_sum[16];
+    const long long r = blockIdx.x;
+    const float4 *src = reinterpret_cast<const float4 *>(s + r * lds);
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    float4 v[EPT4];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < EPT4; ++k)
+    {
+        const int i = 4 * (k * 512 + tid);
+        float4 t = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (i + 3 < n) t = src[k * 512 + tid];
+        else if (i < n)
+        {
+            t.x = s[r * lds + i];
+            if (i + 1 < n) t.y = s[r * lds + i + 1];
+            if (i + 2 < n) t.z = s[r * lds + i + 2];
+        }
+        v[k] = t;
+        m = fmaxf(m, fmaxf(fmaxf(t.x, t.y), fmaxf(t.z, t.w)));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red_max[warp] = m;
+    __syncthreads();
+    m = red_max[0];
+#pragma unroll
+    for (int w = 1; w < 16; ++w) m = fmaxf(m, red_max[w]);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < EPT4; ++k)
+    {
+        float4 &t = v[k];
+        t.x = expf(__fmul_rn(t.x - m, scale)); // masked keys: exp(-inf) = 0
+        t.y = expf(__fmul_rn(t.y - m, scale));
+        t.z = expf(__fmul_rn(t.z - m, scale));
+        t.w = expf(__fmul_rn(t.w - m, scale));
+        sum += (t.x + t.y) + (t.z + t.w);
+    }
+    double total = warp_sum(static_cast<double>(sum));
+    if (lane == 0) red_sum[warp] = total;
+    __syncthreads();
+    total = 0.0;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) total += red_sum[w];
+    const float inv = static_cast<float>(1.0 / total);
+    __nv_bfloat16 *dst = p + r * planes * ldp;
+#pragma unroll
+    for (int k = 0; k < EPT4; ++k)
+    {
+        const int i = 4 * (k * 512 + tid);
+        if (i >= ldp) break;
+        const float e[4] = {v[k].x * inv, v[k].y * inv, v[k].z * inv, v[k].w * inv};
+        if (planes == 1)
+        {
+            __nv_bfloat162 h[2] = {__floats2bfloat162_rn(e[0], e[1]), __floats2bfloat162_rn(e[2], e[3])};
+            *reinterpret_cast<uint2 *>(dst + i) = *reinterpret_cast<const uint2 *>(h);
+        }
+        else
+        {
+            __align__(8) __nv_bfloat16 q[3][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+            {
+                float hi, mid, lo;
+                split3f(e[j], hi, mid, lo);
+                q[0][j] = __float2bfloat16_rn(hi);
+                q[1][j] = __float2bfloat16_rn(mid);
+                q[2][j] = __float2bfloat16_rn(lo);
+            }
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+                *reinterpret_cast<uint2 *>(dst + pl * ldp + i) = *reinterpret_cast<const uint2 *>(q[pl]);
+        }
     }
 }
 
@@ -770,11 +951,11 @@ __global__ void synth_f32_kernel(uint64_t seed, uint64_t stream_id, float scale,
 
 int prepare_conv_kernels()
 {
-    cudaError_t e = ensure_conv_attributes<256, false>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<128, false>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<16, false>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<128, true>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<16, true>();
+    cudaError_t e = ensure_conv_attributes<256, false, 1>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<128, false, 2>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<16, false, 1>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<128, true, 1>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<16, true, 1>();
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(softmax_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSoftmaxMaxRow * 4);
     return e;
@@ -786,6 +967,8 @@ int conv_group(int k_blocks)
         if (k_blocks % g == 0) return g;
     return 1;
 }
+
+int conv_stat_slots(const ConvLaunch &l, int num_sms) { return kEpiWarps * conv_grid(l, num_sms); }
 
 int launch_conv(const ConvLaunch &l, const ConvArgs &epi, int num_sms, cudaStream_t stream)
 {
@@ -804,29 +987,32 @@ int launch_conv(const ConvLaunch &l, const ConvArgs &epi, int num_sms, cudaStrea
     args.products = promote ? (l.b_planes == 3 ? 6 : 3) : 1;
     args.group = conv_group(l.taps * l.cin / CK);
     if (args.stats && args.cpg != 4 && args.cpg != 8 && args.cpg != 16) return cudaErrorInvalidValue;
-    if (args.planar && l.cout != 16) return cudaErrorInvalidValue;
+    if ((args.planar != nullptr) != (l.cout == 16)) return cudaErrorInvalidValue; // 16 columns: conv_out only
     if ((args.out || args.resid) && (args.ldo < l.cout || args.ldo % 4)) return cudaErrorInvalidValue;
-    if (l.cout == 16) return promote ? launch_conv_impl<16, true>(l, args, num_sms, stream)
-                                     : launch_conv_impl<16, false>(l, args, num_sms, stream);
+    if (l.cout == 16) return promote ? launch_conv_impl<16, true, 1>(l, args, num_sms, stream)
+                                     : launch_conv_impl<16, false, 1>(l, args, num_sms, stream);
     if (l.cout % 128) return cudaErrorInvalidValue;
-    if (promote) return launch_conv_impl<128, true>(l, args, num_sms, stream);
-    if (l.cout % 256 == 0) return launch_conv_impl<256, false>(l, args, num_sms, stream);
-    return launch_conv_impl<128, false>(l, args, num_sms, stream);
+    if (promote) return launch_conv_impl<128, true, 1>(l, args, num_sms, stream);
+    if (l.cout % 256 == 0) return launch_conv_impl<256, false, 1>(l, args, num_sms, stream);
+    return launch_conv_impl<128, false, 2>(l, args, num_sms, stream);
 }
 
-int launch_gn_finalize(const double2 *stats, int row_blocks, long long count, int cpg, const float *gamma,
+int launch_gn_finalize(const double2 *stats, int slots, long long count, int cpg, const float *gamma,
                        const float *beta, float eps, float *scale, float *shift, cudaStream_t stream)
 {
-    if (cpg < 1 || cpg > 256 || row_blocks < 1 || count < 1) return cudaErrorInvalidValue;
-    gn_finalize_kernel<<<32, 256, 0, stream>>>(stats, row_blocks, count, cpg, gamma, beta, eps, scale, shift);
+    if (cpg < 1 || cpg > 256 || slots < 1 || count < 1) return cudaErrorInvalidValue;
+    gn_finalize_kernel<<<32, 256, 0, stream>>>(stats, slots, count, cpg, gamma, beta, eps, scale, shift);
     return cudaGetLastError();
 }
 
 int launch_gn_apply(const float *x, long long pixels, int channels, const float *scale, const float *shift, int silu,
                     __nv_bfloat16 *out, int planes, cudaStream_t stream)
 {
-    if (channels % 8 || pixels < 1) return cudaErrorInvalidValue;
-    gn_apply_kernel<<<grid_for_count(pixels * channels / 8, 256), 256, 0, stream>>>(x, pixels, channels, scale, shift,
+    if (channels < 8 || (channels & (channels - 1)) || pixels < 1 || (planes != 1 && planes != 3))
+        return cudaErrorInvalidValue;
+    int log2c = 0;
+    while ((1 << log2c) < channels) ++log2c;
+    gn_apply_kernel<<<grid_for_count(pixels * channels / 8, 256), 256, 0, stream>>>(x, pixels, log2c, scale, shift,
                                                                                     silu, out, planes);
     return cudaGetLastError();
 }
@@ -850,8 +1036,13 @@ int launch_vae_input(const float *unpacked, long long pixels, const float *w, co
 int launch_softmax_rows(const float *s, int rows, int lds, int n, float scale, __nv_bfloat16 *p, int ldp, int planes,
                         cudaStream_t stream)
 {
-    if (n < 1 || n > kSoftmaxMaxRow || ldp % 8 || ldp < n || lds < n) return cudaErrorInvalidValue;
-    softmax_rows_kernel<<<rows, 512, static_cast<size_t>(n) * 4, stream>>>(s, lds, n, scale, p, ldp, planes);
+    if (n < 1 || n > kSoftmaxMaxRow || ldp % 8 || ldp < n || lds < n || lds % 4) return cudaErrorInvalidValue;
+    if (ldp <= 16384)
+        softmax_rows_reg_kernel<8><<<rows, 512, 0, stream>>>(s, lds, n, scale, p, ldp, planes);
+    else if (ldp <= 32768)
+        softmax_rows_reg_kernel<16><<<rows, 512, 0, stream>>>(s, lds, n, scale, p, ldp, planes);
+    else
+        softmax_rows_kernel<<<rows, 512, static_cast<size_t>(n) * 4, stream>>>(s, lds, n, scale, p, ldp, planes);
     return cudaGetLastError();
 }
 

@@ -238,7 +238,7 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
     p.n = h0 * w0;
     p.npad = (p.n + 255) / 256 * 256;
     const size_t px0 = pixels_of(h0, w0), top = 64 * px0;
-    const int rb_max = conv_row_blocks(8 * h0, 8 * w0);
+    const int slots_max = 8 * v->ctx->num_sms; // GroupNorm partial slots per group (8 per conv CTA)
     Arena arena;
     arena.add(&p.input, 32 * px0);
     arena.add(&p.x, 16384 * px0);
@@ -252,8 +252,8 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
     arena.add(&p.s, static_cast<size_t>(p.n) * p.npad);
     arena.add(&p.p, static_cast<size_t>(p.planes) * p.n * p.npad);
     arena.add(&p.o, static_cast<size_t>(p.n) * 512);
-    arena.add(&p.stats_x, static_cast<size_t>(kGroups) * rb_max);
-    arena.add(&p.stats_h, static_cast<size_t>(kGroups) * rb_max);
+    arena.add(&p.stats_x, static_cast<size_t>(kGroups) * slots_max);
+    arena.add(&p.stats_h, static_cast<size_t>(kGroups) * slots_max);
     arena.add(&p.scale, 512);
     arena.add(&p.shift, 512);
     arena.add(&p.decoded, 3 * top);
@@ -278,13 +278,76 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
 }
 
 // ---- the decoder program -----------------------------------------------------------------------------
+// Kernel classes of the profile (ernie_cuda_vae_profile): algorithmic FLOPs for the tensor-core classes,
+// algorithmic HBM bytes for the others.
+enum ProfileClass : int
+{
+    kProfConv = 0,      // decoder convolutions and the attention's 1x1 projections (FLOPs)
+    kProfAttnGemm = 1,  // attention scores q k^T and probabilities x v (FLOPs)
+    kProfSoftmax = 2,   // bytes
+    kProfNorm = 3,      // GroupNorm statistics + apply (+ Swish) (bytes)
+    kProfUpsample = 4,  // bytes
+    kProfOther = 5,     // post_quant_conv input, attention split, operand conversions (bytes)
+    kProfClasses = 6
+};
+
+// Events around every launch of an eager run, summed per class after the run.
+struct Profiler
+{
+    std::vector<cudaEvent_t> events;
+    std::vector<int> classes;
+    std::vector<double> work;
+    size_t used = 0;
+    int begin(cudaStream_t stream)
+    {
+        if (events.size() < 2 * (used + 1))
+        {
+            cudaEvent_t a = nullptr, b = nullptr;
+            ERNIE_CUDA(cudaEventCreate(&a), "profile event");
+            ERNIE_CUDA(cudaEventCreate(&b), "profile event");
+            events.push_back(a);
+            events.push_back(b);
+        }
+        ERNIE_CUDA(cudaEventRecord(events[2 * used], stream), "profile event");
+        return ERNIE_CUDA_OK;
+    }
+    int end(cudaStream_t stream, int cls, double w)
+    {
+        ERNIE_CUDA(cudaEventRecord(events[2 * used + 1], stream), "profile event");
+        if (classes.size() <= used)
+        {
+            classes.push_back(cls);
+            work.push_back(w);
+        }
+        ++used;
+        return ERNIE_CUDA_OK;
+    }
+    ~Profiler()
+    {
+        for (cudaEvent_t e : events) cudaEventDestroy(e);
+    }
+};
+
 struct Program
 {
     ernie_cuda_vae *v;
     Plan &p;
     cudaStream_t stream;
     int sms;
+    Profiler *prof = nullptr;
+    int slots_x = 0, slots_h = 0; // GroupNorm partial slots written by the last producer of x / h1
     bool fp32() const { return p.planes == 3; }
+
+    // One operation of `kernels` launches, of profile class `cls` and algorithmic work `work`.
+    template <class F> int op(int cls, double work, int kernels, const char *what, F &&launch)
+    {
+        if (prof) ERNIE_TRY(prof->begin(stream));
+        ERNIE_LAUNCH(launch(), what);
+        p.launches += kernels;
+        if (prof) ERNIE_TRY(prof->end(stream, cls, work));
+        return ERNIE_CUDA_OK;
+    }
+    double bytes_bf16(double elements) const { return 2.0 * p.planes * elements; }
 
     int conv(const ConvW &c, const __nv_bfloat16 *a, int h, int w, const ConvArgs &epi)
     {
@@ -303,21 +366,21 @@ struct Program
         ConvArgs args = epi;
         args.bias = c.bias;
         args.error_flag = v->ctx->error_flag;
-        ++p.launches;
-        return from_launch(launch_conv(l, args, sms, stream), "VAE convolution");
+        const double flops = 2.0 * pixels_of(h, w) * c.cout * c.cin * c.taps;
+        if (args.stats) (args.stats == p.stats_x ? slots_x : slots_h) = conv_stat_slots(l, sms);
+        return op(kProfConv, flops, 1, "VAE convolution", [&] { return launch_conv(l, args, sms, stream); });
     }
     // GroupNorm(32) of x (statistics from its producer) + optional Swish -> operand `a`
     int group_norm(const NormW &n, const float *x, const double2 *stats, int h, int w, bool silu)
     {
         const int cpg = n.c / kGroups;
-        ERNIE_LAUNCH(launch_gn_finalize(stats, conv_row_blocks(h, w), static_cast<long long>(pixels_of(h, w)) * cpg,
-                                        cpg, n.gamma, n.beta, kGroupNormEps, p.scale, p.shift, stream),
-                     "GroupNorm statistics");
-        ERNIE_LAUNCH(launch_gn_apply(x, static_cast<long long>(pixels_of(h, w)), n.c, p.scale, p.shift, silu ? 1 : 0,
-                                     p.a, p.planes, stream),
-                     "GroupNorm");
-        p.launches += 2;
-        return ERNIE_CUDA_OK;
+        const long long pixels = static_cast<long long>(pixels_of(h, w));
+        const double elements = static_cast<double>(pixels) * n.c;
+        return op(kProfNorm, 4.0 * elements + bytes_bf16(elements), 2, "GroupNorm", [&] {
+            const int e = launch_gn_finalize(stats, stats == p.stats_x ? slots_x : slots_h, pixels * cpg, cpg, n.gamma, n.beta,
+                                             kGroupNormEps, p.scale, p.shift, stream);
+            return e != 0 ? e : launch_gn_apply(x, pixels, n.c, p.scale, p.shift, silu ? 1 : 0, p.a, p.planes, stream);
+        });
     }
     ConvArgs writes_x(int cout, const float *resid)
     {
@@ -329,16 +392,19 @@ struct Program
         e.cpg = cout / kGroups;
         return e;
     }
+    int to_operand(const float *src, long long rows, int cols)
+    {
+        const double elements = static_cast<double>(rows) * cols;
+        return op(kProfOther, 4.0 * elements + bytes_bf16(elements), 1, "operand",
+                  [&] { return launch_to_operand(src, rows, cols, p.a, fp32() ? 1 : 0, stream); });
+    }
     // ResnetBlock2D: x <- shortcut(x) + conv2(swish(norm2(conv1(swish(norm1(x))))))
     int resnet(const ResnetW &r, int h, int w)
     {
         const float *resid = p.x;
         if (r.has_shortcut)
         {
-            ERNIE_LAUNCH(launch_to_operand(p.x, static_cast<long long>(pixels_of(h, w)), r.cin, p.a, fp32() ? 1 : 0,
-                                           stream),
-                         "shortcut operand");
-            ++p.launches;
+            ERNIE_TRY(to_operand(p.x, static_cast<long long>(pixels_of(h, w)), r.cin));
             ConvArgs e;
             e.out = p.sc;
             e.ldo = r.cout;
@@ -364,8 +430,8 @@ struct Program
         eq.out = p.qkv;
         eq.ldo = 1536;
         ERNIE_TRY(conv(at.qkv, p.a, h, w, eq));
-        ERNIE_LAUNCH(launch_attention_split(p.qkv, n, p.q, p.k, p.vt, npad, p.planes, stream), "attention split");
-        p.launches += 2;
+        ERNIE_TRY(op(kProfOther, 4.0 * n * 1536 + bytes_bf16(1536.0 * n), 2, "attention split",
+                     [&] { return launch_attention_split(p.qkv, n, p.q, p.k, p.vt, npad, p.planes, stream); }));
         ConvLaunch ls;
         ls.a = p.q;
         ls.a_planes = p.planes;
@@ -382,9 +448,11 @@ struct Program
         es.out = p.s;
         es.ldo = npad;
         es.error_flag = v->ctx->error_flag;
-        ERNIE_LAUNCH(launch_conv(ls, es, sms, stream), "attention scores");
-        ERNIE_LAUNCH(launch_softmax_rows(p.s, n, npad, n, 1.f / std::sqrt(512.f), p.p, npad, p.planes, stream),
-                     "attention softmax");
+        const double gemm = 2.0 * n * n * 512;
+        ERNIE_TRY(op(kProfAttnGemm, gemm, 1, "attention scores", [&] { return launch_conv(ls, es, sms, stream); }));
+        ERNIE_TRY(op(kProfSoftmax, 4.0 * n * n + bytes_bf16(static_cast<double>(n) * npad), 1, "attention softmax", [&] {
+            return launch_softmax_rows(p.s, n, npad, n, 1.f / std::sqrt(512.f), p.p, npad, p.planes, stream);
+        }));
         ConvLaunch lo;
         lo.a = p.p;
         lo.a_planes = p.planes;
@@ -401,19 +469,18 @@ struct Program
         eo.out = p.o;
         eo.ldo = 512;
         eo.error_flag = v->ctx->error_flag;
-        ERNIE_LAUNCH(launch_conv(lo, eo, sms, stream), "attention values");
-        ERNIE_LAUNCH(launch_to_operand(p.o, n, 512, p.a, fp32() ? 1 : 0, stream), "attention output operand");
-        p.launches += 4;
+        ERNIE_TRY(op(kProfAttnGemm, gemm, 1, "attention values", [&] { return launch_conv(lo, eo, sms, stream); }));
+        ERNIE_TRY(to_operand(p.o, n, 512));
         return conv(at.out, p.a, h, w, writes_x(512, p.x));
     }
     int run()
     {
         const Layout &L = v->layout;
         int h = p.h0, w = p.w0;
-        ERNIE_LAUNCH(launch_vae_input(p.input, static_cast<long long>(pixels_of(h, w)), L.pq_w, L.pq_b, p.a,
-                                      p.planes, stream),
-                     "post_quant_conv");
-        ++p.launches;
+        const double px = static_cast<double>(pixels_of(h, w));
+        ERNIE_TRY(op(kProfOther, 4.0 * 32 * px + bytes_bf16(64.0 * px), 1, "post_quant_conv", [&] {
+            return launch_vae_input(p.input, static_cast<long long>(px), L.pq_w, L.pq_b, p.a, p.planes, stream);
+        }));
         ERNIE_TRY(conv(L.conv_in, p.a, h, w, writes_x(512, nullptr)));
         ERNIE_TRY(resnet(L.mid[0], h, w));
         ERNIE_TRY(attention(L.attn, h, w));
@@ -423,8 +490,9 @@ struct Program
             for (int j = 0; j < 3; ++j) ERNIE_TRY(resnet(L.up[i][j], h, w));
             if (i == 3) break;
             const int c = L.up[i][2].cout;
-            ERNIE_LAUNCH(launch_upsample(p.x, h, w, c, p.a, p.planes, stream), "upsample");
-            ++p.launches;
+            const double elements = static_cast<double>(pixels_of(h, w)) * c;
+            ERNIE_TRY(op(kProfUpsample, 4.0 * elements + bytes_bf16(4.0 * elements), 1, "upsample",
+                         [&] { return launch_upsample(p.x, h, w, c, p.a, p.planes, stream); }));
             h *= 2;
             w *= 2;
             ERNIE_TRY(conv(L.upsample[i], p.a, h, w, writes_x(c, nullptr)));
@@ -741,5 +809,38 @@ extern "C" int ernie_cuda_vae_decode(ernie_cuda_vae *v, const float *unpacked, i
     int flag = 0;
     ERNIE_TRY(read_status(v, &flag));
     if (nonfinite) *nonfinite = flag;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_vae_profile(ernie_cuda_vae *v, int width, int height, int precision, int iters, double *ms,
+                                      double *work)
+{
+    if (!v || !ms || !work || iters < 1) return fail(ERNIE_CUDA_ERROR, "null argument or iters < 1");
+    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    Profiler prof;
+    for (int c = 0; c < kProfClasses; ++c) ms[c] = work[c] = 0.0;
+    for (int it = 0; it < iters; ++it)
+    {
+        const int launches = p.launches;
+        prof.used = 0;
+        Program prog{v, p, v->ctx->stream, v->ctx->num_sms, &prof};
+        const int rc = prog.run();
+        p.launches = launches;
+        ERNIE_TRY(rc);
+        ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE profile");
+        for (size_t i = 0; i < prof.used; ++i)
+        {
+            float t = 0.f;
+            ERNIE_CUDA(cudaEventElapsedTime(&t, prof.events[2 * i], prof.events[2 * i + 1]), "profile event");
+            ms[prof.classes[i]] += t / iters;
+            if (it == 0) work[prof.classes[i]] += prof.work[i];
+        }
+    }
     return ERNIE_CUDA_OK;
 }

@@ -120,6 +120,7 @@ SIGNATURES = {
     "ernie_cuda_vae_synthesize": (I, [P, U64, I]),
     "ernie_cuda_vae_bytes": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64)]),
     "ernie_cuda_vae_launches": (I, [P, I, I, I, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_profile": (I, [P, I, I, I, I, P, P]),
     "ernie_cuda_vae_decode": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
     "ernie_cuda_vae_decode_device": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
 }
@@ -468,6 +469,14 @@ class Vae:
         n = I(0)
         check(lib().ernie_cuda_vae_launches(self.handle, width, height, precision, ctypes.byref(n)))
         return n.value
+
+    PROFILE_CLASSES = ("conv", "attention_gemm", "softmax", "group_norm", "upsample", "other")
+
+    def profile(self, width, height, precision=BF16, iters=3):
+        """{class: (mean ms, algorithmic work: FLOPs for conv/attention_gemm, bytes otherwise)}."""
+        ms, work = np.zeros(6, np.float64), np.zeros(6, np.float64)
+        check(lib().ernie_cuda_vae_profile(self.handle, width, height, precision, iters, ptr(ms), ptr(work)))
+        return {c: (float(ms[i]), float(work[i])) for i, c in enumerate(self.PROFILE_CLASSES)}
 
     def decode(self, unpacked, precision=BF16, rgb=False):
         """unpacked [32, h, w] -> (decoded [3, 8h, 8w] FP32, rgb bytes [8h, 8w, 3] or None, nonfinite flag)."""

@@ -220,6 +220,12 @@ int ernie_cuda_vae_synthesize(ernie_cuda_vae *vae, uint64_t seed, int bf16_weigh
 int ernie_cuda_vae_bytes(ernie_cuda_vae *vae, uint64_t *weights, uint64_t *workspace);
 /* Kernel launches of one decode of this shape (builds the shape's workspace and graph). */
 int ernie_cuda_vae_launches(ernie_cuda_vae *vae, int width, int height, int precision, int *launches);
+/* Eager run of the decode with CUDA events around every launch (measurement hook): per kernel class the
+   mean milliseconds over `iters` runs and the algorithmic work of one run, ms[6] and work[6] indexed
+   0 convolutions (FLOPs), 1 attention score/value GEMMs (FLOPs), 2 softmax (bytes), 3 GroupNorm (bytes),
+   4 upsample (bytes), 5 other bandwidth passes (bytes). */
+int ernie_cuda_vae_profile(ernie_cuda_vae *vae, int width, int height, int precision, int iters, double *ms,
+                           double *work);
 /* Host buffers, synchronous. */
 int ernie_cuda_vae_decode(ernie_cuda_vae *vae, const float *unpacked, int width, int height, int precision,
                           float *decoded, uint8_t *rgb, int *nonfinite);
