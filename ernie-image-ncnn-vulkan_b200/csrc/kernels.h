@@ -166,12 +166,6 @@ struct ConvArgs
     // groups of cpg channels (4, 8 or 16); one slot per epilogue warp (conv_stat_slots of them)
     double2 *stats = nullptr;
     int cpg = 0;
-    // conv_out (16 output columns, valid_out used): planar FP32 [valid_out][pixels], interleaved bytes
-    // [pixels][valid_out] of clamp(x / 2 + 0.5, 0, 1) * 255 rounded to nearest even, non-finite flag
-    float *planar = nullptr;
-    uint8_t *rgb = nullptr;
-    int valid_out = 0;
-    int *nonfinite = nullptr;
     int *error_flag = nullptr;
 };
 struct ConvLaunch
@@ -182,7 +176,7 @@ struct ConvLaunch
     int b_planes = 1;                 // weight planes multiplied in FP32-exact mode (1: exact-BF16 weights)
     long long b_row = 0;
     int cout_rows = 0;
-    int height = 0, width = 0, cin = 0, taps = 1, cout = 0; // cin a multiple of 64; cout 16 or a multiple of 128
+    int height = 0, width = 0, cin = 0, taps = 1, cout = 0; // cin a multiple of 64; cout 32 or a multiple of 128
 };
 // GroupNorm partial slots per group that launch_conv writes for this launch (8 per CTA of its grid).
 int conv_stat_slots(const ConvLaunch &launch, int num_sms);
@@ -192,9 +186,10 @@ int launch_conv(const ConvLaunch &launch, const ConvArgs &epilogue, int num_sms,
 // each of 32 groups.
 int launch_gn_finalize(const double2 *stats, int slots, long long count, int cpg, const float *gamma,
                        const float *beta, float eps, float *scale, float *shift, cudaStream_t stream);
-// x * scale + shift (+ Swish), FP32 NHWC [pixels][channels] -> BF16 operand [pixels][planes * channels].
+// x * scale + shift (+ Swish), FP32 NHWC [pixels][channels] -> BF16 operand [pixels][planes * channels];
+// raw (nullable) receives x itself in the same operand layout.
 int launch_gn_apply(const float *x, long long pixels, int channels, const float *scale, const float *shift, int silu,
-                    __nv_bfloat16 *out, int planes, cudaStream_t stream);
+                    __nv_bfloat16 *out, int planes, cudaStream_t stream, __nv_bfloat16 *raw = nullptr);
 // Nearest x2 of FP32 NHWC [h][w][channels] -> BF16 operand [2h][2w][planes * channels].
 int launch_upsample(const float *x, int h, int w, int channels, __nv_bfloat16 *out, int planes, cudaStream_t stream);
 // post_quant_conv (w [32][32], bias [32], FP32) of the unpacked latent [32][pixels] -> operand [pixels][planes * 64].
@@ -206,6 +201,13 @@ int launch_softmax_rows(const float *s, int rows, int lds, int n, float scale, _
 // [n][1536] FP32 q|k|v -> Q, K [n][planes * 512] and V^T [512][planes * ldv] BF16 planes.
 int launch_attention_split(const float *qkv, int n, __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt, int ldv,
                            int planes, cudaStream_t stream);
+// conv_out (3 outputs) from its tap-expanded 1x1 product p [pixels][32]: bias + 3x3 tap sum, written as the
+// planar image [3][h*w] and RGB bytes [h*w][3] (clamp(x/2 + 0.5, 0, 1) * 255, nearest even; rgb nullable),
+// non-finite flag.
+int launch_conv_out_gather(const float *p, int h, int w, const float *bias, float *planar, uint8_t *rgb, int *nonfinite,
+                           cudaStream_t stream);
+// OIHW [cout][cin][9] FP32 -> tap-expanded [9 * cout][cin] (row t * cout + c).
+int launch_expand_taps(const float *w, int cout, int cin, float *out, cudaStream_t stream);
 // OIHW FP32 [cout][cin][taps] -> conv weights [cout_rows][3 * taps * cin_pad] (three BF16 planes).
 int launch_conv_weight_prep(const float *w, int cout, int cin, int taps, int cout_rows, int cin_pad,
                             __nv_bfloat16 *out, int *inexact, cudaStream_t stream);

@@ -29,6 +29,7 @@
 #include "ptx.cuh"
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <type_traits>
 
 namespace ernie_b200
 {
@@ -48,17 +49,18 @@ enum : int
 // row-segment order) x BN channels. MSUB = 2 lets two M=128 MMAs share each B tile.
 template <int BN, bool PROMOTE, int MSUB> struct ConvCfg
 {
-    static_assert(BN == 16 || BN == 128 || BN == 256, "tile widths");
-    static_assert(MSUB == 1 || (MSUB == 2 && BN == 128), "two pixel sub-tiles with 128-channel tiles only");
-    static_assert(!PROMOTE || (BN <= 128 && MSUB == 1), "FP32 promotion keeps BN/2 running sums per thread");
-    static constexpr int kStages = (BN == 256 || MSUB == 2) ? 4 : BN == 128 ? 6 : 8;
+    static_assert(BN == 32 || BN == 128 || BN == 256, "tile widths");
+    static_assert(MSUB == 1 || (MSUB == 2 && BN <= 128), "two pixel sub-tiles with 32- or 128-channel tiles");
+    static_assert(MSUB == 2 || BN >= 128, "every epilogue warp takes a multiple of 32 columns");
+    static_assert(!PROMOTE || (BN == 128 && MSUB == 1) || BN == 32, "FP32 promotion: at most 64 running sums");
+    static constexpr int kStages = BN == 32 ? 5 : (BN == 256 || MSUB == 2) ? 4 : 6;
     static constexpr int kABytes = MSUB * CM * CK * 2;
     static constexpr int kBBytes = BN * CK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes; // a multiple of 1024 for every configuration
     static constexpr int kAccCols = MSUB * BN;           // one accumulator buffer
-    static constexpr int kTmemCols = 2 * kAccCols <= 32 ? 32 : 2 * kAccCols;
+    static constexpr int kTmemCols = 2 * kAccCols;
     // columns per epilogue warp: warps 2..5 and 6..9 take the two sub-tiles, or the two column halves
-    static constexpr int kWarpCols = MSUB == 2 ? BN : (BN >= 32 ? BN / 2 : BN);
+    static constexpr int kWarpCols = MSUB == 2 ? BN : BN / 2;
     static constexpr int kBarrierBytes = 256;
     // per epilogue warp: a [32][20] FP32 staging tile and 32 FP64 (sum, sum of squares) GroupNorm slots
     static constexpr int kStageFloats = 32 * 20;
@@ -91,108 +93,112 @@ __device__ __forceinline__ double warp_sum(double v)
     return v;
 }
 
-// conv_out's chunk: planar FP32 [valid_out][pixels] and the RGB bytes of src/pipeline.cpp:145-163, one
-// pixel per thread (the lanes' stores are consecutive pixels).
-__device__ __forceinline__ void planar_chunk(const float (&v)[16], int col, bool valid, long long pixel,
-                                             long long pixels, const ConvArgs &a)
+// Columns [col, col + 32) of the warp's 32 pixels (thread `lane` holds pixel row `lane` in v), as two 16-column
+// halves staged through shared memory and written row-major: lane covers columns + 4*(lane % 4) .. +3 of rows
+// 8*i + lane / 4, so 4 lanes store one 64-byte row segment. out = (acc + bias) + resid for the first `limit`
+// rows. The thread's GroupNorm partial sums of each half (one group per thread and half) are added to
+// s[0..1], q[0..1].
+template <typename T>
+__device__ __forceinline__ void rows_pair(const float (&v)[32], float *stage, int col, int limit, long long pixel_first,
+                                          int lane, const ConvArgs &a, T (&s)[2], T (&q)[2])
 {
-    if (!valid) return;
+    const int c4 = (lane & 3) * 4, oct = lane >> 2;
+    // the residual loads of both halves first: `out` may alias `resid` (in place), so a load placed after
+    // an earlier row's store could not be hoisted above it
+    float4 u[2][4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-        if (col + j < a.valid_out)
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
         {
-            const float x = v[j] + (a.bias ? __ldg(a.bias + col + j) : 0.f);
-            a.planar[static_cast<size_t>(col + j) * pixels + pixel] = x;
-            if (!isfinite(x))
+            const int r = 8 * i + oct;
+            u[h][i] = a.resid && r < limit
+                          ? *reinterpret_cast<const float4 *>(a.resid + (pixel_first + r) * a.ldo + col + 16 * h + c4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    const bool stats = a.stats != nullptr;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+    {
+        float4 *mine = reinterpret_cast<float4 *>(stage + lane * 20);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            mine[k] = make_float4(v[16 * h + 4 * k], v[16 * h + 4 * k + 1], v[16 * h + 4 * k + 2], v[16 * h + 4 * k + 3]);
+        __syncwarp();
+        const float4 b = a.bias ? __ldg(reinterpret_cast<const float4 *>(a.bias + col + 16 * h + c4))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            const int r = 8 * i + oct;
+            float4 t = *reinterpret_cast<const float4 *>(stage + r * 20 + c4);
+            // (conv + bias) + residual, the reference graph's Convolution then BinaryOp add
+            t.x = (t.x + b.x) + u[h][i].x;
+            t.y = (t.y + b.y) + u[h][i].y;
+            t.z = (t.z + b.z) + u[h][i].z;
+            t.w = (t.w + b.w) + u[h][i].w;
+            if (r < limit)
             {
-                if (a.nonfinite) atomicOr(a.nonfinite, 1);
-            }
-            else if (a.rgb)
-            {
-                const float n = fminf(fmaxf(__fadd_rn(__fmul_rn(x, 0.5f), 0.5f), 0.f), 1.f);
-                a.rgb[static_cast<size_t>(pixel) * a.valid_out + col + j] =
-                    static_cast<uint8_t>(rintf(__fmul_rn(n, 255.f)));
+                if (a.out) *reinterpret_cast<float4 *>(a.out + (pixel_first + r) * a.ldo + col + 16 * h + c4) = t;
+                if (stats)
+                {
+                    const T d0 = t.x, d1 = t.y, d2 = t.z, d3 = t.w;
+                    s[h] += (d0 + d1) + (d2 + d3);
+                    q[h] += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+                }
             }
         }
+        __syncwarp();
+    }
 }
 
-// One 16-column chunk of the warp's 32 pixels (thread `lane` holds pixel row `lane` in v), staged through
-// shared memory and written row-major: lane covers columns col + 4*(lane % 4) .. +3 of rows 8*i + lane / 4,
-// so 4 lanes store one 64-byte row segment. out = (acc + bias) + resid for the first `limit` rows; the
-// GroupNorm partial sums of the written values are added, per group, into the warp's FP64 slots `acc`.
-__device__ __forceinline__ void rows_chunk(const float (&v)[16], float *stage, double2 *acc, int col, int limit,
-                                           long long pixel_first, int lane, const ConvArgs &a)
+// The tile's per-thread GroupNorm partials (slot k: columns col0 + 16k .. +16 of the warp's range) summed over
+// the lanes of each group in FP64 and added into the warp's group slots `acc` (a fixed order: deterministic).
+template <typename T, int SLOTS>
+__device__ __forceinline__ void flush_stats(const T (&s)[SLOTS], const T (&q)[SLOTS], int col0, int cpg, int lane,
+                                            double2 *acc)
 {
-    float4 *mine = reinterpret_cast<float4 *>(stage + lane * 20);
+    double ds[SLOTS], dq[SLOTS];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) mine[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-    __syncwarp();
-    const int c4 = (lane & 3) * 4, oct = lane >> 2;
-    const float4 b = a.bias ? __ldg(reinterpret_cast<const float4 *>(a.bias + col + c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    // all residual loads first: `out` may alias `resid` (in place), so a load placed after an earlier
-    // row's store could not be hoisted above it
-    float4 u[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int k = 0; k < SLOTS; ++k)
     {
-        const int r = 8 * i + oct;
-        u[i] = a.resid && r < limit ? *reinterpret_cast<const float4 *>(a.resid + (pixel_first + r) * a.ldo + col + c4)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        ds[k] = static_cast<double>(s[k]);
+        dq[k] = static_cast<double>(q[k]);
     }
-    const bool stats = a.stats != nullptr;
-    double s = 0.0, q = 0.0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-    {
-        const int r = 8 * i + oct;
-        float4 t = *reinterpret_cast<const float4 *>(stage + r * 20 + c4);
-        // (conv + bias) + residual, the reference graph's Convolution then BinaryOp add
-        t.x = (t.x + b.x) + u[i].x;
-        t.y = (t.y + b.y) + u[i].y;
-        t.z = (t.z + b.z) + u[i].z;
-        t.w = (t.w + b.w) + u[i].w;
-        if (r < limit)
-        {
-            if (a.out) *reinterpret_cast<float4 *>(a.out + (pixel_first + r) * a.ldo + col + c4) = t;
-            if (stats)
-            {
-                const double d0 = t.x, d1 = t.y, d2 = t.z, d3 = t.w;
-                s += (d0 + d1) + (d2 + d3);
-                q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
-            }
-        }
-    }
-    __syncwarp();
-    if (!stats) return;
     // lanes of one group: the eight row octets, and cpg / 4 neighbouring column quads
 #pragma unroll
     for (int o = 4; o <= 16; o <<= 1)
+#pragma unroll
+        for (int k = 0; k < SLOTS; ++k)
+        {
+            ds[k] += __shfl_xor_sync(0xffffffffu, ds[k], o);
+            dq[k] += __shfl_xor_sync(0xffffffffu, dq[k], o);
+        }
+    if (cpg >= 8)
+#pragma unroll
+        for (int k = 0; k < SLOTS; ++k)
+        {
+            ds[k] += __shfl_xor_sync(0xffffffffu, ds[k], 1);
+            dq[k] += __shfl_xor_sync(0xffffffffu, dq[k], 1);
+        }
+    if (cpg >= 16)
+#pragma unroll
+        for (int k = 0; k < SLOTS; ++k)
+        {
+            ds[k] += __shfl_xor_sync(0xffffffffu, ds[k], 2);
+            dq[k] += __shfl_xor_sync(0xffffffffu, dq[k], 2);
+        }
+    if (lane < 4 && (lane & (cpg / 4 - 1)) == 0)
     {
-        s += __shfl_xor_sync(0xffffffffu, s, o);
-        q += __shfl_xor_sync(0xffffffffu, q, o);
+#pragma unroll
+        for (int k = 0; k < SLOTS; ++k)
+        {
+            const int g = (col0 + 16 * k + lane * 4) / cpg;
+            acc[g].x += ds[k];
+            acc[g].y += dq[k];
+        }
     }
-    if (a.cpg >= 8)
-    {
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        q += __shfl_xor_sync(0xffffffffu, q, 1);
-    }
-    if (a.cpg >= 16)
-    {
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        q += __shfl_xor_sync(0xffffffffu, q, 2);
-    }
-    if (lane < 4 && (lane & (a.cpg / 4 - 1)) == 0)
-    {
-        const int g = (col + c4) / a.cpg;
-        acc[g].x += s;
-        acc[g].y += q;
-    }
-}
-
-template <int N> __device__ __forceinline__ void tmem_load_n(uint32_t taddr, float (&v)[N])
-{
-    static_assert(N == 16, "16-column loads");
-    tmem_load_16(taddr, v);
+    __syncwarp();
 }
 
 template <int BN, bool PROMOTE, int MSUB>
@@ -361,14 +367,13 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     else
     {
-        constexpr int CH = 16, CW = C::kWarpCols;
+        constexpr int CW = C::kWarpCols, SLOTS = CW / 16;
+        using T = std::conditional_t<PROMOTE, double, float>; // per-tile partials: FP32 in BF16 mode
         const int e = warp - 2, quarter = warp & 3, half = e >> 2;
         // this warp's pixel sub-tile and column range of each tile
         const int sub = MSUB == 2 ? half : 0;
         const int col0 = MSUB == 2 ? 0 : half * CW;
-        const bool active = MSUB == 2 || BN >= 32 || half == 0; // conv_out's 16 columns: one warp group
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-        const long long pixels = static_cast<long long>(args.height) * args.width;
         float *stage = reinterpret_cast<float *>(base_ptr + C::kEpilogueOffset) + e * C::kStageFloats;
         double2 *group_acc =
             reinterpret_cast<double2 *>(base_ptr + C::kEpilogueOffset + kEpiWarps * C::kStageFloats * 4) + e * 32;
@@ -385,11 +390,17 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const int limit = y < args.height ? min(32, args.width - x_first) : 0;
             const long long pixel_first = static_cast<long long>(y) * args.width + x_first;
             const uint32_t acc_cols = static_cast<uint32_t>(sub * BN + col0);
-            auto emit = [&](const float(&v)[CH], int c) {
-                if constexpr (BN >= 32)
-                    rows_chunk(v, stage, group_acc, n_blk * BN + col0 + c, limit, pixel_first, lane, args);
-                else
-                    planar_chunk(v, n_blk * BN + col0 + c, lane < limit, pixel_first + lane, pixels, args);
+            const int col_base = n_blk * BN + col0;
+            T s[SLOTS], q[SLOTS];
+#pragma unroll
+            for (int k = 0; k < SLOTS; ++k) s[k] = q[k] = T(0);
+            auto emit = [&](const float(&v)[32], int c) {
+                T ps[2] = {T(0), T(0)}, pq[2] = {T(0), T(0)};
+                rows_pair<T>(v, stage, col_base + c, limit, pixel_first, lane, args, ps, pq);
+                s[c / 16] += ps[0];
+                q[c / 16] += pq[0];
+                s[c / 16 + 1] += ps[1];
+                q[c / 16 + 1] += pq[1];
             };
             if constexpr (!PROMOTE)
             {
@@ -401,15 +412,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                if (active)
+#pragma unroll
+                for (int c = 0; c < CW; c += 32)
                 {
-#pragma unroll 1
-                    for (int c = 0; c < CW; c += CH)
-                    {
-                        float v[CH];
-                        tmem_load_n(lane_base + acc * C::kAccCols + acc_cols + c, v);
-                        emit(v, c);
-                    }
+                    float v[32];
+                    tmem_load_32(lane_base + acc * C::kAccCols + acc_cols + c, v);
+                    emit(v, c);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -432,34 +440,29 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    if (active)
+#pragma unroll
+                    for (int c = 0; c < CW; c += 32)
                     {
+                        float v[32];
+                        tmem_load_32(lane_base + acc * C::kAccCols + acc_cols + c, v);
 #pragma unroll
-                        for (int c = 0; c < CW; c += CH)
-                        {
-                            float v[CH];
-                            tmem_load_n(lane_base + acc * C::kAccCols + acc_cols + c, v);
-#pragma unroll
-                            for (int j = 0; j < CH; ++j) sum[c + j] += v[j];
-                        }
+                        for (int j = 0; j < 32; ++j) sum[c + j] += v[j];
                     }
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(tempty_bar(acc));
                 }
                 if (!ok) break;
-                if (active)
+#pragma unroll
+                for (int c = 0; c < CW; c += 32)
                 {
+                    float v[32];
 #pragma unroll
-                    for (int c = 0; c < CW; c += CH)
-                    {
-                        float v[CH];
-#pragma unroll
-                        for (int j = 0; j < CH; ++j) v[j] = sum[c + j];
-                        emit(v, c);
-                    }
+                    for (int j = 0; j < 32; ++j) v[j] = sum[c + j];
+                    emit(v, c);
                 }
             }
+            if (args.stats) flush_stats<T, SLOTS>(s, q, col_base, args.cpg, lane, group_acc);
         }
         // this warp's GroupNorm partials: every slot written (zero for groups it saw no tile of), in the
         // fixed tile order of this CTA, so the sums are deterministic for a given grid
@@ -515,12 +518,16 @@ bool make_weight_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t 
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Tile shape of a launch: (BN, MSUB). conv_out: 16 columns; FP32-exact mode: 128; BF16 mode: 256 columns,
+// Tile shape of a launch: (BN, MSUB). 32 output columns: 32; FP32-exact mode: 128; BF16 mode: 256 columns,
 // or 2 x 128 pixels x 128 columns where the width is not a multiple of 256.
 void conv_shape(const ConvLaunch &l, int &bn, int &msub)
 {
     msub = 1;
-    if (l.cout == 16) bn = 16;
+    if (l.cout == 32)
+    {
+        bn = 32;
+        msub = 2;
+    }
     else if (l.a_planes == 3) bn = 128;
     else if (l.cout % 256 == 0) bn = 256;
     else
@@ -635,39 +642,46 @@ __global__ void gn_finalize_kernel(const double2 *stats, int slots, long long co
 }
 
 // y = x * scale[c] + shift[c] (then Swish x / (1 + exp(-x)) when silu), FP32 NHWC -> BF16 operand planes.
-// channels = 2^log2c (the decoder's widths 128, 256, 512); 8 channels per thread. BF16 mode evaluates the
-// Swish with the fast exponential and reciprocal (far below the BF16 rounding that follows); FP32-exact
-// mode with expf and an IEEE division.
+// channels = 2^log2c (the decoder's widths 128, 256, 512); 8 channels per thread and step. BF16 mode
+// evaluates the Swish with the fast exponential and division (far below the BF16 rounding that follows);
+// FP32-exact mode with expf and an IEEE division. `raw` (nullable) also receives x
+// itself as operand planes (the resnet's shortcut-convolution operand, from the same read of x).
+__device__ __forceinline__ void gn_apply8(const float4 a, const float4 b, long long e, int c0, int channels,
+                                          const float *scale, const float *shift, int silu, __nv_bfloat16 *out,
+                                          __nv_bfloat16 *raw, int planes)
+{
+    const float4 sa = __ldg(reinterpret_cast<const float4 *>(scale + c0)),
+                 sb = __ldg(reinterpret_cast<const float4 *>(scale + c0 + 4));
+    const float4 ha = __ldg(reinterpret_cast<const float4 *>(shift + c0)),
+                 hb = __ldg(reinterpret_cast<const float4 *>(shift + c0 + 4));
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const long long off = planes == 1 ? e : 3 * e - 2 * c0; // pixel p's plane q at p * planes * channels + q * channels
+    if (raw) store_planes8(raw + off, channels, planes, v);
+    const float sc[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const float sh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+    {
+        float y = __fadd_rn(__fmul_rn(v[j], sc[j]), sh[j]);
+        if (silu)
+            y = planes == 1 ? __fdividef(y, __fadd_rn(1.f, __expf(-y))) : __fdiv_rn(y, __fadd_rn(1.f, expf(-y)));
+        v[j] = y;
+    }
+    store_planes8(out + off, channels, planes, v);
+}
+
 __global__ void gn_apply_kernel(const float *x, long long pixels, int log2c, const float *scale, const float *shift,
-                                int silu, __nv_bfloat16 *out, int planes)
+                                int silu, __nv_bfloat16 *out, __nv_bfloat16 *raw, int planes)
 {
     const int channels = 1 << log2c;
     const long long total = pixels << (log2c - 3);
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x)
     {
-        const long long e = i * 8; // element index p * channels + c0
-        const int c0 = static_cast<int>(e & (channels - 1));
+        const long long e = i * 8;
         const float4 *src = reinterpret_cast<const float4 *>(x + e);
-        const float4 a = src[0], b = src[1];
-        const float4 sa = __ldg(reinterpret_cast<const float4 *>(scale + c0)),
-                     sb = __ldg(reinterpret_cast<const float4 *>(scale + c0 + 4));
-        const float4 ha = __ldg(reinterpret_cast<const float4 *>(shift + c0)),
-                     hb = __ldg(reinterpret_cast<const float4 *>(shift + c0 + 4));
-        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const float sc[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-        const float sh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-        {
-            float y = __fadd_rn(__fmul_rn(v[j], sc[j]), sh[j]);
-            if (silu)
-                y = planes == 1 ? __fmul_rn(y, __frcp_rn(__fadd_rn(1.f, __expf(-y))))
-                                : __fdiv_rn(y, __fadd_rn(1.f, expf(-y)));
-            v[j] = y;
-        }
-        // planes side by side per pixel: pixel p's plane q starts at p * planes * channels + q * channels
-        store_planes8(out + (planes == 1 ? e : 3 * e - 2 * c0), channels, planes, v);
+        gn_apply8(src[0], src[1], e, static_cast<int>(e & (channels - 1)), channels, scale, shift, silu, out, raw,
+                  planes);
     }
 }
 
@@ -934,6 +948,59 @@ __global__ void conv_weight_prep_kernel(const float *w, int cout, int cin, int t
     }
 }
 
+// conv_out from its tap-expanded 1x1 product p [pixels][32] (column t * 3 + c = tap t of output channel c):
+// out[c][y][x] = bias[c] + sum over the 3x3 taps inside the image of p[(y + dy, x + dx)][t * 3 + c], written as
+// the planar FP32 image [3][pixels] and the RGB bytes of rgb_image (src/pipeline.cpp:145-163).
+__global__ void conv_out_gather_kernel(const float *p, int h, int w, const float *bias, float *planar, uint8_t *rgb,
+                                       int *nonfinite)
+{
+    const long long pixels = static_cast<long long>(h) * w;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < pixels;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const int y = static_cast<int>(i / w), x = static_cast<int>(i - static_cast<long long>(y) * w);
+        float acc[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+        {
+            const int yy = y + t / 3 - 1, xx = x + t % 3 - 1;
+            if (yy < 0 || yy >= h || xx < 0 || xx >= w) continue;
+            const float *src = p + (static_cast<long long>(yy) * w + xx) * 32 + t * 3;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) acc[c] += src[c];
+        }
+        bool finite = true;
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+        {
+            const float v = bias[c] + acc[c];
+            planar[c * pixels + i] = v;
+            if (!isfinite(v))
+            {
+                finite = false;
+                continue;
+            }
+            if (rgb)
+            {
+                const float n = fminf(fmaxf(__fadd_rn(__fmul_rn(v, 0.5f), 0.5f), 0.f), 1.f);
+                rgb[i * 3 + c] = static_cast<uint8_t>(rintf(__fmul_rn(n, 255.f)));
+            }
+        }
+        if (!finite && nonfinite) atomicOr(nonfinite, 1);
+    }
+}
+
+// OIHW [cout][cin][9] -> tap-expanded 1x1 weights [9 * cout][cin] (row t * cout + c = tap t of output c).
+__global__ void expand_taps_kernel(const float *w, int cout, int cin, float *out)
+{
+    const int total = 9 * cout * cin;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x)
+    {
+        const int row = i / cin, ch = i - row * cin, t = row / cout, c = row - t * cout;
+        out[i] = w[(c * cin + ch) * 9 + t];
+    }
+}
+
 // float(N(0,1) * scale) + offset for (seed, stream, i) (include/ernie_synth.h), optionally rounded to BF16.
 __global__ void synth_f32_kernel(uint64_t seed, uint64_t stream_id, float scale, float offset, long long count,
                                  int round_bf16, float *out)
@@ -953,9 +1020,9 @@ int prepare_conv_kernels()
 {
     cudaError_t e = ensure_conv_attributes<256, false, 1>();
     if (e == cudaSuccess) e = ensure_conv_attributes<128, false, 2>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<16, false, 1>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<32, false, 2>();
     if (e == cudaSuccess) e = ensure_conv_attributes<128, true, 1>();
-    if (e == cudaSuccess) e = ensure_conv_attributes<16, true, 1>();
+    if (e == cudaSuccess) e = ensure_conv_attributes<32, true, 2>();
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(softmax_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSoftmaxMaxRow * 4);
     return e;
@@ -987,10 +1054,9 @@ int launch_conv(const ConvLaunch &l, const ConvArgs &epi, int num_sms, cudaStrea
     args.products = promote ? (l.b_planes == 3 ? 6 : 3) : 1;
     args.group = conv_group(l.taps * l.cin / CK);
     if (args.stats && args.cpg != 4 && args.cpg != 8 && args.cpg != 16) return cudaErrorInvalidValue;
-    if ((args.planar != nullptr) != (l.cout == 16)) return cudaErrorInvalidValue; // 16 columns: conv_out only
     if ((args.out || args.resid) && (args.ldo < l.cout || args.ldo % 4)) return cudaErrorInvalidValue;
-    if (l.cout == 16) return promote ? launch_conv_impl<16, true, 1>(l, args, num_sms, stream)
-                                     : launch_conv_impl<16, false, 1>(l, args, num_sms, stream);
+    if (l.cout == 32) return promote ? launch_conv_impl<32, true, 2>(l, args, num_sms, stream)
+                                     : launch_conv_impl<32, false, 2>(l, args, num_sms, stream);
     if (l.cout % 128) return cudaErrorInvalidValue;
     if (promote) return launch_conv_impl<128, true, 1>(l, args, num_sms, stream);
     if (l.cout % 256 == 0) return launch_conv_impl<256, false, 1>(l, args, num_sms, stream);
@@ -1006,14 +1072,14 @@ int launch_gn_finalize(const double2 *stats, int slots, long long count, int cpg
 }
 
 int launch_gn_apply(const float *x, long long pixels, int channels, const float *scale, const float *shift, int silu,
-                    __nv_bfloat16 *out, int planes, cudaStream_t stream)
+                    __nv_bfloat16 *out, int planes, cudaStream_t stream, __nv_bfloat16 *raw)
 {
     if (channels < 8 || (channels & (channels - 1)) || pixels < 1 || (planes != 1 && planes != 3))
         return cudaErrorInvalidValue;
     int log2c = 0;
     while ((1 << log2c) < channels) ++log2c;
     gn_apply_kernel<<<grid_for_count(pixels * channels / 8, 256), 256, 0, stream>>>(x, pixels, log2c, scale, shift,
-                                                                                    silu, out, planes);
+                                                                                    silu, out, raw, planes);
     return cudaGetLastError();
 }
 
@@ -1065,6 +1131,22 @@ int launch_conv_weight_prep(const float *w, int cout, int cin, int taps, int cou
         return cudaErrorInvalidValue;
     conv_weight_prep_kernel<<<grid_for_count(static_cast<long long>(cout_rows) * taps * cin_pad, 256), 256, 0,
                               stream>>>(w, cout, cin, taps, cout_rows, cin_pad, out, inexact);
+    return cudaGetLastError();
+}
+
+int launch_conv_out_gather(const float *p, int h, int w, const float *bias, float *planar, uint8_t *rgb, int *nonfinite,
+                           cudaStream_t stream)
+{
+    if (h < 1 || w < 1) return cudaErrorInvalidValue;
+    conv_out_gather_kernel<<<grid_for_count(static_cast<long long>(h) * w, 256), 256, 0, stream>>>(p, h, w, bias, planar,
+                                                                                                   rgb, nonfinite);
+    return cudaGetLastError();
+}
+
+int launch_expand_taps(const float *w, int cout, int cin, float *out, cudaStream_t stream)
+{
+    if (cout < 1 || cin < 1) return cudaErrorInvalidValue;
+    expand_taps_kernel<<<grid_for_count(9LL * cout * cin, 256), 256, 0, stream>>>(w, cout, cin, out);
     return cudaGetLastError();
 }
 

@@ -30,9 +30,13 @@ constexpr int kGroups = 32, kMaxLatentSide = 256;
 struct ConvW
 {
     int cin = 0, cout = 0, taps = 1, cin_pad = 0, cout_rows = 0;
-    __nv_bfloat16 *w = nullptr; // [cout_rows][3 * taps * cin_pad]: hi, mid, lo planes
+    // conv_out: stored as the 1x1 convolution to its 9 taps x 3 outputs (rows t * 3 + c, padded to 32),
+    // whose product a gather kernel sums over the 3x3 neighbourhood
+    bool tap_expanded = false;
+    __nv_bfloat16 *w = nullptr; // [cout_rows][3 * dev_taps() * cin_pad]: hi, mid, lo planes
     float *bias = nullptr;      // [cout_rows]
     int inexact = 0;            // some weight is not a BF16 value (FP32-exact mode multiplies 3 planes)
+    int dev_taps() const { return tap_expanded ? 1 : taps; }
 };
 struct NormW
 {
@@ -184,6 +188,8 @@ struct Layout
         }
         norm("decoder.conv_norm_out", norm_out, 128);
         conv("decoder.conv_out", conv_out, 128, 3, 9);
+        conv_out.tap_expanded = true;
+        conv_out.cout_rows = 32;
     }
 };
 
@@ -194,7 +200,7 @@ struct Plan
     int n = 0, npad = 0; // attention tokens (h0 * w0) and their padding to 256
     float *input = nullptr, *x = nullptr, *h1 = nullptr, *sc = nullptr, *qkv = nullptr, *s = nullptr, *o = nullptr;
     float *scale = nullptr, *shift = nullptr, *decoded = nullptr;
-    __nv_bfloat16 *a = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *p = nullptr;
+    __nv_bfloat16 *a = nullptr, *a2 = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *p = nullptr;
     double2 *stats_x = nullptr, *stats_h = nullptr;
     uint8_t *rgb = nullptr;
     int *nonfinite = nullptr;
@@ -212,7 +218,7 @@ struct ernie_cuda_vae
     ernie_cuda_context *ctx = nullptr;
     Layout layout;
     void *alloc = nullptr;
-    float *staging = nullptr;
+    float *staging = nullptr, *staging2 = nullptr;
     int *d_inexact = nullptr;
     uint64_t bytes = 0;
     std::unique_ptr<Plan> plan;
@@ -245,6 +251,7 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
     arena.add(&p.h1, 8192 * px0);
     arena.add(&p.sc, 8192 * px0);
     arena.add(&p.a, static_cast<size_t>(p.planes) * 16384 * px0);
+    arena.add(&p.a2, static_cast<size_t>(p.planes) * 16384 * px0); // shortcut-convolution operand
     arena.add(&p.qkv, static_cast<size_t>(p.n) * 1536);
     arena.add(&p.q, static_cast<size_t>(p.planes) * 512 * p.npad);
     arena.add(&p.k, static_cast<size_t>(p.planes) * 512 * p.npad);
@@ -356,30 +363,33 @@ struct Program
         l.a_planes = p.planes;
         l.b = c.w;
         l.b_planes = fp32() && c.inexact ? 3 : 1;
-        l.b_row = 3LL * c.taps * c.cin_pad;
+        l.b_row = 3LL * c.dev_taps() * c.cin_pad;
         l.cout_rows = c.cout_rows;
         l.height = h;
         l.width = w;
         l.cin = c.cin_pad;
-        l.taps = c.taps;
+        l.taps = c.dev_taps();
         l.cout = c.cout_rows;
         ConvArgs args = epi;
-        args.bias = c.bias;
+        args.bias = c.tap_expanded ? nullptr : c.bias; // conv_out's bias is added by the gather
         args.error_flag = v->ctx->error_flag;
         const double flops = 2.0 * pixels_of(h, w) * c.cout * c.cin * c.taps;
         if (args.stats) (args.stats == p.stats_x ? slots_x : slots_h) = conv_stat_slots(l, sms);
         return op(kProfConv, flops, 1, "VAE convolution", [&] { return launch_conv(l, args, sms, stream); });
     }
     // GroupNorm(32) of x (statistics from its producer) + optional Swish -> operand `a`
-    int group_norm(const NormW &n, const float *x, const double2 *stats, int h, int w, bool silu)
+    // (raw: also x itself as operand planes, from the same read)
+    int group_norm(const NormW &n, const float *x, const double2 *stats, int h, int w, bool silu,
+                   __nv_bfloat16 *raw = nullptr)
     {
         const int cpg = n.c / kGroups;
         const long long pixels = static_cast<long long>(pixels_of(h, w));
         const double elements = static_cast<double>(pixels) * n.c;
-        return op(kProfNorm, 4.0 * elements + bytes_bf16(elements), 2, "GroupNorm", [&] {
-            const int e = launch_gn_finalize(stats, stats == p.stats_x ? slots_x : slots_h, pixels * cpg, cpg, n.gamma, n.beta,
-                                             kGroupNormEps, p.scale, p.shift, stream);
-            return e != 0 ? e : launch_gn_apply(x, pixels, n.c, p.scale, p.shift, silu ? 1 : 0, p.a, p.planes, stream);
+        return op(kProfNorm, 4.0 * elements + bytes_bf16(elements) * (raw ? 2 : 1), 2, "GroupNorm", [&] {
+            const int e = launch_gn_finalize(stats, stats == p.stats_x ? slots_x : slots_h, pixels * cpg, cpg, n.gamma,
+                                             n.beta, kGroupNormEps, p.scale, p.shift, stream);
+            return e != 0 ? e
+                          : launch_gn_apply(x, pixels, n.c, p.scale, p.shift, silu ? 1 : 0, p.a, p.planes, stream, raw);
         });
     }
     ConvArgs writes_x(int cout, const float *resid)
@@ -402,16 +412,15 @@ struct Program
     int resnet(const ResnetW &r, int h, int w)
     {
         const float *resid = p.x;
+        ERNIE_TRY(group_norm(r.norm1, p.x, p.stats_x, h, w, true, r.has_shortcut ? p.a2 : nullptr));
         if (r.has_shortcut)
         {
-            ERNIE_TRY(to_operand(p.x, static_cast<long long>(pixels_of(h, w)), r.cin));
             ConvArgs e;
             e.out = p.sc;
             e.ldo = r.cout;
-            ERNIE_TRY(conv(r.shortcut, p.a, h, w, e));
+            ERNIE_TRY(conv(r.shortcut, p.a2, h, w, e));
             resid = p.sc;
         }
-        ERNIE_TRY(group_norm(r.norm1, p.x, p.stats_x, h, w, true));
         ConvArgs e1;
         e1.out = p.h1;
         e1.ldo = r.cout;
@@ -498,12 +507,15 @@ struct Program
             ERNIE_TRY(conv(L.upsample[i], p.a, h, w, writes_x(c, nullptr)));
         }
         ERNIE_TRY(group_norm(L.norm_out, p.x, p.stats_x, h, w, true));
+        // conv_out: the 1x1 product to 9 taps x 3 outputs (into h1, free here), then the 3x3 tap sum
         ConvArgs e;
-        e.planar = p.decoded;
-        e.rgb = p.rgb;
-        e.valid_out = 3;
-        e.nonfinite = p.nonfinite;
-        return conv(L.conv_out, p.a, h, w, e);
+        e.out = p.h1;
+        e.ldo = 32;
+        ERNIE_TRY(conv(L.conv_out, p.a, h, w, e));
+        const double px_top = static_cast<double>(pixels_of(h, w));
+        return op(kProfOther, px_top * (32 * 4 + 3 * 4 + 3), 1, "conv_out gather", [&] {
+            return launch_conv_out_gather(p.h1, h, w, L.conv_out.bias, p.decoded, p.rgb, p.nonfinite, stream);
+        });
     }
 };
 
@@ -540,10 +552,18 @@ int place(ernie_cuda_vae *v, Param &prm)
         const int cout = prm.shape[0];
         const int rows = prm.row_offset == 0 && cout == c.cout ? c.cout_rows : cout;
         ERNIE_CUDA(cudaMemsetAsync(v->d_inexact, 0, sizeof(int), stream), "clear flag");
-        ERNIE_LAUNCH(launch_conv_weight_prep(v->staging, cout, c.cin, c.taps, rows, c.cin_pad,
-                                             c.w + static_cast<size_t>(prm.row_offset) * 3 * c.taps * c.cin_pad,
-                                             v->d_inexact, stream),
-                     "prepare weights");
+        if (c.tap_expanded)
+        {
+            ERNIE_LAUNCH(launch_expand_taps(v->staging, c.cout, c.cin, v->staging2, stream), "expand taps");
+            ERNIE_LAUNCH(launch_conv_weight_prep(v->staging2, 9 * c.cout, c.cin, 1, c.cout_rows, c.cin_pad, c.w,
+                                                 v->d_inexact, stream),
+                         "prepare weights");
+        }
+        else
+            ERNIE_LAUNCH(launch_conv_weight_prep(v->staging, cout, c.cin, c.taps, rows, c.cin_pad,
+                                                 c.w + static_cast<size_t>(prm.row_offset) * 3 * c.taps * c.cin_pad,
+                                                 v->d_inexact, stream),
+                         "prepare weights");
         int inexact = 0;
         ERNIE_CUDA(cudaMemcpyAsync(&inexact, v->d_inexact, sizeof(int), cudaMemcpyDeviceToHost, stream), "read flag");
         ERNIE_CUDA(cudaStreamSynchronize(stream), "prepare weights");
@@ -640,12 +660,13 @@ extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **o
     size_t staging = 0;
     for (auto &prm : L.params) staging = std::max(staging, prm.count());
     arena.add(&v->staging, staging);
+    arena.add(&v->staging2, staging); // tap-expanded copy of conv_out's weights
     arena.add(&v->d_inexact, 1);
     arena.add(&L.pq_w, 32 * 32);
     arena.add(&L.pq_b, 32);
     for (ConvW *c : L.convs)
     {
-        arena.add(&c->w, static_cast<size_t>(c->cout_rows) * 3 * c->taps * c->cin_pad);
+        arena.add(&c->w, static_cast<size_t>(c->cout_rows) * 3 * c->dev_taps() * c->cin_pad);
         arena.add(&c->bias, static_cast<size_t>(c->cout_rows));
     }
     for (NormW *n : L.norms)
