@@ -953,4 +953,135 @@ DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucke
     }
     return result;
 }
+
+// ---- the VAE stage --------------------------------------------------------------------------------
+RgbImage rgb_image(const Tensor &decoded)
+{
+    if (decoded.empty() || decoded.dims != 3 || decoded.c != 3)
+        throw std::runtime_error("VAE output must be pack1 RGB FP32");
+    RgbImage image{decoded.w, decoded.h, std::vector<uint8_t>(size_t(decoded.w) * decoded.h * 3)};
+    const size_t plane = size_t(decoded.w) * decoded.h;
+    for (int c = 0; c < 3; ++c)
+        for (size_t i = 0; i < plane; ++i)
+        {
+            const float x = decoded[size_t(c) * plane + i];
+            if (!std::isfinite(x)) throw std::runtime_error("VAE produced non-finite pixels");
+            const float normalized = std::clamp(x / 2.f + .5f, 0.f, 1.f);
+            image.pixels[i * 3 + size_t(c)] = static_cast<uint8_t>(std::nearbyint(normalized * 255.f));
+        }
+    return image;
+}
+
+VaeDecoder::VaeDecoder(GpuContext &ctx) : ctx_(ctx)
+{
+    require(ctx.available(), "VAE decoder needs a CUDA device");
+    check_cuda(ernie_cuda_vae_create(ctx.handle(), &handle_), "create VAE decoder");
+}
+
+VaeDecoder::~VaeDecoder()
+{
+    if (handle_) ernie_cuda_vae_destroy(handle_);
+}
+
+std::vector<std::pair<std::string, std::vector<int>>> VaeDecoder::tensors()
+{
+    int count = 0;
+    check_cuda(ernie_cuda_vae_tensor_count(&count), "VAE tensor count");
+    std::vector<std::pair<std::string, std::vector<int>>> out;
+    for (int i = 0; i < count; ++i)
+    {
+        char name[128];
+        int dims[4] = {0, 0, 0, 0}, ndim = 0;
+        check_cuda(ernie_cuda_vae_tensor_info(i, name, sizeof(name), dims, &ndim), "VAE tensor info");
+        out.emplace_back(name, std::vector<int>(dims, dims + ndim));
+    }
+    return out;
+}
+
+void VaeDecoder::upload(const std::string &name, const Tensor &value)
+{
+    const int rc = ernie_cuda_vae_upload(handle_, name.c_str(), value.ptr(), value.total());
+    if (rc == ERNIE_CUDA_ERROR) throw std::invalid_argument(ernie_cuda_last_error());
+    check_cuda(rc, "upload VAE tensor");
+}
+
+void VaeDecoder::synthesize(uint64_t seed, bool bf16_weights)
+{
+    check_cuda(ernie_cuda_vae_synthesize(handle_, seed, bf16_weights ? 1 : 0), "synthesize VAE weights");
+}
+
+namespace
+{
+int precision_code(Precision p) { return p == Precision::FP32 ? ERNIE_PRECISION_FP32 : ERNIE_PRECISION_BF16; }
+
+void check_unpacked(int c, int w, int h, int dims)
+{
+    require(dims == 3 && c == 32 && w >= 1 && h >= 1 && w <= 256 && h <= 256 && w * h <= 57344,
+            "Expected pack1 FP32 [32,H,W] unpacked latent with 1 <= H,W <= 256 and H*W <= 57344");
+}
+} // namespace
+
+Tensor VaeDecoder::decode(const Tensor &unpacked, Precision precision, VaeStats *stats)
+{
+    check_unpacked(unpacked.c, unpacked.w, unpacked.h, unpacked.dims);
+    if (stats) stats->details.clear();
+    const auto begin = Clock::now();
+    Tensor decoded(8 * unpacked.w, 8 * unpacked.h, 3);
+    const int rc = ernie_cuda_vae_decode(handle_, unpacked.ptr(), unpacked.w, unpacked.h, precision_code(precision),
+                                         decoded.ptr(), nullptr, nullptr);
+    if (stats)
+        stats->details.push_back({"extract_compute_composite", rc == ERNIE_CUDA_OK ? "complete" : "failed",
+                                  seconds_since(begin)});
+    check_cuda(rc, "Decode VAE");
+    return decoded;
+}
+
+DeviceTensor VaeDecoder::decode(const DeviceTensor &unpacked, Precision precision, RgbImage *image)
+{
+    check_unpacked(unpacked.c, unpacked.w, unpacked.h, unpacked.dims);
+    const int w = 8 * unpacked.w, h = 8 * unpacked.h;
+    DeviceTensor decoded(ctx_, size_t(3) * w * h * 4, w, h, 3, 3);
+    DeviceTensor bytes;
+    if (image) bytes = DeviceTensor(ctx_, size_t(3) * w * h, w, h, 3, 3);
+    int nonfinite = 0;
+    check_cuda(ernie_cuda_vae_decode_device(handle_, unpacked.f32(), unpacked.w, unpacked.h, precision_code(precision),
+                                            decoded.f32(), image ? static_cast<uint8_t *>(bytes.data()) : nullptr,
+                                            &nonfinite),
+               "Decode VAE");
+    if (image)
+    {
+        if (nonfinite) throw std::runtime_error("VAE produced non-finite pixels");
+        image->width = w;
+        image->height = h;
+        image->pixels.resize(size_t(3) * w * h);
+        check_cuda(ernie_cuda_download(ctx_.handle(), image->pixels.data(), bytes.data(), image->pixels.size()),
+                   "download RGB bytes");
+    }
+    return decoded;
+}
+
+VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor &mean, const Tensor &variance,
+                             Precision precision, const std::string &trace)
+{
+    check_latent(latent);
+    GpuContext &ctx = vae.context();
+    const auto begin = Clock::now();
+    VaeStageResult result;
+    const DeviceTensor packed = DeviceTensor::upload(ctx, latent);
+    const DeviceTensor unpacked = unpack_for_vae(ctx, packed, mean, variance);
+    const DeviceTensor decoded = vae.decode(unpacked, precision, &result.image);
+    if (decoded.w != latent.w * 16 || decoded.h != latent.h * 16)
+        throw std::runtime_error("Decoded resolution differs from model");
+    result.decoded = decoded.download();
+    result.unpacked = unpacked.download();
+    if (!trace.empty())
+    {
+        const std::filesystem::path folder(trace);
+        write_tensor((folder / "final.f32").string(), latent);
+        write_tensor((folder / "unpacked.f32").string(), result.unpacked);
+        write_tensor((folder / "decoded.f32").string(), result.decoded);
+    }
+    result.seconds = seconds_since(begin);
+    return result;
+}
 } // namespace ernie

@@ -427,4 +427,59 @@ struct DitStageResult
 DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucket, const std::vector<float> &frequencies,
                              const DitStageRequest &request,
                              const std::function<void(const DitStageProgress &)> &notify = {});
+
+// ---- the pipeline's VAE stage (src/vae.h:8-22, src/pipeline.cpp:145-163 and :554-575) -------------
+struct RgbImage // interleaved RGB bytes, row after row (include/ernie/pipeline.h)
+{
+    int width = 0, height = 0;
+    std::vector<uint8_t> pixels;
+};
+// rgb_image (src/pipeline.cpp:145-163): decoded [3][H][W] FP32 -> bytes nearbyint(clamp(x / 2 + 0.5, 0, 1) *
+// 255) in FP32; std::runtime_error for a tensor that is not [3][H][W] or holds a non-finite value.
+RgbImage rgb_image(const Tensor &decoded);
+struct VaeStats // src/vae.h:9-13
+{
+    struct Detail
+    {
+        std::string boundary, status;
+        double seconds = 0;
+    };
+    std::vector<Detail> details;
+};
+// decode_vae on the B200: the AutoencoderKLFlux2 post_quant_conv + decoder the reference exports
+// (tools/export_vae.py), weights resident on the device and addressed by their diffusers names (FP32).
+class VaeDecoder
+{
+  public:
+    explicit VaeDecoder(GpuContext &ctx);
+    ~VaeDecoder();
+    VaeDecoder(const VaeDecoder &) = delete;
+    VaeDecoder &operator=(const VaeDecoder &) = delete;
+    // every tensor the decoder holds: diffusers name and shape, in execution order
+    static std::vector<std::pair<std::string, std::vector<int>>> tensors();
+    void upload(const std::string &name, const Tensor &value);
+    void synthesize(uint64_t seed, bool bf16_weights = false); // include/ernie_synth.h, VAE section
+    // unpacked [32][h][w] -> decoded [3][8h][8w]; stats gets the "extract_compute_composite" boundary
+    Tensor decode(const Tensor &unpacked, Precision precision = Precision::BF16, VaeStats *stats = nullptr);
+    // device tensors; `image` (nullable) receives the RGB bytes, and then a non-finite value throws as
+    // rgb_image does
+    DeviceTensor decode(const DeviceTensor &unpacked, Precision precision, RgbImage *image = nullptr);
+    GpuContext &context() const { return ctx_; }
+
+  private:
+    GpuContext &ctx_;
+    ernie_cuda_vae *handle_ = nullptr;
+};
+struct VaeStageResult
+{
+    Tensor unpacked; // [32][2h][2w]
+    Tensor decoded;  // [3][16h][16w]
+    RgbImage image;
+    double seconds = 0;
+};
+// The stage after the denoise loop (src/pipeline.cpp:554-575): unpack_for_vae with the package's BN
+// statistics, decode_vae and rgb_image. With a trace folder it writes final.f32, unpacked.f32 and
+// decoded.f32 (refusing to overwrite, as write_tensor does).
+VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor &mean, const Tensor &variance,
+                             Precision precision = Precision::BF16, const std::string &trace = {});
 } // namespace ernie

@@ -161,6 +161,65 @@ int main()
         std::cerr << "exception: " << e.what() << "\n";
         return 1;
     }
+    // the VAE stage: host and device decode agree, device RGB bytes equal rgb_image of the decoded tensor,
+    // run_vae_stage equals unpack_for_vae + decode by hand and writes the reference's trace files
+    try
+    {
+        GpuContext ctx(true, 0);
+        VaeDecoder vae(ctx);
+        vae.synthesize(7);
+        const int w = 4, h = 3; // packed latent [128][3][4] -> image 64 x 48
+        const Tensor latent = normal(w, h, 128, ERNIE_SYNTH_LATENT);
+        Tensor mean(128), variance(128);
+        for (int c = 0; c < 128; ++c)
+        {
+            mean[size_t(c)] = 0.01f * float(c % 7);
+            variance[size_t(c)] = 0.5f + 0.01f * float(c % 5);
+        }
+        const DeviceTensor unpacked = unpack_for_vae(ctx, DeviceTensor::upload(ctx, latent), mean, variance);
+        const Tensor unpacked_host = unpacked.download();
+        VaeStats stats;
+        const Tensor decoded = vae.decode(unpacked_host, Precision::BF16, &stats);
+        REQUIRE(decoded.w == 64 && decoded.h == 48 && decoded.c == 3, "decoded shape");
+        REQUIRE(stats.details.size() == 1 && stats.details[0].status == "complete", "VAE stats");
+        RgbImage bytes;
+        const Tensor decoded_dev = vae.decode(unpacked, Precision::BF16, &bytes).download();
+        REQUIRE(decoded_dev.data == decoded.data, "host and device decode differ");
+        REQUIRE(bytes.pixels == rgb_image(decoded).pixels, "device RGB bytes differ from rgb_image");
+        char folder[] = "/tmp/ernie_vae_traceXXXXXX";
+        REQUIRE(mkdtemp(folder) != nullptr, "trace folder");
+        const VaeStageResult stage = run_vae_stage(vae, latent, mean, variance, Precision::BF16, folder);
+        REQUIRE(stage.decoded.data == decoded.data && stage.image.pixels == bytes.pixels, "VAE stage differs");
+        REQUIRE(stage.unpacked.data == unpacked_host.data, "VAE stage unpacked latent differs");
+        for (const char *f : {"final.f32", "unpacked.f32", "decoded.f32"})
+            REQUIRE(std::filesystem::file_size(std::filesystem::path(folder) / f) > 0, "missing trace " << f);
+        REQUIRE(read_tensor((std::filesystem::path(folder) / "decoded.f32").string(), 64, 48, 3).data == decoded.data,
+                "decoded trace");
+        bool threw = false;
+        try
+        {
+            run_vae_stage(vae, latent, mean, variance, Precision::BF16, folder); // traces exist
+        }
+        catch (const std::runtime_error &)
+        {
+            threw = true;
+        }
+        REQUIRE(threw, "existing trace overwritten");
+        std::filesystem::remove_all(folder);
+        const Tensor exact = vae.decode(unpacked_host, Precision::FP32);
+        double num = 0, den = 0;
+        for (size_t i = 0; i < exact.total(); ++i)
+        {
+            num += double(exact[i] - decoded[i]) * double(exact[i] - decoded[i]);
+            den += double(exact[i]) * double(exact[i]);
+        }
+        REQUIRE(std::sqrt(num / den) < 0.02, "BF16 decode against FP32-exact: " << std::sqrt(num / den));
+    }
+    catch (const std::exception &e)
+    {
+        std::cerr << "VAE exception: " << e.what() << "\n";
+        return 1;
+    }
     if (failures) return 1;
     std::cout << "host GPU contracts passed\n";
     return 0;

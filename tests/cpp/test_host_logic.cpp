@@ -416,9 +416,40 @@ static void img2img_contract()
             "NaN noise accepted");
 }
 
+// rgb_image (src/pipeline.cpp:145-163) and the VAE decoder's tensor table (no device needed)
+static void vae_contract()
+{
+    Tensor decoded(4, 1, 3);
+    const float values[4] = {-3.f, 0.f, 0.5f, 1.f / 255.f};
+    for (int c = 0; c < 3; ++c)
+        for (int i = 0; i < 4; ++i) decoded[size_t(c) * 4 + size_t(i)] = values[i] * float(c + 1);
+    const RgbImage image = rgb_image(decoded);
+    REQUIRE(image.width == 4 && image.height == 1 && image.pixels.size() == 12, "RGB shape");
+    // channel 0: -3 -> 0, 0 -> 128 (127.5 rounds to even), 0.5 -> 191, 1/255 -> 128
+    const uint8_t expected0[4] = {0, 128, 191, 128};
+    for (int i = 0; i < 4; ++i) REQUIRE(image.pixels[size_t(i) * 3] == expected0[i], "RGB byte " << i);
+    REQUIRE(image.pixels[2 * 3 + 2] == 255, "0.5 * 3 clamps to 255");
+    decoded[5] = std::numeric_limits<float>::quiet_NaN();
+    REQUIRE(throws<std::runtime_error>([&] { rgb_image(decoded); }), "non-finite pixel accepted");
+    REQUIRE(throws<std::runtime_error>([&] { rgb_image(Tensor(4, 1, 4)); }), "4 channels accepted");
+    const auto tensors = VaeDecoder::tensors();
+    REQUIRE(tensors.size() == 140, "VAE tensor count " << tensors.size());
+    REQUIRE(tensors.front().first == "post_quant_conv.weight" && tensors.back().first == "decoder.conv_out.bias",
+            "VAE tensor order");
+    size_t params = 0;
+    for (const auto &t : tensors)
+    {
+        size_t n = 1;
+        for (int d : t.second) n *= size_t(d);
+        params += n;
+    }
+    REQUIRE(params == 49620259, "VAE parameter count " << params);
+}
+
 int main()
 {
     latent_contract();
+    vae_contract();
     conditioning_contract();
     error_mapping();
     placement_contract();
