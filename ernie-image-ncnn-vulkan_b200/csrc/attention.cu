@@ -6,9 +6,10 @@
 //
 //  * BF16 mode runs the tcgen05/TMEM flash kernel in flash_tc.cu.
 //  * attention_f32_kernel: FP32 scores, FP64 softmax sums and P.V accumulation. Serves the FP32
-//    exactness mode and the stand-alone SDPA layer contract (GQA with one K/V head, widths up to 128,
+//    exactness mode, the stand-alone SDPA layer contract (GQA with one K/V head, widths up to 128,
 //    row or dense additive masks, mask per head), replacing the reference's Kahan-compensated
-//    FP32 shaders (cmake/ErnieAttentionShader.cmake:18-55).
+//    FP32 shaders (cmake/ErnieAttentionShader.cmake:18-55), and the text encoder's causal grouped-query
+//    attention (32 query heads over 8 K/V heads).
 #include "kernels.h"
 #include <cmath>
 
@@ -38,7 +39,7 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
     float *vs = ks + kFK * (kDim + 1);       // [32][128]
     float *ps = vs + kFK * kDim;             // [64][33]
     const int head = blockIdx.y, q0 = blockIdx.x * kFQ;
-    const int kv_head = a.kv_heads == 1 ? 0 : head;
+    const int kv_head = head / (a.heads / a.kv_heads);
     const int tid = threadIdx.x, qi = tid >> 2, sub = tid & 3;
     const int width = a.width;
     const float scale = 1.f / sqrtf(static_cast<float>(width));
@@ -61,7 +62,9 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
     double acc[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0.0;
-    const int tiles = (a.kv_len + kFK - 1) / kFK;
+    // causal: no key past this CTA's last query row
+    const int kv_end = a.causal ? min(a.kv_len, q0 + kFQ) : a.kv_len;
+    const int tiles = (kv_end + kFK - 1) / kFK;
     for (int j = 0; j < tiles; ++j)
     {
         const int key0 = j * kFK;
@@ -86,7 +89,7 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
 #pragma unroll 8
             for (int d = 0; d < kDim; ++d) dot = fmaf(qr[d], kr[d], dot);
             const int key = key0 + kj;
-            float x = key < a.kv_len ? dot * scale + (mrow ? mrow[key] : 0.f) : -INFINITY;
+            float x = key < a.kv_len && !(a.causal && key > qrow) ? dot * scale + (mrow ? mrow[key] : 0.f) : -INFINITY;
             sc[i] = x;
             tile_max = fmaxf(tile_max, x);
         }
@@ -130,6 +133,16 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
             if (d < width) dst[d] = static_cast<float>(acc[i] / l_run);
         }
     }
+    else if (a.out_mode == 2)
+    {
+        __nv_bfloat16 *dst = a.out_split3 + (static_cast<size_t>(qrow) * a.heads + head) * width;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+        {
+            const int d = sub + 4 * i;
+            if (d < width) dst[d] = __float2bfloat16_rn(static_cast<float>(acc[i] / l_run));
+        }
+    }
     else
     {
         const size_t plane = static_cast<size_t>(a.heads) * width;
@@ -152,7 +165,8 @@ int prepare_attention_kernels()
 int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream)
 {
     if (args.nq < 1 || args.nk < 1 || args.kv_len < 1 || args.kv_len > args.nk || args.width < 1 ||
-        args.width > kDim || args.heads < 1 || (args.kv_heads != 1 && args.kv_heads != args.heads) ||
+        args.width > kDim || args.heads < 1 || args.kv_heads < 1 || args.heads % args.kv_heads ||
+        args.out_mode < 0 || args.out_mode > 2 ||
         (args.mask && args.mask_heads != 1 && args.mask_heads != args.heads) ||
         (args.mask && args.mask_rows != 1 && args.mask_rows != args.nq))
         return cudaErrorInvalidValue;

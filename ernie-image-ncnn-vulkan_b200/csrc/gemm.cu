@@ -340,7 +340,20 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
             tmem_load_32(e.taddr + g * 128 + c, up);
             tmem_load_32(e.taddr + g * 128 + 64 + c, gate);
             const int f = e.n_blk * (BN / 2) + g * 64 + c;
-            if (a.h_split3) // FP32-exact mode: erfc as the reference's CPU path computes it
+            if (a.silu) // SwiGLU (MistralMLP: silu(gate) * up)
+            {
+                if (a.h_split3)
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) up[j] = up[j] * __fdiv_rn(gate[j], 1.f + expf(-gate[j]));
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) up[j] = up[j] * __fdividef(gate[j], 1.f + __expf(-gate[j]));
+                }
+            }
+            else if (a.h_split3) // FP32-exact mode: erfc as the reference's CPU path computes it
             {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) up[j] = up[j] * gelu_erf(gate[j]);

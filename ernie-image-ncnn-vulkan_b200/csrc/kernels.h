@@ -48,6 +48,7 @@ struct GemmEpilogueArgs
     __nv_bfloat16 *h = nullptr;
     int h_split3 = 0;
     int ffn = 0;
+    int silu = 0; // Geglu with SiLU instead of GELU: h = up * silu(gate) (the text encoder's SwiGLU MLP)
     // FinalEuler
     float *latent = nullptr;     // [128][ld_latent] (ld_latent 0: rows)
     int ld_latent = 0;
@@ -128,8 +129,10 @@ int launch_flash_f32(const __nv_bfloat16 *q3, const __nv_bfloat16 *k3, const __n
 int prepare_flash_f32_kernels();
 
 // FP32 attention with FP64 softmax accumulation. q [heads][q_stride rows][width] (head stride
-// q_head_stride elements), k/v [kv_heads][...]; mask [mask_heads][mask_rows][nk] additive (nullable).
-// out_mode 0: FP32 [heads][nq][width]; out_mode 1: split-3 BF16 token-major [nq][3*heads*width].
+// q_head_stride elements), k/v [kv_heads][...] with kv_heads dividing heads (query head h reads K/V head
+// h / (heads / kv_heads)); mask [mask_heads][mask_rows][nk] additive (nullable); causal: key j > query i
+// excluded (key tiles past the diagonal skipped). out_mode 0: FP32 [heads][nq][width]; 1: split-3 BF16
+// token-major [nq][3*heads*width]; 2: BF16 token-major [nq][heads*width] (in out_split3).
 struct AttentionF32Args
 {
     const float *q, *k, *v, *mask;
@@ -138,6 +141,7 @@ struct AttentionF32Args
     int out_mode;
     float *out_f32;
     __nv_bfloat16 *out_split3;
+    int causal;
 };
 int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream);
 
@@ -214,6 +218,11 @@ int launch_conv_weight_prep(const float *w, int cout, int cin, int taps, int cou
 int launch_synth_f32(uint64_t seed, uint64_t stream_id, float scale, float offset, long long count, int round_bf16,
                      float *out, cudaStream_t stream);
 int prepare_conv_kernels();
+
+// ---- text encoder (text.cu) -------------------------------------------------------------------------
+// qkv FP32 [tokens][6144] -> rotated head-major q [32][tokens][128], k [8][tokens][128] and v [8][tokens][128].
+int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q, float *k, float *v,
+                     cudaStream_t stream);
 
 // Synthetic weights on device (ernie_synth.h protocol). rows x cols BF16 written at `out` with a
 // destination row index map: dst_row = (row / group) * group_stride + group_offset + row % group.

@@ -1,0 +1,52 @@
+// The text encoder's rotary embedding and head split (reference: the Mistral decoder layer the reference
+// exports per block, tools/export_text_block.py:50-61, with ExportBlock.rotary's half-split rotation,
+// tools/export_dit_block.py:39-47).
+#include "kernels.h"
+
+namespace ernie_b200
+{
+namespace
+{
+constexpr int kTextQHeads = 32, kTextKvHeads = 8, kTextHeadDim = 128, kTextQkv = (32 + 2 * 8) * 128;
+
+// qkv FP32 [tokens][6144] (q 32 heads, k 8 heads, v 8 heads, 128 each) -> head-major FP32 q [32][tokens][128],
+// k, v [8][tokens][128]; q and k rotated: out[:64] = x[:64] cos[:64] - x[64:] sin[:64],
+// out[64:] = x[64:] cos[64:] + x[:64] sin[64:] (FP32, no contraction).
+__global__ void text_rope_kernel(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q,
+                                 float *k, float *v)
+{
+    const int head = blockIdx.y, t = blockIdx.x, d = threadIdx.x; // 64 threads: pairs (d, d + 64)
+    if (t >= tokens) return;
+    const float *row = qkv + static_cast<size_t>(t) * kTextQkv;
+    if (head < kTextQHeads + kTextKvHeads)
+    {
+        const float *x = row + head * kTextHeadDim;
+        const float *c = cos_t + static_cast<size_t>(t) * kTextHeadDim, *s = sin_t + static_cast<size_t>(t) * kTextHeadDim;
+        const float first = x[d], second = x[d + 64];
+        const float lo = __fsub_rn(__fmul_rn(first, c[d]), __fmul_rn(second, s[d]));
+        const float hi = __fadd_rn(__fmul_rn(second, c[d + 64]), __fmul_rn(first, s[d + 64]));
+        float *dst = head < kTextQHeads
+                         ? q + (static_cast<size_t>(head) * tokens + t) * kTextHeadDim
+                         : k + (static_cast<size_t>(head - kTextQHeads) * tokens + t) * kTextHeadDim;
+        dst[d] = lo;
+        dst[d + 64] = hi;
+    }
+    else
+    {
+        const int vh = head - kTextQHeads - kTextKvHeads;
+        const float *x = row + (kTextQHeads + kTextKvHeads + vh) * kTextHeadDim;
+        float *dst = v + (static_cast<size_t>(vh) * tokens + t) * kTextHeadDim;
+        dst[d] = x[d];
+        dst[d + 64] = x[d + 64];
+    }
+}
+} // namespace
+
+int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q, float *k, float *v,
+                     cudaStream_t stream)
+{
+    if (tokens < 1) return cudaErrorInvalidValue;
+    text_rope_kernel<<<dim3(tokens, kTextQHeads + 2 * kTextKvHeads), 64, 0, stream>>>(qkv, cos_t, sin_t, tokens, q, k, v);
+    return cudaGetLastError();
+}
+} // namespace ernie_b200

@@ -1,0 +1,334 @@
+// C ABI of the prompt encoder (include/ernie_cuda.h, "Text encoder"): the Mistral decoder layers the
+// reference runs one ncnn block at a time (run_text_blocks, src/text_encoder.cpp:101-160; the block graph
+// is tools/export_text_block.py:50-61 TextBlock.forward) with every layer's weights resident on the device,
+// and the constants of text_constants (src/text_encoder.cpp:77-100). Host orchestration only.
+//
+// Per layer (hidden 3072, 32 query heads and 8 K/V heads of 128, SwiGLU 9216, RMSNorm eps 1e-5):
+//   norm_modulate (RMSNorm, input_layernorm) -> tcgen05 GEMM [q; k; v] (F32 out) -> text_rope_kernel ->
+//   causal grouped-query FP32 attention -> GEMM o_proj, residual added in its epilogue (gate 1) ->
+//   RMSNorm (post_attention_layernorm) -> GEMM [up; gate] with the SwiGLU epilogue -> GEMM down_proj +
+//   residual.
+#include "capi_internal.h"
+#include "ernie_synth.h"
+#include "kernels.h"
+#include <cmath>
+#include <limits>
+#include <memory>
+#include <vector>
+
+using namespace ernie_b200;
+using namespace ernie_b200::capi;
+
+namespace
+{
+constexpr int kTH = 3072, kTQ = 4096, kTKV = 1024, kTQkv = kTQ + 2 * kTKV, kTFfn = 9216, kTMaxLayers = 26;
+constexpr int kTMaxBucket = 2048;
+constexpr float kTEps = 1e-5f;
+
+struct TextLayer
+{
+    __nv_bfloat16 *wqkv = nullptr; // [6144][3072]: q_proj, k_proj, v_proj rows
+    __nv_bfloat16 *wo = nullptr;   // [3072][4096]
+    __nv_bfloat16 *wug = nullptr;  // [18432][3072]: up_proj / gate_proj interleaved in 64-row groups
+    __nv_bfloat16 *wdown = nullptr; // [3072][9216]
+    float *gamma_attn = nullptr, *gamma_mlp = nullptr; // [3072]
+};
+
+struct TextWork
+{
+    int tokens = 0, precision = -1, planes = 1;
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+    __nv_bfloat16 *a = nullptr, *h = nullptr;
+    void *alloc = nullptr;
+};
+} // namespace
+
+struct ernie_cuda_text_model
+{
+    ernie_cuda_context *ctx = nullptr;
+    int num_layers = 0;
+    std::vector<TextLayer> layers;
+    float *ones = nullptr; // the residual epilogue's gate
+    void *alloc = nullptr;
+    uint64_t bytes = 0;
+    TextWork work;
+};
+
+namespace
+{
+void free_work(TextWork &w)
+{
+    if (w.alloc) cudaFree(w.alloc);
+    w = TextWork{};
+}
+
+int ensure_work(ernie_cuda_text_model *m, int tokens, int precision)
+{
+    TextWork &w = m->work;
+    if (w.alloc && w.tokens == tokens && w.precision == precision) return ERNIE_CUDA_OK;
+    free_work(w);
+    w.tokens = tokens;
+    w.precision = precision;
+    w.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    const size_t t = static_cast<size_t>(tokens);
+    Arena arena;
+    arena.add(&w.x, t * kTH);
+    arena.add(&w.qkv, t * kTQkv);
+    arena.add(&w.q, t * kTQ);
+    arena.add(&w.k, t * kTKV);
+    arena.add(&w.v, t * kTKV);
+    arena.add(&w.cos_t, t * 128);
+    arena.add(&w.sin_t, t * 128);
+    arena.add(&w.a, t * w.planes * kTQ);
+    arena.add(&w.h, t * w.planes * kTFfn);
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess)
+    {
+        w = TextWork{};
+        return from_cuda(e, "Allocate text encoder workspace");
+    }
+    w.alloc = arena.base;
+    return ERNIE_CUDA_OK;
+}
+
+// run_text_blocks on the model's device workspace: w.x [tokens][3072] in, updated in place.
+int enqueue_layers(ernie_cuda_text_model *m, int count)
+{
+    TextWork &w = m->work;
+    cudaStream_t s = m->ctx->stream;
+    const int sms = m->ctx->num_sms, T = w.tokens;
+    const bool fp32 = w.precision == ERNIE_PRECISION_FP32;
+    const int splits = fp32 ? 3 : 1, block_n = fp32 ? 128 : 256;
+    for (int l = 0; l < count; ++l)
+    {
+        const TextLayer &L = m->layers[static_cast<size_t>(l)];
+        GemmEpilogueArgs f32;
+        f32.out = w.qkv;
+        f32.ldo = kTQkv;
+        f32.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_norm_modulate(w.x, T, kTH, L.gamma_attn, nullptr, nullptr, kTEps, 0, w.a, fp32 ? 1 : 0, s),
+                     "text input_layernorm");
+        ERNIE_LAUNCH(launch_gemm(w.a, L.wqkv, T, kTQkv, kTH, splits, block_n, Epilogue::F32Bias, f32, sms, s, fp32),
+                     "text qkv projection");
+        ERNIE_LAUNCH(launch_text_rope(w.qkv, w.cos_t, w.sin_t, T, w.q, w.k, w.v, s), "text rotary");
+        AttentionF32Args at{};
+        at.q = w.q;
+        at.k = w.k;
+        at.v = w.v;
+        at.heads = 32;
+        at.kv_heads = 8;
+        at.mask_heads = 1;
+        at.mask_rows = 1;
+        at.nq = at.nk = at.kv_len = T;
+        at.width = 128;
+        at.q_head_stride = static_cast<long long>(T) * 128;
+        at.kv_head_stride = static_cast<long long>(T) * 128;
+        at.causal = 1;
+        at.out_mode = fp32 ? 1 : 2;
+        at.out_split3 = w.a;
+        ERNIE_LAUNCH(launch_attention_f32(at, s), "text attention");
+        GemmEpilogueArgs res;
+        res.resid = w.x;
+        res.ldo = kTH; // the residual's row stride
+        res.gate = m->ones;
+        res.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_gemm(w.a, L.wo, T, kTH, kTQ, splits, block_n, Epilogue::ResidGate, res, sms, s, fp32),
+                     "text o_proj");
+        ERNIE_LAUNCH(launch_norm_modulate(w.x, T, kTH, L.gamma_mlp, nullptr, nullptr, kTEps, 0, w.a, fp32 ? 1 : 0, s),
+                     "text post_attention_layernorm");
+        GemmEpilogueArgs glu;
+        glu.h = w.h;
+        glu.h_split3 = fp32 ? 1 : 0;
+        glu.ffn = kTFfn;
+        glu.silu = 1;
+        glu.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_gemm(w.a, L.wug, T, 2 * kTFfn, kTH, splits, block_n, Epilogue::Geglu, glu, sms, s, fp32),
+                     "text gate/up projection");
+        ERNIE_LAUNCH(launch_gemm(w.h, L.wdown, T, kTH, kTFfn, splits, block_n, Epilogue::ResidGate, res, sms, s, fp32),
+                     "text down_proj");
+    }
+    return ERNIE_CUDA_OK;
+}
+
+int check_status(ernie_cuda_text_model *m)
+{
+    int flag = 0;
+    ERNIE_CUDA(cudaMemcpyAsync(&flag, m->ctx->error_flag, sizeof(int), cudaMemcpyDeviceToHost, m->ctx->stream),
+               "read status");
+    ERNIE_CUDA(cudaStreamSynchronize(m->ctx->stream), "text encoder");
+    if (flag) return fail(ERNIE_CUDA_ERROR, "Text encoder kernel protocol timeout (status " + std::to_string(flag) + ")");
+    return ERNIE_CUDA_OK;
+}
+} // namespace
+
+extern "C" int ernie_cuda_text_model_create(ernie_cuda_context *ctx, int num_layers, ernie_cuda_text_model **out)
+{
+    if (!ctx || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *out = nullptr;
+    if (num_layers < 1 || num_layers > kTMaxLayers) return fail(ERNIE_CUDA_ERROR, "Text encoder requires 1..26 layers");
+    DeviceGuard guard(ctx->device);
+    auto m = std::make_unique<ernie_cuda_text_model>();
+    m->ctx = ctx;
+    m->num_layers = num_layers;
+    m->layers.resize(static_cast<size_t>(num_layers));
+    Arena arena;
+    for (auto &L : m->layers)
+    {
+        arena.add(&L.wqkv, static_cast<size_t>(kTQkv) * kTH);
+        arena.add(&L.wo, static_cast<size_t>(kTH) * kTQ);
+        arena.add(&L.wug, static_cast<size_t>(2 * kTFfn) * kTH);
+        arena.add(&L.wdown, static_cast<size_t>(kTH) * kTFfn);
+        arena.add(&L.gamma_attn, kTH);
+        arena.add(&L.gamma_mlp, kTH);
+    }
+    arena.add(&m->ones, kTH);
+    m->bytes = arena.bytes();
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess) return from_cuda(e, "Allocate text encoder weights");
+    m->alloc = arena.base;
+    std::vector<float> ones(kTH, 1.f);
+    const cudaError_t c = cudaMemcpy(m->ones, ones.data(), kTH * 4, cudaMemcpyHostToDevice);
+    if (c != cudaSuccess)
+    {
+        cudaFree(m->alloc);
+        return from_cuda(c, "Upload text encoder constants");
+    }
+    *out = m.release();
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_text_model_destroy(ernie_cuda_text_model *m)
+{
+    if (!m) return ERNIE_CUDA_OK;
+    DeviceGuard guard(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    free_work(m->work);
+    if (m->alloc) cudaFree(m->alloc);
+    delete m;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_text_model_bytes(ernie_cuda_text_model *m, uint64_t *bytes)
+{
+    if (!m || !bytes) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *bytes = m->bytes;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_text_model_upload_layer(ernie_cuda_text_model *m, int layer,
+                                                  const ernie_cuda_text_layer_weights *w)
+{
+    if (!m || !w || layer < 0 || layer >= m->num_layers) return fail(ERNIE_CUDA_ERROR, "Invalid text layer upload");
+    if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wgate || !w->wup || !w->wdown || !w->gamma_attn || !w->gamma_mlp)
+        return fail(ERNIE_CUDA_ERROR, "Text layer weights must provide all 9 tensors");
+    DeviceGuard guard(m->ctx->device);
+    const TextLayer &L = m->layers[static_cast<size_t>(layer)];
+    auto copy = [](void *dst, const void *src, size_t bytes) { return cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice); };
+    ERNIE_CUDA(copy(L.wqkv, w->wq, size_t(kTQ) * kTH * 2), "upload q_proj");
+    ERNIE_CUDA(copy(L.wqkv + size_t(kTQ) * kTH, w->wk, size_t(kTKV) * kTH * 2), "upload k_proj");
+    ERNIE_CUDA(copy(L.wqkv + size_t(kTQ + kTKV) * kTH, w->wv, size_t(kTKV) * kTH * 2), "upload v_proj");
+    ERNIE_CUDA(copy(L.wo, w->wo, size_t(kTH) * kTQ * 2), "upload o_proj");
+    const size_t group = size_t(64) * kTH; // [up; gate] interleaved in 64-row groups (the gated epilogue's layout)
+    for (int g = 0; g < kTFfn / 64; ++g)
+    {
+        ERNIE_CUDA(copy(L.wug + size_t(2 * g) * group, w->wup + size_t(g) * group, group * 2), "upload up_proj");
+        ERNIE_CUDA(copy(L.wug + size_t(2 * g + 1) * group, w->wgate + size_t(g) * group, group * 2), "upload gate_proj");
+    }
+    ERNIE_CUDA(copy(L.wdown, w->wdown, size_t(kTH) * kTFfn * 2), "upload down_proj");
+    ERNIE_CUDA(copy(L.gamma_attn, w->gamma_attn, kTH * 4), "upload input_layernorm");
+    ERNIE_CUDA(copy(L.gamma_mlp, w->gamma_mlp, kTH * 4), "upload post_attention_layernorm");
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_text_model_synthesize(ernie_cuda_text_model *m, uint64_t seed)
+{
+    if (!m) return fail(ERNIE_CUDA_ERROR, "null model");
+    DeviceGuard guard(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const float std = ERNIE_SYNTH_WEIGHT_STD;
+    for (int l = 0; l < m->num_layers; ++l)
+    {
+        const TextLayer &L = m->layers[static_cast<size_t>(l)];
+        auto sid = [l](int t) { return static_cast<uint64_t>(ERNIE_SYNTH_TEXT_STREAM(l, t)); };
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WQ), std, 0.f, kTQ, kTH, kTQ, 0, 0, L.wqkv, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WK), std, 0.f, kTKV, kTH, kTKV, 0, kTQ, L.wqkv, s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WV), std, 0.f, kTKV, kTH, kTKV, 0, kTQ + kTKV, L.wqkv,
+                                       s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WO), std, 0.f, kTH, kTQ, kTH, 0, 0, L.wo, s), "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WUP), std, 0.f, kTFfn, kTH, 64, 128, 0, L.wug, s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WGATE), std, 0.f, kTFfn, kTH, 64, 128, 64, L.wug, s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_bf16(seed, sid(ERNIE_SYNTH_TEXT_WDOWN), std, 0.f, kTH, kTFfn, kTH, 0, 0, L.wdown, s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_TEXT_GAMMA_ATTN), std, 1.f, kTH, L.gamma_attn, s),
+                     "synth");
+        ERNIE_LAUNCH(launch_synth_f32_bf16(seed, sid(ERNIE_SYNTH_TEXT_GAMMA_MLP), std, 1.f, kTH, L.gamma_mlp, s),
+                     "synth");
+    }
+    return from_cuda(cudaStreamSynchronize(s), "synthesize text weights");
+}
+
+extern "C" int ernie_cuda_text_constants(const float *inv_freq, int bucket, float *cos_out, float *sin_out,
+                                         float *mask)
+{
+    if (!inv_freq || !cos_out || !sin_out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (bucket < 1 || bucket > kTMaxBucket) return fail(ERNIE_CUDA_ERROR, "Text bucket must be in [1,2048]");
+    for (int j = 0; j < 64; ++j)
+        if (!std::isfinite(inv_freq[j]) || inv_freq[j] <= 0.f) return fail(ERNIE_CUDA_ERROR, "Invalid YaRN frequency");
+    for (int t = 0; t < bucket; ++t)
+    {
+        float *c = cos_out + static_cast<size_t>(t) * 128, *s = sin_out + static_cast<size_t>(t) * 128;
+        for (int j = 0; j < 64; ++j)
+        {
+            const float phase = float(t) * inv_freq[j]; // host code: -ffp-contract=off
+            c[j] = c[j + 64] = std::cos(phase);
+            s[j] = s[j + 64] = std::sin(phase);
+        }
+        if (mask)
+            for (int k = 0; k < bucket; ++k)
+                mask[static_cast<size_t>(t) * bucket + k] = k > t ? -std::numeric_limits<float>::max() : 0.f;
+    }
+    return ERNIE_CUDA_OK;
+}
+
+namespace
+{
+int run_text(ernie_cuda_text_model *m, const float *input, int bucket, const float *cos_t, const float *sin_t,
+             int precision, int layers, float *out, cudaMemcpyKind in_kind, cudaMemcpyKind out_kind)
+{
+    if (!m || !input || !cos_t || !sin_t || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (bucket < 1 || bucket > kTMaxBucket) return fail(ERNIE_CUDA_ERROR, "Text bucket must be in [1,2048]");
+    if (layers < 1 || layers > m->num_layers) return fail(ERNIE_CUDA_ERROR, "Text path requires 1..num_layers blocks");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(m->ctx->device);
+    ERNIE_TRY(ensure_work(m, bucket, precision));
+    TextWork &w = m->work;
+    cudaStream_t s = m->ctx->stream;
+    const size_t t = static_cast<size_t>(bucket);
+    ERNIE_CUDA(cudaMemcpyAsync(w.x, input, t * kTH * 4, in_kind, s), "text input");
+    ERNIE_CUDA(cudaMemcpyAsync(w.cos_t, cos_t, t * 128 * 4, in_kind, s), "text cos");
+    ERNIE_CUDA(cudaMemcpyAsync(w.sin_t, sin_t, t * 128 * 4, in_kind, s), "text sin");
+    ERNIE_TRY(enqueue_layers(m, layers));
+    ERNIE_CUDA(cudaMemcpyAsync(out, w.x, t * kTH * 4, out_kind, s), "text output");
+    return check_status(m);
+}
+} // namespace
+
+extern "C" int ernie_cuda_text_run_blocks(ernie_cuda_text_model *m, const float *input, int bucket, const float *cos_t,
+                                          const float *sin_t, int precision, int layers, float *out)
+{
+    return run_text(m, input, bucket, cos_t, sin_t, precision, layers, out, cudaMemcpyHostToDevice,
+                    cudaMemcpyDeviceToHost);
+}
+
+extern "C" int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *m, const float *input, int bucket,
+                                                 const float *cos_t, const float *sin_t, int precision, int layers,
+                                                 float *out)
+{
+    return run_text(m, input, bucket, cos_t, sin_t, precision, layers, out, cudaMemcpyDeviceToDevice,
+                    cudaMemcpyDeviceToDevice);
+}

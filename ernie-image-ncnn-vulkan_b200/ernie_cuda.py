@@ -54,6 +54,10 @@ class HeadWeights(ctypes.Structure):
                                  "final_b")]
 
 
+class TextLayerWeights(ctypes.Structure):
+    _fields_ = [(n, P) for n in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "gamma_attn", "gamma_mlp")]
+
+
 class Shape(ctypes.Structure):
     _fields_ = [("width", I), ("height", I), ("text_tokens", I), ("valid_text", I)]
 
@@ -112,6 +116,14 @@ SIGNATURES = {
     "ernie_cuda_sp_handle": (I, [P, P]),
     "ernie_cuda_sp_connect": (I, [P, P]),
     "ernie_cuda_sp_layout": (I, [I, I, I, I] + [ctypes.POINTER(I)] * 5),
+    "ernie_cuda_text_model_create": (I, [P, I, ctypes.POINTER(P)]),
+    "ernie_cuda_text_model_destroy": (I, [P]),
+    "ernie_cuda_text_model_bytes": (I, [P, ctypes.POINTER(U64)]),
+    "ernie_cuda_text_model_upload_layer": (I, [P, I, ctypes.POINTER(TextLayerWeights)]),
+    "ernie_cuda_text_model_synthesize": (I, [P, U64]),
+    "ernie_cuda_text_constants": (I, [P, I, P, P, P]),
+    "ernie_cuda_text_run_blocks": (I, [P, P, I, P, P, I, I, P]),
+    "ernie_cuda_text_run_blocks_device": (I, [P, P, I, P, P, I, I, P]),
     "ernie_cuda_vae_create": (I, [P, ctypes.POINTER(P)]),
     "ernie_cuda_vae_destroy": (I, [P]),
     "ernie_cuda_vae_tensor_count": (I, [ctypes.POINTER(I)]),
@@ -423,6 +435,57 @@ class Model:
     def nbytes(self):
         b = U64(0)
         check(lib().ernie_cuda_model_bytes(self.handle, ctypes.byref(b)))
+        return b.value
+
+
+def text_constants(inv_freq, bucket, mask=False):
+    """text_constants: (cos [bucket][128], sin [bucket][128], causal mask [bucket][bucket] or None)."""
+    f = np.ascontiguousarray(inv_freq, np.float32)
+    cos, sin = np.empty((bucket, 128), np.float32), np.empty((bucket, 128), np.float32)
+    m = np.empty((bucket, bucket), np.float32) if mask else None
+    check(lib().ernie_cuda_text_constants(ptr(f), bucket, ptr(cos), ptr(sin), ptr(m)))
+    return cos, sin, m
+
+
+class TextModel:
+    """Device-resident prompt-encoder layers (run_text_blocks on the B200)."""
+
+    NAMES = ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "gamma_attn", "gamma_mlp")
+
+    def __init__(self, ctx, num_layers=25):
+        h = P()
+        check(lib().ernie_cuda_text_model_create(ctx.handle, num_layers, ctypes.byref(h)))
+        self.handle, self.ctx, self.num_layers = h, ctx, num_layers
+
+    def close(self):
+        if self.handle:
+            lib().ernie_cuda_text_model_destroy(self.handle)
+            self.handle = None
+
+    def synthesize(self, seed):
+        check(lib().ernie_cuda_text_model_synthesize(self.handle, seed))
+
+    def upload_layer(self, layer, tensors):
+        """tensors: wq, wk, wv, wo, wgate, wup, wdown as uint16 BF16 bits; gamma_attn, gamma_mlp float32."""
+        keep = {k: np.ascontiguousarray(v) for k, v in tensors.items()}
+        w = TextLayerWeights(*(ptr(keep[n]) for n in self.NAMES))
+        check(lib().ernie_cuda_text_model_upload_layer(self.handle, layer, ctypes.byref(w)))
+
+    def run_blocks(self, x, cos, sin, precision=BF16, layers=None):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        check(lib().ernie_cuda_text_run_blocks(self.handle, ptr(x), x.shape[0], ptr(np.ascontiguousarray(cos, np.float32)),
+                                               ptr(np.ascontiguousarray(sin, np.float32)), precision,
+                                               layers or self.num_layers, ptr(out)))
+        return out
+
+    def run_blocks_device(self, x_dev, bucket, cos_dev, sin_dev, out_dev, precision=BF16, layers=None):
+        check(lib().ernie_cuda_text_run_blocks_device(self.handle, x_dev.c, bucket, cos_dev.c, sin_dev.c, precision,
+                                                      layers or self.num_layers, out_dev.c))
+
+    def nbytes(self):
+        b = U64(0)
+        check(lib().ernie_cuda_text_model_bytes(self.handle, ctypes.byref(b)))
         return b.value
 
 

@@ -195,6 +195,44 @@ int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial
    std::normal_distribution<float>(0, 1), channel after channel, into out [128][height][width]. Host-only. */
 int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out);
 
+/* ---- Text encoder (the prompt encoder before the denoise loop) ------------------------------------
+   run_text_blocks (src/text_encoder.h:17-19, src/text_encoder.cpp:101-160) on one B200: the Mistral decoder
+   layers the reference exports per block (tools/export_text_block.py:50-61: hidden 3072, 32 query and 8
+   K/V heads of 128, SwiGLU 9216, RMSNorm eps 1e-5, no biases), all layers resident on the device (the
+   pipeline runs layers 0..24). Input: the embedded prompt [bucket][3072] FP32 (text_embeddings; rows past
+   the prompt zero), cos/sin [bucket][128] of ernie_cuda_text_constants; the attention mask is the causal
+   mask text_constants builds. Output: the hidden state [bucket][3072] after `layers` layers (1..num_layers).
+   precision: BF16 (BF16 GEMM operands, FP32 accumulation, residual, norms and attention) or FP32
+   (three-plane FP32-exact GEMMs against the exact-BF16 weights; FP32 attention with FP64 sums). */
+typedef struct ernie_cuda_text_model ernie_cuda_text_model;
+/* One layer's weights as the official checkpoint stores them (language_model.model.layers.N.*). */
+typedef struct
+{
+    const uint16_t *wq;             /* [4096,3072] BF16 self_attn.q_proj */
+    const uint16_t *wk, *wv;        /* [1024,3072] self_attn.k_proj / v_proj */
+    const uint16_t *wo;             /* [3072,4096] self_attn.o_proj */
+    const uint16_t *wgate, *wup;    /* [9216,3072] mlp.gate_proj / up_proj */
+    const uint16_t *wdown;          /* [3072,9216] mlp.down_proj */
+    const float *gamma_attn;        /* [3072] input_layernorm */
+    const float *gamma_mlp;         /* [3072] post_attention_layernorm */
+} ernie_cuda_text_layer_weights;
+int ernie_cuda_text_model_create(ernie_cuda_context *ctx, int num_layers, ernie_cuda_text_model **out);
+int ernie_cuda_text_model_destroy(ernie_cuda_text_model *model);
+int ernie_cuda_text_model_bytes(ernie_cuda_text_model *model, uint64_t *bytes);
+int ernie_cuda_text_model_upload_layer(ernie_cuda_text_model *model, int layer, const ernie_cuda_text_layer_weights *host);
+/* Seeded random-init weights (include/ernie_synth.h, text encoder streams). */
+int ernie_cuda_text_model_synthesize(ernie_cuda_text_model *model, uint64_t seed);
+/* text_constants (src/text_encoder.cpp:77-100), host: inv_freq[64] (the YaRN inverse frequencies) ->
+   cos/sin [bucket][128] (both halves of a row repeat the 64 angles t * f_j) and, if mask is not null, the
+   causal mask [bucket][bucket] (0 on and below the diagonal, -FLT_MAX above). */
+int ernie_cuda_text_constants(const float *inv_freq, int bucket, float *cos_out, float *sin_out, float *mask);
+/* Host buffers, synchronous. */
+int ernie_cuda_text_run_blocks(ernie_cuda_text_model *model, const float *input, int bucket, const float *cos_t,
+                               const float *sin_t, int precision, int layers, float *out);
+/* Device buffers on the context's stream (synchronous: the kernels' status is checked). */
+int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *model, const float *input, int bucket,
+                                      const float *cos_t, const float *sin_t, int precision, int layers, float *out);
+
 /* ---- VAE decoder (the stage after the denoise loop) -----------------------------------------------
    decode_vae (src/vae.h:16-22, src/vae.cpp:18-66) of the pinned AutoencoderKLFlux2 post_quant_conv +
    decoder, and rgb_image (src/pipeline.cpp:145-163), on one B200. Weights are addressed by their

@@ -109,6 +109,22 @@ enum ernie_synth_tensor
 #define ERNIE_SYNTH_BLOCK_STREAM(block, tensor) ((uint64_t)((block) + 1) * 64u + (uint64_t)(tensor))
 #define ERNIE_SYNTH_WEIGHT_STD 0.02f
 
+/* Text encoder layers (Mistral decoder layers of the prompt encoder): BF16 weights N(0, 0.02) and RMSNorm
+ * weights 1 + N(0, 0.02) as for the DiT blocks, streams ERNIE_SYNTH_TEXT_STREAM(layer, tensor). */
+enum ernie_synth_text_tensor
+{
+    ERNIE_SYNTH_TEXT_WQ = 0,
+    ERNIE_SYNTH_TEXT_WK = 1,
+    ERNIE_SYNTH_TEXT_WV = 2,
+    ERNIE_SYNTH_TEXT_WO = 3,
+    ERNIE_SYNTH_TEXT_WGATE = 4,
+    ERNIE_SYNTH_TEXT_WUP = 5,
+    ERNIE_SYNTH_TEXT_WDOWN = 6,
+    ERNIE_SYNTH_TEXT_GAMMA_ATTN = 7,
+    ERNIE_SYNTH_TEXT_GAMMA_MLP = 8
+};
+#define ERNIE_SYNTH_TEXT_STREAM(layer, tensor) (0x54455854ULL * 4096u + (uint64_t)((layer) + 1) * 64u + (uint64_t)(tensor))
+
 /* VAE decoder tensors are addressed by their diffusers parameter name (e.g. "decoder.conv_in.weight"):
  * stream = FNV-1a 64 of the name. Values are FP32, float(N(0,1) * scale) + offset, with
  *   convolution / linear weights   scale 1/sqrt(fan_in), offset 0
