@@ -204,6 +204,127 @@ def vae_cpu_line_fields(seconds, threads):
                                      "5% of the 1024² FLOPs, is not scaled up)"}
 
 
+# ---- the stage before the denoise loop: prompt encoder (--stage text) -------------------------------------
+TEXT_METRIC = "prompt encoder ms/prompt (25 Mistral decoder layers, hidden 3072) at the request's text bucket"
+TEXT_LAYER_FLOPS = 2 * (3072 * 6144 + 4096 * 3072 + 3072 * 18432 + 9216 * 3072)  # GEMM FLOPs per token per layer
+TEXT_LAYER_BYTES = 2 * (6144 * 3072 + 3072 * 4096 + 18432 * 3072 + 3072 * 9216)  # BF16 weight bytes per layer
+
+
+def text_flops(bucket, layers=25):
+    """GEMMs (2 * tokens * params) + causal attention (2 * 2 * 32 heads * 128 * tokens * (tokens + 1) / 2)."""
+    return layers * (bucket * TEXT_LAYER_FLOPS + 2.0 * 2 * 32 * 128 * bucket * (bucket + 1) / 2)
+
+
+def text_cpu_sample(bucket):
+    """The oracle's layer (float64 numpy) at a bounded token count, timed on the host cores: (s per layer, tokens)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import text as ot
+    tokens = min(bucket, 64)
+    w = ot.TextLayerWeights(4321, 0)
+    f = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
+    cos, sin = ot.text_constants(f, tokens)
+    x = np.random.default_rng(0).standard_normal((tokens, 3072)) * 0.2
+    ot.layer(w, x, cos, sin)  # warm (weight widening cached)
+    t0 = time.perf_counter()
+    ot.layer(w, x, cos, sin)
+    return time.perf_counter() - t0, tokens
+
+
+def run_text_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times, tokens = [], 1
+    for i in range(args.warmup + args.steps):
+        dt, tokens = text_cpu_sample(TEXT)
+        if i >= args.warmup:
+            times.append(dt)
+    ms = 1000.0 * statistics.median(times) * 25 * (TEXT / tokens)
+    cpu = {"value": ms, "unit": "ms/prompt", "cores": os.cpu_count() or 1, "kind": "port",
+           "sample": f"one oracle layer at {tokens} tokens, x25 layers" +
+                     (f", x{TEXT / tokens:.0f} by token count" if TEXT > tokens else "")}
+    line = {"metric": TEXT_METRIC, "impl": "reference", "value": ms, "unit": "ms/prompt", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"prompt encode, {TEXT}-token bucket, 25 layers", "sample": cpu["sample"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": ms, "unit": "ms/prompt", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_text(args):
+    """One prompt encode per GPU per step (25 layers at the config's text bucket)."""
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    ctx = ec.Context(local)
+    model = ec.TextModel(ctx, 25)
+    model.synthesize(4321)
+    precision = ec.BF16 if args.precision == "bf16" else ec.FP32
+    bucket = TEXT
+    f = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
+    cos, sin, _ = ec.text_constants(f, bucket)
+    x = (np.random.default_rng(dp.request_seed(3000, rank)).standard_normal((bucket, 3072)) * 0.2).astype(np.float32)
+    bx, bc, bs, bo = ctx.to_device(x), ctx.to_device(cos), ctx.to_device(sin), ctx.buffer(x.nbytes)
+    for _ in range(args.warmup):
+        model.run_blocks_device(bx, bucket, bc, bs, bo, precision)
+    clocks = ClockSampler(local)
+    barrier(pg)
+    ctx.synchronize()
+    clocks.start()
+    ctx.record(0)
+    for _ in range(args.steps):
+        model.run_blocks_device(bx, bucket, bc, bs, bo, precision)
+    ctx.record(1)
+    ctx.synchronize()
+    clock_info = clocks.stop()
+    barrier(pg)
+    ms = max_over_ranks(pg, ctx.elapsed(0, 1)) / args.steps
+    flops = text_flops(bucket)
+    bf16_peak, _, hbm_peak, peak_kind = peaks()
+    weight_gbs = 25 * TEXT_LAYER_BYTES / (ms * 1e-3) / 1e9
+    tflops = flops / (ms * 1e-3) / 1e12
+    bound = "hbm" if bucket <= 256 else "tensor"
+    roofline = ({"bound": "hbm", "kernel": "whole encode (weight streaming)", "achieved": weight_gbs, "peak": hbm_peak,
+                 "unit": "GB/s", "frac": weight_gbs / hbm_peak, "peak_kind": peak_kind, "traffic": None}
+                if bound == "hbm" else
+                {"bound": "tensor", "kernel": "whole encode", "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s",
+                 "frac": tflops / bf16_peak, "peak_kind": peak_kind, "traffic": None})
+    e2e = None
+    if not args.no_e2e:
+        model.run_blocks(x, cos, sin, precision)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            out = model.run_blocks(x, cos, sin, precision)
+        dt = max_over_ranks(pg, (time.perf_counter() - t0) / args.steps)
+        assert np.isfinite(out).all()
+        e2e = {"value": 1000.0 * dt, "unit": "ms/prompt", "h2d_bytes_per_step": x.nbytes + cos.nbytes + sin.nbytes,
+               "d2h_bytes_per_step": out.nbytes,
+               "call": "ernie_cuda_text_run_blocks (host embedded prompt and constants in, host hidden state out)"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        layer_s, tokens = text_cpu_sample(bucket)
+        est = layer_s * 25 * (bucket / tokens)
+        cpu = {"value": 1000.0 * est, "unit": "ms/prompt", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"one oracle layer at {tokens} tokens ({layer_s:.2f} s), x25 layers"
+                         + (f", x{bucket / tokens:.0f} by token count" if bucket > tokens else "")}
+    if rank == 0:
+        line = {"metric": TEXT_METRIC, "value": ms, "unit": "ms/prompt", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+                "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+                "config": {"workload": f"prompt encode, {bucket}-token bucket, 25 layers, one prompt per GPU",
+                           "tokens": bucket, "tflops": tflops, "weight_stream_gbs": weight_gbs,
+                           "l2": "inputs larger than L2 (5.65 GB of weights per encode)"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 8 * 25 * args.steps,
+                "clocks": clock_info}
+        print(json.dumps(line), flush=True)
+    for b in (bx, bc, bs, bo):
+        b.free()
+    model.close()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+
+
 def run_vae_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -341,8 +462,9 @@ def main():
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--stage", choices=["dit", "vae"], default="dit",
-                    help="dit: the denoise loop (the metric); vae: the VAE decode after it")
+    ap.add_argument("--stage", choices=["dit", "vae", "text"], default="dit",
+                    help="dit: the denoise loop (the metric); vae: the VAE decode after it; text: the prompt "
+                         "encoder before it (at the config's text bucket)")
     ap.add_argument("--vae-latent", default=None,
                     help="profiling aid: H,W of the unpacked latent of --stage vae (default 128,128: 1024x1024)")
     args = ap.parse_args()
@@ -355,6 +477,8 @@ def main():
         args.warmup = 3
     if args.stage == "vae":
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
+    if args.stage == "text":
+        return run_text_reference(args) if args.impl == "reference" else run_text(args)
     if args.impl == "reference":
         return run_reference(args)
 

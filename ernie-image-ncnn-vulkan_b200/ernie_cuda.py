@@ -124,6 +124,13 @@ SIGNATURES = {
     "ernie_cuda_text_constants": (I, [P, I, P, P, P]),
     "ernie_cuda_text_run_blocks": (I, [P, P, I, P, P, I, I, P]),
     "ernie_cuda_text_run_blocks_device": (I, [P, P, I, P, P, I, I, P]),
+    "ernie_cuda_text_embeddings": (I, [ctypes.c_char_p, P, I, I, P]),
+    "ernie_cuda_model_load_safetensors": (I, [P, I, ctypes.POINTER(ctypes.c_char_p), I, I]),
+    "ernie_cuda_text_model_load_safetensors": (I, [P, I, ctypes.POINTER(ctypes.c_char_p), I]),
+    "ernie_cuda_vae_load_safetensors": (I, [P, ctypes.POINTER(ctypes.c_char_p), I]),
+    "ernie_cuda_safetensors_count": (I, [ctypes.c_char_p, ctypes.POINTER(I)]),
+    "ernie_cuda_safetensors_entry": (I, [ctypes.c_char_p, I, ctypes.c_char_p, SZ, ctypes.c_char_p,
+                                         ctypes.POINTER(I64), ctypes.POINTER(I)]),
     "ernie_cuda_vae_create": (I, [P, ctypes.POINTER(P)]),
     "ernie_cuda_vae_destroy": (I, [P]),
     "ernie_cuda_vae_tensor_count": (I, [ctypes.POINTER(I)]),
@@ -414,6 +421,12 @@ class Model:
     def synthesize(self, seed):
         check(lib().ernie_cuda_model_synthesize(self.handle, seed))
 
+    def load_safetensors(self, files, num_blocks=None, heads=True):
+        """Official checkpoint tensors (layers.{b}.*, and the heads) from one or more safetensors files."""
+        arr, n = _paths(files)
+        check(lib().ernie_cuda_model_load_safetensors(self.handle, self.num_blocks if num_blocks is None else num_blocks,
+                                                      arr, n, 1 if heads else 0))
+
     def upload_block(self, block, mats, gammas):
         """mats: dict name -> uint16 arrays (wq, wk, wv, wo, wup, wgate, wfc2); gammas: gamma_sa, gamma_mlp,
         gamma_q, gamma_k float32 arrays."""
@@ -436,6 +449,33 @@ class Model:
         b = U64(0)
         check(lib().ernie_cuda_model_bytes(self.handle, ctypes.byref(b)))
         return b.value
+
+
+def _paths(files):
+    files = [files] if isinstance(files, (str, bytes, os.PathLike)) else list(files)
+    arr = (ctypes.c_char_p * len(files))(*[os.fsencode(f) for f in files])
+    return arr, len(files)
+
+
+def safetensors_entries(path):
+    """[(name, dtype, shape)] of one safetensors file, in name order."""
+    n = I(0)
+    check(lib().ernie_cuda_safetensors_count(os.fsencode(path), ctypes.byref(n)))
+    out = []
+    for i in range(n.value):
+        name, dtype = ctypes.create_string_buffer(512), ctypes.create_string_buffer(8)
+        dims, nd = (I64 * 8)(), I(0)
+        check(lib().ernie_cuda_safetensors_entry(os.fsencode(path), i, name, 512, dtype, dims, ctypes.byref(nd)))
+        out.append((name.value.decode(), dtype.value.decode(), tuple(dims[j] for j in range(nd.value))))
+    return out
+
+
+def text_embeddings(path, ids, bucket):
+    """text_embeddings: rows of the [131072][3072] BF16 table (raw file or checkpoint) -> [bucket][3072] FP32."""
+    ids = np.ascontiguousarray(ids, np.uint32)
+    out = np.empty((bucket, 3072), np.float32)
+    check(lib().ernie_cuda_text_embeddings(os.fsencode(path), ptr(ids), ids.size, bucket, ptr(out)))
+    return out
 
 
 def text_constants(inv_freq, bucket, mask=False):
@@ -464,6 +504,11 @@ class TextModel:
 
     def synthesize(self, seed):
         check(lib().ernie_cuda_text_model_synthesize(self.handle, seed))
+
+    def load_safetensors(self, files, num_layers=None):
+        """Official checkpoint tensors (language_model.model.layers.{l}.*) from one or more safetensors files."""
+        arr, n = _paths(files)
+        check(lib().ernie_cuda_text_model_load_safetensors(self.handle, num_layers or self.num_layers, arr, n))
 
     def upload_layer(self, layer, tensors):
         """tensors: wq, wk, wv, wo, wgate, wup, wdown as uint16 BF16 bits; gamma_attn, gamma_mlp float32."""
@@ -518,6 +563,11 @@ class Vae:
 
     def synthesize(self, seed, bf16_weights=False):
         check(lib().ernie_cuda_vae_synthesize(self.handle, seed, 1 if bf16_weights else 0))
+
+    def load_safetensors(self, files):
+        """The official VAE checkpoint's post_quant_conv.* and decoder.* tensors."""
+        arr, n = _paths(files)
+        check(lib().ernie_cuda_vae_load_safetensors(self.handle, arr, n))
 
     def upload(self, name, array):
         a = np.ascontiguousarray(array, dtype=np.float32)

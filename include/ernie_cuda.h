@@ -47,6 +47,8 @@ extern "C" {
 typedef struct ernie_cuda_context ernie_cuda_context;
 typedef struct ernie_cuda_model ernie_cuda_model;
 typedef struct ernie_cuda_session ernie_cuda_session;
+typedef struct ernie_cuda_text_model ernie_cuda_text_model; /* prompt encoder layers (Text encoder section) */
+typedef struct ernie_cuda_vae ernie_cuda_vae;               /* VAE decoder (VAE decoder section) */
 
 /* Host weights of one block, as tools/build_dit_weights.py:19-31 binds them to the block graph. */
 typedef struct
@@ -204,7 +206,6 @@ int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out);
    mask text_constants builds. Output: the hidden state [bucket][3072] after `layers` layers (1..num_layers).
    precision: BF16 (BF16 GEMM operands, FP32 accumulation, residual, norms and attention) or FP32
    (three-plane FP32-exact GEMMs against the exact-BF16 weights; FP32 attention with FP64 sums). */
-typedef struct ernie_cuda_text_model ernie_cuda_text_model;
 /* One layer's weights as the official checkpoint stores them (language_model.model.layers.N.*). */
 typedef struct
 {
@@ -233,6 +234,37 @@ int ernie_cuda_text_run_blocks(ernie_cuda_text_model *model, const float *input,
 int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *model, const float *input, int bucket,
                                       const float *cos_t, const float *sin_t, int precision, int layers, float *out);
 
+/* Prompt-token embeddings (text_embeddings, src/text_encoder.cpp:48-75): rows ids[0..count) of the
+   [131072][3072] table into out [bucket][3072] FP32 (rows past count zero). `path` is the reference's raw
+   BF16 table ("text/embeddings.bf16") or a checkpoint .safetensors holding
+   language_model.model.embed_tokens.weight. Only the requested rows are read. */
+int ernie_cuda_text_embeddings(const char *path, const uint32_t *ids, int count, int bucket, float *out);
+
+/* ---- Official checkpoints (safetensors, BF16) ------------------------------------------------------
+   Read the official tensors straight into the resident models, in place of the reference's packaging
+   tools (tools/build_dit_weights.py, tools/build_text_weights.py, tools/export_vae.py). A checkpoint may be
+   sharded over several files; each tensor is taken from the file that holds it. GEMM weights must be BF16
+   (loaded losslessly); norm weights and biases may be BF16, F16 or F32. Shapes are checked (a 1x1
+   convolution's trailing unit dimensions match a linear weight), non-finite values rejected.
+     DiT:  layers.{b}.{self_attention.to_q/to_k/to_v/to_out.0, mlp.up_proj/gate_proj/linear_fc2}.weight,
+           layers.{b}.{adaLN_sa_ln, adaLN_mlp_ln, self_attention.norm_q, self_attention.norm_k}.weight
+           for b < num_blocks (tools/build_dit_weights.py:19-31); with_heads: x_embedder.proj, text_proj,
+           time_embedding.linear_1/linear_2, adaLN_modulation.1, final_norm.linear, final_linear
+           (tools/export_dit_heads.py:19).
+     Text: language_model.model.layers.{l}.{self_attn.q/k/v/o_proj, mlp.gate/up/down_proj,
+           input_layernorm, post_attention_layernorm}.weight for l < num_layers.
+     VAE:  every name of ernie_cuda_vae_tensor_info (post_quant_conv.*, decoder.*). */
+int ernie_cuda_model_load_safetensors(ernie_cuda_model *model, int num_blocks, const char *const *files, int count,
+                                      int with_heads);
+int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *model, int num_layers, const char *const *files,
+                                           int count);
+int ernie_cuda_vae_load_safetensors(ernie_cuda_vae *vae, const char *const *files, int count);
+/* The header of one file: the number of tensors, and tensor `index` (in name order): name, dtype
+   ("BF16", "F16", "F32", ...; 8 bytes), shape (up to 8 dims). */
+int ernie_cuda_safetensors_count(const char *path, int *count);
+int ernie_cuda_safetensors_entry(const char *path, int index, char *name, size_t name_bytes, char *dtype,
+                                 int64_t *dims, int *ndim);
+
 /* ---- VAE decoder (the stage after the denoise loop) -----------------------------------------------
    decode_vae (src/vae.h:16-22, src/vae.cpp:18-66) of the pinned AutoencoderKLFlux2 post_quant_conv +
    decoder, and rgb_image (src/pipeline.cpp:145-163), on one B200. Weights are addressed by their
@@ -245,7 +277,6 @@ int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *model, const float 
    unspecified. 1 <= width, height <= 256 with width * height <= 57344 (the mid-block attention row).
    precision: ERNIE_PRECISION_BF16 (BF16 convolution operands, FP32 accumulation and residuals) or
    ERNIE_PRECISION_FP32 (three-plane FP32-exact operands; the reference's FP32 CPU path is the gate). */
-typedef struct ernie_cuda_vae ernie_cuda_vae;
 int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **out);
 int ernie_cuda_vae_destroy(ernie_cuda_vae *vae);
 int ernie_cuda_vae_tensor_count(int *count);

@@ -15,6 +15,29 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA library through its C ABI)")
 
 
+def write_safetensors(path, tensors, metadata=None):
+    """Writes {name: (dtype, array)} as a safetensors file (dtype "BF16" takes uint16 bits, "F32" float32,
+    "F16" float16); tensors are laid out in name order."""
+    import json
+    import struct
+    header, blobs, offset = {}, [], 0
+    for name in sorted(tensors):
+        dtype, array = tensors[name]
+        raw = np.ascontiguousarray(array).tobytes()
+        header[name] = {"dtype": dtype, "shape": list(np.shape(array)), "data_offsets": [offset, offset + len(raw)]}
+        blobs.append(raw)
+        offset += len(raw)
+    if metadata:
+        header["__metadata__"] = metadata
+    text = json.dumps(header).encode()
+    text += b" " * (-len(text) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(text)))
+        f.write(text)
+        for raw in blobs:
+            f.write(raw)
+
+
 def gate(reference, actual, atol, rtol, nrmse):
     """Reference gate (tools/validate_dit_block.py:113-120): max|d| <= atol + rtol*max|ref| and
     ||d||_2 / ||ref||_2 <= nrmse. Returns (passed, metrics)."""

@@ -1,7 +1,7 @@
 """Prompt encoder on a B200 (run_text_blocks, src/text_encoder.cpp:101-160) against the CPU oracle
 (oracle/text.py) on seeded synthetic weights.
 
-Gates (atol, rtol, nrmse): the reference's text-block fixture gates (tools/export_text_block.py:88-90:
+Gates (atol, rtol, nrmse): the reference's text-block fixture gates (tools/export_text_block.py:89-91:
 fp32 {2e-4, 2e-4, 2e-5}, fp16 {0.03, 0.03, 0.02}) for one and two layers, and the per-tensor pipeline
 gates (tools/validate_pipeline.py:218-222) for the full 25-layer stack.
 """
