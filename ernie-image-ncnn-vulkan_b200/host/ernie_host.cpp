@@ -1084,4 +1084,119 @@ VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor
     result.seconds = seconds_since(begin);
     return result;
 }
+
+// ---- the prompt encoder -----------------------------------------------------------------------------
+namespace
+{
+std::vector<const char *> c_paths(const std::vector<std::string> &files)
+{
+    require(!files.empty(), "No safetensors files");
+    std::vector<const char *> out;
+    for (const auto &f : files) out.push_back(f.c_str());
+    return out;
+}
+
+void check_request(int rc, const char *action)
+{
+    if (rc == ERNIE_CUDA_ERROR) throw std::invalid_argument(std::string(action) + ": " + ernie_cuda_last_error());
+    check_cuda(rc, action);
+}
+} // namespace
+
+Tensor text_embeddings(const std::string &path, const std::vector<uint32_t> &ids, int bucket)
+{
+    require(bucket >= 1 && bucket <= 2048, "Text bucket must be in [1,2048]");
+    require(!ids.empty() && ids.size() <= size_t(bucket), "Invalid token IDs or BF16 embedding table size");
+    Tensor out(3072, bucket);
+    check_request(ernie_cuda_text_embeddings(path.c_str(), ids.data(), static_cast<int>(ids.size()), bucket, out.ptr()),
+                  "text embeddings");
+    return out;
+}
+
+std::vector<Tensor> text_constants(const std::vector<float> &inverse_frequencies, int bucket)
+{
+    require(inverse_frequencies.size() == 64, "Invalid YaRN frequency table size");
+    require(bucket >= 1 && bucket <= 2048, "Text bucket must be in [1,2048]");
+    Tensor cos(128, bucket), sin(128, bucket), mask(bucket, bucket);
+    check_request(ernie_cuda_text_constants(inverse_frequencies.data(), bucket, cos.ptr(), sin.ptr(), mask.ptr()),
+                  "text constants");
+    return {cos, sin, mask};
+}
+
+std::vector<Tensor> text_constants(const std::string &inverse_frequency_path, int bucket)
+{
+    std::ifstream file(inverse_frequency_path, std::ios::binary);
+    file.seekg(0, std::ios::end);
+    require(file && file.tellg() == std::streampos(64 * 4), "Invalid YaRN frequency table size");
+    std::vector<float> f(64);
+    file.seekg(0);
+    if (!file.read(reinterpret_cast<char *>(f.data()), 64 * 4)) throw std::runtime_error("Cannot read YaRN frequencies");
+    return text_constants(f, bucket);
+}
+
+TextModel::TextModel(GpuContext &ctx, int num_layers) : ctx_(ctx), num_layers_(num_layers)
+{
+    require(ctx.available(), "Text encoder needs a CUDA device");
+    check_request(ernie_cuda_text_model_create(ctx.handle(), num_layers, &handle_), "create text encoder");
+}
+
+TextModel::~TextModel()
+{
+    if (handle_) ernie_cuda_text_model_destroy(handle_);
+}
+
+void TextModel::synthesize(uint64_t seed)
+{
+    check_cuda(ernie_cuda_text_model_synthesize(handle_, seed), "synthesize text encoder");
+}
+
+void TextModel::load_safetensors(const std::vector<std::string> &files)
+{
+    const auto paths = c_paths(files);
+    check_request(ernie_cuda_text_model_load_safetensors(handle_, num_layers_, paths.data(), static_cast<int>(paths.size())),
+                  "load text encoder checkpoint");
+}
+
+Tensor run_text_blocks(TextModel &model, const Tensor &input, const std::vector<Tensor> &constants, Precision precision,
+                       BlockSequenceStats &stats, int layers)
+{
+    require(constants.size() == 3, "Text path requires 1..25 blocks and cos/sin/causal mask");
+    const int bucket = input.h;
+    require(input.dims == 2 && input.w == 3072 && bucket >= 1 && bucket <= 2048, "Expected a [bucket][3072] FP32 prompt");
+    require(constants[0].w == 128 && constants[0].h == bucket && constants[1].w == 128 && constants[1].h == bucket,
+            "Text constants have wrong layout");
+    const Tensor &mask = constants[2];
+    require(mask.w == bucket && mask.h == bucket, "Text constants have wrong layout");
+    for (int t = 0; t < bucket; ++t)
+        for (int k = 0; k < bucket; ++k)
+        {
+            const float m = mask[size_t(t) * bucket + k];
+            require(k > t ? m <= -1e30f : m == 0.f, "Only the causal text mask is supported");
+        }
+    stats = {};
+    stats.peak_loaded_nets = 1;
+    const auto begin = Clock::now();
+    Tensor out(3072, bucket);
+    check_request(ernie_cuda_text_run_blocks(model.handle(), input.ptr(), bucket, constants[0].ptr(), constants[1].ptr(),
+                                             precision_code(precision), layers > 0 ? layers : model.num_layers(), out.ptr()),
+                  "text blocks");
+    stats.compute_seconds.push_back(seconds_since(begin));
+    stats.compute_submissions = 1;
+    return out;
+}
+
+void load_safetensors(DitModel &model, const std::vector<std::string> &files, bool heads)
+{
+    const auto paths = c_paths(files);
+    check_request(ernie_cuda_model_load_safetensors(model.handle(), model.num_blocks(), paths.data(),
+                                                    static_cast<int>(paths.size()), heads ? 1 : 0),
+                  "load DiT checkpoint");
+}
+
+void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files)
+{
+    const auto paths = c_paths(files);
+    check_request(ernie_cuda_vae_load_safetensors(vae.handle(), paths.data(), static_cast<int>(paths.size())),
+                  "load VAE checkpoint");
+}
 } // namespace ernie

@@ -465,6 +465,7 @@ class VaeDecoder
     // rgb_image does
     DeviceTensor decode(const DeviceTensor &unpacked, Precision precision, RgbImage *image = nullptr);
     GpuContext &context() const { return ctx_; }
+    ernie_cuda_vae *handle() const noexcept { return handle_; }
 
   private:
     GpuContext &ctx_;
@@ -482,4 +483,43 @@ struct VaeStageResult
 // decoded.f32 (refusing to overwrite, as write_tensor does).
 VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor &mean, const Tensor &variance,
                              Precision precision = Precision::BF16, const std::string &trace = {});
+
+// ---- the prompt encoder (src/text_encoder.h:8-26) ------------------------------------------------
+// text_embeddings: the rows of ids from the [131072][3072] BF16 table (the reference's raw
+// "text/embeddings.bf16" file, or a checkpoint .safetensors with language_model.model.embed_tokens.weight)
+// as [bucket][3072] FP32, rows past the prompt zero. std::invalid_argument for a bucket outside [1,2048],
+// no ids, more ids than the bucket, an id outside the vocabulary or a table of the wrong size.
+Tensor text_embeddings(const std::string &path, const std::vector<uint32_t> &ids, int bucket);
+// text_constants: {cos, sin, causal mask} for a bucket from the 64 YaRN inverse frequencies (the values, or
+// the reference's 256-byte "text/rope-inv-freq.f32" file).
+std::vector<Tensor> text_constants(const std::vector<float> &inverse_frequencies, int bucket);
+std::vector<Tensor> text_constants(const std::string &inverse_frequency_path, int bucket);
+// The Mistral decoder layers of the prompt encoder, resident on the device.
+class TextModel
+{
+  public:
+    TextModel(GpuContext &ctx, int num_layers = 25);
+    ~TextModel();
+    TextModel(const TextModel &) = delete;
+    TextModel &operator=(const TextModel &) = delete;
+    void synthesize(uint64_t seed);
+    // language_model.model.layers.{0..num_layers-1}.* from the official (possibly sharded) safetensors
+    void load_safetensors(const std::vector<std::string> &files);
+    int num_layers() const noexcept { return num_layers_; }
+    ernie_cuda_text_model *handle() const noexcept { return handle_; }
+
+  private:
+    GpuContext &ctx_;
+    ernie_cuda_text_model *handle_ = nullptr;
+    int num_layers_ = 0;
+};
+// run_text_blocks (src/text_encoder.h:17-19): `layers` (default all) layers over the embedded prompt with
+// the constants {cos, sin, mask} of text_constants (the mask must be its causal mask). stats gets one
+// compute time for the whole sequence of layers (the layers stay resident: no per-block load).
+Tensor run_text_blocks(TextModel &model, const Tensor &input, const std::vector<Tensor> &constants,
+                       Precision precision, BlockSequenceStats &stats, int layers = 0);
+
+// ---- official checkpoints (safetensors) ------------------------------------------------------------
+void load_safetensors(DitModel &model, const std::vector<std::string> &files, bool heads = true);
+void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files);
 } // namespace ernie

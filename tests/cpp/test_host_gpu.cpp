@@ -220,6 +220,42 @@ int main()
         std::cerr << "VAE exception: " << e.what() << "\n";
         return 1;
     }
+    // the prompt encoder: run_text_blocks with text_constants; the causal mask is required
+    try
+    {
+        GpuContext ctx(true, 0);
+        TextModel text(ctx, 2);
+        text.synthesize(3);
+        std::vector<float> f(64);
+        for (int j = 0; j < 64; ++j) f[size_t(j)] = 1.f / std::pow(1000000.f, float(j) / 64.f);
+        const int bucket = 12;
+        auto k = text_constants(f, bucket);
+        Tensor x = normal(3072, bucket, 1, ERNIE_SYNTH_TEXT);
+        BlockSequenceStats stats;
+        const Tensor y = run_text_blocks(text, x, k, Precision::BF16, stats);
+        REQUIRE(y.w == 3072 && y.h == bucket && stats.compute_seconds.size() == 1, "text output shape");
+        bool finite = true;
+        for (size_t i = 0; i < y.total(); ++i) finite = finite && std::isfinite(y[i]);
+        REQUIRE(finite, "text output finite");
+        const Tensor one = run_text_blocks(text, x, k, Precision::BF16, stats, 1);
+        REQUIRE(one.data != y.data, "layer count ignored");
+        k[2][5] = 0.f; // a key above the diagonal unmasked
+        bool threw = false;
+        try
+        {
+            run_text_blocks(text, x, k, Precision::BF16, stats);
+        }
+        catch (const std::invalid_argument &)
+        {
+            threw = true;
+        }
+        REQUIRE(threw, "non-causal text mask accepted");
+    }
+    catch (const std::exception &e)
+    {
+        std::cerr << "text exception: " << e.what() << "\n";
+        return 1;
+    }
     if (failures) return 1;
     std::cout << "host GPU contracts passed\n";
     return 0;

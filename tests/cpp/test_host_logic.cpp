@@ -446,10 +446,30 @@ static void vae_contract()
     REQUIRE(params == 49620259, "VAE parameter count " << params);
 }
 
+// text_constants and text_embeddings (src/text_encoder.cpp:48-100) without a device
+static void text_contract()
+{
+    std::vector<float> f(64);
+    for (int j = 0; j < 64; ++j) f[size_t(j)] = 1.f / std::pow(1000000.f, float(j) / 64.f);
+    const auto k = text_constants(f, 5);
+    REQUIRE(k.size() == 3 && k[0].w == 128 && k[0].h == 5 && k[2].w == 5 && k[2].h == 5, "text constant shapes");
+    REQUIRE(k[0][128 * 3 + 7] == std::cos(3.f * f[7]) && k[0][128 * 3 + 71] == k[0][128 * 3 + 7], "cos row");
+    REQUIRE(k[1][128 * 4 + 63] == std::sin(4.f * f[63]), "sin row");
+    REQUIRE(k[2][1 * 5 + 1] == 0.f && k[2][1 * 5 + 2] == -std::numeric_limits<float>::max(), "causal mask");
+    REQUIRE(throws<std::invalid_argument>([&] { text_constants(f, 2049); }), "bucket 2049 accepted");
+    f[3] = -1.f;
+    REQUIRE(throws<std::invalid_argument>([&] { text_constants(f, 4); }), "negative frequency accepted");
+    REQUIRE(throws<std::invalid_argument>([&] { text_embeddings("/nonexistent/embeddings.bf16", {1, 2}, 4); }),
+            "missing table accepted");
+    REQUIRE(throws<std::invalid_argument>([&] { text_embeddings("/nonexistent/embeddings.bf16", {1, 2, 3}, 2); }),
+            "more ids than the bucket accepted");
+}
+
 int main()
 {
     latent_contract();
     vae_contract();
+    text_contract();
     conditioning_contract();
     error_mapping();
     placement_contract();
