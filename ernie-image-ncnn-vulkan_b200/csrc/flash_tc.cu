@@ -1,7 +1,8 @@
 // tcgen05 flash attention for the ERNIE DiT block (BF16 mode).
 //
 // Replaces sdpa_22 (block.ncnn.param:58; ErnieSDPA / AccurateSDPA, src/ernie_attention.cpp:35-233):
-// softmax(Q K^T / sqrt(128) + mask_row) V per head over the joint image+text sequence, non-causal,
+// softmax(Q K^T / sqrt(128) + mask_row) V per head over the joint image+text sequence, non-causal
+// (the prompt encoder's causal grouped-query attention uses the same kernel with `causal` and `kv_group`),
 // keys past the valid count (the -1e30 text padding of src/conditioning.cpp:41-42) skipped.
 //
 // One CTA = one head x 256 queries as two 128-row query tiles A and B that share every K / V^T tile;
@@ -60,6 +61,8 @@ struct FlashArgs
     const float *mask;
     FlashOutput out;
     int *error_flag;
+    int causal = 0;   // key j > query i excluded; key tiles past the CTA's last query skipped
+    int kv_group = 1; // query heads per K/V head (grouped-query attention)
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -106,9 +109,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_done = bars + 8u * 15;
     const uint32_t slot = bars + 8u * 16;
 
-    const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta;
+    const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta, kv_head = head / a.kv_group;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int tiles = (a.kv_len + kTile - 1) / kTile;
+    const int kv_tiles = (a.kv_len + kTile - 1) / kTile;
+    // causal: no key past this CTA's last query row
+    const int q_end = min(a.rows, q0 + kRowsPerCta);
+    const int tiles = a.causal ? min(kv_tiles, (q_end + kTile - 1) / kTile) : kv_tiles;
     // the second query tile of the last CTA of a head may hold no row at all: then only tile A runs
     const int groups = q0 + kTile < a.rows ? 2 : 1;
 
@@ -163,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < tiles; ++j)
             {
                 const int s = j & 1;
-                const int row_k = head * a.rows_pad + j * kTile;
+                const int row_k = kv_head * a.rows_pad + j * kTile;
                 if (!mbar_wait(k_empty(s), ((j >> 1) & 1) ^ 1u))
                 {
                     if (a.error_flag) atomicExch(a.error_flag, kErrFlashProducerTimeout);
@@ -184,8 +190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(v_full, kTileBytes);
-                tma_load_2d(s_v, &map_vt, v_full, j * kTile, head * kTile);
-                tma_load_2d(s_v + kHalfBytes, &map_vt, v_full, j * kTile + 64, head * kTile);
+                tma_load_2d(s_v, &map_vt, v_full, j * kTile, kv_head * kTile);
+                tma_load_2d(s_v + kHalfBytes, &map_vt, v_full, j * kTile + 64, kv_head * kTile);
             }
         }
         else if (warp == 1)
@@ -316,6 +322,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int k = 0; k < 128; ++k)
                     if (key0 + k >= a.kv_len) x[k] = -INFINITY;
+            }
+            if (a.causal)
+            {
+                // key0 + k visible iff k <= lim; key tile 0 holds a visible key for every row, so the running
+                // max is finite before any fully masked tile
+                const int lim = q0 + g * kTile + r - key0;
+                if (lim < kTile - 1)
+                {
+#pragma unroll
+                    for (int k = 0; k < 128; ++k)
+                        if (k > lim) x[k] = -INFINITY;
+                }
             }
             // row max over 8 independent chains
             float mx[8];
@@ -467,19 +485,23 @@ int prepare_flash_kernels()
 
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
                     int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
-                    cudaStream_t stream)
+                    cudaStream_t stream, int causal, int kv_heads)
 {
+    if (kv_heads == 0) kv_heads = heads;
     if (rows < 1 || kv_len < 1 || kv_len > rows_pad || rows_pad % kTile || rows > rows_pad || heads < 1 ||
-        out.rows_per_dest < 1 || out.ld % 8 || out.col_offset % 8 || out.col_offset + heads * kTile > out.ld)
+        kv_heads < 1 || heads % kv_heads || out.rows_per_dest < 1 || out.ld % 8 || out.col_offset % 8 ||
+        out.col_offset + heads * kTile > out.ld)
         return cudaErrorInvalidValue;
     for (int d = 0; d < (rows + out.rows_per_dest - 1) / out.rows_per_dest; ++d)
         if (d >= kMaxDest || !out.dst[d]) return cudaErrorInvalidValue;
     CUtensorMap mq, mk, mv;
     if (!map_2d(&mq, q, static_cast<uint64_t>(heads) * rows_pad, kTile) ||
-        !map_2d(&mk, k, static_cast<uint64_t>(heads) * rows_pad, kTile) ||
-        !map_2d(&mv, vt, static_cast<uint64_t>(heads) * kTile, static_cast<uint64_t>(rows_pad)))
+        !map_2d(&mk, k, static_cast<uint64_t>(kv_heads) * rows_pad, kTile) ||
+        !map_2d(&mv, vt, static_cast<uint64_t>(kv_heads) * kTile, static_cast<uint64_t>(rows_pad)))
         return cudaErrorInvalidValue;
     FlashArgs a{rows, rows_pad, kv_len, mask, out, error_flag};
+    a.causal = causal ? 1 : 0;
+    a.kv_group = heads / kv_heads;
     const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, heads);
     flash_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
     return cudaGetLastError();

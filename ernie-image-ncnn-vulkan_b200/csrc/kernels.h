@@ -96,9 +96,11 @@ struct FlashOutput
     __nv_bfloat16 *dst[kMaxDest] = {};
     int rows_per_dest = 0, ld = 0, col_offset = 0;
 };
+// causal: key j > query i excluded; kv_heads (0: heads) K/V heads, query head h reading K/V head
+// h / (heads / kv_heads), k [kv_heads][rows_pad][128], vt [kv_heads][128][rows_pad].
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
                     int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
-                    cudaStream_t stream);
+                    cudaStream_t stream, int causal = 0, int kv_heads = 0);
 // Barrier of a sequence-parallel group over peer memory: this GPU's arrival is stored (release, system
 // scope) into slot `rank` of every member's slots; then it waits (acquire, bounded by `timeout_ns`) until
 // every member's arrival in its own slots reaches the same epoch. Epochs count up on the device, so the
@@ -223,6 +225,10 @@ int prepare_conv_kernels();
 // qkv FP32 [tokens][6144] -> rotated head-major q [32][tokens][128], k [8][tokens][128] and v [8][tokens][128].
 int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q, float *k, float *v,
                      cudaStream_t stream);
+// The same as the BF16 operands of the tcgen05 attention: q [32][rows_pad][128], k [8][rows_pad][128],
+// v^T [8][128][rows_pad].
+int launch_text_rope_bf16(const float *qkv, const float *cos_t, const float *sin_t, int tokens, int rows_pad,
+                          __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt, cudaStream_t stream);
 
 // Synthetic weights on device (ernie_synth.h protocol). rows x cols BF16 written at `out` with a
 // destination row index map: dst_row = (row / group) * group_stride + group_offset + row % group.

@@ -40,7 +40,47 @@ __global__ void text_rope_kernel(const float *qkv, const float *cos_t, const flo
         dst[d + 64] = x[d + 64];
     }
 }
+
+// BF16 mode: the same rotation written as the tcgen05 attention's operands, q [32][rows_pad][128],
+// k [8][rows_pad][128] and v transposed [8][128][rows_pad] (rows past `tokens` left as they are: zero).
+__global__ void text_rope_bf16_kernel(const float *qkv, const float *cos_t, const float *sin_t, int tokens,
+                                      int rows_pad, __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt)
+{
+    const int head = blockIdx.y, t = blockIdx.x, d = threadIdx.x;
+    if (t >= tokens) return;
+    const float *row = qkv + static_cast<size_t>(t) * kTextQkv;
+    if (head < kTextQHeads + kTextKvHeads)
+    {
+        const float *x = row + head * kTextHeadDim;
+        const float *c = cos_t + static_cast<size_t>(t) * kTextHeadDim, *s = sin_t + static_cast<size_t>(t) * kTextHeadDim;
+        const float first = x[d], second = x[d + 64];
+        const float lo = __fsub_rn(__fmul_rn(first, c[d]), __fmul_rn(second, s[d]));
+        const float hi = __fadd_rn(__fmul_rn(second, c[d + 64]), __fmul_rn(first, s[d + 64]));
+        __nv_bfloat16 *dst = head < kTextQHeads
+                                 ? q + (static_cast<size_t>(head) * rows_pad + t) * kTextHeadDim
+                                 : k + (static_cast<size_t>(head - kTextQHeads) * rows_pad + t) * kTextHeadDim;
+        dst[d] = __float2bfloat16_rn(lo);
+        dst[d + 64] = __float2bfloat16_rn(hi);
+    }
+    else
+    {
+        const int vh = head - kTextQHeads - kTextKvHeads;
+        const float *x = row + (kTextQHeads + kTextKvHeads + vh) * kTextHeadDim;
+        __nv_bfloat16 *dst = vt + static_cast<size_t>(vh) * kTextHeadDim * rows_pad + t;
+        dst[static_cast<size_t>(d) * rows_pad] = __float2bfloat16_rn(x[d]);
+        dst[static_cast<size_t>(d + 64) * rows_pad] = __float2bfloat16_rn(x[d + 64]);
+    }
+}
 } // namespace
+
+int launch_text_rope_bf16(const float *qkv, const float *cos_t, const float *sin_t, int tokens, int rows_pad,
+                          __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt, cudaStream_t stream)
+{
+    if (tokens < 1 || rows_pad < tokens) return cudaErrorInvalidValue;
+    text_rope_bf16_kernel<<<dim3(tokens, kTextQHeads + 2 * kTextKvHeads), 64, 0, stream>>>(qkv, cos_t, sin_t, tokens,
+                                                                                          rows_pad, q, k, vt);
+    return cudaGetLastError();
+}
 
 int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q, float *k, float *v,
                      cudaStream_t stream)

@@ -4,8 +4,10 @@
 // and the constants of text_constants (src/text_encoder.cpp:77-100). Host orchestration only.
 //
 // Per layer (hidden 3072, 32 query heads and 8 K/V heads of 128, SwiGLU 9216, RMSNorm eps 1e-5):
-//   norm_modulate (RMSNorm, input_layernorm) -> tcgen05 GEMM [q; k; v] (F32 out) -> text_rope_kernel ->
-//   causal grouped-query FP32 attention -> GEMM o_proj, residual added in its epilogue (gate 1) ->
+//   norm_modulate (RMSNorm, input_layernorm) -> tcgen05 GEMM [q; k; v] (F32 out) -> rotary ->
+//   causal grouped-query attention (BF16 mode: the tcgen05 flash kernel of the DiT with its causal and
+//   grouped-K/V options; FP32-exact mode: FP32 attention with FP64 sums) -> GEMM o_proj, residual added
+//   in its epilogue (gate 1) ->
 //   RMSNorm (post_attention_layernorm) -> GEMM [up; gate] with the SwiGLU epilogue -> GEMM down_proj +
 //   residual.
 #include "capi_internal.h"
@@ -37,8 +39,10 @@ struct TextLayer
 struct TextWork
 {
     int tokens = 0, precision = -1, planes = 1;
+    int rows_pad = 0;
     float *x = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *cos_t = nullptr, *sin_t = nullptr;
     __nv_bfloat16 *a = nullptr, *h = nullptr;
+    __nv_bfloat16 *qb = nullptr, *kb = nullptr, *vtb = nullptr; // BF16 mode: the tcgen05 attention's operands
     void *alloc = nullptr;
 };
 } // namespace
@@ -71,7 +75,12 @@ int ensure_work(ernie_cuda_text_model *m, int tokens, int precision)
     w.precision = precision;
     w.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
     const size_t t = static_cast<size_t>(tokens);
+    w.rows_pad = (tokens + 127) / 128 * 128;
+    const size_t rp = static_cast<size_t>(w.rows_pad);
     Arena arena;
+    arena.add(&w.qb, rp * kTQ);
+    arena.add(&w.kb, rp * kTKV);
+    arena.add(&w.vtb, rp * kTKV);
     arena.add(&w.x, t * kTH);
     arena.add(&w.qkv, t * kTQkv);
     arena.add(&w.q, t * kTQ);
@@ -88,6 +97,10 @@ int ensure_work(ernie_cuda_text_model *m, int tokens, int precision)
         return from_cuda(e, "Allocate text encoder workspace");
     }
     w.alloc = arena.base;
+    // the attention operands' padding rows / columns stay zero (keys past the prompt are masked, and V^T's
+    // padding columns meet zero probabilities)
+    const cudaError_t z = cudaMemset(w.qb, 0, rp * (kTQ + 2 * kTKV) * 2);
+    if (z != cudaSuccess) return from_cuda(z, "Clear text encoder workspace");
     return ERNIE_CUDA_OK;
 }
 
@@ -110,6 +123,21 @@ int enqueue_layers(ernie_cuda_text_model *m, int count)
                      "text input_layernorm");
         ERNIE_LAUNCH(launch_gemm(w.a, L.wqkv, T, kTQkv, kTH, splits, block_n, Epilogue::F32Bias, f32, sms, s, fp32),
                      "text qkv projection");
+        if (!fp32)
+        {
+            // BF16 mode: the tcgen05 flash attention, causal over 8 grouped K/V heads
+            ERNIE_LAUNCH(launch_text_rope_bf16(w.qkv, w.cos_t, w.sin_t, T, w.rows_pad, w.qb, w.kb, w.vtb, s),
+                         "text rotary");
+            FlashOutput fo;
+            fo.dst[0] = w.a;
+            fo.rows_per_dest = T;
+            fo.ld = kTQ;
+            ERNIE_LAUNCH(launch_flash_tc(w.qb, w.kb, w.vtb, nullptr, T, w.rows_pad, T, 32, fo, m->ctx->error_flag, s,
+                                         1, 8),
+                         "text attention");
+        }
+        else
+        {
         ERNIE_LAUNCH(launch_text_rope(w.qkv, w.cos_t, w.sin_t, T, w.q, w.k, w.v, s), "text rotary");
         AttentionF32Args at{};
         at.q = w.q;
@@ -124,9 +152,10 @@ int enqueue_layers(ernie_cuda_text_model *m, int count)
         at.q_head_stride = static_cast<long long>(T) * 128;
         at.kv_head_stride = static_cast<long long>(T) * 128;
         at.causal = 1;
-        at.out_mode = fp32 ? 1 : 2;
+        at.out_mode = 1;
         at.out_split3 = w.a;
         ERNIE_LAUNCH(launch_attention_f32(at, s), "text attention");
+        }
         GemmEpilogueArgs res;
         res.resid = w.x;
         res.ldo = kTH; // the residual's row stride
