@@ -43,32 +43,53 @@ __global__ void text_rope_kernel(const float *qkv, const float *cos_t, const flo
 
 // BF16 mode: the same rotation written as the tcgen05 attention's operands, q [32][rows_pad][128],
 // k [8][rows_pad][128] and v transposed [8][128][rows_pad] (rows past `tokens` left as they are: zero).
+// One CTA = 32 tokens x one head, one warp per token at a time with lanes on consecutive dimensions (every
+// load and store a whole row segment). V goes through a shared-memory tile so that its transposed rows are
+// written 32 tokens at a time.
 __global__ void text_rope_bf16_kernel(const float *qkv, const float *cos_t, const float *sin_t, int tokens,
                                       int rows_pad, __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt)
 {
-    const int head = blockIdx.y, t = blockIdx.x, d = threadIdx.x;
-    if (t >= tokens) return;
-    const float *row = qkv + static_cast<size_t>(t) * kTextQkv;
-    if (head < kTextQHeads + kTextKvHeads)
+    __shared__ __nv_bfloat16 tile[kTextHeadDim][34]; // [dim][token] (+2 padding: row stride 17 banks)
+    const int head = blockIdx.y, t0 = blockIdx.x * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool rotate = head < kTextQHeads + kTextKvHeads;
+    const int col = rotate ? head * kTextHeadDim : (kTextQHeads + kTextKvHeads) * kTextHeadDim +
+                                                       (head - kTextQHeads - kTextKvHeads) * kTextHeadDim;
+    for (int tt = warp; tt < 32; tt += 4)
     {
-        const float *x = row + head * kTextHeadDim;
-        const float *c = cos_t + static_cast<size_t>(t) * kTextHeadDim, *s = sin_t + static_cast<size_t>(t) * kTextHeadDim;
-        const float first = x[d], second = x[d + 64];
-        const float lo = __fsub_rn(__fmul_rn(first, c[d]), __fmul_rn(second, s[d]));
-        const float hi = __fadd_rn(__fmul_rn(second, c[d + 64]), __fmul_rn(first, s[d + 64]));
-        __nv_bfloat16 *dst = head < kTextQHeads
-                                 ? q + (static_cast<size_t>(head) * rows_pad + t) * kTextHeadDim
-                                 : k + (static_cast<size_t>(head - kTextQHeads) * rows_pad + t) * kTextHeadDim;
-        dst[d] = __float2bfloat16_rn(lo);
-        dst[d + 64] = __float2bfloat16_rn(hi);
+        const int t = t0 + tt;
+        if (t >= tokens) break;
+        const float *x = qkv + static_cast<size_t>(t) * kTextQkv + col;
+        if (rotate)
+        {
+            const float *c = cos_t + static_cast<size_t>(t) * kTextHeadDim;
+            const float *s = sin_t + static_cast<size_t>(t) * kTextHeadDim;
+            __nv_bfloat16 *dst = head < kTextQHeads
+                                     ? q + (static_cast<size_t>(head) * rows_pad + t) * kTextHeadDim
+                                     : k + (static_cast<size_t>(head - kTextQHeads) * rows_pad + t) * kTextHeadDim;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+            {
+                const int d = lane + 32 * j;
+                const float first = x[d], second = x[d + 64];
+                dst[d] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(first, c[d]), __fmul_rn(second, s[d])));
+                dst[d + 64] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(second, c[d + 64]), __fmul_rn(first, s[d + 64])));
+            }
+        }
+        else
+        {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tile[lane + 32 * j][tt] = __float2bfloat16_rn(x[lane + 32 * j]);
+        }
     }
-    else
+    if (rotate) return; // uniform per CTA
+    __syncthreads();
+    // transposed: dimension row d holds tokens t0 .. t0 + 31 (consecutive 64 bytes)
+    const int vh = head - kTextQHeads - kTextKvHeads;
+    __nv_bfloat16 *base = vt + static_cast<size_t>(vh) * kTextHeadDim * rows_pad + t0;
+    for (int i = threadIdx.x; i < kTextHeadDim * 32; i += blockDim.x)
     {
-        const int vh = head - kTextQHeads - kTextKvHeads;
-        const float *x = row + (kTextQHeads + kTextKvHeads + vh) * kTextHeadDim;
-        __nv_bfloat16 *dst = vt + static_cast<size_t>(vh) * kTextHeadDim * rows_pad + t;
-        dst[static_cast<size_t>(d) * rows_pad] = __float2bfloat16_rn(x[d]);
-        dst[static_cast<size_t>(d + 64) * rows_pad] = __float2bfloat16_rn(x[d + 64]);
+        const int d = i >> 5, tt = i & 31;
+        if (t0 + tt < tokens) base[static_cast<size_t>(d) * rows_pad + tt] = tile[d][tt];
     }
 }
 } // namespace
@@ -77,8 +98,8 @@ int launch_text_rope_bf16(const float *qkv, const float *cos_t, const float *sin
                           __nv_bfloat16 *q, __nv_bfloat16 *k, __nv_bfloat16 *vt, cudaStream_t stream)
 {
     if (tokens < 1 || rows_pad < tokens) return cudaErrorInvalidValue;
-    text_rope_bf16_kernel<<<dim3(tokens, kTextQHeads + 2 * kTextKvHeads), 64, 0, stream>>>(qkv, cos_t, sin_t, tokens,
-                                                                                          rows_pad, q, k, vt);
+    text_rope_bf16_kernel<<<dim3((tokens + 31) / 32, kTextQHeads + 2 * kTextKvHeads), 128, 0, stream>>>(
+        qkv, cos_t, sin_t, tokens, rows_pad, q, k, vt);
     return cudaGetLastError();
 }
 

@@ -1199,4 +1199,33 @@ void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files)
     check_request(ernie_cuda_vae_load_safetensors(vae.handle(), paths.data(), static_cast<int>(paths.size())),
                   "load VAE checkpoint");
 }
+
+GeneratedImage generate_from_ids(GenerationModels &m, const std::vector<uint32_t> &ids, int text_bucket,
+                                 const DitStageRequest &request,
+                                 const std::function<void(const DitStageProgress &)> &notify)
+{
+    const auto start = Clock::now();
+    require(m.dit_text_tokens >= int(ids.size()), "Prompt longer than the DiT text slots");
+    GeneratedImage out;
+    const Tensor embedded = text_embeddings(m.embeddings, ids, text_bucket);
+    BlockSequenceStats stats;
+    const Tensor encoded =
+        run_text_blocks(m.text, embedded, text_constants(m.text_frequencies, text_bucket), request.precision, stats);
+    out.text = Tensor(3072, int(ids.size()));
+    std::copy(encoded.data.begin(), encoded.data.begin() + long(ids.size()) * 3072, out.text.data.begin());
+    out.text_seconds = seconds_since(start);
+    if (notify) notify({"text", int(ids.size()), text_bucket, out.text_seconds});
+    if (!request.trace.empty()) write_tensor((std::filesystem::path(request.trace) / "text.f32").string(), out.text);
+    const auto dit_start = Clock::now();
+    DitStageResult dit = run_dit_stage(m.dit, out.text, m.dit_text_tokens, m.dit_frequencies, request, notify);
+    out.dit_seconds = seconds_since(dit_start);
+    out.start_step = dit.start_step;
+    out.latent = std::move(dit.latent);
+    VaeStageResult vae = run_vae_stage(m.vae, out.latent, m.bn_mean, m.bn_variance, request.precision, request.trace);
+    out.vae_seconds = vae.seconds;
+    out.decoded = std::move(vae.decoded);
+    out.image = std::move(vae.image);
+    out.elapsed_seconds = seconds_since(start);
+    return out;
+}
 } // namespace ernie

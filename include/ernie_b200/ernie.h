@@ -519,6 +519,34 @@ class TextModel
 Tensor run_text_blocks(TextModel &model, const Tensor &input, const std::vector<Tensor> &constants,
                        Precision precision, BlockSequenceStats &stats, int layers = 0);
 
+// ---- generate from token ids (src/pipeline.cpp:489-575, everything after the tokenizer) -------------
+struct GenerationModels // the device-resident stages and the package's small tables
+{
+    TextModel &text;                      // layers 0..24 of the prompt encoder
+    DitModel &dit;
+    VaeDecoder &vae;
+    std::string embeddings;               // text/embeddings.bf16, or a checkpoint with embed_tokens
+    std::vector<float> text_frequencies;  // text/rope-inv-freq.f32 (64 YaRN inverse frequencies)
+    std::vector<float> dit_frequencies;   // dit/rope-inv-freq.f32 (empty: the built-in table)
+    Tensor bn_mean, bn_variance;          // vae/bn-mean.f32, vae/bn-variance.f32 ([128])
+    int dit_text_tokens = 0;              // model.cfg dit_text_tokens
+};
+struct GeneratedImage
+{
+    RgbImage image;
+    Tensor text;    // the prompt rows of the encoder's output [T][3072] (trace text.f32)
+    Tensor latent;  // [128][h][w] after the last step
+    Tensor decoded; // [3][16h][16w]
+    int start_step = 0;
+    double text_seconds = 0, dit_seconds = 0, vae_seconds = 0, elapsed_seconds = 0;
+};
+// The token ids of a prompt through the prompt encoder (at `text_bucket` slots), the DiT stage and the VAE
+// stage, with the reference's traces (text.f32, the DiT stage's files, final/unpacked/decoded.f32) when
+// request.trace names a folder, and the "text" / "denoise" progress notifications.
+GeneratedImage generate_from_ids(GenerationModels &models, const std::vector<uint32_t> &ids, int text_bucket,
+                                 const DitStageRequest &request,
+                                 const std::function<void(const DitStageProgress &)> &notify = {});
+
 // ---- official checkpoints (safetensors) ------------------------------------------------------------
 void load_safetensors(DitModel &model, const std::vector<std::string> &files, bool heads = true);
 void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files);

@@ -6,6 +6,7 @@
 #include "ernie_synth.h"
 #include <cmath>
 #include <filesystem>
+#include <fstream>
 #include <iostream>
 #include <unistd.h>
 
@@ -254,6 +255,64 @@ int main()
     catch (const std::exception &e)
     {
         std::cerr << "text exception: " << e.what() << "\n";
+        return 1;
+    }
+    // generate_from_ids: the three stages from token ids to RGB bytes, deterministic, with the traces
+    try
+    {
+        GpuContext ctx(true, 0);
+        TextModel text(ctx, 2);
+        DitModel dit(ctx, 2);
+        VaeDecoder vae(ctx);
+        text.synthesize(3);
+        dit.synthesize(11);
+        vae.synthesize(7);
+        char folder[] = "/tmp/ernie_generateXXXXXX";
+        REQUIRE(mkdtemp(folder) != nullptr, "generate folder");
+        const std::string table = std::string(folder) + "/embeddings.bf16";
+        {
+            std::ofstream f(table, std::ios::binary);
+            for (uint32_t id : {5u, 9u, 100u})
+            {
+                f.seekp(std::streamoff(id) * 3072 * 2);
+                for (int j = 0; j < 3072; ++j)
+                {
+                    const uint16_t b = ernie_synth_bf16_bits(float(0.2 * ernie_synth_normal(1, id, uint64_t(j))));
+                    f.write(reinterpret_cast<const char *>(&b), 2);
+                }
+            }
+            f.seekp(std::streamoff(131072) * 3072 * 2 - 1);
+            f.put('\0'); // sparse table of the full size
+        }
+        std::vector<float> tf(64);
+        for (int j = 0; j < 64; ++j) tf[size_t(j)] = 1.f / std::pow(1000000.f, float(j) / 64.f);
+        Tensor mean(128), variance(128);
+        for (int c = 0; c < 128; ++c) variance[size_t(c)] = 1.f;
+        GenerationModels models{text, dit, vae, table, tf, {}, mean, variance, 8};
+        DitStageRequest req;
+        req.width = 64;
+        req.height = 48;
+        req.steps = 2;
+        req.seed = 4;
+        int notified = 0;
+        const GeneratedImage a = generate_from_ids(models, {5, 9, 100}, 8, req,
+                                                   [&](const DitStageProgress &p) { notified += p.stage == "text"; });
+        const GeneratedImage b = generate_from_ids(models, {5, 9, 100}, 8, req);
+        REQUIRE(a.image.width == 64 && a.image.height == 48 && a.image.pixels.size() == 64 * 48 * 3, "image shape");
+        REQUIRE(a.image.pixels == b.image.pixels && a.latent.data == b.latent.data, "generate not deterministic");
+        REQUIRE(notified == 1 && a.text.h == 3 && a.text.w == 3072, "text stage");
+        const std::string trace = std::string(folder) + "/trace";
+        std::filesystem::create_directory(trace);
+        req.trace = trace;
+        const GeneratedImage t = generate_from_ids(models, {5, 9, 100}, 8, req);
+        for (const char *f : {"text.f32", "final.f32", "unpacked.f32", "decoded.f32"})
+            REQUIRE(std::filesystem::exists(std::filesystem::path(trace) / f), "missing trace " << f);
+        REQUIRE(t.image.pixels == a.image.pixels, "traced generate differs");
+        std::filesystem::remove_all(folder);
+    }
+    catch (const std::exception &e)
+    {
+        std::cerr << "generate exception: " << e.what() << "\n";
         return 1;
     }
     if (failures) return 1;
