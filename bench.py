@@ -424,6 +424,50 @@ def run_vae(args):
         pg.destroy_process_group()
 
 
+def pipeline_stages(ctx, args, ms_per_step, reps=3):
+    """Device time of the whole image on this GPU: prompt encode (25 layers at the config's text bucket),
+    8 denoise steps (the metric's ms_per_step x 8) and the VAE decode (unpacked latent 2h x 2w), BF16."""
+    import ernie_cuda as ec
+    out = {"denoise_ms": 8 * ms_per_step}
+    text = ec.TextModel(ctx, 25)
+    vae = ec.Vae(ctx)
+    bufs = []
+    try:
+        text.synthesize(4321)
+        vae.synthesize(4321)
+        f = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
+        cos, sin, _ = ec.text_constants(f, TEXT)
+        x = (np.random.default_rng(7).standard_normal((TEXT, 3072)) * 0.2).astype(np.float32)
+        bx, bc, bs, bo = ctx.to_device(x), ctx.to_device(cos), ctx.to_device(sin), ctx.buffer(x.nbytes)
+        u = np.random.default_rng(8).standard_normal((32, 2 * HEIGHT, 2 * WIDTH)).astype(np.float32)
+        bu, bd = ctx.to_device(u), ctx.buffer(3 * 64 * u[0].size * 4)
+        bufs = [bx, bc, bs, bo, bu, bd]
+        for _ in range(2):
+            text.run_blocks_device(bx, TEXT, bc, bs, bo, ec.BF16)
+            vae.decode_device(bu, 2 * WIDTH, 2 * HEIGHT, bd, ec.BF16)
+        ctx.synchronize()
+        ctx.record(0)
+        for _ in range(reps):
+            text.run_blocks_device(bx, TEXT, bc, bs, bo, ec.BF16)
+        ctx.record(1)
+        for _ in range(reps):
+            vae.decode_device(bu, 2 * WIDTH, 2 * HEIGHT, bd, ec.BF16)
+        ctx.record(2)
+        ctx.synchronize()
+        out["text_encode_ms"] = ctx.elapsed(0, 1) / reps
+        out["vae_decode_ms"] = ctx.elapsed(1, 2) / reps
+        out["image_ms"] = out["text_encode_ms"] + out["denoise_ms"] + out["vae_decode_ms"]
+        out["images_per_s_per_gpu"] = 1000.0 / out["image_ms"]
+        out["note"] = ("text encoder + 8 DiT steps + VAE decode of one image on one GPU, BF16, device time; the "
+                       "tokenizer is out of scope")
+    finally:
+        for b in bufs:
+            b.free()
+        text.close()
+        vae.close()
+    return out
+
+
 def run_kernel_only(args):
     """Set up the C2 session (with --blocks resident blocks) and launch one block kernel `iters` times.
     Used under ncu on a small case: a 2-block model keeps the device footprint near 1.6 GB while every
@@ -459,6 +503,7 @@ def main():
     ap.add_argument("--blocks", type=int, default=NUM_BLOCKS, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-stages", action="store_true", help="skip the prompt-encode and VAE stage timings")
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
@@ -591,6 +636,12 @@ def main():
                "call": "ernie_cuda_session_set_conditioning + ernie_cuda_session_denoise (8 steps, host buffers) "
                        "per image; bytes per step = per-image bytes / 8"}
 
+    # the other stages of the same image (not part of the metric): prompt encode before the loop and VAE
+    # decode after it, device-timed on this GPU
+    stages = None
+    if not args.no_stages and not sp:
+        stages = pipeline_stages(ctx, args, ms_per_step)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         block_s, cores = cpu_baseline_block()
@@ -610,7 +661,7 @@ def main():
                            "parallelism": f"sp{world}" if sp else f"dp{world}", "rows_per_gpu": T,
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
-                           "kernel_ms": prof, "kernel_ms_in_block": in_block},
+                           "kernel_ms": prof, "kernel_ms_in_block": in_block, "pipeline_stages": stages},
                 "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": bf16_peak,
                              "unit": "TFLOP/s", "frac": achieved / bf16_peak, "peak_kind": peak_kind,
                              "traffic": UPGATE_TRAFFIC_C2 if args.config == "c2" else None,

@@ -146,3 +146,17 @@ def test_full_size_bf16_against_fp32_mode(vae):
     print("VAE 1024x1024, BF16 vs FP32-exact", metrics)
     assert ok, metrics
     assert np.array_equal(rgb, ov.rgb_image(exact))
+
+
+def test_fixed_1376x768_shape(vae):
+    """The reference's fixed decoder shape (tools/vae_shape_contract.py:2: latent 96 x 172, image 1376 x 768):
+    ragged 128-pixel segments on every level, 16512 attention tokens (padded to 16640) on the 32K-key softmax
+    path. BF16 against FP32-exact within the BF16 gate; both finite."""
+    u = latent(96, 172, seed=9)
+    exact, _, bad = vae.decode(u, ec.FP32)
+    fast, rgb, bad2 = vae.decode(u, ec.BF16, rgb=True)
+    assert bad == 0 and bad2 == 0 and exact.shape == (3, 768, 1376)
+    ok, metrics = gate(exact, fast, *VAE_BF16)
+    print("VAE 1376x768, BF16 vs FP32-exact", metrics)
+    assert ok, metrics
+    assert np.array_equal(rgb, ov.rgb_image(fast))
