@@ -163,6 +163,7 @@ struct ConvArgs
 {
     // geometry and schedule (set by launch_conv)
     int height = 0, width = 0, cin = 0, taps = 0, cout = 0, products = 1, group = 1;
+    int stride2 = 0, phase_stride = 0; // stride-2 taps over a space-to-depth operand (ConvLaunch::stride2)
     // out[pixel][c] = acc + bias[c] + resid[pixel][c], FP32 NHWC with row stride ldo (resid may equal out)
     float *out = nullptr;
     int ldo = 0;
@@ -183,11 +184,34 @@ struct ConvLaunch
     long long b_row = 0;
     int cout_rows = 0;
     int height = 0, width = 0, cin = 0, taps = 1, cout = 0; // cin a multiple of 64; cout 32 or a multiple of 128
+    // 3x3 stride-2 convolution whose input is padded by one zero row and column at the bottom and right
+    // (Downsample2D): `a` is the space-to-depth operand [height][width][4][a_planes][cin] of the
+    // [2 height][2 width] input (launch_s2d_operand) and height/width are the output's; tap (ky, kx) reads
+    // phase (ky & 1, kx & 1) at (y + ky / 2, x + kx / 2), and the zero padding is TMA's fill past the edge.
+    int stride2 = 0;
 };
 // GroupNorm partial slots per group that launch_conv writes for this launch (8 per CTA of its grid).
 int conv_stat_slots(const ConvLaunch &launch, int num_sms);
 constexpr int kSoftmaxMaxRow = 57344; // keys per attention row (the row is staged in shared memory)
 int launch_conv(const ConvLaunch &launch, const ConvArgs &epilogue, int num_sms, cudaStream_t stream);
+// ---- VAE encoder passes ----
+// conv_in as a 1x1 product: RGB bytes [h][w][3] -> (v - 127.5f) * (1 / 127.5f), gathered into the 3x3
+// neighbourhood's 27 values per pixel (column t * 3 + c for tap t = ky * 3 + kx, zero outside the image)
+// as the operand [h * w][planes * 64] (columns 27..63 zero).
+int launch_rgb_im2col(const uint8_t *rgb, int h, int w, __nv_bfloat16 *out, int planes, cudaStream_t stream);
+// OIHW FP32 [cout][cin][taps] -> [cout][taps * cin] (column t * cin + c): im2col column order.
+int launch_taps_inner(const float *w, int cout, int cin, int taps, float *out, cudaStream_t stream);
+// FP32 NHWC [h][w][channels] (h, w even) -> the stride-2 convolution's operand [h/2][w/2][4][planes][channels]
+// (phase (y & 1) * 2 + (x & 1)).
+int launch_s2d_operand(const float *x, int h, int w, int channels, __nv_bfloat16 *out, int planes,
+                       cudaStream_t stream);
+// quant_conv (1x1 over the 64 conv_out channels of `hin` [h][w][ldh], FP32) keeping outputs 0..31 (the
+// posterior's mode): mean [32][h][w]; packed = pixel_unshuffle(mean, 2) [128][h/2][w/2] (channel
+// c * 4 + (y & 1) * 2 + (x & 1)); normalized[c] = (packed[c] - rm[c]) / sqrt(rv[c] + eps). Any non-finite
+// output sets *nonfinite.
+int launch_encoder_output(const float *hin, int ldh, int h, int w, const float *wq, const float *bq, const float *rm,
+                          const float *rv, float eps, float *mean, float *packed, float *normalized, int *nonfinite,
+                          cudaStream_t stream);
 // scale[c] = gamma[c] / sqrt(var_g + eps), shift[c] = beta[c] - mean_g * scale[c] from `slots` partials of
 // each of 32 groups.
 int launch_gn_finalize(const double2 *stats, int slots, long long count, int cpg, const float *gamma,

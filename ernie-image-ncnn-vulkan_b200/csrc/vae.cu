@@ -18,6 +18,9 @@
 //               of the NHWC BF16 operand at (plane*Cin + c0, x0 + dx, y + dy): the tap's shift is a
 //               coordinate offset, and TMA's zero fill outside the image is the convolution's
 //               zero padding. The B tile is {64, BN} of the [Cout][planes x taps x Cin] weights.
+//               Stride-2 mode (the encoder's Downsample2D) reads a space-to-depth operand: tap (ky, kx) is
+//               the box at (phase * planes * Cin + plane * Cin + c0, x0 + kx / 2, y + ky / 2), phase =
+//               (ky & 1) * 2 + (kx & 1), so the strided taps stay unit-stride boxes.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per instruction).
 //   warps 2..5  epilogue: one TMEM lane (one pixel) per thread; bias, residual, FP32 NHWC store and
 //               the GroupNorm partial sums of the written values.
@@ -278,7 +281,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                 for (int kb = 0; kb < k_blocks && ok; ++kb)
                 {
                     const int tap = kb / cblk, c0 = (kb - tap * cblk) * CK;
-                    const int dy = args.taps == 9 ? tap / 3 - 1 : 0, dx = args.taps == 9 ? tap % 3 - 1 : 0;
+                    const int ky = tap / 3, kx = tap - ky * 3;
+                    int dy = 0, dx = 0, coff = 0;
+                    if (args.stride2)
+                    {
+                        dy = ky >> 1;
+                        dx = kx >> 1;
+                        coff = ((ky & 1) * 2 + (kx & 1)) * args.phase_stride;
+                    }
+                    else if (args.taps == 9)
+                    {
+                        dy = ky - 1;
+                        dx = kx - 1;
+                    }
                     for (int p = 0; p < products; ++p)
                     {
                         int pa, pb;
@@ -292,8 +307,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                         mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
 #pragma unroll
                         for (int sub = 0; sub < MSUB; ++sub)
-                            tma_load_3d(tile_a(stage, sub), &map_a, full_bar(stage), pa * args.cin + c0, xs[sub] + dx,
-                                        ys[sub] + dy);
+                            tma_load_3d(tile_a(stage, sub), &map_a, full_bar(stage), coff + pa * args.cin + c0,
+                                        xs[sub] + dx, ys[sub] + dy);
                         tma_load_2d(tile_b(stage), &map_b, full_bar(stage), pb * args.taps * args.cin + kb * CK,
                                     n_blk * BN);
                         if (++stage == C::kStages)
@@ -553,7 +568,8 @@ int launch_conv_impl(const ConvLaunch &l, ConvArgs args, int num_sms, cudaStream
     const cudaError_t attr = ensure_conv_attributes<BN, PROMOTE, MSUB>();
     if (attr != cudaSuccess) return attr;
     CUtensorMap map_a, map_b;
-    if (!make_operand_map(&map_a, l.a, static_cast<uint64_t>(l.a_planes) * l.cin, l.width, l.height) ||
+    if (!make_operand_map(&map_a, l.a, static_cast<uint64_t>(l.stride2 ? 4 : 1) * l.a_planes * l.cin, l.width,
+                          l.height) ||
         !make_weight_map(&map_b, l.b, static_cast<uint64_t>(l.cout_rows), static_cast<uint64_t>(l.b_row), BN))
         return cudaErrorInvalidValue;
     conv_kernel<BN, PROMOTE, MSUB><<<conv_grid(l, num_sms), kConvThreads, C::kSmemBytes, stream>>>(map_a, map_b, args);
@@ -705,6 +721,131 @@ __global__ void upsample_kernel(const float *x, int h, int w, int channels, __nv
             const long long q = static_cast<long long>(2 * yy + (d >> 1)) * (2 * w) + 2 * xx + (d & 1);
             store_planes8(out + q * planes * channels + c0, channels, planes, v);
         }
+    }
+}
+
+// ---- encoder passes (encode_vae, src/image_encoder.cpp:29-72) ----
+// The encoder's conv_in (3 -> 128, 3x3) as a 1x1 product over im2col columns: RGB bytes normalised in the
+// reference's FP32 order (src/image_encoder.cpp:44-51) and gathered per pixel: column t * 3 + c is channel c
+// of the neighbour at tap t = ky * 3 + kx (zero outside the image); columns 27..63 are zero.
+__global__ void rgb_im2col_kernel(const uint8_t *rgb, int h, int w, __nv_bfloat16 *out, int planes)
+{
+    const long long pixels = static_cast<long long>(h) * w;
+    for (long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; p < pixels;
+         p += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const int y = static_cast<int>(p / w), x = static_cast<int>(p - static_cast<long long>(y) * w);
+        __nv_bfloat16 *dst = out + p * planes * 64;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+        {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+            {
+                const int k = g * 8 + j;
+                float value = 0.f;
+                if (k < 27)
+                {
+                    const int t = k / 3, c = k % 3, yy = y + t / 3 - 1, xx = x + t % 3 - 1;
+                    if (yy >= 0 && yy < h && xx >= 0 && xx < w)
+                        value = __fmul_rn(__fsub_rn(static_cast<float>(rgb[(static_cast<long long>(yy) * w + xx) * 3 + c]),
+                                                    127.5f),
+                                          1.f / 127.5f);
+                }
+                v[j] = value;
+            }
+            store_planes8(dst + g * 8, 64, planes, v);
+        }
+    }
+}
+
+// OIHW [cout][cin][taps] -> [cout][taps * cin] (column t * cin + c).
+__global__ void taps_inner_kernel(const float *w, int cout, int cin, int taps, float *out)
+{
+    const long long total = static_cast<long long>(cout) * cin * taps;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const long long row = static_cast<long long>(taps) * cin;
+        const long long o = i / row;
+        const int r = static_cast<int>(i - o * row), t = r / cin, c = r - t * cin;
+        out[i] = w[(o * cin + c) * taps + t];
+    }
+}
+
+// Space-to-depth operand of a stride-2 convolution: pixel (y, x) of FP32 NHWC x goes to
+// [(y / 2) * (w / 2) + x / 2][phase = (y & 1) * 2 + (x & 1)][plane][c] as BF16 plane(s).
+__global__ void s2d_operand_kernel(const float *x, int h, int w, int channels, __nv_bfloat16 *out, int planes)
+{
+    const int per_pixel = channels / 8;
+    const long long total = static_cast<long long>(h) * w * per_pixel;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const long long p = i / per_pixel;
+        const int c0 = static_cast<int>(i - p * per_pixel) * 8;
+        const int yy = static_cast<int>(p / w), xx = static_cast<int>(p - static_cast<long long>(yy) * w);
+        const float4 *src = reinterpret_cast<const float4 *>(x + p * channels + c0);
+        const float4 a = src[0], b = src[1];
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const long long q = static_cast<long long>(yy >> 1) * (w >> 1) + (xx >> 1);
+        const int phase = (yy & 1) * 2 + (xx & 1);
+        store_planes8(out + (q * 4 + phase) * planes * channels + c0, channels, planes, v);
+    }
+}
+
+// The encoder's tail (tools/export_vae_encoder.py:74-80): quant_conv in FP32 keeping the posterior's mode
+// (outputs 0..31), pixel_unshuffle(2) and the affine-free BatchNorm in eval mode, one thread per pixel of
+// the mean. normalized = (packed - running_mean) * (1 / sqrt(running_var + eps)).
+__global__ void encoder_output_kernel(const float *hin, int ldh, int h, int w, const float *wq, const float *bq,
+                                      const float *rm, const float *rv, float eps, float *mean, float *packed,
+                                      float *normalized, int *nonfinite)
+{
+    __shared__ float ws[32 * 64], bs[32], ms[128], is[128];
+    for (int i = threadIdx.x; i < 32 * 64; i += blockDim.x) ws[i] = wq[i];
+    if (threadIdx.x < 32) bs[threadIdx.x] = bq[threadIdx.x];
+    if (threadIdx.x < 128)
+    {
+        ms[threadIdx.x] = rm[threadIdx.x];
+        is[threadIdx.x] = __frcp_rn(__fsqrt_rn(__fadd_rn(rv[threadIdx.x], eps)));
+    }
+    __syncthreads();
+    const long long pixels = static_cast<long long>(h) * w;
+    const int w2 = w / 2;
+    const long long plane2 = static_cast<long long>(h / 2) * w2;
+    for (long long p = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; p < pixels;
+         p += static_cast<long long>(gridDim.x) * blockDim.x)
+    {
+        const int y = static_cast<int>(p / w), x = static_cast<int>(p - static_cast<long long>(y) * w);
+        float in[64];
+        const float4 *src = reinterpret_cast<const float4 *>(hin + p * ldh);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+        {
+            const float4 v = src[k];
+            in[4 * k] = v.x;
+            in[4 * k + 1] = v.y;
+            in[4 * k + 2] = v.z;
+            in[4 * k + 3] = v.w;
+        }
+        const long long q = static_cast<long long>(y >> 1) * w2 + (x >> 1);
+        const int phase = (y & 1) * 2 + (x & 1);
+        bool finite = true;
+#pragma unroll 4
+        for (int c = 0; c < 32; ++c)
+        {
+            float acc = bs[c];
+#pragma unroll
+            for (int k = 0; k < 64; ++k) acc = fmaf(ws[c * 64 + k], in[k], acc);
+            const int pc = c * 4 + phase;
+            const float n = __fmul_rn(__fsub_rn(acc, ms[pc]), is[pc]);
+            mean[c * pixels + p] = acc;
+            packed[pc * plane2 + q] = acc;
+            normalized[pc * plane2 + q] = n;
+            finite = finite && isfinite(acc) && isfinite(n);
+        }
+        if (!finite && nonfinite) atomicOr(nonfinite, 1);
     }
 }
 
@@ -1043,6 +1184,7 @@ int launch_conv(const ConvLaunch &l, const ConvArgs &epi, int num_sms, cudaStrea
         (l.a_planes != 1 && l.a_planes != 3) || (l.b_planes != 1 && l.b_planes != 3) || num_sms < 1)
         return cudaErrorInvalidValue;
     if (l.b_row < static_cast<long long>(l.b_planes) * l.taps * l.cin || l.cout_rows < l.cout) return cudaErrorInvalidValue;
+    if (l.stride2 && l.taps != 9) return cudaErrorInvalidValue;
     const bool promote = l.a_planes == 3;
     if (!promote && l.b_planes != 1) return cudaErrorInvalidValue;
     ConvArgs args = epi;
@@ -1051,6 +1193,8 @@ int launch_conv(const ConvLaunch &l, const ConvArgs &epi, int num_sms, cudaStrea
     args.cin = l.cin;
     args.taps = l.taps;
     args.cout = l.cout;
+    args.stride2 = l.stride2 ? 1 : 0;
+    args.phase_stride = l.a_planes * l.cin;
     args.products = promote ? (l.b_planes == 3 ? 6 : 3) : 1;
     args.group = conv_group(l.taps * l.cin / CK);
     if (args.stats && args.cpg != 4 && args.cpg != 8 && args.cpg != 16) return cudaErrorInvalidValue;
@@ -1121,6 +1265,44 @@ int launch_attention_split(const float *qkv, int n, __nv_bfloat16 *q, __nv_bfloa
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     transpose_v_kernel<<<dim3((n + 31) / 32, 512 / 32), dim3(32, 8), 0, stream>>>(qkv, n, vt, ldv, planes);
+    return cudaGetLastError();
+}
+
+int launch_rgb_im2col(const uint8_t *rgb, int h, int w, __nv_bfloat16 *out, int planes, cudaStream_t stream)
+{
+    if (!rgb || !out || h < 1 || w < 1 || (planes != 1 && planes != 3)) return cudaErrorInvalidValue;
+    rgb_im2col_kernel<<<grid_for_count(static_cast<long long>(h) * w, 128), 128, 0, stream>>>(rgb, h, w, out, planes);
+    return cudaGetLastError();
+}
+
+int launch_taps_inner(const float *w, int cout, int cin, int taps, float *out, cudaStream_t stream)
+{
+    if (!w || !out || cout < 1 || cin < 1 || taps < 1) return cudaErrorInvalidValue;
+    taps_inner_kernel<<<grid_for_count(static_cast<long long>(cout) * cin * taps, 256), 256, 0, stream>>>(w, cout, cin,
+                                                                                                        taps, out);
+    return cudaGetLastError();
+}
+
+int launch_s2d_operand(const float *x, int h, int w, int channels, __nv_bfloat16 *out, int planes,
+                       cudaStream_t stream)
+{
+    if (!x || !out || h < 2 || w < 2 || (h & 1) || (w & 1) || channels < 8 || channels % 8 ||
+        (planes != 1 && planes != 3))
+        return cudaErrorInvalidValue;
+    s2d_operand_kernel<<<grid_for_count(static_cast<long long>(h) * w * channels / 8, 256), 256, 0, stream>>>(
+        x, h, w, channels, out, planes);
+    return cudaGetLastError();
+}
+
+int launch_encoder_output(const float *hin, int ldh, int h, int w, const float *wq, const float *bq, const float *rm,
+                          const float *rv, float eps, float *mean, float *packed, float *normalized, int *nonfinite,
+                          cudaStream_t stream)
+{
+    if (!hin || !wq || !bq || !rm || !rv || !mean || !packed || !normalized || ldh < 64 || ldh % 4 || h < 2 ||
+        w < 2 || (h & 1) || (w & 1))
+        return cudaErrorInvalidValue;
+    encoder_output_kernel<<<grid_for_count(static_cast<long long>(h) * w, 128), 128, 0, stream>>>(
+        hin, ldh, h, w, wq, bq, rm, rv, eps, mean, packed, normalized, nonfinite);
     return cudaGetLastError();
 }
 

@@ -1,6 +1,6 @@
-// C ABI of the VAE decoder (include/ernie_cuda.h, "VAE decoder"): resident weights addressed by their
-// diffusers parameter names, a per-shape workspace, and the decoder's layer program replayed as one CUDA
-// graph. Host orchestration only; the arithmetic is in vae.cu's kernels.
+// C ABI of the VAE decoder and encoder (include/ernie_cuda.h, "VAE decoder", "VAE encoder"): resident
+// weights addressed by their diffusers parameter names, a per-shape workspace, and the layer program replayed
+// as one CUDA graph. Host orchestration only; the arithmetic is in vae.cu's kernels.
 //
 // The program follows the reference's exported decoder graph (AutoencoderKLFlux2 post_quant_conv +
 // decoder as vae/head.ncnn.param lists it, run by decode_vae, src/vae.cpp:18-66): post_quant_conv 1x1
@@ -8,6 +8,14 @@
 // four up blocks of three resnets (512, 512, 256, 128 channels; 1x1 shortcut where the width changes)
 // with nearest x2 upsampling + conv after the first three, GroupNorm(32, eps 1e-6) + Swish, conv_out
 // 3x3 128->3. The RGB bytes follow rgb_image (src/pipeline.cpp:145-163).
+//
+// The encoder program follows encode_vae (src/image_encoder.cpp:29-72) over the wrapper its export traces
+// (tools/export_vae_encoder.py:74-80): RGB bytes normalised as (v - 127.5f) * (1 / 127.5f), conv_in 3x3
+// 3->128, four down blocks of two resnets (128, 256, 512, 512 channels) with a 3x3 stride-2 convolution
+// (input padded by one zero row and column at the bottom and right) after the first three, the decoder's
+// mid block, GroupNorm(32, eps 1e-6) + Swish, conv_out 3x3 512->64, quant_conv 1x1 keeping channels 0..31
+// (the posterior's mode: mean), pixel_unshuffle(2) (packed) and BatchNorm(128, eps 1e-4, no affine, eval)
+// (normalized).
 #include "capi_internal.h"
 #include "ernie_synth.h"
 #include "kernels.h"
@@ -24,8 +32,8 @@ using namespace ernie_b200::capi;
 
 namespace
 {
-constexpr float kGroupNormEps = 1e-6f;
-constexpr int kGroups = 32, kMaxLatentSide = 256;
+constexpr float kGroupNormEps = 1e-6f, kEncoderBnEps = 1e-4f;
+constexpr int kGroups = 32, kMaxLatentSide = 256, kMaxImageSide = 2048;
 
 struct ConvW
 {
@@ -33,10 +41,14 @@ struct ConvW
     // conv_out: stored as the 1x1 convolution to its 9 taps x 3 outputs (rows t * 3 + c, padded to 32),
     // whose product a gather kernel sums over the 3x3 neighbourhood
     bool tap_expanded = false;
+    // the encoder's conv_in: a 1x1 product over the 27 im2col columns of its RGB input (padded to 64)
+    bool im2col = false;
+    // Downsample2D: 3x3 stride 2 over the space-to-depth operand (ConvLaunch::stride2)
+    bool stride2 = false;
     __nv_bfloat16 *w = nullptr; // [cout_rows][3 * dev_taps() * cin_pad]: hi, mid, lo planes
     float *bias = nullptr;      // [cout_rows]
     int inexact = 0;            // some weight is not a BF16 value (FP32-exact mode multiplies 3 planes)
-    int dev_taps() const { return tap_expanded ? 1 : taps; }
+    int dev_taps() const { return tap_expanded || im2col ? 1 : taps; }
 };
 struct NormW
 {
@@ -70,6 +82,7 @@ struct Param
     Role role = Role::Vector;
     ConvW *conv = nullptr;
     int row_offset = 0;
+    float **slot = nullptr; // Role::Vector tensors other than GroupNorm gamma/beta: the layout's pointer
     float *dst = nullptr;
     float scale = 0.f, offset = 0.f; // synthetic initialisation (include/ernie_synth.h)
     bool loaded = false;
@@ -81,22 +94,16 @@ struct Param
     }
 };
 
-// Diffusers parameter names and shapes of the decoder, in the order the reference graph runs them.
-struct Layout
+// Builders of diffusers parameter tables (names, shapes, resident destinations).
+struct LayoutBase
 {
-    float *pq_w = nullptr, *pq_b = nullptr;
-    ConvW conv_in;
-    ResnetW mid[2];
-    AttnW attn;
-    ResnetW up[4][3];
-    ConvW upsample[3];
-    NormW norm_out;
-    ConvW conv_out;
     std::vector<Param> params;
     std::vector<ConvW *> convs;
     std::vector<NormW *> norms;
 
-    static constexpr int kUpOut[4] = {512, 512, 256, 128};
+    LayoutBase() = default;
+    LayoutBase(const LayoutBase &) = delete; // params and convs point into the object
+    LayoutBase &operator=(const LayoutBase &) = delete;
 
     void conv(const std::string &name, ConvW &c, int cin, int cout, int taps)
     {
@@ -131,27 +138,11 @@ struct Layout
             conv(name + ".conv_shortcut", r.shortcut, cin, cout, 1);
         }
     }
-    void add(const std::string &name, std::vector<int> shape, Role role, ConvW *c, int row_offset, float scale,
-             float offset)
+    // The mid block's single-head attention (prefix ends in "attentions.0."): GroupNorm, to_q/k/v as one
+    // 1536-row 1x1 product, to_out.0.
+    void attention(const std::string &prefix, AttnW &attn)
     {
-        Param p;
-        p.name = name;
-        p.shape = std::move(shape);
-        p.role = role;
-        p.conv = c;
-        p.row_offset = row_offset;
-        p.scale = scale;
-        p.offset = offset;
-        params.push_back(std::move(p));
-    }
-
-    Layout()
-    {
-        add("post_quant_conv.weight", {32, 32, 1, 1}, Role::Vector, nullptr, 0, 1.f / std::sqrt(32.f), 0.f);
-        add("post_quant_conv.bias", {32}, Role::Vector, nullptr, 0, 0.02f, 0.f);
-        conv("decoder.conv_in", conv_in, 32, 512, 9);
-        resnet("decoder.mid_block.resnets.0", mid[0], 512, 512);
-        norm("decoder.mid_block.attentions.0.group_norm", attn.norm, 512);
+        norm(prefix + "group_norm", attn.norm, 512);
         attn.qkv.cin = 512;
         attn.qkv.cout = 1536;
         attn.qkv.taps = 1;
@@ -162,7 +153,7 @@ struct Layout
         const char *proj[3] = {"to_q", "to_k", "to_v"};
         for (int i = 0; i < 3; ++i)
         {
-            const std::string base = std::string("decoder.mid_block.attentions.0.") + proj[i];
+            const std::string base = prefix + proj[i];
             add(base + ".weight", {512, 512}, Role::ConvWeight, &attn.qkv, 512 * i, lin, 0.f);
             add(base + ".bias", {512}, Role::ConvBias, &attn.qkv, 512 * i, 0.02f, 0.f);
         }
@@ -172,8 +163,46 @@ struct Layout
         attn.out.cin_pad = 512;
         attn.out.cout_rows = 512;
         convs.push_back(&attn.out);
-        add("decoder.mid_block.attentions.0.to_out.0.weight", {512, 512}, Role::ConvWeight, &attn.out, 0, lin, 0.f);
-        add("decoder.mid_block.attentions.0.to_out.0.bias", {512}, Role::ConvBias, &attn.out, 0, 0.02f, 0.f);
+        add(prefix + "to_out.0.weight", {512, 512}, Role::ConvWeight, &attn.out, 0, lin, 0.f);
+        add(prefix + "to_out.0.bias", {512}, Role::ConvBias, &attn.out, 0, 0.02f, 0.f);
+    }
+    void add(const std::string &name, std::vector<int> shape, Role role, ConvW *c, int row_offset, float scale,
+             float offset, float **slot = nullptr)
+    {
+        Param p;
+        p.name = name;
+        p.shape = std::move(shape);
+        p.role = role;
+        p.conv = c;
+        p.row_offset = row_offset;
+        p.scale = scale;
+        p.offset = offset;
+        p.slot = slot;
+        params.push_back(std::move(p));
+    }
+};
+
+// Diffusers parameter names and shapes of the decoder, in the order the reference graph runs them.
+struct Layout : LayoutBase
+{
+    float *pq_w = nullptr, *pq_b = nullptr;
+    ConvW conv_in;
+    ResnetW mid[2];
+    AttnW attn;
+    ResnetW up[4][3];
+    ConvW upsample[3];
+    NormW norm_out;
+    ConvW conv_out;
+
+    static constexpr int kUpOut[4] = {512, 512, 256, 128};
+
+    Layout()
+    {
+        add("post_quant_conv.weight", {32, 32, 1, 1}, Role::Vector, nullptr, 0, 1.f / std::sqrt(32.f), 0.f, &pq_w);
+        add("post_quant_conv.bias", {32}, Role::Vector, nullptr, 0, 0.02f, 0.f, &pq_b);
+        conv("decoder.conv_in", conv_in, 32, 512, 9);
+        resnet("decoder.mid_block.resnets.0", mid[0], 512, 512);
+        attention("decoder.mid_block.attentions.0.", attn);
         resnet("decoder.mid_block.resnets.1", mid[1], 512, 512);
         int c = 512;
         for (int i = 0; i < 4; ++i)
@@ -193,7 +222,54 @@ struct Layout
     }
 };
 
-// Buffers of one decode shape and precision (levels L0..L3 at 1x, 2x, 4x, 8x the input side).
+// Diffusers parameter names and shapes of the encoder (+ quant_conv, bn), in execution order.
+struct EncoderLayout : LayoutBase
+{
+    ConvW conv_in;
+    ResnetW down[4][2];
+    ConvW downsample[3];
+    ResnetW mid[2];
+    AttnW attn;
+    NormW norm_out;
+    ConvW conv_out;
+    float *quant_w = nullptr, *quant_b = nullptr, *bn_mean = nullptr, *bn_var = nullptr;
+
+    static constexpr int kDownOut[4] = {128, 256, 512, 512};
+
+    EncoderLayout()
+    {
+        conv("encoder.conv_in", conv_in, 3, 128, 9);
+        conv_in.im2col = true;
+        int c = 128;
+        for (int i = 0; i < 4; ++i)
+        {
+            for (int j = 0; j < 2; ++j)
+            {
+                resnet("encoder.down_blocks." + std::to_string(i) + ".resnets." + std::to_string(j), down[i][j], c,
+                       kDownOut[i]);
+                c = kDownOut[i];
+            }
+            if (i < 3)
+            {
+                conv("encoder.down_blocks." + std::to_string(i) + ".downsamplers.0.conv", downsample[i], c, c, 9);
+                downsample[i].stride2 = true;
+            }
+        }
+        resnet("encoder.mid_block.resnets.0", mid[0], 512, 512);
+        attention("encoder.mid_block.attentions.0.", attn);
+        resnet("encoder.mid_block.resnets.1", mid[1], 512, 512);
+        norm("encoder.conv_norm_out", norm_out, 512);
+        conv("encoder.conv_out", conv_out, 512, 64, 9);
+        conv_out.cout_rows = 128; // the 128-channel tile; rows 64..127 stay zero
+        add("quant_conv.weight", {64, 64, 1, 1}, Role::Vector, nullptr, 0, 1.f / std::sqrt(64.f), 0.f, &quant_w);
+        add("quant_conv.bias", {64}, Role::Vector, nullptr, 0, 0.02f, 0.f, &quant_b);
+        add("bn.running_mean", {128}, Role::Vector, nullptr, 0, 0.02f, 0.f, &bn_mean);
+        add("bn.running_var", {128}, Role::Vector, nullptr, 0, 0.1f, 1.f, &bn_var);
+    }
+};
+
+// Buffers of one decode (encode) shape and precision: the decoder's levels L0..L3 at 1x, 2x, 4x, 8x the
+// latent side, the encoder's at 1x, 1/2, 1/4, 1/8 the image side.
 struct Plan
 {
     int h0 = 0, w0 = 0, precision = 0, planes = 1;
@@ -203,6 +279,8 @@ struct Plan
     __nv_bfloat16 *a = nullptr, *a2 = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *p = nullptr;
     double2 *stats_x = nullptr, *stats_h = nullptr;
     uint8_t *rgb = nullptr;
+    uint8_t *rgb_in = nullptr;                                      // encoder input
+    float *mean = nullptr, *packed = nullptr, *normalized = nullptr; // encoder outputs
     int *nonfinite = nullptr;
     void *alloc = nullptr;
     cudaGraphExec_t graph = nullptr;
@@ -211,17 +289,25 @@ struct Plan
 };
 
 size_t pixels_of(int h, int w) { return static_cast<size_t>(h) * static_cast<size_t>(w); }
-} // namespace
 
-struct ernie_cuda_vae
+// Resident weights of one layout, their staging buffers and the current shape's plan.
+template <class L> struct VaeModel
 {
     ernie_cuda_context *ctx = nullptr;
-    Layout layout;
+    L layout;
     void *alloc = nullptr;
     float *staging = nullptr, *staging2 = nullptr;
     int *d_inexact = nullptr;
     uint64_t bytes = 0;
     std::unique_ptr<Plan> plan;
+};
+} // namespace
+
+struct ernie_cuda_vae : VaeModel<Layout>
+{
+};
+struct ernie_cuda_vae_encoder : VaeModel<EncoderLayout>
+{
 };
 
 namespace
@@ -233,25 +319,11 @@ void free_plan(Plan *p)
     if (p->alloc) cudaFree(p->alloc);
 }
 
-int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_ptr<Plan> &out)
+// Mid-block attention (p.n tokens) and GroupNorm buffers, common to both programs.
+void add_common(Arena &arena, Plan &p, int num_sms)
 {
-    auto plan = std::make_unique<Plan>();
-    Plan &p = *plan;
-    p.h0 = h0;
-    p.w0 = w0;
-    p.precision = precision;
-    p.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
-    p.n = h0 * w0;
     p.npad = (p.n + 255) / 256 * 256;
-    const size_t px0 = pixels_of(h0, w0), top = 64 * px0;
-    const int slots_max = 8 * v->ctx->num_sms; // GroupNorm partial slots per group (8 per conv CTA)
-    Arena arena;
-    arena.add(&p.input, 32 * px0);
-    arena.add(&p.x, 16384 * px0);
-    arena.add(&p.h1, 8192 * px0);
-    arena.add(&p.sc, 8192 * px0);
-    arena.add(&p.a, static_cast<size_t>(p.planes) * 16384 * px0);
-    arena.add(&p.a2, static_cast<size_t>(p.planes) * 16384 * px0); // shortcut-convolution operand
+    const int slots_max = 8 * num_sms; // GroupNorm partial slots per group (8 per conv CTA)
     arena.add(&p.qkv, static_cast<size_t>(p.n) * 1536);
     arena.add(&p.q, static_cast<size_t>(p.planes) * 512 * p.npad);
     arena.add(&p.k, static_cast<size_t>(p.planes) * 512 * p.npad);
@@ -263,18 +335,20 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
     arena.add(&p.stats_h, static_cast<size_t>(kGroups) * slots_max);
     arena.add(&p.scale, 512);
     arena.add(&p.shift, 512);
-    arena.add(&p.decoded, 3 * top);
-    arena.add(&p.rgb, 3 * top);
     arena.add(&p.nonfinite, 1);
+}
+
+int allocate_plan(ernie_cuda_context *ctx, Arena &arena, std::unique_ptr<Plan> &plan, std::unique_ptr<Plan> &out)
+{
+    Plan &p = *plan;
     p.bytes = arena.bytes();
     const cudaError_t e = arena.allocate();
     if (e != cudaSuccess) return from_cuda(e, "Allocate VAE workspace");
     p.alloc = arena.base;
     // K's rows and V^T's columns past the last token stay zero: their scores and products vanish
-    cudaError_t z = cudaMemsetAsync(p.k, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, v->ctx->stream);
-    if (z == cudaSuccess)
-        z = cudaMemsetAsync(p.vt, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, v->ctx->stream);
-    if (z == cudaSuccess) z = cudaStreamSynchronize(v->ctx->stream);
+    cudaError_t z = cudaMemsetAsync(p.k, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, ctx->stream);
+    if (z == cudaSuccess) z = cudaMemsetAsync(p.vt, 0, static_cast<size_t>(p.planes) * 512 * p.npad * 2, ctx->stream);
+    if (z == cudaSuccess) z = cudaStreamSynchronize(ctx->stream);
     if (z != cudaSuccess)
     {
         free_plan(plan.get());
@@ -282,6 +356,56 @@ int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_pt
     }
     out = std::move(plan);
     return ERNIE_CUDA_OK;
+}
+
+// Decoder: h0 x w0 is the unpacked latent.
+int plan_create(ernie_cuda_vae *v, int h0, int w0, int precision, std::unique_ptr<Plan> &out)
+{
+    auto plan = std::make_unique<Plan>();
+    Plan &p = *plan;
+    p.h0 = h0;
+    p.w0 = w0;
+    p.precision = precision;
+    p.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    p.n = h0 * w0;
+    const size_t px0 = pixels_of(h0, w0), top = 64 * px0;
+    Arena arena;
+    arena.add(&p.input, 32 * px0);
+    arena.add(&p.x, 16384 * px0);
+    arena.add(&p.h1, 8192 * px0);
+    arena.add(&p.sc, 8192 * px0);
+    arena.add(&p.a, static_cast<size_t>(p.planes) * 16384 * px0);
+    arena.add(&p.a2, static_cast<size_t>(p.planes) * 16384 * px0); // shortcut-convolution operand
+    arena.add(&p.decoded, 3 * top);
+    arena.add(&p.rgb, 3 * top);
+    add_common(arena, p, v->ctx->num_sms);
+    return allocate_plan(v->ctx, arena, plan, out);
+}
+
+// Encoder: h0 x w0 is the image (multiples of 16). Largest tensors: 128 channels at full size (level 0),
+// 256 x 1/4 for the level-1 shortcut, the level-0 stride-2 operand (4 phases x 128 channels x 1/4).
+int plan_create(ernie_cuda_vae_encoder *v, int h0, int w0, int precision, std::unique_ptr<Plan> &out)
+{
+    auto plan = std::make_unique<Plan>();
+    Plan &p = *plan;
+    p.h0 = h0;
+    p.w0 = w0;
+    p.precision = precision;
+    p.planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    p.n = (h0 / 8) * (w0 / 8);
+    const size_t px = pixels_of(h0, w0);
+    Arena arena;
+    arena.add(&p.rgb_in, 3 * px);
+    arena.add(&p.x, 128 * px);
+    arena.add(&p.h1, 128 * px);
+    arena.add(&p.sc, 64 * px);
+    arena.add(&p.a, static_cast<size_t>(p.planes) * 128 * px);
+    arena.add(&p.a2, static_cast<size_t>(p.planes) * 32 * px);
+    arena.add(&p.mean, 32 * px / 64);
+    arena.add(&p.packed, 128 * px / 256);
+    arena.add(&p.normalized, 128 * px / 256);
+    add_common(arena, p, v->ctx->num_sms);
+    return allocate_plan(v->ctx, arena, plan, out);
 }
 
 // ---- the decoder program -----------------------------------------------------------------------------
@@ -293,7 +417,7 @@ enum ProfileClass : int
     kProfAttnGemm = 1,  // attention scores q k^T and probabilities x v (FLOPs)
     kProfSoftmax = 2,   // bytes
     kProfNorm = 3,      // GroupNorm statistics + apply (+ Swish) (bytes)
-    kProfUpsample = 4,  // bytes
+    kProfUpsample = 4,  // bytes (decoder: nearest x2 upsampling; encoder: the stride-2 operand)
     kProfOther = 5,     // post_quant_conv input, attention split, operand conversions (bytes)
     kProfClasses = 6
 };
@@ -337,7 +461,7 @@ struct Profiler
 
 struct Program
 {
-    ernie_cuda_vae *v;
+    ernie_cuda_context *ctx;
     Plan &p;
     cudaStream_t stream;
     int sms;
@@ -370,9 +494,10 @@ struct Program
         l.cin = c.cin_pad;
         l.taps = c.dev_taps();
         l.cout = c.cout_rows;
+        l.stride2 = c.stride2 ? 1 : 0;
         ConvArgs args = epi;
         args.bias = c.tap_expanded ? nullptr : c.bias; // conv_out's bias is added by the gather
-        args.error_flag = v->ctx->error_flag;
+        args.error_flag = ctx->error_flag;
         const double flops = 2.0 * pixels_of(h, w) * c.cout * c.cin * c.taps;
         if (args.stats) (args.stats == p.stats_x ? slots_x : slots_h) = conv_stat_slots(l, sms);
         return op(kProfConv, flops, 1, "VAE convolution", [&] { return launch_conv(l, args, sms, stream); });
@@ -456,7 +581,7 @@ struct Program
         ConvArgs es;
         es.out = p.s;
         es.ldo = npad;
-        es.error_flag = v->ctx->error_flag;
+        es.error_flag = ctx->error_flag;
         const double gemm = 2.0 * n * n * 512;
         ERNIE_TRY(op(kProfAttnGemm, gemm, 1, "attention scores", [&] { return launch_conv(ls, es, sms, stream); }));
         ERNIE_TRY(op(kProfSoftmax, 4.0 * n * n + bytes_bf16(static_cast<double>(n) * npad), 1, "attention softmax", [&] {
@@ -477,14 +602,13 @@ struct Program
         ConvArgs eo;
         eo.out = p.o;
         eo.ldo = 512;
-        eo.error_flag = v->ctx->error_flag;
+        eo.error_flag = ctx->error_flag;
         ERNIE_TRY(op(kProfAttnGemm, gemm, 1, "attention values", [&] { return launch_conv(lo, eo, sms, stream); }));
         ERNIE_TRY(to_operand(p.o, n, 512));
         return conv(at.out, p.a, h, w, writes_x(512, p.x));
     }
-    int run()
+    int run(const Layout &L)
     {
-        const Layout &L = v->layout;
         int h = p.h0, w = p.w0;
         const double px = static_cast<double>(pixels_of(h, w));
         ERNIE_TRY(op(kProfOther, 4.0 * 32 * px + bytes_bf16(64.0 * px), 1, "post_quant_conv", [&] {
@@ -517,6 +641,39 @@ struct Program
             return launch_conv_out_gather(p.h1, h, w, L.conv_out.bias, p.decoded, p.rgb, p.nonfinite, stream);
         });
     }
+    int run(const EncoderLayout &L)
+    {
+        int h = p.h0, w = p.w0;
+        const double px = static_cast<double>(pixels_of(h, w));
+        ERNIE_TRY(op(kProfOther, 3.0 * px + bytes_bf16(64.0 * px), 1, "encoder input",
+                     [&] { return launch_rgb_im2col(p.rgb_in, h, w, p.a, p.planes, stream); }));
+        ERNIE_TRY(conv(L.conv_in, p.a, h, w, writes_x(128, nullptr)));
+        for (int i = 0; i < 4; ++i)
+        {
+            for (int j = 0; j < 2; ++j) ERNIE_TRY(resnet(L.down[i][j], h, w));
+            if (i == 3) break;
+            const int c = L.down[i][1].cout;
+            const double elements = static_cast<double>(pixels_of(h, w)) * c;
+            ERNIE_TRY(op(kProfUpsample, 4.0 * elements + bytes_bf16(elements), 1, "downsample operand",
+                         [&] { return launch_s2d_operand(p.x, h, w, c, p.a, p.planes, stream); }));
+            h /= 2;
+            w /= 2;
+            ERNIE_TRY(conv(L.downsample[i], p.a, h, w, writes_x(c, nullptr)));
+        }
+        ERNIE_TRY(resnet(L.mid[0], h, w));
+        ERNIE_TRY(attention(L.attn, h, w));
+        ERNIE_TRY(resnet(L.mid[1], h, w));
+        ERNIE_TRY(group_norm(L.norm_out, p.x, p.stats_x, h, w, true));
+        ConvArgs e;
+        e.out = p.h1;
+        e.ldo = L.conv_out.cout_rows;
+        ERNIE_TRY(conv(L.conv_out, p.a, h, w, e));
+        const double px_mean = static_cast<double>(pixels_of(h, w));
+        return op(kProfOther, px_mean * (64 * 4 + 3 * 32 * 4), 1, "quant_conv + unshuffle + batch norm", [&] {
+            return launch_encoder_output(p.h1, L.conv_out.cout_rows, h, w, L.quant_w, L.quant_b, L.bn_mean, L.bn_var,
+                                         kEncoderBnEps, p.mean, p.packed, p.normalized, p.nonfinite, stream);
+        });
+    }
 };
 
 bool vae_shape_ok(int width, int height)
@@ -525,7 +682,15 @@ bool vae_shape_ok(int width, int height)
            width * height <= kSoftmaxMaxRow;
 }
 
-int find_param(ernie_cuda_vae *v, const char *name)
+// The encoder's images: sides multiples of 16 (an even mean for pixel_unshuffle), at most 2048, and a mid
+// block of at most kSoftmaxMaxRow tokens.
+bool encoder_shape_ok(int width, int height)
+{
+    return width >= 16 && height >= 16 && width % 16 == 0 && height % 16 == 0 && width <= kMaxImageSide &&
+           height <= kMaxImageSide && (width / 8) * (height / 8) <= kSoftmaxMaxRow;
+}
+
+template <class V> int find_param(V *v, const char *name)
 {
     for (size_t i = 0; i < v->layout.params.size(); ++i)
         if (v->layout.params[i].name == name) return static_cast<int>(i);
@@ -533,7 +698,7 @@ int find_param(ernie_cuda_vae *v, const char *name)
 }
 
 // Moves staged FP32 values (device) of parameter i to their resident form.
-int place(ernie_cuda_vae *v, Param &prm)
+template <class V> int place(V *v, Param &prm)
 {
     cudaStream_t stream = v->ctx->stream;
     if (prm.role == Role::Vector)
@@ -559,6 +724,13 @@ int place(ernie_cuda_vae *v, Param &prm)
                                                  v->d_inexact, stream),
                          "prepare weights");
         }
+        else if (c.im2col)
+        {
+            ERNIE_LAUNCH(launch_taps_inner(v->staging, c.cout, c.cin, c.taps, v->staging2, stream), "im2col weights");
+            ERNIE_LAUNCH(launch_conv_weight_prep(v->staging2, c.cout, c.taps * c.cin, 1, c.cout_rows, c.cin_pad, c.w,
+                                                 v->d_inexact, stream),
+                         "prepare weights");
+        }
         else
             ERNIE_LAUNCH(launch_conv_weight_prep(v->staging, cout, c.cin, c.taps, rows, c.cin_pad,
                                                  c.w + static_cast<size_t>(prm.row_offset) * 3 * c.taps * c.cin_pad,
@@ -573,7 +745,7 @@ int place(ernie_cuda_vae *v, Param &prm)
     return ERNIE_CUDA_OK;
 }
 
-void drop_plan(ernie_cuda_vae *v)
+template <class V> void drop_plan(V *v)
 {
     if (v->plan)
     {
@@ -582,15 +754,15 @@ void drop_plan(ernie_cuda_vae *v)
     }
 }
 
-int ensure_plan(ernie_cuda_vae *v, int width, int height, int precision)
+template <class V> int ensure_plan(V *v, int width, int height, int precision)
 {
     if (v->plan && v->plan->w0 == width && v->plan->h0 == height && v->plan->precision == precision)
         return ERNIE_CUDA_OK;
     drop_plan(v);
     std::unique_ptr<Plan> plan;
     ERNIE_TRY(plan_create(v, height, width, precision, plan));
-    // capture the whole decoder once; every later decode of this shape replays it
-    Program prog{v, *plan, v->ctx->stream, v->ctx->num_sms};
+    // capture the whole program once; every later call of this shape replays it
+    Program prog{v->ctx, *plan, v->ctx->stream, v->ctx->num_sms};
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamBeginCapture(v->ctx->stream, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess)
@@ -598,7 +770,7 @@ int ensure_plan(ernie_cuda_vae *v, int width, int height, int precision)
         free_plan(plan.get());
         return from_cuda(e, "Begin VAE capture");
     }
-    const int rc = prog.run();
+    const int rc = prog.run(v->layout);
     e = cudaStreamEndCapture(v->ctx->stream, &graph);
     if (rc != ERNIE_CUDA_OK || e != cudaSuccess)
     {
@@ -617,53 +789,52 @@ int ensure_plan(ernie_cuda_vae *v, int width, int height, int precision)
     return ERNIE_CUDA_OK;
 }
 
-int check_loaded(ernie_cuda_vae *v)
+template <class V> int check_loaded(V *v)
 {
     for (const auto &prm : v->layout.params)
         if (!prm.loaded) return fail(ERNIE_CUDA_ERROR, "VAE tensor not uploaded: " + prm.name);
     return ERNIE_CUDA_OK;
 }
 
-int run_decode(ernie_cuda_vae *v, int width, int height, int precision)
+template <class V> int run_graph(V *v, int width, int height, int precision)
 {
     ERNIE_TRY(check_loaded(v));
     ERNIE_TRY(ensure_plan(v, width, height, precision));
     Plan &p = *v->plan;
     ERNIE_CUDA(cudaMemsetAsync(p.nonfinite, 0, sizeof(int), v->ctx->stream), "clear flag");
-    ERNIE_CUDA(cudaGraphLaunch(p.graph, v->ctx->stream), "VAE decode");
+    ERNIE_CUDA(cudaGraphLaunch(p.graph, v->ctx->stream), "VAE graph");
     return ERNIE_CUDA_OK;
 }
 
-int read_status(ernie_cuda_vae *v, int *nonfinite)
+template <class V> int read_status(V *v, int *nonfinite)
 {
     int flags[2] = {0, 0};
     ERNIE_CUDA(cudaMemcpyAsync(&flags[0], v->plan->nonfinite, sizeof(int), cudaMemcpyDeviceToHost, v->ctx->stream),
                "read flag");
     ERNIE_CUDA(cudaMemcpyAsync(&flags[1], v->ctx->error_flag, sizeof(int), cudaMemcpyDeviceToHost, v->ctx->stream),
                "read status");
-    ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE decode");
+    ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE graph");
     if (flags[1]) return fail(ERNIE_CUDA_ERROR, "VAE kernel protocol timeout (status " + std::to_string(flags[1]) + ")");
     if (nonfinite) *nonfinite = flags[0];
     return ERNIE_CUDA_OK;
 }
-} // namespace
 
-extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **out)
+template <class V> int model_create(ernie_cuda_context *ctx, V **out)
 {
     if (!ctx || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
     *out = nullptr;
     DeviceGuard guard(ctx->device);
-    auto v = std::make_unique<ernie_cuda_vae>();
+    auto v = std::make_unique<V>();
     v->ctx = ctx;
-    Layout &L = v->layout;
+    auto &L = v->layout;
     Arena arena;
     size_t staging = 0;
     for (auto &prm : L.params) staging = std::max(staging, prm.count());
     arena.add(&v->staging, staging);
-    arena.add(&v->staging2, staging); // tap-expanded copy of conv_out's weights
+    arena.add(&v->staging2, staging); // re-ordered copy (tap-expanded or im2col weights)
     arena.add(&v->d_inexact, 1);
-    arena.add(&L.pq_w, 32 * 32);
-    arena.add(&L.pq_b, 32);
+    for (auto &prm : L.params)
+        if (prm.slot) arena.add(prm.slot, prm.count());
     for (ConvW *c : L.convs)
     {
         arena.add(&c->w, static_cast<size_t>(c->cout_rows) * 3 * c->dev_taps() * c->cin_pad);
@@ -677,7 +848,7 @@ extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **o
     v->bytes = arena.bytes();
     ERNIE_CUDA(arena.allocate(), "Allocate VAE weights");
     v->alloc = arena.base;
-    // zero padding rows/channels and the padded conv_out bias
+    // zero padding rows/channels and the padded biases
     cudaError_t e = cudaMemsetAsync(v->alloc, 0, arena.bytes(), ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess)
@@ -685,13 +856,12 @@ extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **o
         cudaFree(v->alloc);
         return from_cuda(e, "Clear VAE weights");
     }
-    // destinations of the FP32 vectors, in table order
+    // destinations of the FP32 vectors: the layout's own pointers, else GroupNorm gamma/beta in table order
     size_t norm_index = 0;
     for (auto &prm : L.params)
     {
         if (prm.role != Role::Vector) continue;
-        if (prm.name == "post_quant_conv.weight") prm.dst = L.pq_w;
-        else if (prm.name == "post_quant_conv.bias") prm.dst = L.pq_b;
+        if (prm.slot) prm.dst = *prm.slot;
         else
         {
             NormW *n = L.norms[norm_index / 2];
@@ -703,7 +873,7 @@ extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **o
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_destroy(ernie_cuda_vae *v)
+template <class V> int model_destroy(V *v)
 {
     if (!v) return ERNIE_CUDA_OK;
     DeviceGuard guard(v->ctx->device);
@@ -714,17 +884,17 @@ extern "C" int ernie_cuda_vae_destroy(ernie_cuda_vae *v)
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_tensor_count(int *count)
+template <class L> int table_count(int *count)
 {
     if (!count) return fail(ERNIE_CUDA_ERROR, "null argument");
-    static const Layout table;
+    static const L table;
     *count = static_cast<int>(table.params.size());
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim)
+template <class L> int table_info(int index, char *name, size_t name_bytes, int *dims, int *ndim)
 {
-    static const Layout table;
+    static const L table;
     if (index < 0 || index >= static_cast<int>(table.params.size()) || !name || !dims || !ndim)
         return fail(ERNIE_CUDA_ERROR, "Invalid VAE tensor index or null argument");
     const Param &prm = table.params[static_cast<size_t>(index)];
@@ -736,7 +906,7 @@ extern "C" int ernie_cuda_vae_tensor_info(int index, char *name, size_t name_byt
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_upload(ernie_cuda_vae *v, const char *name, const float *host, size_t count)
+template <class V> int model_upload(V *v, const char *name, const float *host, size_t count)
 {
     if (!v || !name || !host) return fail(ERNIE_CUDA_ERROR, "null argument");
     const int i = find_param(v, name);
@@ -745,6 +915,9 @@ extern "C" int ernie_cuda_vae_upload(ernie_cuda_vae *v, const char *name, const 
     if (count != prm.count()) return fail(ERNIE_CUDA_ERROR, "VAE tensor size differs: " + prm.name);
     for (size_t j = 0; j < count; ++j)
         if (!std::isfinite(host[j])) return fail(ERNIE_CUDA_ERROR, "VAE tensor is not finite: " + prm.name);
+    if (prm.name == "bn.running_var")
+        for (size_t j = 0; j < count; ++j)
+            if (!(host[j] >= 0.f)) return fail(ERNIE_CUDA_ERROR, "VAE tensor is negative: " + prm.name);
     DeviceGuard guard(v->ctx->device);
     ERNIE_CUDA(cudaMemcpyAsync(v->staging, host, count * 4, cudaMemcpyHostToDevice, v->ctx->stream), "upload");
     ERNIE_TRY(place(v, prm));
@@ -753,7 +926,7 @@ extern "C" int ernie_cuda_vae_upload(ernie_cuda_vae *v, const char *name, const 
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_synthesize(ernie_cuda_vae *v, uint64_t seed, int bf16_weights)
+template <class V> int model_synthesize(V *v, uint64_t seed, int bf16_weights)
 {
     if (!v) return fail(ERNIE_CUDA_ERROR, "null argument");
     DeviceGuard guard(v->ctx->device);
@@ -770,7 +943,7 @@ extern "C" int ernie_cuda_vae_synthesize(ernie_cuda_vae *v, uint64_t seed, int b
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_bytes(ernie_cuda_vae *v, uint64_t *weights, uint64_t *workspace)
+template <class V> int model_bytes(V *v, uint64_t *weights, uint64_t *workspace)
 {
     if (!v) return fail(ERNIE_CUDA_ERROR, "null argument");
     if (weights) *weights = v->bytes;
@@ -778,12 +951,10 @@ extern "C" int ernie_cuda_vae_bytes(ernie_cuda_vae *v, uint64_t *weights, uint64
     return ERNIE_CUDA_OK;
 }
 
-extern "C" int ernie_cuda_vae_launches(ernie_cuda_vae *v, int width, int height, int precision, int *launches)
+bool precision_ok(int precision) { return precision == ERNIE_PRECISION_BF16 || precision == ERNIE_PRECISION_FP32; }
+
+template <class V> int model_launches(V *v, int width, int height, int precision, int *launches)
 {
-    if (!v || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
-    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
-    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
-        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
     DeviceGuard guard(v->ctx->device);
     ERNIE_TRY(check_loaded(v));
     ERNIE_TRY(ensure_plan(v, width, height, precision));
@@ -791,20 +962,109 @@ extern "C" int ernie_cuda_vae_launches(ernie_cuda_vae *v, int width, int height,
     return ERNIE_CUDA_OK;
 }
 
+template <class V> int model_profile(V *v, int width, int height, int precision, int iters, double *ms, double *work)
+{
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    Profiler prof;
+    for (int c = 0; c < kProfClasses; ++c) ms[c] = work[c] = 0.0;
+    for (int it = 0; it < iters; ++it)
+    {
+        const int launches = p.launches;
+        prof.used = 0;
+        Program prog{v->ctx, p, v->ctx->stream, v->ctx->num_sms, &prof};
+        const int rc = prog.run(v->layout);
+        p.launches = launches;
+        ERNIE_TRY(rc);
+        ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE profile");
+        for (size_t i = 0; i < prof.used; ++i)
+        {
+            float t = 0.f;
+            ERNIE_CUDA(cudaEventElapsedTime(&t, prof.events[2 * i], prof.events[2 * i + 1]), "profile event");
+            ms[prof.classes[i]] += t / iters;
+            if (it == 0) work[prof.classes[i]] += prof.work[i];
+        }
+    }
+    return ERNIE_CUDA_OK;
+}
+
+// One encode with the RGB bytes and the three outputs at `kind` (host or device) addresses.
+int encode_impl(ernie_cuda_vae_encoder *v, const uint8_t *rgb, int width, int height, int precision, float *mean,
+                float *packed, float *normalized, int *nonfinite, cudaMemcpyKind in, cudaMemcpyKind out)
+{
+    if (!v || !rgb || !mean || !packed || !normalized) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!encoder_shape_ok(width, height))
+        return fail(ERNIE_CUDA_ERROR, "Unsupported VAE encoder image shape (sides multiples of 16, at most 2048)");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(v->ctx->device);
+    ERNIE_TRY(check_loaded(v));
+    ERNIE_TRY(ensure_plan(v, width, height, precision));
+    Plan &p = *v->plan;
+    const size_t px = pixels_of(height, width);
+    cudaStream_t stream = v->ctx->stream;
+    ERNIE_CUDA(cudaMemcpyAsync(p.rgb_in, rgb, 3 * px, in, stream), "encoder input");
+    ERNIE_TRY(run_graph(v, width, height, precision));
+    ERNIE_CUDA(cudaMemcpyAsync(mean, p.mean, 32 * px / 64 * 4, out, stream), "encoder mean");
+    ERNIE_CUDA(cudaMemcpyAsync(packed, p.packed, 128 * px / 256 * 4, out, stream), "encoder packed");
+    ERNIE_CUDA(cudaMemcpyAsync(normalized, p.normalized, 128 * px / 256 * 4, out, stream), "encoder normalized");
+    if (!nonfinite && out == cudaMemcpyDeviceToDevice) return ERNIE_CUDA_OK; // stays asynchronous
+    int flag = 0;
+    ERNIE_TRY(read_status(v, &flag));
+    if (nonfinite) *nonfinite = flag;
+    return ERNIE_CUDA_OK;
+}
+} // namespace
+
+// ---- VAE decoder ---------------------------------------------------------------------------------------
+extern "C" int ernie_cuda_vae_create(ernie_cuda_context *ctx, ernie_cuda_vae **out) { return model_create(ctx, out); }
+
+extern "C" int ernie_cuda_vae_destroy(ernie_cuda_vae *v) { return model_destroy(v); }
+
+extern "C" int ernie_cuda_vae_tensor_count(int *count) { return table_count<Layout>(count); }
+
+extern "C" int ernie_cuda_vae_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim)
+{
+    return table_info<Layout>(index, name, name_bytes, dims, ndim);
+}
+
+extern "C" int ernie_cuda_vae_upload(ernie_cuda_vae *v, const char *name, const float *host, size_t count)
+{
+    return model_upload(v, name, host, count);
+}
+
+extern "C" int ernie_cuda_vae_synthesize(ernie_cuda_vae *v, uint64_t seed, int bf16_weights)
+{
+    return model_synthesize(v, seed, bf16_weights);
+}
+
+extern "C" int ernie_cuda_vae_bytes(ernie_cuda_vae *v, uint64_t *weights, uint64_t *workspace)
+{
+    return model_bytes(v, weights, workspace);
+}
+
+extern "C" int ernie_cuda_vae_launches(ernie_cuda_vae *v, int width, int height, int precision, int *launches)
+{
+    if (!v || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    return model_launches(v, width, height, precision, launches);
+}
+
 extern "C" int ernie_cuda_vae_decode_device(ernie_cuda_vae *v, const float *unpacked, int width, int height,
                                             int precision, float *decoded, uint8_t *rgb, int *nonfinite)
 {
     if (!v || !unpacked || !decoded) return fail(ERNIE_CUDA_ERROR, "null argument");
     if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
-    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
-        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
     DeviceGuard guard(v->ctx->device);
     ERNIE_TRY(check_loaded(v));
     ERNIE_TRY(ensure_plan(v, width, height, precision));
     Plan &p = *v->plan;
     const size_t in = 32 * pixels_of(height, width), out = 3 * 64 * pixels_of(height, width);
     ERNIE_CUDA(cudaMemcpyAsync(p.input, unpacked, in * 4, cudaMemcpyDeviceToDevice, v->ctx->stream), "VAE input");
-    ERNIE_TRY(run_decode(v, width, height, precision));
+    ERNIE_TRY(run_graph(v, width, height, precision));
     ERNIE_CUDA(cudaMemcpyAsync(decoded, p.decoded, out * 4, cudaMemcpyDeviceToDevice, v->ctx->stream), "VAE output");
     if (rgb) ERNIE_CUDA(cudaMemcpyAsync(rgb, p.rgb, out, cudaMemcpyDeviceToDevice, v->ctx->stream), "RGB output");
     if (!nonfinite) return ERNIE_CUDA_OK; // stays asynchronous
@@ -816,15 +1076,14 @@ extern "C" int ernie_cuda_vae_decode(ernie_cuda_vae *v, const float *unpacked, i
 {
     if (!v || !unpacked || !decoded) return fail(ERNIE_CUDA_ERROR, "null argument");
     if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
-    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
-        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
     DeviceGuard guard(v->ctx->device);
     ERNIE_TRY(check_loaded(v));
     ERNIE_TRY(ensure_plan(v, width, height, precision));
     Plan &p = *v->plan;
     const size_t in = 32 * pixels_of(height, width), out = 3 * 64 * pixels_of(height, width);
     ERNIE_CUDA(cudaMemcpyAsync(p.input, unpacked, in * 4, cudaMemcpyHostToDevice, v->ctx->stream), "VAE input");
-    ERNIE_TRY(run_decode(v, width, height, precision));
+    ERNIE_TRY(run_graph(v, width, height, precision));
     ERNIE_CUDA(cudaMemcpyAsync(decoded, p.decoded, out * 4, cudaMemcpyDeviceToHost, v->ctx->stream), "VAE output");
     if (rgb) ERNIE_CUDA(cudaMemcpyAsync(rgb, p.rgb, out, cudaMemcpyDeviceToHost, v->ctx->stream), "RGB output");
     int flag = 0;
@@ -838,30 +1097,70 @@ extern "C" int ernie_cuda_vae_profile(ernie_cuda_vae *v, int width, int height, 
 {
     if (!v || !ms || !work || iters < 1) return fail(ERNIE_CUDA_ERROR, "null argument or iters < 1");
     if (!vae_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE latent shape");
-    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
-        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
-    DeviceGuard guard(v->ctx->device);
-    ERNIE_TRY(check_loaded(v));
-    ERNIE_TRY(ensure_plan(v, width, height, precision));
-    Plan &p = *v->plan;
-    Profiler prof;
-    for (int c = 0; c < kProfClasses; ++c) ms[c] = work[c] = 0.0;
-    for (int it = 0; it < iters; ++it)
-    {
-        const int launches = p.launches;
-        prof.used = 0;
-        Program prog{v, p, v->ctx->stream, v->ctx->num_sms, &prof};
-        const int rc = prog.run();
-        p.launches = launches;
-        ERNIE_TRY(rc);
-        ERNIE_CUDA(cudaStreamSynchronize(v->ctx->stream), "VAE profile");
-        for (size_t i = 0; i < prof.used; ++i)
-        {
-            float t = 0.f;
-            ERNIE_CUDA(cudaEventElapsedTime(&t, prof.events[2 * i], prof.events[2 * i + 1]), "profile event");
-            ms[prof.classes[i]] += t / iters;
-            if (it == 0) work[prof.classes[i]] += prof.work[i];
-        }
-    }
-    return ERNIE_CUDA_OK;
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    return model_profile(v, width, height, precision, iters, ms, work);
+}
+
+// ---- VAE encoder ---------------------------------------------------------------------------------------
+extern "C" int ernie_cuda_vae_encoder_create(ernie_cuda_context *ctx, ernie_cuda_vae_encoder **out)
+{
+    return model_create(ctx, out);
+}
+
+extern "C" int ernie_cuda_vae_encoder_destroy(ernie_cuda_vae_encoder *v) { return model_destroy(v); }
+
+extern "C" int ernie_cuda_vae_encoder_tensor_count(int *count) { return table_count<EncoderLayout>(count); }
+
+extern "C" int ernie_cuda_vae_encoder_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim)
+{
+    return table_info<EncoderLayout>(index, name, name_bytes, dims, ndim);
+}
+
+extern "C" int ernie_cuda_vae_encoder_upload(ernie_cuda_vae_encoder *v, const char *name, const float *host,
+                                             size_t count)
+{
+    return model_upload(v, name, host, count);
+}
+
+extern "C" int ernie_cuda_vae_encoder_synthesize(ernie_cuda_vae_encoder *v, uint64_t seed, int bf16_weights)
+{
+    return model_synthesize(v, seed, bf16_weights);
+}
+
+extern "C" int ernie_cuda_vae_encoder_bytes(ernie_cuda_vae_encoder *v, uint64_t *weights, uint64_t *workspace)
+{
+    return model_bytes(v, weights, workspace);
+}
+
+extern "C" int ernie_cuda_vae_encoder_launches(ernie_cuda_vae_encoder *v, int width, int height, int precision,
+                                               int *launches)
+{
+    if (!v || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!encoder_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE encoder image shape");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    return model_launches(v, width, height, precision, launches);
+}
+
+extern "C" int ernie_cuda_vae_encoder_profile(ernie_cuda_vae_encoder *v, int width, int height, int precision,
+                                              int iters, double *ms, double *work)
+{
+    if (!v || !ms || !work || iters < 1) return fail(ERNIE_CUDA_ERROR, "null argument or iters < 1");
+    if (!encoder_shape_ok(width, height)) return fail(ERNIE_CUDA_ERROR, "Unsupported VAE encoder image shape");
+    if (!precision_ok(precision)) return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    return model_profile(v, width, height, precision, iters, ms, work);
+}
+
+extern "C" int ernie_cuda_vae_encode(ernie_cuda_vae_encoder *v, const uint8_t *rgb, int width, int height,
+                                     int precision, float *mean, float *packed, float *normalized, int *nonfinite)
+{
+    return encode_impl(v, rgb, width, height, precision, mean, packed, normalized, nonfinite, cudaMemcpyHostToDevice,
+                       cudaMemcpyDeviceToHost);
+}
+
+extern "C" int ernie_cuda_vae_encode_device(ernie_cuda_vae_encoder *v, const uint8_t *rgb, int width, int height,
+                                            int precision, float *mean, float *packed, float *normalized,
+                                            int *nonfinite)
+{
+    return encode_impl(v, rgb, width, height, precision, mean, packed, normalized, nonfinite,
+                       cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice);
 }

@@ -142,6 +142,18 @@ SIGNATURES = {
     "ernie_cuda_vae_profile": (I, [P, I, I, I, I, P, P]),
     "ernie_cuda_vae_decode": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
     "ernie_cuda_vae_decode_device": (I, [P, P, I, I, I, P, P, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encoder_create": (I, [P, ctypes.POINTER(P)]),
+    "ernie_cuda_vae_encoder_destroy": (I, [P]),
+    "ernie_cuda_vae_encoder_tensor_count": (I, [ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encoder_tensor_info": (I, [I, ctypes.c_char_p, SZ, ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encoder_upload": (I, [P, ctypes.c_char_p, P, SZ]),
+    "ernie_cuda_vae_encoder_synthesize": (I, [P, U64, I]),
+    "ernie_cuda_vae_encoder_bytes": (I, [P, ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "ernie_cuda_vae_encoder_launches": (I, [P, I, I, I, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encoder_profile": (I, [P, I, I, I, I, P, P]),
+    "ernie_cuda_vae_encode": (I, [P, P, I, I, I, P, P, P, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encode_device": (I, [P, P, I, I, I, P, P, P, ctypes.POINTER(I)]),
+    "ernie_cuda_vae_encoder_load_safetensors": (I, [P, ctypes.POINTER(ctypes.c_char_p), I]),
 }
 
 
@@ -534,18 +546,27 @@ class TextModel:
         return b.value
 
 
-def vae_tensors():
-    """[(diffusers name, shape)] of every VAE decoder tensor the library holds, in execution order."""
+def _tensor_table(prefix):
     n = I(0)
-    check(lib().ernie_cuda_vae_tensor_count(ctypes.byref(n)))
+    check(getattr(lib(), prefix + "_tensor_count")(ctypes.byref(n)))
     out = []
     for i in range(n.value):
         name = ctypes.create_string_buffer(128)
         dims = (I * 4)()
         nd = I(0)
-        check(lib().ernie_cuda_vae_tensor_info(i, name, 128, dims, ctypes.byref(nd)))
+        check(getattr(lib(), prefix + "_tensor_info")(i, name, 128, dims, ctypes.byref(nd)))
         out.append((name.value.decode(), tuple(dims[j] for j in range(nd.value))))
     return out
+
+
+def vae_tensors():
+    """[(diffusers name, shape)] of every VAE decoder tensor the library holds, in execution order."""
+    return _tensor_table("ernie_cuda_vae")
+
+
+def vae_encoder_tensors():
+    """[(diffusers name, shape)] of every VAE encoder tensor the library holds, in execution order."""
+    return _tensor_table("ernie_cuda_vae_encoder")
 
 
 class Vae:
@@ -606,6 +627,68 @@ class Vae:
         """Asynchronous decode between device buffers (Buffer objects) on the context's stream."""
         check(lib().ernie_cuda_vae_decode_device(self.handle, unpacked_dev.c, width, height, precision,
                                                  decoded_dev.c, rgb_dev.c if rgb_dev is not None else None, None))
+
+
+class VaeEncoder:
+    """Device-resident VAE encoder (encode_vae of src/image_encoder.h on the B200): img2img's image latent."""
+
+    def __init__(self, ctx):
+        h = P()
+        check(lib().ernie_cuda_vae_encoder_create(ctx.handle, ctypes.byref(h)))
+        self.handle, self.ctx = h, ctx
+
+    def close(self):
+        if self.handle:
+            lib().ernie_cuda_vae_encoder_destroy(self.handle)
+            self.handle = None
+
+    def synthesize(self, seed, bf16_weights=False):
+        check(lib().ernie_cuda_vae_encoder_synthesize(self.handle, seed, 1 if bf16_weights else 0))
+
+    def load_safetensors(self, files):
+        """The official VAE checkpoint's encoder.*, quant_conv.* and bn.running_* tensors."""
+        arr, n = _paths(files)
+        check(lib().ernie_cuda_vae_encoder_load_safetensors(self.handle, arr, n))
+
+    def upload(self, name, array):
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        check(lib().ernie_cuda_vae_encoder_upload(self.handle, name.encode(), ptr(a), a.size))
+
+    def nbytes(self):
+        w, ws = U64(0), U64(0)
+        check(lib().ernie_cuda_vae_encoder_bytes(self.handle, ctypes.byref(w), ctypes.byref(ws)))
+        return w.value, ws.value
+
+    def launches(self, width, height, precision=BF16):
+        n = I(0)
+        check(lib().ernie_cuda_vae_encoder_launches(self.handle, width, height, precision, ctypes.byref(n)))
+        return n.value
+
+    PROFILE_CLASSES = ("conv", "attention_gemm", "softmax", "group_norm", "downsample", "other")
+
+    def profile(self, width, height, precision=BF16, iters=3):
+        """{class: (mean ms, algorithmic work: FLOPs for conv/attention_gemm, bytes otherwise)}."""
+        ms, work = np.zeros(6, np.float64), np.zeros(6, np.float64)
+        check(lib().ernie_cuda_vae_encoder_profile(self.handle, width, height, precision, iters, ptr(ms),
+                                                   ptr(work)))
+        return {c: (float(ms[i]), float(work[i])) for i, c in enumerate(self.PROFILE_CLASSES)}
+
+    def encode(self, rgb, precision=BF16):
+        """RGB bytes [h, w, 3] -> (mean [32, h/8, w/8], packed [128, h/16, w/16], normalized, nonfinite)."""
+        x = np.ascontiguousarray(rgb, dtype=np.uint8)
+        h, w, _ = x.shape
+        mean = np.empty((32, h // 8, w // 8), np.float32)
+        packed = np.empty((128, h // 16, w // 16), np.float32)
+        normalized = np.empty_like(packed)
+        flag = I(0)
+        check(lib().ernie_cuda_vae_encode(self.handle, ptr(x), w, h, precision, ptr(mean), ptr(packed),
+                                          ptr(normalized), ctypes.byref(flag)))
+        return mean, packed, normalized, flag.value
+
+    def encode_device(self, rgb_dev, width, height, mean_dev, packed_dev, normalized_dev, precision=BF16):
+        """Asynchronous encode between device buffers (Buffer objects) on the context's stream."""
+        check(lib().ernie_cuda_vae_encode_device(self.handle, rgb_dev.c, width, height, precision, mean_dev.c,
+                                                 packed_dev.c, normalized_dev.c, None))
 
 
 def initial_noise(seed, width, height):

@@ -1085,6 +1085,72 @@ VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor
     return result;
 }
 
+// ---- the VAE encoder ---------------------------------------------------------------------------------
+VaeEncoder::VaeEncoder(GpuContext &ctx) : ctx_(ctx)
+{
+    require(ctx.available(), "VAE encoder needs a CUDA device");
+    check_cuda(ernie_cuda_vae_encoder_create(ctx.handle(), &handle_), "create VAE encoder");
+}
+
+VaeEncoder::~VaeEncoder()
+{
+    if (handle_) ernie_cuda_vae_encoder_destroy(handle_);
+}
+
+std::vector<std::pair<std::string, std::vector<int>>> VaeEncoder::tensors()
+{
+    int count = 0;
+    check_cuda(ernie_cuda_vae_encoder_tensor_count(&count), "VAE encoder tensor count");
+    std::vector<std::pair<std::string, std::vector<int>>> out;
+    for (int i = 0; i < count; ++i)
+    {
+        char name[128];
+        int dims[4] = {0, 0, 0, 0}, ndim = 0;
+        check_cuda(ernie_cuda_vae_encoder_tensor_info(i, name, sizeof(name), dims, &ndim), "VAE encoder tensor info");
+        out.emplace_back(name, std::vector<int>(dims, dims + ndim));
+    }
+    return out;
+}
+
+void VaeEncoder::upload(const std::string &name, const Tensor &value)
+{
+    const int rc = ernie_cuda_vae_encoder_upload(handle_, name.c_str(), value.ptr(), value.total());
+    if (rc == ERNIE_CUDA_ERROR) throw std::invalid_argument(ernie_cuda_last_error());
+    check_cuda(rc, "upload VAE encoder tensor");
+}
+
+void VaeEncoder::synthesize(uint64_t seed, bool bf16_weights)
+{
+    check_cuda(ernie_cuda_vae_encoder_synthesize(handle_, seed, bf16_weights ? 1 : 0), "synthesize VAE encoder");
+}
+
+VaeEncoding encode_vae(VaeEncoder &encoder, const RgbImage &rgb, Precision precision)
+{
+    const bool shape_ok = rgb.width >= 16 && rgb.height >= 16 && rgb.width % 16 == 0 && rgb.height % 16 == 0 &&
+                          rgb.width <= 2048 && rgb.height <= 2048;
+    if (!shape_ok || rgb.pixels.size() != size_t(rgb.width) * size_t(rgb.height) * 3)
+        throw std::invalid_argument("RGB shape has no VAE encoder program");
+    VaeEncoding out;
+    out.mean = Tensor(rgb.width / 8, rgb.height / 8, 32);
+    out.packed = Tensor(rgb.width / 16, rgb.height / 16, 128);
+    out.normalized = Tensor(rgb.width / 16, rgb.height / 16, 128);
+    int nonfinite = 0;
+    check_cuda(ernie_cuda_vae_encode(encoder.handle(), rgb.pixels.data(), rgb.width, rgb.height,
+                                     precision_code(precision), out.mean.ptr(), out.packed.ptr(),
+                                     out.normalized.ptr(), &nonfinite),
+               "Encode VAE");
+    if (nonfinite)
+    {
+        const std::pair<const char *, const Tensor *> outputs[3] = {
+            {"mean", &out.mean}, {"packed", &out.packed}, {"normalized", &out.normalized}};
+        for (const auto &o : outputs)
+            for (float v : o.second->data)
+                if (!std::isfinite(v)) throw std::runtime_error(std::string("Non-finite VAE encoder ") + o.first);
+        throw std::runtime_error("Non-finite VAE encoder output");
+    }
+    return out;
+}
+
 // ---- the prompt encoder -----------------------------------------------------------------------------
 namespace
 {
@@ -1200,6 +1266,14 @@ void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files)
                   "load VAE checkpoint");
 }
 
+void load_safetensors(VaeEncoder &encoder, const std::vector<std::string> &files)
+{
+    const auto paths = c_paths(files);
+    check_request(
+        ernie_cuda_vae_encoder_load_safetensors(encoder.handle(), paths.data(), static_cast<int>(paths.size())),
+        "load VAE encoder checkpoint");
+}
+
 GeneratedImage generate_from_ids(GenerationModels &m, const std::vector<uint32_t> &ids, int text_bucket,
                                  const DitStageRequest &request,
                                  const std::function<void(const DitStageProgress &)> &notify)
@@ -1225,6 +1299,56 @@ GeneratedImage generate_from_ids(GenerationModels &m, const std::vector<uint32_t
     out.vae_seconds = vae.seconds;
     out.decoded = std::move(vae.decoded);
     out.image = std::move(vae.image);
+    out.elapsed_seconds = seconds_since(start);
+    return out;
+}
+GeneratedImage generate_img2img_from_ids(GenerationModels &m, const std::vector<uint32_t> &ids, int text_bucket,
+                                         const RgbImage &input, const DitStageRequest &request,
+                                         const std::function<void(const DitStageProgress &)> &notify)
+{
+    const auto start = Clock::now();
+    if (!m.encoder) throw std::invalid_argument("Selected model package has no img2img encoder");
+    if (!std::isfinite(request.strength) || request.strength < 0.f || request.strength > 1.f)
+        throw std::invalid_argument("img2img strength must be in [0,1]");
+    if (input.width != request.width || input.height != request.height)
+        throw std::invalid_argument("Invalid img2img resize identity");
+    const VaeEncoding encoding = encode_vae(*m.encoder, input, request.precision);
+    const double encoder_seconds = seconds_since(start);
+    if (!request.trace.empty())
+    {
+        const std::filesystem::path folder(request.trace);
+        const auto rgb_path = folder / "input.rgb";
+        if (std::filesystem::exists(rgb_path)) throw std::runtime_error("Trace file exists");
+        std::ofstream rgb(rgb_path, std::ios::binary);
+        if (!rgb.write(reinterpret_cast<const char *>(input.pixels.data()), std::streamsize(input.pixels.size())))
+            throw std::runtime_error("Cannot write img2img input trace");
+        const auto text_path = folder / "img2img.txt";
+        if (std::filesystem::exists(text_path)) throw std::runtime_error("Trace file exists");
+        std::ofstream text(text_path);
+        text << "source_width=" << input.width << "\nsource_height=" << input.height << "\nwidth=" << input.width
+             << "\nheight=" << input.height << "\nstrength=" << std::to_string(request.strength) << "\n";
+        if (!text) throw std::runtime_error("Cannot write img2img input trace");
+        write_tensor((folder / "encoder-mean.f32").string(), encoding.mean);
+        write_tensor((folder / "encoder-packed.f32").string(), encoding.packed);
+        write_tensor((folder / "encoder-normalized.f32").string(), encoding.normalized);
+    }
+    if (request.strength == 0.f)
+    {
+        // strength 0: the encoded image decoded straight back (src/pipeline.cpp:419-436)
+        GeneratedImage out;
+        VaeStageResult vae =
+            run_vae_stage(m.vae, encoding.normalized, m.bn_mean, m.bn_variance, request.precision, request.trace);
+        out.latent = encoding.normalized;
+        out.start_step = request.steps; // no step runs
+        out.decoded = std::move(vae.decoded);
+        out.image = std::move(vae.image);
+        out.vae_seconds = encoder_seconds + vae.seconds;
+        out.elapsed_seconds = seconds_since(start);
+        return out;
+    }
+    DitStageRequest r = request;
+    r.encoded = encoding.normalized;
+    GeneratedImage out = generate_from_ids(m, ids, text_bucket, r, notify);
     out.elapsed_seconds = seconds_since(start);
     return out;
 }

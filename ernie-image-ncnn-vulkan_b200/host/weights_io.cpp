@@ -508,6 +508,28 @@ extern "C" int ernie_cuda_vae_load_safetensors(ernie_cuda_vae *vae, const char *
     });
 }
 
+extern "C" int ernie_cuda_vae_encoder_load_safetensors(ernie_cuda_vae_encoder *encoder, const char *const *files,
+                                                       int count)
+{
+    return guarded([&] {
+        if (!encoder) return fail_weights("null VAE encoder");
+        Checkpoint ck(files, count);
+        int n = 0;
+        ernie_cuda_vae_encoder_tensor_count(&n);
+        for (int i = 0; i < n; ++i)
+        {
+            char name[128];
+            int dims[4] = {0, 0, 0, 0}, nd = 0;
+            ernie_cuda_vae_encoder_tensor_info(i, name, sizeof(name), dims, &nd);
+            const auto v = ck.f32(name, std::vector<int64_t>(dims, dims + nd));
+            const int rc = forward(ernie_cuda_vae_encoder_upload(encoder, name, v.data(), v.size()),
+                                   "upload VAE encoder tensor");
+            if (rc != ERNIE_CUDA_OK) return rc;
+        }
+        return ERNIE_CUDA_OK;
+    });
+}
+
 extern "C" int ernie_cuda_text_embeddings(const char *path, const uint32_t *ids, int count, int bucket, float *out)
 {
     return guarded([&] {

@@ -484,6 +484,39 @@ struct VaeStageResult
 VaeStageResult run_vae_stage(VaeDecoder &vae, const Tensor &latent, const Tensor &mean, const Tensor &variance,
                              Precision precision = Precision::BF16, const std::string &trace = {});
 
+// ---- the VAE encoder (src/image_encoder.h:9-20): img2img's image latent ----------------------------
+struct VaeEncoding // src/image_encoder.h:9-14
+{
+    Tensor mean;       // [32][H/8][W/8]: quant_conv(encoder(x))[:32], the posterior's mode
+    Tensor packed;     // [128][H/16][W/16]: pixel_unshuffle(mean, 2)
+    Tensor normalized; // [128][H/16][W/16]: BatchNorm(packed), make_img2img_start's `encoded`
+};
+// The AutoencoderKLFlux2 encoder + quant_conv + bn the reference exports (tools/export_vae_encoder.py),
+// weights resident on the device and addressed by their diffusers names (FP32).
+class VaeEncoder
+{
+  public:
+    explicit VaeEncoder(GpuContext &ctx);
+    ~VaeEncoder();
+    VaeEncoder(const VaeEncoder &) = delete;
+    VaeEncoder &operator=(const VaeEncoder &) = delete;
+    static std::vector<std::pair<std::string, std::vector<int>>> tensors();
+    void upload(const std::string &name, const Tensor &value);
+    void synthesize(uint64_t seed, bool bf16_weights = false);
+    GpuContext &context() const { return ctx_; }
+    ernie_cuda_vae_encoder *handle() const noexcept { return handle_; }
+
+  private:
+    GpuContext &ctx_;
+    ernie_cuda_vae_encoder *handle_ = nullptr;
+};
+// encode_vae (src/image_encoder.cpp:29-72) on the B200. std::invalid_argument for pixels that are not
+// width * height * 3 bytes or sides that are not multiples of 16 in [16, 2048] (the reference admits only
+// its reviewed 32x32, 64x32, 512x384 and 1024x1024); std::runtime_error "Non-finite VAE encoder ..." for a
+// non-finite output, as validate_output throws. FP32-exact mode is the parity mode of the reference's CPU
+// FP32 contract; BF16 mode uses BF16 convolution operands.
+VaeEncoding encode_vae(VaeEncoder &encoder, const RgbImage &rgb, Precision precision = Precision::FP32);
+
 // ---- the prompt encoder (src/text_encoder.h:8-26) ------------------------------------------------
 // text_embeddings: the rows of ids from the [131072][3072] BF16 table (the reference's raw
 // "text/embeddings.bf16" file, or a checkpoint .safetensors with language_model.model.embed_tokens.weight)
@@ -530,6 +563,7 @@ struct GenerationModels // the device-resident stages and the package's small ta
     std::vector<float> dit_frequencies;   // dit/rope-inv-freq.f32 (empty: the built-in table)
     Tensor bn_mean, bn_variance;          // vae/bn-mean.f32, vae/bn-variance.f32 ([128])
     int dit_text_tokens = 0;              // model.cfg dit_text_tokens
+    VaeEncoder *encoder = nullptr;        // img2img only (vae/encoder.*)
 };
 struct GeneratedImage
 {
@@ -546,8 +580,17 @@ struct GeneratedImage
 GeneratedImage generate_from_ids(GenerationModels &models, const std::vector<uint32_t> &ids, int text_bucket,
                                  const DitStageRequest &request,
                                  const std::function<void(const DitStageProgress &)> &notify = {});
+// img2img (src/pipeline.cpp:341-345, :392-437, :536-540): the input image (request.width x request.height)
+// through models.encoder; strength 0 decodes the encoded latent straight back (no prompt, no DiT), otherwise
+// the encoded latent is request.encoded for the DiT stage's start step. Traces as the reference writes them:
+// input.rgb, img2img.txt, encoder-mean/packed/normalized.f32. std::invalid_argument without an encoder, for a
+// strength outside [0, 1] or an image whose size differs from the request's.
+GeneratedImage generate_img2img_from_ids(GenerationModels &models, const std::vector<uint32_t> &ids,
+                                         int text_bucket, const RgbImage &input, const DitStageRequest &request,
+                                         const std::function<void(const DitStageProgress &)> &notify = {});
 
 // ---- official checkpoints (safetensors) ------------------------------------------------------------
 void load_safetensors(DitModel &model, const std::vector<std::string> &files, bool heads = true);
 void load_safetensors(VaeDecoder &vae, const std::vector<std::string> &files);
+void load_safetensors(VaeEncoder &encoder, const std::vector<std::string> &files);
 } // namespace ernie

@@ -49,6 +49,7 @@ typedef struct ernie_cuda_model ernie_cuda_model;
 typedef struct ernie_cuda_session ernie_cuda_session;
 typedef struct ernie_cuda_text_model ernie_cuda_text_model; /* prompt encoder layers (Text encoder section) */
 typedef struct ernie_cuda_vae ernie_cuda_vae;               /* VAE decoder (VAE decoder section) */
+typedef struct ernie_cuda_vae_encoder ernie_cuda_vae_encoder; /* VAE encoder (VAE encoder section) */
 
 /* Host weights of one block, as tools/build_dit_weights.py:19-31 binds them to the block graph. */
 typedef struct
@@ -253,12 +254,15 @@ int ernie_cuda_text_embeddings(const char *path, const uint32_t *ids, int count,
            (tools/export_dit_heads.py:19).
      Text: language_model.model.layers.{l}.{self_attn.q/k/v/o_proj, mlp.gate/up/down_proj,
            input_layernorm, post_attention_layernorm}.weight for l < num_layers.
-     VAE:  every name of ernie_cuda_vae_tensor_info (post_quant_conv.*, decoder.*). */
+     VAE:  every name of ernie_cuda_vae_tensor_info (post_quant_conv.*, decoder.*).
+     VAE encoder: every name of ernie_cuda_vae_encoder_tensor_info (encoder.*, quant_conv.*,
+           bn.running_mean, bn.running_var). */
 int ernie_cuda_model_load_safetensors(ernie_cuda_model *model, int num_blocks, const char *const *files, int count,
                                       int with_heads);
 int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *model, int num_layers, const char *const *files,
                                            int count);
 int ernie_cuda_vae_load_safetensors(ernie_cuda_vae *vae, const char *const *files, int count);
+int ernie_cuda_vae_encoder_load_safetensors(ernie_cuda_vae_encoder *encoder, const char *const *files, int count);
 /* The header of one file: the number of tensors, and tensor `index` (in name order): name, dtype
    ("BF16", "F16", "F32", ...; 8 bytes), shape (up to 8 dims). */
 int ernie_cuda_safetensors_count(const char *path, int *count);
@@ -301,6 +305,37 @@ int ernie_cuda_vae_decode(ernie_cuda_vae *vae, const float *unpacked, int width,
 /* Device buffers on the context's stream; synchronous only when nonfinite is non-null. */
 int ernie_cuda_vae_decode_device(ernie_cuda_vae *vae, const float *unpacked, int width, int height, int precision,
                                  float *decoded, uint8_t *rgb, int *nonfinite);
+
+/* ---- VAE encoder (img2img's image latent) -------------------------------------------------------
+   encode_vae (src/image_encoder.h:9-20, src/image_encoder.cpp:29-72) of the pinned AutoencoderKLFlux2
+   encoder + quant_conv + bn as tools/export_vae_encoder.py:74-80 wraps it, on one B200. Input: RGB bytes
+   [height][width][3], normalised as (v - 127.5f) * (1 / 127.5f). Outputs (the reference's VaeEncoding,
+   FP32 planar): mean [32][height/8][width/8] (quant_conv(encoder(x))[:32], the posterior's mode), packed
+   = pixel_unshuffle(mean, 2) [128][height/16][width/16], normalized = (packed - bn.running_mean) /
+   sqrt(bn.running_var + 1e-4) [128][height/16][width/16] (make_img2img_start's `encoded`). *nonfinite
+   (nullable) is set to 1 when an output is not finite (the reference throws there). Sides are multiples
+   of 16 up to 2048 (the reference admits its reviewed 32x32, 64x32, 512x384 and 1024x1024). Weights by
+   diffusers name (ernie_cuda_vae_encoder_tensor_info), uploaded as FP32. precision as for the decoder;
+   the reference's encoder is CPU FP32 only, so FP32-exact mode is its parity mode. */
+int ernie_cuda_vae_encoder_create(ernie_cuda_context *ctx, ernie_cuda_vae_encoder **out);
+int ernie_cuda_vae_encoder_destroy(ernie_cuda_vae_encoder *encoder);
+int ernie_cuda_vae_encoder_tensor_count(int *count);
+int ernie_cuda_vae_encoder_tensor_info(int index, char *name, size_t name_bytes, int *dims, int *ndim);
+int ernie_cuda_vae_encoder_upload(ernie_cuda_vae_encoder *encoder, const char *name, const float *host, size_t count);
+/* Seeded random-init weights (include/ernie_synth.h, VAE section; bn.running_var = 1 + 0.1 N(0,1)). */
+int ernie_cuda_vae_encoder_synthesize(ernie_cuda_vae_encoder *encoder, uint64_t seed, int bf16_weights);
+int ernie_cuda_vae_encoder_bytes(ernie_cuda_vae_encoder *encoder, uint64_t *weights, uint64_t *workspace);
+int ernie_cuda_vae_encoder_launches(ernie_cuda_vae_encoder *encoder, int width, int height, int precision,
+                                    int *launches);
+/* As ernie_cuda_vae_profile; class 4 is the stride-2 convolutions' operand pass. */
+int ernie_cuda_vae_encoder_profile(ernie_cuda_vae_encoder *encoder, int width, int height, int precision, int iters,
+                                   double *ms, double *work);
+/* Host buffers, synchronous. */
+int ernie_cuda_vae_encode(ernie_cuda_vae_encoder *encoder, const uint8_t *rgb, int width, int height, int precision,
+                          float *mean, float *packed, float *normalized, int *nonfinite);
+/* Device buffers on the context's stream; synchronous only when nonfinite is non-null. */
+int ernie_cuda_vae_encode_device(ernie_cuda_vae_encoder *encoder, const uint8_t *rgb, int width, int height,
+                                 int precision, float *mean, float *packed, float *normalized, int *nonfinite);
 
 /* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 members, BF16) ---------------
    Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every member

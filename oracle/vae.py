@@ -1,4 +1,4 @@
-"""CPU restatement of the VAE decoder stage — TEST INFRASTRUCTURE ONLY.
+"""CPU restatement of the VAE decoder and encoder stages — TEST INFRASTRUCTURE ONLY.
 
 Only tests/ and bench.py's CPU-baseline leg use this module, as the checker; the CUDA product never
 imports it.
@@ -19,10 +19,20 @@ What it restates:
 * Swish as ncnn evaluates it: x / (1 + exp(-x)).
 * rgb_image (src/pipeline.cpp:145-163): byte = nearbyint(clamp(x / 2 + 0.5, 0, 1) * 255) in FP32,
   non-finite values rejected.
+* encode_vae (src/image_encoder.cpp:29-72): RGB bytes -> (v - 127.5f) * (1 / 127.5f) in FP32
+  (image_encoder.cpp:44-51, tools/export_vae_encoder.py:30-34), then the traced wrapper of
+  tools/export_vae_encoder.py:74-80 over the same pinned AutoencoderKLFlux2: mean =
+  quant_conv(encoder(x))[:32] (the posterior's mode), packed = pixel_unshuffle(mean, 2), normalized =
+  BatchNorm2d(128, eps 1e-4, affine=False, eval) of packed. The published encoder: conv_in 3x3 3->128;
+  four down blocks of two resnets (128, 256, 512, 512 channels) with a 3x3 stride-2 convolution after
+  the first three, its input padded by one zero row and column at the bottom and right; the same mid
+  block as the decoder; GroupNorm + Swish; conv_out 3x3 512->64.
 
 The arithmetic is float64 throughout (the reference's CPU path is FP32); the reference's gates absorb
 the difference. Parity of values is unpinned: the reference ships no decoder output fixture (the
-fixture's in0/out0 tensors are not in its tree); the graph's topology is pinned by the golden JSON.
+fixture's in0/out0 tensors are not in its tree); the decoder graph's topology is pinned by the golden
+JSON. The encoder has neither an exported graph nor output tensors in the reference tree: its topology
+follows the export script's wrapper and the published architecture, and its values are unpinned too.
 
 Synthetic weights follow include/ernie_synth.h's VAE rule (stream = FNV-1a 64 of the diffusers name).
 """
@@ -32,6 +42,56 @@ from oracle import synth_normal
 
 GROUPS, EPS, WIDTH = 32, 1e-6, 512
 UP_OUT = (512, 512, 256, 128)
+DOWN_OUT = (128, 256, 512, 512)
+BN_EPS = 1e-4  # the encoder's BatchNorm (tools/export_vae_encoder.py:59,91)
+
+
+class _Table:
+    """Builder of [(diffusers name, shape)] lists."""
+
+    def __init__(self):
+        self.t = []
+
+    def conv(self, name, cin, cout, k):
+        self.t.extend([(name + ".weight", (cout, cin, k, k)), (name + ".bias", (cout,))])
+
+    def norm(self, name, c):
+        self.t.extend([(name + ".weight", (c,)), (name + ".bias", (c,))])
+
+    def resnet(self, name, cin, cout):
+        self.norm(name + ".norm1", cin)
+        self.conv(name + ".conv1", cin, cout, 3)
+        self.norm(name + ".norm2", cout)
+        self.conv(name + ".conv2", cout, cout, 3)
+        if cin != cout:
+            self.conv(name + ".conv_shortcut", cin, cout, 1)
+
+    def mid_block(self, prefix):
+        self.resnet(prefix + "mid_block.resnets.0", 512, 512)
+        a = prefix + "mid_block.attentions.0."
+        self.norm(a + "group_norm", 512)
+        for p in ("to_q", "to_k", "to_v", "to_out.0"):
+            self.t.extend([(a + p + ".weight", (512, 512)), (a + p + ".bias", (512,))])
+        self.resnet(prefix + "mid_block.resnets.1", 512, 512)
+
+
+def encoder_table():
+    """[(diffusers name, shape)] of the encoder + quant_conv + bn in execution order."""
+    b = _Table()
+    b.conv("encoder.conv_in", 3, 128, 3)
+    c = 128
+    for i, cout in enumerate(DOWN_OUT):
+        for j in range(2):
+            b.resnet(f"encoder.down_blocks.{i}.resnets.{j}", c, cout)
+            c = cout
+        if i < 3:
+            b.conv(f"encoder.down_blocks.{i}.downsamplers.0.conv", c, c, 3)
+    b.mid_block("encoder.")
+    b.norm("encoder.conv_norm_out", 512)
+    b.conv("encoder.conv_out", 512, 64, 3)
+    b.conv("quant_conv", 64, 64, 1)
+    b.t.extend([("bn.running_mean", (128,)), ("bn.running_var", (128,))])
+    return b.t
 
 
 def tensor_table():
@@ -83,7 +143,10 @@ def synth_rule(name, shape):
     """(scale, offset, is a convolution/projection weight) of include/ernie_synth.h's VAE rule."""
     if len(shape) >= 2:
         fan_in = int(np.prod(shape[1:]))
-        return np.float32(1.0) / np.sqrt(np.float32(fan_in)), np.float32(0.0), not name.startswith("post_quant")
+        fp32_layer = name.startswith(("post_quant_conv", "quant_conv"))  # computed in FP32, never rounded
+        return np.float32(1.0) / np.sqrt(np.float32(fan_in)), np.float32(0.0), not fp32_layer
+    if name == "bn.running_var":
+        return np.float32(0.1), np.float32(1.0), False
     if "norm" in name:
         return np.float32(0.1), np.float32(1.0 if name.endswith(".weight") else 0.0), False
     return np.float32(0.02), np.float32(0.0), False
@@ -95,10 +158,11 @@ def bf16_round(x):
     return rounded.astype(np.uint32).view(np.float32)
 
 
-def synth_weights(seed, bf16_weights=False):
-    """{name: float32 array} as ernie_cuda_vae_synthesize makes them."""
+def synth_weights(seed, bf16_weights=False, table=None):
+    """{name: float32 array} as ernie_cuda_vae_synthesize (ernie_cuda_vae_encoder_synthesize with
+    table=encoder_table()) makes them."""
     out = {}
-    for name, shape in tensor_table():
+    for name, shape in (table if table is not None else tensor_table()):
         scale, offset, is_weight = synth_rule(name, shape)
         v = synth_normal(seed, name_stream(name), int(np.prod(shape)), float(scale)) + offset
         if bf16_weights and is_weight:
@@ -148,8 +212,7 @@ def resnet(w, name, x):
     return x + h
 
 
-def attention(w, x):
-    a = "decoder.mid_block.attentions.0."
+def attention(w, x, a="decoder.mid_block.attentions.0."):
     c, h, wd = x.shape
     t = group_norm(x, w[a + "group_norm.weight"], w[a + "group_norm.bias"]).reshape(c, h * wd).T
 
@@ -189,3 +252,57 @@ def rgb_image(decoded):
         raise ValueError("VAE produced non-finite pixels")
     n = np.clip(d / np.float32(2.0) + np.float32(0.5), np.float32(0.0), np.float32(1.0))
     return np.rint(n * np.float32(255.0)).astype(np.uint8).transpose(1, 2, 0).copy()
+
+
+# ---- encoder -------------------------------------------------------------------------------------------
+def normalize_rgb(rgb):
+    """RGB bytes [H][W][3] -> FP32 [3][H][W] as (v - 127.5f) * (1 / 127.5f) (src/image_encoder.cpp:44-51)."""
+    v = np.asarray(rgb, np.uint8).astype(np.float32)
+    return ((v - np.float32(127.5)) * np.float32(1.0 / 127.5)).transpose(2, 0, 1).copy()
+
+
+def downsample(x, w, b):
+    """Downsample2D(padding=0): zero row/column appended at the bottom/right, then a 3x3 stride-2 conv."""
+    c, h, wd = x.shape
+    o = w.shape[0]
+    xp = np.pad(x, ((0, 0), (0, 1), (0, 1)))
+    oh, ow = h // 2, wd // 2
+    cols = np.empty((c, 9, oh, ow))
+    for ky in range(3):
+        for kx in range(3):
+            cols[:, ky * 3 + kx] = xp[:, ky:ky + 2 * oh:2, kx:kx + 2 * ow:2]
+    y = np.asarray(w, np.float64).reshape(o, c * 9) @ cols.reshape(c * 9, oh * ow)
+    return (y + np.asarray(b, np.float64)[:, None]).reshape(o, oh, ow)
+
+
+def pixel_unshuffle(x, r=2):
+    """out[c * r * r + i * r + j][y][x] = in[c][y * r + i][x * r + j] (torch pixel_unshuffle)."""
+    c, h, wd = x.shape
+    return x.reshape(c, h // r, r, wd // r, r).transpose(0, 2, 4, 1, 3).reshape(c * r * r, h // r, wd // r)
+
+
+def encode(w, rgb):
+    """(mean [32][H/8][W/8], packed [128][H/16][W/16], normalized [128][H/16][W/16]) in float64."""
+    x = conv2d(normalize_rgb(rgb).astype(np.float64), w["encoder.conv_in.weight"], w["encoder.conv_in.bias"])
+    for i in range(4):
+        for j in range(2):
+            x = resnet(w, f"encoder.down_blocks.{i}.resnets.{j}", x)
+        if i < 3:
+            x = downsample(x, w[f"encoder.down_blocks.{i}.downsamplers.0.conv.weight"],
+                           w[f"encoder.down_blocks.{i}.downsamplers.0.conv.bias"])
+    x = resnet(w, "encoder.mid_block.resnets.0", x)
+    x = attention(w, x, "encoder.mid_block.attentions.0.")
+    x = resnet(w, "encoder.mid_block.resnets.1", x)
+    x = swish(group_norm(x, w["encoder.conv_norm_out.weight"], w["encoder.conv_norm_out.bias"]))
+    x = conv2d(x, w["encoder.conv_out.weight"], w["encoder.conv_out.bias"])
+    mean = conv2d(x, w["quant_conv.weight"], w["quant_conv.bias"])[:32]
+    packed = pixel_unshuffle(mean)
+    rm = np.asarray(w["bn.running_mean"], np.float64)[:, None, None]
+    rv = np.asarray(w["bn.running_var"], np.float64)[:, None, None]
+    return mean, packed, (packed - rm) / np.sqrt(rv + BN_EPS)
+
+
+def rgb_fixture(width, height):
+    """Deterministic RGB test pattern of the reference's encoder fixtures (tools/export_vae_encoder.py:24-27)."""
+    y, x, c = np.indices((height, width, 3), dtype=np.int32)
+    return ((13 * x + 29 * y + 71 * c + (x * y) % 19) % 256).astype(np.uint8)

@@ -308,6 +308,62 @@ int main()
         for (const char *f : {"text.f32", "final.f32", "unpacked.f32", "decoded.f32"})
             REQUIRE(std::filesystem::exists(std::filesystem::path(trace) / f), "missing trace " << f);
         REQUIRE(t.image.pixels == a.image.pixels, "traced generate differs");
+        // img2img (src/pipeline.cpp:341-345, :392-437, :536-540): strength 0 decodes the encoded image
+        // straight back; a positive strength is generate_from_ids from the encoded latent's start step
+        VaeEncoder encoder(ctx);
+        encoder.synthesize(13);
+        DitStageRequest ir = req;
+        ir.trace.clear();
+        ir.strength = 0.f;
+        bool threw = false;
+        try { generate_img2img_from_ids(models, {}, 8, a.image, ir); }
+        catch (const std::invalid_argument &) { threw = true; }
+        REQUIRE(threw, "img2img without an encoder accepted");
+        models.encoder = &encoder;
+        const VaeEncoding enc = encode_vae(encoder, a.image, ir.precision);
+        REQUIRE(enc.mean.c == 32 && enc.mean.w == 8 && enc.mean.h == 6 && enc.normalized.c == 128 &&
+                    enc.normalized.w == 4 && enc.normalized.h == 3,
+                "encoding shape");
+        const GeneratedImage z = generate_img2img_from_ids(models, {}, 8, a.image, ir);
+        const VaeStageResult back = run_vae_stage(vae, enc.normalized, mean, variance, ir.precision);
+        REQUIRE(z.image.pixels == back.image.pixels && z.latent.data == enc.normalized.data,
+                "strength 0 is not encode + decode");
+        ir.strength = 0.5f;
+        const GeneratedImage h = generate_img2img_from_ids(models, {5, 9, 100}, 8, a.image, ir);
+        DitStageRequest manual = ir;
+        manual.encoded = enc.normalized;
+        const GeneratedImage hm = generate_from_ids(models, {5, 9, 100}, 8, manual);
+        REQUIRE(h.image.pixels == hm.image.pixels && h.start_step == hm.start_step && h.start_step > 0,
+                "img2img is not the DiT stage from the encoded latent");
+        const std::string itrace = std::string(folder) + "/itrace";
+        std::filesystem::create_directory(itrace);
+        ir.trace = itrace;
+        const GeneratedImage ht = generate_img2img_from_ids(models, {5, 9, 100}, 8, a.image, ir);
+        for (const char *f : {"input.rgb", "img2img.txt", "encoder-mean.f32", "encoder-packed.f32",
+                              "encoder-normalized.f32", "text.f32", "final.f32"})
+            REQUIRE(std::filesystem::exists(std::filesystem::path(itrace) / f), "missing img2img trace " << f);
+        REQUIRE(ht.image.pixels == h.image.pixels, "traced img2img differs");
+        ir.trace.clear();
+        for (float bad_strength : {-0.1f, 1.5f})
+        {
+            ir.strength = bad_strength;
+            threw = false;
+            try { generate_img2img_from_ids(models, {5, 9, 100}, 8, a.image, ir); }
+            catch (const std::invalid_argument &) { threw = true; }
+            REQUIRE(threw, "strength " << bad_strength << " accepted");
+        }
+        ir.strength = 0.5f;
+        RgbImage odd = a.image;
+        odd.width = 40;
+        odd.pixels.resize(size_t(40) * 48 * 3);
+        threw = false;
+        try { encode_vae(encoder, odd); }
+        catch (const std::invalid_argument &) { threw = true; }
+        REQUIRE(threw, "40-pixel-wide image accepted by the encoder");
+        threw = false;
+        try { generate_img2img_from_ids(models, {5, 9, 100}, 8, odd, ir); }
+        catch (const std::invalid_argument &) { threw = true; }
+        REQUIRE(threw, "img2img image of another size accepted");
         std::filesystem::remove_all(folder);
     }
     catch (const std::exception &e)

@@ -444,6 +444,19 @@ static void vae_contract()
         params += n;
     }
     REQUIRE(params == 49620259, "VAE parameter count " << params);
+    const auto enc = VaeEncoder::tensors();
+    REQUIRE(enc.size() == 110, "VAE encoder tensor count " << enc.size());
+    REQUIRE(enc.front().first == "encoder.conv_in.weight" && enc.front().second == std::vector<int>({128, 3, 3, 3}) &&
+                enc.back().first == "bn.running_var",
+            "VAE encoder tensor order");
+    size_t enc_params = 0;
+    for (const auto &t : enc)
+    {
+        size_t n = 1;
+        for (int d : t.second) n *= size_t(d);
+        enc_params += n;
+    }
+    REQUIRE(enc_params == 34426112, "VAE encoder parameter count " << enc_params);
 }
 
 // text_constants and text_embeddings (src/text_encoder.cpp:48-100) without a device

@@ -122,3 +122,28 @@ def test_vae_checkpoint(ctx, tmp_path, bf16):
     finally:
         synth.close()
         loaded.close()
+
+
+def test_vae_encoder_checkpoint(ctx, tmp_path):
+    """The official VAE file holds encoder.*, quant_conv.* and bn.* beside the decoder's tensors (here BF16
+    convolution weights, FP32 vectors, and a decoder tensor the encoder skips)."""
+    weights = ov.synth_weights(SEED, bf16_weights=True, table=ov.encoder_table())
+    tensors = {}
+    for name, shape in ov.encoder_table():
+        _, _, is_weight = ov.synth_rule(name, shape)
+        tensors[name] = ("BF16", bits(weights[name])) if is_weight else ("F32", weights[name])
+    tensors["decoder.conv_in.bias"] = ("F32", np.zeros(512, np.float32))
+    path = str(tmp_path / "vae.safetensors")
+    write_safetensors(path, tensors)
+    synth, loaded = ec.VaeEncoder(ctx), ec.VaeEncoder(ctx)
+    try:
+        synth.synthesize(SEED, bf16_weights=True)
+        loaded.load_safetensors(path)
+        rgb = np.random.default_rng(3).integers(0, 256, (32, 48, 3), dtype=np.uint8)
+        for precision in (ec.BF16, ec.FP32):
+            a, b = synth.encode(rgb, precision), loaded.encode(rgb, precision)
+            for x, y in zip(a[:3], b[:3]):
+                assert np.isfinite(x).all() and np.array_equal(x, y)
+    finally:
+        synth.close()
+        loaded.close()
