@@ -424,6 +424,139 @@ def run_vae(args):
         pg.destroy_process_group()
 
 
+# ---- img2img's image latent: VAE encode (--stage vae-encode) -------------------------------------------
+VAE_ENC_METRIC = "VAE encode images/s (1024² RGB -> mean, packed and normalized latents); % BF16 peak"
+VAE_ENC_IMAGE = (1024, 1024)  # (height, width): the reference's reviewed large encoder shape
+VAE_ENC_SAMPLE = (128, 128)   # CPU sample: 1/64 of the pixels
+
+
+def vae_encode_cpu_sample():
+    """The oracle's encode (float64 numpy, all host cores) of one VAE_ENC_SAMPLE image: (seconds, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import vae as ov
+    threads = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=threads)
+    except ImportError:
+        pass
+    w = ov.synth_weights(4321, table=ov.encoder_table())
+    rgb = ov.rgb_fixture(VAE_ENC_SAMPLE[1], VAE_ENC_SAMPLE[0])
+    ov.encode(w, rgb)  # warm
+    t0 = time.perf_counter()
+    ov.encode(w, rgb)
+    return time.perf_counter() - t0, threads
+
+
+def vae_encode_cpu_fields(seconds, threads):
+    scale = (VAE_ENC_IMAGE[0] * VAE_ENC_IMAGE[1]) / (VAE_ENC_SAMPLE[0] * VAE_ENC_SAMPLE[1])
+    image_s = seconds * scale
+    return 1.0 / image_s, {"value": 1.0 / image_s, "unit": "images/s", "cores": threads, "kind": "port",
+                           "sample": f"oracle encode of a {VAE_ENC_SAMPLE[1]}x{VAE_ENC_SAMPLE[0]} image "
+                                     f"({seconds:.2f} s), scaled x{scale:.0f} by pixel count (the attention's "
+                                     "quadratic term, 11% of the 1024² FLOPs, is not scaled up)"}
+
+
+def run_vae_encode_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times, threads = [], 1
+    for i in range(args.warmup + args.steps):
+        dt, threads = vae_encode_cpu_sample()
+        if i >= args.warmup:
+            times.append(dt)
+    value, cpu = vae_encode_cpu_fields(statistics.median(times), threads)
+    line = {"metric": VAE_ENC_METRIC, "impl": "reference", "value": value, "unit": "images/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "VAE encode of one 1024x1024 image", "sample": cpu["sample"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_vae_encode(args):
+    """One VAE encode per GPU per step (independent images, no collective)."""
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    ctx = ec.Context(local)
+    enc = ec.VaeEncoder(ctx)
+    enc.synthesize(4321)
+    precision = ec.BF16 if args.precision == "bf16" else ec.FP32
+    h, w = VAE_ENC_IMAGE
+    rgb = np.random.default_rng(dp.request_seed(4000, rank)).integers(0, 256, (h, w, 3), dtype=np.uint8)
+    src = ctx.to_device(rgb)
+    outs = [ctx.buffer(32 * h * w // 64 * 4), ctx.buffer(128 * h * w // 256 * 4), ctx.buffer(128 * h * w // 256 * 4)]
+    launches = enc.launches(w, h, precision)
+    for _ in range(args.warmup):
+        enc.encode_device(src, w, h, *outs, precision=precision)
+    clocks = ClockSampler(local)
+    barrier(pg)
+    ctx.synchronize()
+    clocks.start()
+    ctx.record(0)
+    for _ in range(args.steps):
+        enc.encode_device(src, w, h, *outs, precision=precision)
+    ctx.record(1)
+    ctx.synchronize()
+    clock_info = clocks.stop()
+    barrier(pg)
+    ms = max_over_ranks(pg, ctx.elapsed(0, 1)) / args.steps
+
+    prof = enc.profile(w, h, precision, iters=3)
+    bf16_peak, _, hbm_peak, peak_kind = peaks()
+    classes = {}
+    for name, (t, work) in prof.items():
+        tensor = name in ("conv", "attention_gemm")
+        rate = work / (t * 1e-3) / (1e12 if tensor else 1e9) if t > 0 else 0.0
+        classes[name] = {"ms": t, "work": work, "work_unit": "FLOP" if tensor else "byte",
+                         "achieved": rate, "unit": "TFLOP/s" if tensor else "GB/s",
+                         "frac": rate / (bf16_peak if tensor else hbm_peak)}
+    total_flops = prof["conv"][1] + prof["attention_gemm"][1]
+    conv = classes["conv"]
+
+    e2e = None
+    if not args.no_e2e:
+        enc.encode(rgb, precision)
+        barrier(pg)
+        reps = max(1, args.steps)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            mean, packed, normalized, bad = enc.encode(rgb, precision)
+        dt = max_over_ranks(pg, (time.perf_counter() - t0) / reps)
+        assert bad == 0 and np.isfinite(normalized).all()
+        e2e = {"value": world / dt, "unit": "images/s", "h2d_bytes_per_step": rgb.nbytes,
+               "d2h_bytes_per_step": mean.nbytes + packed.nbytes + normalized.nbytes,
+               "call": "ernie_cuda_vae_encode (host RGB bytes in, host mean/packed/normalized FP32 out)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        _, cpu = vae_encode_cpu_fields(*vae_encode_cpu_sample())
+
+    if rank == 0:
+        line = {"metric": VAE_ENC_METRIC, "value": world * 1000.0 / ms, "unit": "images/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+                "config": {"workload": "VAE encode (AutoencoderKLFlux2 encoder + quant_conv + pixel_unshuffle + "
+                                       f"BatchNorm) of one {w}x{h} RGB image per GPU per step, seeded synthetic "
+                                       "weights", "global_batch": world, "parallelism": f"dp{world}",
+                           "l2": "inputs larger than L2 (activations of 0.5 GB per layer at the top level)",
+                           "encode_tflops": total_flops / (ms * 1e-3) / 1e12, "kernel_classes": classes},
+                "roofline": {"bound": "tensor", "kernel": "conv_kernel (all encoder convolutions)",
+                             "achieved": conv["achieved"], "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": conv["achieved"] / bf16_peak, "peak_kind": peak_kind, "traffic": None},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clock_info}
+        print(json.dumps(line), flush=True)
+    src.free()
+    for b in outs:
+        b.free()
+    enc.close()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+
+
 def pipeline_stages(ctx, args, ms_per_step, reps=3):
     """Device time of the whole image on this GPU: prompt encode (25 layers at the config's text bucket),
     8 denoise steps (the metric's ms_per_step x 8) and the VAE decode (unpacked latent 2h x 2w), BF16."""
@@ -507,9 +640,10 @@ def main():
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--stage", choices=["dit", "vae", "text"], default="dit",
+    ap.add_argument("--stage", choices=["dit", "vae", "text", "vae-encode"], default="dit",
                     help="dit: the denoise loop (the metric); vae: the VAE decode after it; text: the prompt "
-                         "encoder before it (at the config's text bucket)")
+                         "encoder before it (at the config's text bucket); vae-encode: img2img's image encoder "
+                         "(1024x1024)")
     ap.add_argument("--vae-latent", default=None,
                     help="profiling aid: H,W of the unpacked latent of --stage vae (default 128,128: 1024x1024)")
     args = ap.parse_args()
@@ -524,6 +658,8 @@ def main():
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
     if args.stage == "text":
         return run_text_reference(args) if args.impl == "reference" else run_text(args)
+    if args.stage == "vae-encode":
+        return run_vae_encode_reference(args) if args.impl == "reference" else run_vae_encode(args)
     if args.impl == "reference":
         return run_reference(args)
 
