@@ -168,6 +168,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+DATASHEET_BF16_TFLOPS = 2250.0  # B200 dense BF16, NVIDIA's datasheet figure (context beside the measured peak)
 KERNELS = {"norm_modulate": 0, "qkv_gemm": 1, "attention": 2, "out_gemm": 3, "upgate_gemm": 5, "down_gemm": 6}
 
 # ---- the stage after the denoise loop: VAE decode (--stage vae) -----------------------------------------
@@ -797,6 +798,7 @@ def main():
                            "parallelism": f"sp{world}" if sp else f"dp{world}", "rows_per_gpu": T,
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
+                           "step_frac_of_datasheet_bf16": step_tflops / DATASHEET_BF16_TFLOPS,
                            "kernel_ms": prof, "kernel_ms_in_block": in_block, "pipeline_stages": stages},
                 "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": bf16_peak,
                              "unit": "TFLOP/s", "frac": achieved / bf16_peak, "peak_kind": peak_kind,
