@@ -8,8 +8,9 @@
 //  * attention_f32_kernel: FP32 scores, FP64 softmax sums and P.V accumulation. Serves the FP32
 //    exactness mode, the stand-alone SDPA layer contract (GQA with one K/V head, widths up to 128,
 //    row or dense additive masks, mask per head), replacing the reference's Kahan-compensated
-//    FP32 shaders (cmake/ErnieAttentionShader.cmake:18-55), and the text encoder's causal grouped-query
-//    attention (32 query heads over 8 K/V heads).
+//    FP32 shaders (cmake/ErnieAttentionShader.cmake:18-55), the text encoder's causal grouped-query
+//    attention (32 query heads over 8 K/V heads), and the prompt enhancer's chunks over its K/V cache
+//    (queries at positions causal_offset.., keys 0..kv_len).
 #include "kernels.h"
 #include <cmath>
 
@@ -62,8 +63,8 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
     double acc[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0.0;
-    // causal: no key past this CTA's last query row
-    const int kv_end = a.causal ? min(a.kv_len, q0 + kFQ) : a.kv_len;
+    // causal: no key past this CTA's last query row (rows start at position causal_offset)
+    const int kv_end = a.causal ? min(a.kv_len, q0 + kFQ + a.causal_offset) : a.kv_len;
     const int tiles = (kv_end + kFK - 1) / kFK;
     for (int j = 0; j < tiles; ++j)
     {
@@ -89,7 +90,9 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
 #pragma unroll 8
             for (int d = 0; d < kDim; ++d) dot = fmaf(qr[d], kr[d], dot);
             const int key = key0 + kj;
-            float x = key < a.kv_len && !(a.causal && key > qrow) ? dot * scale + (mrow ? mrow[key] : 0.f) : -INFINITY;
+            float x = key < a.kv_len && !(a.causal && key > qrow + a.causal_offset)
+                          ? dot * scale + (mrow ? mrow[key] : 0.f)
+                          : -INFINITY;
             sc[i] = x;
             tile_max = fmaxf(tile_max, x);
         }
@@ -166,7 +169,7 @@ int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream)
 {
     if (args.nq < 1 || args.nk < 1 || args.kv_len < 1 || args.kv_len > args.nk || args.width < 1 ||
         args.width > kDim || args.heads < 1 || args.kv_heads < 1 || args.heads % args.kv_heads ||
-        args.out_mode < 0 || args.out_mode > 2 ||
+        args.out_mode < 0 || args.out_mode > 2 || args.causal_offset < 0 ||
         (args.mask && args.mask_heads != 1 && args.mask_heads != args.heads) ||
         (args.mask && args.mask_rows != 1 && args.mask_rows != args.nq))
         return cudaErrorInvalidValue;

@@ -143,7 +143,8 @@ struct AttentionF32Args
     int out_mode;
     float *out_f32;
     __nv_bfloat16 *out_split3;
-    int causal;
+    int causal;            // key j visible to query i iff j <= i + causal_offset
+    int causal_offset = 0; // position of query 0 (a KV-cached chunk appended after causal_offset keys)
 };
 int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream);
 

@@ -56,6 +56,11 @@ struct ernie_cuda_text_model
     void *alloc = nullptr;
     uint64_t bytes = 0;
     TextWork work;
+    // the prompt enhancer's LM head (allocated on first upload): final RMSNorm weight and lm_head
+    float *head_norm = nullptr;
+    __nv_bfloat16 *lm_head = nullptr; // [131072][3072]
+    void *head_alloc = nullptr;
+    bool head_loaded = false;
 };
 
 namespace
@@ -243,6 +248,7 @@ extern "C" int ernie_cuda_text_model_destroy(ernie_cuda_text_model *m)
     cudaStreamSynchronize(m->ctx->stream);
     free_work(m->work);
     if (m->alloc) cudaFree(m->alloc);
+    if (m->head_alloc) cudaFree(m->head_alloc);
     delete m;
     return ERNIE_CUDA_OK;
 }
@@ -370,4 +376,266 @@ extern "C" int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *m, const
 {
     return run_text(m, input, bucket, cos_t, sin_t, precision, layers, out, cudaMemcpyDeviceToDevice,
                     cudaMemcpyDeviceToDevice);
+}
+
+// ---- prompt enhancer (PeSession, src/pe_session.cpp; enhance_prompt, src/prompt_enhancer.cpp) -------
+// The PE is the same Mistral decoder layer (the PE block graph, src/pe_graph.cpp, is the text block plus
+// past_k / past_v inputs) over the 26 layers of its own checkpoint, with an LM head of RMSNorm + a
+// 131072 x 3072 projection tied to the embeddings (head.ncnn.param, tools/build_pe_model.py:100-105).
+// Per chunk of 1..32 new tokens at the session's position: the layer as above, the rotated K / V rows
+// appended to the layer's FP32 cache, and the FP32 attention of the chunk's queries over every cached key
+// up to each query's own position (FP64 sums; the decode is a few rows, so its cost is the weight stream).
+namespace
+{
+constexpr int kPeMaxRows = 32, kPeMaxCapacity = 4096, kPeVocab = 131072;
+
+int ensure_head(ernie_cuda_text_model *m)
+{
+    if (m->head_alloc) return ERNIE_CUDA_OK;
+    Arena arena;
+    arena.add(&m->head_norm, kTH);
+    arena.add(&m->lm_head, static_cast<size_t>(kPeVocab) * kTH);
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess) return from_cuda(e, "Allocate PE head");
+    m->head_alloc = arena.base;
+    return ERNIE_CUDA_OK;
+}
+} // namespace
+
+struct ernie_cuda_pe_session
+{
+    ernie_cuda_text_model *model = nullptr;
+    int capacity = 0, precision = 0, planes = 1, position = 0;
+    bool valid = true;
+    float *kcache = nullptr, *vcache = nullptr; // [layers][8][capacity][128]
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+    __nv_bfloat16 *a = nullptr, *h = nullptr;
+    float *hrow = nullptr, *logits = nullptr;
+    __nv_bfloat16 *ha = nullptr;
+    void *alloc = nullptr;
+};
+
+namespace
+{
+// One chunk of `rows` tokens through every layer, appending to the caches at s->position.
+int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
+{
+    ernie_cuda_text_model *m = ps->model;
+    cudaStream_t s = m->ctx->stream;
+    const int sms = m->ctx->num_sms, T = rows, pos = ps->position;
+    const bool fp32 = ps->precision == ERNIE_PRECISION_FP32;
+    const int splits = fp32 ? 3 : 1;
+    const int bn = fp32 ? 128 : text_block_n(T, kTH, sms);
+    const size_t layer_cache = static_cast<size_t>(8) * ps->capacity * 128;
+    for (int l = 0; l < m->num_layers; ++l)
+    {
+        const TextLayer &L = m->layers[static_cast<size_t>(l)];
+        float *kc = ps->kcache + static_cast<size_t>(l) * layer_cache;
+        float *vc = ps->vcache + static_cast<size_t>(l) * layer_cache;
+        GemmEpilogueArgs f32;
+        f32.out = ps->qkv;
+        f32.ldo = kTQkv;
+        f32.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_norm_modulate(ps->x, T, kTH, L.gamma_attn, nullptr, nullptr, kTEps, 0, ps->a, fp32 ? 1 : 0, s),
+                     "PE input_layernorm");
+        ERNIE_LAUNCH(launch_gemm(ps->a, L.wqkv, T, kTQkv, kTH, splits, bn, Epilogue::F32Bias, f32, sms, s, fp32),
+                     "PE qkv projection");
+        ERNIE_LAUNCH(launch_text_rope(ps->qkv, ps->cos_t, ps->sin_t, T, ps->q, ps->k, ps->v, s), "PE rotary");
+        // the chunk's K / V rows of each of the 8 heads into the caches at rows pos..pos+T-1
+        const size_t row_bytes = static_cast<size_t>(T) * 128 * 4, pitch = static_cast<size_t>(ps->capacity) * 128 * 4;
+        ERNIE_CUDA(cudaMemcpy2DAsync(kc + static_cast<size_t>(pos) * 128, pitch, ps->k, row_bytes, row_bytes, 8,
+                                     cudaMemcpyDeviceToDevice, s),
+                   "PE key cache");
+        ERNIE_CUDA(cudaMemcpy2DAsync(vc + static_cast<size_t>(pos) * 128, pitch, ps->v, row_bytes, row_bytes, 8,
+                                     cudaMemcpyDeviceToDevice, s),
+                   "PE value cache");
+        AttentionF32Args at{};
+        at.q = ps->q;
+        at.k = kc;
+        at.v = vc;
+        at.heads = 32;
+        at.kv_heads = 8;
+        at.mask_heads = 1;
+        at.mask_rows = 1;
+        at.nq = T;
+        at.nk = at.kv_len = pos + T;
+        at.width = 128;
+        at.q_head_stride = static_cast<long long>(T) * 128;
+        at.kv_head_stride = static_cast<long long>(ps->capacity) * 128;
+        at.causal = 1;
+        at.causal_offset = pos;
+        at.out_mode = fp32 ? 1 : 2; // the o_proj operand: three BF16 planes or BF16, token-major
+        at.out_split3 = ps->a;
+        ERNIE_LAUNCH(launch_attention_f32(at, s), "PE attention");
+        GemmEpilogueArgs res;
+        res.resid = ps->x;
+        res.ldo = kTH;
+        res.gate = m->ones;
+        res.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_gemm(ps->a, L.wo, T, kTH, kTQ, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
+                     "PE o_proj");
+        ERNIE_LAUNCH(launch_norm_modulate(ps->x, T, kTH, L.gamma_mlp, nullptr, nullptr, kTEps, 0, ps->a, fp32 ? 1 : 0, s),
+                     "PE post_attention_layernorm");
+        GemmEpilogueArgs glu;
+        glu.h = ps->h;
+        glu.h_split3 = fp32 ? 1 : 0;
+        glu.ffn = kTFfn;
+        glu.silu = 1;
+        glu.error_flag = m->ctx->error_flag;
+        ERNIE_LAUNCH(launch_gemm(ps->a, L.wug, T, 2 * kTFfn, kTH, splits, fp32 ? 128 : text_block_n(T, 2 * kTFfn, sms),
+                                 Epilogue::Geglu, glu, sms, s, fp32),
+                     "PE gate/up projection");
+        ERNIE_LAUNCH(launch_gemm(ps->h, L.wdown, T, kTH, kTFfn, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
+                     "PE down_proj");
+    }
+    return ERNIE_CUDA_OK;
+}
+
+bool all_finite(const float *p, size_t n)
+{
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(p[i])) return false;
+    return true;
+}
+} // namespace
+
+extern "C" int ernie_cuda_text_model_upload_head(ernie_cuda_text_model *m, const float *norm, const uint16_t *lm_head)
+{
+    if (!m || !norm || !lm_head) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!all_finite(norm, kTH)) return fail(ERNIE_CUDA_ERROR, "PE head norm is not finite");
+    DeviceGuard guard(m->ctx->device);
+    ERNIE_TRY(ensure_head(m));
+    ERNIE_CUDA(cudaMemcpy(m->head_norm, norm, kTH * 4, cudaMemcpyHostToDevice), "upload PE head norm");
+    ERNIE_CUDA(cudaMemcpy(m->lm_head, lm_head, static_cast<size_t>(kPeVocab) * kTH * 2, cudaMemcpyHostToDevice),
+               "upload PE lm_head");
+    m->head_loaded = true;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_text_model_synthesize_head(ernie_cuda_text_model *m, uint64_t seed)
+{
+    if (!m) return fail(ERNIE_CUDA_ERROR, "null model");
+    DeviceGuard guard(m->ctx->device);
+    ERNIE_TRY(ensure_head(m));
+    cudaStream_t s = m->ctx->stream;
+    const float std = ERNIE_SYNTH_WEIGHT_STD;
+    const uint64_t w = ERNIE_SYNTH_TEXT_STREAM(ERNIE_SYNTH_TEXT_HEAD_LAYER, 0);
+    const uint64_t n = ERNIE_SYNTH_TEXT_STREAM(ERNIE_SYNTH_TEXT_HEAD_LAYER, 1);
+    ERNIE_LAUNCH(launch_synth_bf16(seed, w, std, 0.f, kPeVocab, kTH, kPeVocab, 0, 0, m->lm_head, s), "synth");
+    ERNIE_LAUNCH(launch_synth_f32_bf16(seed, n, std, 1.f, kTH, m->head_norm, s), "synth");
+    ERNIE_CUDA(cudaStreamSynchronize(s), "synthesize PE head");
+    m->head_loaded = true;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_session_create(ernie_cuda_text_model *m, int capacity, int precision,
+                                            ernie_cuda_pe_session **out)
+{
+    if (!m || !out) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *out = nullptr;
+    if (capacity < 1 || capacity > kPeMaxCapacity)
+        return fail(ERNIE_CUDA_ERROR, "PE requires 1..26 blocks and capacity 1..4096");
+    if (precision != ERNIE_PRECISION_BF16 && precision != ERNIE_PRECISION_FP32)
+        return fail(ERNIE_CUDA_ERROR, "Unknown precision");
+    DeviceGuard guard(m->ctx->device);
+    auto ps = std::make_unique<ernie_cuda_pe_session>();
+    ps->model = m;
+    ps->capacity = capacity;
+    ps->precision = precision;
+    ps->planes = precision == ERNIE_PRECISION_FP32 ? 3 : 1;
+    const size_t cache = static_cast<size_t>(m->num_layers) * 8 * capacity * 128, r = kPeMaxRows;
+    Arena arena;
+    arena.add(&ps->kcache, cache);
+    arena.add(&ps->vcache, cache);
+    arena.add(&ps->x, r * kTH);
+    arena.add(&ps->qkv, r * kTQkv);
+    arena.add(&ps->q, r * kTQ);
+    arena.add(&ps->k, r * kTKV);
+    arena.add(&ps->v, r * kTKV);
+    arena.add(&ps->cos_t, r * 128);
+    arena.add(&ps->sin_t, r * 128);
+    arena.add(&ps->a, r * ps->planes * kTQ);
+    arena.add(&ps->h, r * ps->planes * kTFfn);
+    arena.add(&ps->hrow, kTH);
+    arena.add(&ps->ha, static_cast<size_t>(ps->planes) * kTH);
+    arena.add(&ps->logits, kPeVocab);
+    const cudaError_t e = arena.allocate();
+    if (e != cudaSuccess) return from_cuda(e, "Allocate PE session");
+    ps->alloc = arena.base;
+    *out = ps.release();
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_session_destroy(ernie_cuda_pe_session *ps)
+{
+    if (!ps) return ERNIE_CUDA_OK;
+    DeviceGuard guard(ps->model->ctx->device);
+    cudaStreamSynchronize(ps->model->ctx->stream);
+    if (ps->alloc) cudaFree(ps->alloc);
+    delete ps;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_session_reset(ernie_cuda_pe_session *ps)
+{
+    if (!ps) return fail(ERNIE_CUDA_ERROR, "null argument");
+    ps->position = 0;
+    ps->valid = true;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_session_position(ernie_cuda_pe_session *ps, int *position)
+{
+    if (!ps || !position) return fail(ERNIE_CUDA_ERROR, "null argument");
+    *position = ps->position;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_session_append(ernie_cuda_pe_session *ps, const float *embedded, const float *cos,
+                                            const float *sin, int rows, float *hidden)
+{
+    if (!ps || !embedded || !cos || !sin || !hidden) return fail(ERNIE_CUDA_ERROR, "null argument");
+    if (!ps->valid) return fail(ERNIE_CUDA_ERROR, "PE session failed; reset before reuse");
+    if (rows < 1 || rows > kPeMaxRows || rows > ps->capacity - ps->position)
+        return fail(ERNIE_CUDA_ERROR, "PE token count or session capacity exceeded");
+    const size_t r = static_cast<size_t>(rows);
+    if (!all_finite(embedded, r * kTH) || !all_finite(cos, r * 128) || !all_finite(sin, r * 128))
+        return fail(ERNIE_CUDA_ERROR, "PE tensor contains non-finite values");
+    ernie_cuda_text_model *m = ps->model;
+    DeviceGuard guard(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    ps->valid = false; // until this chunk has completed
+    ERNIE_CUDA(cudaMemcpyAsync(ps->x, embedded, r * kTH * 4, cudaMemcpyHostToDevice, s), "PE input");
+    ERNIE_CUDA(cudaMemcpyAsync(ps->cos_t, cos, r * 128 * 4, cudaMemcpyHostToDevice, s), "PE cos");
+    ERNIE_CUDA(cudaMemcpyAsync(ps->sin_t, sin, r * 128 * 4, cudaMemcpyHostToDevice, s), "PE sin");
+    ERNIE_TRY(pe_enqueue(ps, rows));
+    ERNIE_CUDA(cudaMemcpyAsync(hidden, ps->x, r * kTH * 4, cudaMemcpyDeviceToHost, s), "PE hidden");
+    ERNIE_TRY(check_status(m));
+    ps->position += rows;
+    ps->valid = true;
+    return ERNIE_CUDA_OK;
+}
+
+extern "C" int ernie_cuda_pe_logits(ernie_cuda_pe_session *ps, const float *hidden, float *logits)
+{
+    if (!ps || !hidden || !logits) return fail(ERNIE_CUDA_ERROR, "null argument");
+    ernie_cuda_text_model *m = ps->model;
+    if (!m->head_loaded) return fail(ERNIE_CUDA_ERROR, "PE head not uploaded");
+    if (!all_finite(hidden, kTH)) return fail(ERNIE_CUDA_ERROR, "PE tensor contains non-finite values");
+    DeviceGuard guard(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const bool fp32 = ps->precision == ERNIE_PRECISION_FP32;
+    ERNIE_CUDA(cudaMemcpyAsync(ps->hrow, hidden, kTH * 4, cudaMemcpyHostToDevice, s), "PE head input");
+    ERNIE_LAUNCH(launch_norm_modulate(ps->hrow, 1, kTH, m->head_norm, nullptr, nullptr, kTEps, 0, ps->ha, fp32 ? 1 : 0, s),
+                 "PE head norm");
+    GemmEpilogueArgs f32;
+    f32.out = ps->logits;
+    f32.ldo = kPeVocab;
+    f32.error_flag = m->ctx->error_flag;
+    ERNIE_LAUNCH(launch_gemm(ps->ha, m->lm_head, 1, kPeVocab, kTH, fp32 ? 3 : 1, 128, Epilogue::F32Bias, f32,
+                             m->ctx->num_sms, s, fp32),
+                 "PE lm_head");
+    ERNIE_CUDA(cudaMemcpyAsync(logits, ps->logits, static_cast<size_t>(kPeVocab) * 4, cudaMemcpyDeviceToHost, s),
+               "PE logits");
+    return check_status(m);
 }

@@ -154,6 +154,15 @@ SIGNATURES = {
     "ernie_cuda_vae_encode": (I, [P, P, I, I, I, P, P, P, ctypes.POINTER(I)]),
     "ernie_cuda_vae_encode_device": (I, [P, P, I, I, I, P, P, P, ctypes.POINTER(I)]),
     "ernie_cuda_vae_encoder_load_safetensors": (I, [P, ctypes.POINTER(ctypes.c_char_p), I]),
+    "ernie_cuda_pe_model_load_safetensors": (I, [P, I, ctypes.POINTER(ctypes.c_char_p), I]),
+    "ernie_cuda_text_model_upload_head": (I, [P, P, P]),
+    "ernie_cuda_text_model_synthesize_head": (I, [P, U64]),
+    "ernie_cuda_pe_session_create": (I, [P, I, I, ctypes.POINTER(P)]),
+    "ernie_cuda_pe_session_destroy": (I, [P]),
+    "ernie_cuda_pe_session_reset": (I, [P]),
+    "ernie_cuda_pe_session_position": (I, [P, ctypes.POINTER(I)]),
+    "ernie_cuda_pe_session_append": (I, [P, P, P, P, I, P]),
+    "ernie_cuda_pe_logits": (I, [P, P, P]),
 }
 
 
@@ -522,6 +531,20 @@ class TextModel:
         arr, n = _paths(files)
         check(lib().ernie_cuda_text_model_load_safetensors(self.handle, num_layers or self.num_layers, arr, n))
 
+    def load_pe_safetensors(self, files, num_layers=None):
+        """The prompt enhancer's checkpoint (model.layers.{l}.*, model.norm, lm_head or tied embeddings)."""
+        arr, n = _paths(files)
+        check(lib().ernie_cuda_pe_model_load_safetensors(self.handle, num_layers or self.num_layers, arr, n))
+
+    def synthesize_head(self, seed):
+        check(lib().ernie_cuda_text_model_synthesize_head(self.handle, seed))
+
+    def upload_head(self, norm, lm_head_bits):
+        """norm [3072] float32, lm_head [131072, 3072] uint16 BF16 bits."""
+        n = np.ascontiguousarray(norm, dtype=np.float32)
+        w = np.ascontiguousarray(lm_head_bits, dtype=np.uint16)
+        check(lib().ernie_cuda_text_model_upload_head(self.handle, ptr(n), ptr(w)))
+
     def upload_layer(self, layer, tensors):
         """tensors: wq, wk, wv, wo, wgate, wup, wdown as uint16 BF16 bits; gamma_attn, gamma_mlp float32."""
         keep = {k: np.ascontiguousarray(v) for k, v in tensors.items()}
@@ -627,6 +650,46 @@ class Vae:
         """Asynchronous decode between device buffers (Buffer objects) on the context's stream."""
         check(lib().ernie_cuda_vae_decode_device(self.handle, unpacked_dev.c, width, height, precision,
                                                  decoded_dev.c, rgb_dev.c if rgb_dev is not None else None, None))
+
+
+PE_VOCAB = 131072
+
+
+class PeSession:
+    """The prompt enhancer's KV-cached decoder (PeSession of src/pe_session.h) over a TextModel's layers."""
+
+    def __init__(self, model, capacity, precision=BF16):
+        h = P()
+        check(lib().ernie_cuda_pe_session_create(model.handle, capacity, precision, ctypes.byref(h)))
+        self.handle, self.model = h, model
+
+    def close(self):
+        if self.handle:
+            lib().ernie_cuda_pe_session_destroy(self.handle)
+            self.handle = None
+
+    def reset(self):
+        check(lib().ernie_cuda_pe_session_reset(self.handle))
+
+    def position(self):
+        n = I(0)
+        check(lib().ernie_cuda_pe_session_position(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def append(self, embedded, cos, sin):
+        """embedded [rows, 3072], cos / sin [rows, 128] -> hidden [rows, 3072]."""
+        x = np.ascontiguousarray(embedded, dtype=np.float32)
+        c = np.ascontiguousarray(cos, dtype=np.float32)
+        s = np.ascontiguousarray(sin, dtype=np.float32)
+        out = np.empty_like(x)
+        check(lib().ernie_cuda_pe_session_append(self.handle, ptr(x), ptr(c), ptr(s), x.shape[0], ptr(out)))
+        return out
+
+    def logits(self, hidden):
+        h = np.ascontiguousarray(hidden, dtype=np.float32).reshape(-1)
+        out = np.empty(PE_VOCAB, np.float32)
+        check(lib().ernie_cuda_pe_logits(self.handle, ptr(h), ptr(out)))
+        return out
 
 
 class VaeEncoder:

@@ -1352,4 +1352,167 @@ GeneratedImage generate_img2img_from_ids(GenerationModels &m, const std::vector<
     out.elapsed_seconds = seconds_since(start);
     return out;
 }
+// ---- the optional prompt enhancer --------------------------------------------------------------------
+namespace
+{
+void pe_options_check(const PeOptions &o)
+{
+    if (o.max_tokens < 1 || o.max_tokens > 2048 || !std::isfinite(o.temperature) || o.temperature <= 0 ||
+        !std::isfinite(o.top_p) || o.top_p <= 0 || o.top_p > 1)
+        throw std::invalid_argument("PE requires max tokens 1..2048, positive temperature and top-p in (0,1]");
+}
+} // namespace
+
+void TextModel::load_pe_safetensors(const std::vector<std::string> &files)
+{
+    const auto paths = c_paths(files);
+    check_request(ernie_cuda_pe_model_load_safetensors(handle_, num_layers_, paths.data(), static_cast<int>(paths.size())),
+                  "load PE checkpoint");
+}
+
+void TextModel::synthesize_head(uint64_t seed)
+{
+    check_cuda(ernie_cuda_text_model_synthesize_head(handle_, seed), "synthesize PE head");
+}
+
+uint32_t sample_pe_token(const std::vector<float> &logits, const PeOptions &options, std::mt19937 &random)
+{
+    pe_options_check(options);
+    if (logits.empty()) throw std::invalid_argument("PE logits must be an FP32 vector");
+    for (float v : logits)
+        if (!std::isfinite(v)) throw std::runtime_error("Non-finite PE logits");
+    const float *values = logits.data();
+    const int n = static_cast<int>(logits.size());
+    const int best = int(std::max_element(values, values + n) - values);
+    if (options.greedy) return uint32_t(best);
+    std::vector<uint32_t> order(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) order[size_t(i)] = uint32_t(i);
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return values[a] > values[b]; });
+    std::vector<double> weights(order.size());
+    double total = 0;
+    for (size_t i = 0; i < order.size(); ++i)
+    {
+        weights[i] = std::exp((double(values[order[i]]) - values[best]) / options.temperature);
+        total += weights[i];
+    }
+    // the shortest prefix whose weight reaches top_p of the total (at least one token)
+    double cumulative = 0;
+    size_t retained = 0;
+    do
+        cumulative += weights[retained++];
+    while (retained < weights.size() && cumulative < options.top_p * total);
+    weights.resize(retained);
+    std::discrete_distribution<size_t> distribution(weights.begin(), weights.end());
+    return order[distribution(random)];
+}
+
+PeSession::PeSession(TextModel &model, int capacity, Precision precision) : ctx_(model.context())
+{
+    if (capacity < 1 || capacity > 4096) throw std::invalid_argument("PE requires 1..26 blocks and capacity 1..4096");
+    check_request(ernie_cuda_pe_session_create(model.handle(), capacity, precision_code(precision), &handle_),
+                  "create PE session");
+}
+
+PeSession::~PeSession()
+{
+    if (handle_) ernie_cuda_pe_session_destroy(handle_);
+}
+
+void PeSession::reset() { check_cuda(ernie_cuda_pe_session_reset(handle_), "reset PE session"); }
+
+int PeSession::position() const
+{
+    int p = 0;
+    check_cuda(ernie_cuda_pe_session_position(handle_, &p), "PE position");
+    return p;
+}
+
+Tensor PeSession::append(const Tensor &embedded, const Tensor &cos, const Tensor &sin, bool single)
+{
+    const int rows = embedded.h;
+    if (embedded.dims != 2 || embedded.w != 3072 || cos.dims != 2 || sin.dims != 2 || cos.w != 128 || sin.w != 128 ||
+        cos.h != rows || sin.h != rows)
+        throw std::invalid_argument("PE requires pack1 FP32 matrices with matching token rows");
+    if (rows < 1 || rows > (single ? 1 : 32)) throw std::invalid_argument("PE token count or session capacity exceeded");
+    Tensor hidden(3072, rows);
+    check_request(ernie_cuda_pe_session_append(handle_, embedded.ptr(), cos.ptr(), sin.ptr(), rows, hidden.ptr()),
+                  "PE step");
+    return hidden;
+}
+
+Tensor PeSession::step(const Tensor &embedded, const Tensor &cos, const Tensor &sin)
+{
+    return append(embedded, cos, sin, true);
+}
+
+Tensor PeSession::append_chunk(const Tensor &embedded, const Tensor &cos, const Tensor &sin)
+{
+    return append(embedded, cos, sin, false);
+}
+
+std::vector<float> PeSession::logits(const float *hidden_row)
+{
+    std::vector<float> out(131072);
+    check_request(ernie_cuda_pe_logits(handle_, hidden_row, out.data()), "PE logits");
+    return out;
+}
+
+PeResult enhance_prompt_from_ids(TextModel &model, const std::string &embeddings, const std::vector<float> &frequencies,
+                                 const std::vector<uint32_t> &input_ids, const PeOptions &options, Precision precision,
+                                 int prefill_chunk, const PeProgress &progress, const PeLogits &observe)
+{
+    pe_options_check(options);
+    if (prefill_chunk < 1 || prefill_chunk > 32) throw std::invalid_argument("PE prefill chunk must be in [1,32]");
+    if (input_ids.empty() || input_ids.size() > 2048) throw std::invalid_argument("PE chat input exceeds 2048 tokens");
+    if (frequencies.size() != 64) throw std::runtime_error("Invalid PE YaRN table");
+    for (float f : frequencies)
+        if (!std::isfinite(f) || f <= 0) throw std::runtime_error("Invalid PE frequency");
+    PeResult result;
+    result.input_ids = input_ids;
+    PeSession session(model, int(input_ids.size()) + options.max_tokens, precision);
+    // rotary rows of `count` tokens from the session's position: phase = float(position) * f in FP32
+    auto rotary = [&](int count, Tensor &cos, Tensor &sin) {
+        cos = Tensor(128, count);
+        sin = Tensor(128, count);
+        for (int r = 0; r < count; ++r)
+            for (int i = 0; i < 64; ++i)
+            {
+                const float phase = float(session.position() + r) * frequencies[size_t(i)];
+                cos[size_t(r) * 128 + size_t(i)] = cos[size_t(r) * 128 + size_t(i) + 64] = std::cos(phase);
+                sin[size_t(r) * 128 + size_t(i)] = sin[size_t(r) * 128 + size_t(i) + 64] = std::sin(phase);
+            }
+    };
+    auto advance = [&](const std::vector<uint32_t> &ids) {
+        const Tensor embedded = text_embeddings(embeddings, ids, int(ids.size()));
+        Tensor cos, sin;
+        rotary(int(ids.size()), cos, sin);
+        return ids.size() == 1 ? session.step(embedded, cos, sin) : session.append_chunk(embedded, cos, sin);
+    };
+    Tensor hidden;
+    for (size_t first = 0; first < input_ids.size();)
+    {
+        const size_t count = std::min(size_t(prefill_chunk), input_ids.size() - first);
+        hidden = advance(std::vector<uint32_t>(input_ids.begin() + long(first), input_ids.begin() + long(first + count)));
+        first += count;
+        if (progress && (prefill_chunk > 1 || first % 8 == 0 || first == input_ids.size()))
+            progress("prefill", int(first), int(input_ids.size()));
+    }
+    std::mt19937 random(options.seed);
+    for (int i = 0; i < options.max_tokens; ++i)
+    {
+        const std::vector<float> logits = session.logits(hidden.ptr() + size_t(hidden.h - 1) * 3072);
+        if (observe) observe(i, logits);
+        const uint32_t token = sample_pe_token(logits, options, random);
+        result.generated_ids.push_back(token);
+        if (progress && ((i + 1) % 8 == 0 || token == 2 || i + 1 == options.max_tokens))
+            progress("decode", i + 1, options.max_tokens);
+        if (token == 2)
+        {
+            result.eos = true;
+            break;
+        }
+        if (i + 1 < options.max_tokens) hidden = advance({token});
+    }
+    return result;
+}
 } // namespace ernie

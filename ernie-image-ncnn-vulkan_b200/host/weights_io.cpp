@@ -460,16 +460,15 @@ extern "C" int ernie_cuda_model_load_safetensors(ernie_cuda_model *model, int nu
     });
 }
 
-extern "C" int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *model, int num_layers,
-                                                      const char *const *files, int count)
+namespace
 {
-    return guarded([&] {
-        if (!model || num_layers < 1) return fail_weights("null model or no layers");
-        Checkpoint ck(files, count);
+// Mistral decoder layers 0..num_layers-1 under `prefix` + "{l}." into the text model.
+int load_mistral_layers(ernie_cuda_text_model *model, int num_layers, Checkpoint &ck, const std::string &prefix)
+{
         const int64_t H = 3072, Q = 4096, KV = 1024, F = 9216;
         for (int l = 0; l < num_layers; ++l)
         {
-            const std::string p = "language_model.model.layers." + std::to_string(l) + ".";
+            const std::string p = prefix + std::to_string(l) + ".";
             const auto wq = ck.bf16(p + "self_attn.q_proj.weight", {Q, H});
             const auto wk = ck.bf16(p + "self_attn.k_proj.weight", {KV, H});
             const auto wv = ck.bf16(p + "self_attn.v_proj.weight", {KV, H});
@@ -485,6 +484,35 @@ extern "C" int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *mod
             if (rc != ERNIE_CUDA_OK) return rc;
         }
         return ERNIE_CUDA_OK;
+}
+} // namespace
+
+extern "C" int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *model, int num_layers,
+                                                      const char *const *files, int count)
+{
+    return guarded([&] {
+        if (!model || num_layers < 1) return fail_weights("null model or no layers");
+        Checkpoint ck(files, count);
+        return load_mistral_layers(model, num_layers, ck, "language_model.model.layers.");
+    });
+}
+
+extern "C" int ernie_cuda_pe_model_load_safetensors(ernie_cuda_text_model *model, int num_layers,
+                                                    const char *const *files, int count)
+{
+    return guarded([&] {
+        if (!model || num_layers < 1) return fail_weights("null model or no layers");
+        Checkpoint ck(files, count);
+        const int rc = load_mistral_layers(model, num_layers, ck, "model.layers.");
+        if (rc != ERNIE_CUDA_OK) return rc;
+        // the LM head is tied to the embeddings in the official config (tools/build_pe_model.py:68-73)
+        std::string head = "lm_head.weight";
+        bool found = false;
+        for (auto &f : ck.files) found = found || f->entries().count(head) > 0;
+        if (!found) head = "model.embed_tokens.weight";
+        const auto norm = ck.f32("model.norm.weight", {3072});
+        const auto w = ck.bf16(head, {131072, 3072});
+        return forward(ernie_cuda_text_model_upload_head(model, norm.data(), w.data()), "upload PE head");
     });
 }
 

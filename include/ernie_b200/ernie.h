@@ -12,6 +12,7 @@
 #include <map>
 #include <memory>
 #include <optional>
+#include <random>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -538,8 +539,12 @@ class TextModel
     void synthesize(uint64_t seed);
     // language_model.model.layers.{0..num_layers-1}.* from the official (possibly sharded) safetensors
     void load_safetensors(const std::vector<std::string> &files);
+    // the prompt enhancer's checkpoint: model.layers.{l}.*, model.norm and lm_head (or tied embeddings)
+    void load_pe_safetensors(const std::vector<std::string> &files);
+    void synthesize_head(uint64_t seed); // include/ernie_synth.h, ERNIE_SYNTH_TEXT_HEAD_LAYER
     int num_layers() const noexcept { return num_layers_; }
     ernie_cuda_text_model *handle() const noexcept { return handle_; }
+    GpuContext &context() const noexcept { return ctx_; }
 
   private:
     GpuContext &ctx_;
@@ -551,6 +556,60 @@ class TextModel
 // compute time for the whole sequence of layers (the layers stay resident: no per-block load).
 Tensor run_text_blocks(TextModel &model, const Tensor &input, const std::vector<Tensor> &constants,
                        Precision precision, BlockSequenceStats &stats, int layers = 0);
+
+// ---- the optional prompt enhancer (src/prompt_enhancer.h:10-28, src/pe_session.h:9-42) ------------
+struct PeOptions // include/ernie/pipeline.h
+{
+    int max_tokens = 2048;
+    float temperature = .6f, top_p = .95f;
+    uint32_t seed = 42;
+    bool greedy = false;
+};
+// sample_pe_token (src/prompt_enhancer.cpp:33-66): std::invalid_argument for options outside max tokens
+// 1..2048, a positive finite temperature and top-p in (0, 1], or an empty logits vector; std::runtime_error
+// for non-finite logits. Greedy: the first maximum. Otherwise the tokens by descending logit (stable),
+// weights exp((logit - max) / temperature) in double, the shortest prefix reaching top_p of the total,
+// drawn with std::discrete_distribution from `random`.
+uint32_t sample_pe_token(const std::vector<float> &logits, const PeOptions &options, std::mt19937 &random);
+// PeSession on the B200: the layers of `model` (the PE checkpoint's, with its LM head) and a K/V cache of
+// `capacity` tokens (1..4096).
+class PeSession
+{
+  public:
+    PeSession(TextModel &model, int capacity, Precision precision = Precision::FP32);
+    ~PeSession();
+    PeSession(const PeSession &) = delete;
+    PeSession &operator=(const PeSession &) = delete;
+    // one token (step) or 1..32 tokens (append_chunk): embedded [rows][3072], cos / sin [rows][128] ->
+    // hidden [rows][3072]; std::invalid_argument past the capacity or for non-finite inputs
+    Tensor step(const Tensor &embedded, const Tensor &cos, const Tensor &sin);
+    Tensor append_chunk(const Tensor &embedded, const Tensor &cos, const Tensor &sin);
+    void reset();
+    int position() const;
+    // the LM head on one hidden row [3072] -> logits [131072]
+    std::vector<float> logits(const float *hidden_row);
+
+  private:
+    Tensor append(const Tensor &embedded, const Tensor &cos, const Tensor &sin, bool single);
+    GpuContext &ctx_;
+    ernie_cuda_pe_session *handle_ = nullptr;
+};
+struct PeResult // src/prompt_enhancer.h:12-18 (the text is the tokenizer's: out of scope here)
+{
+    std::vector<uint32_t> input_ids, generated_ids;
+    bool eos = false;
+};
+using PeProgress = std::function<void(const char *, int, int)>;
+using PeLogits = std::function<void(int, const std::vector<float> &)>;
+// enhance_prompt (src/prompt_enhancer.cpp:68-197) after the tokenizer: the chat prompt's token ids through
+// the session (prefill one token at a time, or in chunks of prefill_chunk <= 32), then up to
+// options.max_tokens sampled tokens, stopping after the end-of-sequence token 2. embeddings: the PE's BF16
+// table (raw or a checkpoint with model.embed_tokens.weight); frequencies: its 64 YaRN inverse
+// frequencies (rope-inv-freq.f32). Progress "prefill" / "decode" as the reference reports them.
+PeResult enhance_prompt_from_ids(TextModel &model, const std::string &embeddings, const std::vector<float> &frequencies,
+                                 const std::vector<uint32_t> &input_ids, const PeOptions &options,
+                                 Precision precision = Precision::FP32, int prefill_chunk = 1,
+                                 const PeProgress &progress = {}, const PeLogits &observe = {});
 
 // ---- generate from token ids (src/pipeline.cpp:489-575, everything after the tokenizer) -------------
 struct GenerationModels // the device-resident stages and the package's small tables

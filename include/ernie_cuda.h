@@ -50,6 +50,7 @@ typedef struct ernie_cuda_session ernie_cuda_session;
 typedef struct ernie_cuda_text_model ernie_cuda_text_model; /* prompt encoder layers (Text encoder section) */
 typedef struct ernie_cuda_vae ernie_cuda_vae;               /* VAE decoder (VAE decoder section) */
 typedef struct ernie_cuda_vae_encoder ernie_cuda_vae_encoder; /* VAE encoder (VAE encoder section) */
+typedef struct ernie_cuda_pe_session ernie_cuda_pe_session;   /* prompt enhancer (Prompt enhancer section) */
 
 /* Host weights of one block, as tools/build_dit_weights.py:19-31 binds them to the block graph. */
 typedef struct
@@ -263,6 +264,11 @@ int ernie_cuda_text_model_load_safetensors(ernie_cuda_text_model *model, int num
                                            int count);
 int ernie_cuda_vae_load_safetensors(ernie_cuda_vae *vae, const char *const *files, int count);
 int ernie_cuda_vae_encoder_load_safetensors(ernie_cuda_vae_encoder *encoder, const char *const *files, int count);
+/* The prompt enhancer's checkpoint: model.layers.{l}.* for l < num_layers (the same tensor names as the
+   text layers after "language_model."), model.norm.weight and lm_head.weight (or, tied,
+   model.embed_tokens.weight) into a text model and its LM head. */
+int ernie_cuda_pe_model_load_safetensors(ernie_cuda_text_model *model, int num_layers, const char *const *files,
+                                         int count);
 /* The header of one file: the number of tensors, and tensor `index` (in name order): name, dtype
    ("BF16", "F16", "F32", ...; 8 bytes), shape (up to 8 dims). */
 int ernie_cuda_safetensors_count(const char *path, int *count);
@@ -336,6 +342,32 @@ int ernie_cuda_vae_encode(ernie_cuda_vae_encoder *encoder, const uint8_t *rgb, i
 /* Device buffers on the context's stream; synchronous only when nonfinite is non-null. */
 int ernie_cuda_vae_encode_device(ernie_cuda_vae_encoder *encoder, const uint8_t *rgb, int width, int height,
                                  int precision, float *mean, float *packed, float *normalized, int *nonfinite);
+
+/* ---- Prompt enhancer (optional: the LM that rewrites the prompt before the text encoder) -------------
+   PeSession (src/pe_session.h:9-42) and the head of enhance_prompt (src/prompt_enhancer.cpp:68-197) on one
+   B200: the Mistral decoder layers of a text model (the PE checkpoint's 26 layers) with a per-layer K/V
+   cache, and the LM head of head.ncnn.param (tools/build_pe_model.py:100-105: RMSNorm eps 1e-5, then the
+   131072 x 3072 projection). The tokenizer and sampling stay on the host (the C++ surface has
+   sample_pe_token and enhance_prompt_from_ids). precision: ERNIE_PRECISION_FP32 (FP32-exact; the
+   reference's PE is CPU FP32) or ERNIE_PRECISION_BF16. */
+/* LM head weights of a text model: final RMSNorm weight [3072] FP32 and lm_head [131072][3072] BF16. */
+int ernie_cuda_text_model_upload_head(ernie_cuda_text_model *model, const float *norm, const uint16_t *lm_head);
+/* Seeded random-init head (include/ernie_synth.h, ERNIE_SYNTH_TEXT_HEAD_LAYER). */
+int ernie_cuda_text_model_synthesize_head(ernie_cuda_text_model *model, uint64_t seed);
+/* A session of `capacity` tokens (1..4096) over all the model's layers. */
+int ernie_cuda_pe_session_create(ernie_cuda_text_model *model, int capacity, int precision,
+                                 ernie_cuda_pe_session **out);
+int ernie_cuda_pe_session_destroy(ernie_cuda_pe_session *session);
+int ernie_cuda_pe_session_reset(ernie_cuda_pe_session *session);
+int ernie_cuda_pe_session_position(ernie_cuda_pe_session *session, int *position);
+/* append_chunk / step: `rows` (1..32) new tokens at the session's position, embedded [rows][3072] and
+   their rotary rows cos / sin [rows][128] (host FP32) -> the last layer's hidden states [rows][3072]
+   (host). Rejects more rows than the capacity left and non-finite inputs; a call that fails on the device
+   leaves the session unusable until reset (as PeSession does). */
+int ernie_cuda_pe_session_append(ernie_cuda_pe_session *session, const float *embedded, const float *cos,
+                                 const float *sin, int rows, float *hidden);
+/* logits [131072] (host FP32) of one hidden row [3072] through the model's LM head. */
+int ernie_cuda_pe_logits(ernie_cuda_pe_session *session, const float *hidden, float *logits);
 
 /* ---- Ulysses sequence parallelism (one process per GPU, 2, 4 or 8 members, BF16) ---------------
    Tokens are split into contiguous shards of S = ceil(N / world) rows (rounded up to 16); every member

@@ -124,6 +124,9 @@ enum ernie_synth_text_tensor
     ERNIE_SYNTH_TEXT_GAMMA_MLP = 8
 };
 #define ERNIE_SYNTH_TEXT_STREAM(layer, tensor) (0x54455854ULL * 4096u + (uint64_t)((layer) + 1) * 64u + (uint64_t)(tensor))
+/* The prompt enhancer's LM head on a text model: lm_head [131072][3072] N(0, 0.02) BF16 and the final
+ * RMSNorm weight 1 + N(0, 0.02), streams ERNIE_SYNTH_TEXT_STREAM(ERNIE_SYNTH_TEXT_HEAD_LAYER, 0 / 1). */
+#define ERNIE_SYNTH_TEXT_HEAD_LAYER 1023
 
 /* VAE decoder tensors are addressed by their diffusers parameter name (e.g. "decoder.conv_in.weight"):
  * stream = FNV-1a 64 of the name. Values are FP32, float(N(0,1) * scale) + offset, with

@@ -17,6 +17,11 @@ with the constants of text_constants (src/text_encoder.cpp:77-100): cos/sin of t
 halves of the 128-wide row and the causal mask (-FLT_MAX above the diagonal). float64 throughout; the
 weights are the exact BF16 values. Synthetic weights follow include/ernie_synth.h's text streams.
 
+The prompt enhancer (src/prompt_enhancer.cpp, src/pe_session.cpp) runs the same layer over its own
+checkpoint with a K/V cache: by causality, appending tokens chunk by chunk must give each token the hidden
+state of the full causal run, which is what the tests compare against. Its head (head.ncnn.param,
+tools/build_pe_model.py:100-105) is rms_norm(h, model.norm) @ lm_head^T.
+
 Parity of values is unpinned: the reference's text fixtures hash in*.f32 / out0.f32 files that are not in
 its tree, and the official weights are not available.
 """
@@ -107,3 +112,19 @@ def run_blocks(layers, x, cos, sin):
     for w in layers:
         x = layer(w, x, cos, sin)
     return x
+
+
+HEAD_LAYER = 1023  # ERNIE_SYNTH_TEXT_HEAD_LAYER
+
+
+def head_weights(seed, rows):
+    """The synthetic PE head: final RMSNorm weight [3072] and the first `rows` rows of lm_head (float32)."""
+    gamma = synth_f32_from_bf16(seed, text_stream(HEAD_LAYER, 1), HIDDEN, WEIGHT_STD, 1.0)
+    w = bf16_to_f32(synth_bf16(seed, text_stream(HEAD_LAYER, 0), rows * HIDDEN).reshape(rows, HIDDEN))
+    return gamma, w
+
+
+def head_logits(gamma, w, hidden):
+    """Logits of one hidden row against the given lm_head rows (float64)."""
+    h = np.asarray(hidden, np.float64).reshape(1, HIDDEN)
+    return (rms_norm(h, gamma) @ np.asarray(w, np.float64).T)[0]

@@ -364,6 +364,40 @@ int main()
         try { generate_img2img_from_ids(models, {5, 9, 100}, 8, odd, ir); }
         catch (const std::invalid_argument &) { threw = true; }
         REQUIRE(threw, "img2img image of another size accepted");
+        // the prompt enhancer after its tokenizer (enhance_prompt, src/prompt_enhancer.cpp:68-197): greedy and
+        // seeded decoding are reproducible, every step's logits are observed, token ids stay in the vocabulary
+        {
+            TextModel pe(ctx, 2);
+            pe.synthesize(21);
+            pe.synthesize_head(21);
+            PeOptions o;
+            o.greedy = true;
+            o.max_tokens = 6;
+            int observed = 0, decode_reports = 0;
+            const PeResult g1 = enhance_prompt_from_ids(
+                pe, table, tf, {5, 9, 100}, o, Precision::FP32, 1,
+                [&](const char *stage, int, int) { decode_reports += std::string(stage) == "decode"; },
+                [&](int, const std::vector<float> &l) { observed += l.size() == 131072; });
+            const PeResult g2 = enhance_prompt_from_ids(pe, table, tf, {5, 9, 100}, o, Precision::FP32, 1);
+            REQUIRE(!g1.generated_ids.empty() && g1.generated_ids.size() <= 6 && g1.generated_ids == g2.generated_ids,
+                    "greedy PE decode not reproducible");
+            REQUIRE(observed == int(g1.generated_ids.size()) && decode_reports >= 1, "PE observers");
+            for (uint32_t id : g1.generated_ids) REQUIRE(id < 131072, "PE token outside the vocabulary");
+            REQUIRE(g1.eos == (g1.generated_ids.back() == 2), "PE end-of-sequence flag");
+            o.greedy = false;
+            o.seed = 7;
+            const PeResult s1 = enhance_prompt_from_ids(pe, table, tf, {5, 9, 100}, o, Precision::BF16, 3);
+            const PeResult s2 = enhance_prompt_from_ids(pe, table, tf, {5, 9, 100}, o, Precision::BF16, 3);
+            REQUIRE(s1.generated_ids == s2.generated_ids, "seeded PE decode not reproducible");
+            bool rejected = false;
+            try { enhance_prompt_from_ids(pe, table, tf, {5}, o, Precision::BF16, 33); }
+            catch (const std::invalid_argument &) { rejected = true; }
+            REQUIRE(rejected, "PE prefill chunk 33 accepted");
+            rejected = false;
+            try { enhance_prompt_from_ids(pe, table, tf, {}, o, Precision::BF16, 1); }
+            catch (const std::invalid_argument &) { rejected = true; }
+            REQUIRE(rejected, "empty PE input accepted");
+        }
         std::filesystem::remove_all(folder);
     }
     catch (const std::exception &e)

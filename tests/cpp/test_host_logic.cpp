@@ -459,6 +459,54 @@ static void vae_contract()
     REQUIRE(enc_params == 34426112, "VAE encoder parameter count " << enc_params);
 }
 
+// sample_pe_token (src/prompt_enhancer.cpp:33-66) with the cases of the reference's sampling test
+// (tests/test_pe_sampling.cpp:24-100): greedy ties, top-p truncation, frequencies, reproducibility, options
+static void pe_sampling_contract()
+{
+    PeOptions options;
+    std::mt19937 first(42), second(42);
+    options.greedy = true;
+    REQUIRE(sample_pe_token({-1.f, 4.f, 4.f}, options, first) == 1, "greedy tie must choose the first token");
+    options.greedy = false;
+    options.temperature = 1;
+    options.top_p = .6f;
+    const std::vector<float> dist = {std::log(.7f), std::log(.2f), std::log(.1f)};
+    for (int i = 0; i < 32; ++i) REQUIRE(sample_pe_token(dist, options, first) == 0, "top-p 0.6 keeps only the 0.7 token");
+    options.top_p = 1;
+    first.seed(20260906);
+    int counts[3] = {0, 0, 0};
+    constexpr int draws = 100000;
+    for (int i = 0; i < draws; ++i) ++counts[sample_pe_token(dist, options, first)];
+    const double expected[3] = {.7, .2, .1};
+    for (int i = 0; i < 3; ++i)
+        REQUIRE(std::abs(double(counts[i]) / draws - expected[i]) <= .01, "sampling frequency " << i);
+    first.seed(42);
+    second.seed(42);
+    for (int i = 0; i < 32; ++i)
+        REQUIRE(sample_pe_token({-1.f, 4.f, 4.f}, options, first) == sample_pe_token({-1.f, 4.f, 4.f}, options, second),
+                "sampling must be reproducible");
+    for (float bad : {0.f, -1.f, INFINITY, NAN})
+    {
+        options.temperature = bad;
+        REQUIRE(throws<std::invalid_argument>([&] { sample_pe_token(dist, options, first); }), "temperature " << bad);
+    }
+    options.temperature = 1;
+    for (float bad : {0.f, -1.f, 1.01f, INFINITY, NAN})
+    {
+        options.top_p = bad;
+        REQUIRE(throws<std::invalid_argument>([&] { sample_pe_token(dist, options, first); }), "top-p " << bad);
+    }
+    options.top_p = 1;
+    for (int bad : {0, -1, 2049})
+    {
+        options.max_tokens = bad;
+        REQUIRE(throws<std::invalid_argument>([&] { sample_pe_token(dist, options, first); }), "max tokens " << bad);
+    }
+    options.max_tokens = 8;
+    REQUIRE(throws<std::invalid_argument>([&] { sample_pe_token({}, options, first); }), "empty logits accepted");
+    REQUIRE(throws<std::runtime_error>([&] { sample_pe_token({0.f, NAN}, options, first); }), "NaN logits accepted");
+}
+
 // text_constants and text_embeddings (src/text_encoder.cpp:48-100) without a device
 static void text_contract()
 {
@@ -490,6 +538,7 @@ int main()
     recovery_contract();
     tensor_io_contract();
     img2img_contract();
+    pe_sampling_contract();
     if (failures)
     {
         std::cerr << failures << " host contract failure(s)\n";
