@@ -558,6 +558,127 @@ def run_vae_encode(args):
         pg.destroy_process_group()
 
 
+# ---- the optional prompt enhancer (--stage pe) ---------------------------------------------------------
+PE_METRIC = "prompt enhancer decode ms/token (26 Mistral layers + 131072-way LM head, K/V cache after a 512-token prompt)"
+PE_LAYERS, PE_PROMPT = 26, 512
+# BF16 weights streamed per decoded token: 26 layers x (q/k/v/o + gate/up/down) + the LM head
+PE_BYTES_PER_TOKEN = PE_LAYERS * TEXT_LAYER_BYTES + 2 * 131072 * 3072
+
+
+def pe_cpu_sample():
+    """One decode token of the oracle (float64 numpy, all host cores): one layer on one token x 26 plus the LM
+    head measured on 16384 of its 131072 rows x 8. Returns (seconds per token, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import text as ot
+    w = ot.TextLayerWeights(4321, 0)
+    f = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
+    cos, sin = ot.text_constants(f, 1)
+    x = np.random.default_rng(0).standard_normal((1, 3072)) * 0.2
+    ot.layer(w, x, cos, sin)  # warm (weight widening cached)
+    t0 = time.perf_counter()
+    ot.layer(w, x, cos, sin)
+    layer_s = time.perf_counter() - t0
+    gamma, head = ot.head_weights(4321, 16384)
+    head64 = head.astype(np.float64)
+    t0 = time.perf_counter()
+    ot.head_logits(gamma, head64, x[0])
+    head_s = (time.perf_counter() - t0) * 8
+    return PE_LAYERS * layer_s + head_s, (f"one oracle layer on one token ({layer_s:.3f} s) x26 + the LM head on "
+                                          f"16384 rows ({head_s / 8:.3f} s) x8; attention over the cache omitted")
+
+
+def run_pe_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times, sample = [], ""
+    for i in range(args.warmup + args.steps):
+        dt, sample = pe_cpu_sample()
+        if i >= args.warmup:
+            times.append(dt)
+    ms = 1000.0 * statistics.median(times)
+    cpu = {"value": ms, "unit": "ms/token", "cores": os.cpu_count() or 1, "kind": "port", "sample": sample}
+    line = {"metric": PE_METRIC, "impl": "reference", "value": ms, "unit": "ms/token", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "prompt enhancer decode, one token", "sample": sample}, "cpu_baseline": cpu,
+            "e2e": {"value": ms, "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_pe(args):
+    """One decoded token per GPU per step: PeSession append of one row + the LM head, after a 512-token prefill."""
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    ctx = ec.Context(local)
+    model = ec.TextModel(ctx, PE_LAYERS)
+    model.synthesize(4321)
+    model.synthesize_head(4321)
+    precision = ec.BF16 if args.precision == "bf16" else ec.FP32
+    total = PE_PROMPT + args.warmup + args.steps
+    f = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
+    cos, sin, _ = ec.text_constants(f, min(total, 2048))
+    x = (np.random.default_rng(dp.request_seed(5000, rank)).standard_normal((total, 3072)) * 0.2).astype(np.float32)
+    session = ec.PeSession(model, total, precision)
+    t0 = time.perf_counter()
+    for c in range(0, PE_PROMPT, 32):
+        hidden = session.append(x[c:c + 32], cos[c:c + 32], sin[c:c + 32])
+    prefill_s = time.perf_counter() - t0
+    pos = PE_PROMPT
+    for _ in range(args.warmup):
+        hidden = session.append(x[pos:pos + 1], cos[pos:pos + 1], sin[pos:pos + 1])
+        logits = session.logits(hidden[0])
+        pos += 1
+    clocks = ClockSampler(local)
+    barrier(pg)
+    ctx.synchronize()
+    clocks.start()
+    ctx.record(0)
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        hidden = session.append(x[pos:pos + 1], cos[pos:pos + 1], sin[pos:pos + 1])
+        logits = session.logits(hidden[0])
+        pos += 1
+    ctx.record(1)
+    ctx.synchronize()
+    wall = time.perf_counter() - w0
+    clock_info = clocks.stop()
+    barrier(pg)
+    ms = max_over_ranks(pg, ctx.elapsed(0, 1)) / args.steps
+    e2e_ms = 1000.0 * max_over_ranks(pg, wall) / args.steps
+    assert np.isfinite(logits).all()
+    _, _, hbm_peak, peak_kind = peaks()
+    gbs = PE_BYTES_PER_TOKEN / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        s_tok, sample = pe_cpu_sample()
+        cpu = {"value": 1000.0 * s_tok, "unit": "ms/token", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": sample}
+    if rank == 0:
+        line = {"metric": PE_METRIC, "value": ms, "unit": "ms/token", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+                "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+                "config": {"workload": f"prompt enhancer, {PE_LAYERS} layers, {PE_PROMPT}-token prompt prefilled in "
+                                       "32-token chunks, then one token per step (append + LM head), one session "
+                                       "per GPU", "prefill_tokens_per_s": PE_PROMPT / prefill_s,
+                           "weight_bytes_per_token": PE_BYTES_PER_TOKEN,
+                           "l2": "inputs larger than L2 (6.9 GB of weights per token)"},
+                "roofline": {"bound": "hbm", "kernel": "whole decode step (weight streaming)", "achieved": gbs,
+                             "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": peak_kind,
+                             "traffic": None},
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_ms, "unit": "ms/token", "h2d_bytes_per_step": 3072 * 4 + 2 * 128 * 4,
+                        "d2h_bytes_per_step": 3072 * 4 + 131072 * 4,
+                        "call": "ernie_cuda_pe_session_append (one host row) + ernie_cuda_pe_logits (host logits)"},
+                "gpu_launches": args.steps * (9 * PE_LAYERS + 2), "clocks": clock_info}
+        print(json.dumps(line), flush=True)
+    session.close()
+    model.close()
+    ctx.close()
+    if pg is not None:
+        pg.destroy_process_group()
+
+
 def pipeline_stages(ctx, args, ms_per_step, reps=3):
     """Device time of the whole image on this GPU: prompt encode (25 layers at the config's text bucket),
     8 denoise steps (the metric's ms_per_step x 8) and the VAE decode (unpacked latent 2h x 2w), BF16."""
@@ -641,10 +762,10 @@ def main():
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--stage", choices=["dit", "vae", "text", "vae-encode"], default="dit",
+    ap.add_argument("--stage", choices=["dit", "vae", "text", "vae-encode", "pe"], default="dit",
                     help="dit: the denoise loop (the metric); vae: the VAE decode after it; text: the prompt "
                          "encoder before it (at the config's text bucket); vae-encode: img2img's image encoder "
-                         "(1024x1024)")
+                         "(1024x1024); pe: the optional prompt enhancer's decode")
     ap.add_argument("--vae-latent", default=None,
                     help="profiling aid: H,W of the unpacked latent of --stage vae (default 128,128: 1024x1024)")
     args = ap.parse_args()
@@ -661,6 +782,8 @@ def main():
         return run_text_reference(args) if args.impl == "reference" else run_text(args)
     if args.stage == "vae-encode":
         return run_vae_encode_reference(args) if args.impl == "reference" else run_vae_encode(args)
+    if args.stage == "pe":
+        return run_pe_reference(args) if args.impl == "reference" else run_pe(args)
     if args.impl == "reference":
         return run_reference(args)
 

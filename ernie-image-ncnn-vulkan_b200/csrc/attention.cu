@@ -158,6 +158,114 @@ __global__ void __launch_bounds__(kFThreads) attention_f32_kernel(AttentionF32Ar
         }
     }
 }
+// ------------------------------------------------------------------ decode: a few query rows, many keys
+// One CTA per (head, query row); its 8 warps take consecutive groups of 4 keys in turn. Per key a warp forms
+// the FP32 score (4 dimensions per lane, reduced across the warp) and updates its own online softmax, the
+// total and P.V in FP64 as above; the warps' partial results are merged at the end. Same arithmetic
+// contract as attention_f32_kernel: FP32 scores and exponentials, FP64 sums.
+constexpr int kDWarps = 8, kDKeys = 4;
+
+__device__ __forceinline__ float warp_sum_f32(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(kDWarps * 32) attention_decode_kernel(AttentionF32Args a)
+{
+    __shared__ __align__(16) float qs[kDim];
+    __shared__ float wm[kDWarps];
+    __shared__ double wl[kDWarps];
+    __shared__ double wo[kDWarps][kDim];
+    const int head = blockIdx.x, qrow = blockIdx.y;
+    const int kv_head = head / (a.heads / a.kv_heads);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const float scale = 1.f / sqrtf(static_cast<float>(kDim));
+    if (threadIdx.x < kDim) qs[threadIdx.x] = a.q[head * a.q_head_stride + static_cast<size_t>(qrow) * kDim + threadIdx.x];
+    __syncthreads();
+    const float4 q4 = *reinterpret_cast<const float4 *>(qs + lane * 4);
+    const float *kh = a.k + kv_head * a.kv_head_stride;
+    const float *vh = a.v + kv_head * a.kv_head_stride;
+    const float *mrow = nullptr;
+    if (a.mask)
+        mrow = a.mask + (static_cast<size_t>(a.mask_heads == 1 ? 0 : head) * a.mask_rows + (a.mask_rows == 1 ? 0 : qrow)) *
+                            a.nk;
+    const int kv_end = a.causal ? min(a.kv_len, qrow + a.causal_offset + 1) : a.kv_len;
+    float m_w = -INFINITY;
+    double l_w = 0.0, o[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int key0 = warp * kDKeys; key0 < kv_end; key0 += kDWarps * kDKeys)
+    {
+        float sc[kDKeys];
+        float4 v4[kDKeys];
+#pragma unroll
+        for (int j = 0; j < kDKeys; ++j)
+        {
+            const int key = key0 + j;
+            float d = 0.f;
+            v4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (key < kv_end)
+            {
+                const float4 k4 = *reinterpret_cast<const float4 *>(kh + static_cast<size_t>(key) * kDim + lane * 4);
+                v4[j] = *reinterpret_cast<const float4 *>(vh + static_cast<size_t>(key) * kDim + lane * 4);
+                d = fmaf(q4.w, k4.w, fmaf(q4.z, k4.z, fmaf(q4.y, k4.y, q4.x * k4.x)));
+            }
+            sc[j] = d;
+        }
+#pragma unroll
+        for (int j = 0; j < kDKeys; ++j) sc[j] = warp_sum_f32(sc[j]);
+#pragma unroll
+        for (int j = 0; j < kDKeys; ++j)
+        {
+            const int key = key0 + j;
+            if (key >= kv_end) break;
+            const float s = sc[j] * scale + (mrow ? mrow[key] : 0.f);
+            if (s == -INFINITY) continue;
+            const float m_new = fmaxf(m_w, s);
+            const double alpha = static_cast<double>(expf(m_w - m_new)); // 0 while m_w is -inf
+            const double p = static_cast<double>(expf(s - m_new));
+            l_w = l_w * alpha + p;
+            o[0] = fma(p, static_cast<double>(v4[j].x), o[0] * alpha);
+            o[1] = fma(p, static_cast<double>(v4[j].y), o[1] * alpha);
+            o[2] = fma(p, static_cast<double>(v4[j].z), o[2] * alpha);
+            o[3] = fma(p, static_cast<double>(v4[j].w), o[3] * alpha);
+            m_w = m_new;
+        }
+    }
+    if (lane == 0)
+    {
+        wm[warp] = m_w;
+        wl[warp] = l_w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wo[warp][lane * 4 + i] = o[i];
+    __syncthreads();
+    if (threadIdx.x >= kDim) return;
+    const int d = threadIdx.x;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDWarps; ++w) m = fmaxf(m, wm[w]);
+    double l = 0.0, acc = 0.0;
+#pragma unroll
+    for (int w = 0; w < kDWarps; ++w)
+    {
+        if (wm[w] == -INFINITY) continue;
+        const double f = static_cast<double>(expf(wm[w] - m));
+        l += wl[w] * f;
+        acc += wo[w][d] * f;
+    }
+    const float out = static_cast<float>(acc / l);
+    if (a.out_mode == 0)
+        a.out_f32[(static_cast<size_t>(head) * a.nq + qrow) * kDim + d] = out;
+    else if (a.out_mode == 2)
+        a.out_split3[(static_cast<size_t>(qrow) * a.heads + head) * kDim + d] = __float2bfloat16_rn(out);
+    else
+    {
+        const size_t plane = static_cast<size_t>(a.heads) * kDim;
+        __nv_bfloat16 *dst = a.out_split3 + static_cast<size_t>(qrow) * 3 * plane + static_cast<size_t>(head) * kDim + d;
+        split3(out, dst[0], dst[plane], dst[2 * plane]);
+    }
+}
 } // namespace
 
 int prepare_attention_kernels()
@@ -173,6 +281,12 @@ int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream)
         (args.mask && args.mask_heads != 1 && args.mask_heads != args.heads) ||
         (args.mask && args.mask_rows != 1 && args.mask_rows != args.nq))
         return cudaErrorInvalidValue;
+    if (args.decode)
+    {
+        if (args.nq > 4 || args.width != kDim) return cudaErrorInvalidValue;
+        attention_decode_kernel<<<dim3(args.heads, args.nq), kDWarps * 32, 0, stream>>>(args);
+        return cudaGetLastError();
+    }
     const dim3 grid((args.nq + kFQ - 1) / kFQ, args.heads);
     attention_f32_kernel<<<grid, kFThreads, kFSmem, stream>>>(args);
     return cudaGetLastError();

@@ -145,6 +145,7 @@ struct AttentionF32Args
     __nv_bfloat16 *out_split3;
     int causal;            // key j visible to query i iff j <= i + causal_offset
     int causal_offset = 0; // position of query 0 (a KV-cached chunk appended after causal_offset keys)
+    int decode = 0;        // 1..4 query rows of width 128: the keys split over warps (attention_decode_kernel)
 };
 int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream);
 
@@ -250,6 +251,29 @@ int prepare_conv_kernels();
 // qkv FP32 [tokens][6144] -> rotated head-major q [32][tokens][128], k [8][tokens][128] and v [8][tokens][128].
 int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, int tokens, float *q, float *k, float *v,
                      cudaStream_t stream);
+// Weight-streaming product for the prompt enhancer's decode steps (1..4 rows): y[r][n] = sum_k x[r][k] W[n][k]
+// over BF16 weights [n_rows][k] and an A operand in the tensor-core layout ([rows][planes * k] BF16; planes 3:
+// x = hi + mid + lo in FP32). F32Out: out[r][n] = y (row stride ldo). Resid: out[r][n] += y. SwiGLU over
+// interleaved [up; gate] 64-row groups (n_rows = 2 * ffn): h[r][i] = up_i * silu(gate_i), written as the
+// next product's operand (BF16, or three planes with h_split3), with the GEMM epilogue's arithmetic.
+enum class GemvEpilogue : int
+{
+    F32Out = 0,
+    Resid = 1,
+    SwiGLU = 2,
+};
+struct GemvArgs
+{
+    const __nv_bfloat16 *a = nullptr;
+    int rows = 0, k = 0, planes = 1;
+    const __nv_bfloat16 *w = nullptr;
+    int n_rows = 0;
+    float *out = nullptr;
+    int ldo = 0;
+    __nv_bfloat16 *h = nullptr;
+    int ffn = 0, h_split3 = 0;
+};
+int launch_gemv(const GemvArgs &args, GemvEpilogue epilogue, cudaStream_t stream);
 // The same as the BF16 operands of the tcgen05 attention: q [32][rows_pad][128], k [8][rows_pad][128],
 // v^T [8][128][rows_pad].
 int launch_text_rope_bf16(const float *qkv, const float *cos_t, const float *sin_t, int tokens, int rows_pad,

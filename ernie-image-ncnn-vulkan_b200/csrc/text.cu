@@ -110,4 +110,140 @@ int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, i
     text_rope_kernel<<<dim3(tokens, kTextQHeads + 2 * kTextKvHeads), 64, 0, stream>>>(qkv, cos_t, sin_t, tokens, q, k, v);
     return cudaGetLastError();
 }
+
+// ---- decode products (prompt enhancer) -------------------------------------------------------------
+namespace
+{
+constexpr int kGemvRows = 4, kGemvWarps = 8, kGemvMaxK = 9216;
+
+__device__ __forceinline__ float warp_sum_f(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// sum_k x[r][k] * w[k] for the block's staged rows, one weight row per warp, 8 BF16 per lane per step
+__device__ __forceinline__ void gemv_row(const float *xs, int rows, int k, const __nv_bfloat16 *w, int lane,
+                                         float (&acc)[kGemvRows])
+{
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) acc[r] = 0.f;
+    // four 16-byte weight loads in flight per lane (k is a multiple of 256)
+#pragma unroll 4
+    for (int k0 = lane * 8; k0 < k; k0 += 256)
+    {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(w + k0));
+        const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+        float wv[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            const float2 f = __bfloat1622float2(p[j]);
+            wv[2 * j] = f.x;
+            wv[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r)
+        {
+            if (r >= rows) break;
+            const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * k + k0);
+            const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * k + k0 + 4);
+            float s = acc[r];
+            s = fmaf(x0.x, wv[0], s);
+            s = fmaf(x0.y, wv[1], s);
+            s = fmaf(x0.z, wv[2], s);
+            s = fmaf(x0.w, wv[3], s);
+            s = fmaf(x1.x, wv[4], s);
+            s = fmaf(x1.y, wv[5], s);
+            s = fmaf(x1.z, wv[6], s);
+            s = fmaf(x1.w, wv[7], s);
+            acc[r] = s;
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) acc[r] = warp_sum_f(acc[r]);
+}
+
+__device__ __forceinline__ void store_h(const GemvArgs &a, int r, int i, float v)
+{
+    if (a.h_split3)
+    {
+        __nv_bfloat16 *dst = a.h + static_cast<size_t>(r) * 3 * a.ffn + i;
+        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+        const float r1 = v - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        dst[0] = hi;
+        dst[a.ffn] = mid;
+        dst[2 * a.ffn] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    }
+    else
+        a.h[static_cast<size_t>(r) * a.ffn + i] = __float2bfloat16_rn(v);
+}
+
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvArgs a, int epi)
+{
+    extern __shared__ float xs[]; // [rows][k] FP32
+    const int total = a.rows * a.k;
+    for (int i = threadIdx.x; i < total; i += blockDim.x)
+    {
+        const int r = i / a.k, c = i - r * a.k;
+        const __nv_bfloat16 *src = a.a + static_cast<size_t>(r) * a.planes * a.k + c;
+        float v = __bfloat162float(src[0]);
+        if (a.planes == 3) v = (v + __bfloat162float(src[a.k])) + __bfloat162float(src[2 * a.k]);
+        xs[i] = v;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int outputs = epi == static_cast<int>(GemvEpilogue::SwiGLU) ? a.ffn : a.n_rows;
+    const int o = blockIdx.x * kGemvWarps + warp;
+    if (o >= outputs) return;
+    float acc[kGemvRows];
+    if (epi == static_cast<int>(GemvEpilogue::SwiGLU))
+    {
+        // feature o: up row (o / 64) * 128 + o % 64, gate row 64 further
+        const int row_up = (o / 64) * 128 + (o % 64);
+        float gate[kGemvRows];
+        gemv_row(xs, a.rows, a.k, a.w + static_cast<size_t>(row_up + 64) * a.k, lane, gate);
+        gemv_row(xs, a.rows, a.k, a.w + static_cast<size_t>(row_up) * a.k, lane, acc);
+        if (lane == 0)
+            for (int r = 0; r < a.rows; ++r)
+            {
+                const float g = gate[r];
+                const float v = a.h_split3 ? acc[r] * __fdiv_rn(g, 1.f + expf(-g)) : acc[r] * __fdividef(g, 1.f + __expf(-g));
+                store_h(a, r, o, v);
+            }
+        return;
+    }
+    gemv_row(xs, a.rows, a.k, a.w + static_cast<size_t>(o) * a.k, lane, acc);
+    if (lane == 0)
+        for (int r = 0; r < a.rows; ++r)
+        {
+            float *dst = a.out + static_cast<size_t>(r) * a.ldo + o;
+            if (epi == static_cast<int>(GemvEpilogue::Resid)) *dst = *dst + acc[r];
+            else *dst = acc[r];
+        }
+}
+} // namespace
+
+int launch_gemv(const GemvArgs &a, GemvEpilogue epi, cudaStream_t stream)
+{
+    if (!a.a || !a.w || a.rows < 1 || a.rows > kGemvRows || a.k < 256 || a.k % 256 || a.k > kGemvMaxK ||
+        (a.planes != 1 && a.planes != 3) || a.n_rows < 1)
+        return cudaErrorInvalidValue;
+    int outputs = a.n_rows;
+    if (epi == GemvEpilogue::SwiGLU)
+    {
+        if (!a.h || a.ffn < 64 || a.ffn % 64 || a.n_rows != 2 * a.ffn) return cudaErrorInvalidValue;
+        outputs = a.ffn;
+    }
+    else if (!a.out || a.ldo < a.n_rows)
+        return cudaErrorInvalidValue;
+    static const cudaError_t attr = cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         kGemvRows * kGemvMaxK * 4);
+    if (attr != cudaSuccess) return attr;
+    const size_t smem = static_cast<size_t>(a.rows) * a.k * 4;
+    gemv_kernel<<<(outputs + kGemvWarps - 1) / kGemvWarps, kGemvWarps * 32, smem, stream>>>(a, static_cast<int>(epi));
+    return cudaGetLastError();
+}
 } // namespace ernie_b200

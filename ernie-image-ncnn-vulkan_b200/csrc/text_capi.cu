@@ -384,7 +384,8 @@ extern "C" int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *m, const
 // 131072 x 3072 projection tied to the embeddings (head.ncnn.param, tools/build_pe_model.py:100-105).
 // Per chunk of 1..32 new tokens at the session's position: the layer as above, the rotated K / V rows
 // appended to the layer's FP32 cache, and the FP32 attention of the chunk's queries over every cached key
-// up to each query's own position (FP64 sums; the decode is a few rows, so its cost is the weight stream).
+// up to each query's own position (FP64 sums). Decode steps (up to 4 rows) and the LM head stream their
+// weights through warp-per-row products (launch_gemv); prefill chunks use the tensor-core GEMM.
 namespace
 {
 constexpr int kPeMaxRows = 32, kPeMaxCapacity = 4096, kPeVocab = 131072;
@@ -427,6 +428,25 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
     const int splits = fp32 ? 3 : 1;
     const int bn = fp32 ? 128 : text_block_n(T, kTH, sms);
     const size_t layer_cache = static_cast<size_t>(8) * ps->capacity * 128;
+    // decode steps (a few rows) stream the weights through warp-per-row products; prefill chunks use the
+    // tensor cores
+    const bool gemv = T <= 4;
+    auto product = [&](const __nv_bfloat16 *a, const __nv_bfloat16 *w, int n_rows, int k, GemvEpilogue epi,
+                       float *out, int ldo) {
+        GemvArgs g;
+        g.a = a;
+        g.rows = T;
+        g.k = k;
+        g.planes = ps->planes;
+        g.w = w;
+        g.n_rows = n_rows;
+        g.out = out;
+        g.ldo = ldo;
+        g.h = ps->h;
+        g.ffn = kTFfn;
+        g.h_split3 = fp32 ? 1 : 0;
+        return launch_gemv(g, epi, s);
+    };
     for (int l = 0; l < m->num_layers; ++l)
     {
         const TextLayer &L = m->layers[static_cast<size_t>(l)];
@@ -438,7 +458,8 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         f32.error_flag = m->ctx->error_flag;
         ERNIE_LAUNCH(launch_norm_modulate(ps->x, T, kTH, L.gamma_attn, nullptr, nullptr, kTEps, 0, ps->a, fp32 ? 1 : 0, s),
                      "PE input_layernorm");
-        ERNIE_LAUNCH(launch_gemm(ps->a, L.wqkv, T, kTQkv, kTH, splits, bn, Epilogue::F32Bias, f32, sms, s, fp32),
+        ERNIE_LAUNCH(gemv ? product(ps->a, L.wqkv, kTQkv, kTH, GemvEpilogue::F32Out, ps->qkv, kTQkv)
+                          : launch_gemm(ps->a, L.wqkv, T, kTQkv, kTH, splits, bn, Epilogue::F32Bias, f32, sms, s, fp32),
                      "PE qkv projection");
         ERNIE_LAUNCH(launch_text_rope(ps->qkv, ps->cos_t, ps->sin_t, T, ps->q, ps->k, ps->v, s), "PE rotary");
         // the chunk's K / V rows of each of the 8 heads into the caches at rows pos..pos+T-1
@@ -464,6 +485,7 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         at.kv_head_stride = static_cast<long long>(ps->capacity) * 128;
         at.causal = 1;
         at.causal_offset = pos;
+        at.decode = gemv ? 1 : 0;
         at.out_mode = fp32 ? 1 : 2; // the o_proj operand: three BF16 planes or BF16, token-major
         at.out_split3 = ps->a;
         ERNIE_LAUNCH(launch_attention_f32(at, s), "PE attention");
@@ -472,7 +494,8 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         res.ldo = kTH;
         res.gate = m->ones;
         res.error_flag = m->ctx->error_flag;
-        ERNIE_LAUNCH(launch_gemm(ps->a, L.wo, T, kTH, kTQ, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
+        ERNIE_LAUNCH(gemv ? product(ps->a, L.wo, kTH, kTQ, GemvEpilogue::Resid, ps->x, kTH)
+                          : launch_gemm(ps->a, L.wo, T, kTH, kTQ, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
                      "PE o_proj");
         ERNIE_LAUNCH(launch_norm_modulate(ps->x, T, kTH, L.gamma_mlp, nullptr, nullptr, kTEps, 0, ps->a, fp32 ? 1 : 0, s),
                      "PE post_attention_layernorm");
@@ -482,10 +505,13 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         glu.ffn = kTFfn;
         glu.silu = 1;
         glu.error_flag = m->ctx->error_flag;
-        ERNIE_LAUNCH(launch_gemm(ps->a, L.wug, T, 2 * kTFfn, kTH, splits, fp32 ? 128 : text_block_n(T, 2 * kTFfn, sms),
-                                 Epilogue::Geglu, glu, sms, s, fp32),
+        ERNIE_LAUNCH(gemv ? product(ps->a, L.wug, 2 * kTFfn, kTH, GemvEpilogue::SwiGLU, nullptr, 0)
+                          : launch_gemm(ps->a, L.wug, T, 2 * kTFfn, kTH, splits,
+                                        fp32 ? 128 : text_block_n(T, 2 * kTFfn, sms), Epilogue::Geglu, glu, sms, s,
+                                        fp32),
                      "PE gate/up projection");
-        ERNIE_LAUNCH(launch_gemm(ps->h, L.wdown, T, kTH, kTFfn, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
+        ERNIE_LAUNCH(gemv ? product(ps->h, L.wdown, kTH, kTFfn, GemvEpilogue::Resid, ps->x, kTH)
+                          : launch_gemm(ps->h, L.wdown, T, kTH, kTFfn, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
                      "PE down_proj");
     }
     return ERNIE_CUDA_OK;
@@ -628,13 +654,16 @@ extern "C" int ernie_cuda_pe_logits(ernie_cuda_pe_session *ps, const float *hidd
     ERNIE_CUDA(cudaMemcpyAsync(ps->hrow, hidden, kTH * 4, cudaMemcpyHostToDevice, s), "PE head input");
     ERNIE_LAUNCH(launch_norm_modulate(ps->hrow, 1, kTH, m->head_norm, nullptr, nullptr, kTEps, 0, ps->ha, fp32 ? 1 : 0, s),
                  "PE head norm");
-    GemmEpilogueArgs f32;
-    f32.out = ps->logits;
-    f32.ldo = kPeVocab;
-    f32.error_flag = m->ctx->error_flag;
-    ERNIE_LAUNCH(launch_gemm(ps->ha, m->lm_head, 1, kPeVocab, kTH, fp32 ? 3 : 1, 128, Epilogue::F32Bias, f32,
-                             m->ctx->num_sms, s, fp32),
-                 "PE lm_head");
+    GemvArgs g;
+    g.a = ps->ha;
+    g.rows = 1;
+    g.k = kTH;
+    g.planes = ps->planes;
+    g.w = m->lm_head;
+    g.n_rows = kPeVocab;
+    g.out = ps->logits;
+    g.ldo = kPeVocab;
+    ERNIE_LAUNCH(launch_gemv(g, GemvEpilogue::F32Out, s), "PE lm_head");
     ERNIE_CUDA(cudaMemcpyAsync(logits, ps->logits, static_cast<size_t>(kPeVocab) * 4, cudaMemcpyDeviceToHost, s),
                "PE logits");
     return check_status(m);
