@@ -191,7 +191,9 @@ __global__ void __launch_bounds__(kDWarps * 32) attention_decode_kernel(Attentio
     if (a.mask)
         mrow = a.mask + (static_cast<size_t>(a.mask_heads == 1 ? 0 : head) * a.mask_rows + (a.mask_rows == 1 ? 0 : qrow)) *
                             a.nk;
-    const int kv_end = a.causal ? min(a.kv_len, qrow + a.causal_offset + 1) : a.kv_len;
+    const int offset = a.position ? *a.position : a.causal_offset;
+    const int kv_len = a.position ? offset + a.nq : a.kv_len;
+    const int kv_end = a.causal ? min(kv_len, qrow + offset + 1) : kv_len;
     float m_w = -INFINITY;
     double l_w = 0.0, o[4] = {0.0, 0.0, 0.0, 0.0};
     for (int key0 = warp * kDKeys; key0 < kv_end; key0 += kDWarps * kDKeys)

@@ -146,6 +146,9 @@ struct AttentionF32Args
     int causal;            // key j visible to query i iff j <= i + causal_offset
     int causal_offset = 0; // position of query 0 (a KV-cached chunk appended after causal_offset keys)
     int decode = 0;        // 1..4 query rows of width 128: the keys split over warps (attention_decode_kernel)
+    // decode only, nullable: the device-resident position of query 0, in place of causal_offset (and
+    // kv_len = *position + nq), so that a captured step is position-independent
+    const int *position = nullptr;
 };
 int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream);
 
@@ -274,6 +277,12 @@ struct GemvArgs
     int ffn = 0, h_split3 = 0;
 };
 int launch_gemv(const GemvArgs &args, GemvEpilogue epilogue, cudaStream_t stream);
+int prepare_gemv_kernels(); // shared-memory attribute, before any stream capture
+// The chunk's K / V rows (head-major [8][rows][128]) into the caches [8][capacity][128] at rows
+// *position.., then (advance) *position += rows.
+int launch_pe_cache_append(const float *k, const float *v, int rows, float *k_cache, float *v_cache, int capacity,
+                           const int *position, cudaStream_t stream);
+int launch_pe_advance(int *position, int rows, cudaStream_t stream);
 // The same as the BF16 operands of the tcgen05 attention: q [32][rows_pad][128], k [8][rows_pad][128],
 // v^T [8][128][rows_pad].
 int launch_text_rope_bf16(const float *qkv, const float *cos_t, const float *sin_t, int tokens, int rows_pad,

@@ -226,6 +226,38 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvArgs a, int e
 }
 } // namespace
 
+__global__ void pe_cache_append_kernel(const float *k, const float *v, int rows, float *kc, float *vc, int capacity,
+                                       const int *position)
+{
+    const int r = blockIdx.x, head = blockIdx.y, lane = threadIdx.x; // 32 threads: one float4 each
+    const size_t src = (static_cast<size_t>(head) * rows + r) * 128 + lane * 4;
+    const size_t dst = (static_cast<size_t>(head) * capacity + *position + r) * 128 + lane * 4;
+    *reinterpret_cast<float4 *>(kc + dst) = *reinterpret_cast<const float4 *>(k + src);
+    *reinterpret_cast<float4 *>(vc + dst) = *reinterpret_cast<const float4 *>(v + src);
+}
+
+__global__ void pe_advance_kernel(int *position, int rows) { *position += rows; }
+
+int launch_pe_cache_append(const float *k, const float *v, int rows, float *k_cache, float *v_cache, int capacity,
+                           const int *position, cudaStream_t stream)
+{
+    if (!k || !v || !k_cache || !v_cache || !position || rows < 1 || capacity < rows) return cudaErrorInvalidValue;
+    pe_cache_append_kernel<<<dim3(rows, 8), 32, 0, stream>>>(k, v, rows, k_cache, v_cache, capacity, position);
+    return cudaGetLastError();
+}
+
+int launch_pe_advance(int *position, int rows, cudaStream_t stream)
+{
+    if (!position || rows < 1) return cudaErrorInvalidValue;
+    pe_advance_kernel<<<1, 1, 0, stream>>>(position, rows);
+    return cudaGetLastError();
+}
+
+int prepare_gemv_kernels()
+{
+    return cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvRows * kGemvMaxK * 4);
+}
+
 int launch_gemv(const GemvArgs &a, GemvEpilogue epi, cudaStream_t stream)
 {
     if (!a.a || !a.w || a.rows < 1 || a.rows > kGemvRows || a.k < 256 || a.k % 256 || a.k > kGemvMaxK ||
@@ -239,9 +271,6 @@ int launch_gemv(const GemvArgs &a, GemvEpilogue epi, cudaStream_t stream)
     }
     else if (!a.out || a.ldo < a.n_rows)
         return cudaErrorInvalidValue;
-    static const cudaError_t attr = cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                         kGemvRows * kGemvMaxK * 4);
-    if (attr != cudaSuccess) return attr;
     const size_t smem = static_cast<size_t>(a.rows) * a.k * 4;
     gemv_kernel<<<(outputs + kGemvWarps - 1) / kGemvWarps, kGemvWarps * 32, smem, stream>>>(a, static_cast<int>(epi));
     return cudaGetLastError();

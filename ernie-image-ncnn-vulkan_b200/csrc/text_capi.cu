@@ -385,7 +385,8 @@ extern "C" int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *m, const
 // Per chunk of 1..32 new tokens at the session's position: the layer as above, the rotated K / V rows
 // appended to the layer's FP32 cache, and the FP32 attention of the chunk's queries over every cached key
 // up to each query's own position (FP64 sums). Decode steps (up to 4 rows) and the LM head stream their
-// weights through warp-per-row products (launch_gemv); prefill chunks use the tensor-core GEMM.
+// weights through warp-per-row products (launch_gemv) and a key-split attention, captured once per session
+// as a CUDA graph that reads the position from device memory; prefill chunks use the tensor-core GEMM.
 namespace
 {
 constexpr int kPeMaxRows = 32, kPeMaxCapacity = 4096, kPeVocab = 131072;
@@ -413,6 +414,8 @@ struct ernie_cuda_pe_session
     __nv_bfloat16 *a = nullptr, *h = nullptr;
     float *hrow = nullptr, *logits = nullptr;
     __nv_bfloat16 *ha = nullptr;
+    int *d_position = nullptr;                 // the device mirror of `position`
+    cudaGraphExec_t step_graph[5] = {};        // captured decode steps of 1..4 rows
     void *alloc = nullptr;
 };
 
@@ -462,14 +465,9 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
                           : launch_gemm(ps->a, L.wqkv, T, kTQkv, kTH, splits, bn, Epilogue::F32Bias, f32, sms, s, fp32),
                      "PE qkv projection");
         ERNIE_LAUNCH(launch_text_rope(ps->qkv, ps->cos_t, ps->sin_t, T, ps->q, ps->k, ps->v, s), "PE rotary");
-        // the chunk's K / V rows of each of the 8 heads into the caches at rows pos..pos+T-1
-        const size_t row_bytes = static_cast<size_t>(T) * 128 * 4, pitch = static_cast<size_t>(ps->capacity) * 128 * 4;
-        ERNIE_CUDA(cudaMemcpy2DAsync(kc + static_cast<size_t>(pos) * 128, pitch, ps->k, row_bytes, row_bytes, 8,
-                                     cudaMemcpyDeviceToDevice, s),
-                   "PE key cache");
-        ERNIE_CUDA(cudaMemcpy2DAsync(vc + static_cast<size_t>(pos) * 128, pitch, ps->v, row_bytes, row_bytes, 8,
-                                     cudaMemcpyDeviceToDevice, s),
-                   "PE value cache");
+        // the chunk's K / V rows of each of the 8 heads into the caches at rows pos..pos+T-1 (the position read
+        // on the device, so that a captured decode step does not depend on it)
+        ERNIE_LAUNCH(launch_pe_cache_append(ps->k, ps->v, T, kc, vc, ps->capacity, ps->d_position, s), "PE K/V cache");
         AttentionF32Args at{};
         at.q = ps->q;
         at.k = kc;
@@ -486,6 +484,11 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         at.causal = 1;
         at.causal_offset = pos;
         at.decode = gemv ? 1 : 0;
+        if (gemv)
+        {
+            at.position = ps->d_position;
+            at.nk = ps->capacity; // the bound; the kernel reads kv_len from the position
+        }
         at.out_mode = fp32 ? 1 : 2; // the o_proj operand: three BF16 planes or BF16, token-major
         at.out_split3 = ps->a;
         ERNIE_LAUNCH(launch_attention_f32(at, s), "PE attention");
@@ -513,6 +516,32 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         ERNIE_LAUNCH(gemv ? product(ps->h, L.wdown, kTH, kTFfn, GemvEpilogue::Resid, ps->x, kTH)
                           : launch_gemm(ps->h, L.wdown, T, kTH, kTFfn, splits, bn, Epilogue::ResidGate, res, sms, s, fp32),
                      "PE down_proj");
+    }
+    ERNIE_LAUNCH(launch_pe_advance(ps->d_position, T, s), "PE position");
+    return ERNIE_CUDA_OK;
+}
+
+// A decode step of `rows` rows, captured once per session and replayed (its inputs and the position are
+// read from the session's device buffers).
+int pe_step_graph(ernie_cuda_pe_session *ps, int rows)
+{
+    if (ps->step_graph[rows]) return ERNIE_CUDA_OK;
+    cudaStream_t s = ps->model->ctx->stream;
+    cudaGraph_t graph = nullptr;
+    ERNIE_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "Begin PE capture");
+    const int rc = pe_enqueue(ps, rows);
+    const cudaError_t e = cudaStreamEndCapture(s, &graph);
+    if (rc != ERNIE_CUDA_OK || e != cudaSuccess)
+    {
+        if (graph) cudaGraphDestroy(graph);
+        return rc != ERNIE_CUDA_OK ? rc : from_cuda(e, "End PE capture");
+    }
+    const cudaError_t i = cudaGraphInstantiate(&ps->step_graph[rows], graph, 0);
+    cudaGraphDestroy(graph);
+    if (i != cudaSuccess)
+    {
+        ps->step_graph[rows] = nullptr;
+        return from_cuda(i, "Instantiate PE step");
     }
     return ERNIE_CUDA_OK;
 }
@@ -585,9 +614,17 @@ extern "C" int ernie_cuda_pe_session_create(ernie_cuda_text_model *m, int capaci
     arena.add(&ps->hrow, kTH);
     arena.add(&ps->ha, static_cast<size_t>(ps->planes) * kTH);
     arena.add(&ps->logits, kPeVocab);
+    arena.add(&ps->d_position, 1);
     const cudaError_t e = arena.allocate();
     if (e != cudaSuccess) return from_cuda(e, "Allocate PE session");
     ps->alloc = arena.base;
+    cudaError_t z = cudaMemset(ps->d_position, 0, sizeof(int));
+    if (z == cudaSuccess) z = static_cast<cudaError_t>(prepare_gemv_kernels());
+    if (z != cudaSuccess)
+    {
+        cudaFree(ps->alloc);
+        return from_cuda(z, "Prepare PE session");
+    }
     *out = ps.release();
     return ERNIE_CUDA_OK;
 }
@@ -597,6 +634,8 @@ extern "C" int ernie_cuda_pe_session_destroy(ernie_cuda_pe_session *ps)
     if (!ps) return ERNIE_CUDA_OK;
     DeviceGuard guard(ps->model->ctx->device);
     cudaStreamSynchronize(ps->model->ctx->stream);
+    for (cudaGraphExec_t g : ps->step_graph)
+        if (g) cudaGraphExecDestroy(g);
     if (ps->alloc) cudaFree(ps->alloc);
     delete ps;
     return ERNIE_CUDA_OK;
@@ -605,6 +644,9 @@ extern "C" int ernie_cuda_pe_session_destroy(ernie_cuda_pe_session *ps)
 extern "C" int ernie_cuda_pe_session_reset(ernie_cuda_pe_session *ps)
 {
     if (!ps) return fail(ERNIE_CUDA_ERROR, "null argument");
+    DeviceGuard guard(ps->model->ctx->device);
+    ERNIE_CUDA(cudaMemsetAsync(ps->d_position, 0, sizeof(int), ps->model->ctx->stream), "reset PE position");
+    ERNIE_CUDA(cudaStreamSynchronize(ps->model->ctx->stream), "reset PE position");
     ps->position = 0;
     ps->valid = true;
     return ERNIE_CUDA_OK;
@@ -634,7 +676,13 @@ extern "C" int ernie_cuda_pe_session_append(ernie_cuda_pe_session *ps, const flo
     ERNIE_CUDA(cudaMemcpyAsync(ps->x, embedded, r * kTH * 4, cudaMemcpyHostToDevice, s), "PE input");
     ERNIE_CUDA(cudaMemcpyAsync(ps->cos_t, cos, r * 128 * 4, cudaMemcpyHostToDevice, s), "PE cos");
     ERNIE_CUDA(cudaMemcpyAsync(ps->sin_t, sin, r * 128 * 4, cudaMemcpyHostToDevice, s), "PE sin");
-    ERNIE_TRY(pe_enqueue(ps, rows));
+    if (rows <= 4)
+    {
+        ERNIE_TRY(pe_step_graph(ps, rows));
+        ERNIE_CUDA(cudaGraphLaunch(ps->step_graph[rows], s), "PE step");
+    }
+    else
+        ERNIE_TRY(pe_enqueue(ps, rows));
     ERNIE_CUDA(cudaMemcpyAsync(hidden, ps->x, r * kTH * 4, cudaMemcpyDeviceToHost, s), "PE hidden");
     ERNIE_TRY(check_status(m));
     ps->position += rows;
