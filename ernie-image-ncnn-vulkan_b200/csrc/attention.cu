@@ -285,7 +285,7 @@ int launch_attention_f32(const AttentionF32Args &args, cudaStream_t stream)
         return cudaErrorInvalidValue;
     if (args.decode)
     {
-        if (args.nq > 4 || args.width != kDim) return cudaErrorInvalidValue;
+        if (args.nq > 32 || args.width != kDim) return cudaErrorInvalidValue;
         attention_decode_kernel<<<dim3(args.heads, args.nq), kDWarps * 32, 0, stream>>>(args);
         return cudaGetLastError();
     }

@@ -145,7 +145,7 @@ struct AttentionF32Args
     __nv_bfloat16 *out_split3;
     int causal;            // key j visible to query i iff j <= i + causal_offset
     int causal_offset = 0; // position of query 0 (a KV-cached chunk appended after causal_offset keys)
-    int decode = 0;        // 1..4 query rows of width 128: the keys split over warps (attention_decode_kernel)
+    int decode = 0;        // 1..32 query rows of width 128: one CTA per (head, row), keys split over its warps
     // decode only, nullable: the device-resident position of query 0, in place of causal_offset (and
     // kv_len = *position + nq), so that a captured step is position-independent
     const int *position = nullptr;

@@ -385,8 +385,9 @@ extern "C" int ernie_cuda_text_run_blocks_device(ernie_cuda_text_model *m, const
 // Per chunk of 1..32 new tokens at the session's position: the layer as above, the rotated K / V rows
 // appended to the layer's FP32 cache, and the FP32 attention of the chunk's queries over every cached key
 // up to each query's own position (FP64 sums). Decode steps (up to 4 rows) and the LM head stream their
-// weights through warp-per-row products (launch_gemv) and a key-split attention, captured once per session
-// as a CUDA graph that reads the position from device memory; prefill chunks use the tensor-core GEMM.
+// weights through warp-per-row products (launch_gemv), captured once per session as a CUDA graph that reads
+// the position from device memory; prefill chunks use the tensor-core GEMM. Every chunk's attention runs
+// one CTA per (head, query row) with the cached keys split over its warps.
 namespace
 {
 constexpr int kPeMaxRows = 32, kPeMaxCapacity = 4096, kPeVocab = 131072;
@@ -483,12 +484,10 @@ int pe_enqueue(ernie_cuda_pe_session *ps, int rows)
         at.kv_head_stride = static_cast<long long>(ps->capacity) * 128;
         at.causal = 1;
         at.causal_offset = pos;
-        at.decode = gemv ? 1 : 0;
-        if (gemv)
-        {
-            at.position = ps->d_position;
-            at.nk = ps->capacity; // the bound; the kernel reads kv_len from the position
-        }
+        // every chunk (at most 32 rows) on the key-split kernel: one CTA per (head, row) keeps all SMs busy
+        at.decode = 1;
+        at.position = ps->d_position;
+        at.nk = ps->capacity; // the bound; the kernel reads kv_len from the position
         at.out_mode = fp32 ? 1 : 2; // the o_proj operand: three BF16 planes or BF16, token-major
         at.out_split3 = ps->a;
         ERNIE_LAUNCH(launch_attention_f32(at, s), "PE attention");
