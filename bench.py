@@ -90,12 +90,26 @@ class ClockSampler:
         rows = [l.split(",") for l in open(self.file.name).read().strip().splitlines() if l.strip()]
         os.unlink(self.file.name)
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        note = None
         if not sm:
-            return None
+            # a timed region shorter than the sampling interval: one sample right after it
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+                rows = [l.split(",") for l in out.stdout.strip().splitlines() if l.strip()]
+            except (OSError, subprocess.TimeoutExpired):
+                rows = []
+            sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+            if not sm:
+                return None
+            note = "timed region shorter than the 200 ms sampling interval: one sample taken right after it"
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(sm),
+        info = {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(sm) if not note else 0,
                 "reasons": reasons}
+        if note:
+            info["note"] = note
+        return info
 
 
 def dist_setup(gpus):
