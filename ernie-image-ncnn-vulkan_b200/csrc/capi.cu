@@ -1028,7 +1028,6 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     auto on = [only, T](int part) { return (only < 0 || only == part) && (T > 0 || part == 2); };
     const DevBlock &w = s->model->blocks[b];
     cudaStream_t st = s->ctx->stream;
-    const int sp = s->splits, nsm = s->ctx->num_sms;
     const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
     const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
     const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
@@ -1117,7 +1116,6 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
 {
     const DevHeads &hd = s->model->heads;
     cudaStream_t st = s->ctx->stream;
-    const int nsm = s->ctx->num_sms, sp = s->splits;
     const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
     // input head over this session's token range: image rows (x_embedder) then text rows (cached text_proj)
     const int img = s->img_local, text_rows = s->real_local - s->img_local;

@@ -80,14 +80,6 @@ __device__ __forceinline__ float split_plane(float x, int p)
     return __bfloat162float(__float2bfloat16_rn(r1 - mid));
 }
 
-__device__ __forceinline__ void store_bf16x8(__nv_bfloat16 *dst, const float *v)
-{
-    __align__(16) __nv_bfloat162 packed[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) packed[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-    *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(packed);
-}
-
 __device__ __forceinline__ void store_f32x4(float *dst, const float *v)
 {
     *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
