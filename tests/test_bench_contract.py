@@ -1,0 +1,50 @@
+"""bench.py's output contract, checked on the CPU through its reference arm (the CPU restatement timed on the
+host cores): one JSON line with the keys and types the benchmark driver reads, at least 3 warm-up steps,
+and ranks other than 0 of a multi-process launch exiting 0 without doing the work or printing a line."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ARGS = ["--impl", "reference", "--stage", "vae-encode", "--steps", "1", "--warmup", "1"]
+TOP_LEVEL = {"metric": str, "value": float, "unit": str, "n_gpus": int, "steps": int, "warmup": int,
+             "ms_per_step": float, "higher_is_better": bool, "scaling": str, "dtype": str, "data": str,
+             "config": dict, "impl": str, "cpu_baseline": dict, "e2e": dict}
+
+
+def run(args, env=None):
+    return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], capture_output=True, text=True,
+                          timeout=900, cwd=ROOT, env=env)
+
+
+def json_lines(stdout):
+    return [json.loads(line) for line in stdout.splitlines() if line.startswith("{")]
+
+
+def test_reference_arm_prints_one_complete_line():
+    r = run(ARGS)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = json_lines(r.stdout)
+    assert len(lines) == 1
+    d = lines[0]
+    for key, kind in TOP_LEVEL.items():
+        assert key in d, key
+        assert isinstance(d[key], kind) or (kind is float and isinstance(d[key], int)), (key, d[key])
+    assert "vs_baseline" in d
+    assert d["impl"] == "reference" and d["steps"] == 1 and d["warmup"] == 3  # raised to the minimum of 3
+    assert d["value"] > 0 and d["scaling"] in ("weak", "strong")
+    cpu = d["cpu_baseline"]
+    assert cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["value"] == d["value"]
+    assert cpu["unit"] == d["unit"] and isinstance(cpu["sample"], str) and cpu["sample"]
+    e2e = d["e2e"]
+    assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    assert isinstance(d["config"].get("workload"), str)
+
+
+def test_other_ranks_exit_without_work():
+    env = dict(os.environ, RANK="1", LOCAL_RANK="1", WORLD_SIZE="2")
+    r = run(ARGS, env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert json_lines(r.stdout) == []
