@@ -18,7 +18,8 @@ SEED = 11
 FREQ = (1.0 / 1000000.0 ** (np.arange(64) / 64)).astype(np.float32)
 PE_FP32 = (2e-4, 2e-4, 2e-5)
 PE_FP16 = (0.03, 0.03, 0.02)
-PLANS = [[17], [8, 8, 1], [5, 1, 11], [1] * 17]
+# the last plan runs 2- to 4-row chunks through the decode products
+PLANS = [[17], [8, 8, 1], [5, 1, 11], [1] * 17, [4, 3, 2, 4, 1, 3]]
 
 
 @pytest.fixture(scope="module")
@@ -48,7 +49,7 @@ def run_plan(session, x, cos, sin, plan):
     return np.concatenate(out)
 
 
-@pytest.mark.parametrize("plan", PLANS, ids=["17", "8-8-1", "5-1-11", "ones"])
+@pytest.mark.parametrize("plan", PLANS, ids=["17", "8-8-1", "5-1-11", "ones", "4-3-2-4-1-3"])
 @pytest.mark.parametrize("precision", [ec.FP32, ec.BF16], ids=["fp32", "bf16"])
 def test_cached_decode_equals_full_causal_run(model, layers, plan, precision):
     x = prompt(17)
