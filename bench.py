@@ -684,7 +684,9 @@ def run_pe(args):
                 "e2e": {"value": e2e_ms, "unit": "ms/token", "h2d_bytes_per_step": 3072 * 4 + 2 * 128 * 4,
                         "d2h_bytes_per_step": 3072 * 4 + 131072 * 4,
                         "call": "ernie_cuda_pe_session_append (one host row) + ernie_cuda_pe_logits (host logits)"},
-                "gpu_launches": args.steps * (9 * PE_LAYERS + 2), "clocks": clock_info}
+                # per token: 9 kernels per layer (norm, qkv, rotary, cache append, attention, o_proj, norm,
+                # gate/up, down), the position advance, and the head (norm + product)
+                "gpu_launches": args.steps * (9 * PE_LAYERS + 3), "clocks": clock_info}
         print(json.dumps(line), flush=True)
     session.close()
     model.close()
