@@ -42,8 +42,10 @@ def block_case(w, h, text, valid, scale=1.0):
 
 
 @pytest.mark.parametrize("precision", [ec.FP32, ec.BF16])
+# square grids, a ragged one (5 x 3, 7 text slots of which 5 valid), the smallest request (one image
+# token, one text slot) and the scaled-activation case of tools/export_dit_heads.py:172-173
 @pytest.mark.parametrize("w,h,text,valid,scale", [(4, 4, 8, 6, 1.0), (16, 16, 32, 24, 1.0), (32, 32, 32, 24, 1.0),
-                                                  (4, 4, 8, 6, 512.0)])
+                                                  (5, 3, 7, 5, 1.0), (1, 1, 1, 1, 1.0), (4, 4, 8, 6, 512.0)])
 def test_block_parity(model, host_blocks, precision, w, h, text, valid, scale):
     x, mod, cos, sin, mask = block_case(w, h, text, valid, scale)
     ref = o.block(x, host_blocks[0], mod, cos, sin, mask)
