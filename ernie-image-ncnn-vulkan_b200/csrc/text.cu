@@ -112,6 +112,9 @@ int launch_text_rope(const float *qkv, const float *cos_t, const float *sin_t, i
 }
 
 // ---- decode products (prompt enhancer) -------------------------------------------------------------
+// The PE block graph's seven projections (src/pe_graph.cpp:22-28 q/k/v, :62 o_proj, :67-69 gate/up with
+// the Swish on the gate, :71 down_proj) for a step of 1..4 token rows, and the LM head's 131072-row
+// projection: one warp per weight row, FP32 accumulation against the activation rows staged in FP32.
 namespace
 {
 constexpr int kGemvRows = 4, kGemvWarps = 8, kGemvMaxK = 9216;
