@@ -16,6 +16,31 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(ec.SIGNATURES), set(declared) ^ set(ec.SIGNATURES)
 
 
+def test_integration_index_names_every_entry_point():
+    """The integration guide's entry-point index lists each declared function, either in full or as
+    `prefix_a` / `_b` (the suffix replacing the last word of the preceding full name)."""
+    import os
+    import re
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "INTEGRATION.md")
+    text = open(path).read()
+    index = text[text.index("## 8. Entry-point index"):]
+    listed = set()
+    for row in index.splitlines():
+        cells = row.split("|")
+        if len(cells) < 4 or not row.startswith("| ") or row.startswith("| Group"):
+            continue
+        base = None
+        for name in re.findall(r"`([a-z0-9_]+)`", cells[2]):
+            if name.startswith("ernie_cuda_"):
+                listed.add(name)
+                base = name.rsplit("_", 1)[0]
+            elif name.startswith("_") and base:
+                listed.add(base + name)
+    declared = set(ec.declared_functions())
+    assert declared <= listed, sorted(declared - listed)
+    assert listed <= declared, sorted(listed - declared)
+
+
 @pytest.mark.parametrize("kind,name", [(ec.TURBO, "turbo"), (ec.LINEAR, "linear")])
 def test_schedule_matches_oracle(kind, name):
     for steps in list(range(1, 40)) + [100, 999, 1000]:
