@@ -1,6 +1,7 @@
 """bench.py's output contract, checked on the CPU through its reference arm (the CPU restatement timed on the
 host cores): one JSON line with the keys and types the benchmark driver reads, at least 3 warm-up steps,
-and ranks other than 0 of a multi-process launch exiting 0 without doing the work or printing a line."""
+and ranks other than 0 of a multi-process launch (environment variables alone, and a real 2-rank torchrun
+launch) exiting 0 without doing the work or printing a line."""
 import json
 import os
 import subprocess
@@ -48,3 +49,17 @@ def test_other_ranks_exit_without_work():
     r = run(ARGS, env)
     assert r.returncode == 0, r.stderr[-2000:]
     assert json_lines(r.stdout) == []
+
+
+def test_reference_arm_under_torchrun_prints_one_line():
+    """Launched as the driver launches N > 1 (torchrun, one process per rank): rank 0 alone prints."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+           "127.0.0.1", "--master-port", str(port), os.path.join(ROOT, "bench.py"), "--gpus", "2", *ARGS]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = json_lines(r.stdout)
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["n_gpus"] == 2, r.stdout[-2000:]
