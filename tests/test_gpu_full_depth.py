@@ -71,6 +71,43 @@ def test_36_blocks_8_steps_against_oracle(deep, oracle_final, precision):
     assert ok, metrics
 
 
+C1 = (32, 32, 32, 32)  # 32x32 packed latent (512x512) + 32 text tokens, 1056 tokens
+
+
+@pytest.fixture(scope="module")
+def oracle_c1_step(deep):
+    """The oracle's first turbo step at the full C1 geometry through all 36 blocks (about a minute on the
+    host): the prediction of step 0 and the latent after it."""
+    _, _, host_blocks, host_heads = deep
+    latent, txt, cos, sin, mask = case(*C1)
+    return o.denoise(host_heads, host_blocks, latent, txt, cos, sin, mask, 8, 0, 1, keep_predictions=True)
+
+
+@pytest.mark.parametrize("precision", [ec.FP32, ec.BF16], ids=["fp32", "bf16"])
+def test_c1_full_step_against_oracle(deep, oracle_c1_step, precision):
+    """One whole denoise step at C1 (input head, 36 blocks, output head, Euler) against the oracle with the
+    per-tensor pipeline gates of tools/validate_pipeline.py:218-222 on the prediction and the latent."""
+    ctx, model, _, _ = deep
+    w, h, text, valid = C1
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    ref_latent, ref_preds = oracle_c1_step
+    s = ec.Session(model, w, h, text, valid, precision)
+    try:
+        s.set_conditioning(txt, cos, sin, mask)
+        got, preds = s.denoise(latent, 8, 0, 1, keep_predictions=True)
+    finally:
+        s.close()
+    name = "pipeline_fp32" if precision == ec.FP32 else "pipeline_bf16"
+    ok_pred, pred_metrics = gate(ref_preds[0], preds[0], *GATES[name])
+    ok_latent, latent_metrics = gate(ref_latent, got, *GATES[name])
+    mode = "fp32" if precision == ec.FP32 else "bf16"
+    print(f"C1 step 0, 36 blocks vs oracle {mode}: prediction nrmse={pred_metrics['nrmse']:.3e} "
+          f"max_abs={pred_metrics['max_abs_error']:.3e}; latent nrmse={latent_metrics['nrmse']:.3e} "
+          f"max_abs={latent_metrics['max_abs_error']:.3e}")
+    assert ok_pred, pred_metrics
+    assert ok_latent, latent_metrics
+
+
 def test_c1_geometry_bf16_against_fp32_mode(deep):
     ctx, model, _, _ = deep
     w, h, text, valid = 32, 32, 32, 24
