@@ -34,7 +34,7 @@ struct DevHeads
     void *alloc = nullptr;
 };
 
-// FlowSchedule::turbo (src/latent_ops.cpp:89-109) and the evenly spaced variant.
+// FlowSchedule::turbo (src/latent_ops.cpp:31-51) and the evenly spaced variant.
 int host_schedule(int steps, int kind, float *sigmas, float *timesteps)
 {
     if (steps < 1 || steps > 1000) return fail(ERNIE_CUDA_ERROR, "Steps must be in [1,1000]");
@@ -57,7 +57,7 @@ int host_schedule(int steps, int kind, float *sigmas, float *timesteps)
     return ERNIE_CUDA_OK;
 }
 
-// timestep_features (src/denoiser.cpp:152-169), evaluated on the host as the reference does.
+// timestep_features (src/denoiser.cpp:22-39), evaluated on the host as the reference does.
 int host_features(float timestep, float *out)
 {
     if (!std::isfinite(timestep) || timestep < 0.f || timestep > 1000.f)

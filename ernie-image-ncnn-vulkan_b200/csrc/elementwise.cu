@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const __nv_bfloat16 *__restri
     if (lane == 0) y[row] = acc + (bias ? bias[row] : 0.f);
 }
 
-// euler_step (src/latent_ops.cpp:130-150; GLSL `precise` at :186-201): change = delta * v,
+// euler_step (src/latent_ops.cpp:72-92; GLSL `precise` at :135-143): change = delta * v,
 // out = x + change, each rounded separately.
 __global__ void euler_kernel(const float *sample, const float *prediction, float delta, long long count, float *out)
 {
@@ -185,7 +185,7 @@ __global__ void finite_kernel(const float *x, long long count, int *flag)
     if (__any_sync(0xffffffffu, !ok) && (threadIdx.x % 32) == 0) atomicOr(flag, 1);
 }
 
-// unpack_for_vae (src/latent_ops.cpp:152-182, shader :203-222): z * sqrt(var + 1e-5) + mean,
+// unpack_for_vae (src/latent_ops.cpp:94-124, shader :145-164): z * sqrt(var + 1e-5) + mean,
 // channel c -> output channel c/4 at (2y + (c%4)/2, 2x + c%2). One thread per output element, so
 // the writes are coalesced.
 __global__ void unpack_kernel(const float *packed, const float *mean, const float *variance, int w, int h, float *out)

@@ -7,8 +7,8 @@
 //   ResidGate  gemm_3 / gemm_6 + mul_15 / mul_21 (gate) + add_16 / add_22 (FP32 residual, ErnieResidualAdd);
 //   Geglu      gemm_4 + gemm_5 + ErnieGELU + mul_20 over interleaved [up; gate] weights;
 //   F32Bias    head projections (x_embedder conv1x1 + bias, text_proj);
-//   FinalEuler output-head linear + bias + transpose to [128,h,w] + euler_step (src/latent_ops.cpp:130-150)
-//              + the finite scan (src/latent_ops.cpp:118-128).
+//   FinalEuler output-head linear + bias + transpose to [128,h,w] + euler_step (src/latent_ops.cpp:72-92)
+//              + the finite scan (src/latent_ops.cpp:60-70).
 //
 // Structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: A [128 x 64] and B [BN x 64] BF16 tiles, 128-byte swizzle, S-stage ring

@@ -1,5 +1,5 @@
 // The text encoder's rotary embedding and head split (reference: the Mistral decoder layer the reference
-// exports per block, tools/export_text_block.py:50-61, with ExportBlock.rotary's half-split rotation,
+// exports per block, tools/export_text_block.py:51-61, with ExportBlock.rotary's half-split rotation,
 // tools/export_dit_block.py:39-47).
 #include "kernels.h"
 

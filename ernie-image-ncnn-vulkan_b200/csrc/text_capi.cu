@@ -1,7 +1,7 @@
 // C ABI of the prompt encoder (include/ernie_cuda.h, "Text encoder"): the Mistral decoder layers the
-// reference runs one ncnn block at a time (run_text_blocks, src/text_encoder.cpp:101-160; the block graph
-// is tools/export_text_block.py:50-61 TextBlock.forward) with every layer's weights resident on the device,
-// and the constants of text_constants (src/text_encoder.cpp:77-100). Host orchestration only.
+// reference runs one ncnn block at a time (run_text_blocks, src/text_encoder.cpp:106-166; the block graph
+// is tools/export_text_block.py:51-61 TextBlock.forward) with every layer's weights resident on the device,
+// and the constants of text_constants (src/text_encoder.cpp:76-104). Host orchestration only.
 //
 // Per layer (hidden 3072, 32 query heads and 8 K/V heads of 128, SwiGLU 9216, RMSNorm eps 1e-5):
 //   norm_modulate (RMSNorm, input_layernorm) -> tcgen05 GEMM [q; k; v] (F32 out) -> rotary ->

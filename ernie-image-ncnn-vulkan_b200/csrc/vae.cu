@@ -2,7 +2,7 @@
 // GroupNorm / SiLU / upsample / softmax passes around it.
 //
 // Replaces the ncnn layers of the reference's decoder graph (AutoencoderKLFlux2 post_quant_conv +
-// decoder, exported by tools/export_vae.py and run by src/vae.cpp:18-66):
+// decoder, exported by tools/export_vae.py and run by src/vae.cpp:18-64):
 //   Convolution 3x3 / 1x1     conv_kernel (implicit GEMM: M = pixels, N = output channels, K = taps x Cin)
 //   BinaryOp add (residual)   fused into the conv epilogue (out = acc + bias + resid)
 //   GroupNorm (ErnieGroupNorm, src/ernie_groupnorm.cpp:33-64)
@@ -724,7 +724,7 @@ __global__ void upsample_kernel(const float *x, int h, int w, int channels, __nv
     }
 }
 
-// ---- encoder passes (encode_vae, src/image_encoder.cpp:29-72) ----
+// ---- encoder passes (encode_vae, src/image_encoder.cpp:28-72) ----
 // The encoder's conv_in (3 -> 128, 3x3) as a 1x1 product over im2col columns: RGB bytes normalised in the
 // reference's FP32 order (src/image_encoder.cpp:44-51) and gathered per pixel: column t * 3 + c is channel c
 // of the neighbour at tap t = ky * 3 + kx (zero outside the image); columns 27..63 are zero.

@@ -3,13 +3,13 @@
 // as one CUDA graph. Host orchestration only; the arithmetic is in vae.cu's kernels.
 //
 // The program follows the reference's exported decoder graph (AutoencoderKLFlux2 post_quant_conv +
-// decoder as vae/head.ncnn.param lists it, run by decode_vae, src/vae.cpp:18-66): post_quant_conv 1x1
+// decoder as vae/head.ncnn.param lists it, run by decode_vae, src/vae.cpp:18-64): post_quant_conv 1x1
 // 32->32, conv_in 3x3 32->512, mid block (resnet, single-head self-attention over all pixels, resnet),
 // four up blocks of three resnets (512, 512, 256, 128 channels; 1x1 shortcut where the width changes)
 // with nearest x2 upsampling + conv after the first three, GroupNorm(32, eps 1e-6) + Swish, conv_out
 // 3x3 128->3. The RGB bytes follow rgb_image (src/pipeline.cpp:145-163).
 //
-// The encoder program follows encode_vae (src/image_encoder.cpp:29-72) over the wrapper its export traces
+// The encoder program follows encode_vae (src/image_encoder.cpp:28-72) over the wrapper its export traces
 // (tools/export_vae_encoder.py:74-80): RGB bytes normalised as (v - 127.5f) * (1 / 127.5f), conv_in 3x3
 // 3->128, four down blocks of two resnets (128, 256, 512, 512 channels) with a 3x3 stride-2 convolution
 // (input padded by one zero row and column at the bottom and right) after the first three, the decoder's

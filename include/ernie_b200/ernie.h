@@ -104,13 +104,13 @@ struct FlowSchedule
     static FlowSchedule linear(int steps = 8);
     float delta(size_t step) const; // sigma[step+1] - sigma[step]; std::out_of_range past the end
 };
-// Device latents [128][h][w]. Shapes and delta are validated as in src/latent_ops.cpp:69-86.
+// Device latents [128][h][w]. Shapes and delta are validated as in src/latent_ops.cpp:11-29.
 void euler_step(GpuContext &, const DeviceTensor &sample, const DeviceTensor &prediction, float delta,
                 DeviceTensor &next);
 bool finite_latent(GpuContext &, const DeviceTensor &value);
 DeviceTensor unpack_for_vae(GpuContext &, const DeviceTensor &packed, const Tensor &mean, const Tensor &variance);
 
-// ---- conditioning (src/conditioning.h:12-15) and features (src/denoiser.h:96) --------------------
+// ---- conditioning (src/conditioning.h:12-15) and features (src/denoiser.h:12) --------------------
 // Returns {cosine [N][128], sine [N][128], mask [N]}; frequency table (64 values) or empty for the
 // official table. token_limit 6144 (static graphs) or 10240 (runtime).
 std::vector<Tensor> dit_constants(const std::vector<float> &frequencies, int width, int height, int valid_text,
@@ -163,7 +163,7 @@ class DitModel
     int num_blocks_ = 0;
 };
 
-// WeightPlacement (src/weight_placement.h:19-54): the decision logic of the reference, with the
+// WeightPlacement (src/weight_placement.h:20-51): the decision logic of the reference, with the
 // CUDA device budget (cudaMemGetInfo) as the reader.
 enum class WeightMemory { Auto, Device, Host };
 WeightMemory parse_weight_memory(const std::string &value);
@@ -302,7 +302,7 @@ void run_block_sequence(DenoiseSession &, DeviceTensor &x, const DeviceTensor &m
 // run_dit (src/dit.h:17-40): one prediction [128][h][w] for latent [128][h][w] at `timestep`.
 DeviceTensor run_dit(DenoiseSession &, const DeviceTensor &latent, float timestep, DitStats &stats);
 
-struct DenoiseStepStats // src/denoiser.h:102-108
+struct DenoiseStepStats // src/denoiser.h:18-24
 {
     float timestep = 0, delta = 0;
     DitStats dit;
@@ -310,7 +310,7 @@ struct DenoiseStepStats // src/denoiser.h:102-108
     bool complete = false;
 };
 using StepObserver = std::function<void(size_t, const Tensor &prediction, const Tensor &latent)>;
-// denoise (src/denoiser.h:110-128): steps [start_step, steps) of the turbo schedule; the observer
+// denoise (src/denoiser.h:30-44): steps [start_step, steps) of the turbo schedule; the observer
 // (optional) sees each step's prediction and latent (forcing one step per launch). Throws
 // std::invalid_argument on contract errors and std::runtime_error("Non-finite latent after denoise
 // step k"); stats holds the executed steps, a failed one with complete = false.
@@ -379,7 +379,7 @@ std::string numbered(const std::string &stem, int index); // "block-07"
 // Initial noise of a request without a latent file: std::mt19937(seed) feeding
 // std::normal_distribution<float>(0, 1), channel after channel, as src/pipeline.cpp:520-531 draws it.
 Tensor initial_noise(int width, int height, uint32_t seed);
-// img2img start (src/img2img.h:8-21): the latent and step to begin denoising an encoded image from.
+// img2img start (src/img2img.h:7-19): the latent and step to begin denoising an encoded image from.
 // `encoded` is the patchified, BN-normalised mean posterior [128][h][w]; strength 0 returns it unchanged
 // (start_step = schedule length) without using the noise; otherwise denoise_steps = clamp(round-half-up
 // (steps * strength), 1, steps), start_step = steps - denoise_steps and the latent is
@@ -511,7 +511,7 @@ class VaeEncoder
     GpuContext &ctx_;
     ernie_cuda_vae_encoder *handle_ = nullptr;
 };
-// encode_vae (src/image_encoder.cpp:29-72) on the B200. std::invalid_argument for pixels that are not
+// encode_vae (src/image_encoder.cpp:28-72) on the B200. std::invalid_argument for pixels that are not
 // width * height * 3 bytes or sides that are not multiples of 16 in [16, 2048] (the reference admits only
 // its reviewed 32x32, 64x32, 512x384 and 1024x1024); std::runtime_error "Non-finite VAE encoder ..." for a
 // non-finite output, as validate_output throws. FP32-exact mode is the parity mode of the reference's CPU
@@ -551,7 +551,7 @@ class TextModel
     ernie_cuda_text_model *handle_ = nullptr;
     int num_layers_ = 0;
 };
-// run_text_blocks (src/text_encoder.h:17-19): `layers` (default all) layers over the embedded prompt with
+// run_text_blocks (src/text_encoder.h:16-18): `layers` (default all) layers over the embedded prompt with
 // the constants {cos, sin, mask} of text_constants (the mask must be its causal mask). stats gets one
 // compute time for the whole sequence of layers (the layers stay resident: no per-block load).
 Tensor run_text_blocks(TextModel &model, const Tensor &input, const std::vector<Tensor> &constants,

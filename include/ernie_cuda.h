@@ -35,7 +35,7 @@ extern "C" {
    softmax sums), gated like the reference's FP32 path. */
 #define ERNIE_PRECISION_BF16 0
 #define ERNIE_PRECISION_FP32 1
-#define ERNIE_SCHEDULE_TURBO 0  /* FlowSchedule::turbo, src/latent_ops.cpp:89-109 */
+#define ERNIE_SCHEDULE_TURBO 0  /* FlowSchedule::turbo, src/latent_ops.cpp:31-51 */
 #define ERNIE_SCHEDULE_LINEAR 1 /* evenly spaced sigmas 1 -> 0 (benchmark configuration) */
 
 /* Block tensor ids for ernie_cuda_model_read_tensor (test hook). */
@@ -158,7 +158,7 @@ int ernie_cuda_finite_latent(ernie_cuda_context *ctx, const float *latent, int w
 int ernie_cuda_unpack_for_vae(ernie_cuda_context *ctx, const float *packed, const float *mean,
                               const float *variance, int width, int height, float *out);
 /* Host helpers of the same path: FlowSchedule::turbo / linear (sigmas [steps+1], timesteps
-   [steps]), timestep_features (src/denoiser.cpp:152-169), dit_constants (src/conditioning.cpp:10-44)
+   [steps]), timestep_features (src/denoiser.cpp:22-39), dit_constants (src/conditioning.cpp:10-44)
    from the 64-value frequency table (NULL = the official table of tools/prepare_pipeline.py:63). */
 int ernie_cuda_schedule(int steps, int schedule, float *sigmas, float *timesteps);
 int ernie_cuda_timestep_features(float timestep, float *out4096);
@@ -169,7 +169,7 @@ int ernie_cuda_dit_constants(const float *freq64, int width, int height, int val
 int ernie_cuda_session_create(ernie_cuda_model *model, const ernie_cuda_shape *shape, int precision,
                               ernie_cuda_session **out);
 int ernie_cuda_session_destroy(ernie_cuda_session *session);
-/* Conditioning constants of the request (the four `constants` of denoise, src/denoiser.h:110-117):
+/* Conditioning constants of the request (the four `constants` of denoise, src/denoiser.h:26-27):
    text [text_tokens][3072] (padded, pad_text src/conditioning.cpp:56-67; NULL skips text_proj),
    cos/sin [N][128], mask [N] with N = width*height + text_tokens. Host pointers. text_proj runs
    once here, not once per step. */
@@ -183,7 +183,7 @@ int ernie_cuda_session_blocks(ernie_cuda_session *session, int first, int count,
 /* run_dit (src/dit.h:17-40): one prediction [128][h][w] for latent [128][h][w] at `timestep`
    (dev pointers). */
 int ernie_cuda_session_dit(ernie_cuda_session *session, const float *latent, float timestep, float *prediction);
-/* denoise (src/denoiser.h:110-128) on the session's device latent: steps [start_step, end_step)
+/* denoise (src/denoiser.h:30-44) on the session's device latent: steps [start_step, end_step)
    of an S-step schedule, captured as a CUDA graph when use_graph != 0. The latent lives at
    ernie_cuda_session_latent(). *failed_step receives the first step k (1-based) after which the
    latent was non-finite, else 0 (and the call returns -1 in that case). */
@@ -200,8 +200,8 @@ int ernie_cuda_session_denoise(ernie_cuda_session *session, const float *initial
 int ernie_cuda_initial_noise(unsigned seed, int width, int height, float *out);
 
 /* ---- Text encoder (the prompt encoder before the denoise loop) ------------------------------------
-   run_text_blocks (src/text_encoder.h:17-19, src/text_encoder.cpp:101-160) on one B200: the Mistral decoder
-   layers the reference exports per block (tools/export_text_block.py:50-61: hidden 3072, 32 query and 8
+   run_text_blocks (src/text_encoder.h:16-18, src/text_encoder.cpp:106-166) on one B200: the Mistral decoder
+   layers the reference exports per block (tools/export_text_block.py:51-61: hidden 3072, 32 query and 8
    K/V heads of 128, SwiGLU 9216, RMSNorm eps 1e-5, no biases), all layers resident on the device (the
    pipeline runs layers 0..24). Input: the embedded prompt [bucket][3072] FP32 (text_embeddings; rows past
    the prompt zero), cos/sin [bucket][128] of ernie_cuda_text_constants; the attention mask is the causal
@@ -225,7 +225,7 @@ int ernie_cuda_text_model_bytes(ernie_cuda_text_model *model, uint64_t *bytes);
 int ernie_cuda_text_model_upload_layer(ernie_cuda_text_model *model, int layer, const ernie_cuda_text_layer_weights *host);
 /* Seeded random-init weights (include/ernie_synth.h, text encoder streams). */
 int ernie_cuda_text_model_synthesize(ernie_cuda_text_model *model, uint64_t seed);
-/* text_constants (src/text_encoder.cpp:77-100), host: inv_freq[64] (the YaRN inverse frequencies) ->
+/* text_constants (src/text_encoder.cpp:76-104), host: inv_freq[64] (the YaRN inverse frequencies) ->
    cos/sin [bucket][128] (both halves of a row repeat the 64 angles t * f_j) and, if mask is not null, the
    causal mask [bucket][bucket] (0 on and below the diagonal, -FLT_MAX above). */
 int ernie_cuda_text_constants(const float *inv_freq, int bucket, float *cos_out, float *sin_out, float *mask);
@@ -276,7 +276,7 @@ int ernie_cuda_safetensors_entry(const char *path, int index, char *name, size_t
                                  int64_t *dims, int *ndim);
 
 /* ---- VAE decoder (the stage after the denoise loop) -----------------------------------------------
-   decode_vae (src/vae.h:16-22, src/vae.cpp:18-66) of the pinned AutoencoderKLFlux2 post_quant_conv +
+   decode_vae (src/vae.h:16-22, src/vae.cpp:18-64) of the pinned AutoencoderKLFlux2 post_quant_conv +
    decoder, and rgb_image (src/pipeline.cpp:145-163), on one B200. Weights are addressed by their
    diffusers parameter names and shapes (ernie_cuda_vae_tensor_info lists all of them, e.g.
    "decoder.up_blocks.2.resnets.0.conv_shortcut.weight" [256,512,1,1]), uploaded as FP32. The input is
@@ -313,7 +313,7 @@ int ernie_cuda_vae_decode_device(ernie_cuda_vae *vae, const float *unpacked, int
                                  float *decoded, uint8_t *rgb, int *nonfinite);
 
 /* ---- VAE encoder (img2img's image latent) -------------------------------------------------------
-   encode_vae (src/image_encoder.h:9-20, src/image_encoder.cpp:29-72) of the pinned AutoencoderKLFlux2
+   encode_vae (src/image_encoder.h:9-20, src/image_encoder.cpp:28-72) of the pinned AutoencoderKLFlux2
    encoder + quant_conv + bn as tools/export_vae_encoder.py:74-80 wraps it, on one B200. Input: RGB bytes
    [height][width][3], normalised as (v - 127.5f) * (1 / 127.5f). Outputs (the reference's VaeEncoding,
    FP32 planar): mean [32][height/8][width/8] (quant_conv(encoder(x))[:32], the posterior's mode), packed
@@ -390,13 +390,13 @@ int ernie_cuda_sp_layout(int tokens, int image_tokens, int world, int rank, int 
                          int *image_rows, int *real_rows, int *text_begin);
 
 /* Non-finite check that allocates no device memory. It has no counterpart in the reference.
-   Callers that cannot call cudaMalloc when they need the check (a stream capture in progress
-   elsewhere in the process, an application that forbids device allocation after start-up) use it
-   instead of ernie_cuda_finite_latent, which allocates a status word per call. Scratch is a fixed
-   512-byte device array (128 per-channel status words) that every GPU loading the library holds
-   until exit; latents outside 128 x [1..256] x [1..256] are rejected (-1). The first call on each
-   device looks up that array's device address, so make it before any stream capture. Every call
-   shares the array and clears it first; calls that overlap on the GPU race on it. */
+   Applications that reserve their device memory at start-up and forbid device allocation afterwards
+   use it instead of ernie_cuda_finite_latent, which allocates a status word per call. Scratch is a
+   fixed 512-byte device array (128 per-channel status words) that every GPU loading the library holds
+   until exit; latents outside 128 x [1..256] x [1..256] are rejected (-1). Each call looks up that
+   array's device address on the context's device; the first call on a device may load the library's
+   device code there, so make it at start-up. Every call shares the array and clears it first; calls
+   that overlap on the GPU race on it. The call waits for the context's stream. */
 int ernie_cuda_finite_latent_noalloc(ernie_cuda_context *ctx, const float *latent, int width, int height,
                                      int *finite);
 

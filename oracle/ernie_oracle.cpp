@@ -1,6 +1,6 @@
 // CPU restatement of the reference's FP32 DiT hot path — TEST INFRASTRUCTURE ONLY (see ernie_oracle.h).
 // Compiled with -ffp-contract=off like the reference's library (src/CMakeLists.txt:11-13); the one
-// explicit fused multiply-add is the one the reference writes (src/latent_ops.cpp:100).
+// explicit fused multiply-add is the one the reference writes (src/latent_ops.cpp:42).
 #include "ernie_oracle.h"
 #include "ernie_synth.h"
 #include <algorithm>
@@ -59,7 +59,7 @@ void orc_synth_normal_f32(uint64_t seed, uint64_t stream, float scale, float *ou
         out[i] = float(ernie_synth_normal(seed, stream, uint64_t(i)) * double(scale));
 }
 
-// FlowSchedule::turbo, src/latent_ops.cpp:89-109 (shift 4, PyTorch-style linspace from the nearer end).
+// FlowSchedule::turbo, src/latent_ops.cpp:31-51 (shift 4, PyTorch-style linspace from the nearer end).
 int orc_turbo_schedule(int steps, float *sigmas, float *timesteps)
 {
     if (steps < 1 || steps > 1000) return -1;
@@ -91,7 +91,7 @@ int orc_linear_schedule(int steps, float *sigmas, float *timesteps)
     return 0;
 }
 
-// timestep_features, src/denoiser.cpp:152-169 (Timesteps(4096), sin half first).
+// timestep_features, src/denoiser.cpp:22-39 (Timesteps(4096), sin half first).
 int orc_timestep_features(float timestep, float *out)
 {
     if (!std::isfinite(timestep) || timestep < 0.f || timestep > 1000.f) return -1;
@@ -251,7 +251,7 @@ void orc_sdpa(const float *q, const float *k, const float *v, const float *mask,
     }
 }
 
-// euler_step, src/latent_ops.cpp:130-150 (and the contract of check_pair, :80-86).
+// euler_step, src/latent_ops.cpp:72-92 (and the contract of check_pair, :22-29).
 int orc_euler_step(const float *sample, const float *prediction, float delta, int64_t count, float *out)
 {
     if (!std::isfinite(delta) || delta >= 0.f || delta < -1.f) return -1;
@@ -263,7 +263,7 @@ int orc_euler_step(const float *sample, const float *prediction, float delta, in
     return 0;
 }
 
-// finite_latent, src/latent_ops.cpp:118-128.
+// finite_latent, src/latent_ops.cpp:60-70.
 int orc_finite(const float *x, int64_t count)
 {
     for (int64_t i = 0; i < count; ++i)
@@ -271,7 +271,7 @@ int orc_finite(const float *x, int64_t count)
     return 1;
 }
 
-// unpack_for_vae, src/latent_ops.cpp:152-182: BN un-normalise, then channel c -> (c/4, dy, dx).
+// unpack_for_vae, src/latent_ops.cpp:94-124: BN un-normalise, then channel c -> (c/4, dy, dx).
 int orc_unpack_for_vae(const float *packed, const float *mean, const float *variance, int w, int h, float *out)
 {
     if (w < 1 || h < 1 || w > 256 || h > 256) return -1;
@@ -441,7 +441,7 @@ void orc_output_head(const orc_head_weights *w, const float *x, const float *c, 
         for (int ch = 0; ch < kLatent; ++ch) prediction[size_t(ch) * image + i] = p[size_t(i) * kLatent + ch];
 }
 
-// run_dit, src/dit.cpp:146-173: input head -> block sequence (src/block_sequence.cpp:56-94) -> output head.
+// run_dit, src/dit.cpp:104-132: input head -> block sequence (src/block_sequence.cpp:56-94) -> output head.
 void orc_dit(const orc_head_weights *heads, const orc_block_weights *const *blocks, int num_blocks,
              const float *latent, int width, int height, const float *text, int text_tokens, const float *features,
              const float *cos_t, const float *sin_t, const float *mask, float *prediction)
@@ -457,7 +457,7 @@ void orc_dit(const orc_head_weights *heads, const orc_block_weights *const *bloc
     orc_output_head(heads, x.data(), c.data(), width, height, prediction);
 }
 
-// denoise (CPU), src/denoiser.cpp:171-216, including its request checks (:143-150, :177-178).
+// denoise (CPU), src/denoiser.cpp:41-86, including its request checks (:13-20, :46-48).
 int orc_denoise(const orc_head_weights *heads, const orc_block_weights *const *blocks, int num_blocks,
                 const float *initial, int width, int height, const float *text, int text_tokens,
                 const float *cos_t, const float *sin_t, const float *mask, int steps, int start_step, int end_step,

@@ -3,8 +3,8 @@
 Only tests/ and bench.py's CPU-baseline leg use this module, as the checker; the CUDA product never
 imports it.
 
-What it restates: run_text_blocks (src/text_encoder.cpp:101-160) runs, per layer, the graph the reference
-exports from the pinned transformers MistralDecoderLayer (tools/export_text_block.py:50-61, TextBlock):
+What it restates: run_text_blocks (src/text_encoder.cpp:106-166) runs, per layer, the graph the reference
+exports from the pinned transformers MistralDecoderLayer (tools/export_text_block.py:51-61, TextBlock):
 
     n = rms_norm(x, input_layernorm, 1e-5)
     q, k, v = q_proj(n) [32 heads], k_proj(n), v_proj(n) [8 heads], head width 128
@@ -13,7 +13,7 @@ exports from the pinned transformers MistralDecoderLayer (tools/export_text_bloc
     x = x + o_proj(a)
     x = x + down_proj(silu(gate_proj(m)) * up_proj(m)),  m = rms_norm(x, post_attention_layernorm, 1e-5)
 
-with the constants of text_constants (src/text_encoder.cpp:77-100): cos/sin of t * f_j repeated over both
+with the constants of text_constants (src/text_encoder.cpp:76-104): cos/sin of t * f_j repeated over both
 halves of the 128-wide row and the causal mask (-FLT_MAX above the diagonal). float64 throughout; the
 weights are the exact BF16 values. Synthetic weights follow include/ernie_synth.h's text streams.
 

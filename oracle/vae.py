@@ -4,7 +4,7 @@ Only tests/ and bench.py's CPU-baseline leg use this module, as the checker; the
 imports it.
 
 What it restates:
-* decode_vae (src/vae.cpp:18-66) runs the reference's exported graph of the pinned diffusers
+* decode_vae (src/vae.cpp:18-64) runs the reference's exported graph of the pinned diffusers
   AutoencoderKLFlux2 (diffusers 0.41.0.dev0 at commit 7643c482, not vendored in the reference tree):
   decoder(post_quant_conv(x)) (tools/export_vae.py:33-39), whose layer list is
   artifacts/2026-09-05/pipeline/models/vae-128x128-specialized-v1/head.ncnn.param (committed in
@@ -19,7 +19,7 @@ What it restates:
 * Swish as ncnn evaluates it: x / (1 + exp(-x)).
 * rgb_image (src/pipeline.cpp:145-163): byte = nearbyint(clamp(x / 2 + 0.5, 0, 1) * 255) in FP32,
   non-finite values rejected.
-* encode_vae (src/image_encoder.cpp:29-72): RGB bytes -> (v - 127.5f) * (1 / 127.5f) in FP32
+* encode_vae (src/image_encoder.cpp:28-72): RGB bytes -> (v - 127.5f) * (1 / 127.5f) in FP32
   (image_encoder.cpp:44-51, tools/export_vae_encoder.py:30-34), then the traced wrapper of
   tools/export_vae_encoder.py:74-80 over the same pinned AutoencoderKLFlux2: mean =
   quant_conv(encoder(x))[:32] (the posterior's mode), packed = pixel_unshuffle(mean, 2), normalized =
@@ -43,7 +43,7 @@ from oracle import synth_normal
 GROUPS, EPS, WIDTH = 32, 1e-6, 512
 UP_OUT = (512, 512, 256, 128)
 DOWN_OUT = (128, 256, 512, 512)
-BN_EPS = 1e-4  # the encoder's BatchNorm (tools/export_vae_encoder.py:59,91)
+BN_EPS = 1e-4  # the encoder's BatchNorm (tools/export_vae_encoder.py:58,93)
 
 
 class _Table:
@@ -303,6 +303,6 @@ def encode(w, rgb):
 
 
 def rgb_fixture(width, height):
-    """Deterministic RGB test pattern of the reference's encoder fixtures (tools/export_vae_encoder.py:24-27)."""
+    """Deterministic RGB test pattern of the reference's encoder fixtures (tools/export_vae_encoder.py:25-28)."""
     y, x, c = np.indices((height, width, 3), dtype=np.int32)
     return ((13 * x + 29 * y + 71 * c + (x * y) % 19) % 256).astype(np.uint8)

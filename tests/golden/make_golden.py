@@ -110,7 +110,7 @@ def norm_fp64(values, weight, centered):
     return delta * inverse * (1.0 if centered else weight.astype(np.float64))
 
 
-# tests/test_bf16_gemm.cpp:32-45
+# tests/test_bf16_gemm.cpp:30-44
 def gemm_inputs(m, n, k):
     row = np.arange(m)[:, None]
     inner = np.arange(k)[None, :]
@@ -150,7 +150,7 @@ def main():
         a, w, bias = gemm_inputs(m, n, k)
         exact = a.astype(np.float64) @ w.astype(np.float64).T + (bias if with_bias else 0.0)
         sample(f"gemm_m{m}_n{n}_k{k}_b{int(with_bias)}", exact, store)
-    # src/latent_ops.cpp:89-109 turbo schedule for 8 steps, FP32 arithmetic emulated exactly.
+    # src/latent_ops.cpp:31-51 turbo schedule for 8 steps, FP32 arithmetic emulated exactly.
     steps = 8
     inc = np.float32(-1.0) / np.float32(steps)
     sig = []

@@ -1,4 +1,4 @@
-"""Prompt encoder on a B200 (run_text_blocks, src/text_encoder.cpp:101-160) against the CPU oracle
+"""Prompt encoder on a B200 (run_text_blocks, src/text_encoder.cpp:106-166) against the CPU oracle
 (oracle/text.py) on seeded synthetic weights.
 
 Gates (atol, rtol, nrmse): the reference's text-block fixture gates (tools/export_text_block.py:89-91:

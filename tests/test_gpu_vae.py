@@ -1,9 +1,9 @@
-"""VAE decoder on a B200 (decode_vae + rgb_image, src/vae.cpp:18-66, src/pipeline.cpp:145-163) against the
+"""VAE decoder on a B200 (decode_vae + rgb_image, src/vae.cpp:18-64, src/pipeline.cpp:145-163) against the
 CPU oracle (oracle/vae.py) on seeded synthetic weights.
 
 Gates (atol, rtol, nrmse) are the reference's VAE gates: the component fixture's "fp32", "fp16" and "bf16"
 gates (tools/export_dit_heads.py:88-90, written into the VAE fixture by tools/export_vae.py) and the
-decoder cross-check's FP32 gate (tools/diagnose_vae_cross.py:24). FP32-exact mode is held to the FP32
+decoder cross-check's FP32 gate (tools/diagnose_vae_cross.py:22). FP32-exact mode is held to the FP32
 gate; BF16 mode (BF16 convolution operands, FP32 accumulation, FP32 residuals and norms) to the tighter
 FP16 gate.
 """

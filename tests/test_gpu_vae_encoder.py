@@ -1,7 +1,7 @@
-"""VAE encoder on a B200 (encode_vae, src/image_encoder.cpp:29-72) against the CPU oracle (oracle/vae.py
+"""VAE encoder on a B200 (encode_vae, src/image_encoder.cpp:28-72) against the CPU oracle (oracle/vae.py
 encode) on seeded synthetic weights.
 
-Gates (atol, rtol, nrmse) are the reference's encoder fixture gate (tools/export_vae_encoder.py:91: fp32
+Gates (atol, rtol, nrmse) are the reference's encoder fixture gate (tools/export_vae_encoder.py:97: fp32
 {2e-4, 2e-4, 2e-5}) for FP32-exact mode on all three outputs (mean, packed, normalized), the component
 FP16 gate (tools/export_dit_heads.py:88-90) for BF16 mode, and the BF16 gate between the two modes at
 sizes the oracle cannot reach in seconds.

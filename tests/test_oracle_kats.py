@@ -90,7 +90,7 @@ def test_residual_contract():
 @pytest.mark.parametrize("m,n,k,bias", [(32, 48, 64, False), (1, 48, 32, True), (32, 128, 64, False),
                                         (130, 256, 128, True), (300, 512, 4096, False)])
 def test_bf16_gemm_exact(m, n, k, bias):
-    # tests/test_bf16_gemm.cpp:45-58: operands are exact multiples of 1/8, every sum is exact.
+    # tests/test_bf16_gemm.cpp:46-58: operands are exact multiples of 1/8, every sum is exact.
     a, w, b = mg.gemm_inputs(m, n, k)
     bits = (w.view(np.uint32) >> 16).astype(np.uint16)
     assert np.array_equal(o.bf16_to_f32(bits), w)

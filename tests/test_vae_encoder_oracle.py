@@ -1,6 +1,6 @@
 """VAE encoder stage on the CPU: the reference's normalisation known answers, the oracle's layers against
 direct restatements, and the library's tensor table against the oracle's (encode_vae,
-src/image_encoder.cpp:29-72, over the wrapper of tools/export_vae_encoder.py:74-80)."""
+src/image_encoder.cpp:28-72, over the wrapper of tools/export_vae_encoder.py:74-80)."""
 import numpy as np
 import pytest
 
