@@ -1,21 +1,21 @@
 // Non-finite latent check that allocates nothing (ernie_cuda_finite_latent_noalloc).
 //
-// Some callers cannot call cudaMalloc at the moment they need this check: code running while a
-// CUDA graph is being captured on another stream of the process, a host thread that holds a
-// CUDA-aware allocator's lock, or an embedding application with a hard no-device-allocation rule
-// after start-up. ernie_cuda_finite_latent allocates a 4-byte device status word per call; this
-// variant keeps its scratch in a fixed device array instead.
+// ernie_cuda_finite_latent allocates a 4-byte device status word on every call. Some embedding
+// applications reserve all of their device memory at start-up and then forbid device allocation (a
+// fixed memory budget shared with other models, or a rule against cudaMalloc's implicit
+// synchronisation in a serving loop); they call this variant, which keeps its scratch in a fixed
+// device array instead.
 //
 // Scratch: one status word per latent channel (128 x 4 bytes = 512 bytes), a file-scope
 // __device__ array present on every GPU that loads the library until the process exits. Host code
-// never names the array as a device address: at first use on each device, with that device
-// current, the address is taken once with cudaGetSymbolAddress and cached. Every call shares the
-// array, clears it before use and leaves the last call's per-channel status in it; calls that
-// overlap on the GPU (two streams, two host threads on one device) race on it.
+// never names the array as a device address: every call, with the context's device current, looks
+// the address up with cudaGetSymbolAddress (a lookup, no allocation, once the library's device code
+// is loaded on that device; the first call on a device may load it). Every call shares the array,
+// clears it before use and leaves the last call's per-channel status in it; calls that overlap on
+// the GPU (two streams, two host threads on one device) race on it. The call waits for the
+// context's stream before it returns.
 #include "ernie_cuda.h"
 #include <cuda_runtime.h>
-#include <map>
-#include <mutex>
 #include <string>
 
 namespace
@@ -34,25 +34,11 @@ __global__ void finite_channels_kernel(const float *latent, int plane, int *stat
     if (__any_sync(0xffffffffu, !ok) && (threadIdx.x % 32) == 0) atomicOr(status + channel, 1);
 }
 
-std::mutex g_mutex;
-std::map<int, int *> g_addresses; // device -> address of g_channel_status on that device
-
-// Set-up, once per device, with that device current. Returns the cudaError_t of the lookup.
-cudaError_t scratch_address(int device, int **address)
+// The device address of g_channel_status on the current device. Looked up on every call rather than
+// cached, so a device reset (which reloads the module at a new address) cannot leave a stale pointer.
+cudaError_t scratch_address(int **address)
 {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    auto it = g_addresses.find(device);
-    if (it != g_addresses.end())
-    {
-        *address = it->second;
-        return cudaSuccess;
-    }
-    int *ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_channel_status);
-    if (e != cudaSuccess) return e;
-    g_addresses.emplace(device, ptr);
-    *address = ptr;
-    return cudaSuccess;
+    return cudaGetSymbolAddress(reinterpret_cast<void **>(address), g_channel_status);
 }
 } // namespace
 
@@ -76,7 +62,7 @@ extern "C" int ernie_cuda_finite_latent_noalloc(ernie_cuda_context *ctx, const f
     cudaGetDevice(&previous);
     if (previous != device) cudaSetDevice(device);
     int *status = nullptr;
-    cudaError_t e = scratch_address(device, &status);
+    cudaError_t e = scratch_address(&status);
     if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, kStatusWords * sizeof(int), stream);
     if (e == cudaSuccess)
     {

@@ -1,10 +1,9 @@
 """The allocation-free non-finite check (ernie_cuda_finite_latent_noalloc) against the allocating one.
 
-Callers that cannot call cudaMalloc when they need the check, such as code running while another
-stream of the process is being captured into a CUDA graph, or applications that forbid device
-allocation after start-up, use the no-alloc entry point. It must agree with ernie_cuda_finite_latent
-on consecutive calls, because every call reuses the same static device array. This file sorts last so
-that a failure here leaves every other test already run. It passes both alone and after the others.
+Applications that reserve their device memory at start-up and forbid device allocation afterwards
+use the no-alloc entry point. It must agree with ernie_cuda_finite_latent on consecutive calls,
+because every call reuses the same static device array. This file sorts last so that a failure here
+leaves every other test already run. It passes both alone and after the others.
 """
 import ctypes
 
