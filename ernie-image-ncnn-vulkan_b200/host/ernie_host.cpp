@@ -8,6 +8,7 @@
 #include <fstream>
 #include <limits>
 #include <new>
+#include <numeric>
 #include <random>
 #include <utility>
 
@@ -333,225 +334,6 @@ uint64_t DitModel::bytes() const
     return b;
 }
 
-WeightMemory parse_weight_memory(const std::string &value)
-{
-    if (value == "auto") return WeightMemory::Auto;
-    if (value == "device") return WeightMemory::Device;
-    if (value == "host") return WeightMemory::Host;
-    throw std::invalid_argument("DiT weights must be auto, device, or host");
-}
-
-// Decision order of src/weight_placement.cpp:18-46: explicit mode, shape preference, then the
-// device budget after the reserve.
-WeightPlacementDecision choose_weight_placement(WeightMemory mode, bool shape_prefers_host, std::uint64_t weight_bytes,
-                                                std::uint64_t reserve_bytes, std::optional<DeviceMemoryBudget> memory)
-{
-    WeightPlacementDecision d;
-    d.weight_bytes = weight_bytes;
-    d.reserve_bytes = reserve_bytes;
-    if (memory) d.available_bytes = memory->usage_bytes < memory->budget_bytes ? memory->budget_bytes - memory->usage_bytes : 0;
-    if (mode != WeightMemory::Auto)
-    {
-        d.host = mode == WeightMemory::Host;
-        d.reason = "explicit";
-    }
-    else if (shape_prefers_host)
-    {
-        d.host = true;
-        d.reason = "shape";
-    }
-    else if (d.available_bytes)
-    {
-        d.host = *d.available_bytes < reserve_bytes || *d.available_bytes - reserve_bytes < weight_bytes;
-        d.reason = d.host ? "budget" : "available";
-    }
-    return d;
-}
-
-WeightPlacement::WeightPlacement(WeightMemory mode, std::uint64_t reserve_bytes, BudgetReader reader, Observer observer)
-    : mode_(mode), reserve_bytes_(reserve_bytes), reader_(std::move(reader)), observer_(std::move(observer))
-{
-}
-
-bool WeightPlacement::use_host(const std::string &component, std::uint64_t weight_bytes, bool shape_prefers_host,
-                               bool cache_prefers_host, const char *host_reason)
-{
-    const auto memory = mode_ == WeightMemory::Auto && reader_ ? reader_() : std::nullopt;
-    auto d = choose_weight_placement(mode_, shape_prefers_host, weight_bytes, reserve_bytes_, memory);
-    if (mode_ == WeightMemory::Auto && cache_prefers_host)
-    {
-        d.host = true;
-        d.reason = host_reason;
-    }
-    if (mode_ == WeightMemory::Auto && !memory) ++unavailable_queries_;
-    if (d.host) ++host_requests_;
-    else ++device_requests_;
-    if (observer_) observer_(component, d);
-    return d.host;
-}
-
-WeightPlacement::BudgetReader cuda_memory_budget_reader(GpuContext &ctx)
-{
-    ernie_cuda_context *handle = ctx.handle();
-    return [handle]() -> std::optional<DeviceMemoryBudget> {
-        uint64_t free_bytes = 0, total = 0;
-        if (ernie_cuda_context_memory(handle, &free_bytes, &total) != ERNIE_CUDA_OK) return std::nullopt;
-        return DeviceMemoryBudget{total, total - free_bytes};
-    };
-}
-
-// WeightSession: the admission policy of src/weight_session.cpp:60-118 over an opaque payload.
-struct WeightSession::State
-{
-    struct Entry
-    {
-        Payload payload;
-        std::uint64_t charge;
-    };
-    WeightBudget budget;
-    AvailableReader available;
-    Inspector inspect;
-    WeightSessionStats stats;
-    std::map<std::size_t, Entry> idle;
-    std::map<std::size_t, std::string> identities;
-    const void *request = nullptr;
-    bool active = false, cancelled = false;
-    bool headroom(std::uint64_t extra)
-    {
-        const auto bytes = available ? available() : std::nullopt;
-        if (!bytes)
-        {
-            ++stats.unavailable_queries;
-            return false;
-        }
-        return *bytes >= budget.reserve_bytes && *bytes - budget.reserve_bytes >= extra;
-    }
-    void evict_last()
-    {
-        auto last = std::prev(idle.end());
-        stats.live_bytes -= last->second.charge;
-        --stats.cached_nets;
-        idle.erase(last);
-        ++stats.evictions;
-    }
-};
-
-WeightSession::WeightSession(WeightBudget budget, AvailableReader available, Inspector inspect)
-    : state_(std::make_shared<State>())
-{
-    state_->budget = budget;
-    state_->available = std::move(available);
-    state_->inspect = std::move(inspect);
-}
-
-WeightSession::~WeightSession() { cancel(); }
-WeightSessionStats WeightSession::stats() const { return state_->stats; }
-bool WeightSession::contains(std::size_t block) const { return state_->idle.count(block) != 0; }
-
-void WeightSession::cancel()
-{
-    state_->cancelled = true;
-    while (!state_->idle.empty()) state_->evict_last();
-}
-
-WeightSession::Lease WeightSession::acquire(std::size_t block, const std::string &identity, const void *request,
-                                            std::uint64_t estimate, const Loader &loader)
-{
-    auto &s = *state_;
-    if (s.cancelled || s.active) throw std::logic_error("Weight session cancelled or lease still active");
-    if (block >= 36 || !request || !loader || identity.empty()) throw std::invalid_argument("Invalid weight session request");
-    if (s.request && s.request != request) throw std::logic_error("Weight session request identity changed");
-    s.request = request;
-    const auto known = s.identities.find(block);
-    if (known != s.identities.end() && known->second != identity)
-        throw std::logic_error("Weight session model identity changed");
-    s.identities.emplace(block, identity);
-    if (s.budget.host_bytes)
-        while (!s.idle.empty() && !s.headroom(s.idle.count(block) ? 0 : estimate)) s.evict_last();
-    auto found = s.idle.find(block);
-    if (found != s.idle.end())
-    {
-        auto entry = std::move(found->second);
-        s.idle.erase(found);
-        ++s.stats.hits;
-        s.active = true;
-        return Lease(state_, block, std::move(entry.payload), entry.charge);
-    }
-    const bool candidate = s.inspect && s.budget.host_bytes && estimate <= s.budget.host_bytes - s.stats.live_bytes &&
-                           s.headroom(estimate);
-    Payload payload = loader(candidate);
-    if (!payload) throw std::runtime_error("Weight loader returned nothing");
-    ++s.stats.loads;
-    std::uint64_t charge = 0;
-    if (candidate)
-    {
-        const auto measured = s.inspect(payload);
-        if (measured && *measured && *measured <= s.budget.host_bytes - s.stats.live_bytes && s.headroom(0))
-        {
-            charge = *measured;
-            s.stats.live_bytes += charge;
-            s.stats.peak_bytes = std::max(s.stats.peak_bytes, s.stats.live_bytes);
-            ++s.stats.cached_nets;
-            s.stats.peak_nets = std::max(s.stats.peak_nets, s.stats.cached_nets);
-            ++s.stats.admissions;
-        }
-    }
-    s.active = true;
-    return Lease(state_, block, std::move(payload), charge);
-}
-
-WeightSession::Lease::Lease(std::shared_ptr<State> state, std::size_t block, Payload payload, std::uint64_t charge)
-    : state_(std::move(state)), block_(block), payload_(std::move(payload)), charge_(charge)
-{
-}
-
-WeightSession::Lease::Lease(Lease &&o) noexcept
-    : state_(std::move(o.state_)), block_(o.block_), payload_(std::move(o.payload_)), charge_(o.charge_)
-{
-}
-
-WeightSession::Lease &WeightSession::Lease::operator=(Lease &&o) noexcept
-{
-    if (this != &o)
-    {
-        release(false);
-        state_ = std::move(o.state_);
-        block_ = o.block_;
-        payload_ = std::move(o.payload_);
-        charge_ = o.charge_;
-    }
-    return *this;
-}
-
-WeightSession::Lease::~Lease() { release(false); }
-
-const WeightSession::Payload &WeightSession::Lease::payload() const
-{
-    if (!payload_) throw std::logic_error("Weight lease already released");
-    return payload_;
-}
-
-void WeightSession::Lease::complete()
-{
-    if (!payload_) throw std::logic_error("Weight lease already released");
-    release(true);
-}
-
-void WeightSession::Lease::release(bool completed)
-{
-    if (!payload_ || !state_) return;
-    auto &s = *state_;
-    if (completed && charge_ && !s.cancelled) s.idle.emplace(block_, State::Entry{std::move(payload_), charge_});
-    else
-    {
-        payload_.reset();
-        s.stats.live_bytes -= charge_;
-        if (charge_) --s.stats.cached_nets;
-    }
-    s.active = false;
-    state_.reset();
-}
-
 // ---- sessions, block sequence, DiT, denoise --------------------------------------------------------------
 DenoiseSession::DenoiseSession(DitModel &model, int width, int height, int text_tokens, int valid_text,
                                Precision precision)
@@ -827,56 +609,75 @@ Tensor initial_noise(int width, int height, uint32_t seed)
     return noise;
 }
 
+namespace
+{
+bool finite_latent_tensor(const Tensor &t)
+{
+    return !t.empty() && t.dims == 3 && t.c == 128 &&
+           std::all_of(t.data.begin(), t.data.end(), [](float v) { return std::isfinite(v); });
+}
+
+// An img2img request starts inside a flow schedule of 1..1000 steps whose sigmas run from exactly one
+// down to exactly zero, finite, strictly decreasing and inside [0, 1].
+void check_img2img_schedule(const FlowSchedule &schedule)
+{
+    const std::vector<float> &sigma = schedule.sigmas;
+    const size_t steps = schedule.timesteps.size();
+    require(steps >= 1 && steps <= 1000 && sigma.size() == steps + 1 && sigma.front() == 1.f && sigma.back() == 0.f,
+            "Invalid img2img flow schedule");
+    for (size_t i = 0; i < steps; ++i)
+    {
+        const bool ok = std::isfinite(sigma[i]) && std::isfinite(schedule.timesteps[i]) && sigma[i] > sigma[i + 1] &&
+                        sigma[i] >= 0.f && sigma[i] <= 1.f;
+        require(ok, "Img2img flow schedule must descend from one to zero");
+    }
+}
+
+// Steps an img2img request runs: steps * strength rounded half up in FP32, at least one and at most all.
+int img2img_denoise_steps(int steps, float strength)
+{
+    const int rounded = int(std::floor(float(steps) * strength + .5f));
+    return std::clamp(rounded, 1, steps);
+}
+
+// sigma * noise + (1 - sigma) * image with each product and the sum rounded to FP32 on its own (this
+// file is compiled without floating-point contraction).
+Tensor noised_image(const Tensor &image, const Tensor &noise, float sigma)
+{
+    Tensor out(image.w, image.h, 128);
+    const float kept = 1.f - sigma;
+    std::transform(noise.data.begin(), noise.data.end(), image.data.begin(), out.data.begin(), [&](float n, float x) {
+        const float noise_part = sigma * n;
+        const float image_part = kept * x;
+        return noise_part + image_part;
+    });
+    if (!finite_latent_tensor(out)) throw std::runtime_error("Non-finite img2img initial latent");
+    return out;
+}
+} // namespace
+
 Img2ImgStart make_img2img_start(const Tensor &encoded, const Tensor &saved_noise, const FlowSchedule &schedule,
                                 float strength, int threads)
 {
     require(std::isfinite(strength) && strength >= 0.f && strength <= 1.f && threads >= 1 && threads <= 256,
             "Img2img requires strength in [0,1] and threads in [1,256]");
-    const size_t count = schedule.timesteps.size();
-    require(count >= 1 && count <= 1000 && schedule.sigmas.size() == count + 1 && schedule.sigmas.front() == 1.f &&
-                schedule.sigmas.back() == 0.f,
-            "Invalid img2img flow schedule");
-    for (size_t i = 0; i < count; ++i)
-        require(std::isfinite(schedule.sigmas[i]) && std::isfinite(schedule.timesteps[i]) &&
-                    schedule.sigmas[i] > schedule.sigmas[i + 1] && schedule.sigmas[i] >= 0.f && schedule.sigmas[i] <= 1.f,
-                "Img2img flow schedule must descend from one to zero");
-    auto finite = [](const Tensor &t) {
-        if (t.empty() || t.dims != 3 || t.c != 128) return false;
-        for (float v : t.data)
-            if (!std::isfinite(v)) return false;
-        return true;
-    };
-    require(finite(encoded), "Encoded img2img latent must be finite");
-    Img2ImgStart result;
-    result.start_step = int(count);
+    check_img2img_schedule(schedule);
+    require(finite_latent_tensor(encoded), "Encoded img2img latent must be finite");
+    const int steps = int(schedule.timesteps.size());
+    Img2ImgStart start;
     if (strength == 0.f)
     {
-        result.latent = encoded;
-        return result;
+        start.start_step = steps; // nothing to denoise: the encoded image itself
+        start.latent = encoded;
+        return start;
     }
-    require(finite(saved_noise) && saved_noise.w == encoded.w && saved_noise.h == encoded.h,
+    require(finite_latent_tensor(saved_noise) && saved_noise.w == encoded.w && saved_noise.h == encoded.h,
             "Img2img noise must be finite and match the encoded shape");
-    const float scaled = float(count) * strength;
-    result.denoise_steps = std::min(int(count), std::max(1, int(std::floor(scaled + .5f))));
-    result.start_step = int(count) - result.denoise_steps;
-    result.sigma = schedule.sigmas[size_t(result.start_step)];
-    if (result.sigma == 1.f)
-    {
-        result.latent = saved_noise;
-        return result;
-    }
-    result.latent = Tensor(encoded.w, encoded.h, 128);
-    const float retained = 1.f - result.sigma;
-    for (size_t i = 0; i < encoded.total(); ++i)
-    {
-        // two roundings and a third for the sum, no contraction (this file builds with -ffp-contract=off)
-        const float weighted_noise = result.sigma * saved_noise[i];
-        const float weighted_image = retained * encoded[i];
-        result.latent[i] = weighted_noise + weighted_image;
-    }
-    for (float v : result.latent.data)
-        if (!std::isfinite(v)) throw std::runtime_error("Non-finite img2img initial latent");
-    return result;
+    start.denoise_steps = img2img_denoise_steps(steps, strength);
+    start.start_step = steps - start.denoise_steps;
+    start.sigma = schedule.sigmas[size_t(start.start_step)];
+    start.latent = start.sigma == 1.f ? saved_noise : noised_image(encoded, saved_noise, start.sigma);
+    return start;
 }
 
 DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucket, const std::vector<float> &frequencies,
@@ -957,18 +758,18 @@ DitStageResult run_dit_stage(DitModel &model, const Tensor &text, int text_bucke
 // ---- the VAE stage --------------------------------------------------------------------------------
 RgbImage rgb_image(const Tensor &decoded)
 {
-    if (decoded.empty() || decoded.dims != 3 || decoded.c != 3)
-        throw std::runtime_error("VAE output must be pack1 RGB FP32");
-    RgbImage image{decoded.w, decoded.h, std::vector<uint8_t>(size_t(decoded.w) * decoded.h * 3)};
-    const size_t plane = size_t(decoded.w) * decoded.h;
-    for (int c = 0; c < 3; ++c)
-        for (size_t i = 0; i < plane; ++i)
-        {
-            const float x = decoded[size_t(c) * plane + i];
-            if (!std::isfinite(x)) throw std::runtime_error("VAE produced non-finite pixels");
-            const float normalized = std::clamp(x / 2.f + .5f, 0.f, 1.f);
-            image.pixels[i * 3 + size_t(c)] = static_cast<uint8_t>(std::nearbyint(normalized * 255.f));
-        }
+    if (decoded.empty() || decoded.dims != 3 || decoded.c != 3) throw std::runtime_error("VAE output must be pack1 RGB FP32");
+    // [-1, 1] -> [0, 1] clamped -> bytes by round-to-nearest-even of value * 255, as FP32 arithmetic
+    auto to_byte = [](float v) {
+        if (!std::isfinite(v)) throw std::runtime_error("VAE produced non-finite pixels");
+        const float unit = std::clamp(v / 2.f + .5f, 0.f, 1.f);
+        return static_cast<uint8_t>(std::nearbyint(unit * 255.f));
+    };
+    const size_t plane = size_t(decoded.w) * size_t(decoded.h);
+    RgbImage image{decoded.w, decoded.h, std::vector<uint8_t>(plane * 3)};
+    uint8_t *out = image.pixels.data();
+    for (size_t p = 0; p < plane; ++p)
+        for (size_t c = 0; c < 3; ++c) *out++ = to_byte(decoded.data[c * plane + p]); // interleaved RGB
     return image;
 }
 
@@ -1379,31 +1180,32 @@ uint32_t sample_pe_token(const std::vector<float> &logits, const PeOptions &opti
 {
     pe_options_check(options);
     if (logits.empty()) throw std::invalid_argument("PE logits must be an FP32 vector");
-    for (float v : logits)
-        if (!std::isfinite(v)) throw std::runtime_error("Non-finite PE logits");
-    const float *values = logits.data();
-    const int n = static_cast<int>(logits.size());
-    const int best = int(std::max_element(values, values + n) - values);
-    if (options.greedy) return uint32_t(best);
-    std::vector<uint32_t> order(static_cast<size_t>(n));
-    for (int i = 0; i < n; ++i) order[size_t(i)] = uint32_t(i);
-    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return values[a] > values[b]; });
-    std::vector<double> weights(order.size());
+    if (!std::all_of(logits.begin(), logits.end(), [](float v) { return std::isfinite(v); }))
+        throw std::runtime_error("Non-finite PE logits");
+    const auto top = std::max_element(logits.begin(), logits.end()); // the first of equal maxima
+    if (options.greedy) return uint32_t(top - logits.begin());
+    // Tokens by descending logit, equal logits in ascending token order.
+    std::vector<uint32_t> ranked(logits.size());
+    std::iota(ranked.begin(), ranked.end(), 0u);
+    std::sort(ranked.begin(), ranked.end(), [&](uint32_t a, uint32_t b) {
+        return logits[a] != logits[b] ? logits[a] > logits[b] : a < b;
+    });
+    // Relative probabilities exp((logit - max) / temperature) in double, summed in ranked order.
+    std::vector<double> weight(ranked.size());
     double total = 0;
-    for (size_t i = 0; i < order.size(); ++i)
+    for (size_t i = 0; i < ranked.size(); ++i)
+        total += weight[i] = std::exp((double(logits[ranked[i]]) - double(*top)) / double(options.temperature));
+    // Nucleus: the shortest ranked prefix holding top_p of the total weight, never empty.
+    const double nucleus = double(options.top_p) * total;
+    size_t kept = 0;
+    double mass = 0;
+    while (kept < weight.size())
     {
-        weights[i] = std::exp((double(values[order[i]]) - values[best]) / options.temperature);
-        total += weights[i];
+        mass += weight[kept++];
+        if (mass >= nucleus) break;
     }
-    // the shortest prefix whose weight reaches top_p of the total (at least one token)
-    double cumulative = 0;
-    size_t retained = 0;
-    do
-        cumulative += weights[retained++];
-    while (retained < weights.size() && cumulative < options.top_p * total);
-    weights.resize(retained);
-    std::discrete_distribution<size_t> distribution(weights.begin(), weights.end());
-    return order[distribution(random)];
+    std::discrete_distribution<size_t> draw(weight.begin(), weight.begin() + std::ptrdiff_t(kept));
+    return ranked[draw(random)];
 }
 
 PeSession::PeSession(TextModel &model, int capacity, Precision precision) : ctx_(model.context())

@@ -1,7 +1,7 @@
 // Host-side contracts of the C++ surface (no GPU): schedule, features, constants, text padding, error
 // mapping, weight placement decisions, weight-session admission/leases and the recovery loop with a
 // host-side fake backend. Cases follow the reference's tests/test_latent_contract.cpp,
-// tests/test_weight_placement.cpp:42-56, tests/test_weight_session.cpp:36-131 and
+// tests/test_weight_placement.cpp:38-78, tests/test_weight_session.cpp:36-131 and
 // tests/test_memory_execution.cpp:298-419 (recovery_contract); tensor files as src/tensor_io.cpp:10-43.
 #include "ernie_b200/ernie.h"
 #include <cmath>
@@ -122,6 +122,15 @@ static void placement_contract()
     REQUIRE(!first && second && !third && queries == 3 && dynamic.host_requests() == 1 &&
                 dynamic.device_requests() == 2,
             "dynamic budget queries");
+    WeightPlacement manual(WeightMemory::Host, 0, []() -> std::optional<DeviceMemoryBudget> {
+        throw std::runtime_error("an explicit mode must not read the device budget");
+    });
+    REQUIRE(manual.use_host("block", 100, false) && manual.host_requests() == 1, "explicit mode read the budget");
+    std::string seen_reason;
+    WeightPlacement cached(WeightMemory::Auto, 20, [] { return std::optional<DeviceMemoryBudget>(DeviceMemoryBudget{1000, 0}); },
+                           [&](const std::string &, const WeightPlacementDecision &d) { seen_reason = d.reason; });
+    REQUIRE(cached.use_host("block", 100, false, true, "prefetch") && seen_reason == "prefetch",
+            "cache preference in auto mode");
     WeightPlacement unavailable(WeightMemory::Auto, 20);
     REQUIRE(!unavailable.use_host("block", 100, false) && unavailable.unavailable_queries() == 1, "unavailable reader");
     REQUIRE(parse_weight_memory("host") == WeightMemory::Host &&
@@ -184,6 +193,56 @@ static void session_contract()
         REQUIRE(!second.cached() && pressure.stats().evictions == 1 && live_payloads == 1,
                 "Pressure failed to evict idle weights");
         available = 1000;
+    }
+    {
+        // enough RAM above the reserve to reuse a cached block but not to load another: the hit must not
+        // reserve a second copy; below the reserve the idle block is dropped and reloaded
+        WeightSession hit({20, 30}, reader, inspect);
+        auto load = [](bool) { return fake_payload(); };
+        auto first = hit.acquire(0, "graph", &request, 10, load);
+        first.complete();
+        available = 35;
+        auto same = hit.acquire(0, "graph", &request, 10, load);
+        REQUIRE(same.cached() && hit.stats().hits == 1 && hit.stats().loads == 1 && hit.stats().evictions == 0,
+                "Cache hit reserved a second copy of its weights");
+        same.complete();
+        available = 29;
+        auto pressured = hit.acquire(0, "graph", &request, 10, load);
+        REQUIRE(!pressured.cached() && hit.stats().evictions == 1 && hit.stats().loads == 2,
+                "Cache hit ignored the RAM reserve under pressure");
+        pressured.complete();
+        available = 1000;
+    }
+    {
+        WeightSession moves({20, 30}, reader, inspect);
+        auto lease = moves.acquire(0, "graph", &request, 10, [](bool) { return fake_payload(); });
+        auto moved = std::move(lease);
+        REQUIRE(throws<std::logic_error>([&] { lease.payload(); }), "moved-from lease still holds the payload");
+        REQUIRE(moved.payload() != nullptr && moved.cached(), "moved lease lost the payload");
+        moved.complete();
+        REQUIRE(moves.contains(0) && live_payloads == 1, "completed lease did not return to the cache");
+    }
+    REQUIRE(live_payloads == 0, "destroyed session kept an idle payload");
+    {
+        WeightSession oversized({20, 30}, reader, [](const WeightSession::Payload &) -> std::optional<std::uint64_t> { return 21; });
+        auto lease = oversized.acquire(0, "graph", &request, 10, [](bool) { return fake_payload(); });
+        REQUIRE(!lease.cached() && oversized.stats().live_bytes == 0, "Measured charge exceeded budget");
+    }
+    {
+        WeightSession unmeasured({20, 30}, reader,
+                                 [](const WeightSession::Payload &) -> std::optional<std::uint64_t> { return std::nullopt; });
+        auto lease = unmeasured.acquire(0, "graph", &request, 10, [](bool) { return fake_payload(); });
+        REQUIRE(!lease.cached(), "Unverified payload entered the cache");
+    }
+    {
+        WeightSession::Lease orphan;
+        {
+            WeightSession owner({20, 30}, reader, inspect);
+            orphan = owner.acquire(0, "graph", &request, 10, [](bool) { return fake_payload(); });
+        }
+        REQUIRE(live_payloads == 1, "Session destruction invalidated an active lease");
+        orphan.complete();
+        REQUIRE(live_payloads == 0, "Session destruction leaked a payload");
     }
     {
         WeightSession failure({20, 30}, reader, inspect);
@@ -507,7 +566,7 @@ static void pe_sampling_contract()
     REQUIRE(throws<std::runtime_error>([&] { sample_pe_token({0.f, NAN}, options, first); }), "NaN logits accepted");
 }
 
-// text_constants and text_embeddings (src/text_encoder.cpp:48-100) without a device
+// text_constants and text_embeddings (src/text_encoder.cpp:48-104) without a device
 static void text_contract()
 {
     std::vector<float> f(64);
