@@ -16,29 +16,19 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(ec.SIGNATURES), set(declared) ^ set(ec.SIGNATURES)
 
 
-def test_integration_index_names_every_entry_point():
-    """The integration guide's entry-point index lists each declared function, either in full or as
-    `prefix_a` / `_b` (the suffix replacing the last word of the preceding full name)."""
-    import os
-    import re
-    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "INTEGRATION.md")
-    text = open(path).read()
-    index = text[text.index("## 8. Entry-point index"):]
-    listed = set()
-    for row in index.splitlines():
-        cells = row.split("|")
-        if len(cells) < 4 or not row.startswith("| ") or row.startswith("| Group"):
-            continue
-        base = None
-        for name in re.findall(r"`([a-z0-9_]+)`", cells[2]):
-            if name.startswith("ernie_cuda_"):
-                listed.add(name)
-                base = name.rsplit("_", 1)[0]
-            elif name.startswith("_") and base:
-                listed.add(base + name)
+def test_library_exports_nothing_undeclared():
+    """The shared library's dynamic symbol table and include/ernie_cuda.h name the same C entry points:
+    no `ernie_cuda_*` function is exported without a declaration (read with `nm -D`)."""
+    import shutil
+    import subprocess
+    if shutil.which("nm") is None:
+        pytest.skip("binutils nm is not installed")
+    table = subprocess.run(["nm", "-D", "--defined-only", ec.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = {cols[2] for cols in (line.split() for line in table.stdout.splitlines())
+                if len(cols) == 3 and cols[1] == "T" and cols[2].startswith("ernie_cuda_")}
     declared = set(ec.declared_functions())
-    assert declared <= listed, sorted(declared - listed)
-    assert listed <= declared, sorted(listed - declared)
+    assert exported == declared, {"undeclared exports": sorted(exported - declared),
+                                  "declared but not exported": sorted(declared - exported)}
 
 
 @pytest.mark.parametrize("kind,name", [(ec.TURBO, "turbo"), (ec.LINEAR, "linear")])
