@@ -695,6 +695,66 @@ def run_pe(args):
         pg.destroy_process_group()
 
 
+def nccl_version(torch):
+    v = torch.cuda.nccl.version()
+    return ".".join(map(str, v)) if isinstance(v, (tuple, list)) else str(v)
+
+
+def run_exchange(args):
+    """Reference for the sequence-parallel exchange: the same bytes moved by NCCL all-to-alls instead of the
+    library's epilogue peer stores. Per DiT block, one all_to_all_single of this rank's Q, K and V rows of
+    every member's heads (3 x S x 4096 BF16 values out) and one of the attention rows back (S x 4096); 36
+    blocks per step; no compute, so the time is what a plain NCCL exchange adds to each step if nothing
+    hides it. Device-timed with CUDA events on the launching stream, max over ranks."""
+    import torch
+    import ernie_cuda as ec
+    rank, local, world, pg = dist_setup(args.gpus)
+    if world < 2:
+        if rank == 0:
+            print(json.dumps({"metric": "SP exchange ms/step (NCCL all-to-all reference)",
+                              "unavailable": "needs 2 or more ranks under torchrun"}), flush=True)
+        return
+    tokens, image = WIDTH * HEIGHT + TEXT, WIDTH * HEIGHT
+    shard = ec.sp_layout(tokens, image, world, rank)[0]
+    dev = torch.device("cuda", local)
+    qkv_in = torch.randn(3 * shard * 4096, device=dev).to(torch.bfloat16)
+    qkv_out = torch.empty_like(qkv_in)
+    o_in = torch.randn(shard * 4096, device=dev).to(torch.bfloat16)
+    o_out = torch.empty_like(o_in)
+    blocks = args.blocks
+
+    def step():
+        for _ in range(blocks):
+            pg.all_to_all_single(qkv_out, qkv_in)
+            pg.all_to_all_single(o_out, o_in)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    ms_step = max_over_ranks(pg, start.elapsed_time(end) / args.steps)
+    if rank == 0:
+        sent = (4 * shard * 4096 * 2) * (world - 1) // world  # bytes that leave this GPU per block
+        ms_block = ms_step / blocks
+        print(json.dumps({
+            "metric": "SP exchange ms/step (NCCL all-to-all reference)", "impl": "nccl-reference",
+            "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "data": "synthetic",
+            "config": {"workload": f"{args.workload}: the exchange volumes of one Ulysses step, {blocks} blocks x 2 "
+                                   "all_to_all_single (Q/K/V rows out, attention rows back), BF16",
+                       "shard_rows": shard, "ms_per_block": ms_block, "bytes_out_per_rank_per_block": sent,
+                       "gb_per_s_out_per_rank": sent / (ms_block * 1e-3) / 1e9,
+                       "nccl": nccl_version(torch)}}), flush=True)
+    pg.destroy_process_group()
+
+
 def pipeline_stages(ctx, args, ms_per_step, reps=3):
     """Device time of the whole image on this GPU: prompt encode (25 layers at the config's text bucket),
     8 denoise steps (the metric's ms_per_step x 8) and the VAE decode (unpacked latent 2h x 2w), BF16."""
@@ -778,10 +838,11 @@ def main():
     ap.add_argument("--kernel-only", choices=sorted(KERNELS), default=None,
                     help="profiling aid: only run `iters` launches of one block kernel at the C2 shape")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--stage", choices=["dit", "vae", "text", "vae-encode", "pe"], default="dit",
+    ap.add_argument("--stage", choices=["dit", "vae", "text", "vae-encode", "pe", "exchange"], default="dit",
                     help="dit: the denoise loop (the metric); vae: the VAE decode after it; text: the prompt "
                          "encoder before it (at the config's text bucket); vae-encode: img2img's image encoder "
-                         "(1024x1024); pe: the optional prompt enhancer's decode")
+                         "(1024x1024); pe: the optional prompt enhancer's decode; exchange: NCCL all-to-alls of the "
+                         "sequence-parallel exchange volumes (the reference for the fused peer stores)")
     ap.add_argument("--vae-latent", default=None,
                     help="profiling aid: H,W of the unpacked latent of --stage vae (default 128,128: 1024x1024)")
     args = ap.parse_args()
@@ -800,6 +861,8 @@ def main():
         return run_vae_encode_reference(args) if args.impl == "reference" else run_vae_encode(args)
     if args.stage == "pe":
         return run_pe_reference(args) if args.impl == "reference" else run_pe(args)
+    if args.stage == "exchange":
+        return run_exchange(args)
     if args.impl == "reference":
         return run_reference(args)
 
