@@ -154,6 +154,23 @@ def cpu_baseline_block(threads=None):
     return dt, o.lib().orc_num_threads()
 
 
+# The reference's own published CPU timing of the same block: ncnn CPU FP32 on 4 threads of a Ryzen 7 7745HX,
+# 4.484 / 4.434 / 4.403 s for one 4160-token block (artifacts/2026-09-05/dit-block/README.md:53 of the
+# reference). It cannot be reproduced here (empty ncnn submodule); it is printed beside the port's timing so
+# that the GPU/CPU ratio can also be read against the real ncnn CPU path (about 6x faster per core).
+REFERENCE_CPU_BLOCK_S = 4.434
+REFERENCE_CPU_THREADS = 4
+
+
+def reference_published_cpu():
+    image_s = REFERENCE_CPU_BLOCK_S * NUM_BLOCKS * STEPS_PER_IMAGE
+    return {"value": 1.0 / image_s, "unit": "images/s", "cores": REFERENCE_CPU_THREADS,
+            "block_s": REFERENCE_CPU_BLOCK_S,
+            "source": "reference artifacts/2026-09-05/dit-block/README.md:53: ncnn CPU FP32, 4 threads, Ryzen 7 "
+                      "7745HX, one 4160-token block (median of 3); x36 blocks x8 steps; published, not re-run",
+            "applies_to": "c2 (4160 tokens)"}
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference's CPU path on this host's cores (the
     reference itself cannot be built: empty ncnn submodule, no Rust toolchain, no Vulkan)."""
@@ -177,7 +194,8 @@ def run_reference(args):
                        "sample": "1 DiT block per step sample, extrapolated x36 blocks x8 steps"},
             "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port",
                              "sample": f"one DiT block ({WIDTH * HEIGHT + TEXT} tokens) of the oracle per step; "
-                                       "x36 x8 extrapolated"},
+                                       "x36 x8 extrapolated",
+                             "reference_published": reference_published_cpu() if args.config == "c2" else None},
             "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -987,7 +1005,8 @@ def main():
         image_s = block_s * args.blocks * STEPS_PER_IMAGE
         cpu = {"value": 1.0 / image_s, "unit": "images/s", "cores": cores, "kind": "port",
                "sample": f"one DiT block at {tokens} tokens on the CPU restatement ({block_s:.2f} s), "
-                         f"extrapolated x{args.blocks} blocks x{STEPS_PER_IMAGE} steps"}
+                         f"extrapolated x{args.blocks} blocks x{STEPS_PER_IMAGE} steps",
+               "reference_published": reference_published_cpu() if args.config == "c2" else None}
 
     if rank == 0:
         line = {"metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
