@@ -199,6 +199,7 @@ extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_f32_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_conv_kernels());
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_norm_kernels());
     if (e != cudaSuccess)
     {
         ernie_cuda_context_destroy(ctx);
@@ -1032,7 +1033,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
     const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
     if (on(0))
-        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_sa, scale_sa, shift_sa, 1e-6f, 0, s->a, fp32, st), "norm sa");
+        ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_sa, scale_sa, shift_sa, 1e-6f, s->a, fp32, s->ctx->num_sms,
+                                                s->ctx->error_flag, st),
+                     "norm sa");
     GemmEpilogueArgs qkv;
     if (seq_parallel)
     {
@@ -1098,7 +1101,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     res.error_flag = s->ctx->error_flag;
     if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 256, Epilogue::ResidGate, res), "out proj");
     if (on(4))
-        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
+        ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, s->a, fp32,
+                                                s->ctx->num_sms, s->ctx->error_flag, st),
+                     "norm mlp");
     GemmEpilogueArgs gg;
     gg.h = s->h;
     gg.h_split3 = fp32;

@@ -72,6 +72,14 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+// max(a, b, c) in one instruction (the three-input form of max.f32, sm_100)
+__device__ __forceinline__ float max3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
@@ -335,14 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (k > lim) x[k] = -INFINITY;
                 }
             }
-            // row max over 8 independent chains
+            // row max over 8 independent chains, two new scores per three-input max
             float mx[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) mx[k] = x[k];
 #pragma unroll
-            for (int k = 8; k < 128; ++k) mx[k & 7] = fmaxf(mx[k & 7], x[k]);
-            const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            for (int k = 8; k < 128; k += 2) mx[(k >> 1) & 7] = max3(mx[(k >> 1) & 7], x[k], x[k + 1]);
+            const float tmax = fmaxf(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], max3(mx[5], mx[6], mx[7])));
             // PV_g(j-1) has read P_g(j-1) (and added into O_g) before P_g(j) or a rescale may touch them
             if (j > 0)
             {

@@ -432,10 +432,23 @@ __device__ __forceinline__ void run_epilogue(const EpiCtx &e, const GemmEpilogue
 // K=12288 for exact operands; 6.5e-8 when restarted every 64 elements). With PROMOTE the MMA warp
 // restarts the accumulator every `group` k-blocks (two alternating TMEM buffers) and the epilogue
 // warps add each partial into FP32 registers, so no chain exceeds group*64 products.
+// Output tile t -> (m block, n block). Tiles run through the n blocks of a band of `band` m blocks (m
+// fastest inside the band), band after band, so that consecutive rounds of tiles over the SMs reuse
+// one band's A rows from L2 while B streams; band >= num_m is the plain m-fastest order.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int band, int &m_blk, int &n_blk)
+{
+    const int per_band = band * num_n;
+    const int b = t / per_band, r = t - b * per_band;
+    const int first = b * band;
+    const int rows = min(band, num_m - first);
+    m_blk = first + r % rows;
+    n_blk = r / rows;
+}
+
 template <int BN, Epilogue EPI, bool PROMOTE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m, int n,
-                int k_b, int splits, int group, GemmEpilogueArgs args)
+                int k_b, int splits, int group, int band, GemmEpilogueArgs args)
 {
     using C = Cfg<BN, PROMOTE>;
     extern __shared__ uint8_t smem_raw[];
@@ -494,7 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
-                const int m_blk = tile % num_m, n_blk = tile / num_m;
+                int m_blk, n_blk;
+                tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
                 for (int kb = 0; kb < k_blocks; ++kb)
                 {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u))
@@ -575,7 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
         {
-            const int m_blk = tile % num_m, n_blk = tile / num_m;
+            int m_blk, n_blk;
+            tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
             const int row0 = m_blk * BM + quarter * 32;
             uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
             if constexpr (!PROMOTE)
@@ -668,7 +683,7 @@ template <int BN> struct PairCfg
 template <int BN, Epilogue EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m,
-                     int n, int k_b, GemmEpilogueArgs args)
+                     int n, int k_b, int band, GemmEpilogueArgs args)
 {
     using C = PairCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -730,7 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int tile = pair; tile < tiles && ok; tile += pairs)
             {
-                const int m_blk = tile % num_m, n_blk = tile / num_m;
+                int m_blk, n_blk;
+                tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
                 for (int kb = 0; kb < k_blocks; ++kb)
                 {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u))
@@ -827,7 +843,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int unit = 0;
         for (int tile = pair; tile < tiles; tile += pairs, ++unit)
         {
-            const int m_blk = tile % num_m, n_blk = tile / num_m;
+            int m_blk, n_blk;
+            tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
             const int row0 = m_blk * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;
             uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
             const int acc = unit & 1;
@@ -855,6 +872,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---- host side ------------------------------------------------------------------------------
+// Band of m blocks for tile_coords. While A (m x k_a BF16) fits in L2 next to the streamed B tiles and
+// the epilogue's traffic, the m-fastest order keeps it resident and reads B once. A larger A (the down
+// projection's 12288-wide rows: 107 MB at 4160 rows, 203 MB at 8256) would be re-read from DRAM in every
+// round of tiles; then the m blocks are cut into the fewest equal bands of at most kBandBytes of A, each
+// band staying resident while B streams past it once.
+#ifndef ERNIE_GEMM_BAND_BYTES
+#define ERNIE_GEMM_BAND_BYTES (64ll << 20)
+#endif
+constexpr long long kBandBytes = ERNIE_GEMM_BAND_BYTES, kResidentA = 96ll << 20;
+int tile_band(int num_m, int tile_rows, int k_a)
+{
+    const long long per_block = static_cast<long long>(tile_rows) * k_a * 2;
+    const long long a_bytes = num_m * per_block;
+    if (kBandBytes <= 0 || a_bytes <= kResidentA) return num_m;
+    const long long bands = (a_bytes + kBandBytes - 1) / kBandBytes;
+    return static_cast<int>((num_m + bands - 1) / bands);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -958,7 +993,8 @@ int launch_pair(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     attrs[0].val.clusterDim.z = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, args);
+    const int band = tile_band((m + 2 * BM - 1) / (2 * BM), 2 * BM, k_b);
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, band, args);
 }
 
 template <int BN, Epilogue EPI, bool PROMOTE>
@@ -977,8 +1013,9 @@ int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     const int group = k_blocks % 4 == 0 ? 4 : k_blocks % 2 == 0 ? 2 : 1;
     const int tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
+    const int band = tile_band((m + BM - 1) / BM, BM, k_b * splits);
     gemm_kernel<BN, EPI, PROMOTE><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, group,
-                                                                             args);
+                                                                             band, args);
     return cudaGetLastError();
 }
 
