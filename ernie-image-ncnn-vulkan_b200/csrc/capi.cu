@@ -131,6 +131,10 @@ struct ernie_cuda_session
     float *text_stage = nullptr, *gathered = nullptr;
     int *flags_all = nullptr;
     unsigned *slots = nullptr, *epoch = nullptr;
+    // Completion flags carried by the kernels of a whole block (instead of the two barrier kernels):
+    // arrival slots per member in the arena (QKV stores landed, attention rows landed) and this GPU's
+    // counters: [0] QKV warps finished, [1] QKV epoch, [2] attention warps finished, [3] attention epoch.
+    unsigned *arrive_qkv = nullptr, *arrive_att = nullptr, *sync_state = nullptr;
 };
 
 namespace
@@ -155,6 +159,30 @@ int sp_barrier(ernie_cuda_session *s)
     b.timeout_ns = kPeerTimeoutNs;
     b.error_flag = s->ctx->error_flag;
     return from_launch(launch_peer_barrier(b, s->ctx->stream), "peer barrier");
+}
+
+// The signal of a producing kernel: its finished-warp counter and epoch on this GPU, and this GPU's slot
+// in every member's `arrive` array.
+PeerSignal sp_signal(ernie_cuda_session *s, unsigned *counter, unsigned *epoch, unsigned *arrive)
+{
+    PeerSignal g;
+    g.counter = counter;
+    g.epoch = epoch;
+    g.members = s->sp_world;
+    for (int p = 0; p < s->sp_world; ++p) g.peer_slot[p] = peer_ptr(s, p, arrive) + s->sp_rank;
+    return g;
+}
+
+// The wait of a consuming kernel: every member's slot in this GPU's `arrive` array reaches `epoch`.
+PeerWait sp_wait(ernie_cuda_session *s, const unsigned *arrive, const unsigned *epoch)
+{
+    PeerWait w;
+    w.slots = arrive;
+    w.epoch = epoch;
+    w.members = s->sp_world;
+    w.timeout_ns = kPeerTimeoutNs;
+    w.error_flag = s->ctx->error_flag;
+    return w;
 }
 
 // Stores `bytes` of this GPU's `src` at `dst_local`'s place in every member's arena.
@@ -810,6 +838,7 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
         arena.add(&s->text_op, size_t(s->text) * kTextDim);
         arena.add(&s->text_stage, size_t(s->text) * kTextDim);
         arena.add(&s->epoch, 1);
+        arena.add(&s->sync_state, 4);
         shared.add(&s->q_full, hl * F * kHeadDim);
         shared.add(&s->k_full, hl * F * kHeadDim);
         shared.add(&s->vt_full, hl * kHeadDim * F);
@@ -817,6 +846,8 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
         shared.add(&s->gathered, size_t(world) * L);
         shared.add(&s->flags_all, size_t(world) * kMaxSteps);
         shared.add(&s->slots, kMaxDest);
+        shared.add(&s->arrive_qkv, kMaxDest);
+        shared.add(&s->arrive_att, kMaxDest);
     }
     cudaError_t e = arena.allocate();
     s->alloc = arena.base;
@@ -1036,6 +1067,19 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
         ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_sa, scale_sa, shift_sa, 1e-6f, s->a, fp32, s->ctx->num_sms,
                                                 s->ctx->error_flag, st),
                      "norm sa");
+    // A whole block of a sequence-parallel member synchronises through flags carried by its kernels: the
+    // QKV GEMM's last warp announces that its heads have landed, the attention waits for every member's
+    // announcement before its first load and announces its stored rows, and the out-projection waits for
+    // those. Parts enqueued one at a time (the per-part profile) use the barrier kernels instead.
+    const bool flags = seq_parallel && only < 0;
+    PeerSync qkv_sync, att_sync, out_sync;
+    if (flags)
+    {
+        qkv_sync.signal = sp_signal(s, s->sync_state + 0, s->sync_state + 1, s->arrive_qkv);
+        att_sync.wait = sp_wait(s, s->arrive_qkv, s->sync_state + 1);
+        att_sync.signal = sp_signal(s, s->sync_state + 2, s->sync_state + 3, s->arrive_att);
+        out_sync.wait = sp_wait(s, s->arrive_att, s->sync_state + 3);
+    }
     GemmEpilogueArgs qkv;
     if (seq_parallel)
     {
@@ -1066,7 +1110,10 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.cos_t = s->cos_t;
     qkv.sin_t = s->sin_t;
     qkv.error_flag = s->ctx->error_flag;
+    if (flags) qkv.sync = qkv_sync;
     if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, 256, Epilogue::Qkv, qkv), "qkv");
+    else if (flags && T == 0) // no rows of its own: announce the (empty) QKV stores all the same
+        ERNIE_LAUNCH(launch_peer_signal(qkv_sync.signal, st), "qkv signal");
     if (!on(2)) {}
     else if (seq_parallel)
     {
@@ -1078,11 +1125,12 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
         o.rows_per_dest = s->tokens;
         o.ld = kHidden;
         o.col_offset = s->sp_rank * s->heads_local * kHeadDim;
-        ERNIE_TRY(sp_barrier(s));
+        if (!flags) ERNIE_TRY(sp_barrier(s));
         ERNIE_LAUNCH(launch_flash_tc(s->q_full, s->k_full, s->vt_full, s->use_mask ? s->mask : nullptr, rows,
-                                     s->full_rows, s->kv_len, s->heads_local, o, s->ctx->error_flag, st),
+                                     s->full_rows, s->kv_len, s->heads_local, o, s->ctx->error_flag, st, 0, 0,
+                                     flags ? &att_sync : nullptr),
                      "attention");
-        ERNIE_TRY(sp_barrier(s));
+        if (!flags) ERNIE_TRY(sp_barrier(s));
     }
     else if (fp32)
         ERNIE_LAUNCH(launch_flash_f32(static_cast<const __nv_bfloat16 *>(s->q), static_cast<const __nv_bfloat16 *>(s->k),
@@ -1099,7 +1147,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     res.ldo = kHidden;
     res.gate = gate_sa;
     res.error_flag = s->ctx->error_flag;
+    if (flags) res.sync = out_sync;
     if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 256, Epilogue::ResidGate, res), "out proj");
+    res.sync = PeerSync();
     if (on(4))
         ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, s->a, fp32,
                                                 s->ctx->num_sms, s->ctx->error_flag, st),

@@ -27,6 +27,7 @@
 // K-major operands. All mbarrier waits are bounded. Every TMA load fills this CTA's own shared memory.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "peer_sync.cuh"
 #include <cudaTypedefs.h>
 #include <mutex>
 
@@ -63,6 +64,7 @@ struct FlashArgs
     int *error_flag;
     int causal = 0;   // key j > query i excluded; key tiles past the CTA's last query skipped
     int kv_group = 1; // query heads per K/V head (grouped-query attention)
+    PeerSync sync;    // sequence parallel: wait for every member's Q/K/V rows, signal the stored output rows
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -167,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
         if (warp == 0 && lane == 0)
         {
+            peer_wait_all(a.sync.wait);
             const int row_q = head * a.rows_pad + q0;
             mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
             for (int g = 0; g < 2; ++g)
@@ -190,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         else if (warp == 2 && lane == 0)
         {
+            peer_wait_all(a.sync.wait);
             for (int j = 0; j < tiles; ++j)
             {
                 if (!mbar_wait(v_empty, (j & 1) ^ 1u))
@@ -448,6 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tmem_done);
+        peer_signal_warp(a.sync.signal); // this warp's output rows are stored
     }
 }
 
@@ -492,7 +497,7 @@ int prepare_flash_kernels()
 
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
                     int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
-                    cudaStream_t stream, int causal, int kv_heads)
+                    cudaStream_t stream, int causal, int kv_heads, const PeerSync *sync)
 {
     if (kv_heads == 0) kv_heads = heads;
     if (rows < 1 || kv_len < 1 || kv_len > rows_pad || rows_pad % kTile || rows > rows_pad || heads < 1 ||
@@ -510,6 +515,11 @@ int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_b
     a.causal = causal ? 1 : 0;
     a.kv_group = heads / kv_heads;
     const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta, heads);
+    if (sync)
+    {
+        a.sync = *sync;
+        a.sync.signal.warps = static_cast<int>(grid.x * grid.y) * 8; // the eight softmax warps of each CTA
+    }
     flash_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
     return cudaGetLastError();
 }

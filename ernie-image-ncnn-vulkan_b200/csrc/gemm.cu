@@ -18,6 +18,7 @@
 //               i overlap the main loop of tile i+1.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "peer_sync.cuh"
 #include <cudaTypedefs.h>
 #include <mutex>
 
@@ -505,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            peer_wait_all(args.sync.wait); // sequence parallel: every member's rows of A have landed
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
                 int m_blk, n_blk;
@@ -646,6 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 run_epilogue<BN, EPI>(EpiCtx{result, row0, lane, m, n_blk, stage}, args);
             }
         }
+        peer_signal_warp(args.sync.signal); // this warp's stores are done
     }
     __syncthreads();
     if (warp == 1)
@@ -743,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            peer_wait_all(args.sync.wait); // sequence parallel: every member's rows of A have landed
             for (int tile = pair; tile < tiles && ok; tile += pairs)
             {
                 int m_blk, n_blk;
@@ -860,6 +864,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
         }
+        peer_signal_warp(args.sync.signal); // this warp's stores are done
     }
     // no CTA leaves (or frees TMEM) while its partner may still signal its barriers or use its TMEM
     tc_fence_before();
@@ -994,7 +999,9 @@ int launch_pair(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
     const int band = tile_band((m + 2 * BM - 1) / (2 * BM), 2 * BM, k_b);
-    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, band, args);
+    GemmEpilogueArgs launch_args = args;
+    launch_args.sync.signal.warps = 2 * pairs * 4; // four epilogue warps per CTA
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, band, launch_args);
 }
 
 template <int BN, Epilogue EPI, bool PROMOTE>
@@ -1014,8 +1021,10 @@ int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     const int tiles = ((m + BM - 1) / BM) * (n / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     const int band = tile_band((m + BM - 1) / BM, BM, k_b * splits);
+    GemmEpilogueArgs launch_args = args;
+    launch_args.sync.signal.warps = grid * 4; // four epilogue warps per CTA
     gemm_kernel<BN, EPI, PROMOTE><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, group,
-                                                                             band, args);
+                                                                             band, launch_args);
     return cudaGetLastError();
 }
 

@@ -22,6 +22,34 @@ enum class Epilogue : int
 // Destinations of the fused sequence-parallel stores (one per GPU of the group).
 constexpr int kMaxDest = 8;
 
+// Completion flags of a sequence-parallel group, carried by the kernels themselves (used instead of the
+// two barrier kernels when a whole block is enqueued). A producing kernel (the QKV GEMM, whose epilogue
+// stores heads into their owners; the attention, whose epilogue stores rows into their owners) counts
+// its finishing warps; the last one publishes the next epoch into slot `rank` of every member (release,
+// system scope). A consuming kernel's loading threads wait (acquire, bounded by timeout_ns) until every
+// slot of this GPU's array reaches this GPU's own epoch of that producer, before their first bulk load.
+struct PeerSignal
+{
+    unsigned *counter = nullptr;         // this GPU: warps of the current launch that have finished
+    int warps = 0;                       // warps that arrive per launch (set by the launcher)
+    unsigned *epoch = nullptr;           // this GPU: launches of the producer signalled so far
+    unsigned *peer_slot[kMaxDest] = {};  // member p's arrival slot for this GPU
+    int members = 0;
+};
+struct PeerWait
+{
+    const unsigned *slots = nullptr; // this GPU's [members] arrival slots
+    const unsigned *epoch = nullptr; // this GPU's epoch of the producer (its own launch has signalled)
+    int members = 0;
+    long long timeout_ns = 0;
+    int *error_flag = nullptr;
+};
+struct PeerSync
+{
+    PeerWait wait;     // before the first load (slots null: no wait)
+    PeerSignal signal; // after the last store (counter null: no signal)
+};
+
 struct GemmEpilogueArgs
 {
     // F32Bias
@@ -57,6 +85,7 @@ struct GemmEpilogueArgs
     int *finite_flag = nullptr; // set to 1 if any updated latent value is not finite
     // all
     int *error_flag = nullptr;
+    PeerSync sync; // sequence parallel: wait before the first A/B load, signal after the last store
 };
 
 // C[M, N] = A[M, K_a] * B[N, K_b]^T with BF16 operands and FP32 accumulation on tcgen05.
@@ -108,7 +137,7 @@ struct FlashOutput
 // h / (heads / kv_heads), k [kv_heads][rows_pad][128], vt [kv_heads][128][rows_pad].
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,
                     int rows, int rows_pad, int kv_len, int heads, const FlashOutput &out, int *error_flag,
-                    cudaStream_t stream, int causal = 0, int kv_heads = 0);
+                    cudaStream_t stream, int causal = 0, int kv_heads = 0, const PeerSync *sync = nullptr);
 // Barrier of a sequence-parallel group over peer memory: this GPU's arrival is stored (release, system
 // scope) into slot `rank` of every member's slots; then it waits (acquire, bounded by `timeout_ns`) until
 // every member's arrival in its own slots reaches the same epoch. Epochs count up on the device, so the
@@ -123,6 +152,8 @@ struct PeerBarrier
     int *error_flag = nullptr;
 };
 int launch_peer_barrier(const PeerBarrier &barrier, cudaStream_t stream);
+// The signal alone, for a member whose producing kernel has no rows to run.
+int launch_peer_signal(const PeerSignal &signal, cudaStream_t stream);
 // Stores `bytes` (a multiple of 4) of src into every destination (peer memory included).
 struct PeerPut
 {

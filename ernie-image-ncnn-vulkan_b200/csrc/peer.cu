@@ -5,6 +5,7 @@
 // scope and give up after a fixed time (status 21 in the context's error flag). Also the store of one
 // buffer into every member's memory (the gather of latent slices and step flags).
 #include "kernels.h"
+#include "peer_sync.cuh"
 #include <algorithm>
 #include <cstdint>
 
@@ -81,6 +82,22 @@ int launch_peer_barrier(const PeerBarrier &barrier, cudaStream_t stream)
     for (int d = 0; d < barrier.world; ++d)
         if (!barrier.peer_slots[d]) return cudaErrorInvalidValue;
     peer_barrier_kernel<<<1, 32, 0, stream>>>(barrier);
+    return cudaGetLastError();
+}
+
+namespace
+{
+__global__ void peer_signal_kernel(PeerSignal s) { peer_signal_warp(s); }
+} // namespace
+
+int launch_peer_signal(const PeerSignal &signal, cudaStream_t stream)
+{
+    if (!signal.counter || !signal.epoch || signal.members < 1 || signal.members > kMaxDest) return cudaErrorInvalidValue;
+    for (int d = 0; d < signal.members; ++d)
+        if (!signal.peer_slot[d]) return cudaErrorInvalidValue;
+    PeerSignal one = signal;
+    one.warps = 1;
+    peer_signal_kernel<<<1, 32, 0, stream>>>(one);
     return cudaGetLastError();
 }
 
