@@ -957,6 +957,8 @@ def main():
     in_block = {name: session.profile(10 + kernel, 7) for kernel, name in
                 ((0, "norm_modulate"), (1, "qkv_gemm"), (2, "attention"), (3, "out_gemm"), (4, "norm_mlp"),
                  (5, "upgate_gemm"), (6, "down_gemm"))}
+    if sp:  # the same block with the two barrier kernels instead of the kernels' completion flags
+        prof["block_barriers"] = session.profile(17, 36)
     prof["step_eager"] = session.profile(8, 2)  # one step enqueued without a graph
     prof["heads"] = session.profile(9, 10)  # input head, GEMVs, output head + Euler of one step
     bf16_peak, bf16_sustained, hbm_peak, peak_kind = peaks()

@@ -1456,13 +1456,27 @@ extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent
 
 extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int iters, float *ms)
 {
-    if (!s || !ms || kernel < 0 || kernel > 16 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
+    if (!s || !ms || kernel < 0 || kernel > 17 || iters < 1) return fail(ERNIE_CUDA_ERROR, "Invalid profile request");
     if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs set_conditioning");
     DeviceGuard guard(s->ctx->device);
     ernie_cuda_context *ctx = s->ctx;
     // launches cycle through the model's blocks so weights stream from HBM as in a real step;
     // kernel 7 = one whole block (all seven launches), kernel 8 = one full denoise step
     const int nb = s->model->num_blocks;
+    if (kernel == 17)
+    {
+        // whole blocks enqueued part by part (sequence parallel: barrier kernels between the exchanges)
+        for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, p)); // warm-up block
+        ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
+        for (int i = 0; i < iters; ++i)
+            for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p));
+        ERNIE_CUDA(cudaEventRecord(ctx->events[15], ctx->stream), "event");
+        ERNIE_CUDA(cudaEventSynchronize(ctx->events[15]), "event");
+        float total = 0.f;
+        ERNIE_CUDA(cudaEventElapsedTime(&total, ctx->events[14], ctx->events[15]), "event");
+        *ms = total / iters;
+        return ernie_cuda_context_synchronize(ctx);
+    }
     if (kernel >= 10)
     {
         // one part inside whole blocks: events around it in each of up to 7 consecutive blocks

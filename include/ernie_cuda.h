@@ -405,7 +405,9 @@ int ernie_cuda_finite_latent_noalloc(ernie_cuda_context *ctx, const float *laten
    as in a step (kernel 0 norm+modulate, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 MLP
    norm+modulate, 5 up/gate GEMM, 6 down GEMM, 7 a whole block, 8 a whole denoise step after one has
    run, 9 the same step without its blocks; 10..16 = part 0..6 timed inside consecutive whole blocks,
-   at most 7 of them); and the number of kernels one denoise step launches. */
+   at most 7 of them; 17 a whole block enqueued part by part, which in a sequence-parallel session
+   synchronises through the two barrier kernels instead of the kernels' completion flags); and the
+   number of kernels one denoise step launches. */
 int ernie_cuda_session_profile(ernie_cuda_session *session, int kernel, int iters, float *ms);
 int ernie_cuda_session_launches_per_step(ernie_cuda_session *session, int *launches);
 
