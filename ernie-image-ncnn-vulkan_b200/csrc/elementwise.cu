@@ -294,16 +294,19 @@ __global__ void to_operand_kernel(const float *src, long long rows, int cols, __
 // ---- streamed RMSNorm + modulate (the DiT block's two norms) ------------------------------------
 // One persistent CTA per SM walks rows blockIdx.x, + gridDim.x, ... A producer thread keeps up to
 // kStreamStages rows (16 KB of FP32 each) in flight as bulk copies into a shared-memory ring, so each SM
-// has ~190 KB of reads outstanding whatever the consumers are doing; six consumer warps take one row
-// each (lane l holds columns 4(l + 32k) .. +3, k < 32), reduce the sum of squares with shuffles (no
-// block-wide barrier), release the buffer and write the modulated BF16 row (or three planes). Stage s is
-// always consumed by warp s % 6, so a warp's wait on a stage's parity can never see a later round.
-constexpr int kStreamConsumers = 6;
+// has 160 KB of reads outstanding whatever the consumers are doing. gamma, scale and shift are copied
+// into shared memory once per CTA (48 KB), so a consumer's per-element operands are shared-memory
+// reads. Five consumer warps take one row each (lane l holds columns 4(l + 32k) .. +3, k < 32), reduce
+// the sum of squares with shuffles (no block-wide barrier), release the buffer and write the modulated
+// BF16 row (or three planes). Stage s is always consumed by warp s % 5, so a warp's wait on a stage's
+// parity can never see a later round.
+constexpr int kStreamConsumers = 5;
 constexpr int kStreamStages = 2 * kStreamConsumers;
 constexpr int kStreamWidth = 4096;
 constexpr int kStreamRowBytes = kStreamWidth * 4;
 constexpr int kStreamThreads = 32 * (1 + kStreamConsumers);
-constexpr int kStreamSmemBytes = kStreamStages * kStreamRowBytes + 2 * kStreamStages * 8 + 128;
+constexpr int kStreamVectorBytes = 3 * kStreamRowBytes; // gamma, scale, shift
+constexpr int kStreamSmemBytes = kStreamStages * kStreamRowBytes + kStreamVectorBytes + 2 * kStreamStages * 8 + 128;
 constexpr int kErrNormTimeout = 31;
 
 __device__ __forceinline__ void bulk_row_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
@@ -321,8 +324,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 127u) & ~127u;
-    const uint8_t *base_ptr = smem_raw + (base - raw);
-    const uint32_t bars = base + kStreamStages * kStreamRowBytes;
+    uint8_t *base_ptr = smem_raw + (base - raw);
+    float4 *vec = reinterpret_cast<float4 *>(base_ptr + kStreamStages * kStreamRowBytes); // [3][1024]
+    const uint32_t bars = base + kStreamStages * kStreamRowBytes + kStreamVectorBytes;
     auto full = [&](int st) { return bars + 8u * st; };
     auto empty = [&](int st) { return bars + 8u * (kStreamStages + st); };
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -337,14 +341,32 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         fence_barrier_init();
     }
     __syncthreads();
+    if (warp == 0 && lane == 0)
+    {
+        // the row stream starts before the vectors are staged
+        for (int i = 0; i < count && i < kStreamStages; ++i)
+        {
+            mbar_arrive_expect_tx(full(i), kStreamRowBytes);
+            bulk_row_load(base + i * kStreamRowBytes, x + (blockIdx.x + static_cast<size_t>(i) * gridDim.x) * kStreamWidth,
+                          kStreamRowBytes, full(i));
+        }
+    }
+    // gamma (and scale, shift when present: 1 + scale and shift otherwise 1 and 0) into shared memory
+    for (int i = threadIdx.x; i < kStreamWidth / 4; i += kStreamThreads)
+    {
+        vec[i] = __ldg(reinterpret_cast<const float4 *>(gamma) + i);
+        vec[1024 + i] = scale ? __ldg(reinterpret_cast<const float4 *>(scale) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vec[2048 + i] = shift ? __ldg(reinterpret_cast<const float4 *>(shift) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
     if (warp == 0)
     {
         if (lane != 0) return;
-        int issued = 0;
+        int issued = count < kStreamStages ? count : kStreamStages;
         for (; issued < count; ++issued)
         {
             const int st = issued % kStreamStages, round = issued / kStreamStages;
-            if (round > 0 && !mbar_wait(empty(st), (round - 1) & 1))
+            if (!mbar_wait(empty(st), (round - 1) & 1))
             {
                 if (error_flag) atomicExch(error_flag, kErrNormTimeout);
                 break;
@@ -359,6 +381,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                 atomicExch(error_flag, kErrNormTimeout);
         return;
     }
+    const bool modulate = scale != nullptr;
     const int consumer = warp - 1;
     for (int i = consumer; i < count; i += kStreamConsumers)
     {
@@ -386,14 +409,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
         for (int k = 0; k < 32; ++k)
         {
-            const int col = (lane + 32 * k) * 4;
-            const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma + col));
+            const int c4 = lane + 32 * k, col = c4 * 4;
+            const float4 g = vec[c4];
             float y[4] = {v[k].x * inverse * g.x, v[k].y * inverse * g.y, v[k].z * inverse * g.z,
                           v[k].w * inverse * g.w};
-            if (scale)
+            if (modulate)
             {
-                const float4 sc = __ldg(reinterpret_cast<const float4 *>(scale + col));
-                const float4 sh = __ldg(reinterpret_cast<const float4 *>(shift + col));
+                const float4 sc = vec[1024 + c4], sh = vec[2048 + c4];
                 y[0] = y[0] * (1.f + sc.x) + sh.x;
                 y[1] = y[1] * (1.f + sc.y) + sh.y;
                 y[2] = y[2] * (1.f + sc.z) + sh.z;
