@@ -227,7 +227,6 @@ extern "C" int ernie_cuda_context_create(int device, ernie_cuda_context **out)
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_flash_f32_kernels());
     if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_conv_kernels());
-    if (e == cudaSuccess) e = static_cast<cudaError_t>(prepare_norm_kernels());
     if (e != cudaSuccess)
     {
         ernie_cuda_context_destroy(ctx);
@@ -1064,9 +1063,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
     const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
     if (on(0))
-        ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_sa, scale_sa, shift_sa, 1e-6f, s->a, fp32, s->ctx->num_sms,
-                                                s->ctx->error_flag, st),
-                     "norm sa");
+        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_sa, scale_sa, shift_sa, 1e-6f, 0, s->a, fp32, st), "norm sa");
     // A whole block of a sequence-parallel member synchronises through flags carried by its kernels: the
     // QKV GEMM's last warp announces that its heads have landed, the attention waits for every member's
     // announcement before its first load and announces its stored rows, and the out-projection waits for
@@ -1151,9 +1148,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 256, Epilogue::ResidGate, res), "out proj");
     res.sync = PeerSync();
     if (on(4))
-        ERNIE_LAUNCH(launch_rms_modulate_stream(x, T, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, s->a, fp32,
-                                                s->ctx->num_sms, s->ctx->error_flag, st),
-                     "norm mlp");
+        ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
     GemmEpilogueArgs gg;
     gg.h = s->h;
     gg.h_split3 = fp32;

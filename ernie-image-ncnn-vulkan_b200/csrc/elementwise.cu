@@ -4,7 +4,6 @@
 // each element once with 16-byte vector accesses where the layout allows.
 #include "kernels.h"
 #include "ernie_synth.h"
-#include "ptx.cuh"
 
 namespace ernie_b200
 {
@@ -291,154 +290,6 @@ __global__ void to_operand_kernel(const float *src, long long rows, int cols, __
     }
 }
 
-// ---- streamed RMSNorm + modulate (the DiT block's two norms) ------------------------------------
-// One persistent CTA per SM walks rows blockIdx.x, + gridDim.x, ... A producer thread keeps up to
-// kStreamStages rows (16 KB of FP32 each) in flight as bulk copies into a shared-memory ring, so each SM
-// has 160 KB of reads outstanding whatever the consumers are doing. gamma, scale and shift are copied
-// into shared memory once per CTA (48 KB), so a consumer's per-element operands are shared-memory
-// reads. Five consumer warps take one row each (lane l holds columns 4(l + 32k) .. +3, k < 32), reduce
-// the sum of squares with shuffles (no block-wide barrier), release the buffer and write the modulated
-// BF16 row (or three planes). Stage s is always consumed by warp s % 5, so a warp's wait on a stage's
-// parity can never see a later round.
-constexpr int kStreamConsumers = 5;
-constexpr int kStreamStages = 2 * kStreamConsumers;
-constexpr int kStreamWidth = 4096;
-constexpr int kStreamRowBytes = kStreamWidth * 4;
-constexpr int kStreamThreads = 32 * (1 + kStreamConsumers);
-constexpr int kStreamVectorBytes = 3 * kStreamRowBytes; // gamma, scale, shift
-constexpr int kStreamSmemBytes = kStreamStages * kStreamRowBytes + kStreamVectorBytes + 2 * kStreamStages * 8 + 128;
-constexpr int kErrNormTimeout = 31;
-
-__device__ __forceinline__ void bulk_row_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
-__global__ void __launch_bounds__(kStreamThreads, 1)
-    rms_modulate_stream_kernel(const float *__restrict__ x, int rows, const float *__restrict__ gamma,
-                               const float *__restrict__ scale, const float *__restrict__ shift, float eps,
-                               __nv_bfloat16 *out, int split3_out, int *error_flag)
-{
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t base = (raw + 127u) & ~127u;
-    uint8_t *base_ptr = smem_raw + (base - raw);
-    float4 *vec = reinterpret_cast<float4 *>(base_ptr + kStreamStages * kStreamRowBytes); // [3][1024]
-    const uint32_t bars = base + kStreamStages * kStreamRowBytes + kStreamVectorBytes;
-    auto full = [&](int st) { return bars + 8u * st; };
-    auto empty = [&](int st) { return bars + 8u * (kStreamStages + st); };
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int count = rows > static_cast<int>(blockIdx.x) ? (rows - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
-    if (threadIdx.x == 0)
-    {
-        for (int st = 0; st < kStreamStages; ++st)
-        {
-            mbar_init(full(st), 1);
-            mbar_init(empty(st), 1);
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-    if (warp == 0 && lane == 0)
-    {
-        // the row stream starts before the vectors are staged
-        for (int i = 0; i < count && i < kStreamStages; ++i)
-        {
-            mbar_arrive_expect_tx(full(i), kStreamRowBytes);
-            bulk_row_load(base + i * kStreamRowBytes, x + (blockIdx.x + static_cast<size_t>(i) * gridDim.x) * kStreamWidth,
-                          kStreamRowBytes, full(i));
-        }
-    }
-    // gamma (and scale, shift when present: 1 + scale and shift otherwise 1 and 0) into shared memory
-    for (int i = threadIdx.x; i < kStreamWidth / 4; i += kStreamThreads)
-    {
-        vec[i] = __ldg(reinterpret_cast<const float4 *>(gamma) + i);
-        vec[1024 + i] = scale ? __ldg(reinterpret_cast<const float4 *>(scale) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        vec[2048 + i] = shift ? __ldg(reinterpret_cast<const float4 *>(shift) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    __syncthreads();
-    if (warp == 0)
-    {
-        if (lane != 0) return;
-        int issued = count < kStreamStages ? count : kStreamStages;
-        for (; issued < count; ++issued)
-        {
-            const int st = issued % kStreamStages, round = issued / kStreamStages;
-            if (!mbar_wait(empty(st), (round - 1) & 1))
-            {
-                if (error_flag) atomicExch(error_flag, kErrNormTimeout);
-                break;
-            }
-            const size_t row = blockIdx.x + static_cast<size_t>(issued) * gridDim.x;
-            mbar_arrive_expect_tx(full(st), kStreamRowBytes);
-            bulk_row_load(base + st * kStreamRowBytes, x + row * kStreamWidth, kStreamRowBytes, full(st));
-        }
-        // the CTA must outlive every copy into its shared memory: wait for the last fill of each stage
-        for (int i = issued > kStreamStages ? issued - kStreamStages : 0; i < issued; ++i)
-            if (!mbar_wait(full(i % kStreamStages), (i / kStreamStages) & 1) && error_flag)
-                atomicExch(error_flag, kErrNormTimeout);
-        return;
-    }
-    const bool modulate = scale != nullptr;
-    const int consumer = warp - 1;
-    for (int i = consumer; i < count; i += kStreamConsumers)
-    {
-        const int st = i % kStreamStages;
-        if (!mbar_wait(full(st), (i / kStreamStages) & 1))
-        {
-            if (error_flag && lane == 0) atomicExch(error_flag, kErrNormTimeout);
-            break;
-        }
-        const float4 *src = reinterpret_cast<const float4 *>(base_ptr + st * kStreamRowBytes);
-        float4 v[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = src[lane + 32 * k];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty(st)); // the row is in registers: the stage may be refilled
-        float sq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-            sq[k & 3] += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
-        float total = (sq[0] + sq[1]) + (sq[2] + sq[3]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        const float inverse = 1.f / sqrtf(total / float(kStreamWidth) + eps);
-        const size_t row = blockIdx.x + static_cast<size_t>(i) * gridDim.x;
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-        {
-            const int c4 = lane + 32 * k, col = c4 * 4;
-            const float4 g = vec[c4];
-            float y[4] = {v[k].x * inverse * g.x, v[k].y * inverse * g.y, v[k].z * inverse * g.z,
-                          v[k].w * inverse * g.w};
-            if (modulate)
-            {
-                const float4 sc = vec[1024 + c4], sh = vec[2048 + c4];
-                y[0] = y[0] * (1.f + sc.x) + sh.x;
-                y[1] = y[1] * (1.f + sc.y) + sh.y;
-                y[2] = y[2] * (1.f + sc.z) + sh.z;
-                y[3] = y[3] * (1.f + sc.w) + sh.w;
-            }
-            if (!split3_out)
-            {
-                uint2 packed;
-                __nv_bfloat162 lo = __floats2bfloat162_rn(y[0], y[1]), hi = __floats2bfloat162_rn(y[2], y[3]);
-                packed.x = *reinterpret_cast<uint32_t *>(&lo);
-                packed.y = *reinterpret_cast<uint32_t *>(&hi);
-                *reinterpret_cast<uint2 *>(out + row * kStreamWidth + col) = packed;
-            }
-            else
-            {
-                __nv_bfloat16 *dst = out + row * (3 * kStreamWidth) + col;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) split3(y[j], dst[j], dst[kStreamWidth + j], dst[2 * kStreamWidth + j]);
-            }
-        }
-    }
-}
-
 int grid_for(long long count, int threads = 256)
 {
     long long blocks = (count + threads - 1) / threads;
@@ -465,26 +316,6 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
         else norm_modulate_kernel<3, false><<<grid, block, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
     }
     else return cudaErrorInvalidValue;
-    return cudaGetLastError();
-}
-
-int prepare_norm_kernels()
-{
-    return cudaFuncSetAttribute(rms_modulate_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kStreamSmemBytes);
-}
-
-int launch_rms_modulate_stream(const float *x, int rows, const float *gamma, const float *scale, const float *shift,
-                               float eps, __nv_bfloat16 *out, int split3_out, int num_sms, int *error_flag,
-                               cudaStream_t stream)
-{
-    if (rows < 1) return cudaSuccess;
-    if (!x || !out || !gamma || (scale == nullptr) != (shift == nullptr) || num_sms < 1 ||
-        (reinterpret_cast<uintptr_t>(x) & 15u))
-        return cudaErrorInvalidValue;
-    const int grid = rows < num_sms ? rows : num_sms;
-    rms_modulate_stream_kernel<<<grid, kStreamThreads, kStreamSmemBytes, stream>>>(x, rows, gamma, scale, shift, eps,
-                                                                                  out, split3_out, error_flag);
     return cudaGetLastError();
 }
 

@@ -102,14 +102,6 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
 int launch_norm_modulate(const float *x, int rows, int width, const float *gamma, const float *scale,
                          const float *shift, float eps, int centered, __nv_bfloat16 *out, int split3,
                          cudaStream_t stream);
-// RMSNorm + modulate over rows of 4096 (the DiT block's two norms), the same arithmetic as
-// launch_norm_modulate(centered = 0): persistent CTAs (grid = min(rows, num_sms)) stream rows through a
-// shared-memory ring by bulk copies. Bounded waits record status 31 in error_flag (may be null).
-// prepare_norm_kernels sets its shared-memory size (call once before any launch or stream capture).
-int prepare_norm_kernels();
-int launch_rms_modulate_stream(const float *x, int rows, const float *gamma, const float *scale, const float *shift,
-                               float eps, __nv_bfloat16 *out, int split3, int num_sms, int *error_flag,
-                               cudaStream_t stream);
 // Channel-major latent [128][tokens] -> token-major BF16 A operand [tokens][128] (or 3 planes).
 int launch_latent_to_tokens(const float *latent, int tokens, __nv_bfloat16 *out, int split3, cudaStream_t stream,
                             int ld = 0);
