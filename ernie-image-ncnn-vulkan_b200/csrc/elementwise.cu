@@ -10,6 +10,12 @@ namespace ernie_b200
 namespace
 {
 constexpr int kRowThreads = 256;
+// Threads per row of the 4096-wide RMSNorm + modulate (the DiT's two norms per block).
+#ifndef ERNIE_NORM_THREADS
+#define ERNIE_NORM_THREADS 256
+#endif
+constexpr int kNormThreads = ERNIE_NORM_THREADS;
+static_assert(kNormThreads >= 64 && kNormThreads <= 1024 && 1024 % kNormThreads == 0, "norm threads");
 
 __device__ __forceinline__ float block_sum(float value, float *scratch)
 {
@@ -33,21 +39,21 @@ __device__ __forceinline__ void split3(float x, __nv_bfloat16 &hi, __nv_bfloat16
     lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
 }
 
-// One CTA per row of `width` = 1024 * VEC floats. RMSNorm: x * (mean(x^2) + eps)^(-1/2) * gamma
+// One CTA per row of `width` = 4 * VEC * THREADS floats. RMSNorm: x * (mean(x^2) + eps)^(-1/2) * gamma
 // (block.ncnn.param rmsn_8 / rmsn_11); LayerNorm: (x - mean) / sqrt(var + eps) (output head ln_1).
 // Then y * (1 + scale) + shift (add_0/mul_1/add_2, add_17/mul_18/add_19), stored as BF16 or split-3.
-template <int VEC, bool CENTERED>
-__global__ void __launch_bounds__(kRowThreads) norm_modulate_kernel(const float *__restrict__ x, const float *gamma,
+template <int VEC, bool CENTERED, int THREADS = kRowThreads>
+__global__ void __launch_bounds__(THREADS) norm_modulate_kernel(const float *__restrict__ x, const float *gamma,
                                                                      const float *scale, const float *shift,
                                                                      float eps, __nv_bfloat16 *out, int split3_out)
 {
-    constexpr int width = 1024 * VEC;
+    constexpr int width = 4 * VEC * THREADS;
     __shared__ float scratch[32];
     const size_t row = blockIdx.x;
     const float4 *xr = reinterpret_cast<const float4 *>(x + row * width);
     float4 v[VEC];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) v[i] = xr[threadIdx.x + i * kRowThreads];
+    for (int i = 0; i < VEC; ++i) v[i] = xr[threadIdx.x + i * THREADS];
     float mean = 0.f;
     if (CENTERED)
     {
@@ -71,7 +77,7 @@ __global__ void __launch_bounds__(kRowThreads) norm_modulate_kernel(const float 
 #pragma unroll
     for (int i = 0; i < VEC; ++i)
     {
-        const int col = (threadIdx.x + i * kRowThreads) * 4;
+        const int col = (threadIdx.x + i * THREADS) * 4;
         float y[4] = {v[i].x * inverse, v[i].y * inverse, v[i].z * inverse, v[i].w * inverse};
         if (!CENTERED)
         {
@@ -308,7 +314,9 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
     if (width == 4096)
     {
         if (centered) norm_modulate_kernel<4, true><<<grid, block, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
-        else norm_modulate_kernel<4, false><<<grid, block, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
+        else
+            norm_modulate_kernel<1024 / kNormThreads, false, kNormThreads>
+                <<<grid, kNormThreads, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
     }
     else if (width == 3072)
     {
