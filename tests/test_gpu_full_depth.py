@@ -126,3 +126,26 @@ def test_c1_geometry_bf16_against_fp32_mode(deep):
     ok, metrics = gate(out[ec.FP32], out[ec.BF16], *GATES["pipeline_bf16"])
     print("C1 geometry, 36 blocks x 8 steps, BF16 vs FP32-exact", metrics)
     assert ok, metrics
+
+
+def test_c2_geometry_bf16_against_fp32_mode(deep):
+    """The headline configuration's geometry (64x64 packed latent + 64 text slots, 4160 tokens), all 36
+    blocks and 8 steps: BF16 mode against the FP32-exact mode (which passes the oracle's FP32 gates at this
+    block shape) within the BF16 pipeline gate, each mode repeating bit-exactly."""
+    ctx, model, _, _ = deep
+    w, h, text, valid = 64, 64, 64, 64
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    out = {}
+    for precision in (ec.FP32, ec.BF16):
+        s = ec.Session(model, w, h, text, valid, precision)
+        try:
+            s.set_conditioning(txt, cos, sin, mask)
+            first = s.denoise(latent, 8)
+            again = s.denoise(latent, 8)
+        finally:
+            s.close()
+        assert np.isfinite(first).all() and np.array_equal(first, again), "repeat execution must be bit-exact"
+        out[precision] = first
+    ok, metrics = gate(out[ec.FP32], out[ec.BF16], *GATES["pipeline_bf16"])
+    print("C2 geometry, 36 blocks x 8 steps, BF16 vs FP32-exact", metrics)
+    assert ok, metrics
