@@ -140,6 +140,11 @@ struct ernie_cuda_session
 namespace
 {
 constexpr int kMaxSteps = 1000;
+// Output columns per QKV GEMM tile (two heads); a compile-time knob for tile-shape sweeps.
+#ifndef ERNIE_QKV_BLOCK_N
+#define ERNIE_QKV_BLOCK_N 256
+#endif
+constexpr int kQkvBlockN = ERNIE_QKV_BLOCK_N;
 constexpr long long kPeerTimeoutNs = 20000000000LL; // a member more than 20 s behind counts as lost
 
 // The address of `local` (inside this GPU's peer-visible arena) in member p's arena.
@@ -1108,7 +1113,7 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.sin_t = s->sin_t;
     qkv.error_flag = s->ctx->error_flag;
     if (flags) qkv.sync = qkv_sync;
-    if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, 256, Epilogue::Qkv, qkv), "qkv");
+    if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, kQkvBlockN, Epilogue::Qkv, qkv), "qkv");
     else if (flags && T == 0) // no rows of its own: announce the (empty) QKV stores all the same
         ERNIE_LAUNCH(launch_peer_signal(qkv_sync.signal, st), "qkv signal");
     if (!on(2)) {}

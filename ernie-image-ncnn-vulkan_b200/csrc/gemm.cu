@@ -1121,7 +1121,12 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     }
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
     if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
-    if (use_pairs(m, n, splits, block_n, promote, num_sms) && epilogue != Epilogue::FinalEuler)
+#ifdef ERNIE_PAIRS_FOR_QKV // tile-shape sweep: CTA pairs for the QKV GEMM whatever its tile rounds
+    const bool pairs_forced = epilogue == Epilogue::Qkv && block_n == 256 && !promote && splits == 1;
+#else
+    const bool pairs_forced = false;
+#endif
+    if ((pairs_forced || use_pairs(m, n, splits, block_n, promote, num_sms)) && epilogue != Epilogue::FinalEuler)
     {
         switch (epilogue)
         {
