@@ -1121,8 +1121,9 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     }
     if (epilogue == Epilogue::Geglu && n != 2 * args.ffn) return cudaErrorInvalidValue;
     if (promote) return dispatch<128, true>(epilogue, a, b, m, n, k_b, splits, args, num_sms, stream);
-#ifdef ERNIE_PAIRS_FOR_QKV // tile-shape sweep: CTA pairs for the QKV GEMM whatever its tile rounds
-    const bool pairs_forced = epilogue == Epilogue::Qkv && block_n == 256 && !promote && splits == 1;
+#ifdef ERNIE_PAIRS_FOR // tile-shape sweep: CTA pairs whatever the tile rounds, for epilogues in this bit mask
+    const bool pairs_forced = ((ERNIE_PAIRS_FOR >> static_cast<int>(epilogue)) & 1) && block_n == 256 && !promote &&
+                              splits == 1;
 #else
     const bool pairs_forced = false;
 #endif
