@@ -1077,15 +1077,20 @@ cudaError_t prepare_pairs()
 }
 
 // Measured on B200 (C2 shapes, power-capped clocks): a pair tile takes as long per 128 rows as a
-// single-CTA tile, and pairs gain only on the long-K, narrow-N projections (out, down: 3-5%). They
-// are used when they need no more rounds of tiles over the SMs than single CTAs do; otherwise the
-// coarser 256-row quantisation loses (up/gate: 23 rounds instead of 22 at 4160 rows).
-bool use_pairs(int m, int n, int splits, int block_n, bool promote, int num_sms)
+// single-CTA tile for the plain epilogues, and pairs gain only on the long-K, narrow-N projections (out,
+// down: 3-5%). They are used when they need no more rounds of tiles over the SMs than single CTAs do;
+// otherwise the coarser 256-row quantisation loses (up/gate: 23 rounds instead of 22 at 4160 rows, 3-4%
+// slower measured). The QKV GEMM is the exception: its pair rounds run ~13% faster than its single-CTA
+// rounds (C2: 0.32-0.35 against 0.36-0.39 ms with 12 pair rounds against 11; C3: 0.48-0.50 against
+// 0.50-0.58 ms), so it takes pairs unless they need more than 1/0.87 times the rounds (the 1040-row
+// shards of 8-GPU sequence parallelism: 4 pair rounds against 3).
+bool use_pairs(int m, int n, int splits, int block_n, bool promote, int num_sms, Epilogue epilogue)
 {
     if (promote || splits != 1 || block_n != 256 || num_sms < 2) return false;
     const long long tiles1 = static_cast<long long>((m + BM - 1) / BM) * (n / block_n);
     const long long tiles2 = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * (n / block_n);
     const long long rounds1 = (tiles1 + num_sms - 1) / num_sms, rounds2 = (tiles2 + num_sms / 2 - 1) / (num_sms / 2);
+    if (epilogue == Epilogue::Qkv) return rounds2 * 87 <= rounds1 * 100;
     return rounds2 <= rounds1;
 }
 } // namespace
@@ -1127,7 +1132,7 @@ int launch_gemm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
 #else
     const bool pairs_forced = false;
 #endif
-    if ((pairs_forced || use_pairs(m, n, splits, block_n, promote, num_sms)) && epilogue != Epilogue::FinalEuler)
+    if ((pairs_forced || use_pairs(m, n, splits, block_n, promote, num_sms, epilogue)) && epilogue != Epilogue::FinalEuler)
     {
         switch (epilogue)
         {
