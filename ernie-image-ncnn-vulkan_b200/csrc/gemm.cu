@@ -27,11 +27,6 @@ namespace ernie_b200
 namespace
 {
 constexpr int BM = 128, BK = 64, kThreads = 192;
-// 64-row last row blocks on M = 64 MMAs (a compile-time knob so that sweeps can compare against 128-row ones)
-#ifndef ERNIE_HALF_TAIL
-#define ERNIE_HALF_TAIL 1
-#endif
-constexpr bool kHalfTail = ERNIE_HALF_TAIL != 0;
 
 template <int BN, bool PROMOTE> struct Cfg
 {
@@ -100,12 +95,9 @@ struct EpiCtx
     uint32_t taddr; // TMEM address of the accumulator (this warp's lane quarter, column 0)
     int row0;       // first output row of this warp
     int lane;
-    int m;          // rows of the output
+    int m;          // valid rows
     int n_blk;
     uint8_t *stage; // this warp's staging tile
-    int rows = 32;  // lanes of this warp holding its rows: 32, or 16 in a 64-row tile (lanes 0..15)
-    // rows this warp may store: row0 .. row_end - 1
-    __device__ __forceinline__ int row_end() const { return m < row0 + rows ? m : row0 + rows; }
 };
 
 __device__ __forceinline__ uint4 pack_bf16x8(const float *v)
@@ -123,7 +115,7 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float *v)
 template <int BN> __device__ __forceinline__ void epi_f32_bias(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
     const int row = e.row0 + e.lane, col0 = e.n_blk * BN;
-    const bool valid = row < e.row_end();
+    const bool valid = row < e.m;
     float *out = a.out + static_cast<size_t>(row) * a.ldo + col0;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32)
@@ -162,7 +154,7 @@ template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e
         for (int p = 0; p < 8; ++p)
         {
             const int row = e.row0 + p * 4 + (e.lane >> 3);
-            r[p] = row < e.row_end() ? *reinterpret_cast<const float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc)
+            r[p] = row < e.m ? *reinterpret_cast<const float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
@@ -174,7 +166,7 @@ template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e
             r[p].y += g.y * acc.y;
             r[p].z += g.z * acc.z;
             r[p].w += g.w * acc.w;
-            if (row < e.row_end())
+            if (row < e.m)
                 *reinterpret_cast<float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc) = r[p];
         }
         __syncwarp();
@@ -192,7 +184,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
     const int part = col0 / kHidden; // 0 = Q, 1 = K, 2 = V
     const int head0 = (col0 % kHidden) / kHeadDim;
     const int row = e.row0 + e.lane;
-    const bool valid = row < e.row_end();
+    const bool valid = row < e.m;
     const float4 *cs = reinterpret_cast<const float4 *>(a.cos_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
     const float4 *sn = reinterpret_cast<const float4 *>(a.sin_t + static_cast<size_t>(valid ? row : 0) * kHeadDim);
     const float4 *gamma = reinterpret_cast<const float4 *>(part == 0 ? a.gamma_q : a.gamma_k);
@@ -234,7 +226,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
                     // 8-row runs: row_limit and row_offset are multiples of 16, so a run is all in or all out
                     const int d = p * 8 + (e.lane >> 2), q4 = e.lane & 3;
                     const uint4 val = *reinterpret_cast<const uint4 *>(st + d * 40 + q4 * 8);
-                    if (q4 * 8 < e.rows && e.row0 + q4 * 8 < row_limit)
+                    if (e.row0 + q4 * 8 < row_limit)
                         *reinterpret_cast<uint4 *>(dst + (static_cast<size_t>(head) * kHeadDim + half * 64 + d) *
                                                              a.rows_pad +
                                                    a.row_offset + e.row0 + q4 * 8) = val;
@@ -313,7 +305,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
                 {
                     const int rr = p * 4 + (e.lane >> 3), j = e.lane & 7, row_g = e.row0 + rr;
                     const int dim = (j < 4 ? 0 : 64) + c * 32 + (j & 3) * 8;
-                    if (row_g < e.row_end() && row_g < row_limit)
+                    if (row_g < e.m && row_g < row_limit)
                         *reinterpret_cast<uint4 *>(dst + (dst_row + row_g) * kHeadDim + dim) =
                             *reinterpret_cast<const uint4 *>(st + rr * 72 + j * 8);
                 }
@@ -329,7 +321,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
 template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
     const int row = e.row0 + e.lane;
-    const bool valid = row < e.row_end();
+    const bool valid = row < e.m;
     __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage); // [32][40]
 #pragma unroll 1
     for (int g = 0; g < BN / 128; ++g)
@@ -388,7 +380,7 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
             for (int p = 0; p < 4; ++p)
             {
                 const int rr = p * 8 + (e.lane >> 2), q4 = e.lane & 3, row_g = e.row0 + rr;
-                if (row_g < e.row_end())
+                if (row_g < e.m)
                     *reinterpret_cast<uint4 *>(a.h + static_cast<size_t>(row_g) * a.ffn + f + q4 * 8) =
                         *reinterpret_cast<const uint4 *>(st + rr * 40 + q4 * 8);
             }
@@ -402,7 +394,7 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
 __device__ __forceinline__ void epi_final_euler(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
     const int row = e.row0 + e.lane;
-    const bool valid = row < e.row_end();
+    const bool valid = row < e.m;
     bool finite = true;
 #pragma unroll 1
     for (int c = 0; c < 128; c += 32)
@@ -443,23 +435,13 @@ __device__ __forceinline__ void run_epilogue(const EpiCtx &e, const GemmEpilogue
 // warps add each partial into FP32 registers, so no chain exceeds group*64 products.
 // Output tile t -> (m block, n block). Tiles run through the n blocks of a band of `band` m blocks (m
 // fastest inside the band), band after band, so that consecutive rounds of tiles over the SMs reuse
-// one band's A rows from L2 while B streams; band >= num_m is the plain m-fastest order. With `last_apart`
-// the last m block (a 64-row block run as M = 64 MMAs, half the work of a tile) comes after all the
-// others, so its half tiles fill the last round instead of lengthening a full one.
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int band, int &m_blk, int &n_blk,
-                                            bool last_apart = false)
+// one band's A rows from L2 while B streams; band >= num_m is the plain m-fastest order.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int band, int &m_blk, int &n_blk)
 {
-    const int body = last_apart ? num_m - 1 : num_m;
-    if (t >= body * num_n)
-    {
-        m_blk = num_m - 1;
-        n_blk = t - body * num_n;
-        return;
-    }
     const int per_band = band * num_n;
     const int b = t / per_band, r = t - b * per_band;
     const int first = b * band;
-    const int rows = min(band, body - first);
+    const int rows = min(band, num_m - first);
     m_blk = first + r % rows;
     n_blk = r / rows;
 }
@@ -487,9 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_m = (m + BM - 1) / BM, num_n = n / BN, tiles = num_m * num_n;
     const int k_blocks = (k_b * splits) / BK;
     const int span = PROMOTE ? group : k_blocks; // k-blocks per accumulation chain
-    // A last row block of at most 64 rows runs as M = 64 MMAs (half the tensor work); its accumulator
-    // rows 16q + i sit in TMEM lanes 32q + i (i < 16), so epilogue warp q stores 16 rows.
-    const bool half_tail = kHalfTail && !PROMOTE && m - (num_m - 1) * BM <= 64;
 
     if (threadIdx.x == 0)
     {
@@ -531,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
                 int m_blk, n_blk;
-                tile_coords(tile, num_m, num_n, band, m_blk, n_blk, half_tail);
+                tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
                 for (int kb = 0; kb < k_blocks; ++kb)
                 {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u))
@@ -558,16 +537,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
         if (lane == 0)
         {
-            constexpr uint32_t idesc_full = idesc_bf16(BM, BN), idesc_half = idesc_bf16(64, BN);
+            constexpr uint32_t idesc = idesc_bf16(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             int unit = 0;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
             {
-                int m_blk, n_blk;
-                tile_coords(tile, num_m, num_n, band, m_blk, n_blk, half_tail);
-                const uint32_t idesc = half_tail && m_blk == num_m - 1 ? idesc_half : idesc_full;
                 for (int kb0 = 0; kb0 < k_blocks && ok; kb0 += span, ++unit)
                 {
                     const int acc = unit & 1;
@@ -616,9 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x)
         {
             int m_blk, n_blk;
-            tile_coords(tile, num_m, num_n, band, m_blk, n_blk, half_tail);
-            const bool half = half_tail && m_blk == num_m - 1;
-            const int row0 = m_blk * BM + quarter * (half ? 16 : 32);
+            tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
+            const int row0 = m_blk * BM + quarter * 32;
             uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
             if constexpr (!PROMOTE)
             {
@@ -630,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage, half ? 16 : 32}, args);
+                run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty_bar(acc));
