@@ -27,6 +27,12 @@ namespace ernie_b200
 namespace
 {
 constexpr int BM = 128, BK = 64, kThreads = 192;
+// Pair GEMMs split the tiles of a last round that would occupy at most half the pairs (a compile-time
+// knob so that sweeps can compare against whole tiles).
+#ifndef ERNIE_SPLIT_LAST_ROUND
+#define ERNIE_SPLIT_LAST_ROUND 1
+#endif
+constexpr bool kSplitLastRound = ERNIE_SPLIT_LAST_ROUND != 0;
 
 template <int BN, bool PROMOTE> struct Cfg
 {
@@ -686,7 +692,7 @@ template <int BN> struct PairCfg
 template <int BN, Epilogue EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, int m,
-                     int n, int k_b, int band, GemmEpilogueArgs args)
+                     int n, int k_b, int band, int split_from, GemmEpilogueArgs args)
 {
     using C = PairCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -709,6 +715,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int num_m = (m + 2 * BM - 1) / (2 * BM), num_n = n / BN, tiles = num_m * num_n;
     const int k_blocks = k_b / BK;
+    // Work units: tiles [0, split_from) whole; each tile of the last, partial round (from split_from on)
+    // as two BN/2-column halves, so that round spreads over up to twice as many pairs.
+    const bool splitting = BN == 256 && split_from >= 0 && split_from < tiles;
+    const int units = splitting ? split_from + 2 * (tiles - split_from) : tiles;
+    // unit -> (m block, n block, half: -1 whole tile, 0/1 the left/right BN/2 columns)
+    auto unit_coords = [&](int u, int &m_blk, int &n_blk, int &half) {
+        half = -1;
+        int t = u;
+        if (splitting && u >= split_from)
+        {
+            t = split_from + (u - split_from) / 2;
+            half = (u - split_from) & 1;
+        }
+        tile_coords(t, num_m, num_n, band, m_blk, n_blk);
+    };
 
     if (threadIdx.x == 0)
     {
@@ -747,10 +768,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             bool ok = true;
             peer_wait_all(args.sync.wait); // sequence parallel: every member's rows of A have landed
-            for (int tile = pair; tile < tiles && ok; tile += pairs)
+            for (int tile = pair; tile < units && ok; tile += pairs)
             {
-                int m_blk, n_blk;
-                tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
+                int m_blk, n_blk, half;
+                unit_coords(tile, m_blk, n_blk, half);
+                // a half tile's B rows: BN/4 per CTA at n_blk*BN + half*BN/2 (the box loads BN/2, the MMA
+                // reads the first BN/4)
+                const int b_row = half < 0 ? n_blk * BN + static_cast<int>(rank) * (BN / 2)
+                                           : n_blk * BN + half * (BN / 2) + static_cast<int>(rank) * (BN / 4);
                 for (int kb = 0; kb < k_blocks; ++kb)
                 {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u))
@@ -763,8 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
                     const uint32_t bar = mapa_shared(full_bar(stage), 0);
                     tma_load_2d_pair(tile_a(stage), &map_a, bar, kb * BK, m_blk * 2 * BM + static_cast<int>(rank) * BM);
-                    tma_load_2d_pair(tile_b(stage), &map_b, bar, kb * BK,
-                                     n_blk * BN + static_cast<int>(rank) * (BN / 2));
+                    tma_load_2d_pair(tile_b(stage), &map_b, bar, kb * BK, b_row);
                     if (++stage == C::kStages)
                     {
                         stage = 0;
@@ -793,13 +817,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
         if (lane == 0 && leader)
         {
-            constexpr uint32_t idesc = idesc_bf16(2 * BM, BN);
+            constexpr uint32_t idesc_whole = idesc_bf16(2 * BM, BN), idesc_half = idesc_bf16(2 * BM, BN / 2);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             int unit = 0;
-            for (int tile = pair; tile < tiles && ok; tile += pairs, ++unit)
+            for (int tile = pair; tile < units && ok; tile += pairs, ++unit)
             {
+                int m_blk, n_blk, half;
+                unit_coords(tile, m_blk, n_blk, half);
+                const uint32_t idesc = half < 0 ? idesc_whole : idesc_half;
                 const int acc = unit & 1;
                 const uint32_t acc_phase = (unit >> 1) & 1;
                 if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u))
@@ -845,10 +872,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
         const uint32_t leader_tempty0 = mapa_shared(tempty_bar(0), 0), leader_tempty1 = mapa_shared(tempty_bar(1), 0);
         int unit = 0;
-        for (int tile = pair; tile < tiles; tile += pairs, ++unit)
+        for (int tile = pair; tile < units; tile += pairs, ++unit)
         {
-            int m_blk, n_blk;
-            tile_coords(tile, num_m, num_n, band, m_blk, n_blk);
+            int m_blk, n_blk, half;
+            unit_coords(tile, m_blk, n_blk, half);
             const int row0 = m_blk * 2 * BM + static_cast<int>(rank) * BM + quarter * 32;
             uint8_t *stage = base_ptr + C::kStagingOffset + quarter * C::kStagingBytes;
             const int acc = unit & 1;
@@ -859,7 +886,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
+            if constexpr (BN == 256)
+            {
+                if (half >= 0)
+                    run_epilogue<BN / 2, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, 2 * n_blk + half, stage}, args);
+                else
+                    run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
+            }
+            else
+                run_epilogue<BN, EPI>(EpiCtx{lane_base + acc * BN, row0, lane, m, n_blk, stage}, args);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
@@ -999,9 +1034,12 @@ int launch_pair(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
     const int band = tile_band((m + 2 * BM - 1) / (2 * BM), 2 * BM, k_b);
+    // a last, partial round of at most half the pairs runs as twice as many half-width tiles
+    const int rest = tiles % pairs;
+    const int split_from = kSplitLastRound && BN == 256 && rest > 0 && 2 * rest <= pairs ? tiles - rest : -1;
     GemmEpilogueArgs launch_args = args;
     launch_args.sync.signal.warps = 2 * pairs * 4; // four epilogue warps per CTA
-    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, band, launch_args);
+    return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EPI>, map_a, map_b, m, n, k_b, band, split_from, launch_args);
 }
 
 template <int BN, Epilogue EPI, bool PROMOTE>
