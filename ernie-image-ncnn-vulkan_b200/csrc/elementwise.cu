@@ -15,6 +15,11 @@ constexpr int kRowThreads = 256;
 #define ERNIE_NORM_THREADS 256
 #endif
 constexpr int kNormThreads = ERNIE_NORM_THREADS;
+// Rows per CTA of that norm (1: the one-row kernel; 2 or 4: rms_rows_kernel), a launch-shape knob.
+#ifndef ERNIE_NORM_ROWS
+#define ERNIE_NORM_ROWS 1
+#endif
+constexpr int kNormRows = ERNIE_NORM_ROWS;
 static_assert(kNormThreads >= 64 && kNormThreads <= 1024 && 1024 % kNormThreads == 0, "norm threads");
 
 __device__ __forceinline__ float block_sum(float value, float *scratch)
@@ -107,6 +112,90 @@ __global__ void __launch_bounds__(THREADS) norm_modulate_kernel(const float *__r
             __nv_bfloat16 *dst = out + row * (3 * width) + col;
 #pragma unroll
             for (int j = 0; j < 4; ++j) split3(y[j], dst[j], dst[width + j], dst[2 * width + j]);
+        }
+    }
+}
+
+// RMSNorm + modulate of ROWS rows per CTA (a launch-shape variant of norm_modulate_kernel<VEC, false>:
+// every thread keeps ROWS x VEC float4 loads in flight and the rows share one pair of block barriers).
+template <int VEC, int THREADS, int ROWS>
+__global__ void __launch_bounds__(THREADS) rms_rows_kernel(const float *__restrict__ x, int rows, const float *gamma,
+                                                           const float *scale, const float *shift, float eps,
+                                                           __nv_bfloat16 *out, int split3_out)
+{
+    constexpr int width = 4 * VEC * THREADS, warps = THREADS / 32;
+    __shared__ float scratch[warps][ROWS];
+    const int row0 = blockIdx.x * ROWS;
+    float4 v[ROWS][VEC];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+    {
+        const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row0 + r) * width);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i)
+            v[r][i] = row0 + r < rows ? xr[threadIdx.x + i * THREADS] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float sq[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+    {
+        sq[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i)
+            sq[r] += (v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y) + (v[r][i].z * v[r][i].z + v[r][i].w * v[r][i].w);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq[r] += __shfl_xor_sync(0xffffffffu, sq[r], o);
+    }
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) scratch[warp][r] = sq[r];
+    __syncthreads();
+    float inverse[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+    {
+        float total = 0.f;
+        for (int w = 0; w < warps; ++w) total += scratch[w][r];
+        inverse[r] = 1.f / sqrtf(total / float(width) + eps);
+    }
+#pragma unroll
+    for (int i = 0; i < VEC; ++i)
+    {
+        const int col = (threadIdx.x + i * THREADS) * 4;
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma + col));
+        float4 sc = make_float4(0.f, 0.f, 0.f, 0.f), sh = sc;
+        if (scale)
+        {
+            sc = __ldg(reinterpret_cast<const float4 *>(scale + col));
+            sh = __ldg(reinterpret_cast<const float4 *>(shift + col));
+        }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+        {
+            if (row0 + r >= rows) continue;
+            float y[4] = {v[r][i].x * inverse[r] * g.x, v[r][i].y * inverse[r] * g.y, v[r][i].z * inverse[r] * g.z,
+                          v[r][i].w * inverse[r] * g.w};
+            if (scale)
+            {
+                y[0] = y[0] * (1.f + sc.x) + sh.x;
+                y[1] = y[1] * (1.f + sc.y) + sh.y;
+                y[2] = y[2] * (1.f + sc.z) + sh.z;
+                y[3] = y[3] * (1.f + sc.w) + sh.w;
+            }
+            const size_t row = static_cast<size_t>(row0 + r);
+            if (!split3_out)
+            {
+                __nv_bfloat162 *dst = reinterpret_cast<__nv_bfloat162 *>(out + row * width + col);
+                dst[0] = __floats2bfloat162_rn(y[0], y[1]);
+                dst[1] = __floats2bfloat162_rn(y[2], y[3]);
+            }
+            else
+            {
+                __nv_bfloat16 *dst = out + row * (3 * width) + col;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) split3(y[j], dst[j], dst[width + j], dst[2 * width + j]);
+            }
         }
     }
 }
@@ -314,6 +403,10 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
     if (width == 4096)
     {
         if (centered) norm_modulate_kernel<4, true><<<grid, block, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
+        else if (kNormRows > 1)
+            rms_rows_kernel<1024 / kNormThreads, kNormThreads, kNormRows>
+                <<<(rows + kNormRows - 1) / kNormRows, kNormThreads, 0, stream>>>(x, rows, gamma, scale, shift, eps, out,
+                                                                             split3_out);
         else
             norm_modulate_kernel<1024 / kNormThreads, false, kNormThreads>
                 <<<grid, kNormThreads, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
