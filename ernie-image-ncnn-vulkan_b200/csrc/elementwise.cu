@@ -15,9 +15,11 @@ constexpr int kRowThreads = 256;
 #define ERNIE_NORM_THREADS 256
 #endif
 constexpr int kNormThreads = ERNIE_NORM_THREADS;
-// Rows per CTA of that norm (1: the one-row kernel; 2 or 4: rms_rows_kernel), a launch-shape knob.
+// Rows per CTA of that norm (1: the one-row kernel; 2 or 4: rms_rows_kernel), a launch-shape knob. Two
+// rows per CTA measured 0.0187-0.0188 ms per C2 launch against 0.0210-0.0214 for one (0.024-0.025 against
+// 0.027 inside the step); four were slower (0.022).
 #ifndef ERNIE_NORM_ROWS
-#define ERNIE_NORM_ROWS 1
+#define ERNIE_NORM_ROWS 2
 #endif
 constexpr int kNormRows = ERNIE_NORM_ROWS;
 static_assert(kNormThreads >= 64 && kNormThreads <= 1024 && 1024 % kNormThreads == 0, "norm threads");
