@@ -4,6 +4,7 @@
 // each element once with 16-byte vector accesses where the layout allows.
 #include "kernels.h"
 #include "ernie_synth.h"
+#include "ptx.cuh"
 
 namespace ernie_b200
 {
@@ -128,6 +129,8 @@ __global__ void __launch_bounds__(THREADS) rms_rows_kernel(const float *__restri
     constexpr int width = 4 * VEC * THREADS, warps = THREADS / 32;
     __shared__ float scratch[warps][ROWS];
     const int row0 = blockIdx.x * ROWS;
+    grid_dependency_wait(); // launched programmatically after the GEMM that wrote x
+    grid_dependents_launch();
     float4 v[ROWS][VEC];
 #pragma unroll
     for (int r = 0; r < ROWS; ++r)
@@ -406,9 +409,17 @@ int launch_norm_modulate(const float *x, int rows, int width, const float *gamma
     {
         if (centered) norm_modulate_kernel<4, true><<<grid, block, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);
         else if (kNormRows > 1)
-            rms_rows_kernel<1024 / kNormThreads, kNormThreads, kNormRows>
-                <<<(rows + kNormRows - 1) / kNormRows, kNormThreads, 0, stream>>>(x, rows, gamma, scale, shift, eps, out,
-                                                                             split3_out);
+        {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((rows + kNormRows - 1) / kNormRows);
+            cfg.blockDim = dim3(kNormThreads);
+            cfg.stream = stream;
+            cudaLaunchAttribute attrs[1];
+            cfg.attrs = attrs;
+            cfg.numAttrs = add_programmatic_attribute(attrs, 0);
+            return cudaLaunchKernelEx(&cfg, rms_rows_kernel<1024 / kNormThreads, kNormThreads, kNormRows>, x, rows, gamma,
+                                      scale, shift, eps, out, split3_out);
+        }
         else
             norm_modulate_kernel<1024 / kNormThreads, false, kNormThreads>
                 <<<grid, kNormThreads, 0, stream>>>(x, gamma, scale, shift, eps, out, split3_out);

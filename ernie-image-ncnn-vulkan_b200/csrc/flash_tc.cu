@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
+    grid_dependency_wait(); // the previous kernel's writes (Q, K, V^T, mask, peer flags) are visible from here
+    grid_dependents_launch();
     auto s_col = [](int g) { return static_cast<uint32_t>(g * 128); };
     auto o_col = [](int g) { return static_cast<uint32_t>(256 + g * 128); };
     // Each role ends the kernel on its own: the register split differs per warpgroup, so no code
@@ -520,8 +522,15 @@ int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_b
         a.sync = *sync;
         a.sync.signal.warps = static_cast<int>(grid.x * grid.y) * 8; // the eight softmax warps of each CTA
     }
-    flash_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[1];
+    cfg.attrs = attrs;
+    cfg.numAttrs = add_programmatic_attribute(attrs, 0);
+    return cudaLaunchKernelEx(&cfg, flash_tc_kernel, mq, mk, mv, a);
 }
 
 int launch_flash_tc(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *vt, const float *mask,

@@ -504,6 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
+    grid_dependency_wait(); // the previous kernel's writes (A, residual, peer flags) are visible from here
+    grid_dependents_launch();
 
     if (warp == 0)
     {
@@ -759,6 +761,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync(); // both CTAs' barriers are initialised before any remote arrive or TMA completion
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(base_ptr + (slot - base));
+    grid_dependency_wait(); // the previous kernel's writes (A, residual, peer flags) are visible from here
+    grid_dependents_launch();
 
     if (warp == 0)
     {
@@ -1026,13 +1030,13 @@ int launch_pair(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = PairCfg<BN>::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attrs[1];
+    cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
     attrs[0].val.clusterDim.x = 2;
     attrs[0].val.clusterDim.y = 1;
     attrs[0].val.clusterDim.z = 1;
     cfg.attrs = attrs;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = add_programmatic_attribute(attrs, 1);
     const int band = tile_band((m + 2 * BM - 1) / (2 * BM), 2 * BM, k_b);
     // a last, partial round of at most half the pairs runs as twice as many half-width tiles
     const int rest = tiles % pairs;
@@ -1061,9 +1065,16 @@ int launch_impl(const __nv_bfloat16 *a, const __nv_bfloat16 *b, int m, int n, in
     const int band = tile_band((m + BM - 1) / BM, BM, k_b * splits);
     GemmEpilogueArgs launch_args = args;
     launch_args.sync.signal.warps = grid * 4; // four epilogue warps per CTA
-    gemm_kernel<BN, EPI, PROMOTE><<<grid, kThreads, C::kSmemBytes, stream>>>(map_a, map_b, m, n, k_b, splits, group,
-                                                                             band, launch_args);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[1];
+    cfg.attrs = attrs;
+    cfg.numAttrs = add_programmatic_attribute(attrs, 0);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI, PROMOTE>, map_a, map_b, m, n, k_b, splits, group, band,
+                              launch_args);
 }
 
 template <int BN, bool PROMOTE>

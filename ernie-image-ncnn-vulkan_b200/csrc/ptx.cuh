@@ -67,6 +67,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
     return true;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization attribute may
+// start while the previous kernel of its stream is still running; grid_dependency_wait() returns once
+// that kernel has completed and its writes are visible (at once for a launch without the attribute),
+// so everything before it may touch only shared memory, TMEM and kernel parameters.
+// grid_dependents_launch() lets the next such kernel start its own set-up on SMs this grid frees
+// (ERNIE_PDL_TRIGGER=0 leaves it to each CTA's exit).
+#ifndef ERNIE_PDL_TRIGGER
+#define ERNIE_PDL_TRIGGER 1
+#endif
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch()
+{
+#if ERNIE_PDL_TRIGGER
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
