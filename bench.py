@@ -1029,6 +1029,10 @@ def main():
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
                            "step_frac_of_datasheet_bf16": step_tflops / DATASHEET_BF16_TFLOPS,
+                           "norms": "folded into the GEMMs after block 1 (the residual epilogues write bf16(x g) and "
+                                    "row sums of squares, the QKV / up-gate epilogues apply rinv and W shift)"
+                                    if args.precision == "bf16" and os.environ.get("ERNIE_FOLD_NORM", "0") == "1"
+                                    else "two norm kernels per block",
                            "kernel_ms": prof, "kernel_ms_in_block": in_block, "pipeline_stages": stages},
                 "roofline": {"bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": bf16_peak,
                              "unit": "TFLOP/s", "frac": achieved / bf16_peak, "peak_kind": peak_kind,

@@ -6,6 +6,7 @@
 #include "kernels.h"
 #include "capi_internal.h"
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <random>
@@ -135,6 +136,15 @@ struct ernie_cuda_session
     // arrival slots per member in the arena (QKV stores landed, attention rows landed) and this GPU's
     // counters: [0] QKV warps finished, [1] QKV epoch, [2] attention warps finished, [3] attention epoch.
     unsigned *arrive_qkv = nullptr, *arrive_att = nullptr, *sync_state = nullptr;
+    // RMSNorm + modulate folded into the GEMMs around it (BF16 blocks after the first): the folded operand
+    // bf16(x g), each row's sums of squares per 128-column part [kFoldParts][tokens], and per schedule the
+    // projections of every step's shift through every block's weights, [block][step][QKV 12288 | up/gate
+    // 24576] (W shift depends on the weights and the schedule's timesteps only).
+    bool fold = false;
+    __nv_bfloat16 *a2 = nullptr;
+    float *sumsq = nullptr, *fold_c = nullptr;
+    int fold_steps = 0;
+    std::tuple<int, int> fold_key{-1, -1};
 };
 
 namespace
@@ -811,6 +821,12 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
         s->latent_ld = s->image;
     }
     s->rows_pad = (s->tokens + 127) / 128 * 128;
+    // ERNIE_FOLD_NORM=1 folds the BF16 blocks' norms into the GEMMs around them. Off by default: on a
+    // power-capped B200 the extra epilogue work (QKV +4%, out +7%, up/gate +2%, down +2.5% per launch at C2)
+    // costs as much as the two norm launches it removes, and the C2 step measured 67.5-68.1 ms against
+    // 67.2-67.4 with the norm kernels (C4 156.1-157.1 against 154.9-156.1).
+    const char *fold_env = std::getenv("ERNIE_FOLD_NORM");
+    s->fold = precision == ERNIE_PRECISION_BF16 && fold_env && std::strcmp(fold_env, "1") == 0;
     // BF16 Q, K, V^T; FP32-exact mode: three BF16 planes of each
     const size_t T = s->tokens, P = s->rows_pad, qkv_elem = precision == ERNIE_PRECISION_FP32 ? 6 : 2;
     const size_t L = size_t(kLatent) * (world > 1 ? s->shard : s->image);
@@ -829,6 +845,11 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
     arena.add(&s->ss, 2 * kHidden);
     if (world == 1) arena.add(&s->a, T * kHidden * s->splits);
     arena.add(&s->h, T * kFfn * s->splits);
+    if (s->fold)
+    {
+        arena.add(&s->a2, T * kHidden);
+        arena.add(&s->sumsq, size_t(kFoldParts) * T);
+    }
     if (world == 1) // sequence parallel: Q, K, V^T land in the peer-visible arena below
     {
         arena.add(reinterpret_cast<char **>(&s->q), size_t(kHeads) * P * kHeadDim * qkv_elem);
@@ -962,6 +983,7 @@ extern "C" int ernie_cuda_session_destroy(ernie_cuda_session *s)
     if (s->features) cudaFree(s->features);
     if (s->flags) cudaFree(s->flags);
     if (s->preds) cudaFree(s->preds);
+    if (s->fold_c) cudaFree(s->fold_c);
     if (s->pinned) cudaFreeHost(s->pinned);
     delete s;
     return ERNIE_CUDA_OK;
@@ -1055,7 +1077,11 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
 // One DiT block on x [tokens][4096] (block.ncnn.param:14-76), 7 launches.
 // `only` >= 0 enqueues just that part (0 norm sa, 1 QKV GEMM, 2 attention, 3 out-proj GEMM, 4 norm mlp,
 // 5 up/gate GEMM, 6 down GEMM); used by the benchmark's per-kernel timing.
-static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mod, int only = -1)
+// fold_c (a folding session's W shift of block b at this step: QKV 12288 then up/gate 24576 values) folds
+// the two norms into the GEMMs: block b > 0 takes its QKV operand from block b-1's down projection, the
+// out projection writes the up/gate operand, and the down projection writes block b+1's QKV operand.
+static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mod, int only = -1,
+                         const float *fold_c = nullptr)
 {
     // T = real rows of this session's token range; a sequence-parallel rank with none still joins
     // both all-to-alls and computes its heads' attention for every token.
@@ -1067,7 +1093,9 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     const bool fp32 = s->precision == ERNIE_PRECISION_FP32;
     const float *shift_sa = mod, *scale_sa = mod + kHidden, *gate_sa = mod + 2 * kHidden;
     const float *shift_mlp = mod + 3 * kHidden, *scale_mlp = mod + 4 * kHidden, *gate_mlp = mod + 5 * kHidden;
-    if (on(0))
+    const bool fold = fold_c != nullptr && s->fold;
+    const bool folded_in = fold && b > 0; // block b-1's down projection wrote this block's QKV operand
+    if (on(0) && !folded_in)
         ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_sa, scale_sa, shift_sa, 1e-6f, 0, s->a, fp32, st), "norm sa");
     // A whole block of a sequence-parallel member synchronises through flags carried by its kernels: the
     // QKV GEMM's last warp announces that its heads have landed, the attention waits for every member's
@@ -1113,7 +1141,15 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     qkv.sin_t = s->sin_t;
     qkv.error_flag = s->ctx->error_flag;
     if (flags) qkv.sync = qkv_sync;
-    if (on(1)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wqkv, T, 3 * kHidden, kHidden, kQkvBlockN, Epilogue::Qkv, qkv), "qkv");
+    if (folded_in)
+    {
+        qkv.fold_bias = fold_c;
+        qkv.fold_sumsq = s->sumsq;
+        qkv.fold_ld = s->tokens;
+    }
+    if (on(1))
+        ERNIE_LAUNCH(session_gemm(s, folded_in ? s->a2 : s->a, w.wqkv, T, 3 * kHidden, kHidden, kQkvBlockN, Epilogue::Qkv, qkv),
+                     "qkv");
     else if (flags && T == 0) // no rows of its own: announce the (empty) QKV stores all the same
         ERNIE_LAUNCH(launch_peer_signal(qkv_sync.signal, st), "qkv signal");
     if (!on(2)) {}
@@ -1150,24 +1186,53 @@ static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mo
     res.gate = gate_sa;
     res.error_flag = s->ctx->error_flag;
     if (flags) res.sync = out_sync;
+    if (fold) // the out projection also writes the up/gate GEMM's folded operand
+    {
+        res.fold_out = s->a2;
+        res.fold_gamma = w.gamma_mlp;
+        res.fold_scale = scale_mlp;
+        res.fold_sumsq = s->sumsq;
+        res.fold_ld = s->tokens;
+    }
     if (on(3)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wo, T, kHidden, kHidden, 256, Epilogue::ResidGate, res), "out proj");
     res.sync = PeerSync();
-    if (on(4))
+    if (on(4) && !fold)
         ERNIE_LAUNCH(launch_norm_modulate(x, T, kHidden, w.gamma_mlp, scale_mlp, shift_mlp, 1e-6f, 0, s->a, fp32, st), "norm mlp");
     GemmEpilogueArgs gg;
     gg.h = s->h;
     gg.h_split3 = fp32;
     gg.ffn = kFfn;
     gg.error_flag = s->ctx->error_flag;
-    if (on(5)) ERNIE_LAUNCH(session_gemm(s, s->a, w.wug, T, 2 * kFfn, kHidden, 256, Epilogue::Geglu, gg), "up/gate");
+    if (fold)
+    {
+        gg.fold_bias = fold_c + 3 * kHidden;
+        gg.fold_sumsq = s->sumsq;
+        gg.fold_ld = s->tokens;
+    }
+    if (on(5)) ERNIE_LAUNCH(session_gemm(s, fold ? s->a2 : s->a, w.wug, T, 2 * kFfn, kHidden, 256, Epilogue::Geglu, gg), "up/gate");
     res.gate = gate_mlp;
+    // the down projection writes the next block's folded QKV operand (its gamma_sa, this step's scale_sa)
+    res.fold_out = nullptr;
+    if (fold && b + 1 < s->model->num_blocks)
+    {
+        res.fold_out = s->a2;
+        res.fold_gamma = s->model->blocks[b + 1].gamma_sa;
+        res.fold_scale = scale_sa;
+    }
     if (on(6)) ERNIE_LAUNCH(session_gemm(s, s->h, w.wfc2, T, kHidden, kFfn, 256, Epilogue::ResidGate, res), "down");
     return ERNIE_CUDA_OK;
 }
 
+// W shift of block b at step `step` of the schedule whose features are loaded (null: no folding).
+static const float *fold_bias_for(const ernie_cuda_session *s, int b, int step)
+{
+    if (!s->fold || !s->fold_c || step < 0 || step >= s->fold_steps || s->fold_key != s->feature_key) return nullptr;
+    return s->fold_c + (size_t(b) * s->fold_steps + step) * (9 * kHidden);
+}
+
 // Input head + 36 blocks + output head + Euler for one step (run_dit + euler_step).
 static int enqueue_step(ernie_cuda_session *s, float *latent, const float *features, float delta, float *prediction,
-                        int *finite_flag, bool with_blocks = true)
+                        int *finite_flag, bool with_blocks = true, int step = -1)
 {
     const DevHeads &hd = s->model->heads;
     cudaStream_t st = s->ctx->stream;
@@ -1199,7 +1264,8 @@ static int enqueue_step(ernie_cuda_session *s, float *latent, const float *featu
     ERNIE_LAUNCH(launch_gemv(hd.adaln_w, s->c, hd.adaln_b, s->mod, 6 * kHidden, kHidden, 1, st), "adaLN");
     ERNIE_LAUNCH(launch_gemv(hd.final_norm_w, s->c, hd.final_norm_b, s->ss, 2 * kHidden, kHidden, 0, st), "final norm linear");
     if (with_blocks)
-        for (int b = 0; b < s->model->num_blocks; ++b) ERNIE_TRY(enqueue_block(s, b, s->x, s->mod));
+        for (int b = 0; b < s->model->num_blocks; ++b)
+            ERNIE_TRY(enqueue_block(s, b, s->x, s->mod, -1, fold_bias_for(s, b, step)));
     // output head: LayerNorm + modulate on image rows, linear + bias, fused Euler update
     if (img > 0)
     {
@@ -1229,7 +1295,69 @@ extern "C" int ernie_cuda_session_blocks(ernie_cuda_session *s, int first, int c
     return ERNIE_CUDA_OK;
 }
 
-static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, bool predictions)
+// The folded norms' W shift for every block and step of the loaded schedule, once per schedule: each
+// step's time MLP + adaLN give its shift_sa and shift_mlp, which go through every block's QKV and up/gate
+// weights as exact three-plane BF16 operands (GEMMs of M = steps rows into fold_c).
+static int ensure_fold_cache(ernie_cuda_session *s, int steps)
+{
+    if (!s->fold || (s->fold_key == s->feature_key && s->fold_steps == steps)) return ERNIE_CUDA_OK;
+    const int nb = s->model->num_blocks;
+    const DevHeads &hd = s->model->heads;
+    cudaStream_t st = s->ctx->stream;
+    s->fold_key = {-1, -1};
+    if (s->fold_steps != steps)
+    {
+        if (s->fold_c) cudaFree(s->fold_c);
+        s->fold_c = nullptr;
+        s->fold_steps = 0;
+        ERNIE_CUDA(cudaMalloc(&s->fold_c, size_t(nb) * steps * 9 * kHidden * 4), "Allocate folded shifts");
+        s->fold_steps = steps;
+        release_graphs(s);
+    }
+    const size_t mod_n = size_t(steps) * 6 * kHidden, row_n = size_t(steps) * kHidden;
+    void *staging = nullptr;
+    ERNIE_CUDA(cudaMalloc(&staging, (mod_n + 2 * row_n) * 4 + 2 * 3 * row_n * 2), "Allocate fold staging");
+    float *mods = static_cast<float *>(staging), *rows_sa = mods + mod_n, *rows_mlp = rows_sa + row_n;
+    __nv_bfloat16 *op_sa = reinterpret_cast<__nv_bfloat16 *>(rows_mlp + row_n), *op_mlp = op_sa + 3 * row_n;
+    int rc = ERNIE_CUDA_OK;
+    auto run = [&](int code, const char *what) {
+        if (rc == ERNIE_CUDA_OK && code != 0) rc = from_launch(code, what);
+    };
+    for (int i = 0; i < steps; ++i)
+    {
+        run(launch_gemv(hd.time1_w, s->features + size_t(i) * kHidden, hd.time1_b, s->g1, kHidden, kHidden, 0, st), "time linear_1");
+        run(launch_gemv(hd.time2_w, s->g1, hd.time2_b, s->c, kHidden, kHidden, 1, st), "time linear_2");
+        run(launch_gemv(hd.adaln_w, s->c, hd.adaln_b, mods + size_t(i) * 6 * kHidden, 6 * kHidden, kHidden, 1, st), "adaLN");
+    }
+    run(cudaMemcpy2DAsync(rows_sa, kHidden * 4, mods, 6 * kHidden * 4, kHidden * 4, steps, cudaMemcpyDeviceToDevice, st),
+        "shift_sa rows");
+    run(cudaMemcpy2DAsync(rows_mlp, kHidden * 4, mods + 3 * kHidden, 6 * kHidden * 4, kHidden * 4, steps,
+                          cudaMemcpyDeviceToDevice, st),
+        "shift_mlp rows");
+    run(launch_to_operand(rows_sa, steps, kHidden, op_sa, 1, st), "shift_sa operand");
+    run(launch_to_operand(rows_mlp, steps, kHidden, op_mlp, 1, st), "shift_mlp operand");
+    for (int b = 0; b < nb; ++b)
+    {
+        const DevBlock &w = s->model->blocks[b];
+        GemmEpilogueArgs out;
+        out.out = s->fold_c + size_t(b) * steps * 9 * kHidden;
+        out.ldo = 9 * kHidden;
+        out.error_flag = s->ctx->error_flag;
+        run(launch_gemm(op_sa, w.wqkv, steps, 3 * kHidden, kHidden, 3, 256, Epilogue::F32Bias, out, s->ctx->num_sms, st),
+            "W shift (QKV)");
+        out.out += 3 * kHidden;
+        run(launch_gemm(op_mlp, w.wug, steps, 2 * kFfn, kHidden, 3, 256, Epilogue::F32Bias, out, s->ctx->num_sms, st),
+            "W shift (up/gate)");
+    }
+    const cudaError_t done = cudaStreamSynchronize(st);
+    cudaFree(staging);
+    ERNIE_TRY(rc);
+    ERNIE_CUDA(done, "Folded shifts");
+    s->fold_key = s->feature_key;
+    return ERNIE_CUDA_OK;
+}
+
+static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, bool predictions, bool fold_cache = true)
 {
     if (s->feature_capacity < steps)
     {
@@ -1266,7 +1394,7 @@ static int ensure_step_buffers(ernie_cuda_session *s, int steps, int schedule, b
         ERNIE_CUDA(cudaMemcpy(s->features, features.data(), features.size() * 4, cudaMemcpyHostToDevice), "upload features");
         s->feature_key = {steps, schedule};
     }
-    return ERNIE_CUDA_OK;
+    return fold_cache ? ensure_fold_cache(s, steps) : ERNIE_CUDA_OK;
 }
 
 static int enqueue_range(ernie_cuda_session *s, int start, int end, bool predictions)
@@ -1276,7 +1404,7 @@ static int enqueue_range(ernie_cuda_session *s, int start, int end, bool predict
     for (int i = start; i < end; ++i)
     {
         float *pred = predictions ? s->preds + size_t(i) * kLatent * s->latent_ld : nullptr;
-        ERNIE_TRY(enqueue_step(s, s->latent, s->features + size_t(i) * kHidden, s->deltas[i], pred, s->flags + i));
+        ERNIE_TRY(enqueue_step(s, s->latent, s->features + size_t(i) * kHidden, s->deltas[i], pred, s->flags + i, true, i));
     }
     return ERNIE_CUDA_OK;
 }
@@ -1442,7 +1570,7 @@ extern "C" int ernie_cuda_session_dit(ernie_cuda_session *s, const float *latent
     DeviceGuard guard(s->ctx->device);
     std::vector<float> features(kHidden);
     ERNIE_TRY(host_features(timestep, features.data()));
-    ERNIE_TRY(ensure_step_buffers(s, 1, ERNIE_SCHEDULE_TURBO, false));
+    ERNIE_TRY(ensure_step_buffers(s, 1, ERNIE_SCHEDULE_TURBO, false, false)); // any t: the norm kernels run
     cudaStream_t st = s->ctx->stream;
     s->feature_key = {-1, -1}; // features[0] is overwritten below
     ERNIE_CUDA(cudaMemcpyAsync(s->features, features.data(), kHidden * 4, cudaMemcpyHostToDevice, st), "features");
@@ -1466,10 +1594,10 @@ extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int
     if (kernel == 17)
     {
         // whole blocks enqueued part by part (sequence parallel: barrier kernels between the exchanges)
-        for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, p)); // warm-up block
+        for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, p, fold_bias_for(s, nb - 1, 0)));
         ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
         for (int i = 0; i < iters; ++i)
-            for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p));
+            for (int p = 0; p < 7; ++p) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p, fold_bias_for(s, i % nb, 0)));
         ERNIE_CUDA(cudaEventRecord(ctx->events[15], ctx->stream), "event");
         ERNIE_CUDA(cudaEventSynchronize(ctx->events[15]), "event");
         float total = 0.f;
@@ -1481,12 +1609,12 @@ extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int
     {
         // one part inside whole blocks: events around it in each of up to 7 consecutive blocks
         const int part = kernel - 10, n = iters < 7 ? iters : 7;
-        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod)); // warm-up block
+        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, -1, fold_bias_for(s, nb - 1, 0))); // warm-up block
         for (int i = 0; i < n; ++i)
             for (int p = 0; p < 7; ++p)
             {
                 if (p == part) ERNIE_CUDA(cudaEventRecord(ctx->events[2 * i], ctx->stream), "event");
-                ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p));
+                ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, p, fold_bias_for(s, i % nb, 0)));
                 if (p == part) ERNIE_CUDA(cudaEventRecord(ctx->events[2 * i + 1], ctx->stream), "event");
             }
         ERNIE_CUDA(cudaEventSynchronize(ctx->events[2 * n - 1]), "event");
@@ -1504,17 +1632,21 @@ extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int
     {
         if (s->feature_capacity < 1 || s->deltas.empty()) return fail(ERNIE_CUDA_ERROR, "Run a denoise step first");
         const bool blocks = kernel == 8; // 9: the heads of a step without its blocks
-        ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks));
+        ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks, 0));
         ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
         for (int i = 0; i < iters; ++i)
-            ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks));
+            ERNIE_TRY(enqueue_step(s, s->scratch_latent, s->features, 0.f, nullptr, s->flags, blocks, 0));
     }
     else
     {
+        // one kernel alone (0..6) or a whole block (7); the norms (0, 4) are timed as their kernel, which a
+        // folding session runs only in its first block
         const int only = kernel == 7 ? -1 : kernel;
-        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, only)); // warm-up launch
+        const bool norm = kernel == 0 || kernel == 4;
+        ERNIE_TRY(enqueue_block(s, nb - 1, s->x, s->mod, only, norm ? nullptr : fold_bias_for(s, nb - 1, 0)));
         ERNIE_CUDA(cudaEventRecord(ctx->events[14], ctx->stream), "event");
-        for (int i = 0; i < iters; ++i) ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, only));
+        for (int i = 0; i < iters; ++i)
+            ERNIE_TRY(enqueue_block(s, i % nb, s->x, s->mod, only, norm ? nullptr : fold_bias_for(s, i % nb, 0)));
     }
     ERNIE_CUDA(cudaEventRecord(ctx->events[15], ctx->stream), "event");
     ERNIE_CUDA(cudaEventSynchronize(ctx->events[15]), "event");
@@ -1527,17 +1659,17 @@ extern "C" int ernie_cuda_session_profile(ernie_cuda_session *s, int kernel, int
 extern "C" int ernie_cuda_session_launches_per_step(ernie_cuda_session *s, int *launches)
 {
     if (!s || !launches) return fail(ERNIE_CUDA_ERROR, "null argument");
-    // input head: latent transpose + x_embedder GEMM + 4 GEMVs; 7 per block; output head: norm + GEMM.
-    // Sequence parallel: + two peer barriers per block; a member without image rows skips the latent
-    // transpose, x_embedder and output head, one without real rows everything but the attention and its
-    // barriers.
+    // input head: latent transpose + x_embedder GEMM + 4 GEMVs; per block norm, QKV, attention, out
+    // projection, norm, up/gate, down, where a folding session runs the two norms only in its first block;
+    // output head: norm + GEMM. Sequence parallel (whole blocks synchronise through the kernels' completion
+    // flags): a member without image rows skips the latent transpose, x_embedder and output head, one
+    // without real rows runs only the attention and the signal kernel that stands in for its QKV GEMM.
+    const int nb = s->model->num_blocks;
+    const int blocks = s->fold ? 5 * nb + 1 : 7 * nb;
     if (s->sp_world > 1)
-    {
-        const int per_block = s->real_local > 0 ? 9 : 3;
-        *launches = 4 + per_block * s->model->num_blocks + (s->img_local > 0 ? 4 : 0);
-    }
+        *launches = 4 + (s->real_local > 0 ? blocks : 2 * nb) + (s->img_local > 0 ? 4 : 0);
     else
-        *launches = 6 + 7 * s->model->num_blocks + 2;
+        *launches = 6 + blocks + 2;
     return ERNIE_CUDA_OK;
 }
 

@@ -139,11 +139,38 @@ template <int BN> __device__ __forceinline__ void epi_f32_bias(const EpiCtx &e, 
     }
 }
 
+// ---- the norm folded into the GEMMs (BF16 DiT blocks) ---------------------------------------------
+// rinv of `row` from its kFoldParts sums of squares, added in part order.
+__device__ __forceinline__ float fold_rinv(const GemmEpilogueArgs &a, int row)
+{
+    float total = 0.f;
+#pragma unroll 8
+    for (int p = 0; p < kFoldParts; ++p) total += __ldg(a.fold_sumsq + static_cast<size_t>(p) * a.fold_ld + row);
+    return 1.f / sqrtf(total / 4096.f + 1e-6f);
+}
+
+// v[j] = rinv * v[j] + bias[col + j] for the 32 accumulator columns starting at col.
+__device__ __forceinline__ void fold_apply(float (&v)[32], const float *bias, int col, float rinv)
+{
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+    {
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + col + j));
+        v[j] = fmaf(rinv, v[j], b.x);
+        v[j + 1] = fmaf(rinv, v[j + 1], b.y);
+        v[j + 2] = fmaf(rinv, v[j + 2], b.z);
+        v[j + 3] = fmaf(rinv, v[j + 3], b.w);
+    }
+}
+
 // gemm_3 / gemm_6 + mul_15 / mul_21 + add_16 / add_22: resid += gate * acc, FP32, coalesced rows.
+// With fold_out, also the next norm's folded operand and the row sums of squares per 128-column part.
 template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e, const GemmEpilogueArgs &a)
 {
     float *st = reinterpret_cast<float *>(e.stage); // [32][36]
     const int col0 = e.n_blk * BN, cc = (e.lane & 7) * 4;
+    const bool fold = a.fold_out != nullptr;
+    float squares[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}; // rows p * 4 + lane / 8 of this part
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32)
     {
@@ -176,6 +203,45 @@ template <int BN> __device__ __forceinline__ void epi_resid_gate(const EpiCtx &e
                 *reinterpret_cast<float4 *>(a.resid + static_cast<size_t>(row) * a.ldo + col0 + c + cc) = r[p];
         }
         __syncwarp();
+        if (fold)
+        {
+            const int col = col0 + c + cc;
+            const float4 gm = __ldg(reinterpret_cast<const float4 *>(a.fold_gamma + col));
+            const float4 sc = __ldg(reinterpret_cast<const float4 *>(a.fold_scale + col));
+            const float4 k = make_float4(gm.x * (1.f + sc.x), gm.y * (1.f + sc.y), gm.z * (1.f + sc.z), gm.w * (1.f + sc.w));
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+            {
+                const int row = e.row0 + p * 4 + (e.lane >> 3);
+                squares[p] += (r[p].x * r[p].x + r[p].y * r[p].y) + (r[p].z * r[p].z + r[p].w * r[p].w);
+                if (row < e.m)
+                {
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(r[p].x * k.x, r[p].y * k.y);
+                    __nv_bfloat162 hi = __floats2bfloat162_rn(r[p].z * k.z, r[p].w * k.w);
+                    uint2 packed;
+                    packed.x = *reinterpret_cast<uint32_t *>(&lo);
+                    packed.y = *reinterpret_cast<uint32_t *>(&hi);
+                    *reinterpret_cast<uint2 *>(a.fold_out + static_cast<size_t>(row) * kHidden + col) = packed;
+                }
+            }
+            if ((c + 32) % 128 == 0)
+            {
+                // the part's 128 columns are done: add the 8 lanes of each row (butterfly), lane 0 of the
+                // eight stores the row's sum
+                const int part = (col0 + c) / 128;
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+                {
+                    float s = squares[p];
+                    s += __shfl_xor_sync(0xffffffffu, s, 1);
+                    s += __shfl_xor_sync(0xffffffffu, s, 2);
+                    s += __shfl_xor_sync(0xffffffffu, s, 4);
+                    const int row = e.row0 + p * 4 + (e.lane >> 3);
+                    if ((e.lane & 7) == 0 && row < e.m) a.fold_sumsq[static_cast<size_t>(part) * a.fold_ld + row] = s;
+                    squares[p] = 0.f;
+                }
+            }
+        }
     }
 }
 
@@ -196,6 +262,9 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
     const float4 *gamma = reinterpret_cast<const float4 *>(part == 0 ? a.gamma_q : a.gamma_k);
     const int row_limit = a.row_limit > 0 ? a.row_limit : a.rows_pad;
     __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage);
+    // folded norm: the projection of this row is rinv * acc + W shift
+    const bool fold = a.fold_bias != nullptr;
+    const float rinv = fold && valid ? fold_rinv(a, row) : 1.f;
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh)
     {
@@ -221,6 +290,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
                 {
                     float chunk[32];
                     tmem_load_32(tcol + half * 64 + c * 32, chunk);
+                    if (fold) fold_apply(chunk, a.fold_bias, col0 + hh * 128 + half * 64 + c * 32, rinv);
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         st[(c * 32 + j) * 40 + e.lane] = __float2bfloat16_rn(planes == 3 ? split_plane(chunk[j], plane) : chunk[j]);
@@ -251,6 +321,7 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
             {
                 float chunk[32];
                 tmem_load_32(tcol + c * 32, chunk);
+                if (fold) fold_apply(chunk, a.fold_bias, col0 + hh * 128 + c * 32, rinv);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) squared += chunk[j] * chunk[j];
             }
@@ -264,6 +335,11 @@ template <int BN> __device__ __forceinline__ void epi_qkv(const EpiCtx &e, const
             float lo[32], hi[32];
             tmem_load_32(tcol + c * 32, lo);
             tmem_load_32(tcol + 64 + c * 32, hi);
+            if (fold)
+            {
+                fold_apply(lo, a.fold_bias, col0 + hh * 128 + c * 32, rinv);
+                fold_apply(hi, a.fold_bias, col0 + hh * 128 + 64 + c * 32, rinv);
+            }
             if (part < 2)
             {
 #pragma unroll
@@ -329,6 +405,8 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
     const int row = e.row0 + e.lane;
     const bool valid = row < e.m;
     __nv_bfloat16 *st = reinterpret_cast<__nv_bfloat16 *>(e.stage); // [32][40]
+    const bool fold = a.fold_bias != nullptr; // folded norm: rinv * acc + W shift
+    const float rinv = fold && valid ? fold_rinv(a, row) : 1.f;
 #pragma unroll 1
     for (int g = 0; g < BN / 128; ++g)
     {
@@ -338,6 +416,11 @@ template <int BN> __device__ __forceinline__ void epi_geglu(const EpiCtx &e, con
             float up[32], gate[32];
             tmem_load_32(e.taddr + g * 128 + c, up);
             tmem_load_32(e.taddr + g * 128 + 64 + c, gate);
+            if (fold)
+            {
+                fold_apply(up, a.fold_bias, e.n_blk * BN + g * 128 + c, rinv);
+                fold_apply(gate, a.fold_bias, e.n_blk * BN + g * 128 + 64 + c, rinv);
+            }
             const int f = e.n_blk * (BN / 2) + g * 64 + c;
             if (a.silu) // SwiGLU (MistralMLP: silu(gate) * up)
             {

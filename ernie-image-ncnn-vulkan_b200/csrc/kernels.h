@@ -103,10 +103,22 @@ struct GemmEpilogueArgs
     float *prediction = nullptr; // optional [128][rows]
     float delta = 0.f;
     int *finite_flag = nullptr; // set to 1 if any updated latent value is not finite
+    // RMSNorm + modulate folded into the GEMMs around it (BF16 DiT blocks), with x' the FP32 residual row
+    // and g = gamma * (1 + scale): norm(x') g + shift = rinv (x' g) + shift, rinv = (sum x'^2 / 4096 + 1e-6)^(-1/2).
+    // Producer (ResidGate with fold_out): also writes bf16(x' g) to fold_out (row stride kHidden) and the
+    // sum of x'^2 over each 128-column part p of the row to fold_sumsq[p * fold_ld + row].
+    // Consumer (Qkv, Geglu with fold_bias): A holds bf16(x' g); each accumulator becomes
+    // rinv * acc + fold_bias[col] (fold_bias = W shift), rinv from the row's kFoldParts sums.
+    __nv_bfloat16 *fold_out = nullptr;
+    const float *fold_gamma = nullptr, *fold_scale = nullptr;
+    float *fold_sumsq = nullptr;
+    int fold_ld = 0;
+    const float *fold_bias = nullptr;
     // all
     int *error_flag = nullptr;
     PeerSync sync; // sequence parallel: wait before the first A/B load, signal after the last store
 };
+constexpr int kFoldParts = kHidden / 128; // 128-column parts of a folded row's sum of squares
 
 // C[M, N] = A[M, K_a] * B[N, K_b]^T with BF16 operands and FP32 accumulation on tcgen05.
 // K_a = splits * K_b: in FP32-exact mode A holds `splits` BF16 planes (hi, mid, lo) side by side

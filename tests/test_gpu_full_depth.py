@@ -149,3 +149,32 @@ def test_c2_geometry_bf16_against_fp32_mode(deep):
     ok, metrics = gate(out[ec.FP32], out[ec.BF16], *GATES["pipeline_bf16"])
     print("C2 geometry, 36 blocks x 8 steps, BF16 vs FP32-exact", metrics)
     assert ok, metrics
+
+
+def test_c1_step_folded_norm_against_unfolded(deep, oracle_c1_step, monkeypatch):
+    """ERNIE_FOLD_NORM=1 folds each BF16 block's two RMSNorm + modulate passes into the GEMMs around them
+    (the residual GEMMs write bf16(x g) and each row's sums of squares, the next GEMM applies rinv and
+    W shift); the default keeps the norm kernels. One C1 step through 36 blocks in both forms against the oracle:
+    the folded form within the pipeline gate and no further from the oracle than the norm-kernel form
+    allows for one BF16 rounding of its own."""
+    ctx, model, _, _ = deep
+    w, h, text, valid = C1
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    ref_latent, ref_preds = oracle_c1_step
+    out = {}
+    for fold in ("1", "0"):
+        monkeypatch.setenv("ERNIE_FOLD_NORM", fold)
+        s = ec.Session(model, w, h, text, valid, ec.BF16)
+        try:
+            s.set_conditioning(txt, cos, sin, mask)
+            got, preds = s.denoise(latent, 8, 0, 1, keep_predictions=True)
+            again, _ = s.denoise(latent, 8, 0, 1, keep_predictions=True)
+        finally:
+            s.close()
+        assert np.array_equal(got, again), "repeat execution must be bit-exact"
+        out[fold] = gate(ref_preds[0], preds[0], *GATES["pipeline_bf16"])
+    (ok_f, m_f), (ok_u, m_u) = out["1"], out["0"]
+    print(f"C1 step 0 prediction vs oracle: folded nrmse={m_f['nrmse']:.3e} max_abs={m_f['max_abs_error']:.3e}; "
+          f"norm kernels nrmse={m_u['nrmse']:.3e} max_abs={m_u['max_abs_error']:.3e}")
+    assert ok_f and ok_u, (m_f, m_u)
+    assert m_f["nrmse"] <= 1.25 * m_u["nrmse"], (m_f, m_u)
