@@ -48,6 +48,11 @@ constexpr int kHalfBytes = kTile * 64 * 2;   // one 64-column half of a 128 x 12
 constexpr int kTileBytes = 2 * kHalfBytes;   // 32 KB
 constexpr int kSmemBytes = 7 * kTileBytes + 1024 + 256; // Q_A, Q_B, P_A, P_B, 2 K, 1 V^T
 constexpr int kTmemCols = 512;               // S_A 0, S_B 128, O_A 256, O_B 384
+// One-tile CTAs after all two-tile ones (a launch-order knob; 0 keeps the plain head-major order).
+#ifndef ERNIE_FLASH_SHORT_LAST
+#define ERNIE_FLASH_SHORT_LAST 1
+#endif
+constexpr bool kShortLast = ERNIE_FLASH_SHORT_LAST != 0;
 
 enum FlashError : int
 {
@@ -119,7 +124,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_done = bars + 8u * 15;
     const uint32_t slot = bars + 8u * 16;
 
-    const int head = blockIdx.y, q0 = blockIdx.x * kRowsPerCta, kv_head = head / a.kv_group;
+    // CTA -> (head, query block). Non-causal: when the last query block of each head holds a single tile,
+    // those short CTAs take the highest linear indices, after every two-tile CTA, so the grid's final wave
+    // can consist of short CTAs only (C4: 1024 two-tile CTAs, then 32 one-tile ones). Rows are computed
+    // the same way whichever CTA holds them.
+    int head = blockIdx.y, qb = blockIdx.x;
+    if (kShortLast && !a.causal && gridDim.x > 1 && (gridDim.x - 1) * kRowsPerCta + kTile >= a.rows)
+    {
+        const int full = gridDim.x - 1, linear = blockIdx.x + gridDim.x * blockIdx.y, two_tile = full * gridDim.y;
+        head = linear < two_tile ? linear / full : linear - two_tile;
+        qb = linear < two_tile ? linear % full : full;
+    }
+    const int q0 = qb * kRowsPerCta, kv_head = head / a.kv_group;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int kv_tiles = (a.kv_len + kTile - 1) / kTile;
     // causal: no key past this CTA's last query row
