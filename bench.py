@@ -920,7 +920,10 @@ def main():
     text = rng.standard_normal((TEXT, 3072), dtype=np.float32)
     cos, sin, mask = ec.dit_constants(WIDTH, HEIGHT, VALID, TEXT)
     session.set_conditioning(text, cos, sin, mask)
-    flops = step_flops(tokens, n_valid, args.blocks) / (world if sp else 1)  # per GPU
+    # one GPU computes the image rows and the text rows up to the last visible key (later text slots are
+    # masked keys no image row reads); the FLOPs below are those of the rows computed
+    rows_computed = tokens if sp or os.environ.get("ERNIE_ALL_ROWS") == "1" else n_valid
+    flops = step_flops(rows_computed, n_valid, args.blocks) / (world if sp else 1)  # per GPU
     launches_per_step = session.launches_per_step()
 
     # warm-up: graph capture of every step index, then W steps
@@ -1026,6 +1029,7 @@ def main():
                                        ("one request split over the GPUs" if sp else "one seed per GPU"),
                            "global_batch": 1 if sp else world, "seq_len": tokens,
                            "parallelism": f"sp{world}" if sp else f"dp{world}", "rows_per_gpu": T,
+                           "rows_computed": rows_computed,
                            "l2": "inputs larger than L2 (15.7 GB of weights streamed per step)",
                            "step_tflops": step_tflops, "step_frac_of_bf16_peak": step_tflops / bf16_peak,
                            "step_frac_of_datasheet_bf16": step_tflops / DATASHEET_BF16_TFLOPS,

@@ -5,6 +5,7 @@
 #include "ernie_synth.h"
 #include "kernels.h"
 #include "capi_internal.h"
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -119,6 +120,11 @@ struct ernie_cuda_session
     // Rows of this session's token range (the whole sequence unless sequence-parallel): image rows,
     // real (unpadded) rows, first text slot, and the latent's channel stride.
     int img_local = 0, real_local = 0, text_begin = 0, latent_ld = 0;
+    // Rows the denoise computes (one GPU): the image rows and every text row up to the last visible key.
+    // Later text slots are masked keys whose own rows no image row reads, so the step skips them; the
+    // block-level entry points compute every row. ERNIE_ALL_ROWS=1 computes them in the step as well.
+    int live_rows = 0;
+    bool all_rows = false;
     // Ulysses sequence parallelism (world 1 = one GPU): this rank owns tokens [rank*S, rank*S + S).
     int sp_world = 1, sp_rank = 0, full_tokens = 0, shard = 0, full_rows = 0, heads_local = kHeads;
     bool connected = false;
@@ -825,6 +831,8 @@ static int create_session(ernie_cuda_model *model, const ernie_cuda_shape *shape
     // power-capped B200 the extra epilogue work (QKV +4%, out +7%, up/gate +2%, down +2.5% per launch at C2)
     // costs as much as the two norm launches it removes, and the C2 step measured 67.5-68.1 ms against
     // 67.2-67.4 with the norm kernels (C4 156.1-157.1 against 154.9-156.1).
+    const char *rows_env = std::getenv("ERNIE_ALL_ROWS");
+    s->all_rows = rows_env && std::strcmp(rows_env, "1") == 0;
     const char *fold_env = std::getenv("ERNIE_FOLD_NORM");
     s->fold = precision == ERNIE_PRECISION_BF16 && fold_env && std::strcmp(fold_env, "1") == 0;
     // BF16 Q, K, V^T; FP32-exact mode: three BF16 planes of each
@@ -1013,6 +1021,22 @@ static int session_gemm(ernie_cuda_session *s, const __nv_bfloat16 *a, const __n
                        s->ctx->stream, fp32);
 }
 
+// V^T columns of the rows a step does not compute (live_rows..rows_pad) are zeroed: the attention's last
+// key tile reads them with zero weights, which must not meet a non-finite value left by an earlier call.
+static int clear_dead_rows(ernie_cuda_session *s)
+{
+    if (s->sp_world > 1 || s->live_rows >= s->rows_pad) return ERNIE_CUDA_OK;
+    const size_t planes = s->splits, width = size_t(s->rows_pad - s->live_rows) * sizeof(__nv_bfloat16);
+    for (size_t p = 0; p < planes; ++p)
+    {
+        auto *vt = static_cast<__nv_bfloat16 *>(s->v) + p * size_t(kHeads) * kHeadDim * s->rows_pad + s->live_rows;
+        ERNIE_CUDA(cudaMemset2DAsync(vt, size_t(s->rows_pad) * sizeof(__nv_bfloat16), 0, width, size_t(kHeads) * kHeadDim,
+                                     s->ctx->stream),
+                   "clear V rows");
+    }
+    return ERNIE_CUDA_OK;
+}
+
 extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const float *text, const float *cos_table,
                                                    const float *sin_table, const float *mask)
 {
@@ -1037,6 +1061,8 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
                              s->has_text == (text != nullptr);
     s->kv_len = last + 1;
     s->use_mask = general;
+    s->live_rows = s->sp_world > 1 || s->all_rows ? s->real_local : std::min(s->tokens, std::max(s->kv_len, s->image));
+    ERNIE_TRY(clear_dead_rows(s));
     // cos/sin rows of this session's token range (rows past the sequence stay zero)
     const size_t first = size_t(s->sp_rank) * s->tokens, rows = s->real_local;
     ERNIE_CUDA(cudaMemsetAsync(s->cos_t, 0, size_t(s->tokens) * kHeadDim * 4, st), "clear cos");
@@ -1081,11 +1107,12 @@ extern "C" int ernie_cuda_session_set_conditioning(ernie_cuda_session *s, const 
 // the two norms into the GEMMs: block b > 0 takes its QKV operand from block b-1's down projection, the
 // out projection writes the up/gate operand, and the down projection writes block b+1's QKV operand.
 static int enqueue_block(ernie_cuda_session *s, int b, float *x, const float *mod, int only = -1,
-                         const float *fold_c = nullptr)
+                         const float *fold_c = nullptr, int rows = -1)
 {
-    // T = real rows of this session's token range; a sequence-parallel rank with none still joins
-    // both all-to-alls and computes its heads' attention for every token.
-    const int T = s->real_local;
+    // T = the rows computed: by default the step's live rows, `rows` when given (the block-level entry
+    // points pass every real row). A sequence-parallel rank with none still joins both exchanges and
+    // computes its heads' attention for every token.
+    const int T = rows >= 0 ? rows : s->live_rows;
     const bool seq_parallel = s->sp_world > 1;
     auto on = [only, T](int part) { return (only < 0 || only == part) && (T > 0 || part == 2); };
     const DevBlock &w = s->model->blocks[b];
@@ -1291,8 +1318,8 @@ extern "C" int ernie_cuda_session_blocks(ernie_cuda_session *s, int first, int c
     if (!s->conditioned) return fail(ERNIE_CUDA_ERROR, "Session needs its nine constants (set_conditioning)");
     if (first < 0 || count < 1 || first + count > s->model->num_blocks) return fail(ERNIE_CUDA_ERROR, "Require 1..36 blocks");
     DeviceGuard guard(s->ctx->device);
-    for (int b = first; b < first + count; ++b) ERNIE_TRY(enqueue_block(s, b, x, modulation));
-    return ERNIE_CUDA_OK;
+    for (int b = first; b < first + count; ++b) ERNIE_TRY(enqueue_block(s, b, x, modulation, -1, nullptr, s->real_local));
+    return clear_dead_rows(s); // every row was computed here; the denoise steps compute only the live ones
 }
 
 // The folded norms' W shift for every block and step of the loaded schedule, once per schedule: each

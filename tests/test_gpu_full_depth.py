@@ -178,3 +178,33 @@ def test_c1_step_folded_norm_against_unfolded(deep, oracle_c1_step, monkeypatch)
           f"norm kernels nrmse={m_u['nrmse']:.3e} max_abs={m_u['max_abs_error']:.3e}")
     assert ok_f and ok_u, (m_f, m_u)
     assert m_f["nrmse"] <= 1.25 * m_u["nrmse"], (m_f, m_u)
+
+
+@pytest.mark.parametrize("shape", [(32, 32, 32, 24), (86, 48, 2048, 1080)], ids=["c1_padded", "c3"])
+@pytest.mark.parametrize("precision", [ec.FP32, ec.BF16], ids=["fp32", "bf16"])
+def test_denoise_skips_rows_past_the_last_visible_key(deep, monkeypatch, shape, precision):
+    """The denoise computes the image rows and the text rows up to the last visible key only: later text
+    slots are masked keys whose own rows no image row reads (C3: 968 of 6176 rows). ERNIE_ALL_ROWS=1
+    computes every row; the latents must be identical bit for bit, and a block-level call in between (which
+    computes and stores every row) must not change the next denoise."""
+    ctx, model, host_blocks, _ = deep
+    w, h, text, valid = shape
+    latent, txt, cos, sin, mask = case(w, h, text, valid)
+    steps = (0, 2) if w * h <= 1024 else (0, 1)
+    out = {}
+    for all_rows in ("1", "0"):
+        monkeypatch.setenv("ERNIE_ALL_ROWS", all_rows)
+        s = ec.Session(model, w, h, text, valid, precision)
+        try:
+            s.set_conditioning(txt, cos, sin, mask)
+            out[all_rows] = s.denoise(latent, 8, *steps)
+            if all_rows == "0":
+                n = w * h + text
+                x = o.synth_normal(SEED, o.HIDDEN_STREAM, n * 4096).reshape(n, 4096)
+                s.blocks(x, o.block_modulation(SEED), first=0, count=1)
+                again = s.denoise(latent, 8, *steps)
+                assert np.array_equal(out["0"], again), "a block-level call changed the next denoise"
+        finally:
+            s.close()
+    assert np.isfinite(out["0"]).all()
+    assert np.array_equal(out["0"], out["1"]), np.abs(out["0"] - out["1"]).max()
