@@ -2,6 +2,9 @@
 one in-tree shared library (so the built file travels with the source tree to the GPU box).
 
     python ernie-image-ncnn-vulkan_b200/build.py [--force]
+
+ERNIE_NVCC_FLAGS adds nvcc options, e.g. the kernels' compile-time launch-shape knobs for an A/B build:
+    ERNIE_NVCC_FLAGS="-DERNIE_FLASH_SHORT_LAST=0" python ernie-image-ncnn-vulkan_b200/build.py --force
 """
 import concurrent.futures
 import os
@@ -18,7 +21,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 INCLUDES = ["-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
-                     "-Xcompiler", "-fPIC,-ffp-contract=off"] + INCLUDES
+                     "-Xcompiler", "-fPIC,-ffp-contract=off"] + INCLUDES + os.environ.get("ERNIE_NVCC_FLAGS", "").split()
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-ffp-contract=off"] + INCLUDES + ["-I/usr/local/cuda/include"]
 
 
