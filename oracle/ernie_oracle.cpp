@@ -202,51 +202,103 @@ void orc_residual_add(const float *a, const float *b, float *out, int64_t count)
 // ErnieSDPA CPU path (ncnn SDPA with the row mask expanded, src/ernie_attention.cpp:196-221):
 // softmax(q k^T / sqrt(width) + mask) v, non-causal. Accumulation in FP64 as the reference's own
 // oracle does (tests/test_attention_mask.cpp:75-97, probes/attention_accuracy_probe.cpp:40-56).
+// K and V are widened to FP64 once; each dot product and each output row sums 4-lane FP64 vectors.
+typedef double v4d __attribute__((vector_size(32)));
+
+static inline v4d load4d(const double *p)
+{
+    v4d r;
+    std::memcpy(&r, p, sizeof(r));
+    return r;
+}
+
 void orc_sdpa(const float *q, const float *k, const float *v, const float *mask, int heads, int kv_heads,
               int mask_heads, int mask_rows, int nq, int nk, int width, float *out)
 {
     const double scale = 1.0 / std::sqrt(double(width));
+    const int wp = (width + 3) & ~3; // FP64 rows padded to whole vectors (zeros)
+    const int kv_count = kv_heads == 1 ? 1 : heads;
+    std::vector<double> kd(size_t(kv_count) * nk * wp, 0.0), vd(size_t(kv_count) * nk * wp, 0.0);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < int64_t(kv_count) * nk; ++r)
+        for (int d = 0; d < width; ++d)
+        {
+            kd[size_t(r) * wp + d] = k[size_t(r) * width + d];
+            vd[size_t(r) * wp + d] = v[size_t(r) * width + d];
+        }
+    // blocks of QB query rows share each pass over K and V (per row the arithmetic is the same)
+    constexpr int QB = 16;
+    const int qblocks = (nq + QB - 1) / QB;
 #pragma omp parallel
     {
-        std::vector<double> scores(nk), acc(width);
-#pragma omp for schedule(dynamic, 4) collapse(2)
+        std::vector<double> scores(size_t(QB) * nk), qd(size_t(QB) * wp, 0.0), acc(size_t(QB) * wp);
+        double maximum[QB], total[QB];
+#pragma omp for schedule(dynamic, 1) collapse(2)
         for (int h = 0; h < heads; ++h)
-            for (int i = 0; i < nq; ++i)
+            for (int b = 0; b < qblocks; ++b)
             {
-                const float *qi = q + (size_t(h) * nq + i) * width;
-                const int kh = kv_heads == 1 ? 0 : h;
-                const float *kh_base = k + size_t(kh) * nk * width;
-                const float *vh_base = v + size_t(kh) * nk * width;
-                const float *m = mask ? mask + (size_t(mask_heads == 1 ? 0 : h) * mask_rows +
-                                                (mask_rows == 1 ? 0 : i)) * nk
-                                      : nullptr;
-                double maximum = -1e300;
-                for (int j = 0; j < nk; ++j)
+                const int i0 = b * QB, rows = std::min(QB, nq - i0);
+                for (int r = 0; r < rows; ++r)
                 {
-                    const float *kj = kh_base + size_t(j) * width;
-                    double dot = 0;
-                    for (int d = 0; d < width; ++d) dot += double(qi[d]) * kj[d];
-                    double s = dot * scale;
-                    if (m) s += m[j];
-                    scores[j] = s;
-                    maximum = std::max(maximum, s);
+                    const float *qi = q + (size_t(h) * nq + i0 + r) * width;
+                    for (int d = 0; d < width; ++d) qd[size_t(r) * wp + d] = qi[d];
+                    maximum[r] = -1e300;
                 }
-                double total = 0;
+                const int kh = kv_heads == 1 ? 0 : h;
+                const double *kh_base = kd.data() + size_t(kh) * nk * wp;
+                const double *vh_base = vd.data() + size_t(kh) * nk * wp;
+                auto mask_row = [&](int i) -> const float * {
+                    return mask ? mask + (size_t(mask_heads == 1 ? 0 : h) * mask_rows + (mask_rows == 1 ? 0 : i)) * nk
+                                : nullptr;
+                };
                 for (int j = 0; j < nk; ++j)
                 {
-                    scores[j] = std::exp(scores[j] - maximum);
-                    total += scores[j];
+                    const double *kj = kh_base + size_t(j) * wp;
+                    for (int r = 0; r < rows; ++r)
+                    {
+                        const double *qr = qd.data() + size_t(r) * wp;
+                        v4d sum = {0, 0, 0, 0};
+                        for (int d = 0; d < wp; d += 4) sum += load4d(qr + d) * load4d(kj + d);
+                        double s = ((sum[0] + sum[2]) + (sum[1] + sum[3])) * scale;
+                        const float *m = mask_row(i0 + r);
+                        if (m) s += m[j];
+                        scores[size_t(r) * nk + j] = s;
+                        maximum[r] = std::max(maximum[r], s);
+                    }
+                }
+                for (int r = 0; r < rows; ++r)
+                {
+                    double t = 0;
+                    double *sr = scores.data() + size_t(r) * nk;
+                    for (int j = 0; j < nk; ++j)
+                    {
+                        sr[j] = std::exp(sr[j] - maximum[r]);
+                        t += sr[j];
+                    }
+                    total[r] = t;
                 }
                 std::fill(acc.begin(), acc.end(), 0.0);
                 for (int j = 0; j < nk; ++j)
                 {
-                    const double p = scores[j];
-                    if (p == 0.0) continue;
-                    const float *vj = vh_base + size_t(j) * width;
-                    for (int d = 0; d < width; ++d) acc[d] += p * vj[d];
+                    const double *vj = vh_base + size_t(j) * wp;
+                    for (int r = 0; r < rows; ++r)
+                    {
+                        const double p = scores[size_t(r) * nk + j];
+                        if (p == 0.0) continue;
+                        double *ar = acc.data() + size_t(r) * wp;
+                        const v4d pv = {p, p, p, p};
+                        for (int d = 0; d < wp; d += 4)
+                        {
+                            v4d a4 = load4d(ar + d) + pv * load4d(vj + d);
+                            std::memcpy(ar + d, &a4, sizeof(a4));
+                        }
+                    }
                 }
-                float *o = out + (size_t(h) * nq + i) * width;
-                for (int d = 0; d < width; ++d) o[d] = float(acc[d] / total);
+                for (int r = 0; r < rows; ++r)
+                {
+                    float *o = out + (size_t(h) * nq + i0 + r) * width;
+                    for (int d = 0; d < width; ++d) o[d] = float(acc[size_t(r) * wp + d] / total[r]);
+                }
             }
     }
 }
