@@ -157,7 +157,7 @@ def cpu_baseline_block(threads=None):
 # The reference's own published CPU timing of the same block: ncnn CPU FP32 on 4 threads of a Ryzen 7 7745HX,
 # 4.484 / 4.434 / 4.403 s for one 4160-token block (artifacts/2026-09-05/dit-block/README.md:53 of the
 # reference). It cannot be reproduced here (empty ncnn submodule); it is printed beside the port's timing so
-# that the GPU/CPU ratio can also be read against the real ncnn CPU path (about 6x faster per core).
+# that the GPU/CPU ratio can also be read against the real ncnn CPU path (about 3x faster per core).
 REFERENCE_CPU_BLOCK_S = 4.434
 REFERENCE_CPU_THREADS = 4
 
