@@ -6,6 +6,7 @@ import json
 import os
 import subprocess
 import sys
+import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ARGS = ["--impl", "reference", "--stage", "vae-encode", "--steps", "1", "--warmup", "1"]
@@ -24,7 +25,9 @@ def json_lines(stdout):
 
 
 def test_reference_arm_prints_one_complete_line():
+    start = time.perf_counter()
     r = run(ARGS)
+    wall_s = time.perf_counter() - start
     assert r.returncode == 0, r.stderr[-2000:]
     lines = json_lines(r.stdout)
     assert len(lines) == 1
@@ -42,6 +45,8 @@ def test_reference_arm_prints_one_complete_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert isinstance(d["config"].get("workload"), str)
+    # ms_per_step is the measured time of one timed step, so the timed steps fit in the run's own clock
+    assert d["steps"] * d["ms_per_step"] / 1000.0 <= wall_s, (d["ms_per_step"], wall_s)
 
 
 def test_other_ranks_exit_without_work():
